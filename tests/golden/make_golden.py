@@ -1,0 +1,197 @@
+"""Generate the golden fixtures by running the reference itself.
+
+Run in a container that has the reference checkout (read-only) and transformers:
+
+    python tests/golden/make_golden.py /root/reference
+
+What runs is the reference's own code, unmodified:
+  * the torso: transformers' `Qwen3_5ForCausalLM(cfg).model` (the module strands-decider
+    loads, `src/strands_decider/modeling.py:293-303`), fp32 on CPU, with the synthetic
+    weights after quantise -> dequantise (oracle.quant) copied into its parameters;
+  * the readout: strands-decider's `pool_last_token`, `apply_temperature` and
+    `masked_log_softmax` (`modeling.py:193-238`) over the tied embedding rows of the
+    option tokens (`frozen_slot_log_probs`, `modeling.py:412-438`), on the full-prompt
+    path (`infer.py:253-279`), right-padded as `SystemOneEngine._pad` does;
+  * the answer formulas `derive_confidence` / `derive_score_confidence` (`schema.py`);
+  * transformers' `torch_chunk_gated_delta_rule` with an initial state (`TF:234-311`).
+
+The fixtures are small .npz files committed beside this script; the tests read only
+them (the reference is not present where the GPU tests run).
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))  # repo root
+
+
+CHUNK_SEQS = (1, 63, 64, 65, 200)
+
+
+def chunk_rule_inputs(seq: int, heads: int = 2, dim: int = 64):
+    """Seeded inputs of one chunk-rule case (shapes [seq, heads, dim]); correlated keys."""
+    gg = torch.Generator().manual_seed(seq)
+    r = lambda *s: torch.randn(*s, generator=gg)  # noqa: E731
+    shared = 2.0 * r(1, heads, dim)
+    x = dict(query=r(seq, heads, dim), key=r(seq, heads, dim) + shared, value=r(seq, heads, dim),
+             g=-torch.rand(seq, heads, generator=gg) * 0.1,
+             beta=0.5 + 0.5 * torch.rand(seq, heads, generator=gg))
+    return x, r(heads, dim, dim)
+
+
+def build_reference_torso(spec, W):
+    import transformers
+
+    cfg = transformers.Qwen3_5TextConfig(
+        vocab_size=spec.vocab, hidden_size=spec.hidden, intermediate_size=spec.inter,
+        num_hidden_layers=spec.n_layers, num_attention_heads=spec.attn_heads,
+        num_key_value_heads=spec.attn_kv_heads, head_dim=spec.head_dim,
+        linear_num_key_heads=spec.gdn_heads, linear_num_value_heads=spec.gdn_heads,
+        linear_key_head_dim=spec.gdn_dk, linear_value_head_dim=spec.gdn_dv,
+        linear_conv_kernel_dim=spec.conv_width, layer_types=list(spec.layer_types),
+        rms_norm_eps=spec.eps, tie_word_embeddings=True,
+        rope_parameters={"rope_type": "default", "rope_theta": spec.rope_theta,
+                         "partial_rotary_factor": spec.partial_rotary})
+    torso = transformers.Qwen3_5ForCausalLM(cfg).model.float().eval()
+    sd = {"embed_tokens.weight": W["embed"], "norm.weight": W["final_norm"]}
+    for li, L in enumerate(W["layers"]):
+        p = f"layers.{li}."
+        sd[p + "input_layernorm.weight"] = L["input_norm"]
+        sd[p + "post_attention_layernorm.weight"] = L["post_norm"]
+        sd[p + "mlp.gate_proj.weight"] = L["mlp"]["gate"]
+        sd[p + "mlp.up_proj.weight"] = L["mlp"]["up"]
+        sd[p + "mlp.down_proj.weight"] = L["mlp"]["down"]
+        if "gdn" in L:
+            G, q = L["gdn"], p + "linear_attn."
+            sd[q + "in_proj_qkv.weight"] = G["qkv"]
+            sd[q + "in_proj_z.weight"] = G["z"]
+            sd[q + "in_proj_b.weight"] = G["b"]
+            sd[q + "in_proj_a.weight"] = G["a"]
+            sd[q + "out_proj.weight"] = G["out"]
+            sd[q + "conv1d.weight"] = G["conv_w"][:, None, :]
+            sd[q + "A_log"] = G["A_log"]
+            sd[q + "dt_bias"] = G["dt_bias"]
+            sd[q + "norm.weight"] = G["norm_w"]
+        else:
+            A, q = L["attn"], p + "self_attn."
+            for k in ("q", "k", "v", "o"):
+                sd[q + f"{k}_proj.weight"] = A[k]
+            sd[q + "q_norm.weight"] = A["q_norm"]
+            sd[q + "k_norm.weight"] = A["k_norm"]
+    missing, unexpected = torso.load_state_dict(sd, strict=False)
+    missing = [m for m in missing if "rotary" not in m]
+    assert not missing and not unexpected, (missing, unexpected)
+    return torso
+
+
+def reference_probs(torso, rows, opt_ids, n_opts, temps, pad_id=0):
+    """Full-prompt path: right-pad, forward, pool, option rows, temperature, masked softmax."""
+    from strands_decider.modeling import apply_temperature, masked_log_softmax, pool_last_token
+
+    width = max(len(r) for r in rows)
+    ids = torch.tensor([r + [pad_id] * (width - len(r)) for r in rows])
+    mask = torch.tensor([[1] * len(r) + [0] * (width - len(r)) for r in rows])
+    with torch.inference_mode():
+        hidden = torso(input_ids=ids, attention_mask=mask, return_dict=True).last_hidden_state
+        pooled = pool_last_token(hidden, mask).to(torch.float32)
+        table = torso.get_input_embeddings().weight
+        kmax = max(len(o) for o in opt_ids)
+        logits = torch.full((len(rows), kmax), -1e4)
+        for i, o in enumerate(opt_ids):
+            logits[i, : len(o)] = pooled[i] @ table[o].to(torch.float32).t()
+        logits = apply_temperature(logits, torch.tensor(temps, dtype=torch.float32))
+        lp = masked_log_softmax(logits, torch.tensor(n_opts))
+    return lp.exp().numpy(), pooled.numpy(), hidden.numpy(), mask.numpy()
+
+
+def main(reference_root: str) -> None:
+    sys.path.insert(0, os.path.join(reference_root, "src"))
+    import transformers.models.qwen3_5.modeling_qwen3_5 as q35
+    from strands_decider.schema import derive_confidence, derive_score_confidence
+
+    from oracle import synth as osynth
+    from strands_decider_b200 import config
+
+    torch.manual_seed(0)
+    torch.set_num_threads(os.cpu_count() or 1)
+
+    # 1. the reduced CPU decider: 4 prompts x 256 ids, 3 single-token options, at the last position
+    spec = config.REDUCED_1024
+    packed = dict(osynth.quantized_linears(spec, seed=0))
+    W = osynth.logical_weights(spec, seed=0, packed=packed)
+    torso = build_reference_torso(spec, W)
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, spec.vocab, (4, 256), generator=g)
+    rows = ids.tolist()
+    opt = [[11, 12, 13]] * 4
+    probs, pooled, _, _ = reference_probs(torso, rows, opt, [3] * 4, [1.0] * 4)
+    np.savez_compressed(os.path.join(HERE, "reduced_1024_int4.npz"), ids=ids.numpy().astype(np.int32),
+                        opt_ids=np.array(opt, dtype=np.int32), probs=probs.astype(np.float32),
+                        pooled=pooled.astype(np.float32),
+                        packed_digest=np.array(osynth.packed_digest(packed)))
+    print("reduced_1024 probs", probs)
+
+    # 2. ragged prompts with padding, mixed kinds and temperatures, state+question prompts,
+    #    on the tiny spec (every hidden state kept, so the torso is pinned position by position)
+    spec = config.TINY
+    for fmt in ("int4", "nvfp4", "ternary"):
+        packed = dict(osynth.quantized_linears(spec, seed=1, fmt=fmt))
+        W = osynth.logical_weights(spec, seed=1, fmt=fmt, packed=packed)
+        torso = build_reference_torso(spec, W)
+        g = torch.Generator().manual_seed(1)
+        states = [torch.randint(0, spec.vocab, (n,), generator=g).tolist() for n in (70, 5)]
+        qs = [torch.randint(0, spec.vocab, (n,), generator=g).tolist() for n in (9, 1, 33, 64)]
+        rows = [states[0] + qs[0], states[0] + qs[1], states[1] + qs[2], states[1] + qs[3]]
+        opt = [[11, 12, 13], [11, 12], [11, 12, 13, 14, 15], [11, 12, 13, 14]]
+        nopt = [3, 2, 5, 4]
+        temps = [1.0, 0.7, 1.6, 2.5]
+        probs, pooled, hidden, mask = reference_probs(torso, rows, opt, nopt, temps)
+        np.savez_compressed(
+            os.path.join(HERE, f"tiny_{fmt}_ragged.npz"),
+            state0=np.array(states[0], np.int32), state1=np.array(states[1], np.int32),
+            q0=np.array(qs[0], np.int32), q1=np.array(qs[1], np.int32),
+            q2=np.array(qs[2], np.int32), q3=np.array(qs[3], np.int32),
+            opt_ids=np.array([o + [0] * (5 - len(o)) for o in opt], np.int32),
+            n_opts=np.array(nopt, np.int32), temps=np.array(temps, np.float32),
+            probs=probs.astype(np.float32), pooled=pooled.astype(np.float32),
+            hidden=hidden.astype(np.float32) if fmt == "int4" else np.zeros(0, np.float32),
+            mask=mask.astype(np.int32),
+            packed_digest=np.array(osynth.packed_digest(packed)))
+        print(fmt, "tiny probs", probs)
+
+    # 3. the chunk rule with an initial state and correlated keys (tests/test_mps_kernels.py:23-35);
+    #    inputs are regenerated from their seeds by chunk_rule_inputs, only outputs are stored
+    out = {}
+    for seq in CHUNK_SEQS:
+        x, state = chunk_rule_inputs(seq)
+        o, s = q35.torch_chunk_gated_delta_rule(**{k: v[None] for k, v in x.items()},
+                                                initial_state=state[None], output_final_state=True,
+                                                use_qk_l2norm_in_kernel=True)
+        out[f"s{seq}_out"] = o[0].numpy()
+        out[f"s{seq}_state"] = s[0].numpy()
+    np.savez_compressed(os.path.join(HERE, "chunk_rule.npz"), **out)
+
+    # 4. answer formulas
+    dists = [[1 / 3, 1 / 3, 1 / 3], [1.0, 0.0, 0.0], [0.88, 0.12, 0.0], [0.7, 0.2, 0.1],
+             [0.0, 0.5, 0.5, 0.0, 0.0], [0.2] * 5, [0.5, 0.0, 0.0, 0.0, 0.5], [0.3, 0.7],
+             [0.05, 0.9, 0.05], [0.1, 0.2, 0.3, 0.4]]
+    conf = [derive_confidence(d) for d in dists]
+    sconf = [derive_score_confidence(d) for d in dists]
+    sconf_s = [derive_score_confidence(d, ordinal_smoothing=0.1) for d in dists]
+    flat = np.zeros((len(dists), 5), np.float64)
+    for i, d in enumerate(dists):
+        flat[i, : len(d)] = d
+    np.savez_compressed(os.path.join(HERE, "answer_formulas.npz"), probs=flat,
+                        n=np.array([len(d) for d in dists]), confidence=np.array(conf),
+                        score_confidence=np.array(sconf), score_confidence_s01=np.array(sconf_s))
+    print("done")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
