@@ -1,0 +1,255 @@
+/*
+ * strands_b200.h -- C ABI of the B200 (sm_100a) scoring-prefill backend for strands-decider.
+ *
+ * The reference runs its scoring prefill in Python: `SystemOneEngine._slot_probs_batched`
+ * and `_slot_probs_shared_prefix` (src/strands_decider/infer.py:253-337) call the
+ * transformers Qwen3.5 torso (models/qwen3_5/modeling_qwen3_5.py, cited TF:line) and then
+ * the readout in src/strands_decider/modeling.py. This library replaces everything below
+ * those two methods: the torso forward, the prefix-cache fork, and the readout.
+ *
+ * Conventions
+ *   - Every pointer argument is a DEVICE pointer unless its comment says otherwise;
+ *     the caller (torch) allocates and owns all memory. Nothing here calls cudaMalloc.
+ *   - Every call is asynchronous on the given stream (a cudaStream_t) and returns an
+ *     int status (B200_OK == 0). A non-zero status leaves the stream usable;
+ *     b200_last_error() returns a message for the calling thread.
+ *   - Token batches are ragged and packed: sequence i owns tokens
+ *     [cu_seqlens[i], cu_seqlens[i+1]) of every [tokens, ...] activation array.
+ *   - bf16 tensors are passed as uint16_t bit patterns.
+ */
+#ifndef STRANDS_B200_H
+#define STRANDS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* b200_stream; /* cudaStream_t */
+
+/* ---------------------------------------------------------------- status codes */
+enum b200_status {
+  B200_OK = 0,
+  B200_ERR_ARG = 1,         /* null pointer, negative size, unknown enum */
+  B200_ERR_SHAPE = 2,       /* a size the kernels do not support (alignment, limits) */
+  B200_ERR_FORMAT = 3,      /* unknown or mismatched weight format */
+  B200_ERR_CUDA = 4,        /* a CUDA runtime call or launch failed */
+  B200_ERR_WORKSPACE = 5,   /* the caller's workspace is smaller than required */
+  B200_ERR_TIMEOUT = 6,     /* a device-side bounded wait gave up (see b200_read_fault) */
+  B200_ERR_UNSUPPORTED = 7, /* a combination this build does not implement */
+};
+
+/* Message for the last non-zero status returned on this thread. */
+const char* b200_last_error(void);
+/* Library ABI version (major * 100 + minor). */
+int b200_version(void);
+/* Reads and clears the device fault word of the current device (0 = no fault). Blocking. */
+int b200_read_fault(unsigned int* fault_out);
+
+/* ---------------------------------------------------------------- packed weights
+ * Replaces the bf16 `nn.Linear` weights of TF:417-420, TF:403, TF:632-643, TF:701-703.
+ * Formats (bit-exact definitions in oracle/quant.py and DESIGN.md):
+ *   B200_W_BF16     data uint16 [n, k]
+ *   B200_W_INT4G128 data int32 [n, k/8] (8 nibbles per word, element k at bits 4*(k%8)),
+ *                   scales bf16 [n, k/128]
+ *   B200_W_NVFP4    data uint8 [n, k/2] (element k: low nibble if k even, high if odd),
+ *                   scales e4m3 uint8 [n, k/16], row_scale fp32 [n] (the per-tensor scale
+ *                   of the logical tensor each row belongs to)
+ *   B200_W_TERNARY  data uint8 [n, k/4] (2 bits per element: 00=0, 01=+1, 11=-1),
+ *                   scales bf16 [n]
+ */
+enum b200_wfmt { B200_W_BF16 = 0, B200_W_INT4G128 = 1, B200_W_NVFP4 = 2, B200_W_TERNARY = 3 };
+
+typedef struct b200_qweight {
+  int32_t format;
+  int32_t n; /* rows (output features), a multiple of 256 for b200_linear */
+  int32_t k; /* columns (input features), a multiple of 128 */
+  const void* data;
+  const void* scales;
+  const float* row_scale; /* NVFP4 only, else NULL */
+} b200_qweight;
+
+/* Quantise an fp32 weight w[n, k] (one logical nn.Linear) into `format`; writes data,
+ * scales and (NVFP4) row_scale[n]. Bit-exact to oracle/quant.py. */
+int b200_quantize(int32_t format, const float* w, int32_t n, int32_t k, void* data, void* scales,
+                  float* row_scale, b200_stream stream);
+/* Unpack a packed weight to bf16 out[n, k], exactly as the GEMM's shared-memory unpacker. */
+int b200_dequantize(const b200_qweight* w, uint16_t* out, b200_stream stream);
+
+/* ---------------------------------------------------------------- linear (GEMM)
+ * y = x @ dequant(W)^T with a fused epilogue. x is bf16 [m, k] row-major (leading dim
+ * ldx, a multiple of 8); fp32 accumulation in tensor memory (tcgen05 on sm_100a).
+ * Replaces one or several `nn.Linear` calls plus the elementwise op that follows them:
+ *   B200_EP_STORE     out bf16 [m, ldo] for columns < split_n; columns >= split_n go to
+ *                     out_f32 [m, ldo_f32] at column (col - split_n) in fp32
+ *                     (GDN in-projection: qkv and z in bf16, b and a in fp32, TF:442-449)
+ *   B200_EP_RESID_ADD out fp32 [m, ldo] += y (the residual adds of TF:775 and TF:781)
+ *   B200_EP_SWIGLU    W rows interleaved in blocks of 64 (gate, up); out bf16 [m, ldo]
+ *                     column j = silu(y[64*(2b)+i]) * y[64*(2b+1)+i], j = 64*b + i (TF:707)
+ * Only columns < n_valid are written. */
+enum b200_epilogue { B200_EP_STORE = 0, B200_EP_RESID_ADD = 1, B200_EP_SWIGLU = 2 };
+
+typedef struct b200_linear_out {
+  int32_t epilogue;
+  int32_t n_valid;
+  void* out;
+  int32_t ldo;
+  float* out_f32;
+  int32_t ldo_f32;
+  int32_t split_n;
+} b200_linear_out;
+
+int b200_linear(const uint16_t* x, int32_t m, int32_t k, int32_t ldx, const b200_qweight* w,
+                const b200_linear_out* out, b200_stream stream);
+/* Same contract on plain CUDA cores (fp32 FMA), used by the tests to cross-check b200_linear. */
+int b200_linear_simt(const uint16_t* x, int32_t m, int32_t k, int32_t ldx, const b200_qweight* w,
+                     const b200_linear_out* out, b200_stream stream);
+
+/* ---------------------------------------------------------------- ragged batches, prefix cache */
+typedef struct b200_seqs {
+  int32_t n_seqs;
+  int32_t n_tokens;
+  int32_t max_len;             /* host-side upper bound on any sequence's length */
+  const int32_t* cu_seqlens;   /* [n_seqs + 1] */
+  const int32_t* prefix_slot;  /* [n_seqs]: prefix-pool slot this sequence continues, -1 none; may be NULL */
+  const int32_t* save_slot;    /* [n_seqs]: slot to write this sequence's cache into, -1 none; may be NULL */
+} b200_seqs;
+
+/* The prefix-state pool that replaces the reference's cache fork (infer.py:79-124,
+ * _expand_cache): question suffixes read a state's cache in place by slot index, so the
+ * `expand(n).contiguous()` copies of infer.py:103,107 never happen. One pool per model;
+ * arrays are indexed [layer of that kind][slot]. A sequence that continues a prefix
+ * (prefix_slot >= 0) must not also save (save_slot >= 0). */
+typedef struct b200_prefix_pool {
+  int32_t n_slots;
+  int32_t kv_capacity;     /* tokens per attention layer in k_cache / v_cache */
+  int32_t* slot_len;       /* [n_slots]: cached length (positions); written by saving prefills */
+  const int32_t* slot_kv;  /* [n_slots]: token offset of the slot's keys in k_cache / v_cache (host-assigned) */
+  float* gdn_state;        /* [n_gdn_layers][n_slots][heads][dk][dv] fp32 (TF:285-305 state) */
+  uint16_t* conv_hist;     /* [n_gdn_layers][n_slots][conv_width-1][conv_dim] bf16 (TF:462-464) */
+  uint16_t* k_cache;       /* [n_attn_layers][kv_capacity][kv_heads][head_dim] bf16, post norm+RoPE */
+  uint16_t* v_cache;       /* [n_attn_layers][kv_capacity][kv_heads][head_dim] bf16 */
+} b200_prefix_pool;
+
+/* ---------------------------------------------------------------- torso building blocks */
+
+/* x[t, :] = float(table[ids[t], :]) (the embedding lookup, TF:1241). */
+int b200_embed(const int32_t* ids, int32_t n_tokens, const uint16_t* table, int32_t hidden, float* x,
+               b200_stream stream);
+
+/* out = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w)) per row (Qwen3_5RMSNorm, TF:711-728). */
+int b200_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
+                 b200_stream stream);
+
+/* One Gated-DeltaNet token mixer after its in-projection (TF:462-530): depthwise causal
+ * conv (width conv_width) + SiLU, q/k l2norm, beta = sigmoid(b), g = -exp(A_log) *
+ * softplus(a + dt_bias), the chunked gated delta rule (TF:234-311) from the prefix slot's
+ * state, and the gated RMSNorm (TF:175-190). mix: bf16 [tokens, ld_mix] holding
+ * [q | k | v | z] columns; ab: fp32 [tokens, 2*heads] holding [b | a]; out: bf16
+ * [tokens, heads*dv]. gdn_layer indexes the pool's GDN arrays. */
+typedef struct b200_gdn_params {
+  int32_t heads, dk, dv, conv_width;
+  float eps;
+  const float* conv_w;   /* [conv_dim][conv_width] */
+  const float* a_log;    /* [heads] */
+  const float* dt_bias;  /* [heads] */
+  const float* norm_w;   /* [dv] */
+} b200_gdn_params;
+
+int b200_gdn_mixer(const b200_gdn_params* p, const b200_seqs* seqs, const uint16_t* mix, int32_t ld_mix,
+                   const float* ab, uint16_t* out, const b200_prefix_pool* pool, int32_t gdn_layer,
+                   b200_stream stream);
+
+/* Gated GQA attention after its qkv projection (TF:647-690): per-head q/k RMSNorm(1+w),
+ * partial RoPE on the first rope_dim dims (cos/sin tables [max_pos][rope_dim/2]), causal
+ * softmax attention over the prefix slot's keys and the sequence's own, times
+ * sigmoid(gate). qkv: bf16 [tokens, ld_qkv] = [per q head (query, gate) | k | v]
+ * (TF:658-665); k_buf, v_buf: scratch bf16 [tokens][kv_heads][head_dim]; out: bf16
+ * [tokens, heads*head_dim]. */
+typedef struct b200_attn_params {
+  int32_t heads, kv_heads, head_dim, rope_dim, max_pos;
+  float eps;
+  const float* q_norm;   /* [head_dim] */
+  const float* k_norm;   /* [head_dim] */
+  const float* rope_cos; /* [max_pos][rope_dim/2] */
+  const float* rope_sin;
+} b200_attn_params;
+
+int b200_attention(const b200_attn_params* p, const b200_seqs* seqs, const uint16_t* qkv, int32_t ld_qkv,
+                   uint16_t* q_buf, uint16_t* k_buf, uint16_t* v_buf, uint16_t* out,
+                   const b200_prefix_pool* pool, int32_t attn_layer, b200_stream stream);
+
+/* ---------------------------------------------------------------- decision head
+ * Replaces pool_last_token -> final RMSNorm -> option-token logits over the tied
+ * embedding rows -> apply_temperature -> masked_log_softmax -> exp (modeling.py:193-238,
+ * 412-438) and the per-kind read-back of infer.py:444-472 / schema.py:141-198, for rows
+ * whose last token is x[last_tok[i]]. The full-vocabulary logits are never formed.
+ * kinds: 0 noul, 1 choice, 2 score. Outputs per row: probs[i][kmax] (masked slots 0),
+ * argmax[i], confidence[i] (choice: (n p_max - 1)/(n - 1); score: normalised-sigma
+ * confidence with ordinal_smoothing; noul: |2p - 1|) and score[i] (score: expected level;
+ * noul: P(true) = probs[i][1]; choice: argmax). kmax <= 16. */
+typedef struct b200_decide_args {
+  int32_t n_rows, kmax;
+  const int32_t* last_tok;   /* [n_rows] */
+  const int32_t* opt_ids;    /* [n_rows][kmax] */
+  const int32_t* n_opts;     /* [n_rows] */
+  const int32_t* kinds;      /* [n_rows] */
+  const float* temperature;  /* [n_rows] */
+  float ordinal_smoothing;
+  float* probs;              /* [n_rows][kmax] */
+  int32_t* argmax;
+  float* confidence;
+  float* score;
+} b200_decide_args;
+
+int b200_decide(const float* x, int32_t hidden, const float* final_norm, float eps, const uint16_t* table,
+                const b200_decide_args* d, b200_stream stream);
+
+/* ---------------------------------------------------------------- whole-torso runtime
+ * A model context holds the configuration and the device pointers of every weight
+ * (registered once, owned by the caller). b200_model_forward runs the full torso prefill
+ * (TF:1227-1290) over a ragged batch -- reading and/or filling the prefix pool -- and,
+ * when `decide` is non-NULL, the decision head: one call covers the reference's
+ * `self.model(...)` of infer.py:272-279 or the two torso calls of infer.py:298-335. */
+enum b200_layer_kind { B200_LAYER_GDN = 0, B200_LAYER_ATTN = 1 };
+
+typedef struct b200_model_config {
+  int32_t vocab, hidden, inter, n_layers;
+  int32_t layer_kind[64];
+  int32_t gdn_heads, gdn_dk, gdn_dv, conv_width;
+  int32_t attn_heads, attn_kv_heads, head_dim, rope_dim, max_pos;
+  float eps;
+  int32_t weight_format;
+} b200_model_config;
+
+typedef struct b200_layer_weights {
+  const float* input_norm;   /* [hidden] */
+  const float* post_norm;    /* [hidden] */
+  b200_qweight mix_in;       /* GDN: [qkv|z|b|a] rows; attention: [q(+gate)|k|v] rows */
+  b200_qweight mix_out;      /* GDN out_proj / attention o_proj */
+  b200_qweight gate_up;      /* interleaved blocks of 64 */
+  b200_qweight down;
+  b200_gdn_params gdn;       /* GDN layers */
+  const float* q_norm;       /* attention layers */
+  const float* k_norm;
+} b200_layer_weights;
+
+typedef struct b200_model b200_model;
+
+int b200_model_create(const b200_model_config* cfg, b200_model** out);
+int b200_model_destroy(b200_model* m);
+int b200_model_set_layer(b200_model* m, int32_t layer, const b200_layer_weights* w);
+int b200_model_set_globals(b200_model* m, const uint16_t* embed, const float* final_norm, const float* rope_cos,
+                           const float* rope_sin);
+/* Bytes of workspace b200_model_forward needs for batches up to max_tokens tokens. */
+int b200_model_workspace_bytes(const b200_model* m, int32_t max_tokens, size_t* bytes);
+int b200_model_forward(b200_model* m, const int32_t* ids, const b200_seqs* seqs, const b200_prefix_pool* pool,
+                       const b200_decide_args* decide, void* workspace, size_t workspace_bytes,
+                       b200_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* STRANDS_B200_H */

@@ -21,13 +21,14 @@ int4 group-128, symmetric
 NVFP4 (e2m1 values, e4m3 scale per 16 elements, fp32 per-tensor scale)
     gs          = amax(|W|) / 2688  (= 6 * 448), or 1 if W is all zero     (fp32 divide)
     sb[n, b]    = e4m3_rn_sat(amax(|W[n, 16b:16b+16]|) / fp32(gs * 6))
-    scale[n, b] = fp32(e4m3_value(sb) * gs)
+    scale[n, b] = bf16_rn(fp32(e4m3_value(sb) * gs))      (the block's effective scale)
     code[n, k]  = e2m1_rn_sat(W[n, k] / scale[n, b]), 0 where scale is 0  (fp32 divide)
     packed      uint8 [N, K/2]; element k in the low nibble of byte k/2 when k is even,
                   the high nibble when odd. Nibble = sign(bit 3) | magnitude code(bits 0-2);
                   a value that rounds to zero is stored as +0.
-    scales      uint8 [N, K/16] (e4m3 bit patterns), global scale fp32 [1]
-    dequant     bf16_rn(fp32(e2m1_value(code) * scale[n, b]))
+    scales      uint8 [N, K/16] (e4m3 bit patterns), per-tensor scale fp32 (stored per row
+                  on the device, constant within one logical tensor)
+    dequant     bf16_rn(e2m1_value(code) * scale[n, b])  (the product is exact in fp32)
 
 Ternary (BitNet b1.58 absmean, Ma et al. 2024), per-output-row scale
     scale[n]    = bf16_rn(fp32(mean(|W[n, :]|)))   (mean accumulated in float64)
@@ -198,7 +199,7 @@ def quantize_nvfp4(w: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.float32]:
     amax_b = np.abs(b).max(axis=2)
     denom = np.float32(gs * np.float32(6.0))
     sb = e4m3_encode((amax_b / denom).astype(np.float32))
-    scale = (e4m3_decode(sb) * gs).astype(np.float32)
+    scale = nvfp4_block_scale(sb, gs)
     with np.errstate(divide="ignore", invalid="ignore"):
         v = (b / scale[:, :, None]).astype(np.float32)
     v = np.where(scale[:, :, None] == 0, np.float32(0), v)
@@ -216,11 +217,16 @@ def unpack_nvfp4(packed: np.ndarray) -> np.ndarray:
     return out
 
 
+def nvfp4_block_scale(sb: np.ndarray, gs) -> np.ndarray:
+    """Effective block scale bf16_rn(fp32(e4m3(sb) * gs)) as fp32."""
+    return bf16_round((e4m3_decode(sb) * np.float32(gs)).astype(np.float32))
+
+
 def dequantize_nvfp4(packed: np.ndarray, sb: np.ndarray, gs: float) -> np.ndarray:
     codes = unpack_nvfp4(packed)
     n, k = codes.shape
     vals = e2m1_decode(codes).reshape(n, k // NVFP4_BLOCK, NVFP4_BLOCK)
-    scale = (e4m3_decode(sb) * np.float32(gs)).astype(np.float32)
+    scale = nvfp4_block_scale(sb, gs)
     prod = (vals * scale[:, :, None]).astype(np.float32)
     return bf16_round(prod.reshape(n, k))
 

@@ -1,0 +1,204 @@
+// Embedding lookup, RMSNorm, and the fused option-token decision head.
+#include "common.cuh"
+
+namespace sdb {
+
+// x[t, :] = float(table[ids[t], :]); one block per token, 8 bf16 per thread per step.
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const uint16_t* __restrict__ table, int hidden,
+                             float* __restrict__ x, int vocab) {
+  const int t = blockIdx.x;
+  int id = ids[t];
+  if (id < 0 || id >= vocab) {
+    raise_fault(FAULT_BAD_INDEX);
+    id = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + size_t(id) * hidden);
+  float4* dst = reinterpret_cast<float4*>(x + size_t(t) * hidden);
+  for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) {
+    uint4 v = __ldg(src + i);
+    dst[2 * i] = make_float4(bf16_to_f32(v.x & 0xFFFF), bf16_to_f32(v.x >> 16), bf16_to_f32(v.y & 0xFFFF),
+                             bf16_to_f32(v.y >> 16));
+    dst[2 * i + 1] = make_float4(bf16_to_f32(v.z & 0xFFFF), bf16_to_f32(v.z >> 16), bf16_to_f32(v.w & 0xFFFF),
+                                 bf16_to_f32(v.w >> 16));
+  }
+}
+
+// One warp per row: y = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w)).  hidden % 128 == 0.
+__global__ void rmsnorm_kernel(const float* __restrict__ x, int rows, int hidden, const float* __restrict__ w,
+                               float eps, uint16_t* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + size_t(row) * hidden);
+  float ss = 0.0f;
+  for (int i = lane; i < hidden / 4; i += 32) {
+    float4 v = xr[i];
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / float(hidden) + eps);
+  uint2* o = reinterpret_cast<uint2*>(out + size_t(row) * hidden);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  for (int i = lane; i < hidden / 4; i += 32) {
+    float4 v = xr[i], g = __ldg(wr + i);
+    o[i] = make_uint2(pack_bf16x2(v.x * r * (1.0f + g.x), v.y * r * (1.0f + g.y)),
+                      pack_bf16x2(v.z * r * (1.0f + g.z), v.w * r * (1.0f + g.w)));
+  }
+}
+
+// Decision head: one warp per decision row. Gathers the row's last token from the fp32
+// residual stream, applies the final RMSNorm (1 + w), dots it with the option tokens'
+// tied-embedding rows, divides by the row's temperature (clamped at 1e-6), takes the
+// masked softmax and derives the answer numbers. hidden <= 4096, kmax <= 16.
+__global__ void decide_kernel(const float* __restrict__ x, int hidden, const float* __restrict__ fnorm, float eps,
+                              const uint16_t* __restrict__ table, b200_decide_args d, int vocab, int n_tokens) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= d.n_rows) return;
+  int tok = d.last_tok[row];
+  if (tok < 0 || tok >= n_tokens) {
+    if (lane == 0) raise_fault(FAULT_BAD_INDEX);
+    tok = 0;
+  }
+  const float* xr = x + size_t(tok) * hidden;
+  constexpr int MAXP = 4096 / 32;
+  float h[MAXP];
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < MAXP; ++j) {
+    const int i = lane + 32 * j;
+    h[j] = i < hidden ? xr[i] : 0.0f;
+    ss += h[j] * h[j];
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / float(hidden) + eps);
+#pragma unroll
+  for (int j = 0; j < MAXP; ++j) {
+    const int i = lane + 32 * j;
+    h[j] = i < hidden ? h[j] * r * (1.0f + fnorm[i]) : 0.0f;
+  }
+  const int n = d.n_opts[row];
+  const float temp = fmaxf(d.temperature[row], 1e-6f);
+  float logit[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    logit[k] = -1e4f;  // MASK_VALUE for slots past n (modeling.py:39, 210-221)
+    if (k < d.kmax && k < n) {
+      int id = d.opt_ids[row * d.kmax + k];
+      if (id < 0 || id >= vocab) {
+        raise_fault(FAULT_BAD_INDEX);
+        id = 0;
+      }
+      const uint16_t* e = table + size_t(id) * hidden;
+      float acc = 0.0f;
+#pragma unroll
+      for (int j = 0; j < MAXP; ++j) {
+        const int i = lane + 32 * j;
+        if (i < hidden) acc = fmaf(h[j], bf16_to_f32(e[i]), acc);
+      }
+      logit[k] = warp_sum(acc) / temp;
+    }
+  }
+  // masked softmax over the first n slots
+  float mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < 16; ++k)
+    if (k < n && k < d.kmax) mx = fmaxf(mx, logit[k]);
+  float p[16], sum = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    p[k] = (k < n && k < d.kmax) ? __expf(logit[k] - mx) : 0.0f;
+    sum += p[k];
+  }
+  int best = 0;
+  float pmax = -1.0f, mean = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    p[k] /= sum;
+    if (k < n && p[k] > pmax) {
+      pmax = p[k];
+      best = k;
+    }
+    mean += float(k) * p[k];
+  }
+  if (lane == 0) {
+    for (int k = 0; k < d.kmax; ++k) d.probs[row * d.kmax + k] = p[k];
+    float conf, score;
+    const int kind = d.kinds[row];
+    if (kind == 0) {  // noul: P(true) is slot 1 (prompting.py:27, 153-156)
+      score = n > 1 ? p[1] : 0.0f;
+      conf = fabsf(2.0f * score - 1.0f);
+    } else if (kind == 1) {  // choice: schema.py:185-198
+      score = float(best);
+      conf = n <= 1 ? 1.0f : fminf(1.0f, fmaxf(0.0f, (float(n) * pmax - 1.0f) / float(n - 1)));
+    } else {  // score: expected level and schema.py:141-182
+      float tot = 0.0f, m2 = 0.0f, var = 0.0f;
+      for (int k = 0; k < n && k < 16; ++k) tot += p[k];
+      for (int k = 0; k < n && k < 16; ++k) m2 += float(k) * (p[k] / tot);
+      for (int k = 0; k < n && k < 16; ++k) var += (p[k] / tot) * (float(k) - m2) * (float(k) - m2);
+      score = mean;
+      const float sigma = sqrtf(var), smax = float(n - 1) * 0.5f;
+      const float floor_ = d.ordinal_smoothing > 0.0f ? sqrtf(d.ordinal_smoothing) : 0.0f;
+      if (n <= 1)
+        conf = 1.0f;
+      else if (tot <= 0.0f)
+        conf = 0.0f;
+      else if (smax <= floor_)
+        conf = sigma <= floor_ ? 1.0f : 0.0f;
+      else
+        conf = fminf(1.0f, fmaxf(0.0f, (smax - sigma) / (smax - floor_)));
+    }
+    d.argmax[row] = best;
+    d.confidence[row] = conf;
+    d.score[row] = score;
+  }
+}
+
+}  // namespace sdb
+
+using namespace sdb;
+
+extern "C" int b200_embed(const int32_t* ids, int32_t n_tokens, const uint16_t* table, int32_t hidden, float* x,
+                          b200_stream stream) {
+  if (!ids || !table || !x) return sdb_fail(B200_ERR_ARG, "b200_embed: null pointer");
+  if (n_tokens <= 0 || hidden % 8 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_embed: bad shape");
+  embed_kernel<<<n_tokens, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(ids, table, hidden, x, 1 << 30);
+  SDB_LAUNCH_CHECK();
+  return B200_OK;
+}
+
+int sdb_embed_vocab(const int32_t* ids, int32_t n_tokens, const uint16_t* table, int32_t hidden, float* x, int vocab,
+                    cudaStream_t st) {
+  embed_kernel<<<n_tokens, 128, 0, st>>>(ids, table, hidden, x, vocab);
+  SDB_LAUNCH_CHECK();
+  return B200_OK;
+}
+
+extern "C" int b200_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
+                            b200_stream stream) {
+  if (!x || !w || !out) return sdb_fail(B200_ERR_ARG, "b200_rmsnorm: null pointer");
+  if (rows <= 0 || hidden % 128 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_rmsnorm: hidden % 128 must be 0");
+  rmsnorm_kernel<<<(rows + 7) / 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, rows, hidden, w, eps, out);
+  SDB_LAUNCH_CHECK();
+  return B200_OK;
+}
+
+int sdb_decide_vocab(const float* x, int32_t hidden, const float* final_norm, float eps, const uint16_t* table,
+                     const b200_decide_args* d, int vocab, int n_tokens, cudaStream_t st) {
+  if (!x || !final_norm || !table || !d) return sdb_fail(B200_ERR_ARG, "b200_decide: null pointer");
+  if (d->n_rows <= 0) return B200_OK;
+  if (d->kmax < 1 || d->kmax > 16 || hidden > 4096 || hidden % 32 != 0)
+    return sdb_fail(B200_ERR_SHAPE, "b200_decide: kmax must be 1..16 and hidden <= 4096");
+  if (!d->last_tok || !d->opt_ids || !d->n_opts || !d->kinds || !d->temperature || !d->probs || !d->argmax ||
+      !d->confidence || !d->score)
+    return sdb_fail(B200_ERR_ARG, "b200_decide: null array");
+  decide_kernel<<<(d->n_rows + 3) / 4, 128, 0, st>>>(x, hidden, final_norm, eps, table, *d, vocab, n_tokens);
+  SDB_LAUNCH_CHECK();
+  return B200_OK;
+}
+
+extern "C" int b200_decide(const float* x, int32_t hidden, const float* final_norm, float eps, const uint16_t* table,
+                           const b200_decide_args* d, b200_stream stream) {
+  return sdb_decide_vocab(x, hidden, final_norm, eps, table, d, 1 << 30, 1 << 30,
+                          reinterpret_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,193 @@
+// Weight quantisers and the standalone dequantiser (bit-exact to oracle/quant.py).
+#include "dequant.cuh"
+
+namespace sdb {
+
+// int4 group-128: one thread per (row, group).
+__global__ void quant_int4_kernel(const float* __restrict__ w, int n, int k, uint32_t* __restrict__ data,
+                                  uint16_t* __restrict__ scales) {
+  const int groups = k / 128;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * groups) return;
+  const int row = idx / groups, g = idx % groups;
+  const float* src = w + size_t(row) * k + g * 128;
+  float amax = 0.0f;
+  for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(src[i]));
+  const uint16_t sb = f32_to_bf16_rn(__fdiv_rn(amax, 7.0f));
+  const float s = bf16_to_f32(sb);
+  scales[size_t(row) * groups + g] = sb;
+  uint32_t* dst = data + size_t(row) * (k / 8) + g * 16;
+  for (int wd = 0; wd < 16; ++wd) {
+    uint32_t word = 0;
+    for (int j = 0; j < 8; ++j) {
+      int q = 0;
+      if (s != 0.0f) {
+        q = __float2int_rn(__fdiv_rn(src[wd * 8 + j], s));
+        q = max(-8, min(7, q));
+      }
+      word |= (uint32_t(q) & 0xFu) << (4 * j);
+    }
+    dst[wd] = word;
+  }
+}
+
+// |x| max of a tensor into *out (non-negative floats order like their bit patterns).
+__global__ void absmax_kernel(const float* __restrict__ w, size_t count, unsigned int* __restrict__ out) {
+  float m = 0.0f;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < count; i += size_t(gridDim.x) * blockDim.x)
+    m = fmaxf(m, fabsf(w[i]));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+// row_scale[0] holds the tensor's |max| as bits; one block turns it into gs and writes gs
+// to every row (a single block, so the read of row 0 happens before any write).
+__global__ void nvfp4_gs_kernel(float* __restrict__ row_scale, int n) {
+  __shared__ float gs_sh;
+  if (threadIdx.x == 0) {
+    const float amax = __uint_as_float(reinterpret_cast<const unsigned int*>(row_scale)[0]);
+    gs_sh = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 2688.0f);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) row_scale[i] = gs_sh;
+}
+
+// NVFP4: one thread per (row, 16-block).
+__global__ void quant_nvfp4_kernel(const float* __restrict__ w, int n, int k, const float* __restrict__ row_scale,
+                                   uint8_t* __restrict__ data, uint8_t* __restrict__ scales) {
+  const int blocks = k / 16;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * blocks) return;
+  const int row = idx / blocks, b = idx % blocks;
+  const float gs = row_scale[row];
+  const float* src = w + size_t(row) * k + b * 16;
+  float amax_b = 0.0f;
+  for (int i = 0; i < 16; ++i) amax_b = fmaxf(amax_b, fabsf(src[i]));
+  const uint8_t sb = e4m3_encode(__fdiv_rn(amax_b, __fmul_rn(gs, 6.0f)));
+  scales[size_t(row) * blocks + b] = sb;
+  const float s = nvfp4_block_scale(sb, gs);
+  uint8_t* dst = data + size_t(row) * (k / 2) + b * 8;
+  for (int j = 0; j < 8; ++j) {
+    uint8_t lo = 0, hi = 0;
+    if (s != 0.0f) {
+      lo = e2m1_encode(__fdiv_rn(src[2 * j], s));
+      hi = e2m1_encode(__fdiv_rn(src[2 * j + 1], s));
+    }
+    dst[j] = uint8_t(lo | (hi << 4));
+  }
+}
+
+// ternary: one block per row; absmean accumulated in float64.
+__global__ void quant_ternary_kernel(const float* __restrict__ w, int n, int k, uint8_t* __restrict__ data,
+                                     uint16_t* __restrict__ scales) {
+  const int row = blockIdx.x;
+  const float* src = w + size_t(row) * k;
+  double acc = 0.0;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) acc += double(fabsf(src[i]));
+  __shared__ double red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int i = 0; i < int(blockDim.x >> 5); ++i) t += red[i];
+    red[0] = t;
+  }
+  __syncthreads();
+  const uint16_t sb = f32_to_bf16_rn(float(red[0] / double(k)));
+  const float s = bf16_to_f32(sb);
+  if (threadIdx.x == 0) scales[row] = sb;
+  for (int byte = threadIdx.x; byte < k / 4; byte += blockDim.x) {
+    uint8_t v = 0;
+    for (int j = 0; j < 4; ++j) {
+      int t = 0;
+      if (s != 0.0f) t = max(-1, min(1, __float2int_rn(__fdiv_rn(src[byte * 4 + j], s))));
+      v |= uint8_t((t & 3) << (2 * j));
+    }
+    data[size_t(row) * (k / 4) + byte] = v;
+  }
+}
+
+// Standalone dequantiser: one thread per 32 weights, through the GEMM's own unpackers.
+template <int FMT>
+__global__ void dequant_kernel(b200_qweight w, uint16_t* __restrict__ out) {
+  const int per_row = w.k / 32;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= w.n * per_row) return;
+  const int row = idx / per_row, k0 = (idx % per_row) * 32;
+  uint4 dst[4];
+  if constexpr (FMT == B200_W_BF16) {
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(w.data) + size_t(row) * w.k + k0);
+    for (int c = 0; c < 4; ++c) dst[c] = src[c];
+  } else {
+    uint4 raw;
+    uint32_t sc;
+    float gs;
+    load32<FMT>(w, row, k0, raw, sc, gs);
+    unpack32<FMT>(raw, sc, gs, dst);
+  }
+  uint4* o = reinterpret_cast<uint4*>(out + size_t(row) * w.k + k0);
+  for (int c = 0; c < 4; ++c) o[c] = dst[c];
+}
+
+}  // namespace sdb
+
+using namespace sdb;
+
+extern "C" int b200_quantize(int32_t format, const float* w, int32_t n, int32_t k, void* data, void* scales,
+                             float* row_scale, b200_stream stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (!w || !data || n <= 0 || k <= 0) return sdb_fail(B200_ERR_ARG, "b200_quantize: null pointer or empty shape");
+  if (k % 128 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_quantize: k must be a multiple of 128");
+  switch (format) {
+    case B200_W_INT4G128: {
+      if (!scales) return sdb_fail(B200_ERR_ARG, "b200_quantize: int4 needs scales");
+      const int total = n * (k / 128);
+      quant_int4_kernel<<<(total + 127) / 128, 128, 0, st>>>(w, n, k, reinterpret_cast<uint32_t*>(data),
+                                                             reinterpret_cast<uint16_t*>(scales));
+      break;
+    }
+    case B200_W_NVFP4: {
+      if (!scales || !row_scale) return sdb_fail(B200_ERR_ARG, "b200_quantize: nvfp4 needs scales and row_scale");
+      unsigned int* amax = reinterpret_cast<unsigned int*>(row_scale);
+      SDB_CUDA(cudaMemsetAsync(amax, 0, sizeof(unsigned int), st));
+      absmax_kernel<<<592, 256, 0, st>>>(w, size_t(n) * k, amax);
+      nvfp4_gs_kernel<<<1, 1024, 0, st>>>(row_scale, n);
+      const int total = n * (k / 16);
+      quant_nvfp4_kernel<<<(total + 127) / 128, 128, 0, st>>>(w, n, k, row_scale, reinterpret_cast<uint8_t*>(data),
+                                                              reinterpret_cast<uint8_t*>(scales));
+      break;
+    }
+    case B200_W_TERNARY: {
+      if (!scales) return sdb_fail(B200_ERR_ARG, "b200_quantize: ternary needs scales");
+      quant_ternary_kernel<<<n, 256, 0, st>>>(w, n, k, reinterpret_cast<uint8_t*>(data),
+                                              reinterpret_cast<uint16_t*>(scales));
+      break;
+    }
+    default:
+      return sdb_fail(B200_ERR_FORMAT, "b200_quantize: unknown or non-quantised format");
+  }
+  SDB_LAUNCH_CHECK();
+  return B200_OK;
+}
+
+extern "C" int b200_dequantize(const b200_qweight* w, uint16_t* out, b200_stream stream) {
+  if (!w || !out || !w->data) return sdb_fail(B200_ERR_ARG, "b200_dequantize: null pointer");
+  if (w->n <= 0 || w->k <= 0 || w->k % 128 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_dequantize: bad shape");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int total = w->n * (w->k / 32);
+  const dim3 grid((total + 255) / 256), block(256);
+  switch (w->format) {
+    case B200_W_BF16: dequant_kernel<B200_W_BF16><<<grid, block, 0, st>>>(*w, out); break;
+    case B200_W_INT4G128: dequant_kernel<B200_W_INT4G128><<<grid, block, 0, st>>>(*w, out); break;
+    case B200_W_NVFP4:
+      if (!w->row_scale) return sdb_fail(B200_ERR_ARG, "b200_dequantize: nvfp4 needs row_scale");
+      dequant_kernel<B200_W_NVFP4><<<grid, block, 0, st>>>(*w, out);
+      break;
+    case B200_W_TERNARY: dequant_kernel<B200_W_TERNARY><<<grid, block, 0, st>>>(*w, out); break;
+    default: return sdb_fail(B200_ERR_FORMAT, "b200_dequantize: unknown format");
+  }
+  SDB_LAUNCH_CHECK();
+  return B200_OK;
+}

@@ -1,0 +1,255 @@
+// Model context and the whole-torso prefill (TF:1227-1290) as a native layer loop.
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+// error reporting ---------------------------------------------------------------------
+static thread_local std::string g_last_error;
+
+void sdb_set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+int sdb_fail(int status, const char* msg) {
+  sdb_set_last_error(msg);
+  return status;
+}
+
+namespace sdb {
+__device__ unsigned int g_fault = 0;
+}
+
+// kernels' internal entry points (other translation units)
+int sdb_embed_vocab(const int32_t* ids, int32_t n_tokens, const uint16_t* table, int32_t hidden, float* x, int vocab,
+                    cudaStream_t st);
+int sdb_decide_vocab(const float* x, int32_t hidden, const float* final_norm, float eps, const uint16_t* table,
+                     const b200_decide_args* d, int vocab, int n_tokens, cudaStream_t st);
+int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const uint16_t* mix, int32_t ld_mix, const float* ab,
+                  uint16_t* out, const b200_prefix_pool* pool, int32_t layer, cudaStream_t st);
+int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const uint16_t* qkv, int32_t ld_qkv, uint16_t* q_buf,
+                  uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, const b200_prefix_pool* pool, int32_t layer,
+                  cudaStream_t st);
+
+extern "C" const char* b200_last_error(void) { return g_last_error.c_str(); }
+extern "C" int b200_version(void) { return 100; }
+
+extern "C" int b200_read_fault(unsigned int* fault_out) {
+  if (!fault_out) return sdb_fail(B200_ERR_ARG, "b200_read_fault: null pointer");
+  unsigned int v = 0, zero = 0;
+  SDB_CUDA(cudaMemcpyFromSymbol(&v, sdb::g_fault, sizeof(v)));
+  SDB_CUDA(cudaMemcpyToSymbol(sdb::g_fault, &zero, sizeof(zero)));
+  *fault_out = v;
+  return B200_OK;
+}
+
+// model -------------------------------------------------------------------------------
+struct b200_model {
+  b200_model_config cfg;
+  std::vector<b200_layer_weights> layers;
+  std::vector<int> kind_index;  // index among layers of the same kind
+  std::vector<bool> layer_set;
+  const uint16_t* embed = nullptr;
+  const float* final_norm = nullptr;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+
+  int key_dim() const { return cfg.gdn_heads * cfg.gdn_dk; }
+  int value_dim() const { return cfg.gdn_heads * cfg.gdn_dv; }
+  int conv_dim() const { return 2 * key_dim() + value_dim(); }
+  int gdn_split() const { return conv_dim() + value_dim(); }
+  int attn_qkv() const { return 2 * cfg.attn_heads * cfg.head_dim + 2 * cfg.attn_kv_heads * cfg.head_dim; }
+  int attn_o_in() const { return cfg.attn_heads * cfg.head_dim; }
+  bool has_gdn() const {
+    for (int i = 0; i < cfg.n_layers; ++i)
+      if (cfg.layer_kind[i] == B200_LAYER_GDN) return true;
+    return false;
+  }
+  bool has_attn() const {
+    for (int i = 0; i < cfg.n_layers; ++i)
+      if (cfg.layer_kind[i] == B200_LAYER_ATTN) return true;
+    return false;
+  }
+};
+
+namespace {
+
+struct WsLayout {
+  size_t x, xn, big, ab, mid, q, k, v, total;
+  int big_cols, mid_cols;
+};
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+WsLayout layout(const b200_model& m, int T) {
+  WsLayout L{};
+  const auto& c = m.cfg;
+  L.big_cols = c.inter;
+  if (m.has_gdn()) L.big_cols = std::max(L.big_cols, m.gdn_split());
+  if (m.has_attn()) L.big_cols = std::max(L.big_cols, m.attn_qkv());
+  L.mid_cols = std::max(m.has_gdn() ? m.value_dim() : 0, m.has_attn() ? m.attn_o_in() : 0);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  L.x = take(size_t(T) * c.hidden * 4);
+  L.xn = take(size_t(T) * c.hidden * 2);
+  L.big = take(size_t(T) * L.big_cols * 2);
+  L.ab = take(size_t(T) * 2 * std::max(c.gdn_heads, 1) * 4);
+  L.mid = take(size_t(T) * std::max(L.mid_cols, 8) * 2);
+  const size_t kvb = size_t(T) * std::max(c.attn_kv_heads * c.head_dim, 8) * 2;
+  L.q = take(size_t(T) * std::max(m.attn_o_in(), 8) * 2);
+  L.k = take(kvb);
+  L.v = take(kvb);
+  L.total = off;
+  return L;
+}
+
+int check_qw(const b200_qweight& w, int n_min, int k, const char* what) {
+  if (!w.data || w.n < n_min || w.k != k || w.n % 256 != 0) {
+    std::string msg = std::string("b200_model_set_layer: bad weight ") + what;
+    return sdb_fail(B200_ERR_SHAPE, msg.c_str());
+  }
+  return B200_OK;
+}
+
+}  // namespace
+
+extern "C" int b200_model_create(const b200_model_config* cfg, b200_model** out) {
+  if (!cfg || !out) return sdb_fail(B200_ERR_ARG, "b200_model_create: null pointer");
+  if (cfg->n_layers <= 0 || cfg->n_layers > 64 || cfg->hidden % 128 != 0 || cfg->inter % 128 != 0)
+    return sdb_fail(B200_ERR_SHAPE, "b200_model_create: bad layer count or hidden/inter not a multiple of 128");
+  if (cfg->weight_format < 0 || cfg->weight_format > 3) return sdb_fail(B200_ERR_FORMAT, "b200_model_create: format");
+  auto* m = new b200_model();
+  m->cfg = *cfg;
+  m->layers.resize(cfg->n_layers);
+  m->layer_set.assign(cfg->n_layers, false);
+  m->kind_index.resize(cfg->n_layers);
+  int ng = 0, na = 0;
+  for (int i = 0; i < cfg->n_layers; ++i) {
+    if (cfg->layer_kind[i] == B200_LAYER_GDN) m->kind_index[i] = ng++;
+    else if (cfg->layer_kind[i] == B200_LAYER_ATTN) m->kind_index[i] = na++;
+    else {
+      delete m;
+      return sdb_fail(B200_ERR_ARG, "b200_model_create: unknown layer kind");
+    }
+  }
+  if (ng && (cfg->gdn_dk != 128 || cfg->gdn_dv != 128 || cfg->conv_width != 4)) {
+    delete m;
+    return sdb_fail(B200_ERR_UNSUPPORTED, "b200_model_create: GDN layers need dk = dv = 128, conv width 4");
+  }
+  *out = m;
+  return B200_OK;
+}
+
+extern "C" int b200_model_destroy(b200_model* m) {
+  delete m;
+  return B200_OK;
+}
+
+extern "C" int b200_model_set_layer(b200_model* m, int32_t layer, const b200_layer_weights* w) {
+  if (!m || !w) return sdb_fail(B200_ERR_ARG, "b200_model_set_layer: null pointer");
+  if (layer < 0 || layer >= m->cfg.n_layers) return sdb_fail(B200_ERR_ARG, "b200_model_set_layer: layer out of range");
+  const auto& c = m->cfg;
+  if (!w->input_norm || !w->post_norm) return sdb_fail(B200_ERR_ARG, "b200_model_set_layer: null norm");
+  const bool gdn = c.layer_kind[layer] == B200_LAYER_GDN;
+  int rc;
+  if (gdn) {
+    if ((rc = check_qw(w->mix_in, m->gdn_split() + 2 * c.gdn_heads, c.hidden, "mix_in"))) return rc;
+    if ((rc = check_qw(w->mix_out, c.hidden, m->value_dim(), "mix_out"))) return rc;
+    if (!w->gdn.conv_w || !w->gdn.a_log || !w->gdn.dt_bias || !w->gdn.norm_w)
+      return sdb_fail(B200_ERR_ARG, "b200_model_set_layer: null GDN parameter");
+  } else {
+    if ((rc = check_qw(w->mix_in, m->attn_qkv(), c.hidden, "mix_in"))) return rc;
+    if ((rc = check_qw(w->mix_out, c.hidden, m->attn_o_in(), "mix_out"))) return rc;
+    if (!w->q_norm || !w->k_norm) return sdb_fail(B200_ERR_ARG, "b200_model_set_layer: null q/k norm");
+  }
+  if ((rc = check_qw(w->gate_up, 2 * c.inter, c.hidden, "gate_up"))) return rc;
+  if ((rc = check_qw(w->down, c.hidden, c.inter, "down"))) return rc;
+  m->layers[layer] = *w;
+  if (gdn) {
+    m->layers[layer].gdn.heads = c.gdn_heads;
+    m->layers[layer].gdn.dk = c.gdn_dk;
+    m->layers[layer].gdn.dv = c.gdn_dv;
+    m->layers[layer].gdn.conv_width = c.conv_width;
+    m->layers[layer].gdn.eps = c.eps;
+  }
+  m->layer_set[layer] = true;
+  return B200_OK;
+}
+
+extern "C" int b200_model_set_globals(b200_model* m, const uint16_t* embed, const float* final_norm,
+                                      const float* rope_cos, const float* rope_sin) {
+  if (!m || !embed || !final_norm) return sdb_fail(B200_ERR_ARG, "b200_model_set_globals: null pointer");
+  if (m->has_attn() && (!rope_cos || !rope_sin)) return sdb_fail(B200_ERR_ARG, "b200_model_set_globals: rope tables");
+  m->embed = embed;
+  m->final_norm = final_norm;
+  m->rope_cos = rope_cos;
+  m->rope_sin = rope_sin;
+  return B200_OK;
+}
+
+extern "C" int b200_model_workspace_bytes(const b200_model* m, int32_t max_tokens, size_t* bytes) {
+  if (!m || !bytes || max_tokens <= 0) return sdb_fail(B200_ERR_ARG, "b200_model_workspace_bytes: bad argument");
+  *bytes = layout(*m, max_tokens).total;
+  return B200_OK;
+}
+
+extern "C" int b200_model_forward(b200_model* m, const int32_t* ids, const b200_seqs* seqs, const b200_prefix_pool* pool,
+                                  const b200_decide_args* decide, void* workspace, size_t workspace_bytes,
+                                  b200_stream stream) {
+  if (!m || !ids || !seqs || !workspace) return sdb_fail(B200_ERR_ARG, "b200_model_forward: null pointer");
+  if (!m->embed || !m->final_norm) return sdb_fail(B200_ERR_ARG, "b200_model_forward: globals not set");
+  for (int i = 0; i < m->cfg.n_layers; ++i)
+    if (!m->layer_set[i]) return sdb_fail(B200_ERR_ARG, "b200_model_forward: a layer has no weights");
+  const int T = seqs->n_tokens;
+  if (T <= 0 || seqs->n_seqs <= 0) return sdb_fail(B200_ERR_SHAPE, "b200_model_forward: empty batch");
+  const WsLayout L = layout(*m, T);
+  if (workspace_bytes < L.total) return sdb_fail(B200_ERR_WORKSPACE, "b200_model_forward: workspace too small");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return sdb_fail(B200_ERR_SHAPE, "b200_model_forward: workspace must be 256-byte aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const auto& c = m->cfg;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* x = reinterpret_cast<float*>(ws + L.x);
+  uint16_t* xn = reinterpret_cast<uint16_t*>(ws + L.xn);
+  uint16_t* big = reinterpret_cast<uint16_t*>(ws + L.big);
+  float* ab = reinterpret_cast<float*>(ws + L.ab);
+  uint16_t* mid = reinterpret_cast<uint16_t*>(ws + L.mid);
+  uint16_t* qb = reinterpret_cast<uint16_t*>(ws + L.q);
+  uint16_t* kb = reinterpret_cast<uint16_t*>(ws + L.k);
+  uint16_t* vb = reinterpret_cast<uint16_t*>(ws + L.v);
+
+  int rc;
+  if ((rc = sdb_embed_vocab(ids, T, m->embed, c.hidden, x, c.vocab, st))) return rc;
+  for (int li = 0; li < c.n_layers; ++li) {
+    const b200_layer_weights& w = m->layers[li];
+    if ((rc = b200_rmsnorm(x, T, c.hidden, w.input_norm, c.eps, xn, stream))) return rc;
+    if (c.layer_kind[li] == B200_LAYER_GDN) {
+      const int split = m->gdn_split();
+      b200_linear_out o{B200_EP_STORE, split + 2 * c.gdn_heads, big, split, ab, 2 * c.gdn_heads, split};
+      if ((rc = b200_linear(xn, T, c.hidden, c.hidden, &w.mix_in, &o, stream))) return rc;
+      if ((rc = sdb_gdn_mixer(&w.gdn, seqs, big, split, ab, mid, pool, m->kind_index[li], st))) return rc;
+      b200_linear_out r{B200_EP_RESID_ADD, c.hidden, x, c.hidden, nullptr, 0, c.hidden};
+      if ((rc = b200_linear(mid, T, m->value_dim(), m->value_dim(), &w.mix_out, &r, stream))) return rc;
+    } else {
+      const int n = m->attn_qkv();
+      b200_linear_out o{B200_EP_STORE, n, big, n, nullptr, 0, n};
+      if ((rc = b200_linear(xn, T, c.hidden, c.hidden, &w.mix_in, &o, stream))) return rc;
+      b200_attn_params ap{c.attn_heads, c.attn_kv_heads, c.head_dim, c.rope_dim, c.max_pos, c.eps,
+                          w.q_norm, w.k_norm, m->rope_cos, m->rope_sin};
+      if ((rc = sdb_attention(&ap, seqs, big, n, qb, kb, vb, mid, pool, m->kind_index[li], st))) return rc;
+      b200_linear_out r{B200_EP_RESID_ADD, c.hidden, x, c.hidden, nullptr, 0, c.hidden};
+      if ((rc = b200_linear(mid, T, m->attn_o_in(), m->attn_o_in(), &w.mix_out, &r, stream))) return rc;
+    }
+    if ((rc = b200_rmsnorm(x, T, c.hidden, w.post_norm, c.eps, xn, stream))) return rc;
+    b200_linear_out g{B200_EP_SWIGLU, 2 * c.inter, big, c.inter, nullptr, 0, 2 * c.inter};
+    if ((rc = b200_linear(xn, T, c.hidden, c.hidden, &w.gate_up, &g, stream))) return rc;
+    b200_linear_out d{B200_EP_RESID_ADD, c.hidden, x, c.hidden, nullptr, 0, c.hidden};
+    if ((rc = b200_linear(big, T, c.inter, c.inter, &w.down, &d, stream))) return rc;
+  }
+  if (decide && decide->n_rows > 0) {
+    if ((rc = sdb_decide_vocab(x, c.hidden, m->final_norm, c.eps, m->embed, decide, c.vocab, T, st))) return rc;
+  }
+  return B200_OK;
+}

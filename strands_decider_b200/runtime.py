@@ -1,0 +1,213 @@
+"""The device-side decision runtime: one model context, workspace and prefix pool per GPU.
+
+`DecisionModel` wraps `b200_model_forward` (the whole torso prefill plus the fused
+decision head, in native code) with the two paths of the reference engine:
+
+  full prompts   `score_prompts`  - each (state + question) row forwarded whole, as
+                 `SystemOneEngine._slot_probs_batched` (infer.py:253-279)
+  prefix cache   `score_requests` - each state forwarded once into a prefix-pool slot,
+                 then every question suffix forwarded against its state's slot, as
+                 `_slot_probs_shared_prefix` (infer.py:281-337), with no cache copies
+
+Batches are ragged and packed (no padding tokens are computed).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .config import ATTN, GDN, ModelSpec
+from .weights import DeviceWeights
+
+KIND = {"noul": 0, "choice": 1, "score": 2}
+
+
+def rope_tables(spec: ModelSpec, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin [max_positions, rope_dim/2] fp32, computed exactly as the reference computes
+    them on the CPU (TF:124-135 inverse frequencies, TF:144-153 position products)."""
+    dim = spec.rope_dim
+    inv = 1.0 / (spec.rope_theta ** (torch.arange(0, dim, 2, dtype=torch.int64).to(dtype=torch.float) / dim))
+    pos = torch.arange(spec.max_positions, dtype=torch.float32)
+    freqs = (inv[:, None].float() @ pos[None, :].float()).transpose(0, 1)
+    return freqs.cos().contiguous().to(device), freqs.sin().contiguous().to(device)
+
+
+@dataclass
+class Decisions:
+    """Per-row outputs of the fused head (device tensors)."""
+
+    probs: torch.Tensor       # [rows, kmax] fp32, masked slots 0
+    argmax: torch.Tensor      # [rows] int32
+    confidence: torch.Tensor  # [rows] fp32
+    score: torch.Tensor       # [rows] fp32
+
+    def cpu(self) -> Decisions:
+        return Decisions(self.probs.cpu(), self.argmax.cpu(), self.confidence.cpu(), self.score.cpu())
+
+
+class DecisionModel:
+    def __init__(self, weights: DeviceWeights, max_tokens: int = 8192, pool_slots: int = 64,
+                 pool_kv_tokens: int | None = None, device: str | torch.device = "cuda"):
+        _lib.load()
+        self.w = weights
+        self.spec = s = weights.spec
+        self.device = torch.device(device)
+        self.max_tokens = max_tokens
+        cfg = _lib.ModelConfig()
+        cfg.vocab, cfg.hidden, cfg.inter, cfg.n_layers = s.vocab, s.hidden, s.inter, s.n_layers
+        for i, lt in enumerate(s.layer_types):
+            cfg.layer_kind[i] = _lib.LAYER_GDN if lt == GDN else _lib.LAYER_ATTN
+        cfg.gdn_heads, cfg.gdn_dk, cfg.gdn_dv, cfg.conv_width = s.gdn_heads, s.gdn_dk, s.gdn_dv, s.conv_width
+        cfg.attn_heads, cfg.attn_kv_heads, cfg.head_dim = s.attn_heads, s.attn_kv_heads, s.head_dim
+        cfg.rope_dim, cfg.max_pos, cfg.eps = s.rope_dim, s.max_positions, s.eps
+        cfg.weight_format = _lib.FMT[s.weight_format]
+        self._cfg = cfg
+        h = C.c_void_p()
+        _lib.check(_lib.load().b200_model_create(C.byref(cfg), C.byref(h)))
+        self._h = h
+        self._layer_structs = []
+        for li in range(s.n_layers):
+            lw = weights.layer_struct(li)
+            self._layer_structs.append(lw)
+            _lib.check(_lib.load().b200_model_set_layer(h, li, C.byref(lw)))
+        self.rope_cos, self.rope_sin = rope_tables(s, self.device)
+        _lib.check(_lib.load().b200_model_set_globals(h, _lib.ptr(weights.embed), _lib.ptr(weights.final_norm),
+                                                      _lib.ptr(self.rope_cos), _lib.ptr(self.rope_sin)))
+        nbytes = C.c_size_t(0)
+        _lib.check(_lib.load().b200_model_workspace_bytes(h, max_tokens, C.byref(nbytes)))
+        self.workspace = torch.empty(int(nbytes.value), dtype=torch.uint8, device=self.device)
+        self._alloc_pool(pool_slots, pool_kv_tokens or pool_slots * 512)
+
+    # ------------------------------------------------------------------ pool
+    def _alloc_pool(self, slots: int, kv_tokens: int) -> None:
+        s, dev = self.spec, self.device
+        n_gdn = sum(1 for t in s.layer_types if t == GDN)
+        n_attn = sum(1 for t in s.layer_types if t == ATTN)
+        self.pool_slots, self.kv_capacity = slots, kv_tokens
+        self.gdn_state = torch.zeros(max(n_gdn, 1), slots, s.gdn_heads, s.gdn_dk, s.gdn_dv, device=dev)
+        self.conv_hist = torch.zeros(max(n_gdn, 1), slots, s.conv_width - 1, s.conv_dim, dtype=torch.bfloat16,
+                                     device=dev)
+        self.k_cache = torch.zeros(max(n_attn, 1), kv_tokens, s.attn_kv_heads, s.head_dim, dtype=torch.bfloat16,
+                                   device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.slot_len = torch.zeros(slots, dtype=torch.int32, device=dev)
+        self.slot_kv = torch.zeros(slots, dtype=torch.int32, device=dev)
+        self._pool = _lib.PrefixPool(slots, kv_tokens, _lib.ptr(self.slot_len), _lib.ptr(self.slot_kv),
+                                     _lib.ptr(self.gdn_state), _lib.ptr(self.conv_hist), _lib.ptr(self.k_cache),
+                                     _lib.ptr(self.v_cache))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.load().b200_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ------------------------------------------------------------------ raw forward
+    def forward(self, ids: torch.Tensor, cu: torch.Tensor, prefix_slot: torch.Tensor | None = None,
+                save_slot: torch.Tensor | None = None, decide: dict | None = None, max_len: int = 0,
+                stream: torch.cuda.Stream | None = None) -> Decisions | None:
+        """ids int32 [T], cu int32 [B+1] on the device; decide: dict of device tensors
+        (last_tok, opt_ids [R, kmax], n_opts, kinds, temps) -> Decisions."""
+        T = int(ids.numel())
+        B = int(cu.numel()) - 1
+        if T > self.max_tokens:
+            raise ValueError(f"batch of {T} tokens exceeds max_tokens={self.max_tokens}")
+        seqs = _lib.Seqs(B, T, max_len or T, _lib.ptr(cu), _lib.ptr(prefix_slot), _lib.ptr(save_slot))
+        dec = None
+        out = None
+        if decide is not None:
+            R, kmax = decide["opt_ids"].shape
+            out = Decisions(torch.empty(R, kmax, device=self.device), torch.empty(R, dtype=torch.int32,
+                            device=self.device), torch.empty(R, device=self.device), torch.empty(R, device=self.device))
+            dec = _lib.DecideArgs(R, kmax, _lib.ptr(decide["last_tok"]), _lib.ptr(decide["opt_ids"]),
+                                  _lib.ptr(decide["n_opts"]), _lib.ptr(decide["kinds"]), _lib.ptr(decide["temps"]),
+                                  float(decide.get("ordinal_smoothing", 0.0)), _lib.ptr(out.probs),
+                                  _lib.ptr(out.argmax), _lib.ptr(out.confidence), _lib.ptr(out.score))
+        _lib.check(_lib.load().b200_model_forward(
+            self._h, _lib.ptr(ids), C.byref(seqs), C.byref(self._pool), C.byref(dec) if dec is not None else None,
+            _lib.ptr(self.workspace), self.workspace.numel(), _lib.stream_ptr(stream)))
+        return out
+
+    def residual(self, n_tokens: int) -> torch.Tensor:
+        """The fp32 residual stream [T, hidden] the last forward left at the workspace start."""
+        return self.workspace[: n_tokens * self.spec.hidden * 4].view(torch.float32).view(n_tokens, self.spec.hidden)
+
+    # ------------------------------------------------------------------ packing helpers
+    def _dev(self, x, dtype=torch.int32) -> torch.Tensor:
+        return torch.as_tensor(x, dtype=dtype).to(self.device, non_blocking=True)
+
+    @staticmethod
+    def _pack(rows: list[list[int]]) -> tuple[list[int], list[int]]:
+        cu = [0]
+        flat: list[int] = []
+        for r in rows:
+            if not r:
+                raise ValueError("every sequence must have at least one token")
+            flat.extend(r)
+            cu.append(len(flat))
+        return flat, cu
+
+    def _decide_dict(self, last_tok, opt_ids, n_opts, kinds, temps, ordinal_smoothing=0.0) -> dict:
+        kmax = max(max(len(o) for o in opt_ids), 1)
+        if kmax > 16:
+            raise ValueError("the option-token head reads at most 16 options")
+        padded = [list(o) + [0] * (kmax - len(o)) for o in opt_ids]
+        return {"last_tok": self._dev(last_tok), "opt_ids": self._dev(padded), "n_opts": self._dev(n_opts),
+                "kinds": self._dev([KIND.get(k, k) if isinstance(k, str) else int(k) for k in kinds]),
+                "temps": self._dev(temps, torch.float32), "ordinal_smoothing": ordinal_smoothing}
+
+    # ------------------------------------------------------------------ the two reference paths
+    def score_prompts(self, rows: list[list[int]], opt_ids, n_opts, kinds, temps, ordinal_smoothing=0.0,
+                      stream=None) -> Decisions:
+        """Full-prompt path: every row is a whole (state + question) prompt."""
+        flat, cu = self._pack(rows)
+        d = self._decide_dict([c - 1 for c in cu[1:]], opt_ids, n_opts, kinds, temps, ordinal_smoothing)
+        return self.forward(self._dev(flat), self._dev(cu), decide=d, max_len=max(map(len, rows)), stream=stream)
+
+    def prefill_states(self, states: list[list[int]], slots: list[int], stream=None) -> None:
+        """Forward each state once and keep its cache in the given pool slots."""
+        if max(slots) >= self.pool_slots:
+            raise ValueError("pool slot out of range")
+        flat, cu = self._pack(states)
+        if cu[-1] > self.kv_capacity:
+            raise ValueError("states exceed the pool's KV capacity")
+        kv = torch.zeros(self.pool_slots, dtype=torch.int32)
+        for s, c in zip(slots, cu[:-1]):
+            kv[s] = c
+        self.slot_kv.copy_(kv.to(self.device, non_blocking=True))
+        self.forward(self._dev(flat), self._dev(cu), save_slot=self._dev(slots), max_len=max(map(len, states)),
+                     stream=stream)
+
+    def score_suffixes(self, suffixes: list[list[int]], slots: list[int], opt_ids, n_opts, kinds, temps,
+                       ordinal_smoothing=0.0, stream=None) -> Decisions:
+        """Forward question suffixes against their states' pool slots and decide."""
+        flat, cu = self._pack(suffixes)
+        d = self._decide_dict([c - 1 for c in cu[1:]], opt_ids, n_opts, kinds, temps, ordinal_smoothing)
+        return self.forward(self._dev(flat), self._dev(cu), prefix_slot=self._dev(slots), decide=d,
+                            max_len=max(map(len, suffixes)), stream=stream)
+
+    def score_requests(self, requests: list[dict], temps_by_kind: dict | None = None,
+                       ordinal_smoothing: float = 0.0, stream=None) -> Decisions:
+        """Requests {state, questions, kinds, n_opts, opt_ids}: the prefix-cache path."""
+        temps_by_kind = temps_by_kind or {}
+        slots = list(range(len(requests)))
+        self.prefill_states([r["state"] for r in requests], slots, stream=stream)
+        suf, sl, opt, nopt, kinds, temps = [], [], [], [], [], []
+        for s, r in zip(slots, requests):
+            for qi, q in enumerate(r["questions"]):
+                suf.append(q)
+                sl.append(s)
+                opt.append(r["opt_ids"][qi])
+                nopt.append(r["n_opts"][qi])
+                kinds.append(r["kinds"][qi])
+                temps.append(float(temps_by_kind.get(r["kinds"][qi], 1.0)))
+        return self.score_suffixes(suf, sl, opt, nopt, kinds, temps, ordinal_smoothing, stream=stream)

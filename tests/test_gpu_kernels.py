@@ -1,0 +1,239 @@
+"""Kernel-level parity on the B200: every comparison runs the CUDA path through the C ABI
+against the CPU oracle (bit-exact for the integer/byte work, stated tolerances for fp)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant as Q
+
+pytestmark = pytest.mark.gpu
+
+FORMATS = ["int4", "nvfp4", "ternary", "bf16"]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.fail("the -m gpu tests need a CUDA device")
+    from strands_decider_b200 import _lib
+
+    _lib.load()
+    yield
+    torch.cuda.synchronize()
+    assert _lib.read_fault() == 0, "a device-side bounded wait or index check fired"
+
+
+def _weights(n, k, seed=0, zero_row=3):
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(n, k, generator=g) * 0.02
+    w[zero_row] = 0.0
+    w[5, :16] = 0.0        # an all-zero NVFP4 block / partial int4 group
+    w[7, 0] = 0.3          # an outlier
+    return w
+
+
+@pytest.mark.parametrize("fmt", ["int4", "nvfp4", "ternary"])
+def test_quantize_bit_exact(fmt):
+    from strands_decider_b200 import weights as W
+
+    w = _weights(384, 1024)
+    pw = W.quantize(fmt, w.cuda())
+    got = W.packed_to_numpy(pw)
+    want = Q.quantize(fmt, w.numpy())
+    assert np.array_equal(got["data"].view(np.uint8), want["data"].view(np.uint8))
+    assert np.array_equal(np.asarray(got["scales"]).view(np.uint8), np.asarray(want["scales"]).view(np.uint8))
+    if fmt == "nvfp4":
+        assert np.array_equal(pw.row_scale.cpu().numpy(), np.full(384, want["global_scale"][0], np.float32))
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_dequantize_bit_exact(fmt):
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    w = _weights(256, 512, seed=1)
+    pw = W.quantize(fmt, w.cuda())
+    out = torch.empty(256, 512, dtype=torch.int16, device="cuda")
+    qw = pw.qweight()
+    _lib.call("b200_dequantize", _ref(qw), _lib.ptr(out), _lib.stream_ptr())
+    got = out.cpu().numpy().view(np.uint16)
+    want = Q.f32_to_bf16_bits(Q.dequantize(fmt, W.packed_to_numpy(pw)))
+    assert np.array_equal(got, want)
+
+
+def _ref(s):
+    import ctypes as C
+
+    return C.byref(s)
+
+
+def _linear(fn, x, pw, ep, n_valid=None, split=None):
+    """Run b200_linear / b200_linear_simt; returns (bf16-or-fp32 out, fp32 out or None)."""
+    from strands_decider_b200 import _lib
+
+    m, k = x.shape
+    n_valid = n_valid or pw.n
+    f32 = None
+    if ep == _lib.EP_STORE:
+        split = n_valid if split is None else split
+        out = torch.zeros(m, split, dtype=torch.bfloat16, device="cuda")
+        ldo = split
+        if split < n_valid:
+            f32 = torch.zeros(m, n_valid - split, device="cuda")
+    elif ep == _lib.EP_RESID_ADD:
+        out = torch.randn(m, n_valid, device="cuda")
+        ldo = n_valid
+        split = n_valid
+    else:
+        out = torch.zeros(m, n_valid // 2, dtype=torch.bfloat16, device="cuda")
+        ldo = n_valid // 2
+        split = n_valid
+    before = out.clone()
+    o = _lib.LinearOut(ep, n_valid, _lib.ptr(out), ldo, _lib.ptr(f32) if f32 is not None else None,
+                       (n_valid - split) if f32 is not None else 0, split)
+    qw = pw.qweight()
+    _lib.call(fn, _lib.ptr(x), m, k, k, _ref(qw), _ref(o), _lib.stream_ptr())
+    torch.cuda.synchronize()
+    return out, f32, before
+
+
+def _reference(x, pw):
+    from strands_decider_b200 import weights as W
+
+    wd = torch.from_numpy(Q.dequantize(pw.fmt, W.packed_to_numpy(pw)))
+    return x.float().cpu().double() @ wd.double().T
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("m", [1, 77, 128, 300])
+def test_linear_store_matches_reference(fmt, m):
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    k, n = 1024, 512
+    x = (torch.randn(m, k, generator=torch.Generator().manual_seed(m)) ).to(torch.bfloat16).cuda()
+    pw = W.concat_rows([W.quantize(fmt, _weights(n - 40, k, seed=2).cuda())])   # n_valid < n (padding)
+    ref = _reference(x, pw)[:, : n - 40]
+    for fn in ("b200_linear", "b200_linear_simt"):
+        out, _, _ = _linear(fn, x, pw, _lib.EP_STORE, n_valid=n - 40)
+        got = out[:, : n - 40].float().cpu().double()
+        err = (got - ref).abs().max().item() / ref.abs().max().item()
+        assert err < 8e-3, (fn, err)
+
+
+@pytest.mark.parametrize("fmt", ["int4", "nvfp4"])
+def test_linear_split_store_writes_fp32_tail(fmt):
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    k, n_valid, split = 1024, 544, 512
+    x = torch.randn(200, k).to(torch.bfloat16).cuda()
+    pw = W.concat_rows([W.quantize(fmt, _weights(n_valid, k, seed=3).cuda())])
+    ref = _reference(x, pw)
+    out, f32, _ = _linear("b200_linear", x, pw, _lib.EP_STORE, n_valid=n_valid, split=split)
+    tail = f32.cpu().double()
+    assert (tail - ref[:, split:n_valid]).abs().max().item() < 1e-4 * ref.abs().max().item() + 1e-5
+    head = out.float().cpu().double()
+    assert (head - ref[:, :split]).abs().max().item() / ref.abs().max().item() < 8e-3
+
+
+@pytest.mark.parametrize("fmt", ["int4", "ternary"])
+def test_linear_residual_add(fmt):
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    k, n = 2048, 512
+    x = torch.randn(130, k).to(torch.bfloat16).cuda()
+    pw = W.concat_rows([W.quantize(fmt, _weights(n, k, seed=4).cuda())])
+    ref = _reference(x, pw)
+    for fn in ("b200_linear", "b200_linear_simt"):
+        out, _, before = _linear(fn, x, pw, _lib.EP_RESID_ADD)
+        got = (out - before).cpu().double()
+        assert (got - ref).abs().max().item() < 2e-4 * ref.abs().max().item() + 1e-5, fn
+
+
+@pytest.mark.parametrize("fmt", ["int4", "nvfp4"])
+def test_linear_swiglu(fmt):
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    k, inter = 1024, 384
+    x = torch.randn(150, k).to(torch.bfloat16).cuda()
+    gate = W.quantize(fmt, _weights(inter, k, seed=5).cuda())
+    up = W.quantize(fmt, _weights(inter, k, seed=6).cuda())
+    pw = W.interleave_gate_up(gate, up)
+    g = _reference(x, gate)
+    u = _reference(x, up)
+    ref = torch.nn.functional.silu(g) * u
+    for fn in ("b200_linear", "b200_linear_simt"):
+        out, _, _ = _linear(fn, x, pw, _lib.EP_SWIGLU, n_valid=2 * inter)
+        got = out.float().cpu().double()
+        assert (got - ref).abs().max().item() / ref.abs().max().item() < 1e-2, fn
+
+
+def test_linear_rejects_bad_shapes():
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    pw = W.concat_rows([W.quantize("int4", _weights(256, 1024).cuda())])
+    x = torch.zeros(4, 1000, dtype=torch.bfloat16, device="cuda")
+    o = _lib.LinearOut(0, 256, _lib.ptr(torch.zeros(4, 256, dtype=torch.bfloat16, device="cuda")), 256, None, 0, 256)
+    with pytest.raises(_lib.B200Error) as e:
+        _lib.call("b200_linear", _lib.ptr(x), 4, 1000, 1000, _ref(pw.qweight()), _ref(o), _lib.stream_ptr())
+    assert e.value.status == 2
+
+
+# ----------------------------------------------------------------------------- GDN mixer
+
+
+def test_gdn_mixer_matches_oracle_chunk_rule():
+    """conv + gating + chunked delta rule + gated norm, ragged sequences, against the
+    oracle's restatement of TF:462-530 on the same bf16 inputs."""
+    import torch.nn.functional as F
+
+    from oracle import torso as T
+    from strands_decider_b200 import _lib
+
+    H, dk = 2, 128
+    conv_dim, vdim = 3 * H * dk, H * dk
+    g = torch.Generator().manual_seed(0)
+    lens = [1, 31, 32, 33, 100]
+    Ttot = sum(lens)
+    mix = (torch.randn(Ttot, conv_dim + vdim, generator=g)).to(torch.bfloat16)
+    ab = torch.randn(Ttot, 2 * H, generator=g)
+    conv_w = torch.rand(conv_dim, 4, generator=g) - 0.5
+    a_log = torch.log(torch.rand(H, generator=g) * 0.99 + 0.01)
+    dt_bias = torch.ones(H)
+    norm_w = 1 + 0.1 * torch.randn(dk, generator=g)
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    out = torch.zeros(Ttot, vdim, dtype=torch.bfloat16, device="cuda")
+    keep = [conv_w.cuda(), a_log.cuda(), dt_bias.cuda(), norm_w.cuda()]
+    p = _lib.GdnParams(H, 128, 128, 4, 1e-6, *[_lib.ptr(t) for t in keep])
+    cu_d = torch.tensor(cu, dtype=torch.int32, device="cuda")
+    seqs = _lib.Seqs(len(lens), Ttot, max(lens), _lib.ptr(cu_d), None, None)
+    mix_d, ab_d = mix.cuda(), ab.cuda()
+    _lib.call("b200_gdn_mixer", _ref(p), _ref(seqs), _lib.ptr(mix_d), conv_dim + vdim, _lib.ptr(ab_d),
+              _lib.ptr(out), None, 0, _lib.stream_ptr())
+    torch.cuda.synchronize()
+    got = out.float().cpu()
+    for i, n in enumerate(lens):
+        rows = slice(cu[i], cu[i + 1])
+        x = mix[rows].float()
+        conv = torch.zeros(n, conv_dim)
+        xin = torch.cat([torch.zeros(3, conv_dim), x[:, :conv_dim]], 0)
+        for j in range(4):
+            conv = conv + xin[j:j + n] * conv_w[:, j]
+        conv = F.silu(conv)
+        q, k, v = conv[:, :H * dk].view(n, H, dk), conv[:, H * dk:2 * H * dk].view(n, H, dk), conv[:, 2 * H * dk:].view(n, H, dk)
+        beta = ab[rows, :H].sigmoid()
+        gg = -a_log.exp() * F.softplus(ab[rows, H:] + dt_bias)
+        o, _ = T.chunk_gated_delta_rule(q, k, v, gg, beta)
+        z = x[:, conv_dim:].reshape(-1, dk)
+        want = T.gated_rms_norm(o.reshape(-1, dk), z, norm_w, 1e-6).reshape(n, vdim)
+        err = (got[rows] - want).abs().max().item() / (want.abs().max().item() + 1e-6)
+        assert err < 2e-2, (n, err)

@@ -1,0 +1,135 @@
+"""Whole-torso parity on the B200: the native prefill + fused decision head against the
+reference's own outputs (golden fixtures) and the CPU oracle.
+
+Tolerance (BASELINE correctness bar): option probabilities within 2e-3 absolute of the
+reference, identical argmax; packed weights bit-exact to the CPU quantiser."""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import head as OH
+from oracle import synth as osynth
+from oracle import torso as OT
+from strands_decider_b200 import config
+from tests.conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+PROB_TOL = 2e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.fail("the -m gpu tests need a CUDA device")
+    from strands_decider_b200 import _lib
+
+    _lib.load()
+    yield
+    torch.cuda.synchronize()
+    assert _lib.read_fault() == 0
+
+
+def _model(spec, seed, fmt=None, max_tokens=4096, slots=16):
+    from strands_decider_b200.runtime import DecisionModel
+    from strands_decider_b200.weights import DeviceWeights
+
+    spec = spec.with_format(fmt) if fmt else spec
+    w = DeviceWeights.synthetic(spec, seed=seed, latent_device="cpu", keep_logical=True)
+    return DecisionModel(w, max_tokens=max_tokens, pool_slots=slots, pool_kv_tokens=max_tokens)
+
+
+def _logical_digest(model):
+    from strands_decider_b200.weights import packed_to_numpy
+
+    return osynth.packed_digest({k: packed_to_numpy(v) for k, v in model.w.logical.items()})
+
+
+def test_reduced_decider_matches_reference_golden():
+    """4 x 256 ids on the reduced int4 decider (the reference's CPU-runnable config)."""
+    g = np.load(os.path.join(GOLDEN, "reduced_1024_int4.npz"))
+    m = _model(config.REDUCED_1024, seed=0)
+    assert _logical_digest(m) == str(g["packed_digest"]), "device quantisation differs from the CPU quantiser"
+    rows = g["ids"].tolist()
+    out = m.score_prompts(rows, [[11, 12, 13]] * 4, [3] * 4, ["choice"] * 4, [1.0] * 4).cpu()
+    want = g["probs"]
+    assert np.abs(out.probs.numpy() - want).max() < PROB_TOL, (out.probs, want)
+    assert np.array_equal(out.argmax.numpy(), want.argmax(1))
+
+
+@pytest.mark.parametrize("fmt", ["int4", "nvfp4", "ternary"])
+def test_tiny_ragged_matches_reference_golden(fmt):
+    """Ragged prompts, mixed option counts, kinds and temperatures on the tiny spec."""
+    g = np.load(os.path.join(GOLDEN, f"tiny_{fmt}_ragged.npz"))
+    m = _model(config.TINY, seed=1, fmt=fmt)
+    assert _logical_digest(m) == str(g["packed_digest"])
+    s0, s1 = g["state0"].tolist(), g["state1"].tolist()
+    rows = [s0 + g["q0"].tolist(), s0 + g["q1"].tolist(), s1 + g["q2"].tolist(), s1 + g["q3"].tolist()]
+    nopt = g["n_opts"].tolist()
+    opt = [g["opt_ids"][i, :n].tolist() for i, n in enumerate(nopt)]
+    kinds = ["choice", "noul", "score", "choice"]
+    out = m.score_prompts(rows, opt, nopt, kinds, g["temps"].tolist()).cpu()
+    want = g["probs"]
+    assert np.abs(out.probs.numpy() - want[:, : out.probs.shape[1]]).max() < PROB_TOL
+    for i, n in enumerate(nopt):
+        assert int(out.argmax[i]) == int(want[i, :n].argmax())
+    # derived answer numbers against the reference formulas on the reference's probabilities
+    ref = OH.device_style_outputs(torch.from_numpy(want), [0 if k == "noul" else 1 if k == "choice" else 2
+                                                           for k in kinds], nopt)
+    assert torch.allclose(out.confidence, ref["confidence"], atol=5e-3)
+    assert torch.allclose(out.score, ref["score"], atol=5e-3)
+    if fmt == "int4":  # hidden states at every position, after the final norm
+        hid = g["hidden"]
+        resid = m.residual(sum(map(len, rows))).cpu()
+        off = 0
+        for i, r in enumerate(rows):
+            x = resid[off:off + len(r)]
+            normed = OT.rms_norm_1p(x, m.w.final_norm.cpu(), 1e-6)
+            ref_h = torch.from_numpy(hid[i, : len(r)])
+            rel = ((normed - ref_h).norm(dim=1) / ref_h.norm(dim=1)).max().item()
+            assert rel < 2e-2, (i, rel)
+            off += len(r)
+
+
+def test_prefix_cache_equals_full_prompt_on_device():
+    """The shared-prefix path (state once into a pool slot, suffixes read it in place)
+    equals the full-prompt path (tests/test_prefix_cache.py:43-64 of the reference),
+    including states shorter than the conv width and suffixes crossing chunk bounds."""
+    m = _model(config.TINY, seed=1, fmt="int4")
+    g = torch.Generator().manual_seed(3)
+    V = config.TINY.vocab
+    reqs = []
+    for slen, qlens in [(70, [9, 1, 40]), (2, [3, 5]), (33, [64]), (1, [2, 31])]:
+        st = torch.randint(0, V, (slen,), generator=g).tolist()
+        qs = [torch.randint(0, V, (n,), generator=g).tolist() for n in qlens]
+        reqs.append({"state": st, "questions": qs, "kinds": [1] * len(qs), "n_opts": [3] * len(qs),
+                     "opt_ids": [[11, 12, 13]] * len(qs)})
+    cached = m.score_requests(reqs).cpu()
+    rows = [r["state"] + q for r in reqs for q in r["questions"]]
+    n = len(rows)
+    full = m.score_prompts(rows, [[11, 12, 13]] * n, [3] * n, [1] * n, [1.0] * n).cpu()
+    assert torch.abs(cached.probs - full.probs).max().item() < 1e-3
+    assert torch.equal(cached.argmax, full.argmax)
+
+
+def test_oracle_prefix_path_matches_device_prefix_path():
+    """Same requests through the oracle's explicit cache and the device pool."""
+    m = _model(config.TINY, seed=1, fmt="nvfp4")
+    W = osynth.logical_weights(config.TINY, seed=1, fmt="nvfp4")
+    cfg = osynth.torso_config(config.TINY)
+    g = torch.Generator().manual_seed(4)
+    V = config.TINY.vocab
+    st = torch.randint(0, V, (90,), generator=g)
+    qs = [torch.randint(0, V, (n,), generator=g) for n in (12, 40)]
+    _, cache = OT.forward_sequence(cfg, W, st, keep_cache=True)
+    pooled = torch.stack([OT.forward_sequence(cfg, W, q, cache=cache)[0][-1] for q in qs])
+    want = OH.decide(pooled, W["embed"], torch.tensor([[11, 12, 13, 14]] * 2), torch.tensor([4, 4]),
+                     torch.tensor([1.0, 1.0]))
+    got = m.score_requests([{"state": st.tolist(), "questions": [q.tolist() for q in qs], "kinds": [1, 1],
+                             "n_opts": [4, 4], "opt_ids": [[11, 12, 13, 14]] * 2}]).cpu()
+    assert torch.abs(got.probs - want).max().item() < PROB_TOL
