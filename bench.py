@@ -200,21 +200,26 @@ def run_step(model, b: Batch, stream) -> object:
 
 def gemm_roofline(model, tokens: int, pk: dict, reps: int = 20) -> dict:
     """Time the dominant kernel (the gate/up projection GEMM with its SwiGLU epilogue, the
-    largest GEMM of every layer) alone with CUDA events at a state-prefill batch's M."""
+    largest GEMM of every layer) alone with CUDA events at a state-prefill batch's M.
+
+    achieved = algorithmic FLOPs (2 M N K) / time. The activations enter as two bf16 planes
+    (hi + lo, fp32-level precision), so the tensor pipe executes 2x the algorithmic FLOPs;
+    frac is against the measured bf16 peak and is therefore bounded by 0.5."""
     import ctypes as C
 
     from strands_decider_b200 import _lib
 
     s = model.spec
     pw = model.w.layers[0]["gate_up"]
-    x = torch.randn(tokens, s.hidden, device="cuda").to(torch.bfloat16)
-    out = torch.empty(tokens, s.inter, dtype=torch.bfloat16, device="cuda")
-    o = _lib.LinearOut(_lib.EP_SWIGLU, 2 * s.inter, _lib.ptr(out), s.inter, None, 0, 2 * s.inter)
+    xp = torch.randn(2, tokens, s.hidden, device="cuda").to(torch.bfloat16)
+    out = torch.empty(2, tokens, s.inter, dtype=torch.bfloat16, device="cuda")
+    o = _lib.LinearOut(_lib.EP_SWIGLU, 2 * s.inter, _lib.ptr(out), s.inter, tokens * s.inter)
     qw = pw.qweight()
     st = torch.cuda.current_stream()
 
     def launch():
-        _lib.call("b200_linear", _lib.ptr(x), tokens, s.hidden, s.hidden, C.byref(qw), C.byref(o), st.cuda_stream)
+        _lib.call("b200_linear", _lib.ptr(xp[0]), _lib.ptr(xp[1]), tokens, s.hidden, s.hidden, C.byref(qw),
+                  C.byref(o), st.cuda_stream)
 
     for _ in range(3):
         launch()
@@ -236,8 +241,9 @@ def gemm_roofline(model, tokens: int, pk: dict, reps: int = 20) -> dict:
             traffic = per_tok * tokens
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
             "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": traffic,
-            "kernel": f"gemm_tc_kernel<256,nvfp4,swiglu> M={tokens} N={2 * s.inter} K={s.hidden}",
-            "ms_per_launch": round(ms, 4), "peak_src": pk["src"] + " bf16 burst (MMA kind::f16)"}
+            "kernel": f"gemm_tc_kernel<256,nvfp4,swiglu,split> M={tokens} N={2 * s.inter} K={s.hidden}",
+            "ms_per_launch": round(ms, 4), "mma_flops_per_algorithmic_flop": 2,
+            "peak_src": pk["src"] + " bf16 burst (tcgen05 kind::f16)"}
 
 
 def main() -> None:

@@ -69,6 +69,11 @@ typedef struct b200_qweight {
   const void* data;
   const void* scales;
   const float* row_scale; /* NVFP4 only, else NULL */
+  /* The GEMM's streaming copy of data/scales (b200_tile_weights): one contiguous chunk per
+   * (256-row tile, 64-column stage), so each stage is one bulk copy. Required by
+   * b200_linear for the packed formats; NULL for bf16 (read through a tensor map). */
+  const void* tiles;
+  const void* tile_scales;
 } b200_qweight;
 
 /* Quantise an fp32 weight w[n, k] (one logical nn.Linear) into `format`; writes data,
@@ -77,18 +82,26 @@ int b200_quantize(int32_t format, const float* w, int32_t n, int32_t k, void* da
                   float* row_scale, b200_stream stream);
 /* Unpack a packed weight to bf16 out[n, k], exactly as the GEMM's shared-memory unpacker. */
 int b200_dequantize(const b200_qweight* w, uint16_t* out, b200_stream stream);
+/* Bytes of the streaming copy of a packed [n, k] weight (n % 256 == 0, k % 128 == 0). */
+int b200_tile_bytes(int32_t format, int32_t n, int32_t k, size_t* tile_bytes, size_t* tile_scale_bytes);
+/* Write the streaming copy: tiles[n/256][k/64][256 rows][row bytes of 64 columns] and, for
+ * int4 / NVFP4, tile_scales[n/256][k/64][256 rows][scale bytes of 64 columns]. */
+int b200_tile_weights(const b200_qweight* w, void* tiles, void* tile_scales, b200_stream stream);
 
 /* ---------------------------------------------------------------- linear (GEMM)
- * y = x @ dequant(W)^T with a fused epilogue. x is bf16 [m, k] row-major (leading dim
- * ldx, a multiple of 8); fp32 accumulation in tensor memory (tcgen05 on sm_100a).
+ * y = x @ dequant(W)^T with a fused epilogue, fp32 accumulation in tensor memory (tcgen05
+ * on sm_100a). Activations carry fp32-level precision as two bf16 planes, x = x_hi + x_lo
+ * (x_hi = bf16_rn(x), x_lo = bf16_rn(x - x_hi)); the tensor cores run one bf16 MMA per
+ * plane into the same accumulator. Each plane is bf16 [m, ldx] row-major (ldx a multiple of
+ * 8, 16-byte aligned). x_lo may be NULL for a single bf16 pass.
  * Replaces one or several `nn.Linear` calls plus the elementwise op that follows them:
- *   B200_EP_STORE     out bf16 [m, ldo] for columns < split_n; columns >= split_n go to
- *                     out_f32 [m, ldo_f32] at column (col - split_n) in fp32
- *                     (GDN in-projection: qkv and z in bf16, b and a in fp32, TF:442-449)
+ *   B200_EP_STORE     out fp32 [m, ldo] = y  (the in-projections TF:442-449, TF:658-665)
  *   B200_EP_RESID_ADD out fp32 [m, ldo] += y (the residual adds of TF:775 and TF:781)
- *   B200_EP_SWIGLU    W rows interleaved in blocks of 64 (gate, up); out bf16 [m, ldo]
- *                     column j = silu(y[64*(2b)+i]) * y[64*(2b+1)+i], j = 64*b + i (TF:707)
- * Only columns < n_valid are written. */
+ *   B200_EP_SWIGLU    W rows interleaved in blocks of 64 (gate, up); h[:, 64b+i] =
+ *                     silu(y[:, 128b+i]) * y[:, 128b+64+i] (TF:707), written as the two bf16
+ *                     planes of the next GEMM's input: hi at out [m, ldo], lo at
+ *                     out + lo_offset (lo_offset 0: hi plane only)
+ * Only columns < n_valid are written (n_valid a multiple of 32; of 128 for SwiGLU). */
 enum b200_epilogue { B200_EP_STORE = 0, B200_EP_RESID_ADD = 1, B200_EP_SWIGLU = 2 };
 
 typedef struct b200_linear_out {
@@ -96,16 +109,14 @@ typedef struct b200_linear_out {
   int32_t n_valid;
   void* out;
   int32_t ldo;
-  float* out_f32;
-  int32_t ldo_f32;
-  int32_t split_n;
+  int64_t lo_offset;
 } b200_linear_out;
 
-int b200_linear(const uint16_t* x, int32_t m, int32_t k, int32_t ldx, const b200_qweight* w,
-                const b200_linear_out* out, b200_stream stream);
+int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m, int32_t k, int32_t ldx,
+                const b200_qweight* w, const b200_linear_out* out, b200_stream stream);
 /* Same contract on plain CUDA cores (fp32 FMA), used by the tests to cross-check b200_linear. */
-int b200_linear_simt(const uint16_t* x, int32_t m, int32_t k, int32_t ldx, const b200_qweight* w,
-                     const b200_linear_out* out, b200_stream stream);
+int b200_linear_simt(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m, int32_t k, int32_t ldx,
+                     const b200_qweight* w, const b200_linear_out* out, b200_stream stream);
 
 /* ---------------------------------------------------------------- ragged batches, prefix cache */
 typedef struct b200_seqs {
@@ -128,7 +139,7 @@ typedef struct b200_prefix_pool {
   int32_t* slot_len;       /* [n_slots]: cached length (positions); written by saving prefills */
   const int32_t* slot_kv;  /* [n_slots]: token offset of the slot's keys in k_cache / v_cache (host-assigned) */
   float* gdn_state;        /* [n_gdn_layers][n_slots][heads][dk][dv] fp32 (TF:285-305 state) */
-  uint16_t* conv_hist;     /* [n_gdn_layers][n_slots][conv_width-1][conv_dim] bf16 (TF:462-464) */
+  float* conv_hist;        /* [n_gdn_layers][n_slots][conv_width-1][conv_dim] fp32 (TF:462-464) */
   uint16_t* k_cache;       /* [n_attn_layers][kv_capacity][kv_heads][head_dim] bf16, post norm+RoPE */
   uint16_t* v_cache;       /* [n_attn_layers][kv_capacity][kv_heads][head_dim] bf16 */
 } b200_prefix_pool;
@@ -139,16 +150,18 @@ typedef struct b200_prefix_pool {
 int b200_embed(const int32_t* ids, int32_t n_tokens, const uint16_t* table, int32_t hidden, float* x,
                b200_stream stream);
 
-/* out = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w)) per row (Qwen3_5RMSNorm, TF:711-728). */
+/* y = x * rsqrt(mean(x^2) + eps) * (1 + w) per row (Qwen3_5RMSNorm, TF:711-728), written
+ * as the two bf16 planes of a GEMM input: hi at out [rows, hidden], lo at out + lo_offset. */
 int b200_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
-                 b200_stream stream);
+                 int64_t lo_offset, b200_stream stream);
 
 /* One Gated-DeltaNet token mixer after its in-projection (TF:462-530): depthwise causal
  * conv (width conv_width) + SiLU, q/k l2norm, beta = sigmoid(b), g = -exp(A_log) *
  * softplus(a + dt_bias), the chunked gated delta rule (TF:234-311) from the prefix slot's
- * state, and the gated RMSNorm (TF:175-190). mix: bf16 [tokens, ld_mix] holding
- * [q | k | v | z] columns; ab: fp32 [tokens, 2*heads] holding [b | a]; out: bf16
- * [tokens, heads*dv]. gdn_layer indexes the pool's GDN arrays. */
+ * state, and the gated RMSNorm (TF:175-190). mix: fp32 [tokens, ld_mix] holding the
+ * in-projection's [q | k | v | z | b | a] columns; out: the two bf16 planes of the
+ * out-projection's input, hi [tokens, heads*dv] and lo at out + lo_offset. gdn_layer
+ * indexes the pool's GDN arrays. */
 typedef struct b200_gdn_params {
   int32_t heads, dk, dv, conv_width;
   float eps;
@@ -158,16 +171,16 @@ typedef struct b200_gdn_params {
   const float* norm_w;   /* [dv] */
 } b200_gdn_params;
 
-int b200_gdn_mixer(const b200_gdn_params* p, const b200_seqs* seqs, const uint16_t* mix, int32_t ld_mix,
-                   const float* ab, uint16_t* out, const b200_prefix_pool* pool, int32_t gdn_layer,
+int b200_gdn_mixer(const b200_gdn_params* p, const b200_seqs* seqs, const float* mix, int32_t ld_mix,
+                   uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool, int32_t gdn_layer,
                    b200_stream stream);
 
 /* Gated GQA attention after its qkv projection (TF:647-690): per-head q/k RMSNorm(1+w),
  * partial RoPE on the first rope_dim dims (cos/sin tables [max_pos][rope_dim/2]), causal
  * softmax attention over the prefix slot's keys and the sequence's own, times
- * sigmoid(gate). qkv: bf16 [tokens, ld_qkv] = [per q head (query, gate) | k | v]
- * (TF:658-665); k_buf, v_buf: scratch bf16 [tokens][kv_heads][head_dim]; out: bf16
- * [tokens, heads*head_dim]. */
+ * sigmoid(gate). qkv: fp32 [tokens, ld_qkv] = [per q head (query, gate) | k | v]
+ * (TF:658-665); q_buf, k_buf, v_buf: scratch bf16 [tokens][heads][head_dim]; out: the two
+ * bf16 planes of o_proj's input, hi [tokens, heads*head_dim] and lo at out + lo_offset. */
 typedef struct b200_attn_params {
   int32_t heads, kv_heads, head_dim, rope_dim, max_pos;
   float eps;
@@ -177,8 +190,8 @@ typedef struct b200_attn_params {
   const float* rope_sin;
 } b200_attn_params;
 
-int b200_attention(const b200_attn_params* p, const b200_seqs* seqs, const uint16_t* qkv, int32_t ld_qkv,
-                   uint16_t* q_buf, uint16_t* k_buf, uint16_t* v_buf, uint16_t* out,
+int b200_attention(const b200_attn_params* p, const b200_seqs* seqs, const float* qkv, int32_t ld_qkv,
+                   uint16_t* q_buf, uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset,
                    const b200_prefix_pool* pool, int32_t attn_layer, b200_stream stream);
 
 /* ---------------------------------------------------------------- decision head

@@ -33,12 +33,13 @@ class B200Error(RuntimeError):
 
 class QWeight(C.Structure):
     _fields_ = [("format", C.c_int32), ("n", C.c_int32), ("k", C.c_int32), ("data", C.c_void_p),
-                ("scales", C.c_void_p), ("row_scale", C.c_void_p)]
+                ("scales", C.c_void_p), ("row_scale", C.c_void_p), ("tiles", C.c_void_p),
+                ("tile_scales", C.c_void_p)]
 
 
 class LinearOut(C.Structure):
     _fields_ = [("epilogue", C.c_int32), ("n_valid", C.c_int32), ("out", C.c_void_p), ("ldo", C.c_int32),
-                ("out_f32", C.c_void_p), ("ldo_f32", C.c_int32), ("split_n", C.c_int32)]
+                ("lo_offset", C.c_int64)]
 
 
 class Seqs(C.Structure):
@@ -93,14 +94,16 @@ _SIGS = {
     "b200_read_fault": ([C.POINTER(C.c_uint)], C.c_int),
     "b200_quantize": ([_I, _P, _I, _I, _P, _P, _P, _P], C.c_int),
     "b200_dequantize": ([C.POINTER(QWeight), _P, _P], C.c_int),
-    "b200_linear": ([_P, _I, _I, _I, C.POINTER(QWeight), C.POINTER(LinearOut), _P], C.c_int),
-    "b200_linear_simt": ([_P, _I, _I, _I, C.POINTER(QWeight), C.POINTER(LinearOut), _P], C.c_int),
+    "b200_tile_bytes": ([_I, _I, _I, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)], C.c_int),
+    "b200_tile_weights": ([C.POINTER(QWeight), _P, _P, _P], C.c_int),
+    "b200_linear": ([_P, _P, _I, _I, _I, C.POINTER(QWeight), C.POINTER(LinearOut), _P], C.c_int),
+    "b200_linear_simt": ([_P, _P, _I, _I, _I, C.POINTER(QWeight), C.POINTER(LinearOut), _P], C.c_int),
     "b200_embed": ([_P, _I, _P, _I, _P, _P], C.c_int),
-    "b200_rmsnorm": ([_P, _I, _I, _P, C.c_float, _P, _P], C.c_int),
-    "b200_gdn_mixer": ([C.POINTER(GdnParams), C.POINTER(Seqs), _P, _I, _P, _P, C.POINTER(PrefixPool), _I, _P],
-                       C.c_int),
-    "b200_attention": ([C.POINTER(AttnParams), C.POINTER(Seqs), _P, _I, _P, _P, _P, _P, C.POINTER(PrefixPool),
-                        _I, _P], C.c_int),
+    "b200_rmsnorm": ([_P, _I, _I, _P, C.c_float, _P, C.c_int64, _P], C.c_int),
+    "b200_gdn_mixer": ([C.POINTER(GdnParams), C.POINTER(Seqs), _P, _I, _P, C.c_int64, C.POINTER(PrefixPool), _I,
+                        _P], C.c_int),
+    "b200_attention": ([C.POINTER(AttnParams), C.POINTER(Seqs), _P, _I, _P, _P, _P, _P, C.c_int64,
+                        C.POINTER(PrefixPool), _I, _P], C.c_int),
     "b200_decide": ([_P, _I, _P, C.c_float, _P, C.POINTER(DecideArgs), _P], C.c_int),
     "b200_model_create": ([C.POINTER(ModelConfig), C.POINTER(C.c_void_p)], C.c_int),
     "b200_model_destroy": ([_P], C.c_int),
@@ -160,6 +163,14 @@ def ptr(t: torch.Tensor | None) -> int | None:
 def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
     s = stream if stream is not None else torch.cuda.current_stream()
     return s.cuda_stream
+
+
+def split_planes(x: torch.Tensor) -> torch.Tensor:
+    """fp32 [..., k] -> bf16 [2, ..., k]: hi = bf16_rn(x), lo = bf16_rn(x - hi) (the
+    activation format of every GEMM input)."""
+    hi = x.to(torch.bfloat16)
+    lo = (x - hi.float()).to(torch.bfloat16)
+    return torch.stack([hi, lo]).contiguous()
 
 
 def read_fault() -> int:

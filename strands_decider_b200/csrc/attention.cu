@@ -17,12 +17,13 @@ struct AttnArgs {
   const int32_t* prefix_slot;
   const int32_t* save_slot;
   int n_seqs;
-  const uint16_t* qkv;
+  const float* qkv;
   int ld_qkv;
   uint16_t* q_buf;
   uint16_t* k_buf;
   uint16_t* v_buf;
   uint16_t* out;
+  long long lo_offset;
   const int32_t* slot_len;
   const int32_t* slot_kv;
   uint16_t* k_pool;   // this layer's [kv_capacity][kv_heads][head_dim]
@@ -58,8 +59,8 @@ __global__ void attn_prep_kernel(const AttnArgs a) {
     if (lane == 0) raise_fault(FAULT_BAD_INDEX);
     pos = a.p.max_pos - 1;
   }
-  const uint16_t* row = a.qkv + size_t(t) * a.ld_qkv;
-  const uint16_t* src;
+  const float* row = a.qkv + size_t(t) * a.ld_qkv;
+  const float* src;
   const float* nw = nullptr;
   uint16_t* dst;
   uint16_t* pool_dst = nullptr;
@@ -86,7 +87,7 @@ __global__ void attn_prep_kernel(const AttnArgs a) {
   }
   float x[PER];
 #pragma unroll
-  for (int e = 0; e < PER; ++e) x[e] = bf16_to_f32(src[lane * PER + e]);
+  for (int e = 0; e < PER; ++e) x[e] = src[lane * PER + e];
   if (nw) {
     float ss2 = 0.0f;
 #pragma unroll
@@ -165,12 +166,15 @@ __global__ void attn_kernel(const AttnArgs a, int n_tokens) {
   }
   for (int i = 0; i <= j; ++i)
     step(a.k_buf + (size_t(tok0 + i) * nkv + kh) * HD, a.v_buf + (size_t(tok0 + i) * nkv + kh) * HD);
-  const uint16_t* gate = a.qkv + size_t(t) * a.ld_qkv + h * 2 * HD + HD;
+  const float* gate = a.qkv + size_t(t) * a.ld_qkv + h * 2 * HD + HD;
   const float inv = 1.0f / l;
 #pragma unroll
   for (int e = 0; e < PER; ++e) {
-    const float gv = sigmoid(bf16_to_f32(gate[lane * PER + e]));
-    a.out[(size_t(t) * nq + h) * HD + lane * PER + e] = f32_to_bf16_rn(acc[e] * inv * gv);
+    const float y = acc[e] * inv * sigmoid(gate[lane * PER + e]);
+    const size_t o = (size_t(t) * nq + h) * HD + lane * PER + e;
+    const uint16_t hb = f32_to_bf16_rn(y);
+    a.out[o] = hb;
+    if (a.lo_offset) a.out[a.lo_offset + o] = f32_to_bf16_rn(y - bf16_to_f32(hb));
   }
 }
 
@@ -189,16 +193,17 @@ static int launch_attn(const AttnArgs& a, int n_tokens, cudaStream_t st) {
 
 using namespace sdb;
 
-int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const uint16_t* qkv, int32_t ld_qkv, uint16_t* q_buf,
-                  uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, const b200_prefix_pool* pool, int32_t layer,
-                  cudaStream_t st) {
+int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qkv, int32_t ld_qkv, uint16_t* q_buf,
+                  uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool,
+                  int32_t layer, cudaStream_t st) {
   if (!p || !s || !qkv || !q_buf || !k_buf || !v_buf || !out) return sdb_fail(B200_ERR_ARG, "b200_attention: null pointer");
   if (!p->q_norm || !p->k_norm || !p->rope_cos || !p->rope_sin) return sdb_fail(B200_ERR_ARG, "b200_attention: null param");
   if (p->heads <= 0 || p->kv_heads <= 0 || p->heads % p->kv_heads != 0 || p->heads + 2 * p->kv_heads > 32)
     return sdb_fail(B200_ERR_SHAPE, "b200_attention: bad head counts");
   const int per = p->head_dim / 32;
-  if (p->rope_dim <= 0 || p->rope_dim > p->head_dim || (p->rope_dim / 2) % per != 0)
-    return sdb_fail(B200_ERR_SHAPE, "b200_attention: rope_dim/2 must be a multiple of head_dim/32");
+  const int xd = per ? (p->rope_dim / 2) / per : 0;
+  if (p->rope_dim <= 0 || p->rope_dim > p->head_dim || (p->rope_dim / 2) % per != 0 || xd <= 0 || (xd & (xd - 1)))
+    return sdb_fail(B200_ERR_SHAPE, "b200_attention: rope_dim/2 / (head_dim/32) must be a power of two");
   if (s->n_seqs <= 0 || s->n_tokens <= 0 || !s->cu_seqlens) return sdb_fail(B200_ERR_SHAPE, "b200_attention: empty batch");
   const bool uses_pool = s->prefix_slot || s->save_slot;
   if (uses_pool && (!pool || !pool->k_cache || !pool->v_cache || !pool->slot_len || !pool->slot_kv))
@@ -215,6 +220,7 @@ int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const uint16_t*
   a.k_buf = k_buf;
   a.v_buf = v_buf;
   a.out = out;
+  a.lo_offset = lo_offset;
   a.n_slots = uses_pool ? pool->n_slots : 0;
   a.kv_capacity = uses_pool ? pool->kv_capacity : 0;
   a.slot_len = uses_pool ? pool->slot_len : nullptr;
@@ -230,9 +236,9 @@ int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const uint16_t*
   }
 }
 
-extern "C" int b200_attention(const b200_attn_params* p, const b200_seqs* seqs, const uint16_t* qkv, int32_t ld_qkv,
-                              uint16_t* q_buf, uint16_t* k_buf, uint16_t* v_buf, uint16_t* out,
+extern "C" int b200_attention(const b200_attn_params* p, const b200_seqs* seqs, const float* qkv, int32_t ld_qkv,
+                              uint16_t* q_buf, uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset,
                               const b200_prefix_pool* pool, int32_t attn_layer, b200_stream stream) {
-  return sdb_attention(p, seqs, qkv, ld_qkv, q_buf, k_buf, v_buf, out, pool, attn_layer,
+  return sdb_attention(p, seqs, qkv, ld_qkv, q_buf, k_buf, v_buf, out, lo_offset, pool, attn_layer,
                        reinterpret_cast<cudaStream_t>(stream));
 }

@@ -24,6 +24,7 @@ enum FaultSite : unsigned int {
   FAULT_GEMM_WAIT_FULL_A = 1u << 1,
   FAULT_GEMM_WAIT_FULL_B = 1u << 2,
   FAULT_GEMM_WAIT_ACCUM = 1u << 3,
+  FAULT_GEMM_WAIT_FULL_W = 1u << 4,
   FAULT_BAD_INDEX = 1u << 8,
 };
 
@@ -134,6 +135,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
           smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

@@ -63,42 +63,77 @@ __device__ __forceinline__ float nvfp4_block_scale(uint8_t sb, float gs) {
 }
 
 // ----------------------------------------------------------------------------- unpackers
-// Each produces 8 consecutive bf16 weights (one 16-byte chunk of a 128-byte K row).
+// Each produces 8 consecutive bf16 weights (one 16-byte chunk of a 128-byte K row) with
+// packed bf16x2 arithmetic. Every product below is a single round-to-nearest-even of an
+// exact product, so the results equal the fp32 definitions bit for bit.
 
-// int4: one 32-bit word = 8 nibbles; w = bf16_rn(q * s), s a bf16 value.
-__device__ __forceinline__ uint4 unpack8_int4(uint32_t word, float s) {
-  uint32_t o[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    int q0 = int(word << (28 - 8 * j)) >> 28;          // nibble 2j, sign-extended
-    int q1 = int(word << (24 - 8 * j)) >> 28;          // nibble 2j+1
-    o[j] = pack_bf16x2(__fmul_rn(float(q0), s), __fmul_rn(float(q1), s));
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
 }
 
-// NVFP4: 4 bytes = 8 e2m1 values (low nibble first); s the effective block scale.
-__device__ __forceinline__ uint4 unpack8_nvfp4(uint32_t word, float s) {
-  uint32_t o[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t byte = (word >> (8 * j)) & 0xFF;
-    o[j] = pack_bf16x2(__fmul_rn(e2m1_decode(byte & 0xF), s), __fmul_rn(e2m1_decode(byte >> 4), s));
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
+// int4: one word = 8 two's-complement nibbles; s2 = the bf16 group scale in both halves.
+// n ^ 8 placed in the mantissa of bf16 128.0 gives 128 + (n ^ 8); minus 136 is q exactly;
+// times s is bf16_rn(q * s).
+__device__ __forceinline__ uint4 unpack8_int4(uint32_t word, uint32_t s2) {
+  const uint32_t x = word ^ 0x88888888u;
+  const uint32_t ev = x & 0x0F0F0F0Fu;          // elements 0, 2, 4, 6
+  const uint32_t od = (x >> 4) & 0x0F0F0F0Fu;   // elements 1, 3, 5, 7
+  const uint32_t t01 = prmt(ev, od, 0x5140);    // elements 0, 1, 2, 3
+  const uint32_t t23 = prmt(ev, od, 0x7362);    // elements 4, 5, 6, 7
+  const uint32_t K = 0x43434343u, C136 = 0x43084308u;
+  uint4 o;
+  o.x = bf16x2_mul(bf16x2_sub(prmt(t01, K, 0x4140), C136), s2);
+  o.y = bf16x2_mul(bf16x2_sub(prmt(t01, K, 0x4342), C136), s2);
+  o.z = bf16x2_mul(bf16x2_sub(prmt(t23, K, 0x4140), C136), s2);
+  o.w = bf16x2_mul(bf16x2_sub(prmt(t23, K, 0x4342), C136), s2);
+  return o;
 }
 
-// ternary: 16 bits = 8 two-bit codes (00 = 0, 01 = +1, 11 = -1); s the row scale.
-__device__ __forceinline__ uint4 unpack8_ternary(uint32_t bits16, float s) {
-  uint32_t o[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t c0 = (bits16 >> (4 * j)) & 3, c1 = (bits16 >> (4 * j + 2)) & 3;
-    float t0 = c0 == 1 ? 1.0f : (c0 == 3 ? -1.0f : 0.0f);
-    float t1 = c1 == 1 ? 1.0f : (c1 == 3 ? -1.0f : 0.0f);
-    o[j] = pack_bf16x2(t0 * s, t1 * s);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
+// NVFP4: one word = 8 e2m1 codes (low nibble first); s2 = the bf16 block scale in both halves.
+// The magnitude (3 bits) indexes byte tables of the bf16 encodings of 0, .5, 1, 1.5, 2, 3, 4, 6;
+// the sign bit is moved to bit 15 / 31; times s is bf16_rn(e2m1 * s).
+__device__ __forceinline__ uint4 unpack8_nvfp4(uint32_t word, uint32_t s2) {
+  const uint32_t m = word & 0x77777777u;
+  const uint32_t HI_A = 0x3F3F3F00u, HI_B = 0x40404040u, LO_A = 0xC0800000u, LO_B = 0xC0804000u;
+  const uint32_t hi03 = prmt(HI_A, HI_B, m), lo03 = prmt(LO_A, LO_B, m);
+  const uint32_t hi47 = prmt(HI_A, HI_B, m >> 16), lo47 = prmt(LO_A, LO_B, m >> 16);
+  const uint32_t sg = word & 0x88888888u;
+  const uint32_t A = sg << 4, B = sg;           // bit 7 of byte j: sign of element 2j (A), 2j+1 (B)
+  uint4 o;
+  o.x = bf16x2_mul(prmt(lo03, hi03, 0x5140) ^ (prmt(A, B, 0x4000) & 0x80008000u), s2);
+  o.y = bf16x2_mul(prmt(lo03, hi03, 0x7362) ^ (prmt(A, B, 0x5111) & 0x80008000u), s2);
+  o.z = bf16x2_mul(prmt(lo47, hi47, 0x5140) ^ (prmt(A, B, 0x6222) & 0x80008000u), s2);
+  o.w = bf16x2_mul(prmt(lo47, hi47, 0x7362) ^ (prmt(A, B, 0x7333) & 0x80008000u), s2);
+  return o;
+}
+
+// ternary: 16 bits = 8 two-bit codes (00 = 0, 01 = +1, 11 = -1); `lut` maps a pair's 4 bits
+// to the bf16x2 of its two t values; times s (both halves) is exact.
+__device__ __forceinline__ uint4 unpack8_ternary(uint32_t bits16, uint32_t s2, const uint32_t* lut) {
+  uint4 o;
+  o.x = bf16x2_mul(lut[bits16 & 0xF], s2);
+  o.y = bf16x2_mul(lut[(bits16 >> 4) & 0xF], s2);
+  o.z = bf16x2_mul(lut[(bits16 >> 8) & 0xF], s2);
+  o.w = bf16x2_mul(lut[(bits16 >> 12) & 0xF], s2);
+  return o;
+}
+
+// bf16x2 of the two t values {0, +1, -1} coded by 4 bits (low code first).
+__host__ __device__ constexpr uint32_t ternary_pair_bits(uint32_t x) {
+  return ((x & 3) == 1 ? 0x3F80u : (x & 3) == 3 ? 0xBF80u : 0u) |
+         ((((x >> 2) & 3) == 1 ? 0x3F80u : ((x >> 2) & 3) == 3 ? 0xBF80u : 0u) << 16);
 }
 
 // Unpack 32 consecutive weights k0 .. k0+31 (k0 a multiple of 32) of row n into four
@@ -108,29 +143,38 @@ __device__ __forceinline__ uint4 unpack8_ternary(uint32_t bits16, float s) {
 //   NVFP4: e4m3 scales of blocks k0/16 and k0/16+1 (bytes 0 and 1), gs the row scale
 //   ternary: bf16 row scale (low 16 bits)
 template <int FMT>
-__device__ __forceinline__ void unpack32(const uint4& raw, uint32_t sc, float gs, uint4 (&out)[4]) {
+__device__ __forceinline__ void unpack32(const uint4& raw, uint32_t sc, float gs, uint4 (&out)[4],
+                                         const uint32_t* lut = nullptr) {
   if constexpr (FMT == B200_W_INT4G128) {
-    float s = bf16_to_f32(uint16_t(sc & 0xFFFF));
-    out[0] = unpack8_int4(raw.x, s);
-    out[1] = unpack8_int4(raw.y, s);
-    out[2] = unpack8_int4(raw.z, s);
-    out[3] = unpack8_int4(raw.w, s);
+    const uint32_t s2 = (sc & 0xFFFFu) * 0x10001u;
+    out[0] = unpack8_int4(raw.x, s2);
+    out[1] = unpack8_int4(raw.y, s2);
+    out[2] = unpack8_int4(raw.z, s2);
+    out[3] = unpack8_int4(raw.w, s2);
   } else if constexpr (FMT == B200_W_NVFP4) {
-    float s0 = nvfp4_block_scale(uint8_t(sc & 0xFF), gs);
-    float s1 = nvfp4_block_scale(uint8_t((sc >> 8) & 0xFF), gs);
+    const uint32_t s0 = uint32_t(f32_to_bf16_rn(__fmul_rn(e4m3_decode(uint8_t(sc & 0xFF)), gs))) * 0x10001u;
+    const uint32_t s1 = uint32_t(f32_to_bf16_rn(__fmul_rn(e4m3_decode(uint8_t((sc >> 8) & 0xFF)), gs))) * 0x10001u;
     out[0] = unpack8_nvfp4(raw.x, s0);
     out[1] = unpack8_nvfp4(raw.y, s0);
     out[2] = unpack8_nvfp4(raw.z, s1);
     out[3] = unpack8_nvfp4(raw.w, s1);
   } else if constexpr (FMT == B200_W_TERNARY) {
-    float s = bf16_to_f32(uint16_t(sc & 0xFFFF));
-    out[0] = unpack8_ternary(raw.x & 0xFFFF, s);
-    out[1] = unpack8_ternary(raw.x >> 16, s);
-    out[2] = unpack8_ternary(raw.y & 0xFFFF, s);
-    out[3] = unpack8_ternary(raw.y >> 16, s);
+    const uint32_t s2 = (sc & 0xFFFFu) * 0x10001u;
+    out[0] = unpack8_ternary(raw.x & 0xFFFF, s2, lut);
+    out[1] = unpack8_ternary(raw.x >> 16, s2, lut);
+    out[2] = unpack8_ternary(raw.y & 0xFFFF, s2, lut);
+    out[3] = unpack8_ternary(raw.y >> 16, s2, lut);
   } else {  // bf16: 64 bytes of raw data do not fit `raw`; handled by the caller
     out[0] = out[1] = out[2] = out[3] = make_uint4(0, 0, 0, 0);
   }
+}
+
+// Streaming-copy geometry: bytes of one row's 64 columns, and of their scales.
+__host__ __device__ constexpr int tile_row_bytes(int fmt) {
+  return fmt == B200_W_INT4G128 ? 32 : fmt == B200_W_NVFP4 ? 32 : fmt == B200_W_TERNARY ? 16 : 128;
+}
+__host__ __device__ constexpr int tile_scale_row_bytes(int fmt) {
+  return fmt == B200_W_INT4G128 ? 2 : fmt == B200_W_NVFP4 ? 4 : 0;
 }
 
 // Bytes of packed data per 32 weights, and per-row pitch helpers.

@@ -26,13 +26,13 @@ struct GdnArgs {
   const int32_t* cu;
   const int32_t* prefix_slot;
   const int32_t* save_slot;
-  const uint16_t* mix;
+  const float* mix;      // [T, ld_mix]: q | k | v | z | b | a
   int ld_mix;
-  const float* ab;
-  uint16_t* out;
+  uint16_t* out;         // hi plane [T, value_dim]; lo plane at out + lo_offset
+  long long lo_offset;
   int32_t* slot_len;
   float* state_pool;     // this layer's [n_slots][heads][dk][dv]
-  uint16_t* conv_pool;   // this layer's [n_slots][conv_width-1][conv_dim]
+  float* conv_pool;      // this layer's [n_slots][conv_width-1][conv_dim]
   int n_slots;
 };
 
@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
     (&sm.S[0][0])[i] = pvalid ? a.state_pool[(size_t(pslot) * H + h) * GDK * GDV + i] : 0.0f;
   for (int i = tid; i < 3 * GQKV; i += GDN_THREADS) {
     const int r = i / GQKV, c = i % GQKV;
-    sm.hist[r][c] = pvalid ? bf16_to_f32(a.conv_pool[(size_t(pslot) * 3 + r) * conv_dim + chan(c)]) : 0.0f;
+    sm.hist[r][c] = pvalid ? a.conv_pool[(size_t(pslot) * 3 + r) * conv_dim + chan(c)] : 0.0f;
   }
   const float A_exp = __expf(a.p.a_log[h]);
   const float dtb = a.p.dt_bias[h];
@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         const int jj = j - 3 + t;
-        const float xv = jj < 0 ? sm.hist[3 + jj][c] : bf16_to_f32(a.mix[size_t(tok0 + c0 + jj) * a.ld_mix + ch]);
+        const float xv = jj < 0 ? sm.hist[3 + jj][c] : a.mix[size_t(tok0 + c0 + jj) * a.ld_mix + ch];
         acc = fmaf(a.p.conv_w[ch * 4 + t], xv, acc);
       }
       acc = silu(acc);
@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       for (int i = tid; i < 3 * GQKV; i += GDN_THREADS, ++n) {
         const int r = i / GQKV, c = i % GQKV;
         const int jj = L - 3 + r;
-        keep[n] = jj < 0 ? sm.hist[3 + jj][c] : bf16_to_f32(a.mix[size_t(tok0 + c0 + jj) * a.ld_mix + chan(c)]);
+        keep[n] = jj < 0 ? sm.hist[3 + jj][c] : a.mix[size_t(tok0 + c0 + jj) * a.ld_mix + chan(c)];
       }
       __syncthreads();
       n = 0;
@@ -124,8 +124,9 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
     }
     if (tid < L) {
       const size_t t = size_t(tok0 + c0 + tid);
-      sm.beta[tid] = sigmoid(a.ab[t * 2 * H + h]);
-      sm.G[tid] = -A_exp * softplus(a.ab[t * 2 * H + H + h] + dtb);
+      const float* ab = a.mix + t * a.ld_mix + conv_dim + value_dim;
+      sm.beta[tid] = sigmoid(ab[h]);
+      sm.G[tid] = -A_exp * softplus(ab[H + h] + dtb);
     }
     __syncthreads();
     if (tid == 0) {
@@ -240,9 +241,11 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       const float r = rsqrtf(ss / float(GDV) + a.p.eps);
       const size_t t = size_t(tok0 + c0 + j);
       for (int d = lane; d < GDV; d += 32) {
-        const float z = bf16_to_f32(a.mix[t * a.ld_mix + conv_dim + h * GDV + d]);
+        const float z = a.mix[t * a.ld_mix + conv_dim + h * GDV + d];
         const float y = a.p.norm_w[d] * (sm.w[j][d] * r) * silu(z);
-        a.out[t * value_dim + h * GDV + d] = f32_to_bf16_rn(y);
+        const uint16_t hb = f32_to_bf16_rn(y);
+        a.out[t * value_dim + h * GDV + d] = hb;
+        if (a.lo_offset) a.out[a.lo_offset + t * value_dim + h * GDV + d] = f32_to_bf16_rn(y - bf16_to_f32(hb));
       }
     }
     __syncthreads();
@@ -253,7 +256,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       a.state_pool[(size_t(sslot) * H + h) * GDK * GDV + i] = (&sm.S[0][0])[i];
     for (int i = tid; i < 3 * GQKV; i += GDN_THREADS) {
       const int r = i / GQKV, cc = i % GQKV;
-      a.conv_pool[(size_t(sslot) * 3 + r) * conv_dim + chan(cc)] = f32_to_bf16_rn(sm.hist[r][cc]);
+      a.conv_pool[(size_t(sslot) * 3 + r) * conv_dim + chan(cc)] = sm.hist[r][cc];
     }
     if (h == 0 && tid == 0) a.slot_len[sslot] = (pvalid ? a.slot_len[pslot] : 0) + len;
   }
@@ -263,9 +266,9 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
 
 using namespace sdb;
 
-int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const uint16_t* mix, int32_t ld_mix, const float* ab,
-                  uint16_t* out, const b200_prefix_pool* pool, int32_t layer, cudaStream_t st) {
-  if (!p || !s || !mix || !ab || !out) return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: null pointer");
+int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix, int32_t ld_mix, uint16_t* out,
+                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, cudaStream_t st) {
+  if (!p || !s || !mix || !out) return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: null pointer");
   if (p->dk != GDK || p->dv != GDV || p->conv_width != 4)
     return sdb_fail(B200_ERR_UNSUPPORTED, "b200_gdn_mixer: only dk = dv = 128 and conv width 4 are built");
   if (!p->conv_w || !p->a_log || !p->dt_bias || !p->norm_w) return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: null param");
@@ -280,9 +283,11 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const uint16_t* 
   a.save_slot = s->save_slot;
   a.mix = mix;
   a.ld_mix = ld_mix;
-  a.ab = ab;
   a.out = out;
+  a.lo_offset = lo_offset;
   const int conv_dim = 2 * p->heads * GDK + p->heads * GDV;
+  if (ld_mix < conv_dim + p->heads * GDV + 2 * p->heads)
+    return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: ld_mix is narrower than [q|k|v|z|b|a]");
   a.n_slots = uses_pool ? pool->n_slots : 0;
   a.slot_len = uses_pool ? pool->slot_len : nullptr;
   a.state_pool = uses_pool ? pool->gdn_state + size_t(layer) * pool->n_slots * p->heads * GDK * GDV : nullptr;
@@ -297,8 +302,8 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const uint16_t* 
   return B200_OK;
 }
 
-extern "C" int b200_gdn_mixer(const b200_gdn_params* p, const b200_seqs* seqs, const uint16_t* mix, int32_t ld_mix,
-                              const float* ab, uint16_t* out, const b200_prefix_pool* pool, int32_t gdn_layer,
+extern "C" int b200_gdn_mixer(const b200_gdn_params* p, const b200_seqs* seqs, const float* mix, int32_t ld_mix,
+                              uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool, int32_t gdn_layer,
                               b200_stream stream) {
-  return sdb_gdn_mixer(p, seqs, mix, ld_mix, ab, out, pool, gdn_layer, reinterpret_cast<cudaStream_t>(stream));
+  return sdb_gdn_mixer(p, seqs, mix, ld_mix, out, lo_offset, pool, gdn_layer, reinterpret_cast<cudaStream_t>(stream));
 }

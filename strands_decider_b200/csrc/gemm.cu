@@ -1,15 +1,21 @@
 // Weight-only quantised linear layers on the 5th-generation tensor cores (tcgen05).
 //
-// y[m, n] = sum_k x[m, k] * W[n, k] with x bf16 and W packed (int4 g128, NVFP4, ternary or
-// bf16). One CTA computes a 128 x BN tile (BN = 256 by default) with the accumulator in
-// tensor memory:
-//   warp 0      one lane issues TMA loads of the x tile (128 rows x 64 k, 128-byte swizzle)
-//   warp 1      allocates TMEM; one lane issues tcgen05.mma (M=128, N=BN, K=16) x 4 per stage
-//   warps 2..5  unpack the packed weights of the stage to bf16 directly into the same
-//               128-byte-swizzled K-major layout the MMA reads, then run the epilogue
-//               (TMEM -> registers -> fused op -> global)
-// A 4-stage ring of shared-memory stages is guarded by mbarriers: full_a (TMA bytes),
-// full_b (128 unpacking threads), empty (tcgen05.commit). Every wait is bounded.
+// y[m, n] = sum_k x[m, k] * W[n, k] with W packed (int4 g128, NVFP4, ternary or bf16) and x
+// held as two bf16 planes x_hi + x_lo (fp32-level precision). One CTA computes a 128 x BN
+// tile (BN = 256) with the accumulator in tensor memory:
+//   warp 0      one lane streams each stage: TMA loads of the x tiles (128 rows x 64 k
+//               per plane, 128-byte swizzle) and bulk copies of the stage's packed weight
+//               chunk and scales (the b200_tile_weights layout); bf16 weights come as a
+//               swizzled TMA tile straight into the B stage
+//   warp 1      allocates TMEM; one lane issues tcgen05.mma (M=128, N=BN, K=16): per 16 k,
+//               one MMA for x_hi and one for x_lo against the same weight tile
+//   warps 2..9  unpack the stage's packed weights from shared memory to bf16, directly into
+//               the 128-byte-swizzled K-major layout the MMA reads, then run the epilogue
+//               (TMEM -> registers -> fused op -> global); each TMEM lane quarter is read by
+//               two warps, one per column half
+// A 3-stage ring of shared-memory stages is guarded by mbarriers: full_a (activation TMA
+// bytes), full_w (packed weight bytes), full_b (256 unpacking threads), empty
+// (tcgen05.commit). Every wait is bounded.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -20,8 +26,10 @@ namespace sdb {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
-constexpr int GEMM_STAGES = 4;
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_THREADS = 320;          // warp 0 TMA, warp 1 MMA, warps 2..9 unpack + epilogue
+constexpr int GEMM_UNPACK_THREADS = 256;
+
+constexpr int GEMM_STAGES = 3;
 
 struct GemmArgs {
   b200_qweight w;
@@ -29,46 +37,39 @@ struct GemmArgs {
   int m, k;
 };
 
-template <int BN>
-__host__ __device__ constexpr int gemm_smem_bytes() {
-  return GEMM_STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) + 1024 + (3 * GEMM_STAGES + 1) * 8 + 16;
-}
+template <int BN, int FMT, bool SPLIT>
+struct GemmSmem {
+  static constexpr bool PACKED = FMT != B200_W_BF16;
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;          // one activation plane
+  static constexpr int A_STAGE = A_BYTES * (SPLIT ? 2 : 1);
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;               // unpacked bf16 weight tile
+  static constexpr int W_BYTES = PACKED ? BN * tile_row_bytes(FMT) : 0;
+  static constexpr int S_BYTES = BN * tile_scale_row_bytes(FMT);
+  static constexpr int STAGE = A_STAGE + B_BYTES + W_BYTES + S_BYTES;
+  static constexpr int BARS = 4 * GEMM_STAGES + 1;
+  static constexpr int TOTAL = GEMM_STAGES * STAGE + 1024 + BARS * 8 + 16 + 64;
+};
 
 // --------------------------------------------------------------------------- epilogue
+// One thread holds 32 consecutive fp32 accumulators of its row.
 template <int EP>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int gcol, const uint32_t (&v)[32]) {
   const b200_linear_out& o = a.o;
   if (row >= a.m || gcol >= o.n_valid) return;
   const int nv = min(32, o.n_valid - gcol);
+  float* dst = reinterpret_cast<float*>(o.out) + size_t(row) * o.ldo + gcol;
   if constexpr (EP == B200_EP_STORE) {
-    if (gcol >= o.split_n) {
-      float* dst = o.out_f32 + size_t(row) * o.ldo_f32 + (gcol - o.split_n);
-      if (nv == 32) {
+    if (nv == 32) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          reinterpret_cast<float4*>(dst)[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
-                                                          __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
-      } else {
-        for (int j = 0; j < nv; ++j) dst[j] = __uint_as_float(v[j]);
-      }
+      for (int j = 0; j < 8; ++j)
+        reinterpret_cast<float4*>(dst)[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                                        __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
     } else {
-      uint16_t* dst = reinterpret_cast<uint16_t*>(o.out) + size_t(row) * o.ldo + gcol;
-      if (nv == 32) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 p;
-          p.x = pack_bf16x2(__uint_as_float(v[8 * j + 0]), __uint_as_float(v[8 * j + 1]));
-          p.y = pack_bf16x2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
-          p.z = pack_bf16x2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
-          p.w = pack_bf16x2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
-          reinterpret_cast<uint4*>(dst)[j] = p;
-        }
-      } else {
-        for (int j = 0; j < nv; ++j) dst[j] = f32_to_bf16_rn(__uint_as_float(v[j]));
-      }
+      for (int j = 0; j < 32; ++j)
+        if (j < nv) dst[j] = __uint_as_float(v[j]);
     }
   } else if constexpr (EP == B200_EP_RESID_ADD) {
-    float* dst = reinterpret_cast<float*>(o.out) + size_t(row) * o.ldo + gcol;
     if (nv == 32) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -80,12 +81,22 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int g
         reinterpret_cast<float4*>(dst)[j] = r;
       }
     } else {
-      for (int j = 0; j < nv; ++j) dst[j] += __uint_as_float(v[j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nv) dst[j] += __uint_as_float(v[j]);
     }
   }
 }
 
-// SwiGLU: gate chunk g and up chunk u (same 32 intermediate features) -> 32 bf16 outputs.
+// hi = bf16_rn(x), lo = bf16_rn(x - hi): the two planes of an fp32 activation.
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const uint16_t ha = f32_to_bf16_rn(a), hb = f32_to_bf16_rn(b);
+  hi = uint32_t(ha) | (uint32_t(hb) << 16);
+  lo = pack_bf16x2(a - bf16_to_f32(ha), b - bf16_to_f32(hb));
+}
+
+// SwiGLU: gate chunk g and up chunk u (same 32 intermediate features) -> 32 outputs as
+// hi/lo bf16 planes.
 __device__ __forceinline__ void epilogue_swiglu(const GemmArgs& a, int row, int ocol, const uint32_t (&g)[32],
                                                 const uint32_t (&u)[32]) {
   const b200_linear_out& o = a.o;
@@ -96,12 +107,13 @@ __device__ __forceinline__ void epilogue_swiglu(const GemmArgs& a, int row, int 
     float h[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) h[e] = silu(__uint_as_float(g[8 * j + e])) * __uint_as_float(u[8 * j + e]);
-    uint4 p;
-    p.x = pack_bf16x2(h[0], h[1]);
-    p.y = pack_bf16x2(h[2], h[3]);
-    p.z = pack_bf16x2(h[4], h[5]);
-    p.w = pack_bf16x2(h[6], h[7]);
-    reinterpret_cast<uint4*>(dst)[j] = p;
+    uint4 hi, lo;
+    split_bf16x2(h[0], h[1], hi.x, lo.x);
+    split_bf16x2(h[2], h[3], hi.y, lo.y);
+    split_bf16x2(h[4], h[5], hi.z, lo.z);
+    split_bf16x2(h[6], h[7], hi.w, lo.w);
+    reinterpret_cast<uint4*>(dst)[j] = hi;
+    if (o.lo_offset) reinterpret_cast<uint4*>(dst + o.lo_offset)[j] = lo;
   }
 }
 
@@ -109,9 +121,13 @@ __device__ __forceinline__ void epilogue_swiglu(const GemmArgs& a, int row, int 
 // Raw packed data for one (row, half) unit: 32 weights.
 template <int FMT>
 struct Raw32 {
-  uint4 d0, d1, d2, d3;  // bf16 needs 64 bytes; the packed formats use d0 only
+  uint4 d0;
   uint32_t sc;
   float gs;
+};
+template <>
+struct Raw32<B200_W_BF16> {
+  uint4 d0, d1, d2, d3;  // 64 bytes of bf16
 };
 
 template <int FMT>
@@ -122,48 +138,70 @@ __device__ __forceinline__ void load_unit(const b200_qweight& w, int n, int k0, 
     r.d1 = __ldg(src + 1);
     r.d2 = __ldg(src + 2);
     r.d3 = __ldg(src + 3);
-    r.sc = 0;
-    r.gs = 1.0f;
   } else {
     load32<FMT>(w, n, k0, r.d0, r.sc, r.gs);
   }
 }
 
 template <int FMT>
-__device__ __forceinline__ void store_unit(uint8_t* sB, int r, int half, const Raw32<FMT>& raw) {
-  uint4 out[4];
+__device__ __forceinline__ void unit_values(const Raw32<FMT>& raw, uint4 (&out)[4], const uint32_t* lut) {
   if constexpr (FMT == B200_W_BF16) {
     out[0] = raw.d0;
     out[1] = raw.d1;
     out[2] = raw.d2;
     out[3] = raw.d3;
   } else {
-    unpack32<FMT>(raw.d0, raw.sc, raw.gs, out);
+    unpack32<FMT>(raw.d0, raw.sc, raw.gs, out, lut);
   }
+}
+
+// Unpack unit (row r, half h) of a stage from its shared-memory chunk into the swizzled
+// B tile. `rowc` is the per-row constant (ternary scale bits / NVFP4 row scale).
+template <int FMT>
+__device__ __forceinline__ void unpack_unit_smem(uint8_t* sB, const uint8_t* sW, const uint8_t* sS, int r, int h,
+                                                 uint32_t row_sc, float row_gs, const uint32_t* lut) {
+  constexpr int RB = tile_row_bytes(FMT);
+  uint4 raw;
+  if constexpr (FMT == B200_W_TERNARY) {
+    const uint2 v = *reinterpret_cast<const uint2*>(sW + r * RB + h * 8);
+    raw = make_uint4(v.x, v.y, 0, 0);
+  } else {
+    raw = *reinterpret_cast<const uint4*>(sW + r * RB + h * 16);
+  }
+  uint32_t sc;
+  if constexpr (FMT == B200_W_INT4G128) sc = *reinterpret_cast<const uint16_t*>(sS + r * 2);
+  else if constexpr (FMT == B200_W_NVFP4) sc = *reinterpret_cast<const uint16_t*>(sS + r * 4 + h * 2);
+  else sc = row_sc;
+  uint4 out[4];
+  unpack32<FMT>(raw, sc, row_gs, out, lut);
   uint8_t* rowp = sB + r * 128;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    const int chunk = half * 4 + c;
+    const int chunk = h * 4 + c;
     *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) << 4)) = out[c];
   }
 }
 
 // --------------------------------------------------------------------------- kernel
-template <int BN, int FMT, int EP>
+template <int BN, int FMT, int EP, bool SPLIT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const GemmArgs args) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA_lo,
+                   const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  using SM = GemmSmem<BN, FMT, SPLIT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
-  constexpr int B_BYTES = BN * GEMM_BK * 2;
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + GEMM_STAGES * A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + GEMM_STAGES * B_BYTES);
+  uint8_t* sA = smem;                                   // STAGES x A_STAGE
+  uint8_t* sB = sA + GEMM_STAGES * SM::A_STAGE;         // STAGES x B_BYTES
+  uint8_t* sW = sB + GEMM_STAGES * SM::B_BYTES;         // STAGES x W_BYTES
+  uint8_t* sS = sW + GEMM_STAGES * SM::W_BYTES;         // STAGES x S_BYTES
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sS + GEMM_STAGES * SM::S_BYTES);
   uint64_t* full_a = bars;
-  uint64_t* full_b = bars + GEMM_STAGES;
-  uint64_t* empty = bars + 2 * GEMM_STAGES;
-  uint64_t* accum = bars + 3 * GEMM_STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * GEMM_STAGES + 1);
+  uint64_t* full_w = bars + GEMM_STAGES;
+  uint64_t* full_b = bars + 2 * GEMM_STAGES;
+  uint64_t* empty = bars + 3 * GEMM_STAGES;
+  uint64_t* accum = bars + 4 * GEMM_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + SM::BARS);
+  uint32_t* lut = tmem_slot + 4;  // 16 words: ternary pair table
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * GEMM_BM;
@@ -172,12 +210,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < GEMM_STAGES; ++s) {
       mbar_init(&full_a[s], 1);
-      mbar_init(&full_b[s], 128);
+      mbar_init(&full_w[s], 1);
+      mbar_init(&full_b[s], GEMM_UNPACK_THREADS);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum, 1);
     mbar_fence_init();
   }
+  if (threadIdx.x < 16) lut[threadIdx.x] = ternary_pair_bits(threadIdx.x);
   if (warp == 1) {
     tmem_alloc(tmem_slot, BN);
     tmem_relinquish();
@@ -190,12 +230,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
+      if constexpr (SPLIT) tma_prefetch_desc(&tmA_lo);
+      if constexpr (!SM::PACKED) tma_prefetch_desc(&tmB);
+      const uint8_t* wtiles = reinterpret_cast<const uint8_t*>(args.w.tiles) + size_t(blockIdx.x) * nk * SM::W_BYTES;
+      const uint8_t* stiles =
+          reinterpret_cast<const uint8_t*>(args.w.tile_scales) + size_t(blockIdx.x) * nk * SM::S_BYTES;
       for (int kt = 0; kt < nk; ++kt) {
         const int s = kt % GEMM_STAGES;
         const uint32_t ph = (kt / GEMM_STAGES) & 1;
         mbar_wait(&empty[s], ph ^ 1, FAULT_GEMM_WAIT_EMPTY);
-        mbar_arrive_expect_tx(&full_a[s], A_BYTES);
-        tma_load_2d(sA + s * A_BYTES, &tmA, &full_a[s], kt * GEMM_BK, m0);
+        if constexpr (SM::PACKED) {
+          mbar_arrive_expect_tx(&full_w[s], SM::W_BYTES + SM::S_BYTES);
+          bulk_load(sW + s * SM::W_BYTES, wtiles + size_t(kt) * SM::W_BYTES, SM::W_BYTES, &full_w[s]);
+          if constexpr (SM::S_BYTES > 0)
+            bulk_load(sS + s * SM::S_BYTES, stiles + size_t(kt) * SM::S_BYTES, SM::S_BYTES, &full_w[s]);
+        }
+        mbar_arrive_expect_tx(&full_a[s], SM::A_STAGE + (SM::PACKED ? 0 : SM::B_BYTES));
+        tma_load_2d(sA + s * SM::A_STAGE, &tmA, &full_a[s], kt * GEMM_BK, m0);
+        if constexpr (SPLIT) tma_load_2d(sA + s * SM::A_STAGE + SM::A_BYTES, &tmA_lo, &full_a[s], kt * GEMM_BK, m0);
+        if constexpr (!SM::PACKED) tma_load_2d(sB + s * SM::B_BYTES, &tmB, &full_a[s], kt * GEMM_BK, n0);
       }
     }
   } else if (warp == 1) {
@@ -205,72 +258,69 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int s = kt % GEMM_STAGES;
         const uint32_t ph = (kt / GEMM_STAGES) & 1;
         mbar_wait(&full_a[s], ph, FAULT_GEMM_WAIT_FULL_A);
-        mbar_wait(&full_b[s], ph, FAULT_GEMM_WAIT_FULL_B);
+        if constexpr (SM::PACKED) mbar_wait(&full_b[s], ph, FAULT_GEMM_WAIT_FULL_B);
         tc_fence_after();
-        const uint64_t ad = umma_desc_sw128(smem_addr(sA + s * A_BYTES));
-        const uint64_t bd = umma_desc_sw128(smem_addr(sB + s * B_BYTES));
+        const uint64_t ad = umma_desc_sw128(smem_addr(sA + s * SM::A_STAGE));
+        const uint64_t bd = umma_desc_sw128(smem_addr(sB + s * SM::B_BYTES));
 #pragma unroll
-        for (int j = 0; j < GEMM_BK / 16; ++j)  // +32 bytes of K per MMA = +2 in 16-byte units
+        for (int j = 0; j < GEMM_BK / 16; ++j) {  // +32 bytes of K per MMA = +2 in 16-byte units
           umma_bf16(tmem_base, ad + 2 * j, bd + 2 * j, idesc, (kt | j) != 0 ? 1u : 0u);
+          if constexpr (SPLIT) umma_bf16(tmem_base, ad + (SM::A_BYTES >> 4) + 2 * j, bd + 2 * j, idesc, 1u);
+        }
         umma_commit(&empty[s]);
       }
       umma_commit(accum);
     }
     __syncwarp();
   } else {
-    // ---------------- weight unpack producers (128 threads)
-    const int t = threadIdx.x - 64;
-    constexpr int UNITS = BN * 2 / 128;
-    Raw32<FMT> cur[UNITS], nxt[UNITS];
-#pragma unroll
-    for (int i = 0; i < UNITS; ++i) {
-      const int u = t + 128 * i;
-      load_unit<FMT>(args.w, n0 + (u >> 1), (u & 1) * 32, cur[i]);
-    }
-    for (int kt = 0; kt < nk; ++kt) {
-      const int s = kt % GEMM_STAGES;
-      const uint32_t ph = (kt / GEMM_STAGES) & 1;
-      if (kt + 1 < nk) {
-#pragma unroll
-        for (int i = 0; i < UNITS; ++i) {
-          const int u = t + 128 * i;
-          load_unit<FMT>(args.w, n0 + (u >> 1), (kt + 1) * GEMM_BK + (u & 1) * 32, nxt[i]);
-        }
-      }
-      mbar_wait(&empty[s], ph ^ 1, FAULT_GEMM_WAIT_EMPTY);
-      uint8_t* stage = sB + s * B_BYTES;
+    // ---------------- weight unpack (256 threads): shared chunk -> swizzled bf16 tile
+    if constexpr (SM::PACKED) {
+      const int t = threadIdx.x - 64;
+      constexpr int UNITS = BN * 2 / GEMM_UNPACK_THREADS;
+      uint32_t row_sc[UNITS];
+      float row_gs[UNITS];
 #pragma unroll
       for (int i = 0; i < UNITS; ++i) {
-        const int u = t + 128 * i;
-        store_unit<FMT>(stage, u >> 1, u & 1, cur[i]);
+        const int r = (t + GEMM_UNPACK_THREADS * i) >> 1;
+        row_sc[i] = FMT == B200_W_TERNARY ? uint32_t(__ldg(reinterpret_cast<const uint16_t*>(args.w.scales) + n0 + r)) : 0u;
+        row_gs[i] = FMT == B200_W_NVFP4 ? __ldg(args.w.row_scale + n0 + r) : 1.0f;
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&full_b[s]);
+      for (int kt = 0; kt < nk; ++kt) {
+        const int s = kt % GEMM_STAGES;
+        const uint32_t ph = (kt / GEMM_STAGES) & 1;
+        mbar_wait(&full_w[s], ph, FAULT_GEMM_WAIT_FULL_W);
+        uint8_t* stage = sB + s * SM::B_BYTES;
 #pragma unroll
-      for (int i = 0; i < UNITS; ++i) cur[i] = nxt[i];
+        for (int i = 0; i < UNITS; ++i) {
+          const int u = t + GEMM_UNPACK_THREADS * i;
+          unpack_unit_smem<FMT>(stage, sW + s * SM::W_BYTES, sS + s * SM::S_BYTES, u >> 1, u & 1, row_sc[i],
+                                row_gs[i], lut);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&full_b[s]);
+      }
     }
 
-    // ---------------- epilogue: this warp owns TMEM lanes 32*(warp%4) .. +31
+    // ---------------- epilogue: TMEM lanes 32*(warp%4)..+31, one column half per warp
     mbar_wait(accum, 0, FAULT_GEMM_WAIT_ACCUM);
     tc_fence_after();
     const int q = warp & 3;
+    const int ch = (warp - 2) >> 2;  // column half
     const int row = m0 + q * 32 + lane;
     const uint32_t tl = tmem_base + (uint32_t(q * 32) << 16);
     if constexpr (EP == B200_EP_SWIGLU) {
+      const int b = ch;  // 128-column block: gate cols 0..63, up cols 64..127
 #pragma unroll 1
-      for (int b = 0; b < BN / 128; ++b) {
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t g[32], u[32];
-          tmem_ld_32x32b_x32(tl + b * 128 + c * 32, g);
-          tmem_ld_32x32b_x32(tl + b * 128 + 64 + c * 32, u);
-          tmem_ld_wait();
-          epilogue_swiglu(args, row, (n0 + b * 128) / 2 + c * 32, g, u);
-        }
+      for (int c = 0; c < 2; ++c) {
+        uint32_t g[32], u[32];
+        tmem_ld_32x32b_x32(tl + b * 128 + c * 32, g);
+        tmem_ld_32x32b_x32(tl + b * 128 + 64 + c * 32, u);
+        tmem_ld_wait();
+        epilogue_swiglu(args, row, (n0 + b * 128) / 2 + c * 32, g, u);
       }
     } else {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = ch * (BN / 64); c < (ch + 1) * (BN / 64); ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tl + c * 32, v);
         tmem_ld_wait();
@@ -290,36 +340,37 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // --------------------------------------------------------------------------- SIMT cross-check
 template <int FMT>
 __device__ __forceinline__ void load_row32_f32(const b200_qweight& w, int n, int k0, float (&out)[32]) {
+  __shared__ uint32_t lut[16];
+  for (int i = threadIdx.x; i < 16; i += blockDim.x) lut[i] = ternary_pair_bits(i);
+  __syncwarp();
   Raw32<FMT> r;
   load_unit<FMT>(w, n, k0, r);
   uint4 u[4];
-  if constexpr (FMT == B200_W_BF16) {
-    u[0] = r.d0;
-    u[1] = r.d1;
-    u[2] = r.d2;
-    u[3] = r.d3;
-  } else {
-    unpack32<FMT>(r.d0, r.sc, r.gs, u);
-  }
+  unit_values<FMT>(r, u, lut);
   const uint16_t* h = reinterpret_cast<const uint16_t*>(u);
 #pragma unroll
   for (int j = 0; j < 32; ++j) out[j] = bf16_to_f32(h[j]);
 }
 
 template <int FMT>
-__device__ float simt_dot(const GemmArgs& a, const uint16_t* x, int ldx, int m, int n) {
+__device__ float simt_dot(const GemmArgs& a, const uint16_t* x, const uint16_t* xl, int ldx, int m, int n) {
   float acc = 0.0f;
   for (int k0 = 0; k0 < a.k; k0 += 32) {
     float wv[32];
     load_row32_f32<FMT>(a.w, n, k0, wv);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) acc = fmaf(bf16_to_f32(x[size_t(m) * ldx + k0 + j]), wv[j], acc);
+    for (int j = 0; j < 32; ++j) {
+      const size_t i = size_t(m) * ldx + k0 + j;
+      const float xv = bf16_to_f32(x[i]) + (xl ? bf16_to_f32(xl[i]) : 0.0f);
+      acc = fmaf(xv, wv[j], acc);
+    }
   }
   return acc;
 }
 
 template <int FMT, int EP>
-__global__ void gemm_simt_kernel(const uint16_t* __restrict__ x, int ldx, const GemmArgs a) {
+__global__ void gemm_simt_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ xl, int ldx,
+                                 const GemmArgs a) {
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   const int m = blockIdx.y;
   const b200_linear_out& o = a.o;
@@ -327,17 +378,18 @@ __global__ void gemm_simt_kernel(const uint16_t* __restrict__ x, int ldx, const 
   if constexpr (EP == B200_EP_SWIGLU) {
     if (2 * n >= o.n_valid) return;
     const int blk = n / 64, i = n % 64;
-    const float g = simt_dot<FMT>(a, x, ldx, m, blk * 128 + i);
-    const float u = simt_dot<FMT>(a, x, ldx, m, blk * 128 + 64 + i);
-    reinterpret_cast<uint16_t*>(o.out)[size_t(m) * o.ldo + n] = f32_to_bf16_rn(silu(g) * u);
+    const float g = simt_dot<FMT>(a, x, xl, ldx, m, blk * 128 + i);
+    const float u = simt_dot<FMT>(a, x, xl, ldx, m, blk * 128 + 64 + i);
+    const float h = silu(g) * u;
+    uint16_t* dst = reinterpret_cast<uint16_t*>(o.out) + size_t(m) * o.ldo + n;
+    const uint16_t hb = f32_to_bf16_rn(h);
+    dst[0] = hb;
+    if (o.lo_offset) dst[o.lo_offset] = f32_to_bf16_rn(h - bf16_to_f32(hb));
   } else {
     if (n >= o.n_valid) return;
-    const float y = simt_dot<FMT>(a, x, ldx, m, n);
+    const float y = simt_dot<FMT>(a, x, xl, ldx, m, n);
     if constexpr (EP == B200_EP_STORE) {
-      if (n >= o.split_n)
-        o.out_f32[size_t(m) * o.ldo_f32 + (n - o.split_n)] = y;
-      else
-        reinterpret_cast<uint16_t*>(o.out)[size_t(m) * o.ldo + n] = f32_to_bf16_rn(y);
+      reinterpret_cast<float*>(o.out)[size_t(m) * o.ldo + n] = y;
     } else {
       reinterpret_cast<float*>(o.out)[size_t(m) * o.ldo + n] += y;
     }
@@ -359,11 +411,11 @@ static int get_encode_fn() {
   return g_encode ? B200_OK : sdb_fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
 }
 
-static int make_act_map(CUtensorMap* map, const uint16_t* x, int m, int k, int ldx) {
+static int make_act_map(CUtensorMap* map, const uint16_t* x, int m, int k, int ldx, int box_rows = GEMM_BM) {
   if (int rc = get_encode_fn()) return rc;
   cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(m)};
   cuuint64_t strides[1] = {cuuint64_t(ldx) * 2};
-  cuuint32_t box[2] = {GEMM_BK, GEMM_BM};
+  cuuint32_t box[2] = {GEMM_BK, cuuint32_t(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -372,24 +424,22 @@ static int make_act_map(CUtensorMap* map, const uint16_t* x, int m, int k, int l
   return B200_OK;
 }
 
-static int check_linear(const uint16_t* x, int m, int k, int ldx, const b200_qweight* w, const b200_linear_out* o) {
+static int check_linear(const uint16_t* x, const uint16_t* xl, int m, int k, int ldx, const b200_qweight* w,
+                        const b200_linear_out* o) {
   if (!x || !w || !o || !w->data || !o->out) return sdb_fail(B200_ERR_ARG, "b200_linear: null pointer");
   if (m <= 0 || k <= 0) return sdb_fail(B200_ERR_SHAPE, "b200_linear: empty shape");
   if (w->k != k) return sdb_fail(B200_ERR_SHAPE, "b200_linear: x and W disagree on k");
   if (k % 128 != 0 || w->n % 256 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_linear: k % 128 and n % 256 must be 0");
-  if (ldx < k || ldx % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15))
-    return sdb_fail(B200_ERR_SHAPE, "b200_linear: x must be 16-byte aligned with ldx a multiple of 8");
-  if (o->n_valid <= 0 || o->n_valid > w->n) return sdb_fail(B200_ERR_SHAPE, "b200_linear: bad n_valid");
+  if (ldx < k || ldx % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(xl) & 15))
+    return sdb_fail(B200_ERR_SHAPE, "b200_linear: x planes must be 16-byte aligned with ldx a multiple of 8");
+  if (o->n_valid <= 0 || o->n_valid > w->n || o->n_valid % 32 != 0)
+    return sdb_fail(B200_ERR_SHAPE, "b200_linear: n_valid must be in (0, n] and a multiple of 32");
   if (o->ldo % 8 != 0 || (reinterpret_cast<uintptr_t>(o->out) & 15))
     return sdb_fail(B200_ERR_SHAPE, "b200_linear: out must be 16-byte aligned with ldo a multiple of 8");
-  if (o->epilogue == B200_EP_STORE && o->split_n < o->n_valid) {
-    if (!o->out_f32 || o->split_n % 32 != 0 || o->ldo_f32 % 4 != 0 || (reinterpret_cast<uintptr_t>(o->out_f32) & 15))
-      return sdb_fail(B200_ERR_SHAPE, "b200_linear: split store needs aligned out_f32, split_n % 32 == 0");
-  }
-  if (o->epilogue == B200_EP_SWIGLU && o->n_valid % 128 != 0)
-    return sdb_fail(B200_ERR_SHAPE, "b200_linear: SwiGLU needs n_valid % 128 == 0");
-  if (o->epilogue == B200_EP_RESID_ADD && o->n_valid % 32 != 0)
-    return sdb_fail(B200_ERR_SHAPE, "b200_linear: residual add needs n_valid % 32 == 0");
+  if (o->epilogue == B200_EP_SWIGLU && (o->n_valid % 128 != 0 || o->lo_offset % 8 != 0))
+    return sdb_fail(B200_ERR_SHAPE, "b200_linear: SwiGLU needs n_valid % 128 == 0 and lo_offset % 8 == 0");
+  if (o->epilogue != B200_EP_SWIGLU && o->ldo < o->n_valid)
+    return sdb_fail(B200_ERR_SHAPE, "b200_linear: ldo < n_valid");
   if (o->epilogue < 0 || o->epilogue > 2) return sdb_fail(B200_ERR_ARG, "b200_linear: unknown epilogue");
   if (w->format < 0 || w->format > 3) return sdb_fail(B200_ERR_FORMAT, "b200_linear: unknown weight format");
   if (w->format != B200_W_BF16 && !w->scales) return sdb_fail(B200_ERR_ARG, "b200_linear: missing scales");
@@ -397,37 +447,61 @@ static int check_linear(const uint16_t* x, int m, int k, int ldx, const b200_qwe
   return B200_OK;
 }
 
-template <int BN, int FMT, int EP>
-static int launch_tc(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
-  constexpr int smem = gemm_smem_bytes<BN>();
-  static bool attr_set = false;  // per instantiation; set before first launch on this device
+static int check_tiles(const b200_qweight* w) {
+  if (w->format == B200_W_BF16) return B200_OK;
+  if (!w->tiles || (tile_scale_row_bytes(w->format) && !w->tile_scales))
+    return sdb_fail(B200_ERR_ARG, "b200_linear: packed weights need their streaming copy (b200_tile_weights)");
+  if ((reinterpret_cast<uintptr_t>(w->tiles) & 15) || (reinterpret_cast<uintptr_t>(w->tile_scales) & 15))
+    return sdb_fail(B200_ERR_SHAPE, "b200_linear: weight tiles must be 16-byte aligned");
+  return B200_OK;
+}
+
+template <int BN, int FMT, int EP, bool SPLIT>
+static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b, const GemmArgs& a,
+                     cudaStream_t st) {
+  constexpr int smem = GemmSmem<BN, FMT, SPLIT>::TOTAL;
+  static_assert(smem <= 227 * 1024, "GEMM shared memory exceeds the 227 KB per-CTA limit");
+  static bool attr_set = false;  // per instantiation; one process drives one device
   if (!attr_set) {
-    SDB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, FMT, EP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    SDB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, FMT, EP, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  smem));
     attr_set = true;
   }
   dim3 grid(a.w.n / BN, (a.m + GEMM_BM - 1) / GEMM_BM);
-  gemm_tc_kernel<BN, FMT, EP><<<grid, GEMM_THREADS, smem, st>>>(map, a);
+  gemm_tc_kernel<BN, FMT, EP, SPLIT><<<grid, GEMM_THREADS, smem, st>>>(map, map_lo, map_b, a);
   SDB_LAUNCH_CHECK();
   return B200_OK;
 }
 
-template <int FMT>
-static int dispatch_ep(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
+template <int FMT, bool SPLIT>
+static int dispatch_ep(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b, const GemmArgs& a,
+                       cudaStream_t st) {
   switch (a.o.epilogue) {
-    case B200_EP_STORE: return launch_tc<256, FMT, B200_EP_STORE>(map, a, st);
-    case B200_EP_RESID_ADD: return launch_tc<256, FMT, B200_EP_RESID_ADD>(map, a, st);
-    default: return launch_tc<256, FMT, B200_EP_SWIGLU>(map, a, st);
+    case B200_EP_STORE: return launch_tc<256, FMT, B200_EP_STORE, SPLIT>(map, map_lo, map_b, a, st);
+    case B200_EP_RESID_ADD: return launch_tc<256, FMT, B200_EP_RESID_ADD, SPLIT>(map, map_lo, map_b, a, st);
+    default: return launch_tc<256, FMT, B200_EP_SWIGLU, SPLIT>(map, map_lo, map_b, a, st);
+  }
+}
+
+template <bool SPLIT>
+static int dispatch_fmt(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b, const GemmArgs& a,
+                        cudaStream_t st) {
+  switch (a.w.format) {
+    case B200_W_BF16: return dispatch_ep<B200_W_BF16, SPLIT>(map, map_lo, map_b, a, st);
+    case B200_W_INT4G128: return dispatch_ep<B200_W_INT4G128, SPLIT>(map, map_lo, map_b, a, st);
+    case B200_W_NVFP4: return dispatch_ep<B200_W_NVFP4, SPLIT>(map, map_lo, map_b, a, st);
+    default: return dispatch_ep<B200_W_TERNARY, SPLIT>(map, map_lo, map_b, a, st);
   }
 }
 
 template <int FMT>
-static int dispatch_simt(const uint16_t* x, int ldx, const GemmArgs& a, cudaStream_t st) {
+static int dispatch_simt(const uint16_t* x, const uint16_t* xl, int ldx, const GemmArgs& a, cudaStream_t st) {
   const int ncols = a.o.epilogue == B200_EP_SWIGLU ? a.o.n_valid / 2 : a.o.n_valid;
   dim3 grid((ncols + 127) / 128, a.m);
   switch (a.o.epilogue) {
-    case B200_EP_STORE: gemm_simt_kernel<FMT, B200_EP_STORE><<<grid, 128, 0, st>>>(x, ldx, a); break;
-    case B200_EP_RESID_ADD: gemm_simt_kernel<FMT, B200_EP_RESID_ADD><<<grid, 128, 0, st>>>(x, ldx, a); break;
-    default: gemm_simt_kernel<FMT, B200_EP_SWIGLU><<<grid, 128, 0, st>>>(x, ldx, a); break;
+    case B200_EP_STORE: gemm_simt_kernel<FMT, B200_EP_STORE><<<grid, 128, 0, st>>>(x, xl, ldx, a); break;
+    case B200_EP_RESID_ADD: gemm_simt_kernel<FMT, B200_EP_RESID_ADD><<<grid, 128, 0, st>>>(x, xl, ldx, a); break;
+    default: gemm_simt_kernel<FMT, B200_EP_SWIGLU><<<grid, 128, 0, st>>>(x, xl, ldx, a); break;
   }
   SDB_LAUNCH_CHECK();
   return B200_OK;
@@ -437,30 +511,37 @@ static int dispatch_simt(const uint16_t* x, int ldx, const GemmArgs& a, cudaStre
 
 using namespace sdb;
 
-extern "C" int b200_linear(const uint16_t* x, int32_t m, int32_t k, int32_t ldx, const b200_qweight* w,
-                           const b200_linear_out* out, b200_stream stream) {
-  if (int rc = check_linear(x, m, k, ldx, w, out)) return rc;
-  CUtensorMap map;
-  if (int rc = make_act_map(&map, x, m, k, ldx)) return rc;
+extern "C" int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m, int32_t k, int32_t ldx,
+                           const b200_qweight* w, const b200_linear_out* out, b200_stream stream) {
+  if (int rc = check_linear(x_hi, x_lo, m, k, ldx, w, out)) return rc;
+  if (int rc = check_tiles(w)) return rc;
+  CUtensorMap map, map_lo, map_b;
+  if (int rc = make_act_map(&map, x_hi, m, k, ldx)) return rc;
+  if (x_lo) {
+    if (int rc = make_act_map(&map_lo, x_lo, m, k, ldx)) return rc;
+  } else {
+    map_lo = map;
+  }
+  if (w->format == B200_W_BF16) {  // the weight tile streams through TMA as [n, k] bf16, 256 rows per box
+    if (reinterpret_cast<uintptr_t>(w->data) & 15) return sdb_fail(B200_ERR_SHAPE, "b200_linear: bf16 W unaligned");
+    if (int rc = make_act_map(&map_b, reinterpret_cast<const uint16_t*>(w->data), w->n, k, k, 256)) return rc;
+  } else {
+    map_b = map;
+  }
   GemmArgs a{*w, *out, m, k};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  switch (w->format) {
-    case B200_W_BF16: return dispatch_ep<B200_W_BF16>(map, a, st);
-    case B200_W_INT4G128: return dispatch_ep<B200_W_INT4G128>(map, a, st);
-    case B200_W_NVFP4: return dispatch_ep<B200_W_NVFP4>(map, a, st);
-    default: return dispatch_ep<B200_W_TERNARY>(map, a, st);
-  }
+  return x_lo ? dispatch_fmt<true>(map, map_lo, map_b, a, st) : dispatch_fmt<false>(map, map_lo, map_b, a, st);
 }
 
-extern "C" int b200_linear_simt(const uint16_t* x, int32_t m, int32_t k, int32_t ldx, const b200_qweight* w,
-                                const b200_linear_out* out, b200_stream stream) {
-  if (int rc = check_linear(x, m, k, ldx, w, out)) return rc;
+extern "C" int b200_linear_simt(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m, int32_t k, int32_t ldx,
+                                const b200_qweight* w, const b200_linear_out* out, b200_stream stream) {
+  if (int rc = check_linear(x_hi, x_lo, m, k, ldx, w, out)) return rc;
   GemmArgs a{*w, *out, m, k};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (w->format) {
-    case B200_W_BF16: return dispatch_simt<B200_W_BF16>(x, ldx, a, st);
-    case B200_W_INT4G128: return dispatch_simt<B200_W_INT4G128>(x, ldx, a, st);
-    case B200_W_NVFP4: return dispatch_simt<B200_W_NVFP4>(x, ldx, a, st);
-    default: return dispatch_simt<B200_W_TERNARY>(x, ldx, a, st);
+    case B200_W_BF16: return dispatch_simt<B200_W_BF16>(x_hi, x_lo, ldx, a, st);
+    case B200_W_INT4G128: return dispatch_simt<B200_W_INT4G128>(x_hi, x_lo, ldx, a, st);
+    case B200_W_NVFP4: return dispatch_simt<B200_W_NVFP4>(x_hi, x_lo, ldx, a, st);
+    default: return dispatch_simt<B200_W_TERNARY>(x_hi, x_lo, ldx, a, st);
   }
 }

@@ -23,9 +23,17 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const uint16_t* __
   }
 }
 
-// One warp per row: y = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w)).  hidden % 128 == 0.
+// hi = bf16_rn(x), lo = bf16_rn(x - hi) for two values, packed.
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const uint16_t ha = f32_to_bf16_rn(a), hb = f32_to_bf16_rn(b);
+  hi = uint32_t(ha) | (uint32_t(hb) << 16);
+  lo = pack_bf16x2(a - bf16_to_f32(ha), b - bf16_to_f32(hb));
+}
+
+// One warp per row: y = x * rsqrt(mean(x^2) + eps) * (1 + w) as hi/lo bf16 planes.
+// hidden % 128 == 0.
 __global__ void rmsnorm_kernel(const float* __restrict__ x, int rows, int hidden, const float* __restrict__ w,
-                               float eps, uint16_t* __restrict__ out) {
+                               float eps, uint16_t* __restrict__ out, long long lo_offset) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -38,11 +46,15 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, int rows, int hidden
   ss = warp_sum(ss);
   const float r = rsqrtf(ss / float(hidden) + eps);
   uint2* o = reinterpret_cast<uint2*>(out + size_t(row) * hidden);
+  uint2* ol = reinterpret_cast<uint2*>(out + lo_offset + size_t(row) * hidden);
   const float4* wr = reinterpret_cast<const float4*>(w);
   for (int i = lane; i < hidden / 4; i += 32) {
     float4 v = xr[i], g = __ldg(wr + i);
-    o[i] = make_uint2(pack_bf16x2(v.x * r * (1.0f + g.x), v.y * r * (1.0f + g.y)),
-                      pack_bf16x2(v.z * r * (1.0f + g.z), v.w * r * (1.0f + g.w)));
+    uint2 hi, lo;
+    split2(v.x * r * (1.0f + g.x), v.y * r * (1.0f + g.y), hi.x, lo.x);
+    split2(v.z * r * (1.0f + g.z), v.w * r * (1.0f + g.w), hi.y, lo.y);
+    o[i] = hi;
+    if (lo_offset) ol[i] = lo;
   }
 }
 
@@ -175,10 +187,12 @@ int sdb_embed_vocab(const int32_t* ids, int32_t n_tokens, const uint16_t* table,
 }
 
 extern "C" int b200_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
-                            b200_stream stream) {
+                            int64_t lo_offset, b200_stream stream) {
   if (!x || !w || !out) return sdb_fail(B200_ERR_ARG, "b200_rmsnorm: null pointer");
-  if (rows <= 0 || hidden % 128 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_rmsnorm: hidden % 128 must be 0");
-  rmsnorm_kernel<<<(rows + 7) / 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, rows, hidden, w, eps, out);
+  if (rows <= 0 || hidden % 128 != 0 || lo_offset % 8 != 0)
+    return sdb_fail(B200_ERR_SHAPE, "b200_rmsnorm: hidden % 128 and lo_offset % 8 must be 0");
+  rmsnorm_kernel<<<(rows + 7) / 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, rows, hidden, w, eps, out,
+                                                                                   lo_offset);
   SDB_LAUNCH_CHECK();
   return B200_OK;
 }

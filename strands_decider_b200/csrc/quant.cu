@@ -112,6 +112,9 @@ __global__ void quant_ternary_kernel(const float* __restrict__ w, int n, int k, 
 // Standalone dequantiser: one thread per 32 weights, through the GEMM's own unpackers.
 template <int FMT>
 __global__ void dequant_kernel(b200_qweight w, uint16_t* __restrict__ out) {
+  __shared__ uint32_t lut[16];
+  if (threadIdx.x < 16) lut[threadIdx.x] = ternary_pair_bits(threadIdx.x);
+  __syncthreads();
   const int per_row = w.k / 32;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= w.n * per_row) return;
@@ -125,15 +128,64 @@ __global__ void dequant_kernel(b200_qweight w, uint16_t* __restrict__ out) {
     uint32_t sc;
     float gs;
     load32<FMT>(w, row, k0, raw, sc, gs);
-    unpack32<FMT>(raw, sc, gs, dst);
+    unpack32<FMT>(raw, sc, gs, dst, lut);
   }
   uint4* o = reinterpret_cast<uint4*>(out + size_t(row) * w.k + k0);
   for (int c = 0; c < 4; ++c) o[c] = dst[c];
 }
 
+// Streaming copy for the GEMM: one thread per (row, 64-column stage) copies the row's
+// packed bytes of that stage (and its scales) into the stage's contiguous chunk.
+__global__ void tile_kernel(b200_qweight w, uint8_t* __restrict__ tiles, uint8_t* __restrict__ tile_scales) {
+  const int stages = w.k / 64;
+  const long idx = blockIdx.x * long(blockDim.x) + threadIdx.x;
+  if (idx >= long(w.n) * stages) return;
+  const int row = int(idx / stages), st = int(idx % stages);
+  const int tile = row / 256, r = row % 256;
+  const size_t chunk = size_t(tile) * stages + st;
+  const int rb = tile_row_bytes(w.format);
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(w.data) + size_t(row) * (size_t(w.k) * rb / 64) + size_t(st) * rb;
+  uint8_t* dst = tiles + (chunk * 256 + r) * rb;
+  for (int b = 0; b < rb; b += 4) *reinterpret_cast<uint32_t*>(dst + b) = *reinterpret_cast<const uint32_t*>(src + b);
+  if (w.format == B200_W_INT4G128) {
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(w.scales) + size_t(row) * (w.k / 128) + st / 2;
+    reinterpret_cast<uint16_t*>(tile_scales)[chunk * 256 + r] = *sc;
+  } else if (w.format == B200_W_NVFP4) {
+    const uint8_t* sc = reinterpret_cast<const uint8_t*>(w.scales) + size_t(row) * (w.k / 16) + st * 4;
+    uint8_t* d = tile_scales + (chunk * 256 + r) * 4;
+    for (int b = 0; b < 4; ++b) d[b] = sc[b];
+  }
+}
+
 }  // namespace sdb
 
 using namespace sdb;
+
+extern "C" int b200_tile_bytes(int32_t format, int32_t n, int32_t k, size_t* tile_bytes, size_t* tile_scale_bytes) {
+  if (!tile_bytes || !tile_scale_bytes) return sdb_fail(B200_ERR_ARG, "b200_tile_bytes: null pointer");
+  if (n <= 0 || k <= 0 || n % 256 != 0 || k % 128 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_tile_bytes: bad shape");
+  if (format < 0 || format > 3) return sdb_fail(B200_ERR_FORMAT, "b200_tile_bytes: unknown format");
+  if (format == B200_W_BF16) {
+    *tile_bytes = *tile_scale_bytes = 0;
+    return B200_OK;
+  }
+  *tile_bytes = size_t(n) * (k / 64) * tile_row_bytes(format);
+  *tile_scale_bytes = size_t(n) * (k / 64) * tile_scale_row_bytes(format);
+  return B200_OK;
+}
+
+extern "C" int b200_tile_weights(const b200_qweight* w, void* tiles, void* tile_scales, b200_stream stream) {
+  if (!w || !w->data) return sdb_fail(B200_ERR_ARG, "b200_tile_weights: null pointer");
+  if (w->n % 256 != 0 || w->k % 128 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_tile_weights: bad shape");
+  if (w->format == B200_W_BF16) return B200_OK;
+  if (!tiles || (tile_scale_row_bytes(w->format) && !tile_scales))
+    return sdb_fail(B200_ERR_ARG, "b200_tile_weights: null output");
+  const long total = long(w->n) * (w->k / 64);
+  tile_kernel<<<int((total + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      *w, reinterpret_cast<uint8_t*>(tiles), reinterpret_cast<uint8_t*>(tile_scales));
+  SDB_LAUNCH_CHECK();
+  return B200_OK;
+}
 
 extern "C" int b200_quantize(int32_t format, const float* w, int32_t n, int32_t k, void* data, void* scales,
                              float* row_scale, b200_stream stream) {

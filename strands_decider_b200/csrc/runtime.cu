@@ -23,11 +23,11 @@ int sdb_embed_vocab(const int32_t* ids, int32_t n_tokens, const uint16_t* table,
                     cudaStream_t st);
 int sdb_decide_vocab(const float* x, int32_t hidden, const float* final_norm, float eps, const uint16_t* table,
                      const b200_decide_args* d, int vocab, int n_tokens, cudaStream_t st);
-int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const uint16_t* mix, int32_t ld_mix, const float* ab,
-                  uint16_t* out, const b200_prefix_pool* pool, int32_t layer, cudaStream_t st);
-int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const uint16_t* qkv, int32_t ld_qkv, uint16_t* q_buf,
-                  uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, const b200_prefix_pool* pool, int32_t layer,
-                  cudaStream_t st);
+int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix, int32_t ld_mix, uint16_t* out,
+                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, cudaStream_t st);
+int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qkv, int32_t ld_qkv, uint16_t* q_buf,
+                  uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool,
+                  int32_t layer, cudaStream_t st);
 
 extern "C" const char* b200_last_error(void) { return g_last_error.c_str(); }
 extern "C" int b200_version(void) { return 100; }
@@ -56,6 +56,9 @@ struct b200_model {
   int value_dim() const { return cfg.gdn_heads * cfg.gdn_dv; }
   int conv_dim() const { return 2 * key_dim() + value_dim(); }
   int gdn_split() const { return conv_dim() + value_dim(); }
+  // columns the GDN in-projection writes: [q|k|v|z|b|a] rounded up to a multiple of 32
+  // (the padding columns come from zero weight rows)
+  int gdn_in_cols() const { return (gdn_split() + 2 * cfg.gdn_heads + 31) / 32 * 32; }
   int attn_qkv() const { return 2 * cfg.attn_heads * cfg.head_dim + 2 * cfg.attn_kv_heads * cfg.head_dim; }
   int attn_o_in() const { return cfg.attn_heads * cfg.head_dim; }
   bool has_gdn() const {
@@ -72,9 +75,16 @@ struct b200_model {
 
 namespace {
 
+// Workspace (all offsets 256-byte aligned), for T tokens:
+//   x    fp32 [T, hidden]            residual stream (first, so callers can read it back)
+//   xn   2 x bf16 [T, hidden]        normed activations as hi/lo planes (GEMM input)
+//   mix  fp32 [T, mix_cols]          in-projection outputs (GDN [q|k|v|z|b|a], attention [q,gate|k|v])
+//   act  2 x bf16 [T, act_cols]      mixer outputs / SwiGLU outputs as hi/lo planes (GEMM input)
+//   q, k, v  bf16                    attention scratch (post norm + RoPE)
 struct WsLayout {
-  size_t x, xn, big, ab, mid, q, k, v, total;
-  int big_cols, mid_cols;
+  size_t x, xn, mix, act, q, k, v, total;
+  int mix_cols, act_cols;
+  long long xn_lo, act_lo;  // element offsets of the lo planes
 };
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -82,10 +92,10 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 WsLayout layout(const b200_model& m, int T) {
   WsLayout L{};
   const auto& c = m.cfg;
-  L.big_cols = c.inter;
-  if (m.has_gdn()) L.big_cols = std::max(L.big_cols, m.gdn_split());
-  if (m.has_attn()) L.big_cols = std::max(L.big_cols, m.attn_qkv());
-  L.mid_cols = std::max(m.has_gdn() ? m.value_dim() : 0, m.has_attn() ? m.attn_o_in() : 0);
+  L.mix_cols = 32;
+  if (m.has_gdn()) L.mix_cols = std::max(L.mix_cols, m.gdn_in_cols());
+  if (m.has_attn()) L.mix_cols = std::max(L.mix_cols, m.attn_qkv());
+  L.act_cols = std::max({c.inter, m.has_gdn() ? m.value_dim() : 0, m.has_attn() ? m.attn_o_in() : 0});
   size_t off = 0;
   auto take = [&](size_t bytes) {
     size_t o = off;
@@ -93,10 +103,13 @@ WsLayout layout(const b200_model& m, int T) {
     return o;
   };
   L.x = take(size_t(T) * c.hidden * 4);
-  L.xn = take(size_t(T) * c.hidden * 2);
-  L.big = take(size_t(T) * L.big_cols * 2);
-  L.ab = take(size_t(T) * 2 * std::max(c.gdn_heads, 1) * 4);
-  L.mid = take(size_t(T) * std::max(L.mid_cols, 8) * 2);
+  const size_t xn_plane = align256(size_t(T) * c.hidden * 2);
+  L.xn = take(2 * xn_plane);
+  L.xn_lo = (long long)(xn_plane / 2);
+  L.mix = take(size_t(T) * L.mix_cols * 4);
+  const size_t act_plane = align256(size_t(T) * L.act_cols * 2);
+  L.act = take(2 * act_plane);
+  L.act_lo = (long long)(act_plane / 2);
   const size_t kvb = size_t(T) * std::max(c.attn_kv_heads * c.head_dim, 8) * 2;
   L.q = take(size_t(T) * std::max(m.attn_o_in(), 8) * 2);
   L.k = take(kvb);
@@ -213,40 +226,41 @@ extern "C" int b200_model_forward(b200_model* m, const int32_t* ids, const b200_
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   float* x = reinterpret_cast<float*>(ws + L.x);
   uint16_t* xn = reinterpret_cast<uint16_t*>(ws + L.xn);
-  uint16_t* big = reinterpret_cast<uint16_t*>(ws + L.big);
-  float* ab = reinterpret_cast<float*>(ws + L.ab);
-  uint16_t* mid = reinterpret_cast<uint16_t*>(ws + L.mid);
+  float* mix = reinterpret_cast<float*>(ws + L.mix);
+  uint16_t* act = reinterpret_cast<uint16_t*>(ws + L.act);
   uint16_t* qb = reinterpret_cast<uint16_t*>(ws + L.q);
   uint16_t* kb = reinterpret_cast<uint16_t*>(ws + L.k);
   uint16_t* vb = reinterpret_cast<uint16_t*>(ws + L.v);
+  const uint16_t* xn_lo = xn + L.xn_lo;
 
   int rc;
   if ((rc = sdb_embed_vocab(ids, T, m->embed, c.hidden, x, c.vocab, st))) return rc;
   for (int li = 0; li < c.n_layers; ++li) {
     const b200_layer_weights& w = m->layers[li];
-    if ((rc = b200_rmsnorm(x, T, c.hidden, w.input_norm, c.eps, xn, stream))) return rc;
+    if ((rc = b200_rmsnorm(x, T, c.hidden, w.input_norm, c.eps, xn, L.xn_lo, stream))) return rc;
+    int mix_in_dim;
     if (c.layer_kind[li] == B200_LAYER_GDN) {
-      const int split = m->gdn_split();
-      b200_linear_out o{B200_EP_STORE, split + 2 * c.gdn_heads, big, split, ab, 2 * c.gdn_heads, split};
-      if ((rc = b200_linear(xn, T, c.hidden, c.hidden, &w.mix_in, &o, stream))) return rc;
-      if ((rc = sdb_gdn_mixer(&w.gdn, seqs, big, split, ab, mid, pool, m->kind_index[li], st))) return rc;
-      b200_linear_out r{B200_EP_RESID_ADD, c.hidden, x, c.hidden, nullptr, 0, c.hidden};
-      if ((rc = b200_linear(mid, T, m->value_dim(), m->value_dim(), &w.mix_out, &r, stream))) return rc;
+      const int n = m->gdn_in_cols();
+      b200_linear_out o{B200_EP_STORE, n, mix, n, 0};
+      if ((rc = b200_linear(xn, xn_lo, T, c.hidden, c.hidden, &w.mix_in, &o, stream))) return rc;
+      if ((rc = sdb_gdn_mixer(&w.gdn, seqs, mix, n, act, L.act_lo, pool, m->kind_index[li], st))) return rc;
+      mix_in_dim = m->value_dim();
     } else {
       const int n = m->attn_qkv();
-      b200_linear_out o{B200_EP_STORE, n, big, n, nullptr, 0, n};
-      if ((rc = b200_linear(xn, T, c.hidden, c.hidden, &w.mix_in, &o, stream))) return rc;
+      b200_linear_out o{B200_EP_STORE, n, mix, n, 0};
+      if ((rc = b200_linear(xn, xn_lo, T, c.hidden, c.hidden, &w.mix_in, &o, stream))) return rc;
       b200_attn_params ap{c.attn_heads, c.attn_kv_heads, c.head_dim, c.rope_dim, c.max_pos, c.eps,
                           w.q_norm, w.k_norm, m->rope_cos, m->rope_sin};
-      if ((rc = sdb_attention(&ap, seqs, big, n, qb, kb, vb, mid, pool, m->kind_index[li], st))) return rc;
-      b200_linear_out r{B200_EP_RESID_ADD, c.hidden, x, c.hidden, nullptr, 0, c.hidden};
-      if ((rc = b200_linear(mid, T, m->attn_o_in(), m->attn_o_in(), &w.mix_out, &r, stream))) return rc;
+      if ((rc = sdb_attention(&ap, seqs, mix, n, qb, kb, vb, act, L.act_lo, pool, m->kind_index[li], st))) return rc;
+      mix_in_dim = m->attn_o_in();
     }
-    if ((rc = b200_rmsnorm(x, T, c.hidden, w.post_norm, c.eps, xn, stream))) return rc;
-    b200_linear_out g{B200_EP_SWIGLU, 2 * c.inter, big, c.inter, nullptr, 0, 2 * c.inter};
-    if ((rc = b200_linear(xn, T, c.hidden, c.hidden, &w.gate_up, &g, stream))) return rc;
-    b200_linear_out d{B200_EP_RESID_ADD, c.hidden, x, c.hidden, nullptr, 0, c.hidden};
-    if ((rc = b200_linear(big, T, c.inter, c.inter, &w.down, &d, stream))) return rc;
+    b200_linear_out r{B200_EP_RESID_ADD, c.hidden, x, c.hidden, 0};
+    if ((rc = b200_linear(act, act + L.act_lo, T, mix_in_dim, mix_in_dim, &w.mix_out, &r, stream))) return rc;
+    if ((rc = b200_rmsnorm(x, T, c.hidden, w.post_norm, c.eps, xn, L.xn_lo, stream))) return rc;
+    b200_linear_out g{B200_EP_SWIGLU, 2 * c.inter, act, c.inter, L.act_lo};
+    if ((rc = b200_linear(xn, xn_lo, T, c.hidden, c.hidden, &w.gate_up, &g, stream))) return rc;
+    b200_linear_out d{B200_EP_RESID_ADD, c.hidden, x, c.hidden, 0};
+    if ((rc = b200_linear(act, act + L.act_lo, T, c.inter, c.inter, &w.down, &d, stream))) return rc;
   }
   if (decide && decide->n_rows > 0) {
     if ((rc = sdb_decide_vocab(x, c.hidden, m->final_norm, c.eps, m->embed, decide, c.vocab, T, st))) return rc;

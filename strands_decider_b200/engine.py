@@ -1,0 +1,240 @@
+"""The `--device b200` engine: the reference's engine API with the prefill on B200.
+
+strands-decider's device plugins override exactly two methods of `SystemOneEngine`
+(src/strands_decider/infer.py:127-411): `_slot_probs_batched` (infer.py:253-279) and
+`_slot_probs_shared_prefix` (infer.py:281-337); `MLXEngine` is the precedent
+(src/strands_decider/mlx_engine.py:121-205). `B200SlotProbs` is that pair, running the
+torso prefill, the prefix-state cache and the option-token readout on the GPU through the
+native runtime (runtime.DecisionModel -> libstrands_b200.so). It works on top of:
+
+  * the reference's own engine, when strands_decider is installed:
+    `reference_engine_class()` returns `class B200Engine(B200SlotProbs, SystemOneEngine)`,
+    so rendering, tokenisation, `_fit`, batching, temperatures and the answer read-back
+    are the reference's own code (the MLX pattern);
+  * `B200Engine`, a standalone mirror of the engine's host logic (`_fit`,
+    `_temperatures`, `_option_token_ids`, `evaluate`) for machines without the reference.
+
+Contract of both methods (infer.py:253-337): return (probs [n, K] float32 on the CPU with
+entries past each row's n_slots equal to 0, input-token count). The readout is the
+frozen torso's option-number distribution (`frozen_slot_log_probs`, modeling.py:412-438):
+slot k is the tied-embedding row of the token "k+1".
+"""
+
+from __future__ import annotations
+
+import threading
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+
+from .runtime import KIND, DecisionModel
+
+
+@dataclass
+class EngineConfig:
+    """Mirror of infer.EngineConfig (infer.py:55-66) with device "b200"."""
+
+    device: str = "b200"
+    use_prefix_cache: bool = True
+    max_batch: int = 32
+    model_name: str = "strands-decider-0.1.0"
+    max_question_fraction: float = 0.75
+    strict_window: bool = False
+
+
+@dataclass
+class DeciderConfig:
+    """The fields of StrandsDeciderConfig (modeling.py:43-97) the engine reads."""
+
+    max_length: int = 3072
+    num_slots: int = 24
+    head_type: str = "option_token"
+    temperature: float = 1.0
+    temperature_by_kind: dict[str, float] = field(default_factory=dict)
+    ordinal_smoothing: float = 0.0
+
+
+class _Readout:
+    """What the engine reads from StrandsDeciderModel besides the torso (as mlx_engine._Readout)."""
+
+    def __init__(self, config: Any, tokenizer: Any):
+        self.config = config
+        self.tokenizer = tokenizer
+
+
+def option_token_ids(tokenizer: Any, num_slots: int) -> list[int]:
+    """slot k -> the single token of "k+1" (modeling.py:359-373); stops at the first slot
+    whose number is not one token."""
+    out = []
+    for k in range(num_slots):
+        ids = tokenizer.encode(str(k + 1), add_special_tokens=False)
+        if len(ids) != 1:
+            break
+        out.append(int(ids[0]))
+    return out
+
+
+class B200SlotProbs:
+    """The two device overrides. Expects the SystemOneEngine attributes: `cfg`, `model`
+    (with `.config`), `tok`, `_fit`, `_temperatures`, plus `_rt` (a DecisionModel)."""
+
+    _rt: DecisionModel
+
+    def _option_rows(self, n_slots: list[int]) -> list[list[int]]:
+        ids = getattr(self, "_opt_ids", None)
+        if ids is None:
+            ids = self._opt_ids = option_token_ids(self.tok, self.model.config.num_slots)
+        for n in n_slots:
+            if n > len(ids):
+                raise ValueError(
+                    f"question has {n} options but the option-token readout has {len(ids)} single-token "
+                    f"option numbers; split the question")
+        return [ids[:n] for n in n_slots]
+
+    def _temps(self, kinds: list[str]) -> list[float]:
+        t = self._temperatures(kinds)
+        return [float(x) for x in (t.tolist() if isinstance(t, torch.Tensor) else t)]
+
+    def _slot_probs_batched(self, state_text: str, question_texts: list[str], n_slots: list[int], kinds: list[str],
+                            rendered: Any = None) -> tuple[torch.Tensor, int]:
+        """infer.py:253-279 on the device: every (state + question) forwarded whole."""
+        s, q = self._fit(state_text, question_texts)
+        rows = [s + qi for qi in q]
+        dec = self._rt.score_prompts(rows, self._option_rows(n_slots), n_slots, kinds, self._temps(kinds),
+                                     getattr(self.model.config, "ordinal_smoothing", 0.0))
+        return dec.probs.float().cpu(), sum(len(r) for r in rows)
+
+    def _slot_probs_shared_prefix(self, state_text: str, question_texts: list[str], n_slots: list[int],
+                                  kinds: list[str], rendered: Any = None) -> tuple[torch.Tensor, int]:
+        """infer.py:281-337 on the device: the state once into a pool slot, every suffix
+        against it in place (no `_expand_cache` copies)."""
+        s, q = self._fit(state_text, question_texts)
+        self._rt.prefill_states([s], [0])
+        dec = self._rt.score_suffixes(q, [0] * len(q), self._option_rows(n_slots), n_slots, kinds,
+                                      self._temps(kinds), getattr(self.model.config, "ordinal_smoothing", 0.0))
+        return dec.probs.float().cpu(), len(s) + sum(len(x) for x in q)
+
+
+class B200Engine(B200SlotProbs):
+    """Standalone engine: the host logic of SystemOneEngine restated (for machines where the
+    reference is not installed), with the device overrides. One evaluation at a time."""
+
+    def __init__(self, runtime: DecisionModel, tokenizer: Any, decider_config: Any = None,
+                 config: EngineConfig | None = None):
+        self.cfg = config or EngineConfig()
+        self.model = _Readout(decider_config or DeciderConfig(), tokenizer)
+        self.tok = tokenizer
+        self.device = "cpu"  # where the small index/temperature tensors live, as in MLXEngine
+        self._rt = runtime
+        self._lock = threading.Lock()
+        self._last_offsets: list = []
+
+    def _temperatures(self, kinds: list[str]) -> torch.Tensor:
+        """infer.py:163-171."""
+        cfg = self.model.config
+        by_kind = getattr(cfg, "temperature_by_kind", None) or {}
+        return torch.tensor([float(by_kind.get(k, cfg.temperature)) for k in kinds], dtype=torch.float32)
+
+    def _fit(self, state_text: str, question_texts: list[str]) -> tuple[list[int], list[list[int]]]:
+        """infer.py:174-219: the question gets first claim on the window and is cut from the front."""
+        max_len = self.model.config.max_length
+        enc = self.tok(question_texts, add_special_tokens=False, return_offsets_mapping=True)
+        q = enc["input_ids"]
+        offs = enc["offset_mapping"]
+        longest = max(len(x) for x in q)
+        if self.cfg.strict_window:
+            s = self.tok(state_text, add_special_tokens=True)["input_ids"]
+            if len(s) + longest > max_len:
+                raise ValueError(f"prompt of {len(s) + longest} tokens exceeds the context window of "
+                                 f"{max_len} tokens")
+            self._last_offsets = list(offs)
+            return s, q
+        reserve = min(longest, max(1, int(max_len * self.cfg.max_question_fraction)))
+        cut = [max(0, len(x) - reserve) for x in q]
+        self._last_offsets = [o[c:] for o, c in zip(offs, cut, strict=True)]
+        q = [x[c:] for x, c in zip(q, cut, strict=True)]
+        s = self.tok(state_text, add_special_tokens=True, truncation=True,
+                     max_length=max(1, max_len - reserve))["input_ids"]
+        return s, q
+
+    def evaluate(self, request: Any) -> Any:
+        """infer.py:341-408 (needs strands_decider's prompting and schema modules)."""
+        with self._lock:
+            try:
+                from strands_decider.infer import _to_answer
+                from strands_decider.prompting import render_question, render_state
+                from strands_decider.schema import SystemOneResponse, Usage
+            except ImportError as e:  # pragma: no cover - depends on the host install
+                raise RuntimeError("evaluate() needs the strands-decider package for prompt rendering and "
+                                   "answer types; the token-level API (_slot_probs_*) does not") from e
+            if getattr(request, "images", None):
+                raise ValueError("this engine has no vision tower; serve with --vision for images")
+            names = list(request.questions.keys())
+            rendered = [render_question(request.questions[n]) for n in names]
+            state_text = render_state(request.state)
+            answers, total = {}, 0
+            for start in range(0, len(names), self.cfg.max_batch):
+                chunk = slice(start, start + self.cfg.max_batch)
+                rq = rendered[chunk]
+                slots = [r.n_slots for r in rq]
+                kinds = [r.kind for r in rq]
+                texts = [r.text for r in rq]
+                if self.cfg.use_prefix_cache and len(rq) > 1:
+                    probs, ntok = self._slot_probs_shared_prefix(state_text, texts, slots, kinds, rendered=rq)
+                else:
+                    probs, ntok = self._slot_probs_batched(state_text, texts, slots, kinds, rendered=rq)
+                total += ntok
+                for i, name in enumerate(names[chunk]):
+                    answers[name] = _to_answer(rq[i], probs[i, : rq[i].n_slots].tolist(),
+                                               ordinal_smoothing=self.model.config.ordinal_smoothing)
+            return SystemOneResponse(model=self.cfg.model_name, answers=answers,
+                                     usage=Usage(input_tokens=total, output_tokens=len(names)))
+
+
+def reference_engine_class():
+    """`class B200Engine(B200SlotProbs, strands_decider.infer.SystemOneEngine)`, built on
+    the installed reference (raises ImportError when it is not installed)."""
+    from strands_decider.infer import SystemOneEngine
+
+    class ReferenceB200Engine(B200SlotProbs, SystemOneEngine):
+        def __init__(self, runtime: DecisionModel, readout: Any, config: Any):
+            # Not SystemOneEngine.__init__: that moves a torch torso to a torch device
+            # (mlx_engine.py:124-137 does the same).
+            self.cfg = config
+            self.model = readout
+            self.tok = readout.tokenizer
+            self.device = "cpu"
+            self._rt = runtime
+            self._lock = threading.Lock()
+
+        def evaluate(self, request):
+            with self._lock:
+                return super().evaluate(request)
+
+    return ReferenceB200Engine
+
+
+def b200_available() -> bool:
+    """True when a CUDA device of compute capability 10.x is visible and the library loads."""
+    if not torch.cuda.is_available():
+        return False
+    if torch.cuda.get_device_capability(0)[0] != 10:
+        return False
+    try:
+        from . import _lib
+
+        _lib.load()
+    except Exception:
+        return False
+    return True
+
+
+def require_b200() -> None:
+    """The device-registration check (infer.py:516-519 convention): refuse before loading."""
+    if not b200_available():
+        raise RuntimeError("device 'b200' needs an NVIDIA B200 (sm_100a) and the built library: "
+                           "python -m strands_decider_b200.build")
+
+
+KINDS = KIND

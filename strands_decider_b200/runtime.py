@@ -89,8 +89,7 @@ class DecisionModel:
         n_attn = sum(1 for t in s.layer_types if t == ATTN)
         self.pool_slots, self.kv_capacity = slots, kv_tokens
         self.gdn_state = torch.zeros(max(n_gdn, 1), slots, s.gdn_heads, s.gdn_dk, s.gdn_dv, device=dev)
-        self.conv_hist = torch.zeros(max(n_gdn, 1), slots, s.conv_width - 1, s.conv_dim, dtype=torch.bfloat16,
-                                     device=dev)
+        self.conv_hist = torch.zeros(max(n_gdn, 1), slots, s.conv_width - 1, s.conv_dim, device=dev)
         self.k_cache = torch.zeros(max(n_attn, 1), kv_tokens, s.attn_kv_heads, s.head_dim, dtype=torch.bfloat16,
                                    device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)

@@ -25,11 +25,32 @@ class PackedWeight:
     data: torch.Tensor
     scales: torch.Tensor | None = None
     row_scale: torch.Tensor | None = None
+    tiles: torch.Tensor | None = None        # the GEMM's streaming copy (b200_tile_weights)
+    tile_scales: torch.Tensor | None = None
 
-    def qweight(self) -> _lib.QWeight:
+    def _base(self) -> _lib.QWeight:
         return _lib.QWeight(_lib.FMT[self.fmt], self.n, self.k, _lib.ptr(self.data),
                             _lib.ptr(self.scales) if self.scales is not None else None,
-                            _lib.ptr(self.row_scale) if self.row_scale is not None else None)
+                            _lib.ptr(self.row_scale) if self.row_scale is not None else None, None, None)
+
+    def ensure_tiles(self) -> None:
+        """Build the per-(256-row tile, 64-column stage) streaming copy the GEMM reads."""
+        if self.fmt == "bf16" or self.tiles is not None or self.n % 256 != 0:
+            return
+        tb, sb = C.c_size_t(), C.c_size_t()
+        _lib.check(_lib.load().b200_tile_bytes(_lib.FMT[self.fmt], self.n, self.k, C.byref(tb), C.byref(sb)))
+        self.tiles = torch.empty(tb.value, dtype=torch.uint8, device=self.data.device)
+        self.tile_scales = torch.empty(max(sb.value, 16), dtype=torch.uint8, device=self.data.device)
+        base = self._base()
+        _lib.call("b200_tile_weights", C.byref(base), _lib.ptr(self.tiles), _lib.ptr(self.tile_scales),
+                  _lib.stream_ptr())
+
+    def qweight(self) -> _lib.QWeight:
+        self.ensure_tiles()
+        q = self._base()
+        q.tiles = _lib.ptr(self.tiles) if self.tiles is not None else None
+        q.tile_scales = _lib.ptr(self.tile_scales) if self.tile_scales is not None else None
+        return q
 
     def parts(self) -> list[tuple[str, torch.Tensor]]:
         out = [("data", self.data)]
@@ -45,6 +66,7 @@ class PackedWeight:
         return PackedWeight(self.fmt, n, self.k, sel(self.data), sel(self.scales), sel(self.row_scale))
 
     def nbytes(self) -> int:
+        """Bytes of the canonical packed weight (the streaming copy duplicates them)."""
         return sum(t.numel() * t.element_size() for _, t in self.parts())
 
 
@@ -156,6 +178,9 @@ class DeviceWeights:
                 L["q_norm"] = sp["self_attn.q_norm.weight"]
                 L["k_norm"] = sp["self_attn.k_norm.weight"]
             self.layers.append(L)
+        for L in self.layers:
+            for key in ("mix_in", "mix_out", "gate_up", "down"):
+                L[key].ensure_tiles()
         torch.cuda.synchronize()
         return self
 
@@ -189,9 +214,10 @@ def packed_to_numpy(pw: PackedWeight) -> dict:
     """Device packed weight -> the dict oracle.quant expects (CPU numpy, unsigned views)."""
     import numpy as np
 
-    out = {"data": pw.data.cpu().numpy()}
     if pw.fmt == "bf16":
-        out["data"] = pw.data.view(torch.int16).cpu().numpy().view(np.uint16)
+        out = {"data": pw.data.view(torch.int16).cpu().numpy().view(np.uint16)}
+    else:
+        out = {"data": pw.data.cpu().numpy()}
     if pw.scales is not None:
         s = pw.scales.cpu().numpy()
         out["scales"] = s.view(np.uint16) if s.dtype == np.int16 else s

@@ -52,7 +52,7 @@ def test_null_arguments_return_status_not_abort(lib):
 
     o = _lib.LinearOut()
     w = _lib.QWeight()
-    assert lib.b200_linear(None, 1, 128, 128, C.byref(w), C.byref(o), None) == 1
+    assert lib.b200_linear(None, None, 1, 128, 128, C.byref(w), C.byref(o), None) == 1
     assert b"null" in lib.b200_last_error()
     assert lib.b200_quantize(1, None, 1, 128, None, None, None, None) == 1
     assert lib.b200_decide(None, 64, None, 1e-6, None, None, None) == 1
@@ -65,12 +65,17 @@ def test_linear_shape_checks_on_host(lib):
     p = C.cast(buf, C.c_void_p).value
     p16 = (p + 15) // 16 * 16
     w = _lib.QWeight(1, 256, 1000, p16, p16, None)   # k not a multiple of 128
-    o = _lib.LinearOut(0, 256, p16, 256, None, 0, 256)
-    assert lib.b200_linear(p16, 4, 1000, 1000, C.byref(w), C.byref(o), None) == 2
+    o = _lib.LinearOut(0, 256, p16, 256, 0)
+    assert lib.b200_linear(p16, None, 4, 1000, 1000, C.byref(w), C.byref(o), None) == 2
     w = _lib.QWeight(1, 200, 1024, p16, p16, None)   # n not a multiple of 256
-    assert lib.b200_linear(p16, 4, 1024, 1024, C.byref(w), C.byref(o), None) == 2
+    assert lib.b200_linear(p16, None, 4, 1024, 1024, C.byref(w), C.byref(o), None) == 2
     w = _lib.QWeight(9, 256, 1024, p16, p16, None)   # unknown format
-    assert lib.b200_linear(p16, 4, 1024, 1024, C.byref(w), C.byref(o), None) == 3
+    assert lib.b200_linear(p16, None, 4, 1024, 1024, C.byref(w), C.byref(o), None) == 3
+    w = _lib.QWeight(1, 256, 1024, p16, p16, None)
+    o = _lib.LinearOut(0, 200, p16, 256, 0)             # n_valid not a multiple of 32
+    assert lib.b200_linear(p16, None, 4, 1024, 1024, C.byref(w), C.byref(o), None) == 2
+    o = _lib.LinearOut(0, 256, p16, 256, 0)
+    assert lib.b200_linear(p16, p16 + 8, 4, 1024, 1024, C.byref(w), C.byref(o), None) == 2  # lo plane unaligned
 
 
 def test_model_context_host_side(lib):
