@@ -5,8 +5,8 @@
 //   one query head each; the next kv_heads warps do the same for the keys, and the last
 //   kv_heads warps copy the values. Keys and values go to the batch scratch, and, for a
 //   sequence that saves its cache, to the prefix pool as well.
-// attn_kernel: one warp per (token, query head): online softmax over the prefix slot's
-//   keys (positions 0..P-1) then the sequence's own keys (P..P+j), times sigmoid(gate).
+// attn_flash_kernel: tensor-core flash attention over the prefix slot's keys (positions
+//   0..P-1) then the sequence's own keys (P..P+j), causal, times sigmoid(gate).
 #include "common.cuh"
 
 namespace sdb {
@@ -120,71 +120,241 @@ __global__ void attn_prep_kernel(const AttnArgs a) {
   }
 }
 
+// ----------------------------------------------------------------------------- flash kernel
+// Tensor-core (mma.sync m16n8k16, bf16 in, fp32 accumulate) flash attention. One CTA = 4
+// warps = 64 queries of one sequence and one query head; each warp owns 16 query rows.
+// Keys stream in tiles of 32 (prefix-pool keys first, then the sequence's own), double
+// buffered with cp.async; online softmax in registers; P is fed to the P V product straight
+// from the score accumulators. Shared tiles are row-major with 16-byte chunks XOR-swizzled
+// by row, so ldmatrix reads are conflict-free.
+constexpr int FA_Q = 64;
+constexpr int FA_K = 32;
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// byte offset of 16-byte chunk c of row r in a row-major tile with HD bf16 per row
 template <int HD>
-__global__ void attn_kernel(const AttnArgs a, int n_tokens) {
-  constexpr int PER = HD / 32;
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const int nq = a.p.heads, nkv = a.p.kv_heads;
-  const int t = gw / nq, h = gw % nq;
-  if (t >= n_tokens) return;
-  const int kh = h / (nq / nkv);
-  const int seq = find_seq(a.cu, a.n_seqs, t);
-  const int tok0 = a.cu[seq], j = t - tok0;
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+  return uint32_t(r * HD * 2 + ((c ^ (r & 7)) << 4));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) attn_flash_kernel(const AttnArgs a) {
+  constexpr int CH = HD / 8;  // 16-byte chunks per row
+  extern __shared__ uint8_t fa_smem[];
+  uint8_t* sQ = fa_smem;                          // [FA_Q][HD]
+  uint8_t* sK = sQ + FA_Q * HD * 2;               // [2][FA_K][HD]
+  uint8_t* sV = sK + 2 * FA_K * HD * 2;           // [2][FA_K][HD]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int seq = blockIdx.y, h = blockIdx.z;
+  const int nq = a.p.heads, nkv = a.p.kv_heads, kh = h / (nq / nkv);
+  const int tok0 = a.cu[seq], len = a.cu[seq + 1] - tok0;
+  const int q0 = blockIdx.x * FA_Q;
+  if (q0 >= len) return;
   const int ps = a.prefix_slot ? a.prefix_slot[seq] : -1;
   bool pv = ps >= 0 && ps < a.n_slots;
   int P = pv ? a.slot_len[ps] : 0;
   if (pv && (a.slot_kv[ps] < 0 || a.slot_kv[ps] + P > a.kv_capacity)) {
-    if (lane == 0) raise_fault(FAULT_BAD_INDEX);
+    if (tid == 0) raise_fault(FAULT_BAD_INDEX);
     pv = false;
     P = 0;
   }
-  const float scale = rsqrtf(float(HD));
-  float q[PER], acc[PER];
-#pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    q[e] = bf16_to_f32(a.q_buf[(size_t(t) * nq + h) * HD + lane * PER + e]) * scale;
-    acc[e] = 0.0f;
+  const size_t pbase = pv ? size_t(a.slot_kv[ps]) : 0;
+  const int n_keys = P + min(len, q0 + FA_Q);   // causal: the tile's last query sees these
+  const int n_tiles = (n_keys + FA_K - 1) / FA_K;
+
+  // Q tile (rows past the sequence are zero)
+  for (int i = tid; i < FA_Q * CH; i += 128) {
+    const int r = i / CH, c = i % CH;
+    const bool ok = q0 + r < len;
+    const uint16_t* src = a.q_buf + ((size_t(tok0 + q0 + (ok ? r : 0)) * nq + h) * HD) + c * 8;
+    cp_async16(sQ + sw_off<HD>(r, c), src, ok);
   }
-  float m = -INFINITY, l = 0.0f;
-  auto step = [&](const uint16_t* kp, const uint16_t* vp) {
-    float s = 0.0f;
-#pragma unroll
-    for (int e = 0; e < PER; ++e) s = fmaf(q[e], bf16_to_f32(kp[lane * PER + e]), s);
-    s = warp_sum(s);
-    const float mn = fmaxf(m, s);
-    const float alpha = __expf(m - mn), pr = __expf(s - mn);
-    l = l * alpha + pr;
-#pragma unroll
-    for (int e = 0; e < PER; ++e) acc[e] = fmaf(pr, bf16_to_f32(vp[lane * PER + e]), acc[e] * alpha);
-    m = mn;
+  auto load_kv = [&](int tile, int buf) {
+    for (int i = tid; i < FA_K * CH; i += 128) {
+      const int r = i / CH, c = i % CH;
+      const int kk = tile * FA_K + r;
+      const bool ok = kk < n_keys;
+      const uint16_t *ks, *vs;
+      if (kk < P) {
+        ks = a.k_pool + ((pbase + kk) * nkv + kh) * HD;
+        vs = a.v_pool + ((pbase + kk) * nkv + kh) * HD;
+      } else {
+        const size_t t = size_t(tok0 + (ok ? kk - P : 0));
+        ks = a.k_buf + (t * nkv + kh) * HD;
+        vs = a.v_buf + (t * nkv + kh) * HD;
+      }
+      cp_async16(sK + buf * FA_K * HD * 2 + sw_off<HD>(r, c), ks + c * 8, ok);
+      cp_async16(sV + buf * FA_K * HD * 2 + sw_off<HD>(r, c), vs + c * 8, ok);
+    }
   };
-  if (pv) {
-    const size_t base = size_t(a.slot_kv[ps]);
-    for (int i = 0; i < P; ++i)
-      step(a.k_pool + ((base + i) * nkv + kh) * HD, a.v_pool + ((base + i) * nkv + kh) * HD);
-  }
-  for (int i = 0; i <= j; ++i)
-    step(a.k_buf + (size_t(tok0 + i) * nkv + kh) * HD, a.v_buf + (size_t(tok0 + i) * nkv + kh) * HD);
-  const float* gate = a.qkv + size_t(t) * a.ld_qkv + h * 2 * HD + HD;
-  const float inv = 1.0f / l;
+  load_kv(0, 0);
+  cp_async_commit();
+
+  float o[HD / 8][4];
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const float y = acc[e] * inv * sigmoid(gate[lane * PER + e]);
-    const size_t o = (size_t(t) * nq + h) * HD + lane * PER + e;
-    const uint16_t hb = f32_to_bf16_rn(y);
-    a.out[o] = hb;
-    if (a.lo_offset) a.out[a.lo_offset + o] = f32_to_bf16_rn(y - bf16_to_f32(hb));
+  for (int j = 0; j < HD / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
+  const float scale = rsqrtf(float(HD));
+  const int g = lane >> 2, tq = lane & 3;
+  const int qrow0 = warp * 16;                          // warp's first row in the tile
+  const int qpos0 = P + q0 + qrow0 + g, qpos1 = qpos0 + 8;  // positions of this thread's two rows
+  const uint32_t sQa = smem_addr(sQ);
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const int buf = tile & 1;
+    if (tile + 1 < n_tiles) load_kv(tile + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const uint32_t sKa = smem_addr(sK + buf * FA_K * HD * 2), sVa = smem_addr(sV + buf * FA_K * HD * 2);
+    // ---- S = Q K^T : 16 x 32 per warp
+    float sc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+#pragma unroll
+    for (int kd = 0; kd < HD / 16; ++kd) {
+      uint32_t qa[4];
+      {
+        const int r = qrow0 + (lane & 15), c = kd * 2 + (lane >> 4);
+        ldsm_x4(qa, sQa + sw_off<HD>(r, c));
+      }
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {  // two n-tile pairs of 8 keys
+        uint32_t kb[4];
+        const int r = nb * 16 + (lane & 7) + ((lane >> 4) << 3), c = kd * 2 + ((lane >> 3) & 1);
+        ldsm_x4(kb, sKa + sw_off<HD>(r, c));
+        mma_bf16_16816(sc[2 * nb], qa, kb[0], kb[1]);
+        mma_bf16_16816(sc[2 * nb + 1], qa, kb[2], kb[3]);
+      }
+    }
+    // ---- mask + online softmax (rows g and g+8 of the warp's 16)
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = tile * FA_K + j * 8 + tq * 2 + (e & 1);
+        const int qp = e < 2 ? qpos0 : qpos1;
+        float v = sc[j][e] * scale;
+        if (key >= n_keys || key > qp) v = -INFINITY;
+        sc[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+    float alpha[2], rs[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float mn = fmaxf(m_run[r], mx[r]);
+      alpha[r] = mn == -INFINITY ? 1.0f : __expf(m_run[r] - mn);
+      m_run[r] = mn;
+    }
+    uint32_t pa[2][4];  // P as A fragments for two k16 steps (keys 0-15, 16-31)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float p[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float mref = m_run[e >> 1];
+        p[e] = mref == -INFINITY ? 0.0f : __expf(sc[j][e] - mref);
+        rs[e >> 1] += p[e];
+      }
+      const int ks = j >> 1, hi = j & 1;
+      pa[ks][hi * 2 + 0] = pack_bf16x2(p[0], p[1]);
+      pa[ks][hi * 2 + 1] = pack_bf16x2(p[2], p[3]);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+      l_run[r] = l_run[r] * alpha[r] + rs[r];
+    }
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      o[j][0] *= alpha[0];
+      o[j][1] *= alpha[0];
+      o[j][2] *= alpha[1];
+      o[j][3] *= alpha[1];
+    }
+    // ---- O += P V   (A fragment register order: rows g / g+8 x keys lo / hi)
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      const uint32_t a4[4] = {pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3]};
+#pragma unroll
+      for (int nd = 0; nd < HD / 16; ++nd) {  // 16 value dims per ldmatrix.x4.trans
+        uint32_t vb[4];
+        const int r = ks * 16 + (lane & 15), c = nd * 2 + (lane >> 4);
+        ldsm_x4_t(vb, sVa + sw_off<HD>(r, c));
+        mma_bf16_16816(o[2 * nd], a4, vb[0], vb[1]);
+        mma_bf16_16816(o[2 * nd + 1], a4, vb[2], vb[3]);
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- epilogue: O / l * sigmoid(gate) -> hi/lo planes
+  const float inv[2] = {l_run[0] > 0.0f ? 1.0f / l_run[0] : 0.0f, l_run[1] > 0.0f ? 1.0f / l_run[1] : 0.0f};
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int q = q0 + qrow0 + g + 8 * r;
+    if (q >= len) continue;
+    const size_t t = size_t(tok0 + q);
+    const float* gate = a.qkv + t * a.ld_qkv + h * 2 * HD + HD;
+    uint16_t* dst = a.out + (t * nq + h) * HD;
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      const int d = j * 8 + tq * 2;
+      const float y0 = o[j][2 * r] * inv[r] * sigmoid(gate[d]);
+      const float y1 = o[j][2 * r + 1] * inv[r] * sigmoid(gate[d + 1]);
+      const uint16_t h0 = f32_to_bf16_rn(y0), h1 = f32_to_bf16_rn(y1);
+      *reinterpret_cast<uint32_t*>(dst + d) = uint32_t(h0) | (uint32_t(h1) << 16);
+      if (a.lo_offset)
+        *reinterpret_cast<uint32_t*>(dst + a.lo_offset + d) =
+            pack_bf16x2(y0 - bf16_to_f32(h0), y1 - bf16_to_f32(h1));
+    }
   }
 }
 
 template <int HD>
-static int launch_attn(const AttnArgs& a, int n_tokens, cudaStream_t st) {
+static int launch_attn(const AttnArgs& a, int n_tokens, int n_seqs, int max_len, cudaStream_t st) {
   const int warps = a.p.heads + 2 * a.p.kv_heads;
   attn_prep_kernel<HD><<<n_tokens, 32 * warps, 0, st>>>(a);
   SDB_LAUNCH_CHECK();
-  const long total = long(n_tokens) * a.p.heads;
-  attn_kernel<HD><<<int((total + 7) / 8), 256, 0, st>>>(a, n_tokens);
+  constexpr int smem = FA_Q * HD * 2 + 4 * FA_K * HD * 2;
+  static bool attr = false;
+  if (!attr) {
+    SDB_CUDA(cudaFuncSetAttribute(attn_flash_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  dim3 grid((max_len + FA_Q - 1) / FA_Q, n_seqs, a.p.heads);
+  attn_flash_kernel<HD><<<grid, 128, smem, st>>>(a);
   SDB_LAUNCH_CHECK();
   return B200_OK;
 }
@@ -228,10 +398,11 @@ int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qk
   const size_t per_layer = uses_pool ? size_t(pool->kv_capacity) * p->kv_heads * p->head_dim : 0;
   a.k_pool = uses_pool ? pool->k_cache + size_t(layer) * per_layer : nullptr;
   a.v_pool = uses_pool ? pool->v_cache + size_t(layer) * per_layer : nullptr;
+  if (s->max_len <= 0) return sdb_fail(B200_ERR_SHAPE, "b200_attention: max_len must bound the sequence lengths");
   switch (p->head_dim) {
-    case 64: return launch_attn<64>(a, s->n_tokens, st);
-    case 128: return launch_attn<128>(a, s->n_tokens, st);
-    case 256: return launch_attn<256>(a, s->n_tokens, st);
+    case 64: return launch_attn<64>(a, s->n_tokens, s->n_seqs, s->max_len, st);
+    case 128: return launch_attn<128>(a, s->n_tokens, s->n_seqs, s->max_len, st);
+    case 256: return launch_attn<256>(a, s->n_tokens, s->n_seqs, s->max_len, st);
     default: return sdb_fail(B200_ERR_UNSUPPORTED, "b200_attention: head_dim must be 64, 128 or 256");
   }
 }

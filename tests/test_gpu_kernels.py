@@ -276,3 +276,72 @@ def test_tile_weights_layout(fmt):
         srb = sc.shape[1] // (k // 64)
         want_s = sc.reshape(n // 256, 256, k // 64, srb).transpose(0, 2, 1, 3).reshape(-1)
         assert np.array_equal(pw.tile_scales.cpu().numpy()[: want_s.size], want_s)
+
+
+@pytest.mark.parametrize("with_prefix", [False, True])
+@pytest.mark.parametrize("hd", [128, 256])
+def test_attention_matches_reference(with_prefix, hd):
+    """q/k RMSNorm(1+w), partial RoPE, causal GQA softmax over (prefix-pool keys +) own
+    keys, times sigmoid(gate) (TF:647-690), ragged lengths around the 64/32 tile sizes."""
+    from oracle import torso as OT
+    from strands_decider_b200 import _lib, config
+    from strands_decider_b200.runtime import rope_tables
+
+    nq, nkv = 8, 2
+    spec = config.HYBRID_2B if hd == 256 else config.REDUCED_1024
+    g = torch.Generator().manual_seed(hd)
+    lens = [1, 37, 64, 65, 130]
+    P = [0, 0, 0, 0, 0] if not with_prefix else [5, 0, 70, 33, 2]
+    T = sum(lens)
+    cols = 2 * nq * hd + 2 * nkv * hd
+    qkv = torch.randn(T, cols, generator=g)
+    qn, kn = 0.1 * torch.randn(hd, generator=g), 0.1 * torch.randn(hd, generator=g)
+    cos, sin = rope_tables(spec, "cpu")
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    # prefix pool: per-sequence slot i holding P[i] keys (post norm+rope) at offset sum(P[:i])
+    kv_cap = max(sum(P), 1)
+    kpool = torch.randn(1, kv_cap, nkv, hd, generator=g).to(torch.bfloat16)
+    vpool = torch.randn(1, kv_cap, nkv, hd, generator=g).to(torch.bfloat16)
+    slot_kv = torch.tensor([sum(P[:i]) for i in range(len(P))], dtype=torch.int32)
+    slot_len = torch.tensor(P, dtype=torch.int32)
+    dev = {k: v.cuda() for k, v in dict(qkv=qkv, qn=qn, kn=kn, cos=cos, sin=sin, kpool=kpool, vpool=vpool,
+                                        slot_kv=slot_kv, slot_len=slot_len).items()}
+    cu_d = torch.tensor(cu, dtype=torch.int32, device="cuda")
+    pslot = torch.arange(len(lens), dtype=torch.int32, device="cuda") if with_prefix else None
+    qb = torch.empty(T, nq, hd, dtype=torch.bfloat16, device="cuda")
+    kb = torch.empty(T, nkv, hd, dtype=torch.bfloat16, device="cuda")
+    vb = torch.empty_like(kb)
+    out = torch.zeros(2, T, nq * hd, dtype=torch.bfloat16, device="cuda")
+    p = _lib.AttnParams(nq, nkv, hd, hd // 4, cos.shape[0], 1e-6, _lib.ptr(dev["qn"]), _lib.ptr(dev["kn"]),
+                        _lib.ptr(dev["cos"]), _lib.ptr(dev["sin"]))
+    seqs = _lib.Seqs(len(lens), T, max(lens), _lib.ptr(cu_d), _lib.ptr(pslot), None)
+    pool = _lib.PrefixPool(len(lens), kv_cap, _lib.ptr(dev["slot_len"]), _lib.ptr(dev["slot_kv"]), None, None,
+                           _lib.ptr(dev["kpool"]), _lib.ptr(dev["vpool"]))
+    _lib.call("b200_attention", _ref(p), _ref(seqs), _lib.ptr(dev["qkv"]), cols, _lib.ptr(qb), _lib.ptr(kb),
+              _lib.ptr(vb), _lib.ptr(out), T * nq * hd, _ref(pool) if with_prefix else None, 0, _lib.stream_ptr())
+    torch.cuda.synchronize()
+    got = (out[0].double() + out[1].double()).cpu()
+    cfg = OT.TorsoConfig(vocab=1, hidden=1, inter=1, layer_types=(), gdn_heads=1, attn_heads=nq,
+                         attn_kv_heads=nkv, head_dim=hd)
+    for i, n in enumerate(lens):
+        x = qkv[cu[i]:cu[i + 1]].double()
+        qg = x[:, : 2 * nq * hd].view(n, nq, 2 * hd)
+        q, gate = qg[..., :hd], qg[..., hd:].reshape(n, -1)
+        k = x[:, 2 * nq * hd: 2 * nq * hd + nkv * hd].view(n, nkv, hd)
+        v = x[:, 2 * nq * hd + nkv * hd:].view(n, nkv, hd)
+        q = OT.rms_norm_1p(q, qn, 1e-6).double()
+        k = OT.rms_norm_1p(k, kn, 1e-6).double()
+        pos = torch.arange(P[i], P[i] + n)
+        q = OT.apply_rope(q, cos[pos].repeat(1, 2).double(), sin[pos].repeat(1, 2).double())
+        k = OT.apply_rope(k, cos[pos].repeat(1, 2).double(), sin[pos].repeat(1, 2).double())
+        kp = kpool[0, slot_kv[i]:slot_kv[i] + P[i]].double()
+        vp = vpool[0, slot_kv[i]:slot_kv[i] + P[i]].double()
+        ka, va = torch.cat([kp, k]), torch.cat([vp, v])
+        kr, vr = ka.repeat_interleave(nq // nkv, 1), va.repeat_interleave(nq // nkv, 1)
+        s = torch.einsum("thd,shd->hts", q, kr) * hd ** -0.5
+        s = s.masked_fill((torch.arange(P[i] + n)[None, :] > pos[:, None])[None], float("-inf"))
+        o = torch.einsum("hts,shd->thd", s.softmax(-1), vr).reshape(n, -1) * torch.sigmoid(gate)
+        err = (got[cu[i]:cu[i + 1]] - o).abs().max().item() / o.abs().max().item()
+        assert err < 2e-2, (n, P[i], err)
