@@ -1,24 +1,29 @@
-// Gated-DeltaNet token mixer (after the in-projection GEMM), one CTA per (sequence, head).
+// Gated-DeltaNet token mixer (after the in-projection GEMM) on tensor cores.
 //
-// Per chunk of GC tokens (TF:234-311, with TF:462-530 fused around it):
-//   1. causal depthwise conv (width 4) + SiLU over the head's q, k, v channels, reading the
-//      3 previous raw inputs from the previous chunk, the prefix slot, or zeros
-//   2. l2norm(q), l2norm(k), q *= dk^-1/2; beta = sigmoid(b); g = -exp(A_log)*softplus(a+dt)
-//   3. G = cumsum(g); A = strictly-lower(beta_i k_i.k_j e^{G_i-G_j}); P = lower(q_i.k_j e^{G_i-G_j})
-//   4. solve (I + A) [U | W] = [beta v | beta k e^G] by forward substitution (one column per thread)
-//   5. Vn = U - W S;  O = (q e^G) S + P Vn;  S = e^{G_last} S + (k e^{G_last - G})^T Vn
-//   6. gated RMSNorm: out = norm_w * O * rsqrt(mean O^2 + eps) * silu(z)
-// The state S [dk, dv] lives in shared memory in fp32 for the whole sequence; it starts
-// from the prefix slot (or zero) and is written back to the save slot at the end.
+// One CTA (8 warps) per (sequence, head); chunks of GC = 32 tokens run in order. Per chunk,
+// restating TF:234-311 with TF:462-530 fused around it:
+//   1. g_j = -exp(A_log) softplus(a_j + dt_bias), beta_j = sigmoid(b_j); G = cumsum(g)
+//   2. causal depthwise conv (width 4) + SiLU over the head's q, k, v channels (the 3
+//      previous raw inputs come from the sequence itself or the prefix slot's history),
+//      l2norm(q) * dk^-1/2, l2norm(k)
+//   3. A = strictly-lower(beta_i k_i.k_j e^{G_i-G_j}), P = lower(q_i.k_j e^{G_i-G_j})
+//   4. T = (I + A)^{-1} by block forward substitution (fp32)
+//   5. [U | W] = T [beta v | beta k e^G]
+//   6. Vn = U - W S
+//   7. O = e^G (q S) + P Vn;  S = e^{G_last} S + k^T (Vn e^{G_last - G})
+//   8. gated RMSNorm: out = norm_w * O * rsqrt(mean O^2 + eps) * silu(z), as hi/lo planes
+// Every matrix product runs on mma.sync m16n8k16 with fp32 accumulation and operands split
+// into bf16 planes x = x_hi + x_lo; a product is hi*hi + hi*lo + lo*hi (about 16
+// significant bits per operand). The fp32 state S [dk, dv] lives in the warps' accumulator
+// registers (warp w holds rows 16w..16w+15) and is republished to shared memory as hi/lo
+// planes for the next chunk's products.
 #include "common.cuh"
 
 namespace sdb {
 
-constexpr int GC = 32;     // chunk length
-constexpr int GDK = 128;   // key head dim
-constexpr int GDV = 128;   // value head dim
-constexpr int GQKV = GDK + GDK + GDV;
-constexpr int GPAD = GDK + 1;
+constexpr int GC = 32;          // chunk length
+constexpr int GD = 128;         // key / value head dim
+constexpr int GQKV = 3 * GD;
 constexpr int GDN_THREADS = 256;
 
 struct GdnArgs {
@@ -36,25 +41,106 @@ struct GdnArgs {
   int n_slots;
 };
 
+// bf16 planes, row-major, 16-byte chunks XOR-swizzled by row so ldmatrix is conflict-free
 struct GdnSmem {
-  float q[GC][GPAD];
-  float k[GC][GPAD];
-  float v[GC][GDV];   // v, then U, then Vn
-  float w[GC][GDK];   // W, then O
-  float A[GC][GC + 1];
-  float P[GC][GC + 1];
-  float S[GDK][GDV];
-  float hist[3][GQKV];
-  float G[GC], beta[GC], eG[GC];
+  uint16_t Sh[GD * GD], Sl[GD * GD];           // state, rows dk, cols dv
+  uint16_t Qh[GC * GD], Ql[GC * GD];           // q (l2normed, scaled)
+  uint16_t Kh[GC * GD], Kl[GC * GD];           // k (l2normed)
+  union {
+    struct {
+      uint16_t Rh[GC * 2 * GD], Rl[GC * 2 * GD];  // [beta v | beta k e^G]
+    } r;
+    struct {
+      float U[GC * GD];                         // fp32
+      uint16_t Wh[GC * GD], Wl[GC * GD];
+    } uw;
+  } ru;
+  uint16_t Vh[GC * GD], Vl[GC * GD];           // Vn
+  uint16_t Th[GC * GD], Tl[GC * GD];           // Vn * e^{G_last - G} (named T for "tail-decayed")
+  uint16_t Ph[GC * GC], Pl[GC * GC];           // P
+  uint16_t Ih[GC * GC], Il[GC * GC];           // (I + A)^{-1}
+  float A[GC][GC + 1];                          // A, then the inverse in fp32
+  float O[GC][GD + 4];
+  float hist[3][GQKV];                          // prefix conv history (raw inputs)
+  float G[GC], beta[GC], eG[GC], eL[GC];
 };
 
+// ----------------------------------------------------------------------------- helpers
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm4t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// byte offset of element (r, col) in a swizzled plane whose rows hold RL bf16
+template <int RL>
+__device__ __forceinline__ uint32_t soff(int r, int col) {
+  constexpr int CH = RL / 8;
+  const int c = col >> 3;
+  const int sw = CH >= 8 ? (r & 7) : ((r >> 1) & (CH - 1));
+  return uint32_t(r * RL * 2 + ((c ^ sw) << 4) + (col & 7) * 2);
+}
+
+__device__ __forceinline__ void split_store(uint16_t* hi, uint16_t* lo, uint32_t off, float a, float b) {
+  const uint16_t ha = f32_to_bf16_rn(a), hb = f32_to_bf16_rn(b);
+  *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(hi) + off) = uint32_t(ha) | (uint32_t(hb) << 16);
+  *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(lo) + off) =
+      pack_bf16x2(a - bf16_to_f32(ha), b - bf16_to_f32(hb));
+}
+
+// A fragment (16 x 16) of a plane stored [m][k] with RL elements per row, rows m0.., cols k0..
+template <int RL>
+__device__ __forceinline__ void frag_a(uint32_t (&f)[4], const uint16_t* plane, int m0, int k0, int lane) {
+  ldsm4(f, smem_addr(plane) + soff<RL>(m0 + (lane & 15), k0 + ((lane >> 4) << 3)));
+}
+// A fragment of the transpose of a plane stored [k][m]: A[m][k] = plane[k][m]
+template <int RL>
+__device__ __forceinline__ void frag_at(uint32_t (&f)[4], const uint16_t* plane, int m0, int k0, int lane) {
+  ldsm4t(f, smem_addr(plane) + soff<RL>(k0 + (lane & 7) + ((lane >> 4) << 3), m0 + (((lane >> 3) & 1) << 3)));
+}
+// B fragments of two n-tiles (n0..n0+15) x k16 from a plane stored [n][k] (B[k][n] = plane[n][k])
+template <int RL>
+__device__ __forceinline__ void frag_b(uint32_t (&f)[4], const uint16_t* plane, int n0, int k0, int lane) {
+  ldsm4(f, smem_addr(plane) + soff<RL>(n0 + (lane & 7) + ((lane >> 4) << 3), k0 + (((lane >> 3) & 1) << 3)));
+}
+// B fragments of two n-tiles from a plane stored [k][n] (B[k][n] = plane[k][n])
+template <int RL>
+__device__ __forceinline__ void frag_bt(uint32_t (&f)[4], const uint16_t* plane, int n0, int k0, int lane) {
+  ldsm4t(f, smem_addr(plane) + soff<RL>(k0 + (lane & 15), n0 + ((lane >> 4) << 3)));
+}
+
+// split product of one k16 step into two n-tiles: d0 (n0..n0+7), d1 (n0+8..)
+__device__ __forceinline__ void mma3(float (&d0)[4], float (&d1)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                     const uint32_t (&bh)[4], const uint32_t (&bl)[4]) {
+  mma16816(d0, ah, bh[0], bh[1]);
+  mma16816(d0, ah, bl[0], bl[1]);
+  mma16816(d0, al, bh[0], bh[1]);
+  mma16816(d1, ah, bh[2], bh[3]);
+  mma16816(d1, ah, bl[2], bl[3]);
+  mma16816(d1, al, bh[2], bh[3]);
+}
+
+// ----------------------------------------------------------------------------- kernel
 __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs a) {
   extern __shared__ uint8_t gdn_smem_raw[];
   GdnSmem& sm = *reinterpret_cast<GdnSmem*>(gdn_smem_raw);
   const int h = blockIdx.x, seq = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g8 = lane >> 2, t4 = lane & 3;
   const int H = a.p.heads;
-  const int key_dim = H * GDK, value_dim = H * GDV, conv_dim = 2 * key_dim + value_dim;
+  const int key_dim = H * GD, value_dim = H * GD, conv_dim = 2 * key_dim + value_dim;
   const int tok0 = a.cu[seq], len = a.cu[seq + 1] - tok0;
   const int pslot = a.prefix_slot ? a.prefix_slot[seq] : -1;
   const int sslot = a.save_slot ? a.save_slot[seq] : -1;
@@ -63,200 +149,351 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
   if ((pslot >= a.n_slots || sslot >= a.n_slots) && tid == 0) raise_fault(FAULT_BAD_INDEX);
 
   // channel of head-local index c in 0..383 (q, k, v)
-  auto chan = [&](int c) { return c < GDK ? h * GDK + c : c < 2 * GDK ? key_dim + h * GDK + (c - GDK) : 2 * key_dim + h * GDV + (c - 2 * GDK); };
+  auto chan = [&](int c) {
+    return c < GD ? h * GD + c : c < 2 * GD ? key_dim + h * GD + (c - GD) : 2 * key_dim + h * GD + (c - 2 * GD);
+  };
+  // raw pre-conv input of channel c (head-local) at sequence position p (p < 0: history)
+  auto raw = [&](int p, int c) -> float {
+    return p >= 0 ? a.mix[size_t(tok0 + p) * a.ld_mix + chan(c)] : sm.hist[3 + p][c];
+  };
 
-  // initial state and conv history
-  for (int i = tid; i < GDK * GDV; i += GDN_THREADS)
-    (&sm.S[0][0])[i] = pvalid ? a.state_pool[(size_t(pslot) * H + h) * GDK * GDV + i] : 0.0f;
+  // ---- initial state (fp32 slab in registers) and prefix conv history
+  float S[16][4];  // rows 16*warp + g8 (+8), cols 8*nt + 2*t4 (+1)
+  {
+    const float* src = pvalid ? a.state_pool + (size_t(pslot) * H + h) * GD * GD : nullptr;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = 16 * warp + g8 + 8 * (e >> 1), c = 8 * nt + 2 * t4 + (e & 1);
+        S[nt][e] = src ? src[r * GD + c] : 0.0f;
+      }
+    }
+  }
   for (int i = tid; i < 3 * GQKV; i += GDN_THREADS) {
     const int r = i / GQKV, c = i % GQKV;
     sm.hist[r][c] = pvalid ? a.conv_pool[(size_t(pslot) * 3 + r) * conv_dim + chan(c)] : 0.0f;
   }
+  auto publish_state = [&]() {
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int r = 16 * warp + g8 + 8 * hr, c = 8 * nt + 2 * t4;
+        split_store(sm.Sh, sm.Sl, soff<GD>(r, c), S[nt][2 * hr], S[nt][2 * hr + 1]);
+      }
+    }
+  };
+  publish_state();
   const float A_exp = __expf(a.p.a_log[h]);
   const float dtb = a.p.dt_bias[h];
+  const float qscale = rsqrtf(float(GD));
   __syncthreads();
 
   for (int c0 = 0; c0 < len; c0 += GC) {
     const int L = min(GC, len - c0);
-    // ---- 1. conv + SiLU
-    for (int i = tid; i < L * GQKV; i += GDN_THREADS) {
-      const int j = i / GQKV, c = i % GQKV, ch = chan(c);
-      float acc = 0.0f;
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int jj = j - 3 + t;
-        const float xv = jj < 0 ? sm.hist[3 + jj][c] : a.mix[size_t(tok0 + c0 + jj) * a.ld_mix + ch];
-        acc = fmaf(a.p.conv_w[ch * 4 + t], xv, acc);
+    // ---- 1. gating, cumulative decay
+    if (tid < GC) {
+      float gj = 0.0f, bj = 0.0f;
+      if (tid < L) {
+        const float* ab = a.mix + size_t(tok0 + c0 + tid) * a.ld_mix + conv_dim + value_dim;
+        bj = sigmoid(ab[h]);
+        gj = -A_exp * softplus(ab[H + h] + dtb);
       }
-      acc = silu(acc);
-      if (c < GDK) sm.q[j][c] = acc;
-      else if (c < 2 * GDK) sm.k[j][c - GDK] = acc;
-      else sm.v[j][c - 2 * GDK] = acc;
+      // inclusive warp scan of g over the chunk
+      float v = gj;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+      }
+      sm.G[tid] = v;
+      sm.beta[tid] = bj;
+      sm.eG[tid] = __expf(v);
     }
     __syncthreads();
-    // new history = last 3 raw inputs of (history ++ chunk)
-    {
-      float keep[5];
-      int n = 0;
-      for (int i = tid; i < 3 * GQKV; i += GDN_THREADS, ++n) {
-        const int r = i / GQKV, c = i % GQKV;
-        const int jj = L - 3 + r;
-        keep[n] = jj < 0 ? sm.hist[3 + jj][c] : a.mix[size_t(tok0 + c0 + jj) * a.ld_mix + chan(c)];
+    if (tid < GC) sm.eL[tid] = tid < L ? __expf(sm.G[L - 1] - sm.G[tid]) : 0.0f;
+    // ---- 2. conv + SiLU + l2norm; write q, k, [beta v | beta k e^G] as hi/lo planes
+    for (int j = warp; j < GC; j += GDN_THREADS / 32) {
+      float q[4], k[4], v[4];
+      if (j < L) {
+        const int p = c0 + j;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int cq = lane * 4 + e;
+          float aq = 0.0f, ak = 0.0f, av = 0.0f;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            aq = fmaf(a.p.conv_w[chan(cq) * 4 + t], raw(p - 3 + t, cq), aq);
+            ak = fmaf(a.p.conv_w[chan(GD + cq) * 4 + t], raw(p - 3 + t, GD + cq), ak);
+            av = fmaf(a.p.conv_w[chan(2 * GD + cq) * 4 + t], raw(p - 3 + t, 2 * GD + cq), av);
+          }
+          q[e] = silu(aq);
+          k[e] = silu(ak);
+          v[e] = silu(av);
+        }
+        float sq = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
+        float sk = k[0] * k[0] + k[1] * k[1] + k[2] * k[2] + k[3] * k[3];
+        sq = warp_sum(sq);
+        sk = warp_sum(sk);
+        const float rq = rsqrtf(sq + 1e-6f) * qscale, rk = rsqrtf(sk + 1e-6f);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          q[e] *= rq;
+          k[e] *= rk;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) q[e] = k[e] = v[e] = 0.0f;
       }
+      const float bj = sm.beta[j], bke = bj * sm.eG[j];
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int c = lane * 4 + e;
+        split_store(sm.Qh, sm.Ql, soff<GD>(j, c), q[e], q[e + 1]);
+        split_store(sm.Kh, sm.Kl, soff<GD>(j, c), k[e], k[e + 1]);
+        split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, c), bj * v[e], bj * v[e + 1]);
+        split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, GD + c), bke * k[e], bke * k[e + 1]);
+      }
+    }
+    __syncthreads();
+    // ---- 3. A = beta k k^T, P = q k^T (x decay, masked): warp -> rows 16*(w>>2), cols 8*(w&3)
+    {
+      const int m0 = 16 * (warp >> 2), n0 = 8 * (warp & 3);
+      float kk[4] = {0, 0, 0, 0}, qk[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int k0 = 0; k0 < GD; k0 += 16) {
+        uint32_t kh[4], kl[4], qh[4], ql[4], bh[4], bl[4];
+        frag_a<GD>(kh, sm.Kh, m0, k0, lane);
+        frag_a<GD>(kl, sm.Kl, m0, k0, lane);
+        frag_a<GD>(qh, sm.Qh, m0, k0, lane);
+        frag_a<GD>(ql, sm.Ql, m0, k0, lane);
+        frag_b<GD>(bh, sm.Kh, n0 & ~15, k0, lane);   // n-tiles (n0&~15) and +8
+        frag_b<GD>(bl, sm.Kl, n0 & ~15, k0, lane);
+        const int sel = (n0 & 8) ? 2 : 0;
+        const uint32_t b0h = bh[sel], b1h = bh[sel + 1], b0l = bl[sel], b1l = bl[sel + 1];
+        mma16816(kk, kh, b0h, b1h);
+        mma16816(kk, kh, b0l, b1l);
+        mma16816(kk, kl, b0h, b1h);
+        mma16816(qk, qh, b0h, b1h);
+        mma16816(qk, qh, b0l, b1l);
+        mma16816(qk, ql, b0h, b1h);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = m0 + g8 + 8 * (e >> 1), j = n0 + 2 * t4 + (e & 1);
+        const bool ok = i < L && j < L;
+        const float dec = ok && j <= i ? __expf(sm.G[i] - sm.G[j]) : 0.0f;
+        sm.A[i][j] = (ok && j < i) ? sm.beta[i] * kk[e] * dec : 0.0f;
+        qk[e] = (ok && j <= i) ? qk[e] * dec : 0.0f;
+      }
+      split_store(sm.Ph, sm.Pl, soff<GC>(m0 + g8, n0 + 2 * t4), qk[0], qk[1]);
+      split_store(sm.Ph, sm.Pl, soff<GC>(m0 + g8 + 8, n0 + 2 * t4), qk[2], qk[3]);
+    }
+    __syncthreads();
+    // ---- 4. (I + A)^{-1}: diagonal 16x16 blocks by forward substitution, then the
+    //         off-diagonal block T10 = -T11 A10 T00; result in sm.A (fp32) and the I planes
+    if (warp < 2 && lane < 16) {
+      const int b = 16 * warp, c = lane;
+      float x[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float r = i == c ? 1.0f : 0.0f;
+#pragma unroll
+        for (int j = 0; j < i; ++j) r = fmaf(-sm.A[b + i][b + j], x[j], r);
+        x[i] = r;
+      }
+      __syncwarp(0x0000FFFFu);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) sm.A[b + i][b + c] = x[i];  // diagonal block now holds T_bb
+    }
+    __syncthreads();
+    {
+      // M = A10 T00 (16x16), then T10 = -T11 M; thread -> (row i, col c) with 256 threads
+      const int i = tid >> 4, c = tid & 15;
+      float mval = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) mval = fmaf(sm.A[16 + i][j], sm.A[j][c], mval);
       __syncthreads();
-      n = 0;
-      for (int i = tid; i < 3 * GQKV; i += GDN_THREADS, ++n) sm.hist[i / GQKV][i % GQKV] = keep[n];
-    }
-    // ---- 2. l2norm q, k; gating
-    for (int j = warp; j < L; j += GDN_THREADS / 32) {
-      float sq = 0.0f, sk = 0.0f;
-      for (int d = lane; d < GDK; d += 32) {
-        sq += sm.q[j][d] * sm.q[j][d];
-        sk += sm.k[j][d] * sm.k[j][d];
-      }
-      sq = warp_sum(sq);
-      sk = warp_sum(sk);
-      const float rq = rsqrtf(sq + 1e-6f) * rsqrtf(float(GDK)), rk = rsqrtf(sk + 1e-6f);
-      for (int d = lane; d < GDK; d += 32) {
-        sm.q[j][d] *= rq;
-        sm.k[j][d] *= rk;
-      }
-    }
-    if (tid < L) {
-      const size_t t = size_t(tok0 + c0 + tid);
-      const float* ab = a.mix + t * a.ld_mix + conv_dim + value_dim;
-      sm.beta[tid] = sigmoid(ab[h]);
-      sm.G[tid] = -A_exp * softplus(ab[H + h] + dtb);
+      sm.O[i][c] = mval;  // scratch
+      __syncthreads();
+      float t = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) t = fmaf(sm.A[16 + i][16 + j], sm.O[j][c], t);
+      __syncthreads();
+      sm.A[16 + i][c] = -t;
     }
     __syncthreads();
-    if (tid == 0) {
-      float acc = 0.0f;
-      for (int j = 0; j < L; ++j) {
-        acc += sm.G[j];
-        sm.G[j] = acc;
-        sm.eG[j] = __expf(acc);
-      }
+    for (int i = tid; i < GC * GC / 2; i += GDN_THREADS) {
+      const int r = i / (GC / 2), c = 2 * (i % (GC / 2));
+      const float v0 = c <= r ? sm.A[r][c] : 0.0f, v1 = c + 1 <= r ? sm.A[r][c + 1] : 0.0f;
+      split_store(sm.Ih, sm.Il, soff<GC>(r, c), v0, v1);
     }
     __syncthreads();
-    // ---- 3. A (strictly lower) and P (lower incl. diagonal); lane = column j
-    for (int i = warp; i < L; i += GDN_THREADS / 32) {
-      const int j = lane;
-      float kk = 0.0f, qk = 0.0f;
-      if (j <= i && j < L) {
-        for (int d = 0; d < GDK; ++d) {
-          kk = fmaf(sm.k[i][d], sm.k[j][d], kk);
-          qk = fmaf(sm.q[i][d], sm.k[j][d], qk);
-        }
-        const float dec = __expf(sm.G[i] - sm.G[j]);
-        sm.A[i][j] = j < i ? sm.beta[i] * kk * dec : 0.0f;
-        sm.P[i][j] = qk * dec;
-      }
-    }
-    __syncthreads();
-    // ---- 4. forward substitution, one column per thread (columns 0..127 U, 128..255 W)
+    // ---- 5. [U | W] = T R : warp -> rows 16*(w&1), cols 64*(w>>1) .. +64
     {
-      const int c = tid;
-      float x[GC];
+      const int m0 = 16 * (warp & 1), nb = 64 * (warp >> 1);
+      float acc[8][4];
 #pragma unroll
-      for (int i = 0; i < GC; ++i) {
-        if (i < L) {
-          float r = c < GDV ? sm.beta[i] * sm.v[i][c] : sm.beta[i] * sm.k[i][c - GDV] * sm.eG[i];
+      for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
 #pragma unroll
-          for (int j = 0; j < i; ++j) r = fmaf(-sm.A[i][j], x[j], r);
-          x[i] = r;
-        } else {
-          x[i] = 0.0f;
+      for (int k0 = 0; k0 < GC; k0 += 16) {
+        uint32_t ah[4], al[4];
+        frag_a<GC>(ah, sm.Ih, m0, k0, lane);
+        frag_a<GC>(al, sm.Il, m0, k0, lane);
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          uint32_t bh[4], bl[4];
+          frag_bt<2 * GD>(bh, sm.ru.r.Rh, nb + 16 * np, k0, lane);
+          frag_bt<2 * GD>(bl, sm.ru.r.Rl, nb + 16 * np, k0, lane);
+          mma3(acc[2 * np], acc[2 * np + 1], ah, al, bh, bl);
         }
       }
-      __syncthreads();  // everyone has read v before U overwrites it
-      for (int i = 0; i < L; ++i) {
-        if (c < GDV) sm.v[i][c] = x[i];
-        else sm.w[i][c - GDV] = x[i];
-      }
-    }
-    __syncthreads();
-    // ---- 5a. Vn = U - W S   (thread: column c, 16 rows)
-    const int c = tid & (GDV - 1), half = tid >> 7;
-    {
-      float acc[GC / 2];
+      __syncthreads();  // R is fully read before U / W overwrite it
 #pragma unroll
-      for (int ii = 0; ii < GC / 2; ++ii) acc[ii] = 0.0f;
-      for (int r = 0; r < GDK; ++r) {
-        const float s = sm.S[r][c];
+      for (int j = 0; j < 8; ++j) {
 #pragma unroll
-        for (int ii = 0; ii < GC / 2; ++ii) acc[ii] = fmaf(sm.w[half * (GC / 2) + ii][r], s, acc[ii]);
-      }
-#pragma unroll
-      for (int ii = 0; ii < GC / 2; ++ii) {
-        const int i = half * (GC / 2) + ii;
-        if (i < L) sm.v[i][c] -= acc[ii];
-      }
-    }
-    __syncthreads();
-    // ---- 5b. O = e^G (q S) + P Vn  -> stored in w
-    {
-      float acc[GC / 2];
-#pragma unroll
-      for (int ii = 0; ii < GC / 2; ++ii) acc[ii] = 0.0f;
-      for (int r = 0; r < GDK; ++r) {
-        const float s = sm.S[r][c];
-#pragma unroll
-        for (int ii = 0; ii < GC / 2; ++ii) acc[ii] = fmaf(sm.q[half * (GC / 2) + ii][r], s, acc[ii]);
-      }
-#pragma unroll
-      for (int ii = 0; ii < GC / 2; ++ii) {
-        const int i = half * (GC / 2) + ii;
-        if (i < L) {
-          float o = acc[ii] * sm.eG[i];
-          for (int j = 0; j <= i; ++j) o = fmaf(sm.P[i][j], sm.v[j][c], o);
-          acc[ii] = o;
+        for (int hr = 0; hr < 2; ++hr) {
+          const int r = m0 + g8 + 8 * hr, c = nb + 8 * j + 2 * t4;
+          if (c < GD) {
+            sm.ru.uw.U[r * GD + c] = acc[j][2 * hr];
+            sm.ru.uw.U[r * GD + c + 1] = acc[j][2 * hr + 1];
+          } else {
+            split_store(sm.ru.uw.Wh, sm.ru.uw.Wl, soff<GD>(r, c - GD), acc[j][2 * hr], acc[j][2 * hr + 1]);
+          }
         }
       }
-      __syncthreads();  // all reads of w (as W) are done
+    }
+    __syncthreads();
+    // ---- 6. Vn = U - W S  and  O = e^G (q S): warp -> rows 16*(w&1), cols 32*(w>>1) .. +32
+    {
+      const int m0 = 16 * (warp & 1), nb = 32 * (warp >> 1);
+      float ws[4][4], qs[4][4];
 #pragma unroll
-      for (int ii = 0; ii < GC / 2; ++ii) {
-        const int i = half * (GC / 2) + ii;
-        if (i < L) sm.w[i][c] = acc[ii];
+      for (int j = 0; j < 4; ++j) ws[j][0] = ws[j][1] = ws[j][2] = ws[j][3] = qs[j][0] = qs[j][1] = qs[j][2] = qs[j][3] = 0.0f;
+#pragma unroll
+      for (int k0 = 0; k0 < GD; k0 += 16) {
+        uint32_t wh[4], wl[4], qh[4], ql[4];
+        frag_a<GD>(wh, sm.ru.uw.Wh, m0, k0, lane);
+        frag_a<GD>(wl, sm.ru.uw.Wl, m0, k0, lane);
+        frag_a<GD>(qh, sm.Qh, m0, k0, lane);
+        frag_a<GD>(ql, sm.Ql, m0, k0, lane);
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+          uint32_t bh[4], bl[4];
+          frag_bt<GD>(bh, sm.Sh, nb + 16 * np, k0, lane);
+          frag_bt<GD>(bl, sm.Sl, nb + 16 * np, k0, lane);
+          mma3(ws[2 * np], ws[2 * np + 1], wh, wl, bh, bl);
+          mma3(qs[2 * np], qs[2 * np + 1], qh, ql, bh, bl);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const int r = m0 + g8 + 8 * hr, c = nb + 8 * j + 2 * t4;
+          const bool ok = r < L;
+          const float v0 = ok ? sm.ru.uw.U[r * GD + c] - ws[j][2 * hr] : 0.0f;
+          const float v1 = ok ? sm.ru.uw.U[r * GD + c + 1] - ws[j][2 * hr + 1] : 0.0f;
+          split_store(sm.Vh, sm.Vl, soff<GD>(r, c), v0, v1);
+          split_store(sm.Th, sm.Tl, soff<GD>(r, c), v0 * sm.eL[r], v1 * sm.eL[r]);
+          sm.O[r][c] = qs[j][2 * hr] * sm.eG[r];
+          sm.O[r][c + 1] = qs[j][2 * hr + 1] * sm.eG[r];
+        }
       }
     }
     __syncthreads();
-    // ---- 5c. S = e^{G_last} S + (k e^{G_last - G})^T Vn   (thread: column c, 64 rows)
+    // ---- 7a. O += P Vn  (same tiling as step 6)
     {
-      const float gl = sm.G[L - 1], el = sm.eG[L - 1];
-      float kd[GC];
+      const int m0 = 16 * (warp & 1), nb = 32 * (warp >> 1);
+      float pv[4][4];
 #pragma unroll
-      for (int i = 0; i < GC; ++i) kd[i] = i < L ? __expf(gl - sm.G[i]) : 0.0f;
-      for (int rr = 0; rr < GDK / 2; ++rr) {
-        const int r = half * (GDK / 2) + rr;
-        float s = sm.S[r][c] * el;
-        for (int i = 0; i < L; ++i) s = fmaf(sm.k[i][r] * kd[i], sm.v[i][c], s);
-        sm.S[r][c] = s;
+      for (int j = 0; j < 4; ++j) pv[j][0] = pv[j][1] = pv[j][2] = pv[j][3] = 0.0f;
+#pragma unroll
+      for (int k0 = 0; k0 < GC; k0 += 16) {
+        uint32_t ph[4], pl[4];
+        frag_a<GC>(ph, sm.Ph, m0, k0, lane);
+        frag_a<GC>(pl, sm.Pl, m0, k0, lane);
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+          uint32_t bh[4], bl[4];
+          frag_bt<GD>(bh, sm.Vh, nb + 16 * np, k0, lane);
+          frag_bt<GD>(bl, sm.Vl, nb + 16 * np, k0, lane);
+          mma3(pv[2 * np], pv[2 * np + 1], ph, pl, bh, bl);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const int r = m0 + g8 + 8 * hr, c = nb + 8 * j + 2 * t4;
+          sm.O[r][c] += pv[j][2 * hr];
+          sm.O[r][c + 1] += pv[j][2 * hr + 1];
+        }
       }
     }
-    // ---- 6. gated RMSNorm of O rows -> out
+    // ---- 7b. S = e^{G_last} S + k^T (Vn e^{G_last - G}): warp w owns S rows 16w..16w+15
+    {
+      const float el = __expf(sm.G[L - 1]);
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) S[nt][e] *= el;
+      }
+#pragma unroll
+      for (int k0 = 0; k0 < GC; k0 += 16) {
+        uint32_t ah[4], al[4];
+        frag_at<GD>(ah, sm.Kh, 16 * warp, k0, lane);
+        frag_at<GD>(al, sm.Kl, 16 * warp, k0, lane);
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+          uint32_t bh[4], bl[4];
+          frag_bt<GD>(bh, sm.Th, 16 * np, k0, lane);
+          frag_bt<GD>(bl, sm.Tl, 16 * np, k0, lane);
+          mma3(S[2 * np], S[2 * np + 1], ah, al, bh, bl);
+        }
+      }
+    }
+    __syncthreads();  // all reads of the old S planes (step 6) and of O's partials are done
+    publish_state();
+    // ---- 8. gated RMSNorm of the O rows -> hi/lo planes
     for (int j = warp; j < L; j += GDN_THREADS / 32) {
       float ss = 0.0f;
-      for (int d = lane; d < GDV; d += 32) ss += sm.w[j][d] * sm.w[j][d];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ss += sm.O[j][lane * 4 + e] * sm.O[j][lane * 4 + e];
       ss = warp_sum(ss);
-      const float r = rsqrtf(ss / float(GDV) + a.p.eps);
+      const float r = rsqrtf(ss / float(GD) + a.p.eps);
       const size_t t = size_t(tok0 + c0 + j);
-      for (int d = lane; d < GDV; d += 32) {
-        const float z = a.mix[t * a.ld_mix + conv_dim + h * GDV + d];
-        const float y = a.p.norm_w[d] * (sm.w[j][d] * r) * silu(z);
-        const uint16_t hb = f32_to_bf16_rn(y);
-        a.out[t * value_dim + h * GDV + d] = hb;
-        if (a.lo_offset) a.out[a.lo_offset + t * value_dim + h * GDV + d] = f32_to_bf16_rn(y - bf16_to_f32(hb));
+      const float* z = a.mix + t * a.ld_mix + conv_dim + h * GD;
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int d = lane * 4 + e;
+        const float y0 = a.p.norm_w[d] * (sm.O[j][d] * r) * silu(z[d]);
+        const float y1 = a.p.norm_w[d + 1] * (sm.O[j][d + 1] * r) * silu(z[d + 1]);
+        uint16_t* dst = a.out + t * value_dim + h * GD + d;
+        const uint16_t h0 = f32_to_bf16_rn(y0), h1 = f32_to_bf16_rn(y1);
+        *reinterpret_cast<uint32_t*>(dst) = uint32_t(h0) | (uint32_t(h1) << 16);
+        if (a.lo_offset)
+          *reinterpret_cast<uint32_t*>(dst + a.lo_offset) = pack_bf16x2(y0 - bf16_to_f32(h0), y1 - bf16_to_f32(h1));
       }
     }
     __syncthreads();
   }
 
   if (svalid) {
-    for (int i = tid; i < GDK * GDV; i += GDN_THREADS)
-      a.state_pool[(size_t(sslot) * H + h) * GDK * GDV + i] = (&sm.S[0][0])[i];
+    float* dst = a.state_pool + (size_t(sslot) * H + h) * GD * GD;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = 16 * warp + g8 + 8 * (e >> 1), c = 8 * nt + 2 * t4 + (e & 1);
+        dst[r * GD + c] = S[nt][e];
+      }
+    }
+    // conv history: the last 3 raw inputs of (prefix history ++ this sequence)
     for (int i = tid; i < 3 * GQKV; i += GDN_THREADS) {
-      const int r = i / GQKV, cc = i % GQKV;
-      a.conv_pool[(size_t(sslot) * 3 + r) * conv_dim + chan(cc)] = sm.hist[r][cc];
+      const int r = i / GQKV, c = i % GQKV;
+      a.conv_pool[(size_t(sslot) * 3 + r) * conv_dim + chan(c)] = raw(len - 3 + r, c);
     }
     if (h == 0 && tid == 0) a.slot_len[sslot] = (pvalid ? a.slot_len[pslot] : 0) + len;
   }
@@ -269,13 +506,14 @@ using namespace sdb;
 int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix, int32_t ld_mix, uint16_t* out,
                   int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, cudaStream_t st) {
   if (!p || !s || !mix || !out) return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: null pointer");
-  if (p->dk != GDK || p->dv != GDV || p->conv_width != 4)
+  if (p->dk != GD || p->dv != GD || p->conv_width != 4)
     return sdb_fail(B200_ERR_UNSUPPORTED, "b200_gdn_mixer: only dk = dv = 128 and conv width 4 are built");
   if (!p->conv_w || !p->a_log || !p->dt_bias || !p->norm_w) return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: null param");
   if (s->n_seqs <= 0 || !s->cu_seqlens) return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: empty batch");
   const bool uses_pool = s->prefix_slot || s->save_slot;
   if (uses_pool && (!pool || !pool->gdn_state || !pool->conv_hist || !pool->slot_len))
     return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: prefix/save slots need a pool");
+  if (lo_offset % 2 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: lo_offset must be even");
   GdnArgs a;
   a.p = *p;
   a.cu = s->cu_seqlens;
@@ -285,12 +523,12 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
   a.ld_mix = ld_mix;
   a.out = out;
   a.lo_offset = lo_offset;
-  const int conv_dim = 2 * p->heads * GDK + p->heads * GDV;
-  if (ld_mix < conv_dim + p->heads * GDV + 2 * p->heads)
+  const int conv_dim = 3 * p->heads * GD;
+  if (ld_mix < conv_dim + p->heads * GD + 2 * p->heads)
     return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: ld_mix is narrower than [q|k|v|z|b|a]");
   a.n_slots = uses_pool ? pool->n_slots : 0;
   a.slot_len = uses_pool ? pool->slot_len : nullptr;
-  a.state_pool = uses_pool ? pool->gdn_state + size_t(layer) * pool->n_slots * p->heads * GDK * GDV : nullptr;
+  a.state_pool = uses_pool ? pool->gdn_state + size_t(layer) * pool->n_slots * p->heads * GD * GD : nullptr;
   a.conv_pool = uses_pool ? pool->conv_hist + size_t(layer) * pool->n_slots * 3 * conv_dim : nullptr;
   static bool attr = false;
   if (!attr) {
