@@ -194,6 +194,23 @@ int b200_attention(const b200_attn_params* p, const b200_seqs* seqs, const float
                    uint16_t* q_buf, uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset,
                    const b200_prefix_pool* pool, int32_t attn_layer, b200_stream stream);
 
+/* Same as b200_attention, but it allocates nothing and takes no scratch argument: the
+ * q / k / v scratch lives in a static 8 MiB device array inside this library (one per GPU
+ * that loads it, held until the process exits). It has no counterpart in the reference.
+ * It is for callers that cannot call cudaMalloc: a host runtime whose device memory is owned
+ * by its own arena or caching allocator (an embedding server that preallocated its pool, a
+ * Go or Java host that hands the library only its request buffers) cannot allocate or free
+ * mid-request, because cudaFree synchronises the device and a fresh cudaMalloc can fail on a
+ * full pool. Limits: tokens * (heads + 2*kv_heads) * head_dim * 2 bytes <= 8 MiB, else
+ * B200_ERR_SHAPE. The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress) with that device current. Every call shares the array and it keeps
+ * the last call's contents (each call overwrites all the scratch it reads, so nothing needs
+ * clearing); calls that can overlap on the GPU (different streams, or different host threads)
+ * race on it and must be serialised by the caller. */
+int b200_attention_noalloc(const b200_attn_params* p, const b200_seqs* seqs, const float* qkv, int32_t ld_qkv,
+                           uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool, int32_t attn_layer,
+                           b200_stream stream);
+
 /* ---------------------------------------------------------------- decision head
  * Replaces pool_last_token -> final RMSNorm -> option-token logits over the tied
  * embedding rows -> apply_temperature -> masked_log_softmax -> exp (modeling.py:193-238,

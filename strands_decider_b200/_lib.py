@@ -104,6 +104,8 @@ _SIGS = {
                         _P], C.c_int),
     "b200_attention": ([C.POINTER(AttnParams), C.POINTER(Seqs), _P, _I, _P, _P, _P, _P, C.c_int64,
                         C.POINTER(PrefixPool), _I, _P], C.c_int),
+    "b200_attention_noalloc": ([C.POINTER(AttnParams), C.POINTER(Seqs), _P, _I, _P, C.c_int64,
+                                C.POINTER(PrefixPool), _I, _P], C.c_int),
     "b200_decide": ([_P, _I, _P, C.c_float, _P, C.POINTER(DecideArgs), _P], C.c_int),
     "b200_model_create": ([C.POINTER(ModelConfig), C.POINTER(C.c_void_p)], C.c_int),
     "b200_model_destroy": ([_P], C.c_int),

@@ -7,6 +7,8 @@
 //   sequence that saves its cache, to the prefix pool as well.
 // attn_flash_kernel: tensor-core flash attention over the prefix slot's keys (positions
 //   0..P-1) then the sequence's own keys (P..P+j), causal, times sigmoid(gate).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace sdb {
@@ -410,6 +412,53 @@ int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qk
 extern "C" int b200_attention(const b200_attn_params* p, const b200_seqs* seqs, const float* qkv, int32_t ld_qkv,
                               uint16_t* q_buf, uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset,
                               const b200_prefix_pool* pool, int32_t attn_layer, b200_stream stream) {
+  return sdb_attention(p, seqs, qkv, ld_qkv, q_buf, k_buf, v_buf, out, lo_offset, pool, attn_layer,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+// ----------------------------------------------------------------------------- no-allocation variant
+// Scratch for b200_attention_noalloc: the post-norm, post-RoPE q / k / v of one call, in a
+// file-scope device array that every GPU loading this library holds until the process exits.
+// Host code must not pass the symbol itself to a kernel (on the host it names a host-side
+// stand-in); it looks the device address up once per device with cudaGetSymbolAddress.
+constexpr size_t kAttnNoAllocBytes = size_t(8) << 20;  // 8 MiB per device
+static __device__ __align__(256) uint16_t g_attn_noalloc_scratch[kAttnNoAllocBytes / 2];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+uint16_t* g_noalloc_ptr[kMaxDevices] = {};
+}  // namespace
+
+extern "C" int b200_attention_noalloc(const b200_attn_params* p, const b200_seqs* seqs, const float* qkv,
+                                      int32_t ld_qkv, uint16_t* out, int64_t lo_offset,
+                                      const b200_prefix_pool* pool, int32_t attn_layer, b200_stream stream) {
+  if (!p || !seqs) return sdb_fail(B200_ERR_ARG, "b200_attention_noalloc: null pointer");
+  const size_t per_token = size_t(p->heads + 2 * p->kv_heads) * size_t(p->head_dim);
+  if (seqs->n_tokens <= 0 || p->heads <= 0 || p->kv_heads < 0 || p->head_dim <= 0)
+    return sdb_fail(B200_ERR_SHAPE, "b200_attention_noalloc: bad shape");
+  if (size_t(seqs->n_tokens) * per_token * 2 > kAttnNoAllocBytes)
+    return sdb_fail(B200_ERR_SHAPE,
+                    "b200_attention_noalloc: tokens x (heads + 2 kv_heads) x head_dim x 2 bytes exceeds the "
+                    "8 MiB static scratch; use b200_attention with a caller-allocated scratch");
+  int dev = 0;
+  SDB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return sdb_fail(B200_ERR_UNSUPPORTED, "b200_attention_noalloc: device id");
+  uint16_t* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* ptr = nullptr;
+      // the current device is `dev`, so this returns that device's copy of the array
+      SDB_CUDA(cudaGetSymbolAddress(&ptr, g_attn_noalloc_scratch));
+      g_noalloc_ptr[dev] = static_cast<uint16_t*>(ptr);
+    }
+    base = g_noalloc_ptr[dev];
+  }
+  const size_t T = size_t(seqs->n_tokens);
+  uint16_t* q_buf = base;
+  uint16_t* k_buf = q_buf + T * p->heads * p->head_dim;
+  uint16_t* v_buf = k_buf + T * p->kv_heads * p->head_dim;
   return sdb_attention(p, seqs, qkv, ld_qkv, q_buf, k_buf, v_buf, out, lo_offset, pool, attn_layer,
                        reinterpret_cast<cudaStream_t>(stream));
 }
