@@ -161,7 +161,8 @@ int b200_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, f
  * state, and the gated RMSNorm (TF:175-190). mix: fp32 [tokens, ld_mix] holding the
  * in-projection's [q | k | v | z | b | a] columns; out: the two bf16 planes of the
  * out-projection's input, hi [tokens, heads*dv] and lo at out + lo_offset. gdn_layer
- * indexes the pool's GDN arrays. */
+ * indexes the pool's GDN arrays. scratch: fp32, b200_gdn_scratch_floats(heads, tokens)
+ * floats (the conv / l2norm / gating outputs the chunk kernel reads). */
 typedef struct b200_gdn_params {
   int32_t heads, dk, dv, conv_width;
   float eps;
@@ -173,7 +174,9 @@ typedef struct b200_gdn_params {
 
 int b200_gdn_mixer(const b200_gdn_params* p, const b200_seqs* seqs, const float* mix, int32_t ld_mix,
                    uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool, int32_t gdn_layer,
-                   b200_stream stream);
+                   float* scratch, b200_stream stream);
+/* fp32 scratch floats b200_gdn_mixer needs for a batch of n_tokens. */
+int b200_gdn_scratch_floats(int32_t heads, int32_t n_tokens);
 
 /* Gated GQA attention after its qkv projection (TF:647-690): per-head q/k RMSNorm(1+w),
  * partial RoPE on the first rope_dim dims (cos/sin tables [max_pos][rope_dim/2]), causal

@@ -1,11 +1,14 @@
 // Gated-DeltaNet token mixer (after the in-projection GEMM) on tensor cores.
 //
-// One CTA (8 warps) per (sequence, head); chunks of GC = 32 tokens run in order. Per chunk,
-// restating TF:234-311 with TF:462-530 fused around it:
-//   1. g_j = -exp(A_log) softplus(a_j + dt_bias), beta_j = sigmoid(b_j); G = cumsum(g)
-//   2. causal depthwise conv (width 4) + SiLU over the head's q, k, v channels (the 3
-//      previous raw inputs come from the sequence itself or the prefix slot's history),
-//      l2norm(q) * dk^-1/2, l2norm(k)
+// Two kernels, restating TF:234-311 with TF:462-530 fused around it.
+// gdn_prep_kernel, one warp per (token, head), fully parallel:
+//   causal depthwise conv (width 4) + SiLU over the head's q, k, v channels (the 3 previous
+//   raw inputs come from the sequence itself or the prefix slot's history), l2norm(q) *
+//   dk^-1/2, l2norm(k), beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias); a sequence
+//   that saves its cache also writes its last 3 raw inputs (the conv history) to the pool.
+// gdn_mixer_kernel, one CTA (8 warps) per (sequence, head), chunks of GC = 32 tokens in order:
+//   1. G = cumsum(g) within the chunk
+//   2. q, k and [beta v | beta k e^G] as hi/lo planes in shared memory
 //   3. A = strictly-lower(beta_i k_i.k_j e^{G_i-G_j}), P = lower(q_i.k_j e^{G_i-G_j})
 //   4. T = (I + A)^{-1} by block forward substitution (fp32)
 //   5. [U | W] = T [beta v | beta k e^G]
@@ -24,6 +27,7 @@ namespace sdb {
 constexpr int GC = 32;          // chunk length
 constexpr int GD = 128;         // key / value head dim
 constexpr int GQKV = 3 * GD;
+constexpr int GPREP = GQKV + 4;   // per (token, head): q | k | v | beta, g, pad
 constexpr int GDN_THREADS = 256;
 
 struct GdnArgs {
@@ -31,8 +35,10 @@ struct GdnArgs {
   const int32_t* cu;
   const int32_t* prefix_slot;
   const int32_t* save_slot;
+  int n_seqs;
   const float* mix;      // [T, ld_mix]: q | k | v | z | b | a
   int ld_mix;
+  float* prep;           // [T][heads][GPREP]: q (128) | k (128) | v (128) | beta | g  (fp32)
   uint16_t* out;         // hi plane [T, value_dim]; lo plane at out + lo_offset
   long long lo_offset;
   int32_t* slot_len;
@@ -61,7 +67,6 @@ struct GdnSmem {
   uint16_t Ih[GC * GC], Il[GC * GC];           // (I + A)^{-1}
   float A[GC][GC + 1];                          // A, then the inverse in fp32
   float O[GC][GD + 4];
-  float hist[3][GQKV];                          // prefix conv history (raw inputs)
   float G[GC], beta[GC], eG[GC], eL[GC];
 };
 
@@ -132,6 +137,89 @@ __device__ __forceinline__ void mma3(float (&d0)[4], float (&d1)[4], const uint3
   mma16816(d1, al, bh[2], bh[3]);
 }
 
+// ----------------------------------------------------------------------------- prep kernel
+__device__ __forceinline__ int gdn_find_seq(const int32_t* cu, int n, int t) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// One warp per (token, head); lane l owns channels 4l..4l+3 of q, k and v.
+__global__ void __launch_bounds__(256) gdn_prep_kernel(const GdnArgs a, int n_tokens) {
+  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int H = a.p.heads;
+  const int t = gw / H, h = gw % H;
+  if (t >= n_tokens) return;
+  const int key_dim = H * GD, conv_dim = 3 * key_dim, value_dim = key_dim;
+  const int seq = gdn_find_seq(a.cu, a.n_seqs, t);
+  const int tok0 = a.cu[seq], len = a.cu[seq + 1] - tok0, p = t - tok0;
+  const int pslot = a.prefix_slot ? a.prefix_slot[seq] : -1;
+  const int sslot = a.save_slot ? a.save_slot[seq] : -1;
+  const bool pvalid = pslot >= 0 && pslot < a.n_slots;
+  const int base[3] = {h * GD, key_dim + h * GD, 2 * key_dim + h * GD};
+  float out[3][4];
+#pragma unroll
+  for (int part = 0; part < 3; ++part) {
+    const int ch = base[part] + lane * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int tap = 0; tap < 4; ++tap) {
+      const int pp = p - 3 + tap;
+      float4 x;
+      if (pp >= 0) x = *reinterpret_cast<const float4*>(a.mix + size_t(tok0 + pp) * a.ld_mix + ch);
+      else if (pvalid) x = *reinterpret_cast<const float4*>(a.conv_pool + (size_t(pslot) * 3 + (3 + pp)) * conv_dim + ch);
+      else x = make_float4(0.f, 0.f, 0.f, 0.f);
+      acc.x = fmaf(a.p.conv_w[(ch + 0) * 4 + tap], x.x, acc.x);
+      acc.y = fmaf(a.p.conv_w[(ch + 1) * 4 + tap], x.y, acc.y);
+      acc.z = fmaf(a.p.conv_w[(ch + 2) * 4 + tap], x.z, acc.z);
+      acc.w = fmaf(a.p.conv_w[(ch + 3) * 4 + tap], x.w, acc.w);
+    }
+    out[part][0] = silu(acc.x);
+    out[part][1] = silu(acc.y);
+    out[part][2] = silu(acc.z);
+    out[part][3] = silu(acc.w);
+  }
+  float sq = 0.f, sk = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    sq += out[0][e] * out[0][e];
+    sk += out[1][e] * out[1][e];
+  }
+  sq = warp_sum(sq);
+  sk = warp_sum(sk);
+  const float rq = rsqrtf(sq + 1e-6f) * rsqrtf(float(GD)), rk = rsqrtf(sk + 1e-6f);
+  float* dst = a.prep + (size_t(t) * H + h) * GPREP;
+  reinterpret_cast<float4*>(dst)[lane] = make_float4(out[0][0] * rq, out[0][1] * rq, out[0][2] * rq, out[0][3] * rq);
+  reinterpret_cast<float4*>(dst + GD)[lane] =
+      make_float4(out[1][0] * rk, out[1][1] * rk, out[1][2] * rk, out[1][3] * rk);
+  reinterpret_cast<float4*>(dst + 2 * GD)[lane] = make_float4(out[2][0], out[2][1], out[2][2], out[2][3]);
+  if (lane == 0) {
+    const float* ab = a.mix + size_t(t) * a.ld_mix + conv_dim + value_dim;
+    dst[GQKV] = sigmoid(ab[h]);
+    dst[GQKV + 1] = -__expf(a.p.a_log[h]) * softplus(ab[H + h] + a.p.dt_bias[h]);
+  }
+  // conv history of a saving sequence: its last 3 raw inputs, written by the last token's warps
+  const int sv = (sslot >= 0 && sslot < a.n_slots) ? sslot : -1;
+  if (sv >= 0 && p == len - 1) {
+    for (int r = 0; r < 3; ++r) {
+      const int pp = len - 3 + r;
+#pragma unroll
+      for (int part = 0; part < 3; ++part) {
+        const int ch = base[part] + lane * 4;
+        float4 x;
+        if (pp >= 0) x = *reinterpret_cast<const float4*>(a.mix + size_t(tok0 + pp) * a.ld_mix + ch);
+        else if (pvalid) x = *reinterpret_cast<const float4*>(a.conv_pool + (size_t(pslot) * 3 + (3 + pp)) * conv_dim + ch);
+        else x = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(a.conv_pool + (size_t(sv) * 3 + r) * conv_dim + ch) = x;
+      }
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------- kernel
 __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs a) {
   extern __shared__ uint8_t gdn_smem_raw[];
@@ -148,16 +236,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
   const bool svalid = sslot >= 0 && sslot < a.n_slots;
   if ((pslot >= a.n_slots || sslot >= a.n_slots) && tid == 0) raise_fault(FAULT_BAD_INDEX);
 
-  // channel of head-local index c in 0..383 (q, k, v)
-  auto chan = [&](int c) {
-    return c < GD ? h * GD + c : c < 2 * GD ? key_dim + h * GD + (c - GD) : 2 * key_dim + h * GD + (c - 2 * GD);
-  };
-  // raw pre-conv input of channel c (head-local) at sequence position p (p < 0: history)
-  auto raw = [&](int p, int c) -> float {
-    return p >= 0 ? a.mix[size_t(tok0 + p) * a.ld_mix + chan(c)] : sm.hist[3 + p][c];
-  };
-
-  // ---- initial state (fp32 slab in registers) and prefix conv history
+  // ---- initial state (fp32 slab in registers)
   float S[16][4];  // rows 16*warp + g8 (+8), cols 8*nt + 2*t4 (+1)
   {
     const float* src = pvalid ? a.state_pool + (size_t(pslot) * H + h) * GD * GD : nullptr;
@@ -170,10 +249,6 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       }
     }
   }
-  for (int i = tid; i < 3 * GQKV; i += GDN_THREADS) {
-    const int r = i / GQKV, c = i % GQKV;
-    sm.hist[r][c] = pvalid ? a.conv_pool[(size_t(pslot) * 3 + r) * conv_dim + chan(c)] : 0.0f;
-  }
   auto publish_state = [&]() {
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt) {
@@ -185,23 +260,19 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
     }
   };
   publish_state();
-  const float A_exp = __expf(a.p.a_log[h]);
-  const float dtb = a.p.dt_bias[h];
-  const float qscale = rsqrtf(float(GD));
   __syncthreads();
 
   for (int c0 = 0; c0 < len; c0 += GC) {
     const int L = min(GC, len - c0);
-    // ---- 1. gating, cumulative decay
+    // ---- 1. cumulative decay within the chunk
     if (tid < GC) {
       float gj = 0.0f, bj = 0.0f;
       if (tid < L) {
-        const float* ab = a.mix + size_t(tok0 + c0 + tid) * a.ld_mix + conv_dim + value_dim;
-        bj = sigmoid(ab[h]);
-        gj = -A_exp * softplus(ab[H + h] + dtb);
+        const float* pr = a.prep + (size_t(tok0 + c0 + tid) * H + h) * GPREP + GQKV;
+        bj = pr[0];
+        gj = pr[1];
       }
-      // inclusive warp scan of g over the chunk
-      float v = gj;
+      float v = gj;  // inclusive warp scan
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const float n = __shfl_up_sync(0xffffffffu, v, o);
@@ -213,55 +284,32 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
     }
     __syncthreads();
     if (tid < GC) sm.eL[tid] = tid < L ? __expf(sm.G[L - 1] - sm.G[tid]) : 0.0f;
-    // ---- 2. conv + SiLU + l2norm; write q, k, [beta v | beta k e^G] as hi/lo planes
+    // ---- 2. q, k, [beta v | beta k e^G] as hi/lo planes (rows past L are zero)
     for (int j = warp; j < GC; j += GDN_THREADS / 32) {
-      float q[4], k[4], v[4];
+      float4 q = make_float4(0.f, 0.f, 0.f, 0.f), k = q, v = q;
       if (j < L) {
-        const int p = c0 + j;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int cq = lane * 4 + e;
-          float aq = 0.0f, ak = 0.0f, av = 0.0f;
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            aq = fmaf(a.p.conv_w[chan(cq) * 4 + t], raw(p - 3 + t, cq), aq);
-            ak = fmaf(a.p.conv_w[chan(GD + cq) * 4 + t], raw(p - 3 + t, GD + cq), ak);
-            av = fmaf(a.p.conv_w[chan(2 * GD + cq) * 4 + t], raw(p - 3 + t, 2 * GD + cq), av);
-          }
-          q[e] = silu(aq);
-          k[e] = silu(ak);
-          v[e] = silu(av);
-        }
-        float sq = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
-        float sk = k[0] * k[0] + k[1] * k[1] + k[2] * k[2] + k[3] * k[3];
-        sq = warp_sum(sq);
-        sk = warp_sum(sk);
-        const float rq = rsqrtf(sq + 1e-6f) * qscale, rk = rsqrtf(sk + 1e-6f);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          q[e] *= rq;
-          k[e] *= rk;
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) q[e] = k[e] = v[e] = 0.0f;
+        const float* pr = a.prep + (size_t(tok0 + c0 + j) * H + h) * GPREP;
+        q = reinterpret_cast<const float4*>(pr)[lane];
+        k = reinterpret_cast<const float4*>(pr + GD)[lane];
+        v = reinterpret_cast<const float4*>(pr + 2 * GD)[lane];
       }
       const float bj = sm.beta[j], bke = bj * sm.eG[j];
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const int c = lane * 4 + e;
-        split_store(sm.Qh, sm.Ql, soff<GD>(j, c), q[e], q[e + 1]);
-        split_store(sm.Kh, sm.Kl, soff<GD>(j, c), k[e], k[e + 1]);
-        split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, c), bj * v[e], bj * v[e + 1]);
-        split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, GD + c), bke * k[e], bke * k[e + 1]);
-      }
+      const int c = lane * 4;
+      split_store(sm.Qh, sm.Ql, soff<GD>(j, c), q.x, q.y);
+      split_store(sm.Qh, sm.Ql, soff<GD>(j, c + 2), q.z, q.w);
+      split_store(sm.Kh, sm.Kl, soff<GD>(j, c), k.x, k.y);
+      split_store(sm.Kh, sm.Kl, soff<GD>(j, c + 2), k.z, k.w);
+      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, c), bj * v.x, bj * v.y);
+      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, c + 2), bj * v.z, bj * v.w);
+      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, GD + c), bke * k.x, bke * k.y);
+      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, GD + c + 2), bke * k.z, bke * k.w);
     }
     __syncthreads();
     // ---- 3. A = beta k k^T, P = q k^T (x decay, masked): warp -> rows 16*(w>>2), cols 8*(w&3)
     {
       const int m0 = 16 * (warp >> 2), n0 = 8 * (warp & 3);
       float kk[4] = {0, 0, 0, 0}, qk[4] = {0, 0, 0, 0};
-#pragma unroll
+#pragma unroll 2
       for (int k0 = 0; k0 < GD; k0 += 16) {
         uint32_t kh[4], kl[4], qh[4], ql[4], bh[4], bl[4];
         frag_a<GD>(kh, sm.Kh, m0, k0, lane);
@@ -371,7 +419,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       float ws[4][4], qs[4][4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) ws[j][0] = ws[j][1] = ws[j][2] = ws[j][3] = qs[j][0] = qs[j][1] = qs[j][2] = qs[j][3] = 0.0f;
-#pragma unroll
+#pragma unroll 1
       for (int k0 = 0; k0 < GD; k0 += 16) {
         uint32_t wh[4], wl[4], qh[4], ql[4];
         frag_a<GD>(wh, sm.ru.uw.Wh, m0, k0, lane);
@@ -490,11 +538,6 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
         dst[r * GD + c] = S[nt][e];
       }
     }
-    // conv history: the last 3 raw inputs of (prefix history ++ this sequence)
-    for (int i = tid; i < 3 * GQKV; i += GDN_THREADS) {
-      const int r = i / GQKV, c = i % GQKV;
-      a.conv_pool[(size_t(sslot) * 3 + r) * conv_dim + chan(c)] = raw(len - 3 + r, c);
-    }
     if (h == 0 && tid == 0) a.slot_len[sslot] = (pvalid ? a.slot_len[pslot] : 0) + len;
   }
 }
@@ -503,8 +546,10 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
 
 using namespace sdb;
 
+int sdb_gdn_prep_floats(int heads, int n_tokens) { return n_tokens * heads * GPREP; }
+
 int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix, int32_t ld_mix, uint16_t* out,
-                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, cudaStream_t st) {
+                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, float* prep, cudaStream_t st) {
   if (!p || !s || !mix || !out) return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: null pointer");
   if (p->dk != GD || p->dv != GD || p->conv_width != 4)
     return sdb_fail(B200_ERR_UNSUPPORTED, "b200_gdn_mixer: only dk = dv = 128 and conv width 4 are built");
@@ -519,6 +564,9 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
   a.cu = s->cu_seqlens;
   a.prefix_slot = s->prefix_slot;
   a.save_slot = s->save_slot;
+  a.n_seqs = s->n_seqs;
+  a.prep = prep;
+  if (!prep) return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: null scratch");
   a.mix = mix;
   a.ld_mix = ld_mix;
   a.out = out;
@@ -535,6 +583,9 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
     SDB_CUDA(cudaFuncSetAttribute(gdn_mixer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GdnSmem))));
     attr = true;
   }
+  const long warps = long(s->n_tokens) * p->heads;
+  gdn_prep_kernel<<<int((warps + 7) / 8), 256, 0, st>>>(a, s->n_tokens);
+  SDB_LAUNCH_CHECK();
   gdn_mixer_kernel<<<dim3(p->heads, s->n_seqs), GDN_THREADS, sizeof(GdnSmem), st>>>(a);
   SDB_LAUNCH_CHECK();
   return B200_OK;
@@ -542,6 +593,9 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
 
 extern "C" int b200_gdn_mixer(const b200_gdn_params* p, const b200_seqs* seqs, const float* mix, int32_t ld_mix,
                               uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool, int32_t gdn_layer,
-                              b200_stream stream) {
-  return sdb_gdn_mixer(p, seqs, mix, ld_mix, out, lo_offset, pool, gdn_layer, reinterpret_cast<cudaStream_t>(stream));
+                              float* scratch, b200_stream stream) {
+  return sdb_gdn_mixer(p, seqs, mix, ld_mix, out, lo_offset, pool, gdn_layer, scratch,
+                       reinterpret_cast<cudaStream_t>(stream));
 }
+
+extern "C" int b200_gdn_scratch_floats(int32_t heads, int32_t n_tokens) { return sdb_gdn_prep_floats(heads, n_tokens); }

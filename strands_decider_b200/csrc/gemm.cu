@@ -1,23 +1,26 @@
 // Weight-only quantised linear layers on the 5th-generation tensor cores (tcgen05).
 //
 // y[m, n] = sum_k x[m, k] * W[n, k] with W packed (int4 g128, NVFP4, ternary or bf16) and x
-// held as two bf16 planes x_hi + x_lo (fp32-level precision). One CTA computes a 128 x BN
-// tile (BN = 256) with the accumulator in tensor memory:
+// held as two bf16 planes x_hi + x_lo (fp32-level precision). A persistent CTA per SM walks
+// 128 x BN output tiles (BN = 256, N fastest so concurrent CTAs share activation tiles),
+// with two accumulators in tensor memory (2 x 256 columns) so the epilogue of one tile
+// overlaps the main loop of the next:
 //   warp 0      one lane streams each stage: TMA loads of the x tiles (128 rows x 64 k
 //               per plane, 128-byte swizzle) and bulk copies of the stage's packed weight
 //               chunk and scales (the b200_tile_weights layout); bf16 weights come as a
 //               swizzled TMA tile straight into the B stage
 //   warp 1      allocates TMEM; one lane issues tcgen05.mma (M=128, N=BN, K=16): per 16 k,
 //               one MMA for x_hi and one for x_lo against the same weight tile
-//   warps 2..9  unpack the stage's packed weights from shared memory to bf16, directly into
-//               the 128-byte-swizzled K-major layout the MMA reads, then run the epilogue
-//               (TMEM -> registers -> fused op -> global); each TMEM lane quarter is read by
-//               two warps, one per column half
+//   warps 2..5  epilogue: TMEM -> registers -> fused op -> global, one TMEM lane quarter each
+//   warps 6..13 unpack the stage's packed weights from shared memory to bf16, directly into
+//               the 128-byte-swizzled K-major layout the MMA reads
 // A 3-stage ring of shared-memory stages is guarded by mbarriers: full_a (activation TMA
 // bytes), full_w (packed weight bytes), full_b (256 unpacking threads), empty
-// (tcgen05.commit). Every wait is bounded.
+// (tcgen05.commit); the two accumulators by acc_full (tcgen05.commit) and acc_empty (the 4
+// epilogue warps). Every wait is bounded.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "dequant.cuh"
@@ -26,8 +29,12 @@ namespace sdb {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
-constexpr int GEMM_THREADS = 320;          // warp 0 TMA, warp 1 MMA, warps 2..9 unpack + epilogue
+// warp 0 streams stages, warp 1 issues MMAs, warps 2..5 run the epilogue (one per TMEM lane
+// quarter), warps 6..13 unpack weights
+constexpr int GEMM_THREADS = 448;
 constexpr int GEMM_UNPACK_THREADS = 256;
+constexpr int GEMM_EPI_WARP0 = 2;
+constexpr int GEMM_UNPACK_WARP0 = 6;
 
 constexpr int GEMM_STAGES = 3;
 
@@ -46,7 +53,7 @@ struct GemmSmem {
   static constexpr int W_BYTES = PACKED ? BN * tile_row_bytes(FMT) : 0;
   static constexpr int S_BYTES = BN * tile_scale_row_bytes(FMT);
   static constexpr int STAGE = A_STAGE + B_BYTES + W_BYTES + S_BYTES;
-  static constexpr int BARS = 4 * GEMM_STAGES + 1;
+  static constexpr int BARS = 4 * GEMM_STAGES + 4;
   static constexpr int TOTAL = GEMM_STAGES * STAGE + 1024 + BARS * 8 + 16 + 64;
 };
 
@@ -199,13 +206,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* full_w = bars + GEMM_STAGES;
   uint64_t* full_b = bars + 2 * GEMM_STAGES;
   uint64_t* empty = bars + 3 * GEMM_STAGES;
-  uint64_t* accum = bars + 4 * GEMM_STAGES;
+  uint64_t* acc_full = bars + 4 * GEMM_STAGES;       // [2]
+  uint64_t* acc_empty = bars + 4 * GEMM_STAGES + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + SM::BARS);
   uint32_t* lut = tmem_slot + 4;  // 16 words: ternary pair table
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * GEMM_BM;
   const int nk = args.k / GEMM_BK;
+  const int n_tiles_n = args.w.n / BN;
+  const int n_tiles = n_tiles_n * ((args.m + GEMM_BM - 1) / GEMM_BM);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < GEMM_STAGES; ++s) {
@@ -214,12 +223,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&full_b[s], GEMM_UNPACK_THREADS);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4 * 32);
+    }
     mbar_fence_init();
   }
   if (threadIdx.x < 16) lut[threadIdx.x] = ternary_pair_bits(threadIdx.x);
   if (warp == 1) {
-    tmem_alloc(tmem_slot, BN);
+    tmem_alloc(tmem_slot, 2 * BN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -228,103 +240,129 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
+    // ---------------- producer: activations (TMA) and packed weights (bulk copies)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       if constexpr (SPLIT) tma_prefetch_desc(&tmA_lo);
       if constexpr (!SM::PACKED) tma_prefetch_desc(&tmB);
-      const uint8_t* wtiles = reinterpret_cast<const uint8_t*>(args.w.tiles) + size_t(blockIdx.x) * nk * SM::W_BYTES;
-      const uint8_t* stiles =
-          reinterpret_cast<const uint8_t*>(args.w.tile_scales) + size_t(blockIdx.x) * nk * SM::S_BYTES;
-      for (int kt = 0; kt < nk; ++kt) {
-        const int s = kt % GEMM_STAGES;
-        const uint32_t ph = (kt / GEMM_STAGES) & 1;
-        mbar_wait(&empty[s], ph ^ 1, FAULT_GEMM_WAIT_EMPTY);
-        if constexpr (SM::PACKED) {
-          mbar_arrive_expect_tx(&full_w[s], SM::W_BYTES + SM::S_BYTES);
-          bulk_load(sW + s * SM::W_BYTES, wtiles + size_t(kt) * SM::W_BYTES, SM::W_BYTES, &full_w[s]);
-          if constexpr (SM::S_BYTES > 0)
-            bulk_load(sS + s * SM::S_BYTES, stiles + size_t(kt) * SM::S_BYTES, SM::S_BYTES, &full_w[s]);
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const int nt = tile % n_tiles_n, m0 = (tile / n_tiles_n) * GEMM_BM, n0 = nt * BN;
+        const uint8_t* wtiles = reinterpret_cast<const uint8_t*>(args.w.tiles) + size_t(nt) * nk * SM::W_BYTES;
+        const uint8_t* stiles = reinterpret_cast<const uint8_t*>(args.w.tile_scales) + size_t(nt) * nk * SM::S_BYTES;
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % GEMM_STAGES;
+          const uint32_t ph = (it / GEMM_STAGES) & 1;
+          mbar_wait(&empty[s], ph ^ 1, FAULT_GEMM_WAIT_EMPTY);
+          if constexpr (SM::PACKED) {
+            mbar_arrive_expect_tx(&full_w[s], SM::W_BYTES + SM::S_BYTES);
+            bulk_load(sW + s * SM::W_BYTES, wtiles + size_t(kt) * SM::W_BYTES, SM::W_BYTES, &full_w[s]);
+            if constexpr (SM::S_BYTES > 0)
+              bulk_load(sS + s * SM::S_BYTES, stiles + size_t(kt) * SM::S_BYTES, SM::S_BYTES, &full_w[s]);
+          }
+          mbar_arrive_expect_tx(&full_a[s], SM::A_STAGE + (SM::PACKED ? 0 : SM::B_BYTES));
+          tma_load_2d(sA + s * SM::A_STAGE, &tmA, &full_a[s], kt * GEMM_BK, m0);
+          if constexpr (SPLIT)
+            tma_load_2d(sA + s * SM::A_STAGE + SM::A_BYTES, &tmA_lo, &full_a[s], kt * GEMM_BK, m0);
+          if constexpr (!SM::PACKED) tma_load_2d(sB + s * SM::B_BYTES, &tmB, &full_a[s], kt * GEMM_BK, n0);
         }
-        mbar_arrive_expect_tx(&full_a[s], SM::A_STAGE + (SM::PACKED ? 0 : SM::B_BYTES));
-        tma_load_2d(sA + s * SM::A_STAGE, &tmA, &full_a[s], kt * GEMM_BK, m0);
-        if constexpr (SPLIT) tma_load_2d(sA + s * SM::A_STAGE + SM::A_BYTES, &tmA_lo, &full_a[s], kt * GEMM_BK, m0);
-        if constexpr (!SM::PACKED) tma_load_2d(sB + s * SM::B_BYTES, &tmB, &full_a[s], kt * GEMM_BK, n0);
       }
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(GEMM_BM, BN);
-      for (int kt = 0; kt < nk; ++kt) {
-        const int s = kt % GEMM_STAGES;
-        const uint32_t ph = (kt / GEMM_STAGES) & 1;
-        mbar_wait(&full_a[s], ph, FAULT_GEMM_WAIT_FULL_A);
-        if constexpr (SM::PACKED) mbar_wait(&full_b[s], ph, FAULT_GEMM_WAIT_FULL_B);
+      uint32_t it = 0, local = 0;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
+        const uint32_t ab = local & 1, aph = (local >> 1) & 1;
+        mbar_wait(&acc_empty[ab], aph ^ 1, FAULT_GEMM_WAIT_ACCUM);
         tc_fence_after();
-        const uint64_t ad = umma_desc_sw128(smem_addr(sA + s * SM::A_STAGE));
-        const uint64_t bd = umma_desc_sw128(smem_addr(sB + s * SM::B_BYTES));
+        const uint32_t acc = tmem_base + ab * BN;
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % GEMM_STAGES;
+          const uint32_t ph = (it / GEMM_STAGES) & 1;
+          mbar_wait(&full_a[s], ph, FAULT_GEMM_WAIT_FULL_A);
+          if constexpr (SM::PACKED) mbar_wait(&full_b[s], ph, FAULT_GEMM_WAIT_FULL_B);
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128(smem_addr(sA + s * SM::A_STAGE));
+          const uint64_t bd = umma_desc_sw128(smem_addr(sB + s * SM::B_BYTES));
 #pragma unroll
-        for (int j = 0; j < GEMM_BK / 16; ++j) {  // +32 bytes of K per MMA = +2 in 16-byte units
-          umma_bf16(tmem_base, ad + 2 * j, bd + 2 * j, idesc, (kt | j) != 0 ? 1u : 0u);
-          if constexpr (SPLIT) umma_bf16(tmem_base, ad + (SM::A_BYTES >> 4) + 2 * j, bd + 2 * j, idesc, 1u);
+          for (int j = 0; j < GEMM_BK / 16; ++j) {  // +32 bytes of K per MMA = +2 in 16-byte units
+            umma_bf16(acc, ad + 2 * j, bd + 2 * j, idesc, (kt | j) != 0 ? 1u : 0u);
+            if constexpr (SPLIT) umma_bf16(acc, ad + (SM::A_BYTES >> 4) + 2 * j, bd + 2 * j, idesc, 1u);
+          }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        umma_commit(&acc_full[ab]);
       }
-      umma_commit(accum);
     }
     __syncwarp();
+  } else if (warp < GEMM_UNPACK_WARP0) {
+    // ---------------- epilogue: warp (2..5) owns TMEM lanes 32*(warp%4)..+31, all columns
+    const int q = warp & 3;
+    uint32_t local = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
+      const int nt = tile % n_tiles_n, m0 = (tile / n_tiles_n) * GEMM_BM, n0 = nt * BN;
+      const uint32_t ab = local & 1, aph = (local >> 1) & 1;
+      mbar_wait(&acc_full[ab], aph, FAULT_GEMM_WAIT_ACCUM);
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const uint32_t tl = tmem_base + ab * BN + (uint32_t(q * 32) << 16);
+      if constexpr (EP == B200_EP_SWIGLU) {
+#pragma unroll 1
+        for (int b = 0; b < BN / 128; ++b) {  // 128-column block: gate cols 0..63, up cols 64..127
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            uint32_t g[32], u[32];
+            tmem_ld_32x32b_x32(tl + b * 128 + c * 32, g);
+            tmem_ld_32x32b_x32(tl + b * 128 + 64 + c * 32, u);
+            tmem_ld_wait();
+            epilogue_swiglu(args, row, (n0 + b * 128) / 2 + c * 32, g, u);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tl + c * 32, v);
+          tmem_ld_wait();
+          epilogue_chunk<EP>(args, row, n0 + c * 32, v);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[ab]);
+    }
   } else {
     // ---------------- weight unpack (256 threads): shared chunk -> swizzled bf16 tile
     if constexpr (SM::PACKED) {
-      const int t = threadIdx.x - 64;
+      const int t = threadIdx.x - GEMM_UNPACK_WARP0 * 32;
       constexpr int UNITS = BN * 2 / GEMM_UNPACK_THREADS;
-      uint32_t row_sc[UNITS];
-      float row_gs[UNITS];
-#pragma unroll
-      for (int i = 0; i < UNITS; ++i) {
-        const int r = (t + GEMM_UNPACK_THREADS * i) >> 1;
-        row_sc[i] = FMT == B200_W_TERNARY ? uint32_t(__ldg(reinterpret_cast<const uint16_t*>(args.w.scales) + n0 + r)) : 0u;
-        row_gs[i] = FMT == B200_W_NVFP4 ? __ldg(args.w.row_scale + n0 + r) : 1.0f;
-      }
-      for (int kt = 0; kt < nk; ++kt) {
-        const int s = kt % GEMM_STAGES;
-        const uint32_t ph = (kt / GEMM_STAGES) & 1;
-        mbar_wait(&full_w[s], ph, FAULT_GEMM_WAIT_FULL_W);
-        uint8_t* stage = sB + s * SM::B_BYTES;
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const int n0 = (tile % n_tiles_n) * BN;
+        uint32_t row_sc[UNITS];
+        float row_gs[UNITS];
 #pragma unroll
         for (int i = 0; i < UNITS; ++i) {
-          const int u = t + GEMM_UNPACK_THREADS * i;
-          unpack_unit_smem<FMT>(stage, sW + s * SM::W_BYTES, sS + s * SM::S_BYTES, u >> 1, u & 1, row_sc[i],
-                                row_gs[i], lut);
+          const int r = (t + GEMM_UNPACK_THREADS * i) >> 1;
+          row_sc[i] =
+              FMT == B200_W_TERNARY ? uint32_t(__ldg(reinterpret_cast<const uint16_t*>(args.w.scales) + n0 + r)) : 0u;
+          row_gs[i] = FMT == B200_W_NVFP4 ? __ldg(args.w.row_scale + n0 + r) : 1.0f;
         }
-        fence_proxy_async_smem();
-        mbar_arrive(&full_b[s]);
-      }
-    }
-
-    // ---------------- epilogue: TMEM lanes 32*(warp%4)..+31, one column half per warp
-    mbar_wait(accum, 0, FAULT_GEMM_WAIT_ACCUM);
-    tc_fence_after();
-    const int q = warp & 3;
-    const int ch = (warp - 2) >> 2;  // column half
-    const int row = m0 + q * 32 + lane;
-    const uint32_t tl = tmem_base + (uint32_t(q * 32) << 16);
-    if constexpr (EP == B200_EP_SWIGLU) {
-      const int b = ch;  // 128-column block: gate cols 0..63, up cols 64..127
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t g[32], u[32];
-        tmem_ld_32x32b_x32(tl + b * 128 + c * 32, g);
-        tmem_ld_32x32b_x32(tl + b * 128 + 64 + c * 32, u);
-        tmem_ld_wait();
-        epilogue_swiglu(args, row, (n0 + b * 128) / 2 + c * 32, g, u);
-      }
-    } else {
-#pragma unroll 1
-      for (int c = ch * (BN / 64); c < (ch + 1) * (BN / 64); ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tl + c * 32, v);
-        tmem_ld_wait();
-        epilogue_chunk<EP>(args, row, n0 + c * 32, v);
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % GEMM_STAGES;
+          const uint32_t ph = (it / GEMM_STAGES) & 1;
+          mbar_wait(&full_w[s], ph, FAULT_GEMM_WAIT_FULL_W);
+          uint8_t* stage = sB + s * SM::B_BYTES;
+#pragma unroll
+          for (int i = 0; i < UNITS; ++i) {
+            const int u = t + GEMM_UNPACK_THREADS * i;
+            unpack_unit_smem<FMT>(stage, sW + s * SM::W_BYTES, sS + s * SM::S_BYTES, u >> 1, u & 1, row_sc[i],
+                                  row_gs[i], lut);
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&full_b[s]);
+        }
       }
     }
   }
@@ -333,16 +371,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, BN);
+    tmem_dealloc(tmem_base, 2 * BN);
   }
 }
 
 // --------------------------------------------------------------------------- SIMT cross-check
 template <int FMT>
 __device__ __forceinline__ void load_row32_f32(const b200_qweight& w, int n, int k0, float (&out)[32]) {
-  __shared__ uint32_t lut[16];
-  for (int i = threadIdx.x; i < 16; i += blockDim.x) lut[i] = ternary_pair_bits(i);
-  __syncwarp();
+  uint32_t lut[16];  // per-thread copy: this cross-check kernel has threads that exit early
+#pragma unroll
+  for (int i = 0; i < 16; ++i) lut[i] = ternary_pair_bits(i);
   Raw32<FMT> r;
   load_unit<FMT>(w, n, k0, r);
   uint4 u[4];
@@ -467,8 +505,14 @@ static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_lo, const CU
                                   smem));
     attr_set = true;
   }
-  dim3 grid(a.w.n / BN, (a.m + GEMM_BM - 1) / GEMM_BM);
-  gemm_tc_kernel<BN, FMT, EP, SPLIT><<<grid, GEMM_THREADS, smem, st>>>(map, map_lo, map_b, a);
+  static int n_sm = 0;
+  if (!n_sm) {
+    int dev = 0;
+    SDB_CUDA(cudaGetDevice(&dev));
+    SDB_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const int tiles = (a.w.n / BN) * ((a.m + GEMM_BM - 1) / GEMM_BM);
+  gemm_tc_kernel<BN, FMT, EP, SPLIT><<<std::min(tiles, n_sm), GEMM_THREADS, smem, st>>>(map, map_lo, map_b, a);
   SDB_LAUNCH_CHECK();
   return B200_OK;
 }

@@ -24,7 +24,8 @@ int sdb_embed_vocab(const int32_t* ids, int32_t n_tokens, const uint16_t* table,
 int sdb_decide_vocab(const float* x, int32_t hidden, const float* final_norm, float eps, const uint16_t* table,
                      const b200_decide_args* d, int vocab, int n_tokens, cudaStream_t st);
 int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix, int32_t ld_mix, uint16_t* out,
-                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, cudaStream_t st);
+                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, float* prep, cudaStream_t st);
+int sdb_gdn_prep_floats(int heads, int n_tokens);
 int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qkv, int32_t ld_qkv, uint16_t* q_buf,
                   uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool,
                   int32_t layer, cudaStream_t st);
@@ -81,8 +82,9 @@ namespace {
 //   mix  fp32 [T, mix_cols]          in-projection outputs (GDN [q|k|v|z|b|a], attention [q,gate|k|v])
 //   act  2 x bf16 [T, act_cols]      mixer outputs / SwiGLU outputs as hi/lo planes (GEMM input)
 //   q, k, v  bf16                    attention scratch (post norm + RoPE)
+//   prep fp32                        GDN scratch (conv / l2norm / gating outputs)
 struct WsLayout {
-  size_t x, xn, mix, act, q, k, v, total;
+  size_t x, xn, mix, act, q, k, v, prep, total;
   int mix_cols, act_cols;
   long long xn_lo, act_lo;  // element offsets of the lo planes
 };
@@ -114,6 +116,7 @@ WsLayout layout(const b200_model& m, int T) {
   L.q = take(size_t(T) * std::max(m.attn_o_in(), 8) * 2);
   L.k = take(kvb);
   L.v = take(kvb);
+  L.prep = take(m.has_gdn() ? size_t(sdb_gdn_prep_floats(c.gdn_heads, T)) * 4 : 16);
   L.total = off;
   return L;
 }
@@ -231,6 +234,7 @@ extern "C" int b200_model_forward(b200_model* m, const int32_t* ids, const b200_
   uint16_t* qb = reinterpret_cast<uint16_t*>(ws + L.q);
   uint16_t* kb = reinterpret_cast<uint16_t*>(ws + L.k);
   uint16_t* vb = reinterpret_cast<uint16_t*>(ws + L.v);
+  float* prep = reinterpret_cast<float*>(ws + L.prep);
   const uint16_t* xn_lo = xn + L.xn_lo;
 
   int rc;
@@ -243,7 +247,7 @@ extern "C" int b200_model_forward(b200_model* m, const int32_t* ids, const b200_
       const int n = m->gdn_in_cols();
       b200_linear_out o{B200_EP_STORE, n, mix, n, 0};
       if ((rc = b200_linear(xn, xn_lo, T, c.hidden, c.hidden, &w.mix_in, &o, stream))) return rc;
-      if ((rc = sdb_gdn_mixer(&w.gdn, seqs, mix, n, act, L.act_lo, pool, m->kind_index[li], st))) return rc;
+      if ((rc = sdb_gdn_mixer(&w.gdn, seqs, mix, n, act, L.act_lo, pool, m->kind_index[li], prep, st))) return rc;
       mix_in_dim = m->value_dim();
     } else {
       const int n = m->attn_qkv();

@@ -233,8 +233,9 @@ def test_gdn_mixer_matches_oracle_chunk_rule():
     cu_d = torch.tensor(cu, dtype=torch.int32, device="cuda")
     seqs = _lib.Seqs(len(lens), Ttot, max(lens), _lib.ptr(cu_d), None, None)
     mix_d = mix.cuda()
+    scratch = torch.empty(_lib.load().b200_gdn_scratch_floats(H, Ttot), device="cuda")
     _lib.call("b200_gdn_mixer", _ref(p), _ref(seqs), _lib.ptr(mix_d), mix.shape[1], _lib.ptr(out),
-              Ttot * vdim, None, 0, _lib.stream_ptr())
+              Ttot * vdim, None, 0, _lib.ptr(scratch), _lib.stream_ptr())
     torch.cuda.synchronize()
     got = out[0].float().cpu() + out[1].float().cpu()
     for i, n in enumerate(lens):
