@@ -1,6 +1,7 @@
 """Decisions/s of the batched scoring prefill on B200 (the hybrid-2B NVFP4 workload).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload nvfp4|prefix|ternary-batch|latency]
 
 Workload (one GPU): the 2B-shape hybrid decider (hidden 2048, 24 layers at 3:1
 GDN:attention, GDN 16 heads x 128, attention 8q/2kv x 256, FFN 6144, vocab 248320 tied)
@@ -10,13 +11,19 @@ with NVFP4 weights; 1024 requests of 512 uniform-random tokens, each with 3 ques
 into a pool slot, then all question suffixes are forwarded against their slots and decided
 by the fused head. Data are synthetic (seeded), weights random-init.
 
-Under torchrun (N > 1) every rank takes its own requests (weak scaling, no collective in the
-forward) and the per-step answer records are all-gathered over NCCL.
+Other workloads: `prefix` (512 requests with states of U[64, 2048] tokens, 32 questions of
+48 tokens, 2-5 options), `ternary-batch` (4096 single-question 96-token requests as full
+prompts, ternary weights) and `latency` (p50 / p99 of one 96-token request, CUDA-graphed).
+
+Steps replay one CUDA graph per batch. Under torchrun (N > 1) the requests are sharded
+longest-processing-time first (weak scaling, no collective in the forward) and every step's
+answer records are all-gathered over NCCL.
 """
 
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -93,19 +100,9 @@ class ClockSampler:
 # ----------------------------------------------------------------------------- CPU baseline
 
 
-def cpu_baseline(spec: config.ModelSpec, n_requests: int = 1) -> dict:
-    """The CPU oracle (a restatement of the reference's torso and readout) on a bounded
-    sample of the same workload: n_requests requests through the prefix-cache path,
-    fp32, all host threads. Weights are fp32 tensors of the same shapes (the per-token
-    arithmetic does not depend on their values)."""
-    from oracle import head as OH
-    from oracle import synth as osynth
-    from oracle import torso as OT
+def _oracle_weights(spec: config.ModelSpec) -> dict:
     from strands_decider_b200 import synth
 
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    cfg = osynth.torso_config(spec)
     W = {"embed": synth.embedding(spec, 0).float(), "final_norm": synth.final_norm(spec, 0), "layers": []}
     for li in range(spec.n_layers):
         lat = {n.split(".", 2)[2].rsplit(".", 1)[0]: t for n, t in synth.linear_latents(spec, li, 0)}
@@ -123,21 +120,49 @@ def cpu_baseline(spec: config.ModelSpec, n_requests: int = 1) -> dict:
                          "o": lat["self_attn.o_proj"], "q_norm": sp["self_attn.q_norm.weight"],
                          "k_norm": sp["self_attn.k_norm.weight"]}
         W["layers"].append(L)
-    reqs = synth.request_batch(config.HYBRID_2B_WORKLOAD, spec.vocab, 0, n_requests)
+    return W
+
+
+def cpu_baseline(spec: config.ModelSpec, wl: config.Workload, n_requests: int = 1, n_questions: int | None = None,
+                 full_prompt: bool = False) -> dict:
+    """The CPU oracle (a restatement of the reference's torso and readout) on a bounded
+    sample of the same workload: the first n_requests requests (their first n_questions
+    questions) through the prefix-cache path (state once, then each question against the
+    state's cache) or, with full_prompt, each question as one full prompt; fp32 on all
+    host threads. Weights are fp32 tensors of the same shapes (the per-token arithmetic
+    does not depend on their values)."""
+    from oracle import head as OH
+    from oracle import synth as osynth
+    from oracle import torso as OT
+    from strands_decider_b200 import synth
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    cfg = osynth.torso_config(spec)
+    W = _oracle_weights(spec)
+    reqs = synth.request_batch(wl, spec.vocab, 0, n_requests)
     decisions = 0
+    tokens = 0
     t0 = time.perf_counter()
     with torch.inference_mode():
         for r in reqs:
-            _, cache = OT.forward_sequence(cfg, W, torch.tensor(r["state"]), keep_cache=True)
-            for qi, q in enumerate(r["questions"]):
-                hid, _ = OT.forward_sequence(cfg, W, torch.tensor(q), cache=cache)
+            qs = r["questions"][: n_questions or len(r["questions"])]
+            cache = None
+            if not full_prompt:
+                _, cache = OT.forward_sequence(cfg, W, torch.tensor(r["state"]), keep_cache=True)
+                tokens += len(r["state"])
+            for qi, q in enumerate(qs):
+                ids = q if cache is not None else r["state"] + q
+                hid, _ = OT.forward_sequence(cfg, W, torch.tensor(ids), cache=cache)
+                tokens += len(ids)
                 n = r["n_opts"][qi]
                 OH.decide(hid[-1:], W["embed"], torch.tensor([r["opt_ids"][qi]]), torch.tensor([n]),
                           torch.tensor([1.0]))
                 decisions += 1
     dt = time.perf_counter() - t0
+    path = "full prompts" if full_prompt else "prefix-cache path"
     return {"value": decisions / dt, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{n_requests} request(s) x (512-token state + 3 x 32-token questions), prefix-cache path, "
+            "sample": f"{n_requests} request(s) of {wl.name}, {decisions} decisions, {tokens} tokens, {path}, "
                       f"fp32 torch on {cores} threads, {dt:.1f} s"}
 
 
@@ -145,57 +170,106 @@ def cpu_baseline(spec: config.ModelSpec, n_requests: int = 1) -> dict:
 
 
 def launches_per_forward(spec: config.ModelSpec, decide: bool) -> int:
+    """Kernels one b200_model_forward launches (embed, per layer: 2 norms, 4 GEMMs and the
+    mixer's kernels, then the head)."""
     n = 1 + (1 if decide else 0)
     for lt in spec.layer_types:
-        n += 2 + 4 + (1 if lt == config.GDN else 2)
+        n += 2 + 4 + 2  # GDN: prep + chunk kernel; attention: prep + flash kernel
     return n
 
 
 class Batch:
-    """One step's inputs, resident on the device (or in pinned host memory for e2e)."""
+    """One step's inputs, resident on the device (or in pinned host memory for e2e).
 
-    def __init__(self, reqs: list[dict], device, pinned: bool = False):
+    Prefix-cache form: every state is forwarded once into its pool slot, then every question
+    suffix against its state's slot. Full-prompt form (prefix=False): each question is
+    forwarded as state + question in one sequence."""
+
+    def __init__(self, reqs: list[dict], device, pinned: bool = False, kmax: int = 3, prefix: bool = True):
         flat_s, cu_s, flat_q, cu_q = [], [0], [], [0]
-        slots, qslots, opt, nopt, kinds = [], [], [], [], []
+        slots, qslots, opt, nopt, kinds, qids = [], [], [], [], [], []
         for i, r in enumerate(reqs):
-            flat_s += r["state"]
-            cu_s.append(len(flat_s))
-            slots.append(i)
+            if prefix:
+                flat_s += r["state"]
+                cu_s.append(len(flat_s))
+                slots.append(i)
             for qi, q in enumerate(r["questions"]):
-                flat_q += q
+                flat_q += q if prefix else r["state"] + q
                 cu_q.append(len(flat_q))
                 qslots.append(i)
-                opt.append(r["opt_ids"][qi] + [0] * (3 - len(r["opt_ids"][qi])))
+                opt.append(r["opt_ids"][qi] + [0] * (kmax - len(r["opt_ids"][qi])))
                 nopt.append(r["n_opts"][qi])
                 kinds.append(r["kinds"][qi])
+                qids.append(r["id"] * len(r["questions"]) + qi)
+        self.prefix = prefix
         self.n_state_tokens, self.n_suffix_tokens = len(flat_s), len(flat_q)
-        self.max_state, self.max_q = max(map(len, (r["state"] for r in reqs))), max(
-            len(q) for r in reqs for q in r["questions"])
+        self.max_state = max(len(r["state"]) for r in reqs) if prefix else 0
+        self.max_q = max(cu_q[j + 1] - cu_q[j] for j in range(len(cu_q) - 1))
         I = torch.int32
-        host = {
-            "s_ids": torch.tensor(flat_s, dtype=I), "s_cu": torch.tensor(cu_s, dtype=I),
-            "s_slot": torch.tensor(slots, dtype=I), "slot_kv": torch.tensor(cu_s[:-1], dtype=I),
-            "q_ids": torch.tensor(flat_q, dtype=I), "q_cu": torch.tensor(cu_q, dtype=I),
-            "q_slot": torch.tensor(qslots, dtype=I), "last_tok": torch.tensor([c - 1 for c in cu_q[1:]], dtype=I),
-            "opt_ids": torch.tensor(opt, dtype=I), "n_opts": torch.tensor(nopt, dtype=I),
-            "kinds": torch.tensor(kinds, dtype=I), "temps": torch.ones(len(nopt), dtype=torch.float32)}
+        host = {"q_ids": torch.tensor(flat_q, dtype=I), "q_cu": torch.tensor(cu_q, dtype=I),
+                "last_tok": torch.tensor([c - 1 for c in cu_q[1:]], dtype=I),
+                "opt_ids": torch.tensor(opt, dtype=I), "n_opts": torch.tensor(nopt, dtype=I),
+                "kinds": torch.tensor(kinds, dtype=I), "temps": torch.ones(len(nopt), dtype=torch.float32),
+                "qid": torch.tensor(qids, dtype=I)}
+        if prefix:
+            host.update({"s_ids": torch.tensor(flat_s, dtype=I), "s_cu": torch.tensor(cu_s, dtype=I),
+                         "s_slot": torch.tensor(slots, dtype=I), "slot_kv": torch.tensor(cu_s[:-1], dtype=I),
+                         "q_slot": torch.tensor(qslots, dtype=I)})
         self.h2d_bytes = sum(t.numel() * t.element_size() for t in host.values())
         if pinned:
             self.host = {k: v.pin_memory() for k, v in host.items()}
             self.dev = {k: torch.empty_like(v, device=device) for k, v in host.items()}
+            for k in host:
+                self.dev[k].copy_(self.host[k])
         else:
             self.host = None
             self.dev = {k: v.to(device) for k, v in host.items()}
         self.n_decisions = len(nopt)
+        self.tokens = self.n_state_tokens + self.n_suffix_tokens
+
+    def upload(self) -> None:
+        """The step's host-to-device copies (pinned host memory, current stream)."""
+        for k, v in self.host.items():
+            self.dev[k].copy_(v, non_blocking=True)
 
 
 def run_step(model, b: Batch, stream) -> object:
+    """One pass of the hot path over one batch, ending in the fused decision head."""
     d = b.dev
-    model.slot_kv[: d["slot_kv"].numel()].copy_(d["slot_kv"], non_blocking=True)
-    model.forward(d["s_ids"], d["s_cu"], save_slot=d["s_slot"], max_len=b.max_state, stream=stream)
     dec = {"last_tok": d["last_tok"], "opt_ids": d["opt_ids"], "n_opts": d["n_opts"], "kinds": d["kinds"],
            "temps": d["temps"]}
+    if not b.prefix:
+        return model.forward(d["q_ids"], d["q_cu"], decide=dec, max_len=b.max_q, stream=stream)
+    model.slot_kv[: d["slot_kv"].numel()].copy_(d["slot_kv"], non_blocking=True)
+    model.forward(d["s_ids"], d["s_cu"], save_slot=d["s_slot"], max_len=b.max_state, stream=stream)
     return model.forward(d["q_ids"], d["q_cu"], prefix_slot=d["q_slot"], decide=dec, max_len=b.max_q, stream=stream)
+
+
+class StepGraph:
+    """run_step for one batch captured as a CUDA graph: the ~200-400 launches of the
+    native layer loop replay as one graph launch on the batch's device inputs."""
+
+    def __init__(self, model, b: Batch):
+        self.b = b
+        self.g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            run_step(model, b, s)          # one eager pass outside the capture
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(self.g):
+            self.out = run_step(model, b, torch.cuda.current_stream())
+
+    def replay(self):
+        self.g.replay()
+        return self.out
+
+
+def records(dec, b: Batch):
+    from strands_decider_b200 import dispatch
+
+    return dispatch.AnswerRecords.pack(b.dev["qid"], dec.argmax, dec.confidence, dec.score, dec.probs)
 
 
 def gemm_roofline(model, tokens: int, pk: dict, reps: int = 20) -> dict:
@@ -246,26 +320,123 @@ def gemm_roofline(model, tokens: int, pk: dict, reps: int = 20) -> dict:
             "peak_src": pk["src"] + " bf16 burst (tcgen05 kind::f16)"}
 
 
+WORKLOADS = {
+    "nvfp4": (config.HYBRID_2B, config.HYBRID_2B_WORKLOAD, 128, True),
+    "prefix": (config.HYBRID_2B, config.PREFIX_CACHE_WORKLOAD, 32, True),
+    "ternary-batch": (config.HYBRID_2B.with_format("ternary"),
+                      dataclasses.replace(config.LATENCY_WORKLOAD, name="hybrid-2b-ternary-4096x96", n_requests=4096),
+                      1024, False),
+}
+
+
+def _kmax(wl: config.Workload) -> int:
+    return wl.option_range[1] if wl.option_range else max(wl.options)
+
+
+def latency(args) -> None:
+    """p50 / p99 single-request latency: one 96-token request (93-token state + 3-token
+    question, one 3-way choice) as one full-prompt forward of the ternary 2B-shape decider,
+    CUDA-graphed, each replay timed alone with CUDA events (inputs resident; e2e adds the
+    96 ids' upload and the answer's download to every replay)."""
+    from strands_decider_b200 import _lib
+    from strands_decider_b200.runtime import DecisionModel
+    from strands_decider_b200.synth import request_batch
+    from strands_decider_b200.weights import DeviceWeights
+
+    spec, wl = config.HYBRID_2B.with_format("ternary"), config.LATENCY_WORKLOAD
+    torch.cuda.set_device(0)
+    weights = DeviceWeights.synthetic(spec, seed=0, device="cuda", latent_device="cuda")
+    model = DecisionModel(weights, max_tokens=128, pool_slots=1, pool_kv_tokens=128)
+    reqs = request_batch(wl, spec.vocab, 0, 1)
+    reqs[0]["id"] = 0
+    b = Batch(reqs, "cuda", pinned=True, kmax=3, prefix=False)
+    g = StepGraph(model, b)
+    runs = max(args.steps, 1000)
+    for _ in range(max(args.warmup, 20)):
+        g.replay()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(runs)]
+    clocks = ClockSampler(0)
+    clocks.start()
+    for e0, e1 in ev:
+        e0.record(st)
+        g.replay()
+        e1.record(st)
+    torch.cuda.synchronize()
+    ms = sorted(e0.elapsed_time(e1) for e0, e1 in ev)
+    out_host = torch.empty(b.n_decisions, 3, pin_memory=True)
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(runs)]
+    for e0, e1 in ev2:
+        e0.record(st)
+        b.upload()
+        dec = g.replay()
+        out_host.copy_(dec.probs, non_blocking=True)
+        e1.record(st)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms2 = sorted(e0.elapsed_time(e1) for e0, e1 in ev2)
+    assert _lib.read_fault() == 0
+
+    def pct(v, q):
+        return v[min(len(v) - 1, int(q * len(v)))]
+
+    cb = cpu_baseline(spec, wl, 1, full_prompt=True) if args.cpu_sample > 0 else None
+    line = {"metric": METRIC, "value": round(pct(ms, 0.5), 4), "unit": "ms", "n_gpus": 1, "steps": runs,
+            "warmup": max(args.warmup, 20), "ms_per_step": round(statistics.mean(ms), 4),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": wl.name, "model": spec.name, "weights": "ternary", "tokens": b.tokens,
+                       "path": "full prompt, one CUDA graph per request",
+                       "l2": "weights (0.34 GB ternary + 1 GB embedding) exceed L2; no flush between replays"},
+            "latency_ms": {"p50": round(pct(ms, 0.5), 4), "p99": round(pct(ms, 0.99), 4),
+                           "min": round(ms[0], 4), "runs": runs},
+            "e2e": {"value": round(pct(ms2, 0.5), 4), "unit": "ms", "p99": round(pct(ms2, 0.99), 4),
+                    "h2d_bytes_per_step": b.h2d_bytes, "d2h_bytes_per_step": out_host.numel() * 4},
+            "gpu_launches": runs * launches_per_forward(spec, True), "clocks": clk, "cpu_baseline": cb}
+    if cb:
+        cb["ms_per_request"] = round(1e3 / cb["value"], 1)
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--requests-per-step", type=int, default=128)
-    ap.add_argument("--cpu-sample", type=int, default=1, help="requests in the CPU baseline sample (0 = skip)")
+    ap.add_argument("--workload", default="nvfp4", choices=sorted(WORKLOADS) + ["latency"])
+    ap.add_argument("--requests-per-step", type=int, default=0, help="0 = the workload's default")
+    ap.add_argument("--cpu-sample", type=int, default=3, help="requests in the CPU baseline sample (0 = skip)")
+    ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    spec = config.HYBRID_2B
-    wl = config.HYBRID_2B_WORKLOAD
+    if args.workload == "latency":
+        if args.impl == "reference":
+            if rank == 0:
+                spec, wl = config.HYBRID_2B.with_format("ternary"), config.LATENCY_WORKLOAD
+                cb = cpu_baseline(spec, wl, 1, full_prompt=True)
+                ms = 1e3 / cb["value"]
+                print(json.dumps({"metric": METRIC, "value": round(ms, 2), "unit": "ms", "impl": "reference",
+                                  "higher_is_better": False, "config": {"workload": wl.name, "model": spec.name},
+                                  "cpu_baseline": cb, "e2e": {"value": round(ms, 2), "unit": "ms",
+                                                              "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+            return
+        if rank == 0:
+            latency(args)
+        return
+    spec, wl, r_default, prefix = WORKLOADS[args.workload]
+    R = args.requests_per_step or r_default
+    kmax = _kmax(wl)
 
     if args.impl == "reference":
         if rank != 0:
             return
-        cb = cpu_baseline(spec, max(args.cpu_sample, 1))
+        n_q = None if wl.n_questions <= 3 else 4
+        cb = cpu_baseline(spec, wl, max(args.cpu_sample, 1), n_questions=n_q, full_prompt=not prefix)
         line = {"metric": METRIC, "value": round(cb["value"], 4), "unit": UNIT, "impl": "reference",
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -277,7 +448,7 @@ def main() -> None:
 
     import torch.distributed as dist
 
-    from strands_decider_b200 import _lib
+    from strands_decider_b200 import _lib, dispatch
     from strands_decider_b200.runtime import DecisionModel
     from strands_decider_b200.synth import request_batch
     from strands_decider_b200.weights import DeviceWeights
@@ -287,34 +458,41 @@ def main() -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    R = args.requests_per_step
+
+    # every rank holds the whole workload's request list and plans the same LPT shards;
+    # rank r forwards shards[r] in batches of R requests (weak scaling: each rank's share
+    # is the full single-GPU workload, so N GPUs answer N times the questions)
+    n_total = wl.n_requests * world
+    need = (args.steps + args.warmup) * R
+    reqs_all = request_batch(wl, spec.vocab, 0, min(n_total, need * world))
+    for i, r in enumerate(reqs_all):
+        r["id"] = i
+    shards = dispatch.plan_shards([dispatch.request_cost(r) for r in reqs_all], world)
+    mine = [reqs_all[i] for i in shards[rank]]
+    n_batches = max(1, min(len(mine) // R, args.steps + args.warmup))
+    batches = [Batch(mine[j * R:(j + 1) * R], "cuda", pinned=True, kmax=kmax, prefix=prefix)
+               for j in range(n_batches)]
+    max_tok = max(max(b.n_state_tokens, b.n_suffix_tokens) for b in batches)
+    slots = R if prefix else 1
+    kv = max(b.n_state_tokens for b in batches) if prefix else 1
     weights = DeviceWeights.synthetic(spec, seed=0, device="cuda", latent_device="cuda")
-    model = DecisionModel(weights, max_tokens=R * wl.state_len[1], pool_slots=R, pool_kv_tokens=R * wl.state_len[1])
-    # this rank's share of the workload (uniform lengths: round robin), cycled per step
-    mine = list(range(rank, wl.n_requests, world))
-    n_batches = max(1, len(mine) // R)
-    batches, hbatches = [], []
-    for b in range(min(n_batches, args.steps + args.warmup)):
-        ids = mine[b * R:(b + 1) * R]
-        reqs = [request_batch(wl, spec.vocab, i, 1)[0] for i in ids]
-        batches.append(Batch(reqs, "cuda"))
-        hbatches.append(Batch(reqs, "cuda", pinned=True))
+    model = DecisionModel(weights, max_tokens=max_tok, pool_slots=slots, pool_kv_tokens=max(kv, 1))
     stream = torch.cuda.current_stream()
-    gather_buf = None
+    use_graph = not args.no_graph
+    graphs = [StepGraph(model, b) for b in batches] if use_graph else None
 
-    def gather(dec, n):
-        nonlocal gather_buf
-        if world == 1:
-            return
-        rec = torch.cat([dec.probs, dec.argmax.float()[:, None], dec.confidence[:, None], dec.score[:, None]], 1)
-        if gather_buf is None or gather_buf.shape[1:] != rec.shape:
-            gather_buf = torch.empty(world, *rec.shape, device="cuda")
-        dist.all_gather_into_tensor(gather_buf, rec.contiguous())
+    def step(i, upload=False):
+        j = i % len(batches)
+        b = batches[j]
+        if upload:
+            b.upload()
+        dec = graphs[j].replay() if use_graph else run_step(model, b, stream)
+        rec = records(dec, b)
+        out = dispatch.gather_answers(rec) if world > 1 else rec.rows
+        return b, out
 
-    # warm-up
     for i in range(args.warmup):
-        dec = run_step(model, batches[i % len(batches)], stream)
-        gather(dec, batches[i % len(batches)].n_decisions)
+        step(i)
     torch.cuda.synchronize()
     assert _lib.read_fault() == 0
 
@@ -327,52 +505,49 @@ def main() -> None:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     decisions = 0
+    tokens = 0
     for i in range(args.steps):
-        b = batches[(args.warmup + i) % len(batches)]
-        dec = run_step(model, b, stream)
-        gather(dec, b.n_decisions)
+        b, _ = step(args.warmup + i)
         decisions += b.n_decisions
+        tokens += b.tokens
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    clk = clocks.stop()
 
-    # e2e: through the public path with pinned host inputs, H2D + D2H every step
+    # e2e: host inputs uploaded and the gathered answers read back every step
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    out_host = None
     d2h = 0
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
+    h2d = 0
     for i in range(args.steps):
-        b = hbatches[(args.warmup + i) % len(hbatches)]
-        for k, v in b.host.items():
-            b.dev[k].copy_(v, non_blocking=True)
-        dec = run_step(model, b, stream)
-        gather(dec, b.n_decisions)
-        res = torch.cat([dec.probs, dec.argmax.float()[:, None], dec.confidence[:, None], dec.score[:, None]], 1)
-        if out_host is None:
-            out_host = torch.empty(res.shape, dtype=res.dtype, pin_memory=True)
-        out_host.copy_(res, non_blocking=True)
-        d2h = res.numel() * 4
+        b, out = step(args.warmup + i, upload=True)
+        host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        host.copy_(out, non_blocking=True)
+        d2h += out.numel() * 4
+        h2d += b.h2d_bytes
     f1.record(stream)
     torch.cuda.synchronize()
     ms_e2e = f0.elapsed_time(f1)
+    clk = clocks.stop()
 
-    t = torch.tensor([ms, ms_e2e, float(decisions)], device="cuda")
+    t = torch.tensor([ms, ms_e2e, float(decisions), float(tokens)], device="cuda")
     if world > 1:
         g = [torch.zeros_like(t) for _ in range(world)]
         dist.all_gather(g, t)
         ms = max(float(x[0]) for x in g)
         ms_e2e = max(float(x[1]) for x in g)
         total = sum(float(x[2]) for x in g)
+        total_tok = sum(float(x[3]) for x in g)
     else:
-        total = float(decisions)
+        total, total_tok = float(decisions), float(tokens)
     value = total / (ms * 1e-3)
     e2e = total / (ms_e2e * 1e-3)
     pk = peaks()
-    roof = gemm_roofline(model, R * wl.state_len[1], pk) if rank == 0 else None
+    del graphs
+    roof = gemm_roofline(model, batches[0].n_state_tokens or batches[0].n_suffix_tokens, pk) if rank == 0 else None
     assert _lib.read_fault() == 0
     if world > 1:
         dist.barrier()
@@ -383,19 +558,26 @@ def main() -> None:
     if world == 1 and args.cpu_sample > 0:
         del model, weights
         torch.cuda.empty_cache()
-        cb = cpu_baseline(spec, args.cpu_sample)
+        n_q = None if wl.n_questions <= 3 else 4
+        cb = cpu_baseline(spec, wl, args.cpu_sample, n_questions=n_q, full_prompt=not prefix)
     b0 = batches[0]
+    fl = 2.0 * spec.linear_params() * total_tok
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": wl.name, "model": spec.name, "weights": spec.weight_format,
                    "requests_per_step": R, "decisions_per_step": b0.n_decisions,
-                   "tokens_per_step": b0.n_state_tokens + b0.n_suffix_tokens, "question_tokens": wl.question_len,
+                   "tokens_per_step": b0.tokens, "question_tokens": wl.question_len,
+                   "path": "prefix cache (state once, questions against its pool slot)" if prefix else "full prompts",
+                   "cuda_graphs": use_graph,
                    "l2": "inputs larger than L2 (0.8 GB weights + GBs of activations per step)",
-                   "parallelism": f"dp{world} (requests sharded, answers all-gathered)"},
-        "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": b0.h2d_bytes, "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps * (launches_per_forward(spec, False) + launches_per_forward(spec, True)),
+                   "parallelism": f"dp{world} (requests LPT-sharded, answers all-gathered over NCCL)"},
+        "linear_tflops": round(fl / (ms * 1e-3) / 1e12 / world, 1),
+        "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
+                "d2h_bytes_per_step": d2h // args.steps},
+        "gpu_launches": args.steps * ((launches_per_forward(spec, False) if prefix else 0)
+                                      + launches_per_forward(spec, True)),
         "roofline": roof, "clocks": clk, "cpu_baseline": cb,
     }
     print(json.dumps(line), flush=True)

@@ -166,11 +166,20 @@ class Workload:
     state_len: tuple[int, int]        # inclusive range; (L, L) for fixed length
     n_questions: int
     question_len: int
-    options: tuple[int, ...] = field(default=(3, 2, 3))  # per question kind cycle, or range
+    options: tuple[int, ...] = field(default=(3, 2, 3))  # option count per question, cycled with kinds
     kinds: tuple[int, ...] = (1, 0, 2)                    # choice, noul, score
     seed: int = 0
+    option_range: tuple[int, int] | None = None          # if set, option counts ~ U{lo..hi}, all choice
 
 
 # 1024 prompts of 512 uniform-random tokens, 3 questions each (3-way choice, yes/no noul,
 # 3-level score), each question a 32-token suffix ending at the decision position.
 HYBRID_2B_WORKLOAD = Workload("hybrid-2b-nvfp4-1024x512x3", 1024, (512, 512), 3, 32)
+
+# 512 requests with shared states of U[64, 2048] tokens, 32 questions of 48 tokens each,
+# scoring 2-5 single-token options.
+PREFIX_CACHE_WORKLOAD = Workload("hybrid-2b-nvfp4-prefix-512x32q", 512, (64, 2048), 32, 48, kinds=(1,),
+                                 options=(2,), option_range=(2, 5))
+
+# one request of 96 tokens with a single 3-way choice (the latency workload), and its batch
+LATENCY_WORKLOAD = Workload("hybrid-2b-ternary-1x96", 1, (93, 93), 1, 3, kinds=(1,), options=(3,))

@@ -99,8 +99,9 @@ def request_batch(w: Workload, vocab: int, first: int = 0, count: int | None = N
         for qi in range(w.n_questions):
             qs.append(torch.randint(0, vocab, (w.question_len,), generator=g).tolist())
             kinds.append(w.kinds[qi % len(w.kinds)])
-            if len(w.options) == 2 and w.options[0] < w.options[1] and w.n_questions > 3:
-                nopts.append(int(torch.randint(w.options[0], w.options[1] + 1, (1,), generator=g)))
+            if w.option_range is not None:
+                lo_o, hi_o = w.option_range
+                nopts.append(int(torch.randint(lo_o, hi_o + 1, (1,), generator=g)))
             else:
                 nopts.append(w.options[qi % len(w.options)])
         out.append({"state": state, "questions": qs, "kinds": kinds, "n_opts": nopts,
