@@ -503,6 +503,7 @@ def main() -> None:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.cudart().cudaProfilerStart()    # a profiler started with capture off records this region only
     e0.record(stream)
     decisions = 0
     tokens = 0
@@ -512,6 +513,7 @@ def main() -> None:
         tokens += b.tokens
     e1.record(stream)
     torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
     ms = e0.elapsed_time(e1)
 
     # e2e: host inputs uploaded and the gathered answers read back every step

@@ -128,6 +128,50 @@ class ModelSpec:
         assert fmt in WEIGHT_FORMATS
         return replace(self, weight_format=fmt)
 
+    @classmethod
+    def from_hf_config(cls, cfg, weight_format: str = "nvfp4", name: str | None = None,
+                       max_positions: int = 32768) -> ModelSpec:
+        """The spec of a transformers `Qwen3_5TextConfig` (the torso strands-decider loads,
+        src/strands_decider/modeling.py:293-303). Raises ValueError for shapes the kernels
+        do not take."""
+        rp = getattr(cfg, "rope_parameters", None) or {}
+        spec = cls(
+            name=name or f"qwen3_5-h{cfg.hidden_size}-l{cfg.num_hidden_layers}", vocab=cfg.vocab_size,
+            hidden=cfg.hidden_size, inter=cfg.intermediate_size, layer_types=tuple(cfg.layer_types),
+            gdn_heads=cfg.linear_num_key_heads, gdn_dk=cfg.linear_key_head_dim, gdn_dv=cfg.linear_value_head_dim,
+            conv_width=cfg.linear_conv_kernel_dim, attn_heads=cfg.num_attention_heads,
+            attn_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
+            rope_theta=float(rp.get("rope_theta", getattr(cfg, "rope_theta", 1e7))),
+            partial_rotary=float(rp.get("partial_rotary_factor", getattr(cfg, "partial_rotary_factor", 0.25))),
+            eps=cfg.rms_norm_eps, weight_format=weight_format,
+            max_positions=min(int(getattr(cfg, "max_position_embeddings", max_positions)), max_positions))
+        if cfg.linear_num_value_heads != cfg.linear_num_key_heads:
+            raise ValueError("GDN layers with different key and value head counts are not supported")
+        if not getattr(cfg, "tie_word_embeddings", True):
+            raise ValueError("the option-token head reads the tied embedding; untied checkpoints are not supported")
+        spec.validate()
+        return spec
+
+    def validate(self) -> None:
+        """The shapes the kernels take (raises ValueError otherwise)."""
+        problems = []
+        if self.gdn_dk != 128 or self.gdn_dv != 128:
+            problems.append("GDN head dims must be 128")
+        if self.head_dim not in (64, 128, 256):
+            problems.append("attention head_dim must be 64, 128 or 256")
+        if self.hidden % 128 or self.inter % 128 or self.hidden > 4096:
+            problems.append("hidden and intermediate sizes must be multiples of 128 (hidden <= 4096)")
+        if self.conv_width != 4:
+            problems.append("the depthwise conv width must be 4")
+        if self.attn_heads % self.attn_kv_heads:
+            problems.append("query heads must be a multiple of kv heads")
+        if any(t not in (GDN, ATTN) for t in self.layer_types):
+            problems.append("layer types must be linear_attention or full_attention")
+        if self.weight_format not in WEIGHT_FORMATS:
+            problems.append(f"weight format must be one of {WEIGHT_FORMATS}")
+        if problems:
+            raise ValueError("; ".join(problems))
+
 
 def hybrid_pattern(n_layers: int) -> tuple[str, ...]:
     """[GDN, GDN, GDN, attention] repeated (Qwen3.5's full_attention_interval 4)."""

@@ -147,19 +147,69 @@ class DeviceWeights:
         faster for the 2B shape (different random streams, same distributions)."""
         if latent_device is None:
             latent_device = "cpu" if spec.linear_params() < 400_000_000 else "cuda"
+
+        def layer(li):
+            return synth.linear_latents(spec, li, seed, latent_device), synth.small_params(spec, li, seed)
+
+        return cls._assemble(spec, synth.embedding(spec, seed, latent_device), synth.final_norm(spec, seed, "cpu"),
+                             layer, device, keep_logical)
+
+    @classmethod
+    def from_state_dict(cls, spec: ModelSpec, sd: dict[str, torch.Tensor], device: str = "cuda",
+                        keep_logical: bool = False) -> DeviceWeights:
+        """Quantise a Qwen3.5 text-model state dict (transformers' names, as
+        `Qwen3_5ForCausalLM(cfg).model.state_dict()` has them; the torso strands-decider loads,
+        src/strands_decider/modeling.py:293-303) into spec.weight_format on the GPU.
+
+        The linears may be fp32, bf16 or fp16; each is quantised from its fp32 value. The
+        depthwise conv weight may be [C, 1, W] (nn.Conv1d) or [C, W]. The embedding is
+        stored as bf16 (the tied output rows of the decision head read it too)."""
+        sd = {k.removeprefix("model."): v for k, v in sd.items()}
+        need = ["embed_tokens.weight", "norm.weight"]
+        for li in range(spec.n_layers):
+            need += [f"layers.{li}.{n}.weight" for n, _, _ in spec.logical_linears(li)]
+        missing = [k for k in need if k not in sd]
+        if missing:
+            raise ValueError(f"state dict lacks {len(missing)} tensors, e.g. {missing[:3]}")
+
+        def layer(li):
+            p = f"layers.{li}."
+            lin = [(f"{p}{n}.weight", sd[f"{p}{n}.weight"].float()) for n, _, _ in spec.logical_linears(li)]
+            for name, w in lin:
+                n_out, n_in = next((o, i) for n, o, i in spec.logical_linears(li) if name.endswith(n + ".weight"))
+                if tuple(w.shape) != (n_out, n_in):
+                    raise ValueError(f"{name}: shape {tuple(w.shape)} != {(n_out, n_in)}")
+            small = {}
+            for k, v in sd.items():
+                if k.startswith(p) and not any(k == nm for nm, _ in lin):
+                    v = v.float()
+                    if k.endswith("conv1d.weight") and v.dim() == 3:
+                        v = v[:, 0, :]
+                    small[k] = v
+            return iter(lin), small
+
+        return cls._assemble(spec, sd["embed_tokens.weight"].to(torch.bfloat16), sd["norm.weight"].float(), layer,
+                             device, keep_logical)
+
+    @classmethod
+    def _assemble(cls, spec: ModelSpec, embed: torch.Tensor, final_norm: torch.Tensor, layer, device: str,
+                  keep_logical: bool) -> DeviceWeights:
+        """Quantise every logical linear of every layer and build the fused layouts.
+        layer(li) -> (iterator of (full name, [out, in] tensor), {full name: small tensor})."""
         self = cls(spec)
         fmt = spec.weight_format
-        self.embed = synth.embedding(spec, seed, latent_device).to(device)
-        self.final_norm = synth.final_norm(spec, seed, "cpu").to(device)
+        self.embed = embed.to(device).contiguous()
+        self.final_norm = final_norm.to(device).contiguous()
         for li in range(spec.n_layers):
             q = {}
-            for name, w in synth.linear_latents(spec, li, seed, latent_device):
-                pw = quantize(fmt, w.to(device))
+            lin, small = layer(li)
+            for name, w in lin:
+                pw = quantize(fmt, w.to(device).contiguous())
                 del w
                 q[name.split(".", 2)[2].rsplit(".", 1)[0]] = pw   # e.g. "linear_attn.in_proj_qkv"
                 if keep_logical:
                     self.logical[name] = pw
-            sp = {k.split(".", 2)[2]: v.to(device).contiguous() for k, v in synth.small_params(spec, li, seed).items()}
+            sp = {k.split(".", 2)[2]: v.to(device).contiguous() for k, v in small.items()}
             L = {"kind": spec.layer_types[li], "input_norm": sp["input_layernorm.weight"],
                  "post_norm": sp["post_attention_layernorm.weight"],
                  "gate_up": interleave_gate_up(q["mlp.gate_proj"], q["mlp.up_proj"]),

@@ -1,0 +1,151 @@
+"""The `--device b200` engine's two overrides and the checkpoint-style weight loader, on the GPU.
+
+* `_slot_probs_batched` (infer.py:253-279) and `_slot_probs_shared_prefix` (infer.py:281-337)
+  through `B200Engine` with a word-level tokenizer (the fixture pattern of the reference's
+  tests/test_mlx_engine.py:56-67): both paths agree with each other, return the reference's
+  contract (probs [n, K] float32 with zeros past n_slots, the input-token count) and match
+  the oracle's full-prompt probabilities within 2e-3.
+* `DeviceWeights.from_state_dict` on a transformers-named state dict packs the same bytes
+  as the synthetic loader from the same latents.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORDS = ("the a of to and in is it that for on with as was at by this be are from or an policy "
+         "library book renew renewal loan due date fine days week member card return overdue "
+         "item hold request staff desk online account limit late fee paid cookbook friday "
+         "leave failed my can i what which how many should we answer question options yes no "
+         "score low mid high choose one best rate urgency team billing support sales").split()
+
+
+def _tokenizer():
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+
+    vocab = {w: i for i, w in enumerate(["<pad>", "<eos>", "<unk>", *[str(k) for k in range(1, 25)],
+                                         *sorted(set(WORDS))])}
+    tok = Tokenizer(models.WordLevel(vocab, unk_token="<unk>"))
+    tok.pre_tokenizer = pre_tokenizers.Whitespace()
+    return PreTrainedTokenizerFast(tokenizer_object=tok, pad_token="<pad>", eos_token="<eos>", unk_token="<unk>")
+
+
+def _text(g: torch.Generator, n: int) -> str:
+    return " ".join(WORDS[int(i)] for i in torch.randint(0, len(WORDS), (n,), generator=g))
+
+
+def _engine(max_length=256):
+    from strands_decider_b200 import config
+    from strands_decider_b200.engine import B200Engine, DeciderConfig, EngineConfig
+    from strands_decider_b200.runtime import DecisionModel
+    from strands_decider_b200.weights import DeviceWeights
+
+    spec = config.TINY
+    w = DeviceWeights.synthetic(spec, seed=3, latent_device="cpu")
+    rt = DecisionModel(w, max_tokens=2048, pool_slots=2, pool_kv_tokens=512)
+    tok = _tokenizer()
+    eng = B200Engine(rt, tok, DeciderConfig(max_length=max_length, temperature_by_kind={"score": 1.5}),
+                     EngineConfig(max_batch=8))
+    return spec, eng, tok
+
+
+def _oracle_probs(spec, rows, opt_rows, n_slots, temps):
+    from oracle import head as OH
+    from oracle import synth as osynth
+    from oracle import torso as OT
+
+    W = osynth.logical_weights(spec, seed=3)
+    cfg = osynth.torso_config(spec)
+    pooled = torch.stack([OT.forward_sequence(cfg, W, torch.tensor(r))[0][-1] for r in rows])
+    K = max(n_slots)
+    opt = torch.tensor([o + [0] * (K - len(o)) for o in opt_rows])
+    return OH.decide(pooled, W["embed"], opt, torch.tensor(n_slots), torch.tensor(temps))
+
+
+def test_engine_batched_and_shared_prefix_paths_match_each_other_and_the_oracle():
+    spec, eng, tok = _engine()
+    g = torch.Generator().manual_seed(0)
+    state = _text(g, 60)
+    questions = [_text(g, 9), _text(g, 14), _text(g, 5)]
+    n_slots, kinds = [3, 2, 5], ["choice", "noul", "score"]
+    pb, nb = eng._slot_probs_batched(state, questions, n_slots, kinds)
+    pp, npfx = eng._slot_probs_shared_prefix(state, questions, n_slots, kinds)
+    assert pb.dtype == torch.float32 and pb.shape == (3, 5) and pb.device.type == "cpu"
+    for i, n in enumerate(n_slots):
+        assert torch.all(pb[i, n:] == 0) and torch.all(pp[i, n:] == 0)
+        assert abs(float(pb[i, :n].sum()) - 1.0) < 1e-5
+    assert (pb - pp).abs().max().item() < 2e-4
+    s, q = eng._fit(state, questions)
+    assert nb == sum(len(s) + len(x) for x in q) and npfx == len(s) + sum(len(x) for x in q)
+    rows = [s + x for x in q]
+    opt_rows = eng._option_rows(n_slots)
+    assert opt_rows[2] == [tok.convert_tokens_to_ids(str(k)) for k in range(1, 6)]
+    want = _oracle_probs(spec, rows, opt_rows, n_slots, [1.0, 1.0, 1.5])
+    assert (pb - want).abs().max().item() < 2e-3
+    assert torch.equal(pb.argmax(1), want.argmax(1))
+
+
+def test_engine_front_truncates_long_questions_like_the_reference():
+    spec, eng, tok = _engine(max_length=40)
+    g = torch.Generator().manual_seed(1)
+    state, questions = _text(g, 80), [_text(g, 50), _text(g, 6)]
+    s, q = eng._fit(state, questions)
+    reserve = min(50, max(1, int(40 * 0.75)))
+    assert len(q[0]) == reserve and len(q[1]) == 6 and len(s) <= 40 - reserve
+    full = tok(questions[0], add_special_tokens=False)["input_ids"]
+    assert q[0] == full[-reserve:]
+    p, _ = eng._slot_probs_shared_prefix(state, questions, [4, 2], ["choice", "noul"])
+    assert p.shape == (2, 4)
+
+
+def test_engine_rejects_more_options_than_single_token_numbers():
+    spec, eng, tok = _engine()
+    with pytest.raises(ValueError):
+        eng._slot_probs_batched("the policy", ["which one"], [30], ["choice"])
+
+
+def test_state_dict_loader_packs_the_same_bytes_as_the_synthetic_loader():
+    from strands_decider_b200 import config, synth
+    from strands_decider_b200.weights import DeviceWeights
+
+    for fmt in ("int4", "nvfp4", "ternary"):
+        spec = config.TINY.with_format(fmt)
+        a = DeviceWeights.synthetic(spec, seed=5, latent_device="cpu")
+        sd = {"model.embed_tokens.weight": synth.embedding(spec, 5).float(),
+              "model.norm.weight": synth.final_norm(spec, 5)}
+        for li in range(spec.n_layers):
+            for name, t in synth.linear_latents(spec, li, 5, "cpu"):
+                sd["model." + name] = t
+            for k, v in synth.small_params(spec, li, 5).items():
+                sd["model." + k] = v[:, None, :] if k.endswith("conv1d.weight") else v   # nn.Conv1d shape
+        b = DeviceWeights.from_state_dict(spec, sd)
+        assert torch.equal(a.embed, b.embed) and torch.equal(a.final_norm, b.final_norm)
+        for la, lb in zip(a.layers, b.layers, strict=True):
+            for key in ("mix_in", "mix_out", "down", "gate_up"):
+                for (na, ta), (nb_, tb) in zip(la[key].parts(), lb[key].parts(), strict=True):
+                    assert na == nb_ and torch.equal(ta, tb), (fmt, key, na)
+            for key in la:
+                if isinstance(la[key], torch.Tensor):
+                    assert torch.equal(la[key], lb[key]), key
+
+
+def test_state_dict_loader_rejects_missing_and_misshapen_tensors():
+    from strands_decider_b200 import config
+    from strands_decider_b200.weights import DeviceWeights
+
+    spec = config.TINY
+    with pytest.raises(ValueError, match="lacks"):
+        DeviceWeights.from_state_dict(spec, {"embed_tokens.weight": torch.zeros(spec.vocab, spec.hidden)})
+    from strands_decider_b200 import synth
+
+    sd = {"embed_tokens.weight": synth.embedding(spec, 0).float(), "norm.weight": synth.final_norm(spec, 0)}
+    for li in range(spec.n_layers):
+        sd.update({n: t for n, t in synth.linear_latents(spec, li, 0, "cpu")})
+        sd.update(synth.small_params(spec, li, 0))
+    sd["layers.0.mlp.down_proj.weight"] = sd["layers.0.mlp.down_proj.weight"][:, :-128]
+    with pytest.raises(ValueError, match="shape"):
+        DeviceWeights.from_state_dict(spec, sd)
