@@ -25,6 +25,7 @@ enum FaultSite : unsigned int {
   FAULT_GEMM_WAIT_FULL_B = 1u << 2,
   FAULT_GEMM_WAIT_ACCUM = 1u << 3,
   FAULT_GEMM_WAIT_FULL_W = 1u << 4,
+  FAULT_GDN_WAIT_STAGE = 1u << 5,
   FAULT_BAD_INDEX = 1u << 8,
 };
 

@@ -1,7 +1,7 @@
 // Gated-DeltaNet token mixer (after the in-projection GEMM) on tensor cores.
 //
 // Two kernels, restating TF:234-311 with TF:462-530 fused around it.
-// gdn_prep_kernel, one warp per (token, head), fully parallel:
+// gdn_prep_kernel, one warp per (head, 8 consecutive tokens), fully parallel:
 //   causal depthwise conv (width 4) + SiLU over the head's q, k, v channels (the 3 previous
 //   raw inputs come from the sequence itself or the prefix slot's history), l2norm(q) *
 //   dk^-1/2, l2norm(k), beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias); a sequence
@@ -36,9 +36,11 @@ struct GdnArgs {
   const int32_t* prefix_slot;
   const int32_t* save_slot;
   int n_seqs;
+  int n_tokens;
   const float* mix;      // [T, ld_mix]: q | k | v | z | b | a
   int ld_mix;
-  float* prep;           // [T][heads][GPREP]: q (128) | k (128) | v (128) | beta | g  (fp32)
+  float* prep;           // [heads][T][GPREP]: q (128) | k (128) | v (128) | beta | g  (fp32); a chunk of
+                         // one head is one contiguous run of GC records (GPREP * 4 = 1552 bytes each)
   uint16_t* out;         // hi plane [T, value_dim]; lo plane at out + lo_offset
   long long lo_offset;
   int32_t* slot_len;
@@ -48,7 +50,12 @@ struct GdnArgs {
 };
 
 // bf16 planes, row-major, 16-byte chunks XOR-swizzled by row so ldmatrix is conflict-free
+constexpr int UPAD = GD + 4;    // fp32 row stride of U / O (padding spreads accumulator-layout stores over banks)
+
 struct GdnSmem {
+  float stage[GC * GPREP];                      // the chunk's prep records, filled by a bulk copy one chunk ahead
+  uint64_t bar;                                 // completes when a stage copy has landed
+  uint64_t pad_;
   uint16_t Sh[GD * GD], Sl[GD * GD];           // state, rows dk, cols dv
   uint16_t Qh[GC * GD], Ql[GC * GD];           // q (l2normed, scaled)
   uint16_t Kh[GC * GD], Kl[GC * GD];           // k (l2normed)
@@ -57,7 +64,7 @@ struct GdnSmem {
       uint16_t Rh[GC * 2 * GD], Rl[GC * 2 * GD];  // [beta v | beta k e^G]
     } r;
     struct {
-      float U[GC * GD];                         // fp32
+      float U[GC][UPAD];                        // fp32 U, then (same thread per element) the output O
       uint16_t Wh[GC * GD], Wl[GC * GD];
     } uw;
   } ru;
@@ -66,7 +73,6 @@ struct GdnSmem {
   uint16_t Ph[GC * GC], Pl[GC * GC];           // P
   uint16_t Ih[GC * GC], Il[GC * GC];           // (I + A)^{-1}
   float A[GC][GC + 1];                          // A, then the inverse in fp32
-  float O[GC][GD + 4];
   float G[GC], beta[GC], eG[GC], eL[GC];
 };
 
@@ -148,82 +154,131 @@ __device__ __forceinline__ int gdn_find_seq(const int32_t* cu, int n, int t) {
   return lo;
 }
 
-// One warp per (token, head); lane l owns channels 4l..4l+3 of q, k and v.
-__global__ void __launch_bounds__(256) gdn_prep_kernel(const GdnArgs a, int n_tokens) {
-  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  const int H = a.p.heads;
-  const int t = gw / H, h = gw % H;
-  if (t >= n_tokens) return;
-  const int key_dim = H * GD, conv_dim = 3 * key_dim, value_dim = key_dim;
-  const int seq = gdn_find_seq(a.cu, a.n_seqs, t);
-  const int tok0 = a.cu[seq], len = a.cu[seq + 1] - tok0, p = t - tok0;
-  const int pslot = a.prefix_slot ? a.prefix_slot[seq] : -1;
-  const int sslot = a.save_slot ? a.save_slot[seq] : -1;
-  const bool pvalid = pslot >= 0 && pslot < a.n_slots;
-  const int base[3] = {h * GD, key_dim + h * GD, 2 * key_dim + h * GD};
-  float out[3][4];
+constexpr int PREP_TPW = 8;    // tokens per warp (the conv window slides in registers)
+
+// x rows p (sequence position) of the lane's 4 channels in each of q, k, v: the sequence's
+// own in-projection output for p >= 0, the prefix slot's conv history for p in [-3, 0),
+// zeros without a prefix
+__device__ __forceinline__ void prep_row(const GdnArgs& a, int key_dim, int h, int lane, int tok0, int p,
+                                         bool pvalid, int pslot, int conv_dim, float4 (&x)[3]) {
 #pragma unroll
   for (int part = 0; part < 3; ++part) {
-    const int ch = base[part] + lane * 4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int tap = 0; tap < 4; ++tap) {
-      const int pp = p - 3 + tap;
-      float4 x;
-      if (pp >= 0) x = *reinterpret_cast<const float4*>(a.mix + size_t(tok0 + pp) * a.ld_mix + ch);
-      else if (pvalid) x = *reinterpret_cast<const float4*>(a.conv_pool + (size_t(pslot) * 3 + (3 + pp)) * conv_dim + ch);
-      else x = make_float4(0.f, 0.f, 0.f, 0.f);
-      acc.x = fmaf(a.p.conv_w[(ch + 0) * 4 + tap], x.x, acc.x);
-      acc.y = fmaf(a.p.conv_w[(ch + 1) * 4 + tap], x.y, acc.y);
-      acc.z = fmaf(a.p.conv_w[(ch + 2) * 4 + tap], x.z, acc.z);
-      acc.w = fmaf(a.p.conv_w[(ch + 3) * 4 + tap], x.w, acc.w);
+    const int ch = part * key_dim + h * GD + lane * 4;
+    if (p >= 0) x[part] = *reinterpret_cast<const float4*>(a.mix + size_t(tok0 + p) * a.ld_mix + ch);
+    else if (pvalid) x[part] = *reinterpret_cast<const float4*>(a.conv_pool + (size_t(pslot) * 3 + (3 + p)) * conv_dim + ch);
+    else x[part] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// grid (ceil(T / 64), heads), 8 warps: warp w of block b handles head blockIdx.y, tokens
+// 64 b + 8 w .. +7; lane l owns channels 4l..4l+3 of the head's q, k and v. The warp keeps
+// the conv weights and the last 3 input rows in registers and loads each input row once.
+__global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const GdnArgs a) {
+  __shared__ float4 wsm[3][4][32];  // conv taps (oldest first) of channel base[part] + 4 lane + c
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int h = blockIdx.y, H = a.p.heads, T = a.n_tokens;
+  const int key_dim = H * GD, conv_dim = 3 * key_dim, value_dim = key_dim;
+  for (int i = threadIdx.x; i < 3 * GD; i += blockDim.x) {
+    const int part = i / GD, ch = i % GD;
+    wsm[part][ch & 3][ch >> 2] = *reinterpret_cast<const float4*>(a.p.conv_w + (part * key_dim + h * GD + ch) * 4);
+  }
+  __syncthreads();
+  const int t_begin = (blockIdx.x * 8 + warp) * PREP_TPW;
+  if (t_begin >= T) return;
+  const int t_end = min(T, t_begin + PREP_TPW);
+  const float a_coef = -__expf(a.p.a_log[h]), dt_bias = a.p.dt_bias[h];
+  int seq = gdn_find_seq(a.cu, a.n_seqs, t_begin);
+  int tok0 = a.cu[seq], tend = a.cu[seq + 1];
+  int pslot = -1, sv = -1;
+  bool pvalid = false, fresh = true;
+  float4 win[3][3];  // [row: p-3, p-2, p-1][part]
+  for (int t = t_begin; t < t_end; ++t) {
+    while (t >= tend) {  // next (possibly empty) sequence; ends because t < T = cu[n_seqs]
+      ++seq;
+      tok0 = tend;
+      tend = a.cu[seq + 1];
+      fresh = true;
     }
-    out[part][0] = silu(acc.x);
-    out[part][1] = silu(acc.y);
-    out[part][2] = silu(acc.z);
-    out[part][3] = silu(acc.w);
-  }
-  float sq = 0.f, sk = 0.f;
+    const int p = t - tok0;
+    if (fresh) {
+      pslot = a.prefix_slot ? a.prefix_slot[seq] : -1;
+      pvalid = pslot >= 0 && pslot < a.n_slots;
+      const int ss = a.save_slot ? a.save_slot[seq] : -1;
+      sv = (ss >= 0 && ss < a.n_slots) ? ss : -1;
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    sq += out[0][e] * out[0][e];
-    sk += out[1][e] * out[1][e];
-  }
-  sq = warp_sum(sq);
-  sk = warp_sum(sk);
-  const float rq = rsqrtf(sq + 1e-6f) * rsqrtf(float(GD)), rk = rsqrtf(sk + 1e-6f);
-  float* dst = a.prep + (size_t(t) * H + h) * GPREP;
-  reinterpret_cast<float4*>(dst)[lane] = make_float4(out[0][0] * rq, out[0][1] * rq, out[0][2] * rq, out[0][3] * rq);
-  reinterpret_cast<float4*>(dst + GD)[lane] =
-      make_float4(out[1][0] * rk, out[1][1] * rk, out[1][2] * rk, out[1][3] * rk);
-  reinterpret_cast<float4*>(dst + 2 * GD)[lane] = make_float4(out[2][0], out[2][1], out[2][2], out[2][3]);
-  if (lane == 0) {
-    const float* ab = a.mix + size_t(t) * a.ld_mix + conv_dim + value_dim;
-    dst[GQKV] = sigmoid(ab[h]);
-    dst[GQKV + 1] = -__expf(a.p.a_log[h]) * softplus(ab[H + h] + a.p.dt_bias[h]);
-  }
-  // conv history of a saving sequence: its last 3 raw inputs, written by the last token's warps
-  const int sv = (sslot >= 0 && sslot < a.n_slots) ? sslot : -1;
-  if (sv >= 0 && p == len - 1) {
-    for (int r = 0; r < 3; ++r) {
-      const int pp = len - 3 + r;
+      for (int r = 0; r < 3; ++r) prep_row(a, key_dim, h, lane, tok0, p - 3 + r, pvalid, pslot, conv_dim, win[r]);
+      fresh = false;
+    }
+    float4 x[3];
+    prep_row(a, key_dim, h, lane, tok0, p, pvalid, pslot, conv_dim, x);
+    float o[3][4];
 #pragma unroll
-      for (int part = 0; part < 3; ++part) {
-        const int ch = base[part] + lane * 4;
-        float4 x;
-        if (pp >= 0) x = *reinterpret_cast<const float4*>(a.mix + size_t(tok0 + pp) * a.ld_mix + ch);
-        else if (pvalid) x = *reinterpret_cast<const float4*>(a.conv_pool + (size_t(pslot) * 3 + (3 + pp)) * conv_dim + ch);
-        else x = make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4*>(a.conv_pool + (size_t(sv) * 3 + r) * conv_dim + ch) = x;
+    for (int part = 0; part < 3; ++part) {
+      const float xi[4][4] = {{win[0][part].x, win[1][part].x, win[2][part].x, x[part].x},
+                              {win[0][part].y, win[1][part].y, win[2][part].y, x[part].y},
+                              {win[0][part].z, win[1][part].z, win[2][part].z, x[part].z},
+                              {win[0][part].w, win[1][part].w, win[2][part].w, x[part].w}};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float4 w = wsm[part][c][lane];
+        float acc = 0.0f;
+        acc = fmaf(w.x, xi[c][0], acc);
+        acc = fmaf(w.y, xi[c][1], acc);
+        acc = fmaf(w.z, xi[c][2], acc);
+        acc = fmaf(w.w, xi[c][3], acc);
+        o[part][c] = silu(acc);
+      }
+    }
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+      win[0][part] = win[1][part];
+      win[1][part] = win[2][part];
+      win[2][part] = x[part];
+    }
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      sq += o[0][c] * o[0][c];
+      sk += o[1][c] * o[1][c];
+    }
+    sq = warp_sum(sq);
+    sk = warp_sum(sk);
+    const float rq = rsqrtf(sq + 1e-6f) * rsqrtf(float(GD)), rk = rsqrtf(sk + 1e-6f);
+    float* dst = a.prep + (size_t(h) * T + t) * GPREP;
+    reinterpret_cast<float4*>(dst)[lane] = make_float4(o[0][0] * rq, o[0][1] * rq, o[0][2] * rq, o[0][3] * rq);
+    reinterpret_cast<float4*>(dst + GD)[lane] = make_float4(o[1][0] * rk, o[1][1] * rk, o[1][2] * rk, o[1][3] * rk);
+    reinterpret_cast<float4*>(dst + 2 * GD)[lane] = make_float4(o[2][0], o[2][1], o[2][2], o[2][3]);
+    if (lane == 0) {
+      const float* ab = a.mix + size_t(t) * a.ld_mix + conv_dim + value_dim;
+      dst[GQKV] = sigmoid(ab[h]);
+      dst[GQKV + 1] = a_coef * softplus(ab[H + h] + dt_bias);
+    }
+    // conv history of a saving sequence: its last 3 raw inputs (the window now ends at p)
+    if (sv >= 0 && t == tend - 1) {
+#pragma unroll
+      for (int r = 0; r < 3; ++r) {
+#pragma unroll
+        for (int part = 0; part < 3; ++part)
+          *reinterpret_cast<float4*>(a.conv_pool + (size_t(sv) * 3 + r) * conv_dim + part * key_dim + h * GD + lane * 4) =
+              win[r][part];
       }
     }
   }
 }
 
 // ----------------------------------------------------------------------------- kernel
+
+// Bulk-copy the prep records of chunk c (rows tok0 + c .., head h: one contiguous run of
+// GPREP * 4 = 1552-byte records, 16-byte aligned) into the stage; completes on sm.bar.
+__device__ __forceinline__ void gdn_stage_chunk(GdnSmem& sm, const GdnArgs& a, int h, int tok0, int len, int c) {
+  const uint32_t bytes = uint32_t(min(GC, len - c)) * GPREP * 4;
+  mbar_arrive_expect_tx(&sm.bar, bytes);
+  bulk_load(sm.stage, a.prep + (size_t(h) * a.n_tokens + tok0 + c) * GPREP, bytes, &sm.bar);
+}
 __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs a) {
-  extern __shared__ uint8_t gdn_smem_raw[];
+  extern __shared__ __align__(128) uint8_t gdn_smem_raw[];
   GdnSmem& sm = *reinterpret_cast<GdnSmem*>(gdn_smem_raw);
+  float (*const O)[UPAD] = sm.ru.uw.U;
   const int h = blockIdx.x, seq = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;
@@ -259,18 +314,26 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       }
     }
   };
+  if (tid == 0) {
+    mbar_init(&sm.bar, 1);
+    mbar_fence_init();
+    if (len > 0) gdn_stage_chunk(sm, a, h, tok0, len, 0);
+  }
   publish_state();
   __syncthreads();
 
+  uint32_t phase = 0;
   for (int c0 = 0; c0 < len; c0 += GC) {
     const int L = min(GC, len - c0);
+    const bool landed = mbar_wait(&sm.bar, phase, FAULT_GDN_WAIT_STAGE);
+    phase ^= 1u;
+    if (__syncthreads_or(!landed)) break;  // a copy that never landed: give up (fault recorded)
     // ---- 1. cumulative decay within the chunk
     if (tid < GC) {
       float gj = 0.0f, bj = 0.0f;
       if (tid < L) {
-        const float* pr = a.prep + (size_t(tok0 + c0 + tid) * H + h) * GPREP + GQKV;
-        bj = pr[0];
-        gj = pr[1];
+        bj = sm.stage[tid * GPREP + GQKV];
+        gj = sm.stage[tid * GPREP + GQKV + 1];
       }
       float v = gj;  // inclusive warp scan
 #pragma unroll
@@ -288,7 +351,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
     for (int j = warp; j < GC; j += GDN_THREADS / 32) {
       float4 q = make_float4(0.f, 0.f, 0.f, 0.f), k = q, v = q;
       if (j < L) {
-        const float* pr = a.prep + (size_t(tok0 + c0 + j) * H + h) * GPREP;
+        const float* pr = sm.stage + j * GPREP;
         q = reinterpret_cast<const float4*>(pr)[lane];
         k = reinterpret_cast<const float4*>(pr + GD)[lane];
         v = reinterpret_cast<const float4*>(pr + 2 * GD)[lane];
@@ -305,6 +368,10 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, GD + c + 2), bke * k.z, bke * k.w);
     }
     __syncthreads();
+    if (tid == 0 && c0 + GC < len) {  // every read of the stage is done: fetch the next chunk
+      fence_proxy_async_smem();
+      gdn_stage_chunk(sm, a, h, tok0, len, c0 + GC);
+    }
     // ---- 3. A = beta k k^T, P = q k^T (x decay, masked): warp -> rows 16*(w>>2), cols 8*(w&3)
     {
       const int m0 = 16 * (warp >> 2), n0 = 8 * (warp & 3);
@@ -362,12 +429,13 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       float mval = 0.0f;
 #pragma unroll
       for (int j = 0; j < 16; ++j) mval = fmaf(sm.A[16 + i][j], sm.A[j][c], mval);
+      float* scratch = reinterpret_cast<float*>(sm.Vh);  // Vh is first written in step 6
       __syncthreads();
-      sm.O[i][c] = mval;  // scratch
+      scratch[i * 16 + c] = mval;
       __syncthreads();
       float t = 0.0f;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) t = fmaf(sm.A[16 + i][16 + j], sm.O[j][c], t);
+      for (int j = 0; j < 16; ++j) t = fmaf(sm.A[16 + i][16 + j], scratch[j * 16 + c], t);
       __syncthreads();
       sm.A[16 + i][c] = -t;
     }
@@ -404,8 +472,8 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
         for (int hr = 0; hr < 2; ++hr) {
           const int r = m0 + g8 + 8 * hr, c = nb + 8 * j + 2 * t4;
           if (c < GD) {
-            sm.ru.uw.U[r * GD + c] = acc[j][2 * hr];
-            sm.ru.uw.U[r * GD + c + 1] = acc[j][2 * hr + 1];
+            sm.ru.uw.U[r][c] = acc[j][2 * hr];
+            sm.ru.uw.U[r][c + 1] = acc[j][2 * hr + 1];
           } else {
             split_store(sm.ru.uw.Wh, sm.ru.uw.Wl, soff<GD>(r, c - GD), acc[j][2 * hr], acc[j][2 * hr + 1]);
           }
@@ -441,12 +509,12 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
         for (int hr = 0; hr < 2; ++hr) {
           const int r = m0 + g8 + 8 * hr, c = nb + 8 * j + 2 * t4;
           const bool ok = r < L;
-          const float v0 = ok ? sm.ru.uw.U[r * GD + c] - ws[j][2 * hr] : 0.0f;
-          const float v1 = ok ? sm.ru.uw.U[r * GD + c + 1] - ws[j][2 * hr + 1] : 0.0f;
+          const float v0 = ok ? sm.ru.uw.U[r][c] - ws[j][2 * hr] : 0.0f;
+          const float v1 = ok ? sm.ru.uw.U[r][c + 1] - ws[j][2 * hr + 1] : 0.0f;
           split_store(sm.Vh, sm.Vl, soff<GD>(r, c), v0, v1);
           split_store(sm.Th, sm.Tl, soff<GD>(r, c), v0 * sm.eL[r], v1 * sm.eL[r]);
-          sm.O[r][c] = qs[j][2 * hr] * sm.eG[r];
-          sm.O[r][c + 1] = qs[j][2 * hr + 1] * sm.eG[r];
+          O[r][c] = qs[j][2 * hr] * sm.eG[r];  // overwrites U[r][c], read just above by this thread only
+          O[r][c + 1] = qs[j][2 * hr + 1] * sm.eG[r];
         }
       }
     }
@@ -475,8 +543,8 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
 #pragma unroll
         for (int hr = 0; hr < 2; ++hr) {
           const int r = m0 + g8 + 8 * hr, c = nb + 8 * j + 2 * t4;
-          sm.O[r][c] += pv[j][2 * hr];
-          sm.O[r][c + 1] += pv[j][2 * hr + 1];
+          O[r][c] += pv[j][2 * hr];
+          O[r][c + 1] += pv[j][2 * hr + 1];
         }
       }
     }
@@ -508,7 +576,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
     for (int j = warp; j < L; j += GDN_THREADS / 32) {
       float ss = 0.0f;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) ss += sm.O[j][lane * 4 + e] * sm.O[j][lane * 4 + e];
+      for (int e = 0; e < 4; ++e) ss += O[j][lane * 4 + e] * O[j][lane * 4 + e];
       ss = warp_sum(ss);
       const float r = rsqrtf(ss / float(GD) + a.p.eps);
       const size_t t = size_t(tok0 + c0 + j);
@@ -516,8 +584,8 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         const int d = lane * 4 + e;
-        const float y0 = a.p.norm_w[d] * (sm.O[j][d] * r) * silu(z[d]);
-        const float y1 = a.p.norm_w[d + 1] * (sm.O[j][d + 1] * r) * silu(z[d + 1]);
+        const float y0 = a.p.norm_w[d] * (O[j][d] * r) * silu(z[d]);
+        const float y1 = a.p.norm_w[d + 1] * (O[j][d + 1] * r) * silu(z[d + 1]);
         uint16_t* dst = a.out + t * value_dim + h * GD + d;
         const uint16_t h0 = f32_to_bf16_rn(y0), h1 = f32_to_bf16_rn(y1);
         *reinterpret_cast<uint32_t*>(dst) = uint32_t(h0) | (uint32_t(h1) << 16);
@@ -583,8 +651,8 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
     SDB_CUDA(cudaFuncSetAttribute(gdn_mixer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GdnSmem))));
     attr = true;
   }
-  const long warps = long(s->n_tokens) * p->heads;
-  gdn_prep_kernel<<<int((warps + 7) / 8), 256, 0, st>>>(a, s->n_tokens);
+  a.n_tokens = s->n_tokens;
+  gdn_prep_kernel<<<dim3((s->n_tokens + 8 * PREP_TPW - 1) / (8 * PREP_TPW), p->heads), 256, 0, st>>>(a);
   SDB_LAUNCH_CHECK();
   gdn_mixer_kernel<<<dim3(p->heads, s->n_seqs), GDN_THREADS, sizeof(GdnSmem), st>>>(a);
   SDB_LAUNCH_CHECK();
