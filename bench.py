@@ -60,7 +60,13 @@ class ClockSampler:
          "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
-        self.index = index
+        # nvidia-smi numbers GPUs physically; CUDA_VISIBLE_DEVICES may renumber them for torch,
+        # so the device is named by its UUID
+        self.index = str(index)
+        try:
+            self.index = "GPU-" + str(torch.cuda.get_device_properties(index).uuid)
+        except Exception:
+            pass
         self.rows: list[list[str]] = []
         self.proc = None
         self.t = None
@@ -355,6 +361,10 @@ def latency(args) -> None:
     for _ in range(max(args.warmup, 20)):
         g.replay()
     torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()    # a profiler started with capture off records this one replay
+    g.replay()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
     st = torch.cuda.current_stream()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(runs)]
     clocks = ClockSampler(0)

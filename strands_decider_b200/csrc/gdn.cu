@@ -1,7 +1,7 @@
 // Gated-DeltaNet token mixer (after the in-projection GEMM) on tensor cores.
 //
 // Two kernels, restating TF:234-311 with TF:462-530 fused around it.
-// gdn_prep_kernel, one warp per (head, 8 consecutive tokens), fully parallel:
+// gdn_prep_kernel, one warp per (head, TPW consecutive tokens), fully parallel:
 //   causal depthwise conv (width 4) + SiLU over the head's q, k, v channels (the 3 previous
 //   raw inputs come from the sequence itself or the prefix slot's history), l2norm(q) *
 //   dk^-1/2, l2norm(k), beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias); a sequence
@@ -20,7 +20,11 @@
 // significant bits per operand). The fp32 state S [dk, dv] lives in the warps' accumulator
 // registers (warp w holds rows 16w..16w+15) and is republished to shared memory as hi/lo
 // planes for the next chunk's products.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace sdb {
 
@@ -29,6 +33,7 @@ constexpr int GD = 128;         // key / value head dim
 constexpr int GQKV = 3 * GD;
 constexpr int GPREP = GQKV + 4;   // per (token, head): q | k | v | beta, g, pad
 constexpr int GDN_THREADS = 256;
+constexpr int GDN_DV_SPLIT = 32;   // value columns per CTA when a head is split over a cluster
 
 struct GdnArgs {
   b200_gdn_params p;
@@ -50,30 +55,34 @@ struct GdnArgs {
 };
 
 // bf16 planes, row-major, 16-byte chunks XOR-swizzled by row so ldmatrix is conflict-free
-constexpr int UPAD = GD + 4;    // fp32 row stride of U / O (padding spreads accumulator-layout stores over banks)
-
+// Shared memory of one CTA that owns DV of the head's 128 value columns (DV = 128: the whole
+// head; DV = 32: a quarter, four CTAs of a cluster per head).
+template <int DV>
 struct GdnSmem {
+  static constexpr int RW = (DV + GD + 63) / 64 * 64;  // R row width: [beta v (DV) | beta k e^G (128) | pad]
+  static constexpr int UP = DV + 4;                     // fp32 row stride of U / O (spreads stores over banks)
   float stage[GC * GPREP];                      // the chunk's prep records, filled by a bulk copy one chunk ahead
   uint64_t bar;                                 // completes when a stage copy has landed
   uint64_t pad_;
-  uint16_t Sh[GD * GD], Sl[GD * GD];           // state, rows dk, cols dv
+  uint16_t Sh[GD * DV], Sl[GD * DV];           // state slab, rows dk, cols: this CTA's dv columns
   uint16_t Qh[GC * GD], Ql[GC * GD];           // q (l2normed, scaled)
   uint16_t Kh[GC * GD], Kl[GC * GD];           // k (l2normed)
   union {
     struct {
-      uint16_t Rh[GC * 2 * GD], Rl[GC * 2 * GD];  // [beta v | beta k e^G]
+      uint16_t Rh[GC * RW], Rl[GC * RW];
     } r;
     struct {
-      float U[GC][UPAD];                        // fp32 U, then (same thread per element) the output O
+      float U[GC][UP];                          // fp32 U, then (same thread per element) the output O
       uint16_t Wh[GC * GD], Wl[GC * GD];
     } uw;
   } ru;
-  uint16_t Vh[GC * GD], Vl[GC * GD];           // Vn
-  uint16_t Th[GC * GD], Tl[GC * GD];           // Vn * e^{G_last - G} (named T for "tail-decayed")
+  uint16_t Vh[GC * DV], Vl[GC * DV];           // Vn
+  uint16_t Th[GC * DV], Tl[GC * DV];           // Vn * e^{G_last - G} (named T for "tail-decayed")
   uint16_t Ph[GC * GC], Pl[GC * GC];           // P
   uint16_t Ih[GC * GC], Il[GC * GC];           // (I + A)^{-1}
   float A[GC][GC + 1];                          // A, then the inverse in fp32
   float G[GC], beta[GC], eG[GC], eL[GC];
+  float part[2][GC];                            // per-row partial sums of O^2 (DV < 128; by chunk parity)
 };
 
 // ----------------------------------------------------------------------------- helpers
@@ -154,7 +163,9 @@ __device__ __forceinline__ int gdn_find_seq(const int32_t* cu, int n, int t) {
   return lo;
 }
 
-constexpr int PREP_TPW = 8;    // tokens per warp (the conv window slides in registers)
+// tokens per warp: 8 for large batches (each input row is loaded once, the conv window
+// slides in registers), 1 for small ones (latency: every warp loads its 4 rows at once)
+constexpr int PREP_TPW_LARGE = 8;
 
 // x rows p (sequence position) of the lane's 4 channels in each of q, k, v: the sequence's
 // own in-projection output for p >= 0, the prefix slot's conv history for p in [-3, 0),
@@ -173,6 +184,7 @@ __device__ __forceinline__ void prep_row(const GdnArgs& a, int key_dim, int h, i
 // grid (ceil(T / 64), heads), 8 warps: warp w of block b handles head blockIdx.y, tokens
 // 64 b + 8 w .. +7; lane l owns channels 4l..4l+3 of the head's q, k and v. The warp keeps
 // the conv weights and the last 3 input rows in registers and loads each input row once.
+template <int TPW>
 __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const GdnArgs a) {
   __shared__ float4 wsm[3][4][32];  // conv taps (oldest first) of channel base[part] + 4 lane + c
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -183,9 +195,9 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const GdnArgs a) {
     wsm[part][ch & 3][ch >> 2] = *reinterpret_cast<const float4*>(a.p.conv_w + (part * key_dim + h * GD + ch) * 4);
   }
   __syncthreads();
-  const int t_begin = (blockIdx.x * 8 + warp) * PREP_TPW;
+  const int t_begin = (blockIdx.x * 8 + warp) * TPW;
   if (t_begin >= T) return;
-  const int t_end = min(T, t_begin + PREP_TPW);
+  const int t_end = min(T, t_begin + TPW);
   const float a_coef = -__expf(a.p.a_log[h]), dt_bias = a.p.dt_bias[h];
   int seq = gdn_find_seq(a.cu, a.n_seqs, t_begin);
   int tok0 = a.cu[seq], tend = a.cu[seq + 1];
@@ -269,17 +281,29 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const GdnArgs a) {
 // ----------------------------------------------------------------------------- kernel
 
 // Bulk-copy the prep records of chunk c (rows tok0 + c .., head h: one contiguous run of
-// GPREP * 4 = 1552-byte records, 16-byte aligned) into the stage; completes on sm.bar.
-__device__ __forceinline__ void gdn_stage_chunk(GdnSmem& sm, const GdnArgs& a, int h, int tok0, int len, int c) {
+// GPREP * 4 = 1552-byte records, 16-byte aligned) into the stage; completes on bar.
+__device__ __forceinline__ void gdn_stage_chunk(float* stage, uint64_t* bar, const GdnArgs& a, int h, int tok0, int len,
+                                                int c) {
   const uint32_t bytes = uint32_t(min(GC, len - c)) * GPREP * 4;
-  mbar_arrive_expect_tx(&sm.bar, bytes);
-  bulk_load(sm.stage, a.prep + (size_t(h) * a.n_tokens + tok0 + c) * GPREP, bytes, &sm.bar);
+  mbar_arrive_expect_tx(bar, bytes);
+  bulk_load(stage, a.prep + (size_t(h) * a.n_tokens + tok0 + c) * GPREP, bytes, bar);
 }
+
+// grid (heads * NS, n_seqs), NS = 128 / DV CTAs per (sequence, head) forming one cluster; the
+// CTA with cluster rank `slice` owns value columns col0 = slice * DV .. col0 + DV - 1 of the
+// state, U, Vn and O. The dv columns of the delta rule are independent except for the gated
+// RMSNorm's sum of squares, which the cluster exchanges through distributed shared memory.
+// Steps 1-5 (decay, A, P, T, W) are computed by every CTA of the cluster.
+template <int DV>
 __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs a) {
+  constexpr int NS = GD / DV;
+  constexpr int NT = DV / 8;              // n8 tiles of the state slab per warp
+  using SMT = GdnSmem<DV>;
+  constexpr int RW = SMT::RW;
   extern __shared__ __align__(128) uint8_t gdn_smem_raw[];
-  GdnSmem& sm = *reinterpret_cast<GdnSmem*>(gdn_smem_raw);
-  float (*const O)[UPAD] = sm.ru.uw.U;
-  const int h = blockIdx.x, seq = blockIdx.y;
+  SMT& sm = *reinterpret_cast<SMT*>(gdn_smem_raw);
+  float (*const O)[SMT::UP] = sm.ru.uw.U;
+  const int h = blockIdx.x / NS, slice = blockIdx.x % NS, col0 = slice * DV, seq = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;
   const int H = a.p.heads;
@@ -292,34 +316,29 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
   if ((pslot >= a.n_slots || sslot >= a.n_slots) && tid == 0) raise_fault(FAULT_BAD_INDEX);
 
   // ---- initial state (fp32 slab in registers)
-  float S[16][4];  // rows 16*warp + g8 (+8), cols 8*nt + 2*t4 (+1)
+  float S[NT][4];  // rows 16*warp + g8 (+8), cols col0 + 8*nt + 2*t4 (+1)
   {
     const float* src = pvalid ? a.state_pool + (size_t(pslot) * H + h) * GD * GD : nullptr;
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = 16 * warp + g8 + 8 * (e >> 1), c = 8 * nt + 2 * t4 + (e & 1);
-        S[nt][e] = src ? src[r * GD + c] : 0.0f;
+        S[nt][e] = src ? src[r * GD + col0 + c] : 0.0f;
       }
     }
   }
-  auto publish_state = [&]() {
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        const int r = 16 * warp + g8 + 8 * hr, c = 8 * nt + 2 * t4;
-        split_store(sm.Sh, sm.Sl, soff<GD>(r, c), S[nt][2 * hr], S[nt][2 * hr + 1]);
-      }
-    }
-  };
   if (tid == 0) {
     mbar_init(&sm.bar, 1);
     mbar_fence_init();
-    if (len > 0) gdn_stage_chunk(sm, a, h, tok0, len, 0);
+    if (len > 0) gdn_stage_chunk(sm.stage, &sm.bar, a, h, tok0, len, 0);
   }
-  publish_state();
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr)
+      split_store(sm.Sh, sm.Sl, soff<DV>(16 * warp + g8 + 8 * hr, 8 * nt + 2 * t4), S[nt][2 * hr], S[nt][2 * hr + 1]);
+  }
   __syncthreads();
 
   uint32_t phase = 0;
@@ -327,7 +346,15 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
     const int L = min(GC, len - c0);
     const bool landed = mbar_wait(&sm.bar, phase, FAULT_GDN_WAIT_STAGE);
     phase ^= 1u;
-    if (__syncthreads_or(!landed)) break;  // a copy that never landed: give up (fault recorded)
+    if constexpr (NS == 1) {
+      if (__syncthreads_or(!landed)) break;  // a copy that never landed: give up (fault recorded)
+    } else {
+      // a cluster keeps going (every CTA must reach every cluster barrier); the data of a
+      // copy that never landed is garbage, and the fault word already reports it
+      __syncthreads();
+    }
+    if (warp == GDN_THREADS / 32 - 1 && lane < L)  // the chunk's z gate rows, read in step 8
+      bulk_prefetch_l2(a.mix + size_t(tok0 + c0 + lane) * a.ld_mix + conv_dim + h * GD + col0, DV * 4);
     // ---- 1. cumulative decay within the chunk
     if (tid < GC) {
       float gj = 0.0f, bj = 0.0f;
@@ -354,7 +381,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
         const float* pr = sm.stage + j * GPREP;
         q = reinterpret_cast<const float4*>(pr)[lane];
         k = reinterpret_cast<const float4*>(pr + GD)[lane];
-        v = reinterpret_cast<const float4*>(pr + 2 * GD)[lane];
+        if (lane < DV / 4) v = reinterpret_cast<const float4*>(pr + 2 * GD + col0)[lane];
       }
       const float bj = sm.beta[j], bke = bj * sm.eG[j];
       const int c = lane * 4;
@@ -362,15 +389,17 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       split_store(sm.Qh, sm.Ql, soff<GD>(j, c + 2), q.z, q.w);
       split_store(sm.Kh, sm.Kl, soff<GD>(j, c), k.x, k.y);
       split_store(sm.Kh, sm.Kl, soff<GD>(j, c + 2), k.z, k.w);
-      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, c), bj * v.x, bj * v.y);
-      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, c + 2), bj * v.z, bj * v.w);
-      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, GD + c), bke * k.x, bke * k.y);
-      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<2 * GD>(j, GD + c + 2), bke * k.z, bke * k.w);
+      if (lane < DV / 4) {
+        split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<RW>(j, c), bj * v.x, bj * v.y);
+        split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<RW>(j, c + 2), bj * v.z, bj * v.w);
+      }
+      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<RW>(j, DV + c), bke * k.x, bke * k.y);
+      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<RW>(j, DV + c + 2), bke * k.z, bke * k.w);
     }
     __syncthreads();
     if (tid == 0 && c0 + GC < len) {  // every read of the stage is done: fetch the next chunk
       fence_proxy_async_smem();
-      gdn_stage_chunk(sm, a, h, tok0, len, c0 + GC);
+      gdn_stage_chunk(sm.stage, &sm.bar, a, h, tok0, len, c0 + GC);
     }
     // ---- 3. A = beta k k^T, P = q k^T (x decay, masked): warp -> rows 16*(w>>2), cols 8*(w&3)
     {
@@ -429,7 +458,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       float mval = 0.0f;
 #pragma unroll
       for (int j = 0; j < 16; ++j) mval = fmaf(sm.A[16 + i][j], sm.A[j][c], mval);
-      float* scratch = reinterpret_cast<float*>(sm.Vh);  // Vh is first written in step 6
+      float* scratch = reinterpret_cast<float*>(sm.Vh);  // Vh (>= 2 KB) is first written in step 6
       __syncthreads();
       scratch[i * 16 + c] = mval;
       __syncthreads();
@@ -446,105 +475,145 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       split_store(sm.Ih, sm.Il, soff<GC>(r, c), v0, v1);
     }
     __syncthreads();
-    // ---- 5. [U | W] = T R : warp -> rows 16*(w&1), cols 64*(w>>1) .. +64
+    // ---- 5. [U | W] = T R : job j = (rows 16*(j&1), cols 16*(j>>1) .. +16) of the DV + 128
+    //         columns; warp w takes jobs w, w + 8, ... (all with rows 16*(w&1))
     {
-      const int m0 = 16 * (warp & 1), nb = 64 * (warp >> 1);
-      float acc[8][4];
+      constexpr int NB = (DV + GD) / 16, PER = (2 * NB + 7) / 8;
+      const int m0 = 16 * (warp & 1);
+      float acc[PER][2][4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+      for (int i = 0; i < PER; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][0][e] = acc[i][1][e] = 0.0f;
 #pragma unroll
       for (int k0 = 0; k0 < GC; k0 += 16) {
         uint32_t ah[4], al[4];
         frag_a<GC>(ah, sm.Ih, m0, k0, lane);
         frag_a<GC>(al, sm.Il, m0, k0, lane);
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          uint32_t bh[4], bl[4];
-          frag_bt<2 * GD>(bh, sm.ru.r.Rh, nb + 16 * np, k0, lane);
-          frag_bt<2 * GD>(bl, sm.ru.r.Rl, nb + 16 * np, k0, lane);
-          mma3(acc[2 * np], acc[2 * np + 1], ah, al, bh, bl);
+        for (int i = 0; i < PER; ++i) {
+          const int nb = (warp >> 1) + 4 * i;
+          if (nb < NB) {
+            uint32_t bh[4], bl[4];
+            frag_bt<RW>(bh, sm.ru.r.Rh, 16 * nb, k0, lane);
+            frag_bt<RW>(bl, sm.ru.r.Rl, 16 * nb, k0, lane);
+            mma3(acc[i][0], acc[i][1], ah, al, bh, bl);
+          }
         }
       }
       __syncthreads();  // R is fully read before U / W overwrite it
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int i = 0; i < PER; ++i) {
+        const int nb = (warp >> 1) + 4 * i;
+        if (nb < NB) {
 #pragma unroll
-        for (int hr = 0; hr < 2; ++hr) {
-          const int r = m0 + g8 + 8 * hr, c = nb + 8 * j + 2 * t4;
-          if (c < GD) {
-            sm.ru.uw.U[r][c] = acc[j][2 * hr];
-            sm.ru.uw.U[r][c + 1] = acc[j][2 * hr + 1];
-          } else {
-            split_store(sm.ru.uw.Wh, sm.ru.uw.Wl, soff<GD>(r, c - GD), acc[j][2 * hr], acc[j][2 * hr + 1]);
+          for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int hr = 0; hr < 2; ++hr) {
+              const int r = m0 + g8 + 8 * hr, c = 16 * nb + 8 * half + 2 * t4;
+              if (c < DV) {
+                sm.ru.uw.U[r][c] = acc[i][half][2 * hr];
+                sm.ru.uw.U[r][c + 1] = acc[i][half][2 * hr + 1];
+              } else {
+                split_store(sm.ru.uw.Wh, sm.ru.uw.Wl, soff<GD>(r, c - DV), acc[i][half][2 * hr],
+                            acc[i][half][2 * hr + 1]);
+              }
+            }
           }
         }
       }
     }
     __syncthreads();
-    // ---- 6. Vn = U - W S  and  O = e^G (q S): warp -> rows 16*(w&1), cols 32*(w>>1) .. +32
+    // ---- 6. Vn = U - W S  and  O = e^G (q S): job j = (rows 16*(j&1), cols 16*(j>>1) .. +16)
+    //         of the DV columns; warp w takes jobs w, w + 8
+    constexpr int NB6 = DV / 16, PER6 = (2 * NB6 + 7) / 8;
     {
-      const int m0 = 16 * (warp & 1), nb = 32 * (warp >> 1);
-      float ws[4][4], qs[4][4];
+      const int m0 = 16 * (warp & 1);
+      float ws[PER6][2][4], qs[PER6][2][4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) ws[j][0] = ws[j][1] = ws[j][2] = ws[j][3] = qs[j][0] = qs[j][1] = qs[j][2] = qs[j][3] = 0.0f;
+      for (int i = 0; i < PER6; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ws[i][0][e] = ws[i][1][e] = qs[i][0][e] = qs[i][1][e] = 0.0f;
+      if (warp < 2 * NB6) {
 #pragma unroll 1
-      for (int k0 = 0; k0 < GD; k0 += 16) {
-        uint32_t wh[4], wl[4], qh[4], ql[4];
-        frag_a<GD>(wh, sm.ru.uw.Wh, m0, k0, lane);
-        frag_a<GD>(wl, sm.ru.uw.Wl, m0, k0, lane);
-        frag_a<GD>(qh, sm.Qh, m0, k0, lane);
-        frag_a<GD>(ql, sm.Ql, m0, k0, lane);
+        for (int k0 = 0; k0 < GD; k0 += 16) {
+          uint32_t wh[4], wl[4], qh[4], ql[4];
+          frag_a<GD>(wh, sm.ru.uw.Wh, m0, k0, lane);
+          frag_a<GD>(wl, sm.ru.uw.Wl, m0, k0, lane);
+          frag_a<GD>(qh, sm.Qh, m0, k0, lane);
+          frag_a<GD>(ql, sm.Ql, m0, k0, lane);
 #pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          uint32_t bh[4], bl[4];
-          frag_bt<GD>(bh, sm.Sh, nb + 16 * np, k0, lane);
-          frag_bt<GD>(bl, sm.Sl, nb + 16 * np, k0, lane);
-          mma3(ws[2 * np], ws[2 * np + 1], wh, wl, bh, bl);
-          mma3(qs[2 * np], qs[2 * np + 1], qh, ql, bh, bl);
+          for (int i = 0; i < PER6; ++i) {
+            const int nb = (warp >> 1) + 4 * i;
+            if (nb < NB6) {
+              uint32_t bh[4], bl[4];
+              frag_bt<DV>(bh, sm.Sh, 16 * nb, k0, lane);
+              frag_bt<DV>(bl, sm.Sl, 16 * nb, k0, lane);
+              mma3(ws[i][0], ws[i][1], wh, wl, bh, bl);
+              mma3(qs[i][0], qs[i][1], qh, ql, bh, bl);
+            }
+          }
         }
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int i = 0; i < PER6; ++i) {
+        const int nb = (warp >> 1) + 4 * i;
+        if (warp < 2 * NB6 && nb < NB6) {
 #pragma unroll
-        for (int hr = 0; hr < 2; ++hr) {
-          const int r = m0 + g8 + 8 * hr, c = nb + 8 * j + 2 * t4;
-          const bool ok = r < L;
-          const float v0 = ok ? sm.ru.uw.U[r][c] - ws[j][2 * hr] : 0.0f;
-          const float v1 = ok ? sm.ru.uw.U[r][c + 1] - ws[j][2 * hr + 1] : 0.0f;
-          split_store(sm.Vh, sm.Vl, soff<GD>(r, c), v0, v1);
-          split_store(sm.Th, sm.Tl, soff<GD>(r, c), v0 * sm.eL[r], v1 * sm.eL[r]);
-          O[r][c] = qs[j][2 * hr] * sm.eG[r];  // overwrites U[r][c], read just above by this thread only
-          O[r][c + 1] = qs[j][2 * hr + 1] * sm.eG[r];
+          for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int hr = 0; hr < 2; ++hr) {
+              const int r = m0 + g8 + 8 * hr, c = 16 * nb + 8 * half + 2 * t4;
+              const bool ok = r < L;
+              const float v0 = ok ? sm.ru.uw.U[r][c] - ws[i][half][2 * hr] : 0.0f;
+              const float v1 = ok ? sm.ru.uw.U[r][c + 1] - ws[i][half][2 * hr + 1] : 0.0f;
+              split_store(sm.Vh, sm.Vl, soff<DV>(r, c), v0, v1);
+              split_store(sm.Th, sm.Tl, soff<DV>(r, c), v0 * sm.eL[r], v1 * sm.eL[r]);
+              O[r][c] = qs[i][half][2 * hr] * sm.eG[r];  // overwrites U[r][c], read just above by this thread
+              O[r][c + 1] = qs[i][half][2 * hr + 1] * sm.eG[r];
+            }
+          }
         }
       }
     }
     __syncthreads();
-    // ---- 7a. O += P Vn  (same tiling as step 6)
-    {
-      const int m0 = 16 * (warp & 1), nb = 32 * (warp >> 1);
-      float pv[4][4];
+    // ---- 7a. O += P Vn  (same jobs as step 6)
+    if (warp < 2 * NB6) {
+      const int m0 = 16 * (warp & 1);
+      float pv[PER6][2][4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) pv[j][0] = pv[j][1] = pv[j][2] = pv[j][3] = 0.0f;
+      for (int i = 0; i < PER6; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pv[i][0][e] = pv[i][1][e] = 0.0f;
 #pragma unroll
       for (int k0 = 0; k0 < GC; k0 += 16) {
         uint32_t ph[4], pl[4];
         frag_a<GC>(ph, sm.Ph, m0, k0, lane);
         frag_a<GC>(pl, sm.Pl, m0, k0, lane);
 #pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          uint32_t bh[4], bl[4];
-          frag_bt<GD>(bh, sm.Vh, nb + 16 * np, k0, lane);
-          frag_bt<GD>(bl, sm.Vl, nb + 16 * np, k0, lane);
-          mma3(pv[2 * np], pv[2 * np + 1], ph, pl, bh, bl);
+        for (int i = 0; i < PER6; ++i) {
+          const int nb = (warp >> 1) + 4 * i;
+          if (nb < NB6) {
+            uint32_t bh[4], bl[4];
+            frag_bt<DV>(bh, sm.Vh, 16 * nb, k0, lane);
+            frag_bt<DV>(bl, sm.Vl, 16 * nb, k0, lane);
+            mma3(pv[i][0], pv[i][1], ph, pl, bh, bl);
+          }
         }
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int i = 0; i < PER6; ++i) {
+        const int nb = (warp >> 1) + 4 * i;
+        if (nb < NB6) {
 #pragma unroll
-        for (int hr = 0; hr < 2; ++hr) {
-          const int r = m0 + g8 + 8 * hr, c = nb + 8 * j + 2 * t4;
-          O[r][c] += pv[j][2 * hr];
-          O[r][c + 1] += pv[j][2 * hr + 1];
+          for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int hr = 0; hr < 2; ++hr) {
+              const int r = m0 + g8 + 8 * hr, c = 16 * nb + 8 * half + 2 * t4;
+              O[r][c] += pv[i][half][2 * hr];
+              O[r][c + 1] += pv[i][half][2 * hr + 1];
+            }
+          }
         }
       }
     }
@@ -552,7 +621,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
     {
       const float el = __expf(sm.G[L - 1]);
 #pragma unroll
-      for (int nt = 0; nt < 16; ++nt) {
+      for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) S[nt][e] *= el;
       }
@@ -562,35 +631,101 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
         frag_at<GD>(ah, sm.Kh, 16 * warp, k0, lane);
         frag_at<GD>(al, sm.Kl, 16 * warp, k0, lane);
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {
+        for (int np = 0; np < NT / 2; ++np) {
           uint32_t bh[4], bl[4];
-          frag_bt<GD>(bh, sm.Th, 16 * np, k0, lane);
-          frag_bt<GD>(bl, sm.Tl, 16 * np, k0, lane);
+          frag_bt<DV>(bh, sm.Th, 16 * np, k0, lane);
+          frag_bt<DV>(bl, sm.Tl, 16 * np, k0, lane);
           mma3(S[2 * np], S[2 * np + 1], ah, al, bh, bl);
         }
       }
     }
     __syncthreads();  // all reads of the old S planes (step 6) and of O's partials are done
-    publish_state();
-    // ---- 8. gated RMSNorm of the O rows -> hi/lo planes
-    for (int j = warp; j < L; j += GDN_THREADS / 32) {
-      float ss = 0.0f;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) ss += O[j][lane * 4 + e] * O[j][lane * 4 + e];
-      ss = warp_sum(ss);
-      const float r = rsqrtf(ss / float(GD) + a.p.eps);
-      const size_t t = size_t(tok0 + c0 + j);
-      const float* z = a.mix + t * a.ld_mix + conv_dim + h * GD;
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const int d = lane * 4 + e;
-        const float y0 = a.p.norm_w[d] * (O[j][d] * r) * silu(z[d]);
-        const float y1 = a.p.norm_w[d + 1] * (O[j][d + 1] * r) * silu(z[d + 1]);
-        uint16_t* dst = a.out + t * value_dim + h * GD + d;
-        const uint16_t h0 = f32_to_bf16_rn(y0), h1 = f32_to_bf16_rn(y1);
-        *reinterpret_cast<uint32_t*>(dst) = uint32_t(h0) | (uint32_t(h1) << 16);
-        if (a.lo_offset)
-          *reinterpret_cast<uint32_t*>(dst + a.lo_offset) = pack_bf16x2(y0 - bf16_to_f32(h0), y1 - bf16_to_f32(h1));
+      for (int hr = 0; hr < 2; ++hr)
+        split_store(sm.Sh, sm.Sl, soff<DV>(16 * warp + g8 + 8 * hr, 8 * nt + 2 * t4), S[nt][2 * hr],
+                    S[nt][2 * hr + 1]);
+    }
+    // ---- 8. gated RMSNorm of the O rows -> hi/lo planes; warp w owns rows w, w + 8, ...;
+    //         lane l owns this CTA's columns CPL*l .. CPL*l + CPL - 1
+    {
+      constexpr int CPL = DV / 32;
+      const int cpar = (c0 / GC) & 1;
+      float nw[CPL], zv[GC / 8][CPL], ov[GC / 8][CPL], ss[GC / 8];
+#pragma unroll
+      for (int e = 0; e < CPL; ++e) nw[e] = a.p.norm_w[col0 + lane * CPL + e];
+#pragma unroll
+      for (int i = 0; i < GC / 8; ++i) {  // the z gates of all the warp's rows, loaded before any is used
+        const int j = warp + 8 * i;
+        const float* z = a.mix + size_t(tok0 + c0 + (j < L ? j : 0)) * a.ld_mix + conv_dim + h * GD + col0 + lane * CPL;
+        if constexpr (CPL == 4) {
+          const float4 z4 = j < L ? *reinterpret_cast<const float4*>(z) : make_float4(0.f, 0.f, 0.f, 0.f);
+          zv[i][0] = z4.x;
+          zv[i][1] = z4.y;
+          zv[i][2] = z4.z;
+          zv[i][3] = z4.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < CPL; ++e) zv[i][e] = j < L ? z[e] : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < GC / 8; ++i) {
+        const int j = warp + 8 * i;
+        float q = 0.0f;
+#pragma unroll
+        for (int e = 0; e < CPL; ++e) {
+          ov[i][e] = O[j][lane * CPL + e];
+          q += ov[i][e] * ov[i][e];
+        }
+        ss[i] = warp_sum(q);
+        if constexpr (NS > 1) {
+          if (lane == 0) sm.part[cpar][j] = ss[i];
+        }
+      }
+      if constexpr (NS > 1) {
+        // the cluster's partial sums: each CTA reads every CTA's part[cpar] after this barrier;
+        // part[cpar] is written again two chunks later, after the next chunk's barrier
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+#pragma unroll
+        for (int i = 0; i < GC / 8; ++i) {
+          const int j = warp + 8 * i;
+          float tot = 0.0f;
+#pragma unroll
+          for (int r = 0; r < NS; ++r) tot += cluster.map_shared_rank(&sm.part[cpar][0], r)[j];
+          ss[i] = tot;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < GC / 8; ++i) {
+        const int j = warp + 8 * i;
+        if (j < L) {  // uniform across the warp
+          const float r = rsqrtf(ss[i] / float(GD) + a.p.eps);
+          float y[CPL];
+          uint16_t hb[CPL];
+#pragma unroll
+          for (int e = 0; e < CPL; ++e) {
+            y[e] = nw[e] * (ov[i][e] * r) * silu(zv[i][e]);
+            hb[e] = f32_to_bf16_rn(y[e]);
+          }
+          uint16_t* dst = a.out + size_t(tok0 + c0 + j) * value_dim + h * GD + col0 + lane * CPL;
+          if constexpr (CPL == 4) {
+            *reinterpret_cast<uint2*>(dst) =
+                make_uint2(uint32_t(hb[0]) | (uint32_t(hb[1]) << 16), uint32_t(hb[2]) | (uint32_t(hb[3]) << 16));
+            if (a.lo_offset)
+              *reinterpret_cast<uint2*>(dst + a.lo_offset) =
+                  make_uint2(pack_bf16x2(y[0] - bf16_to_f32(hb[0]), y[1] - bf16_to_f32(hb[1])),
+                             pack_bf16x2(y[2] - bf16_to_f32(hb[2]), y[3] - bf16_to_f32(hb[3])));
+          } else {
+#pragma unroll
+            for (int e = 0; e < CPL; ++e) {
+              dst[e] = hb[e];
+              if (a.lo_offset) dst[e + a.lo_offset] = f32_to_bf16_rn(y[e] - bf16_to_f32(hb[e]));
+            }
+          }
+        }
       }
     }
     __syncthreads();
@@ -599,14 +734,18 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
   if (svalid) {
     float* dst = a.state_pool + (size_t(sslot) * H + h) * GD * GD;
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = 16 * warp + g8 + 8 * (e >> 1), c = 8 * nt + 2 * t4 + (e & 1);
-        dst[r * GD + c] = S[nt][e];
+        dst[r * GD + col0 + c] = S[nt][e];
       }
     }
-    if (h == 0 && tid == 0) a.slot_len[sslot] = (pvalid ? a.slot_len[pslot] : 0) + len;
+    if (h == 0 && slice == 0 && tid == 0) a.slot_len[sslot] = (pvalid ? a.slot_len[pslot] : 0) + len;
+  }
+  if constexpr (NS > 1) {
+    // no CTA leaves while another may still read its part[] (the last chunk's exchange)
+    cg::this_cluster().sync();
   }
 }
 
@@ -626,7 +765,7 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
   const bool uses_pool = s->prefix_slot || s->save_slot;
   if (uses_pool && (!pool || !pool->gdn_state || !pool->conv_hist || !pool->slot_len))
     return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: prefix/save slots need a pool");
-  if (lo_offset % 2 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: lo_offset must be even");
+  if (lo_offset % 4 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: lo_offset must be a multiple of 4");
   GdnArgs a;
   a.p = *p;
   a.cu = s->cu_seqlens;
@@ -640,6 +779,8 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
   a.out = out;
   a.lo_offset = lo_offset;
   const int conv_dim = 3 * p->heads * GD;
+  if (ld_mix % 4 != 0 || (reinterpret_cast<uintptr_t>(mix) & 15) || (reinterpret_cast<uintptr_t>(out) & 7))
+    return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: mix must be 16-byte aligned with ld_mix % 4 == 0, out 8-byte aligned");
   if (ld_mix < conv_dim + p->heads * GD + 2 * p->heads)
     return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: ld_mix is narrower than [q|k|v|z|b|a]");
   a.n_slots = uses_pool ? pool->n_slots : 0;
@@ -648,13 +789,41 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
   a.conv_pool = uses_pool ? pool->conv_hist + size_t(layer) * pool->n_slots * 3 * conv_dim : nullptr;
   static bool attr = false;
   if (!attr) {
-    SDB_CUDA(cudaFuncSetAttribute(gdn_mixer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GdnSmem))));
+    SDB_CUDA(cudaFuncSetAttribute(gdn_mixer_kernel<GD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(sizeof(GdnSmem<GD>))));
+    SDB_CUDA(cudaFuncSetAttribute(gdn_mixer_kernel<GDN_DV_SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(sizeof(GdnSmem<GDN_DV_SPLIT>))));
     attr = true;
   }
   a.n_tokens = s->n_tokens;
-  gdn_prep_kernel<<<dim3((s->n_tokens + 8 * PREP_TPW - 1) / (8 * PREP_TPW), p->heads), 256, 0, st>>>(a);
+  if (long(s->n_tokens) * p->heads >= 64L * 1024) {  // enough warps at 8 tokens each to fill the GPU
+    constexpr int TPW = PREP_TPW_LARGE;
+    gdn_prep_kernel<TPW><<<dim3((s->n_tokens + 8 * TPW - 1) / (8 * TPW), p->heads), 256, 0, st>>>(a);
+  } else {
+    gdn_prep_kernel<1><<<dim3((s->n_tokens + 7) / 8, p->heads), 256, 0, st>>>(a);
+  }
   SDB_LAUNCH_CHECK();
-  gdn_mixer_kernel<<<dim3(p->heads, s->n_seqs), GDN_THREADS, sizeof(GdnSmem), st>>>(a);
+  if (long(s->n_seqs) * p->heads * 2 > 148) {  // enough (sequence, head) CTAs: one per head
+    gdn_mixer_kernel<GD><<<dim3(p->heads, s->n_seqs), GDN_THREADS, sizeof(GdnSmem<GD>), st>>>(a);
+    SDB_LAUNCH_CHECK();
+    return B200_OK;
+  }
+  // few sequences (latency): a cluster of 128 / GDN_DV_SPLIT CTAs per head, each owning a
+  // slice of the value columns
+  constexpr int NS = GD / GDN_DV_SPLIT;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p->heads * NS, s->n_seqs);
+  cfg.blockDim = dim3(GDN_THREADS);
+  cfg.dynamicSmemBytes = sizeof(GdnSmem<GDN_DV_SPLIT>);
+  cfg.stream = st;
+  cudaLaunchAttribute attr_cl[1];
+  attr_cl[0].id = cudaLaunchAttributeClusterDimension;
+  attr_cl[0].val.clusterDim.x = NS;
+  attr_cl[0].val.clusterDim.y = 1;
+  attr_cl[0].val.clusterDim.z = 1;
+  cfg.attrs = attr_cl;
+  cfg.numAttrs = 1;
+  SDB_CUDA(cudaLaunchKernelEx(&cfg, gdn_mixer_kernel<GDN_DV_SPLIT>, a));
   SDB_LAUNCH_CHECK();
   return B200_OK;
 }

@@ -36,13 +36,33 @@ constexpr int GEMM_UNPACK_THREADS = 256;
 constexpr int GEMM_EPI_WARP0 = 2;
 constexpr int GEMM_UNPACK_WARP0 = 6;
 
-constexpr int GEMM_STAGES = 3;
+// Shared-memory stages: 3 of 72 KB for 256-column tiles, 4 of 52 KB for 128-column tiles
+// (the narrow tiles serve small M, where the depth hides the weights' HBM latency).
+constexpr int gemm_stages(int bn) { return bn == 128 ? 4 : 3; }
+// Packed weight tiles are prefetched into L2 this many k-blocks ahead of the copy into a stage.
+constexpr int GEMM_L2_AHEAD = 6;
+
+constexpr int GEMM_TILE_ROWS = 256;  // rows of one b200_tile_weights tile (a 128-column tile reads half of one)
 
 struct GemmArgs {
   b200_qweight w;
   b200_linear_out o;
   int m, k;
+  int ksplit;  // > 1: each output tile is summed from ksplit K-ranges by fp32 atomic adds
 };
+
+// Work unit u -> output tile (m0, n0) and its K range [kb0, kb1) in GEMM_BK blocks. N is
+// fastest so the CTAs running at one time share activation tiles; then the K split.
+struct GemmUnit {
+  int m0, n0, kb0, kb1;
+};
+template <int BN>
+__device__ __forceinline__ GemmUnit gemm_unit(const GemmArgs& a, int u, int nk) {
+  const int n_tiles_n = a.w.n / BN;
+  const int nt = u % n_tiles_n, rest = u / n_tiles_n;
+  const int ks = rest % a.ksplit, mt = rest / a.ksplit;
+  return {mt * GEMM_BM, nt * BN, ks * nk / a.ksplit, (ks + 1) * nk / a.ksplit};
+}
 
 template <int BN, int FMT, bool SPLIT>
 struct GemmSmem {
@@ -53,8 +73,9 @@ struct GemmSmem {
   static constexpr int W_BYTES = PACKED ? BN * tile_row_bytes(FMT) : 0;
   static constexpr int S_BYTES = BN * tile_scale_row_bytes(FMT);
   static constexpr int STAGE = A_STAGE + B_BYTES + W_BYTES + S_BYTES;
-  static constexpr int BARS = 4 * GEMM_STAGES + 4;
-  static constexpr int TOTAL = GEMM_STAGES * STAGE + 1024 + BARS * 8 + 16 + 64;
+  static constexpr int STAGES = gemm_stages(BN);
+  static constexpr int BARS = 4 * STAGES + 4;
+  static constexpr int TOTAL = STAGES * STAGE + 1024 + BARS * 8 + 16 + 64;
 };
 
 // --------------------------------------------------------------------------- epilogue
@@ -92,6 +113,26 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int g
       for (int j = 0; j < 32; ++j)
         if (j < nv) dst[j] += __uint_as_float(v[j]);
     }
+  }
+}
+
+// Split-K partial: out[row, gcol..] += v (fp32 atomic adds; the store epilogue's output was
+// zeroed before the launch, the residual epilogue adds into the residual itself).
+__device__ __forceinline__ void epilogue_chunk_atomic(const GemmArgs& a, int row, int gcol, const uint32_t (&v)[32]) {
+  const b200_linear_out& o = a.o;
+  if (row >= a.m || gcol >= o.n_valid) return;
+  const int nv = min(32, o.n_valid - gcol);
+  float* dst = reinterpret_cast<float*>(o.out) + size_t(row) * o.ldo + gcol;
+  if (nv == 32) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4 * j), "r"(v[4 * j]), "r"(v[4 * j + 1]),
+                   "r"(v[4 * j + 2]), "r"(v[4 * j + 3])
+                   : "memory");
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nv) atomicAdd(dst + j, __uint_as_float(v[j]));
   }
 }
 
@@ -198,26 +239,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;                                   // STAGES x A_STAGE
-  uint8_t* sB = sA + GEMM_STAGES * SM::A_STAGE;         // STAGES x B_BYTES
-  uint8_t* sW = sB + GEMM_STAGES * SM::B_BYTES;         // STAGES x W_BYTES
-  uint8_t* sS = sW + GEMM_STAGES * SM::W_BYTES;         // STAGES x S_BYTES
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sS + GEMM_STAGES * SM::S_BYTES);
+  uint8_t* sB = sA + SM::STAGES * SM::A_STAGE;         // STAGES x B_BYTES
+  uint8_t* sW = sB + SM::STAGES * SM::B_BYTES;         // STAGES x W_BYTES
+  uint8_t* sS = sW + SM::STAGES * SM::W_BYTES;         // STAGES x S_BYTES
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sS + SM::STAGES * SM::S_BYTES);
   uint64_t* full_a = bars;
-  uint64_t* full_w = bars + GEMM_STAGES;
-  uint64_t* full_b = bars + 2 * GEMM_STAGES;
-  uint64_t* empty = bars + 3 * GEMM_STAGES;
-  uint64_t* acc_full = bars + 4 * GEMM_STAGES;       // [2]
-  uint64_t* acc_empty = bars + 4 * GEMM_STAGES + 2;  // [2]
+  uint64_t* full_w = bars + SM::STAGES;
+  uint64_t* full_b = bars + 2 * SM::STAGES;
+  uint64_t* empty = bars + 3 * SM::STAGES;
+  uint64_t* acc_full = bars + 4 * SM::STAGES;       // [2]
+  uint64_t* acc_empty = bars + 4 * SM::STAGES + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + SM::BARS);
   uint32_t* lut = tmem_slot + 4;  // 16 words: ternary pair table
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = args.k / GEMM_BK;
-  const int n_tiles_n = args.w.n / BN;
-  const int n_tiles = n_tiles_n * ((args.m + GEMM_BM - 1) / GEMM_BM);
+  const int n_units = (args.w.n / BN) * ((args.m + GEMM_BM - 1) / GEMM_BM) * args.ksplit;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GEMM_STAGES; ++s) {
+    for (int s = 0; s < SM::STAGES; ++s) {
       mbar_init(&full_a[s], 1);
       mbar_init(&full_w[s], 1);
       mbar_init(&full_b[s], GEMM_UNPACK_THREADS);
@@ -245,20 +285,32 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tma_prefetch_desc(&tmA);
       if constexpr (SPLIT) tma_prefetch_desc(&tmA_lo);
       if constexpr (!SM::PACKED) tma_prefetch_desc(&tmB);
+      constexpr int RB = SM::PACKED ? tile_row_bytes(FMT) : 0, SB = tile_scale_row_bytes(FMT);
       uint32_t it = 0;
-      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        const int nt = tile % n_tiles_n, m0 = (tile / n_tiles_n) * GEMM_BM, n0 = nt * BN;
-        const uint8_t* wtiles = reinterpret_cast<const uint8_t*>(args.w.tiles) + size_t(nt) * nk * SM::W_BYTES;
-        const uint8_t* stiles = reinterpret_cast<const uint8_t*>(args.w.tile_scales) + size_t(nt) * nk * SM::S_BYTES;
-        for (int kt = 0; kt < nk; ++kt, ++it) {
-          const int s = it % GEMM_STAGES;
-          const uint32_t ph = (it / GEMM_STAGES) & 1;
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const GemmUnit w = gemm_unit<BN>(args, u, nk);
+        const int m0 = w.m0, n0 = w.n0;
+        // this tile's rows inside the 256-row streaming tiles: tile n0 / 256, row offset n0 % 256
+        const size_t lt = size_t(n0 / GEMM_TILE_ROWS) * nk, sub = n0 % GEMM_TILE_ROWS;
+        const uint8_t* wtiles = reinterpret_cast<const uint8_t*>(args.w.tiles) + sub * RB;
+        const uint8_t* stiles = reinterpret_cast<const uint8_t*>(args.w.tile_scales) + sub * SB;
+        if constexpr (SM::PACKED) {
+          for (int kt = w.kb0; kt < min(w.kb1, w.kb0 + GEMM_L2_AHEAD); ++kt)
+            bulk_prefetch_l2(wtiles + (lt + kt) * GEMM_TILE_ROWS * RB, SM::W_BYTES);
+        }
+        for (int kt = w.kb0; kt < w.kb1; ++kt, ++it) {
+          const int s = it % SM::STAGES;
+          const uint32_t ph = (it / SM::STAGES) & 1;
+          if constexpr (SM::PACKED) {
+            if (kt + GEMM_L2_AHEAD < w.kb1)
+              bulk_prefetch_l2(wtiles + (lt + kt + GEMM_L2_AHEAD) * GEMM_TILE_ROWS * RB, SM::W_BYTES);
+          }
           mbar_wait(&empty[s], ph ^ 1, FAULT_GEMM_WAIT_EMPTY);
           if constexpr (SM::PACKED) {
             mbar_arrive_expect_tx(&full_w[s], SM::W_BYTES + SM::S_BYTES);
-            bulk_load(sW + s * SM::W_BYTES, wtiles + size_t(kt) * SM::W_BYTES, SM::W_BYTES, &full_w[s]);
+            bulk_load(sW + s * SM::W_BYTES, wtiles + (lt + kt) * GEMM_TILE_ROWS * RB, SM::W_BYTES, &full_w[s]);
             if constexpr (SM::S_BYTES > 0)
-              bulk_load(sS + s * SM::S_BYTES, stiles + size_t(kt) * SM::S_BYTES, SM::S_BYTES, &full_w[s]);
+              bulk_load(sS + s * SM::S_BYTES, stiles + (lt + kt) * GEMM_TILE_ROWS * SB, SM::S_BYTES, &full_w[s]);
           }
           mbar_arrive_expect_tx(&full_a[s], SM::A_STAGE + (SM::PACKED ? 0 : SM::B_BYTES));
           tma_load_2d(sA + s * SM::A_STAGE, &tmA, &full_a[s], kt * GEMM_BK, m0);
@@ -273,14 +325,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(GEMM_BM, BN);
       uint32_t it = 0, local = 0;
-      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++local) {
+        const GemmUnit w = gemm_unit<BN>(args, u, nk);
         const uint32_t ab = local & 1, aph = (local >> 1) & 1;
         mbar_wait(&acc_empty[ab], aph ^ 1, FAULT_GEMM_WAIT_ACCUM);
         tc_fence_after();
         const uint32_t acc = tmem_base + ab * BN;
-        for (int kt = 0; kt < nk; ++kt, ++it) {
-          const int s = it % GEMM_STAGES;
-          const uint32_t ph = (it / GEMM_STAGES) & 1;
+        for (int kt = w.kb0; kt < w.kb1; ++kt, ++it) {
+          const int s = it % SM::STAGES;
+          const uint32_t ph = (it / SM::STAGES) & 1;
           mbar_wait(&full_a[s], ph, FAULT_GEMM_WAIT_FULL_A);
           if constexpr (SM::PACKED) mbar_wait(&full_b[s], ph, FAULT_GEMM_WAIT_FULL_B);
           tc_fence_after();
@@ -288,7 +341,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint64_t bd = umma_desc_sw128(smem_addr(sB + s * SM::B_BYTES));
 #pragma unroll
           for (int j = 0; j < GEMM_BK / 16; ++j) {  // +32 bytes of K per MMA = +2 in 16-byte units
-            umma_bf16(acc, ad + 2 * j, bd + 2 * j, idesc, (kt | j) != 0 ? 1u : 0u);
+            umma_bf16(acc, ad + 2 * j, bd + 2 * j, idesc, (kt != w.kb0 || j != 0) ? 1u : 0u);
             if constexpr (SPLIT) umma_bf16(acc, ad + (SM::A_BYTES >> 4) + 2 * j, bd + 2 * j, idesc, 1u);
           }
           umma_commit(&empty[s]);
@@ -301,8 +354,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ---------------- epilogue: warp (2..5) owns TMEM lanes 32*(warp%4)..+31, all columns
     const int q = warp & 3;
     uint32_t local = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
-      const int nt = tile % n_tiles_n, m0 = (tile / n_tiles_n) * GEMM_BM, n0 = nt * BN;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++local) {
+      const GemmUnit w = gemm_unit<BN>(args, u, nk);
+      const int m0 = w.m0, n0 = w.n0;
       const uint32_t ab = local & 1, aph = (local >> 1) & 1;
       mbar_wait(&acc_full[ab], aph, FAULT_GEMM_WAIT_ACCUM);
       tc_fence_after();
@@ -326,7 +380,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint32_t v[32];
           tmem_ld_32x32b_x32(tl + c * 32, v);
           tmem_ld_wait();
-          epilogue_chunk<EP>(args, row, n0 + c * 32, v);
+          if (args.ksplit > 1) epilogue_chunk_atomic(args, row, n0 + c * 32, v);
+          else epilogue_chunk<EP>(args, row, n0 + c * 32, v);
         }
       }
       tc_fence_before();
@@ -338,8 +393,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int t = threadIdx.x - GEMM_UNPACK_WARP0 * 32;
       constexpr int UNITS = BN * 2 / GEMM_UNPACK_THREADS;
       uint32_t it = 0;
-      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        const int n0 = (tile % n_tiles_n) * BN;
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const GemmUnit w = gemm_unit<BN>(args, u, nk);
+        const int n0 = w.n0;
         uint32_t row_sc[UNITS];
         float row_gs[UNITS];
 #pragma unroll
@@ -349,9 +405,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               FMT == B200_W_TERNARY ? uint32_t(__ldg(reinterpret_cast<const uint16_t*>(args.w.scales) + n0 + r)) : 0u;
           row_gs[i] = FMT == B200_W_NVFP4 ? __ldg(args.w.row_scale + n0 + r) : 1.0f;
         }
-        for (int kt = 0; kt < nk; ++kt, ++it) {
-          const int s = it % GEMM_STAGES;
-          const uint32_t ph = (it / GEMM_STAGES) & 1;
+        for (int kt = w.kb0; kt < w.kb1; ++kt, ++it) {
+          const int s = it % SM::STAGES;
+          const uint32_t ph = (it / SM::STAGES) & 1;
           mbar_wait(&full_w[s], ph, FAULT_GEMM_WAIT_FULL_W);
           uint8_t* stage = sB + s * SM::B_BYTES;
 #pragma unroll
@@ -494,6 +550,18 @@ static int check_tiles(const b200_qweight* w) {
   return B200_OK;
 }
 
+static int sm_count() {  // one process drives one device
+  static int n_sm = 0;
+  if (!n_sm) {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      n_sm = v;
+    else
+      n_sm = 148;
+  }
+  return n_sm;
+}
+
 template <int BN, int FMT, int EP, bool SPLIT>
 static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b, const GemmArgs& a,
                      cudaStream_t st) {
@@ -505,25 +573,43 @@ static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_lo, const CU
                                   smem));
     attr_set = true;
   }
-  static int n_sm = 0;
-  if (!n_sm) {
-    int dev = 0;
-    SDB_CUDA(cudaGetDevice(&dev));
-    SDB_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
-  }
+  const int n_sm = sm_count();
+  GemmArgs args = a;
   const int tiles = (a.w.n / BN) * ((a.m + GEMM_BM - 1) / GEMM_BM);
-  gemm_tc_kernel<BN, FMT, EP, SPLIT><<<std::min(tiles, n_sm), GEMM_THREADS, smem, st>>>(map, map_lo, map_b, a);
+  const int nk = a.k / GEMM_BK;
+  // Small M (few output tiles): split K so every SM has work; each unit keeps >= 2 k-blocks.
+  // (The SwiGLU needs whole sums, so it is never split.)
+  args.ksplit = 1;
+  if (EP != B200_EP_SWIGLU && 2 * tiles <= n_sm) args.ksplit = std::max(1, std::min({n_sm / tiles, nk / 2, 16}));
+  if (args.ksplit > 1 && EP == B200_EP_STORE)
+    SDB_CUDA(cudaMemset2DAsync(a.o.out, size_t(a.o.ldo) * 4, 0, size_t(a.o.n_valid) * 4, a.m, st));
+  const int units = tiles * args.ksplit;
+  gemm_tc_kernel<BN, FMT, EP, SPLIT><<<std::min(units, n_sm), GEMM_THREADS, smem, st>>>(map, map_lo, map_b, args);
   SDB_LAUNCH_CHECK();
   return B200_OK;
+}
+
+// 128-column tiles when 256-column tiles would leave most SMs idle (small M): twice the
+// tiles, a deeper stage ring, and (for the split-K epilogues) half the K split.
+static int tile_bn(const GemmArgs& a) {
+  const int tiles256 = (a.w.n / 256) * ((a.m + GEMM_BM - 1) / GEMM_BM);
+  return 2 * tiles256 <= sm_count() ? 128 : 256;
 }
 
 template <int FMT, bool SPLIT>
 static int dispatch_ep(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b, const GemmArgs& a,
                        cudaStream_t st) {
+  const bool narrow = tile_bn(a) == 128;
   switch (a.o.epilogue) {
-    case B200_EP_STORE: return launch_tc<256, FMT, B200_EP_STORE, SPLIT>(map, map_lo, map_b, a, st);
-    case B200_EP_RESID_ADD: return launch_tc<256, FMT, B200_EP_RESID_ADD, SPLIT>(map, map_lo, map_b, a, st);
-    default: return launch_tc<256, FMT, B200_EP_SWIGLU, SPLIT>(map, map_lo, map_b, a, st);
+    case B200_EP_STORE:
+      return narrow ? launch_tc<128, FMT, B200_EP_STORE, SPLIT>(map, map_lo, map_b, a, st)
+                    : launch_tc<256, FMT, B200_EP_STORE, SPLIT>(map, map_lo, map_b, a, st);
+    case B200_EP_RESID_ADD:
+      return narrow ? launch_tc<128, FMT, B200_EP_RESID_ADD, SPLIT>(map, map_lo, map_b, a, st)
+                    : launch_tc<256, FMT, B200_EP_RESID_ADD, SPLIT>(map, map_lo, map_b, a, st);
+    default:
+      return narrow ? launch_tc<128, FMT, B200_EP_SWIGLU, SPLIT>(map, map_lo, map_b, a, st)
+                    : launch_tc<256, FMT, B200_EP_SWIGLU, SPLIT>(map, map_lo, map_b, a, st);
   }
 }
 
@@ -566,13 +652,14 @@ extern "C" int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m
   } else {
     map_lo = map;
   }
-  if (w->format == B200_W_BF16) {  // the weight tile streams through TMA as [n, k] bf16, 256 rows per box
+  GemmArgs a{*w, *out, m, k, 1};
+  if (w->format == B200_W_BF16) {  // the weight tile streams through TMA as [n, k] bf16, one box per N tile
     if (reinterpret_cast<uintptr_t>(w->data) & 15) return sdb_fail(B200_ERR_SHAPE, "b200_linear: bf16 W unaligned");
-    if (int rc = make_act_map(&map_b, reinterpret_cast<const uint16_t*>(w->data), w->n, k, k, 256)) return rc;
+    const int bn = tile_bn(a);
+    if (int rc = make_act_map(&map_b, reinterpret_cast<const uint16_t*>(w->data), w->n, k, k, bn)) return rc;
   } else {
     map_b = map;
   }
-  GemmArgs a{*w, *out, m, k};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return x_lo ? dispatch_fmt<true>(map, map_lo, map_b, a, st) : dispatch_fmt<false>(map, map_lo, map_b, a, st);
 }
@@ -580,7 +667,7 @@ extern "C" int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m
 extern "C" int b200_linear_simt(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m, int32_t k, int32_t ldx,
                                 const b200_qweight* w, const b200_linear_out* out, b200_stream stream) {
   if (int rc = check_linear(x_hi, x_lo, m, k, ldx, w, out)) return rc;
-  GemmArgs a{*w, *out, m, k};
+  GemmArgs a{*w, *out, m, k, 1};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (w->format) {
     case B200_W_BF16: return dispatch_simt<B200_W_BF16>(x_hi, x_lo, ldx, a, st);

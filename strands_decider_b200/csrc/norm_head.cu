@@ -58,6 +58,48 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, int rows, int hidden
   }
 }
 
+// Few rows (a latency-bound batch): one 256-thread block per row, the row held in registers
+// (hidden <= 4096, hidden % 1024 == 0), so each row costs one load round trip.
+__global__ void __launch_bounds__(256) rmsnorm_block_kernel(const float* __restrict__ x, int hidden,
+                                                            const float* __restrict__ w, float eps,
+                                                            uint16_t* __restrict__ out, long long lo_offset) {
+  __shared__ float part[8];
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int n4 = hidden / 1024;  // float4 per thread
+  const float4* xr = reinterpret_cast<const float4*>(x + size_t(row) * hidden);
+  float4 v[4];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (i < n4) {
+      v[i] = xr[tid + 256 * i];
+      ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) part[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += part[i];
+  const float r = rsqrtf(tot / float(hidden) + eps);
+  uint2* o = reinterpret_cast<uint2*>(out + size_t(row) * hidden);
+  uint2* ol = reinterpret_cast<uint2*>(out + lo_offset + size_t(row) * hidden);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (i < n4) {
+      const int j = tid + 256 * i;
+      const float4 g = __ldg(wr + j);
+      uint2 hi, lo;
+      split2(v[i].x * r * (1.0f + g.x), v[i].y * r * (1.0f + g.y), hi.x, lo.x);
+      split2(v[i].z * r * (1.0f + g.z), v[i].w * r * (1.0f + g.w), hi.y, lo.y);
+      o[j] = hi;
+      if (lo_offset) ol[j] = lo;
+    }
+  }
+}
+
 // Decision head: one warp per decision row. Gathers the row's last token from the fp32
 // residual stream, applies the final RMSNorm (1 + w), dots it with the option tokens'
 // tied-embedding rows, divides by the row's temperature (clamped at 1e-6), takes the
@@ -191,8 +233,11 @@ extern "C" int b200_rmsnorm(const float* x, int32_t rows, int32_t hidden, const 
   if (!x || !w || !out) return sdb_fail(B200_ERR_ARG, "b200_rmsnorm: null pointer");
   if (rows <= 0 || hidden % 128 != 0 || lo_offset % 8 != 0)
     return sdb_fail(B200_ERR_SHAPE, "b200_rmsnorm: hidden % 128 and lo_offset % 8 must be 0");
-  rmsnorm_kernel<<<(rows + 7) / 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, rows, hidden, w, eps, out,
-                                                                                   lo_offset);
+  if (rows <= 1024 && hidden % 1024 == 0 && hidden <= 4096)
+    rmsnorm_block_kernel<<<rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, hidden, w, eps, out, lo_offset);
+  else
+    rmsnorm_kernel<<<(rows + 7) / 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, rows, hidden, w, eps, out,
+                                                                                     lo_offset);
   SDB_LAUNCH_CHECK();
   return B200_OK;
 }

@@ -86,7 +86,7 @@ def _linear(fn, xp, pw, ep, n_valid=None, split=True):
     n_valid = n_valid or pw.n
     lo_off = 0
     if ep == _lib.EP_STORE:
-        out = torch.zeros(m, n_valid, device="cuda")
+        out = torch.full((m, n_valid), 7.0, device="cuda")  # the store must overwrite it (split K zeroes it first)
         ldo = n_valid
     elif ep == _lib.EP_RESID_ADD:
         out = torch.randn(m, n_valid, device="cuda")
@@ -175,6 +175,31 @@ def test_linear_swiglu(fmt):
         assert (got - ref).abs().max().item() / ref.abs().max().item() < 1e-4, fn
 
 
+@pytest.mark.parametrize("ep", ["store", "resid", "swiglu"])
+def test_linear_many_tiles_without_k_split(ep):
+    """M large enough that every SM gets whole output tiles: 256-column tiles, no K split
+    (the small-M tests above run the split-K and 128-column paths)."""
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    m, k, n = 2048, 1024, 2560          # 16 x 10 = 160 tiles of 128 x 256
+    _, xp = _planes(m, k, 21)
+    if ep == "swiglu":
+        gate = W.quantize("nvfp4", _weights(n // 2, k, seed=22).cuda())
+        up = W.quantize("nvfp4", _weights(n // 2, k, seed=23).cuda())
+        pw = W.interleave_gate_up(gate, up)
+        ref = torch.nn.functional.silu(_reference(xp, gate)) * _reference(xp, up)
+        out, _ = _linear("b200_linear", xp, pw, _lib.EP_SWIGLU, n_valid=n)
+        got = out[0].double().cpu() + out[1].double().cpu()
+        assert (got - ref).abs().max().item() / ref.abs().max().item() < 1e-4
+        return
+    pw = W.concat_rows([W.quantize("int4", _weights(n, k, seed=24).cuda())])
+    ref = _reference(xp, pw)
+    out, before = _linear("b200_linear", xp, pw, _lib.EP_STORE if ep == "store" else _lib.EP_RESID_ADD)
+    got = out.double().cpu() - (before.double().cpu() if ep == "resid" else 0)
+    assert (got - ref).abs().max().item() < 2e-5 * ref.abs().max().item() + 1e-6
+
+
 def test_linear_large_k_and_m_tail():
     """K = 6144 (the down projection), M not a multiple of the 128-row tile."""
     from strands_decider_b200 import _lib
@@ -205,9 +230,11 @@ def test_linear_rejects_bad_shapes():
 # ----------------------------------------------------------------------------- GDN mixer
 
 
-def test_gdn_mixer_matches_oracle_chunk_rule():
+@pytest.mark.parametrize("batch", ["few", "many"])
+def test_gdn_mixer_matches_oracle_chunk_rule(batch):
     """conv + gating + chunked delta rule + gated norm, ragged sequences, against the
-    oracle's restatement of TF:462-530 on the same bf16 inputs."""
+    oracle's restatement of TF:462-530 on the same bf16 inputs. A few sequences run on
+    clusters of CTAs that split each head's value columns; many run one CTA per head."""
     import torch.nn.functional as F
 
     from oracle import torso as T
@@ -216,7 +243,10 @@ def test_gdn_mixer_matches_oracle_chunk_rule():
     H, dk = 2, 128
     conv_dim, vdim = 3 * H * dk, H * dk
     g = torch.Generator().manual_seed(0)
-    lens = [1, 31, 32, 33, 100]
+    if batch == "few":
+        lens = [1, 31, 32, 33, 100]
+    else:   # 40 sequences x 2 heads: more CTAs than half the SMs
+        lens = [int(x) for x in torch.randint(1, 80, (40,), generator=g)]
     Ttot = sum(lens)
     mix = torch.randn(Ttot, conv_dim + vdim + 2 * H, generator=g)
     ab = mix[:, conv_dim + vdim:]
@@ -346,3 +376,23 @@ def test_attention_matches_reference(with_prefix, hd):
         o = torch.einsum("hts,shd->thd", s.softmax(-1), vr).reshape(n, -1) * torch.sigmoid(gate)
         err = (got[cu[i]:cu[i + 1]] - o).abs().max().item() / o.abs().max().item()
         assert err < 2e-2, (n, P[i], err)
+
+
+@pytest.mark.parametrize("rows,hidden", [(5, 2048), (96, 1024), (3000, 2048), (40, 256)])
+def test_rmsnorm_planes_match_reference(rows, hidden):
+    """Qwen3_5RMSNorm (TF:711-728): x * rsqrt(mean x^2 + eps) * (1 + w), as hi/lo bf16 planes;
+    both the block-per-row (few rows) and warp-per-row kernels."""
+    from strands_decider_b200 import _lib
+
+    g = torch.Generator().manual_seed(rows)
+    x = torch.randn(rows, hidden, generator=g) * 3
+    w = 0.1 * torch.randn(hidden, generator=g)
+    out = torch.zeros(2, rows, hidden, dtype=torch.bfloat16, device="cuda")
+    xd, wd = x.cuda(), w.cuda()
+    _lib.call("b200_rmsnorm", _lib.ptr(xd), rows, hidden, _lib.ptr(wd), 1e-6, _lib.ptr(out), rows * hidden,
+              _lib.stream_ptr())
+    torch.cuda.synchronize()
+    xx = x.double()
+    ref = xx * torch.rsqrt(xx.pow(2).mean(-1, keepdim=True) + 1e-6) * (1 + w.double())
+    got = out[0].double().cpu() + out[1].double().cpu()
+    assert (got - ref).abs().max().item() < 1e-5 * ref.abs().max().item()

@@ -117,6 +117,26 @@ def test_prefix_cache_equals_full_prompt_on_device():
     assert torch.equal(cached.argmax, full.argmax)
 
 
+def test_prefix_cache_equals_full_prompt_with_many_sequences():
+    """The same equivalence with 40 requests (80 suffixes): the GDN layers then run one CTA
+    per (sequence, head) instead of the clusters a few sequences use."""
+    m = _model(config.TINY, seed=2, fmt="nvfp4", max_tokens=8192, slots=40)
+    g = torch.Generator().manual_seed(5)
+    V = config.TINY.vocab
+    reqs = []
+    for _ in range(40):
+        slen = int(torch.randint(1, 90, (1,), generator=g))
+        st = torch.randint(0, V, (slen,), generator=g).tolist()
+        qs = [torch.randint(0, V, (int(n),), generator=g).tolist() for n in torch.randint(1, 40, (2,), generator=g)]
+        reqs.append({"state": st, "questions": qs, "kinds": [1, 2], "n_opts": [3, 3], "opt_ids": [[11, 12, 13]] * 2})
+    cached = m.score_requests(reqs).cpu()
+    rows = [r["state"] + q for r in reqs for q in r["questions"]]
+    n = len(rows)
+    full = m.score_prompts(rows, [[11, 12, 13]] * n, [3] * n, [1, 2] * (n // 2), [1.0] * n).cpu()
+    assert torch.abs(cached.probs - full.probs).max().item() < 1e-3
+    assert torch.equal(cached.argmax, full.argmax)
+
+
 def test_oracle_prefix_path_matches_device_prefix_path():
     """Same requests through the oracle's explicit cache and the device pool."""
     m = _model(config.TINY, seed=1, fmt="nvfp4")
