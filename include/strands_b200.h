@@ -255,6 +255,11 @@ typedef struct b200_model_config {
   int32_t attn_heads, attn_kv_heads, head_dim, rope_dim, max_pos;
   float eps;
   int32_t weight_format;
+  /* Batches of at least this many tokens dequantise each packed weight once per GEMM into a
+   * bf16 [N, K] workspace buffer and run the GEMM on it (the in-kernel unpack would repeat for
+   * every 128-token tile); smaller batches stream the packed tiles. 0 = the library default
+   * (4096), < 0 = never. */
+  int32_t dequant_min_tokens;
 } b200_model_config;
 
 typedef struct b200_layer_weights {

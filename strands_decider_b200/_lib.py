@@ -77,7 +77,8 @@ class ModelConfig(C.Structure):
                 ("layer_kind", C.c_int32 * 64), ("gdn_heads", C.c_int32), ("gdn_dk", C.c_int32),
                 ("gdn_dv", C.c_int32), ("conv_width", C.c_int32), ("attn_heads", C.c_int32),
                 ("attn_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("rope_dim", C.c_int32),
-                ("max_pos", C.c_int32), ("eps", C.c_float), ("weight_format", C.c_int32)]
+                ("max_pos", C.c_int32), ("eps", C.c_float), ("weight_format", C.c_int32),
+                ("dequant_min_tokens", C.c_int32)]
 
 
 class LayerWeights(C.Structure):

@@ -353,8 +353,8 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       // copy that never landed is garbage, and the fault word already reports it
       __syncthreads();
     }
-    if (warp == GDN_THREADS / 32 - 1 && lane < L)  // the chunk's z gate rows, read in step 8
-      bulk_prefetch_l2(a.mix + size_t(tok0 + c0 + lane) * a.ld_mix + conv_dim + h * GD + col0, DV * 4);
+    if (lane < GC / 8 && warp + 8 * lane < L)  // the z gate rows this warp reads in step 8
+      bulk_prefetch_l2(a.mix + size_t(tok0 + c0 + warp + 8 * lane) * a.ld_mix + conv_dim + h * GD + col0, DV * 4);
     // ---- 1. cumulative decay within the chunk
     if (tid < GC) {
       float gj = 0.0f, bj = 0.0f;

@@ -67,6 +67,10 @@ struct b200_model {
       if (cfg.layer_kind[i] == B200_LAYER_GDN) return true;
     return false;
   }
+  bool dequant_at(int T) const {
+    const int from = cfg.dequant_min_tokens == 0 ? 4096 : cfg.dequant_min_tokens;
+    return from > 0 && T >= from;
+  }
   bool has_attn() const {
     for (int i = 0; i < cfg.n_layers; ++i)
       if (cfg.layer_kind[i] == B200_LAYER_ATTN) return true;
@@ -83,8 +87,9 @@ namespace {
 //   act  2 x bf16 [T, act_cols]      mixer outputs / SwiGLU outputs as hi/lo planes (GEMM input)
 //   q, k, v  bf16                    attention scratch (post norm + RoPE)
 //   prep fp32                        GDN scratch (conv / l2norm / gating outputs)
+//   wdq  bf16 [N, K]                 one dequantised weight (batches of >= dequant_min_tokens)
 struct WsLayout {
-  size_t x, xn, mix, act, q, k, v, prep, total;
+  size_t x, xn, mix, act, q, k, v, prep, wdq, total;
   int mix_cols, act_cols;
   long long xn_lo, act_lo;  // element offsets of the lo planes
 };
@@ -117,8 +122,34 @@ WsLayout layout(const b200_model& m, int T) {
   L.k = take(kvb);
   L.v = take(kvb);
   L.prep = take(m.has_gdn() ? size_t(sdb_gdn_prep_floats(c.gdn_heads, T)) * 4 : 16);
+  L.wdq = 0;
+  if (m.dequant_at(T)) {
+    size_t most = 0;
+    for (int i = 0; i < c.n_layers; ++i) {
+      const b200_layer_weights& w = m.layers[i];
+      for (const b200_qweight* q : {&w.mix_in, &w.mix_out, &w.gate_up, &w.down})
+        most = std::max(most, size_t(q->n) * size_t(q->k));
+    }
+    L.wdq = take(most * 2);
+  }
   L.total = off;
   return L;
+}
+
+// One linear layer: for large batches the packed weight is first dequantised into the bf16
+// buffer (bit-exact with the GEMM's own unpack), then the GEMM streams it by TMA.
+int run_linear(const b200_model& m, const uint16_t* x, const uint16_t* x_lo, int T, int k, const b200_qweight& w,
+               const b200_linear_out& o, uint16_t* wdq, b200_stream stream) {
+  if (wdq && m.dequant_at(T) && w.format != B200_W_BF16) {
+    if (int rc = b200_dequantize(&w, wdq, stream)) return rc;
+    b200_qweight wb{};
+    wb.format = B200_W_BF16;
+    wb.n = w.n;
+    wb.k = w.k;
+    wb.data = wdq;
+    return b200_linear(x, x_lo, T, k, k, &wb, &o, stream);
+  }
+  return b200_linear(x, x_lo, T, k, k, &w, &o, stream);
 }
 
 int check_qw(const b200_qweight& w, int n_min, int k, const char* what) {
@@ -235,6 +266,7 @@ extern "C" int b200_model_forward(b200_model* m, const int32_t* ids, const b200_
   uint16_t* kb = reinterpret_cast<uint16_t*>(ws + L.k);
   uint16_t* vb = reinterpret_cast<uint16_t*>(ws + L.v);
   float* prep = reinterpret_cast<float*>(ws + L.prep);
+  uint16_t* wdq = L.wdq ? reinterpret_cast<uint16_t*>(ws + L.wdq) : nullptr;
   const uint16_t* xn_lo = xn + L.xn_lo;
 
   int rc;
@@ -246,25 +278,25 @@ extern "C" int b200_model_forward(b200_model* m, const int32_t* ids, const b200_
     if (c.layer_kind[li] == B200_LAYER_GDN) {
       const int n = m->gdn_in_cols();
       b200_linear_out o{B200_EP_STORE, n, mix, n, 0};
-      if ((rc = b200_linear(xn, xn_lo, T, c.hidden, c.hidden, &w.mix_in, &o, stream))) return rc;
+      if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.mix_in, o, wdq, stream))) return rc;
       if ((rc = sdb_gdn_mixer(&w.gdn, seqs, mix, n, act, L.act_lo, pool, m->kind_index[li], prep, st))) return rc;
       mix_in_dim = m->value_dim();
     } else {
       const int n = m->attn_qkv();
       b200_linear_out o{B200_EP_STORE, n, mix, n, 0};
-      if ((rc = b200_linear(xn, xn_lo, T, c.hidden, c.hidden, &w.mix_in, &o, stream))) return rc;
+      if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.mix_in, o, wdq, stream))) return rc;
       b200_attn_params ap{c.attn_heads, c.attn_kv_heads, c.head_dim, c.rope_dim, c.max_pos, c.eps,
                           w.q_norm, w.k_norm, m->rope_cos, m->rope_sin};
       if ((rc = sdb_attention(&ap, seqs, mix, n, qb, kb, vb, act, L.act_lo, pool, m->kind_index[li], st))) return rc;
       mix_in_dim = m->attn_o_in();
     }
     b200_linear_out r{B200_EP_RESID_ADD, c.hidden, x, c.hidden, 0};
-    if ((rc = b200_linear(act, act + L.act_lo, T, mix_in_dim, mix_in_dim, &w.mix_out, &r, stream))) return rc;
+    if ((rc = run_linear(*m, act, act + L.act_lo, T, mix_in_dim, w.mix_out, r, wdq, stream))) return rc;
     if ((rc = b200_rmsnorm(x, T, c.hidden, w.post_norm, c.eps, xn, L.xn_lo, stream))) return rc;
     b200_linear_out g{B200_EP_SWIGLU, 2 * c.inter, act, c.inter, L.act_lo};
-    if ((rc = b200_linear(xn, xn_lo, T, c.hidden, c.hidden, &w.gate_up, &g, stream))) return rc;
+    if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.gate_up, g, wdq, stream))) return rc;
     b200_linear_out d{B200_EP_RESID_ADD, c.hidden, x, c.hidden, 0};
-    if ((rc = b200_linear(act, act + L.act_lo, T, c.inter, c.inter, &w.down, &d, stream))) return rc;
+    if ((rc = run_linear(*m, act, act + L.act_lo, T, c.inter, w.down, d, wdq, stream))) return rc;
   }
   if (decide && decide->n_rows > 0) {
     if ((rc = sdb_decide_vocab(x, c.hidden, m->final_norm, c.eps, m->embed, decide, c.vocab, T, st))) return rc;

@@ -51,7 +51,10 @@ class Decisions:
 
 class DecisionModel:
     def __init__(self, weights: DeviceWeights, max_tokens: int = 8192, pool_slots: int = 64,
-                 pool_kv_tokens: int | None = None, device: str | torch.device = "cuda"):
+                 pool_kv_tokens: int | None = None, device: str | torch.device = "cuda",
+                 dequant_min_tokens: int = 0):
+        """dequant_min_tokens: batches of at least this many tokens run each GEMM on a bf16 copy
+        of its weight dequantised once per call (0 = the library default, 4096; < 0 = never)."""
         _lib.load()
         self.w = weights
         self.spec = s = weights.spec
@@ -65,6 +68,7 @@ class DecisionModel:
         cfg.attn_heads, cfg.attn_kv_heads, cfg.head_dim = s.attn_heads, s.attn_kv_heads, s.head_dim
         cfg.rope_dim, cfg.max_pos, cfg.eps = s.rope_dim, s.max_positions, s.eps
         cfg.weight_format = _lib.FMT[s.weight_format]
+        cfg.dequant_min_tokens = dequant_min_tokens
         self._cfg = cfg
         h = C.c_void_p()
         _lib.check(_lib.load().b200_model_create(C.byref(cfg), C.byref(h)))

@@ -1,0 +1,95 @@
+"""Why every GEMM input is carried as two bf16 planes (CPU, on the oracle).
+
+The correctness bar is option probabilities within 2e-3 of the reference's fp32 path. On the
+reduced int4 decider and its golden prompts (4 x 256 ids), rounding the inputs of any ONE
+class of linear layers to a single bf16 plane (8 mantissa bits) already moves a probability
+by more than 2e-3, while the hi + lo planes the device uses (about 16 bits) stay far inside
+it. The device kernels therefore split every GEMM input (see csrc/gemm.cu)."""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import head as OH
+from oracle import synth as osynth
+from oracle import torso as OT
+from strands_decider_b200 import config
+
+from tests.conftest import GOLDEN
+
+TOL = 2e-3
+
+
+def _bf16(x: torch.Tensor) -> torch.Tensor:
+    return x.to(torch.bfloat16).float()
+
+
+def _planes(x: torch.Tensor) -> torch.Tensor:
+    hi = _bf16(x)
+    return hi + _bf16(x - hi)
+
+
+class _Linear:
+    """A weight whose `.T` rounds the left operand of `x @ W.T` as its class is told to."""
+
+    def __init__(self, w, cls, mode):
+        self.w, self.cls, self.mode = w, cls, mode
+
+    @property
+    def T(self):
+        return self
+
+    def __rmatmul__(self, x):
+        how = self.mode.get(self.cls)
+        x = _bf16(x) if how == "bf16" else _planes(x) if how == "planes" else x
+        return x @ self.w.T
+
+
+def _wrap(W, mode):
+    for L in W["layers"]:
+        if "gdn" in L:
+            for k in ("qkv", "z", "b", "a"):
+                L["gdn"][k] = _Linear(L["gdn"][k], "in_proj", mode)
+            L["gdn"]["out"] = _Linear(L["gdn"]["out"], "out_proj", mode)
+        else:
+            for k in ("q", "k", "v"):
+                L["attn"][k] = _Linear(L["attn"][k], "in_proj", mode)
+            L["attn"]["o"] = _Linear(L["attn"]["o"], "out_proj", mode)
+        for k in ("gate", "up"):
+            L["mlp"][k] = _Linear(L["mlp"][k], "gate_up", mode)
+        L["mlp"]["down"] = _Linear(L["mlp"]["down"], "down", mode)
+    return W
+
+
+@pytest.fixture(scope="module")
+def case():
+    g = np.load(os.path.join(GOLDEN, "reduced_1024_int4.npz"))
+    spec = config.REDUCED_1024
+    mode: dict[str, str] = {}
+    W = _wrap(osynth.logical_weights(spec, seed=0), mode)
+    return spec, W, mode, g["ids"].astype(np.int64).tolist(), g["opt_ids"].tolist(), torch.from_numpy(g["probs"])
+
+
+def _err(case, how: dict[str, str]) -> float:
+    spec, W, mode, rows, opt, ref = case
+    mode.clear()
+    mode.update(how)
+    cfg = osynth.torso_config(spec)
+    with torch.inference_mode():
+        pooled = torch.stack([OT.forward_sequence(cfg, W, torch.tensor(r))[0][-1] for r in rows])
+        p = OH.decide(pooled, W["embed"], torch.tensor(opt), torch.tensor([3] * len(rows)),
+                      torch.tensor([1.0] * len(rows)))
+    return (p - ref).abs().max().item()
+
+
+def test_split_planes_everywhere_meet_the_bar(case):
+    assert _err(case, {c: "planes" for c in ("in_proj", "out_proj", "gate_up", "down")}) < TOL / 20
+
+
+@pytest.mark.parametrize("cls", ["in_proj", "out_proj", "gate_up", "down"])
+def test_one_bf16_plane_in_any_linear_class_misses_the_bar(case, cls):
+    assert _err(case, {cls: "bf16"}) > TOL
