@@ -175,12 +175,14 @@ def cpu_baseline(spec: config.ModelSpec, wl: config.Workload, n_requests: int = 
 # ----------------------------------------------------------------------------- GPU arm
 
 
-def launches_per_forward(spec: config.ModelSpec, decide: bool) -> int:
+def launches_per_forward(spec: config.ModelSpec, decide: bool, tokens: int = 0) -> int:
     """Kernels one b200_model_forward launches (embed, per layer: 2 norms, 4 GEMMs and the
-    mixer's kernels, then the head)."""
+    mixer's kernels, then the head); forwards of >= 4096 tokens also dequantise each of the
+    4 weights per layer once."""
+    dq = 4 if tokens >= 4096 and spec.weight_format != "bf16" else 0
     n = 1 + (1 if decide else 0)
     for lt in spec.layer_types:
-        n += 2 + 4 + 2  # GDN: prep + chunk kernel; attention: prep + flash kernel
+        n += 2 + 4 + 2 + dq  # GDN: prep + chunk kernel; attention: prep + flash kernel
     return n
 
 
@@ -604,8 +606,9 @@ def main() -> None:
         "linear_tflops": round(fl / (ms * 1e-3) / 1e12 / world, 1),
         "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
                 "d2h_bytes_per_step": d2h // args.steps},
-        "gpu_launches": world * args.steps * ((launches_per_forward(spec, False) if prefix else 0)
-                                              + launches_per_forward(spec, True)),
+        "gpu_launches": sum(((launches_per_forward(spec, False, b.n_state_tokens) if prefix else 0)
+                             + launches_per_forward(spec, True, b.n_suffix_tokens))
+                            for b in (batches[(args.warmup + i) % len(batches)] for i in range(args.steps))) * world,
         "roofline": roof, "clocks": clk, "cpu_baseline": cb,
     }
     print(json.dumps(line), flush=True)

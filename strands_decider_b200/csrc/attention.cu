@@ -123,14 +123,20 @@ __global__ void attn_prep_kernel(const AttnArgs a) {
 }
 
 // ----------------------------------------------------------------------------- flash kernel
-// Tensor-core (mma.sync m16n8k16, bf16 in, fp32 accumulate) flash attention. One CTA = 4
-// warps = 64 queries of one sequence and one query head; each warp owns 16 query rows.
+// Tensor-core (mma.sync m16n8k16, bf16 in, fp32 accumulate) flash attention. One CTA = 64
+// queries of one sequence and one query head, 4 x FA_DG warps: warp w owns query rows
+// 16*(w%4).. and value columns (w/4) * HD/FA_DG ..; the FA_DG warps of a row block each
+// compute the same scores (so they agree on the softmax without talking) and a slice of P V.
 // Keys stream in tiles of 32 (prefix-pool keys first, then the sequence's own), double
 // buffered with cp.async; online softmax in registers; P is fed to the P V product straight
 // from the score accumulators. Shared tiles are row-major with 16-byte chunks XOR-swizzled
 // by row, so ldmatrix reads are conflict-free.
 constexpr int FA_Q = 64;
 constexpr int FA_K = 32;
+// value-column groups: wide heads split P V and the output over two warp groups, which
+// halves each warp's accumulators and doubles the warps that hide latency
+template <int HD>
+constexpr int fa_dg() { return HD >= 128 ? 2 : 1; }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -166,8 +172,9 @@ __device__ __forceinline__ uint32_t sw_off(int r, int c) {
 }
 
 template <int HD>
-__global__ void __launch_bounds__(128) attn_flash_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(128 * fa_dg<HD>(), 2) attn_flash_kernel(const AttnArgs a) {
   constexpr int CH = HD / 8;  // 16-byte chunks per row
+  constexpr int DG = fa_dg<HD>(), NT = 128 * DG, DW = HD / DG;  // DW: value columns per warp
   extern __shared__ uint8_t fa_smem[];
   uint8_t* sQ = fa_smem;                          // [FA_Q][HD]
   uint8_t* sK = sQ + FA_Q * HD * 2;               // [2][FA_K][HD]
@@ -191,14 +198,14 @@ __global__ void __launch_bounds__(128) attn_flash_kernel(const AttnArgs a) {
   const int n_tiles = (n_keys + FA_K - 1) / FA_K;
 
   // Q tile (rows past the sequence are zero)
-  for (int i = tid; i < FA_Q * CH; i += 128) {
+  for (int i = tid; i < FA_Q * CH; i += NT) {
     const int r = i / CH, c = i % CH;
     const bool ok = q0 + r < len;
     const uint16_t* src = a.q_buf + ((size_t(tok0 + q0 + (ok ? r : 0)) * nq + h) * HD) + c * 8;
     cp_async16(sQ + sw_off<HD>(r, c), src, ok);
   }
   auto load_kv = [&](int tile, int buf) {
-    for (int i = tid; i < FA_K * CH; i += 128) {
+    for (int i = tid; i < FA_K * CH; i += NT) {
       const int r = i / CH, c = i % CH;
       const int kk = tile * FA_K + r;
       const bool ok = kk < n_keys;
@@ -218,13 +225,14 @@ __global__ void __launch_bounds__(128) attn_flash_kernel(const AttnArgs a) {
   load_kv(0, 0);
   cp_async_commit();
 
-  float o[HD / 8][4];
+  float o[DW / 8][4];
 #pragma unroll
-  for (int j = 0; j < HD / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  for (int j = 0; j < DW / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
   const float scale = rsqrtf(float(HD));
   const int g = lane >> 2, tq = lane & 3;
-  const int qrow0 = warp * 16;                          // warp's first row in the tile
+  const int qrow0 = (warp & 3) * 16;                    // warp's first row in the tile
+  const int col0 = (warp >> 2) * DW;                    // warp's first value column
   const int qpos0 = P + q0 + qrow0 + g, qpos1 = qpos0 + 8;  // positions of this thread's two rows
   const uint32_t sQa = smem_addr(sQ);
 
@@ -299,7 +307,7 @@ __global__ void __launch_bounds__(128) attn_flash_kernel(const AttnArgs a) {
       l_run[r] = l_run[r] * alpha[r] + rs[r];
     }
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j) {
+    for (int j = 0; j < DW / 8; ++j) {
       o[j][0] *= alpha[0];
       o[j][1] *= alpha[0];
       o[j][2] *= alpha[1];
@@ -310,9 +318,9 @@ __global__ void __launch_bounds__(128) attn_flash_kernel(const AttnArgs a) {
     for (int ks = 0; ks < 2; ++ks) {
       const uint32_t a4[4] = {pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3]};
 #pragma unroll
-      for (int nd = 0; nd < HD / 16; ++nd) {  // 16 value dims per ldmatrix.x4.trans
+      for (int nd = 0; nd < DW / 16; ++nd) {  // 16 value dims per ldmatrix.x4.trans
         uint32_t vb[4];
-        const int r = ks * 16 + (lane & 15), c = nd * 2 + (lane >> 4);
+        const int r = ks * 16 + (lane & 15), c = col0 / 8 + nd * 2 + (lane >> 4);
         ldsm_x4_t(vb, sVa + sw_off<HD>(r, c));
         mma_bf16_16816(o[2 * nd], a4, vb[0], vb[1]);
         mma_bf16_16816(o[2 * nd + 1], a4, vb[2], vb[3]);
@@ -331,8 +339,8 @@ __global__ void __launch_bounds__(128) attn_flash_kernel(const AttnArgs a) {
     const float* gate = a.qkv + t * a.ld_qkv + h * 2 * HD + HD;
     uint16_t* dst = a.out + (t * nq + h) * HD;
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j) {
-      const int d = j * 8 + tq * 2;
+    for (int j = 0; j < DW / 8; ++j) {
+      const int d = col0 + j * 8 + tq * 2;
       const float y0 = o[j][2 * r] * inv[r] * sigmoid(gate[d]);
       const float y1 = o[j][2 * r + 1] * inv[r] * sigmoid(gate[d + 1]);
       const uint16_t h0 = f32_to_bf16_rn(y0), h1 = f32_to_bf16_rn(y1);
@@ -356,7 +364,7 @@ static int launch_attn(const AttnArgs& a, int n_tokens, int n_seqs, int max_len,
     attr = true;
   }
   dim3 grid((max_len + FA_Q - 1) / FA_Q, n_seqs, a.p.heads);
-  attn_flash_kernel<HD><<<grid, 128, smem, st>>>(a);
+  attn_flash_kernel<HD><<<grid, 128 * fa_dg<HD>(), smem, st>>>(a);
   SDB_LAUNCH_CHECK();
   return B200_OK;
 }

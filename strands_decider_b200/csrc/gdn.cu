@@ -113,6 +113,16 @@ __device__ __forceinline__ uint32_t soff(int r, int col) {
   return uint32_t(r * RL * 2 + ((c ^ sw) << 4) + (col & 7) * 2);
 }
 
+// four consecutive values (8-byte aligned offset): one 8-byte store per plane
+__device__ __forceinline__ void split_store4(uint16_t* hi, uint16_t* lo, uint32_t off, float4 v) {
+  const uint16_t h0 = f32_to_bf16_rn(v.x), h1 = f32_to_bf16_rn(v.y), h2 = f32_to_bf16_rn(v.z), h3 = f32_to_bf16_rn(v.w);
+  *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(hi) + off) =
+      make_uint2(uint32_t(h0) | (uint32_t(h1) << 16), uint32_t(h2) | (uint32_t(h3) << 16));
+  *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(lo) + off) =
+      make_uint2(pack_bf16x2(v.x - bf16_to_f32(h0), v.y - bf16_to_f32(h1)),
+                 pack_bf16x2(v.z - bf16_to_f32(h2), v.w - bf16_to_f32(h3)));
+}
+
 __device__ __forceinline__ void split_store(uint16_t* hi, uint16_t* lo, uint32_t off, float a, float b) {
   const uint16_t ha = f32_to_bf16_rn(a), hb = f32_to_bf16_rn(b);
   *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(hi) + off) = uint32_t(ha) | (uint32_t(hb) << 16);
@@ -385,16 +395,12 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       }
       const float bj = sm.beta[j], bke = bj * sm.eG[j];
       const int c = lane * 4;
-      split_store(sm.Qh, sm.Ql, soff<GD>(j, c), q.x, q.y);
-      split_store(sm.Qh, sm.Ql, soff<GD>(j, c + 2), q.z, q.w);
-      split_store(sm.Kh, sm.Kl, soff<GD>(j, c), k.x, k.y);
-      split_store(sm.Kh, sm.Kl, soff<GD>(j, c + 2), k.z, k.w);
-      if (lane < DV / 4) {
-        split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<RW>(j, c), bj * v.x, bj * v.y);
-        split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<RW>(j, c + 2), bj * v.z, bj * v.w);
-      }
-      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<RW>(j, DV + c), bke * k.x, bke * k.y);
-      split_store(sm.ru.r.Rh, sm.ru.r.Rl, soff<RW>(j, DV + c + 2), bke * k.z, bke * k.w);
+      split_store4(sm.Qh, sm.Ql, soff<GD>(j, c), q);
+      split_store4(sm.Kh, sm.Kl, soff<GD>(j, c), k);
+      if (lane < DV / 4)
+        split_store4(sm.ru.r.Rh, sm.ru.r.Rl, soff<RW>(j, c), make_float4(bj * v.x, bj * v.y, bj * v.z, bj * v.w));
+      split_store4(sm.ru.r.Rh, sm.ru.r.Rl, soff<RW>(j, DV + c),
+                   make_float4(bke * k.x, bke * k.y, bke * k.z, bke * k.w));
     }
     __syncthreads();
     if (tid == 0 && c0 + GC < len) {  // every read of the stage is done: fetch the next chunk
