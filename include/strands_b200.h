@@ -235,10 +235,42 @@ typedef struct b200_decide_args {
   int32_t* argmax;
   float* confidence;
   float* score;
+  const int32_t* opt_tok;    /* pointer readout only: [n_rows][kmax] token index (into x) of the last
+                                token of each option's line, -1 past the row's options; else NULL */
 } b200_decide_args;
 
 int b200_decide(const float* x, int32_t hidden, const float* final_norm, float eps, const uint16_t* table,
                 const b200_decide_args* d, b200_stream stream);
+
+/* Trained readouts (modeling.py:99-158, build_head 161-180), used instead of the option-token
+ * logits by checkpoints whose head_type is "slot" or "pointer". Both start from the final
+ * hidden state (the torso's final RMSNorm applied to x) and a LayerNorm(hidden):
+ *   slot:    logits = Linear(hidden -> out)(LN(h_last)), or with mlp_hidden > 0
+ *            Linear(mlp_hidden -> out)(GELU(Linear(hidden -> mlp_hidden)(LN(h_last))))
+ *            (SlotHead.forward, modeling.py:120-121; out = num_slots)
+ *   pointer: logits[k] = k(LN(h_opt_k)) . q(LN(h_last)) * out^-1/2 with q, k: hidden -> out
+ *            and h_opt_k the hidden state at opt_tok[i][k] (PointerHead.forward,
+ *            modeling.py:154-158; gather_options 183-190; out = pointer_dim)
+ * then apply_temperature / masked_log_softmax / the per-kind answers as b200_decide.
+ * Weights are fp32 in nn.Linear layout ([out_features][in_features]). kmax <= 32; slot
+ * heads need out <= 32 (logits past kmax are dropped). */
+enum b200_head_kind { B200_HEAD_OPTION_TOKEN = 0, B200_HEAD_SLOT = 1, B200_HEAD_POINTER = 2 };
+typedef struct b200_readout {
+  int32_t kind;        /* B200_HEAD_SLOT or B200_HEAD_POINTER */
+  int32_t hidden;      /* torso hidden size, <= 4096, a multiple of 32 */
+  int32_t out;         /* slot: number of slots; pointer: the q / k dimension (<= 1024) */
+  int32_t mlp_hidden;  /* slot: width of the GELU layer, 0 for a single linear layer (<= 4096) */
+  float ln_eps;        /* the LayerNorm's eps (nn.LayerNorm default 1e-5) */
+  const float* ln_w;   /* [hidden] */
+  const float* ln_b;   /* [hidden] */
+  const float* w1;     /* slot: [mlp_hidden or out][hidden]; pointer: q.weight [out][hidden] */
+  const float* b1;     /* its bias */
+  const float* w2;     /* slot with mlp_hidden > 0: [out][mlp_hidden]; pointer: k.weight [out][hidden] */
+  const float* b2;     /* its bias */
+} b200_readout;
+
+int b200_decide_readout(const float* x, int32_t hidden, const float* final_norm, float eps, const b200_readout* head,
+                        const b200_decide_args* d, int32_t n_tokens, b200_stream stream);
 
 /* ---------------------------------------------------------------- whole-torso runtime
  * A model context holds the configuration and the device pointers of every weight
@@ -281,6 +313,9 @@ int b200_model_destroy(b200_model* m);
 int b200_model_set_layer(b200_model* m, int32_t layer, const b200_layer_weights* w);
 int b200_model_set_globals(b200_model* m, const uint16_t* embed, const float* final_norm, const float* rope_cos,
                            const float* rope_sin);
+/* A trained readout for the forward's decision head (NULL: the option-token logits). The
+ * struct is copied; its weight pointers must stay valid. */
+int b200_model_set_readout(b200_model* m, const b200_readout* head);
 /* Bytes of workspace b200_model_forward needs for batches up to max_tokens tokens. */
 int b200_model_workspace_bytes(const b200_model* m, int32_t max_tokens, size_t* bytes);
 int b200_model_forward(b200_model* m, const int32_t* ids, const b200_seqs* seqs, const b200_prefix_pool* pool,

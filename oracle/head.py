@@ -58,6 +58,43 @@ def decide(pooled, table, opt_ids, n_opts, temperature):
     return masked_log_softmax(apply_temperature(logits, temperature), n_opts).exp()
 
 
+def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """nn.LayerNorm over the last dim (biased variance), fp32."""
+    mean = x.mean(-1, keepdim=True)
+    var = ((x - mean) ** 2).mean(-1, keepdim=True)
+    return (x - mean) / torch.sqrt(var + eps) * w + b
+
+
+def slot_head(pooled: torch.Tensor, H: dict, eps: float = 1e-5) -> torch.Tensor:
+    """SlotHead.forward (modeling.py:120-121): [B, hidden] -> [B, num_slots]. H holds
+    `norm.weight/bias` and `proj.weight/bias` (one linear) or `proj.0.*`, `proj.2.*` (the
+    Linear -> GELU -> Linear variant, modeling.py:110-116); eval mode, dropout is identity."""
+    h = layer_norm(pooled, H["norm.weight"], H["norm.bias"], eps)
+    if "proj.weight" in H:
+        return h @ H["proj.weight"].T + H["proj.bias"]
+    h = torch.nn.functional.gelu(h @ H["proj.0.weight"].T + H["proj.0.bias"])
+    return h @ H["proj.2.weight"].T + H["proj.2.bias"]
+
+
+def pointer_head(decide_h: torch.Tensor, options: torch.Tensor, H: dict, eps: float = 1e-5) -> torch.Tensor:
+    """PointerHead.forward (modeling.py:154-158): decide [B, hidden], options [B, K, hidden]
+    -> logits [B, K] = k(LN(options)) . q(LN(decide)) * dim^-1/2."""
+    q = layer_norm(decide_h, H["norm.weight"], H["norm.bias"], eps) @ H["q.weight"].T + H["q.bias"]
+    o = layer_norm(options, H["norm.weight"], H["norm.bias"], eps) @ H["k.weight"].T + H["k.bias"]
+    return (o @ q.unsqueeze(-1)).squeeze(-1) * q.shape[-1] ** -0.5
+
+
+def gather_options(hidden: torch.Tensor, opt_idx: torch.Tensor) -> torch.Tensor:
+    """modeling.py:183-190: hidden [B, L, d] + opt_idx [B, K] (-1 pads) -> [B, K, d]."""
+    idx = opt_idx.clamp_min(0).unsqueeze(-1).expand(-1, -1, hidden.size(-1))
+    return hidden.gather(1, idx)
+
+
+def decide_from_logits(logits: torch.Tensor, n_opts: torch.Tensor, temperature: torch.Tensor) -> torch.Tensor:
+    """apply_temperature -> masked_log_softmax -> exp (modeling.py:463-468)."""
+    return masked_log_softmax(apply_temperature(logits, temperature), n_opts).exp()
+
+
 def derive_confidence(p: list[float]) -> float:
     """schema.py:185-198."""
     n = len(p)

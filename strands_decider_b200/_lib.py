@@ -69,7 +69,16 @@ class DecideArgs(C.Structure):
     _fields_ = [("n_rows", C.c_int32), ("kmax", C.c_int32), ("last_tok", C.c_void_p), ("opt_ids", C.c_void_p),
                 ("n_opts", C.c_void_p), ("kinds", C.c_void_p), ("temperature", C.c_void_p),
                 ("ordinal_smoothing", C.c_float), ("probs", C.c_void_p), ("argmax", C.c_void_p),
-                ("confidence", C.c_void_p), ("score", C.c_void_p)]
+                ("confidence", C.c_void_p), ("score", C.c_void_p), ("opt_tok", C.c_void_p)]
+
+
+HEAD_OPTION_TOKEN, HEAD_SLOT, HEAD_POINTER = 0, 1, 2
+
+
+class Readout(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("hidden", C.c_int32), ("out", C.c_int32), ("mlp_hidden", C.c_int32),
+                ("ln_eps", C.c_float), ("ln_w", C.c_void_p), ("ln_b", C.c_void_p), ("w1", C.c_void_p),
+                ("b1", C.c_void_p), ("w2", C.c_void_p), ("b2", C.c_void_p)]
 
 
 class ModelConfig(C.Structure):
@@ -109,10 +118,12 @@ _SIGS = {
     "b200_attention_noalloc": ([C.POINTER(AttnParams), C.POINTER(Seqs), _P, _I, _P, C.c_int64,
                                 C.POINTER(PrefixPool), _I, _P], C.c_int),
     "b200_decide": ([_P, _I, _P, C.c_float, _P, C.POINTER(DecideArgs), _P], C.c_int),
+    "b200_decide_readout": ([_P, _I, _P, C.c_float, C.POINTER(Readout), C.POINTER(DecideArgs), _I, _P], C.c_int),
     "b200_model_create": ([C.POINTER(ModelConfig), C.POINTER(C.c_void_p)], C.c_int),
     "b200_model_destroy": ([_P], C.c_int),
     "b200_model_set_layer": ([_P, _I, C.POINTER(LayerWeights)], C.c_int),
     "b200_model_set_globals": ([_P, _P, _P, _P, _P], C.c_int),
+    "b200_model_set_readout": ([_P, C.POINTER(Readout)], C.c_int),
     "b200_model_workspace_bytes": ([_P, _I, C.POINTER(C.c_size_t)], C.c_int),
     "b200_model_forward": ([_P, _P, C.POINTER(Seqs), C.POINTER(PrefixPool), C.POINTER(DecideArgs), _P,
                             C.c_size_t, _P], C.c_int),

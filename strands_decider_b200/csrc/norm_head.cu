@@ -1,4 +1,6 @@
 // Embedding lookup, RMSNorm, and the fused option-token decision head.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace sdb {
@@ -208,9 +210,213 @@ __global__ void decide_kernel(const float* __restrict__ x, int hidden, const flo
   }
 }
 
+// ----------------------------------------------------------------------------- trained readouts
+constexpr int HEAD_THREADS = 256;
+constexpr int HEAD_KMAX = 32;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < HEAD_THREADS / 32; ++i) t += red[i];
+  return t;
+}
+
+// v = LayerNorm(RMSNorm_final(x[t])) into shared memory (SlotHead / PointerHead norm of the
+// torso's final hidden state, modeling.py:120-121, 154-157); every thread returns after v is
+// complete.
+__device__ void head_input(const float* __restrict__ x, int hidden, const float* __restrict__ fnorm, float eps,
+                           const b200_readout& hd, int t, float* v, float* red) {
+  const float* xr = x + size_t(t) * hidden;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < hidden; i += HEAD_THREADS) {
+    const float xv = xr[i];
+    v[i] = xv;
+    ss += xv * xv;
+  }
+  const float r = rsqrtf(block_sum(ss, red) / float(hidden) + eps);
+  float s1 = 0.0f;
+  for (int i = threadIdx.x; i < hidden; i += HEAD_THREADS) {
+    const float hv = v[i] * r * (1.0f + fnorm[i]);
+    v[i] = hv;
+    s1 += hv;
+  }
+  const float mean = block_sum(s1, red) / float(hidden);
+  float s2 = 0.0f;
+  for (int i = threadIdx.x; i < hidden; i += HEAD_THREADS) {
+    const float dv = v[i] - mean;
+    s2 += dv * dv;
+  }
+  const float rs = rsqrtf(block_sum(s2, red) / float(hidden) + hd.ln_eps);
+  for (int i = threadIdx.x; i < hidden; i += HEAD_THREADS) v[i] = (v[i] - mean) * rs * hd.ln_w[i] + hd.ln_b[i];
+  __syncthreads();
+}
+
+// y[o] = b[o] + W[o, :] . v for o < n_out (W [n_out][n_in], nn.Linear layout): warp per
+// output row, lanes across the input; gelu applies the exact-erf GELU (nn.GELU default).
+__device__ void head_linear(const float* __restrict__ w, const float* __restrict__ b, const float* v, int n_in,
+                           int n_out, float* y, bool gelu) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int o = warp; o < n_out; o += HEAD_THREADS / 32) {
+    const float* wr = w + size_t(o) * n_in;
+    float acc = 0.0f;
+    for (int i = lane; i < n_in; i += 32) acc = fmaf(wr[i], v[i], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      float yv = acc + b[o];
+      if (gelu) yv = 0.5f * yv * (1.0f + erff(yv * 0.70710678118654752f));
+      y[o] = yv;
+    }
+  }
+  __syncthreads();
+}
+
+// temperature, masked softmax over the first n of kmax slots, per-kind answers (the same
+// read-back as decide_kernel); run by one thread.
+__device__ void head_answers(const b200_decide_args& d, int row, const float* logit, int n) {
+  const float temp = fmaxf(d.temperature[row], 1e-6f);
+  float mx = -INFINITY;
+  for (int k = 0; k < n; ++k) mx = fmaxf(mx, logit[k] / temp);
+  float p[HEAD_KMAX], sum = 0.0f;
+  for (int k = 0; k < HEAD_KMAX; ++k) {
+    p[k] = k < n ? __expf(logit[k] / temp - mx) : 0.0f;
+    sum += p[k];
+  }
+  int best = 0;
+  float pmax = -1.0f, mean = 0.0f;
+  for (int k = 0; k < HEAD_KMAX; ++k) {
+    p[k] = sum > 0.0f ? p[k] / sum : 0.0f;
+    if (k < n && p[k] > pmax) {
+      pmax = p[k];
+      best = k;
+    }
+    mean += float(k) * p[k];
+  }
+  for (int k = 0; k < d.kmax; ++k) d.probs[row * d.kmax + k] = p[k];
+  float conf, score;
+  const int kind = d.kinds[row];
+  if (kind == 0) {  // noul: P(true) is slot 1 (prompting.py:27, 153-156)
+    score = n > 1 ? p[1] : 0.0f;
+    conf = fabsf(2.0f * score - 1.0f);
+  } else if (kind == 1) {  // choice: schema.py:185-198
+    score = float(best);
+    conf = n <= 1 ? 1.0f : fminf(1.0f, fmaxf(0.0f, (float(n) * pmax - 1.0f) / float(n - 1)));
+  } else {  // score: expected level and schema.py:141-182
+    float tot = 0.0f, m2 = 0.0f, var = 0.0f;
+    for (int k = 0; k < n; ++k) tot += p[k];
+    for (int k = 0; k < n; ++k) m2 += float(k) * (p[k] / tot);
+    for (int k = 0; k < n; ++k) var += (p[k] / tot) * (float(k) - m2) * (float(k) - m2);
+    score = mean;
+    const float sigma = sqrtf(var), smax = float(n - 1) * 0.5f;
+    const float floor_ = d.ordinal_smoothing > 0.0f ? sqrtf(d.ordinal_smoothing) : 0.0f;
+    if (n <= 1)
+      conf = 1.0f;
+    else if (tot <= 0.0f)
+      conf = 0.0f;
+    else if (smax <= floor_)
+      conf = sigma <= floor_ ? 1.0f : 0.0f;
+    else
+      conf = fminf(1.0f, fmaxf(0.0f, (smax - sigma) / (smax - floor_)));
+  }
+  d.argmax[row] = best;
+  d.confidence[row] = conf;
+  d.score[row] = score;
+}
+
+// One CTA per decision row. Shared memory: v [hidden] | y [max(out, mlp_hidden)] | q [out] |
+// logits [32] | reduction scratch [8].
+__global__ void __launch_bounds__(HEAD_THREADS) head_decide_kernel(const float* __restrict__ x, int hidden,
+                                                                    const float* __restrict__ fnorm, float eps,
+                                                                    b200_readout hd, b200_decide_args d, int n_tokens,
+                                                                    int ybuf) {
+  extern __shared__ float hsm[];
+  float* v = hsm;
+  float* y = v + hidden;
+  float* q = y + ybuf;
+  float* logit = q + hd.out;
+  float* red = logit + HEAD_KMAX;
+  const int row = blockIdx.x;
+  int tok = d.last_tok[row];
+  if (tok < 0 || tok >= n_tokens) {
+    if (threadIdx.x == 0) raise_fault(FAULT_BAD_INDEX);
+    tok = 0;
+  }
+  const int n = min(min(d.n_opts[row], d.kmax), hd.kind == B200_HEAD_SLOT ? hd.out : HEAD_KMAX);
+  head_input(x, hidden, fnorm, eps, hd, tok, v, red);
+  if (hd.kind == B200_HEAD_SLOT) {
+    if (hd.mlp_hidden > 0) {
+      head_linear(hd.w1, hd.b1, v, hidden, hd.mlp_hidden, y, true);
+      head_linear(hd.w2, hd.b2, y, hd.mlp_hidden, min(hd.out, d.kmax), logit, false);
+    } else {
+      head_linear(hd.w1, hd.b1, v, hidden, min(hd.out, d.kmax), logit, false);
+    }
+  } else {  // pointer
+    head_linear(hd.w1, hd.b1, v, hidden, hd.out, q, false);
+    const float scale = rsqrtf(float(hd.out));
+    for (int k = 0; k < n; ++k) {
+      int t = d.opt_tok[row * d.kmax + k];
+      if (t < 0 || t >= n_tokens) {
+        if (threadIdx.x == 0) raise_fault(FAULT_BAD_INDEX);
+        t = 0;
+      }
+      head_input(x, hidden, fnorm, eps, hd, t, v, red);
+      head_linear(hd.w2, hd.b2, v, hidden, hd.out, y, false);
+      float part = 0.0f;
+      for (int i = threadIdx.x; i < hd.out; i += HEAD_THREADS) part = fmaf(y[i], q[i], part);
+      const float dot = block_sum(part, red);
+      if (threadIdx.x == 0) logit[k] = dot * scale;
+      __syncthreads();
+    }
+  }
+  if (threadIdx.x == 0) head_answers(d, row, logit, n);
+}
+
+int sdb_check_readout(const b200_readout* hd, int hidden) {
+  if (!hd || !hd->ln_w || !hd->ln_b || !hd->w1 || !hd->b1) return sdb_fail(B200_ERR_ARG, "readout: null weight");
+  if (hd->kind != B200_HEAD_SLOT && hd->kind != B200_HEAD_POINTER)
+    return sdb_fail(B200_ERR_ARG, "readout: kind must be B200_HEAD_SLOT or B200_HEAD_POINTER");
+  if (hd->hidden != hidden || hidden > 4096 || hidden % 32 != 0)
+    return sdb_fail(B200_ERR_SHAPE, "readout: hidden must match the torso (<= 4096, a multiple of 32)");
+  if (hd->out <= 0 || hd->out > 1024 || hd->mlp_hidden < 0 || hd->mlp_hidden > 4096)
+    return sdb_fail(B200_ERR_SHAPE, "readout: out must be 1..1024 and mlp_hidden 0..4096");
+  if (hd->kind == B200_HEAD_POINTER && (!hd->w2 || !hd->b2 || hd->mlp_hidden != 0))
+    return sdb_fail(B200_ERR_ARG, "readout: a pointer head needs k weights and no mlp_hidden");
+  if (hd->kind == B200_HEAD_SLOT && hd->mlp_hidden > 0 && (!hd->w2 || !hd->b2))
+    return sdb_fail(B200_ERR_ARG, "readout: a slot head with mlp_hidden needs its second layer");
+  return B200_OK;
+}
+
+int sdb_decide_readout(const float* x, int32_t hidden, const float* final_norm, float eps, const b200_readout* hd,
+                       const b200_decide_args* d, int n_tokens, cudaStream_t st) {
+  if (!x || !final_norm || !d) return sdb_fail(B200_ERR_ARG, "b200_decide_readout: null pointer");
+  if (int rc = sdb_check_readout(hd, hidden)) return rc;
+  if (d->n_rows <= 0) return B200_OK;
+  if (d->kmax < 1 || d->kmax > HEAD_KMAX) return sdb_fail(B200_ERR_SHAPE, "b200_decide_readout: kmax must be 1..32");
+  if (!d->last_tok || !d->n_opts || !d->kinds || !d->temperature || !d->probs || !d->argmax || !d->confidence ||
+      !d->score)
+    return sdb_fail(B200_ERR_ARG, "b200_decide_readout: null array");
+  if (hd->kind == B200_HEAD_POINTER && !d->opt_tok)
+    return sdb_fail(B200_ERR_ARG, "b200_decide_readout: a pointer head needs opt_tok (option token positions)");
+  const int ybuf = std::max(hd->out, hd->mlp_hidden);
+  const size_t smem = size_t(hidden + ybuf + hd->out + HEAD_KMAX + 8) * 4;  // <= 37 KB by the checks above
+  head_decide_kernel<<<d->n_rows, HEAD_THREADS, smem, st>>>(x, hidden, final_norm, eps, *hd, *d, n_tokens, ybuf);
+  SDB_LAUNCH_CHECK();
+  return B200_OK;
+}
+
 }  // namespace sdb
 
 using namespace sdb;
+
+extern "C" int b200_decide_readout(const float* x, int32_t hidden, const float* final_norm, float eps,
+                                   const b200_readout* head, const b200_decide_args* d, int32_t n_tokens,
+                                   b200_stream stream) {
+  if (n_tokens <= 0) return sdb_fail(B200_ERR_SHAPE, "b200_decide_readout: n_tokens must be positive");
+  return sdb_decide_readout(x, hidden, final_norm, eps, head, d, n_tokens, reinterpret_cast<cudaStream_t>(stream));
+}
 
 extern "C" int b200_embed(const int32_t* ids, int32_t n_tokens, const uint16_t* table, int32_t hidden, float* x,
                           b200_stream stream) {

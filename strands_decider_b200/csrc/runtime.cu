@@ -26,6 +26,11 @@ int sdb_decide_vocab(const float* x, int32_t hidden, const float* final_norm, fl
 int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix, int32_t ld_mix, uint16_t* out,
                   int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, float* prep, cudaStream_t st);
 int sdb_gdn_prep_floats(int heads, int n_tokens);
+namespace sdb {
+int sdb_check_readout(const b200_readout* hd, int hidden);
+int sdb_decide_readout(const float* x, int32_t hidden, const float* final_norm, float eps, const b200_readout* hd,
+                       const b200_decide_args* d, int n_tokens, cudaStream_t st);
+}  // namespace sdb
 int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qkv, int32_t ld_qkv, uint16_t* q_buf,
                   uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool,
                   int32_t layer, cudaStream_t st);
@@ -52,6 +57,7 @@ struct b200_model {
   const float* final_norm = nullptr;
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
+  b200_readout readout{};  // kind B200_HEAD_OPTION_TOKEN (0): the option-token logits
 
   int key_dim() const { return cfg.gdn_heads * cfg.gdn_dk; }
   int value_dim() const { return cfg.gdn_heads * cfg.gdn_dv; }
@@ -236,6 +242,17 @@ extern "C" int b200_model_set_globals(b200_model* m, const uint16_t* embed, cons
   return B200_OK;
 }
 
+extern "C" int b200_model_set_readout(b200_model* m, const b200_readout* head) {
+  if (!m) return sdb_fail(B200_ERR_ARG, "b200_model_set_readout: null model");
+  if (!head) {
+    m->readout = b200_readout{};
+    return B200_OK;
+  }
+  if (int rc = sdb::sdb_check_readout(head, m->cfg.hidden)) return rc;
+  m->readout = *head;
+  return B200_OK;
+}
+
 extern "C" int b200_model_workspace_bytes(const b200_model* m, int32_t max_tokens, size_t* bytes) {
   if (!m || !bytes || max_tokens <= 0) return sdb_fail(B200_ERR_ARG, "b200_model_workspace_bytes: bad argument");
   *bytes = layout(*m, max_tokens).total;
@@ -299,7 +316,11 @@ extern "C" int b200_model_forward(b200_model* m, const int32_t* ids, const b200_
     if ((rc = run_linear(*m, act, act + L.act_lo, T, c.inter, w.down, d, wdq, stream))) return rc;
   }
   if (decide && decide->n_rows > 0) {
-    if ((rc = sdb_decide_vocab(x, c.hidden, m->final_norm, c.eps, m->embed, decide, c.vocab, T, st))) return rc;
+    if (m->readout.kind != B200_HEAD_OPTION_TOKEN) {
+      if ((rc = sdb::sdb_decide_readout(x, c.hidden, m->final_norm, c.eps, &m->readout, decide, T, st))) return rc;
+    } else if ((rc = sdb_decide_vocab(x, c.hidden, m->final_norm, c.eps, m->embed, decide, c.vocab, T, st))) {
+      return rc;
+    }
   }
   return B200_OK;
 }

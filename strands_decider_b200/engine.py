@@ -92,6 +92,31 @@ class B200SlotProbs:
                     f"option numbers; split the question")
         return [ids[:n] for n in n_slots]
 
+    def _head_type(self) -> str:
+        """The checkpoint's readout: "slot" / "pointer" (a trained head, modeling.py:161-180) or
+        "option_token" (the torso's own option-number logits)."""
+        ht = getattr(self.model.config, "head_type", "option_token")
+        if ht in ("slot", "pointer") and self._rt.readout is None:
+            head = getattr(self.model, "head", None)
+            if head is None:
+                raise RuntimeError(f"head_type {ht!r} needs the trained head's weights: call "
+                                   "DecisionModel.set_readout(DeviceReadout(...)) first")
+            from .readout import DeviceReadout
+
+            self._rt.set_readout(DeviceReadout.from_module(head, ht, self._rt.spec.hidden, self._rt.device))
+        return ht
+
+    def _readout_args(self, rendered: Any, n_slots: list[int], base: int) -> dict:
+        """opt_ids for the option-token readout, opt_pos for a pointer head, nothing for a slot head."""
+        ht = self._head_type()
+        if ht == "pointer":
+            if rendered is None:
+                raise ValueError("a pointer head needs the rendered questions (option spans)")
+            return {"opt_ids": None, "opt_pos": self._option_idx(rendered, base).tolist()}
+        if ht == "slot":
+            return {"opt_ids": None}
+        return {"opt_ids": self._option_rows(n_slots)}
+
     def _temps(self, kinds: list[str]) -> list[float]:
         t = self._temperatures(kinds)
         return [float(x) for x in (t.tolist() if isinstance(t, torch.Tensor) else t)]
@@ -101,8 +126,9 @@ class B200SlotProbs:
         """infer.py:253-279 on the device: every (state + question) forwarded whole."""
         s, q = self._fit(state_text, question_texts)
         rows = [s + qi for qi in q]
-        dec = self._rt.score_prompts(rows, self._option_rows(n_slots), n_slots, kinds, self._temps(kinds),
-                                     getattr(self.model.config, "ordinal_smoothing", 0.0))
+        ra = self._readout_args(rendered, n_slots, len(s))   # full prompts: options sit after the state
+        dec = self._rt.score_prompts(rows, ra["opt_ids"], n_slots, kinds, self._temps(kinds),
+                                     getattr(self.model.config, "ordinal_smoothing", 0.0), opt_pos=ra.get("opt_pos"))
         return dec.probs.float().cpu(), sum(len(r) for r in rows)
 
     def _slot_probs_shared_prefix(self, state_text: str, question_texts: list[str], n_slots: list[int],
@@ -110,9 +136,10 @@ class B200SlotProbs:
         """infer.py:281-337 on the device: the state once into a pool slot, every suffix
         against it in place (no `_expand_cache` copies)."""
         s, q = self._fit(state_text, question_texts)
+        ra = self._readout_args(rendered, n_slots, 0)         # suffix-relative positions
         self._rt.prefill_states([s], [0])
-        dec = self._rt.score_suffixes(q, [0] * len(q), self._option_rows(n_slots), n_slots, kinds,
-                                      self._temps(kinds), getattr(self.model.config, "ordinal_smoothing", 0.0))
+        dec = self._rt.score_suffixes(q, [0] * len(q), ra["opt_ids"], n_slots, kinds, self._temps(kinds),
+                                      getattr(self.model.config, "ordinal_smoothing", 0.0), opt_pos=ra.get("opt_pos"))
         return dec.probs.float().cpu(), len(s) + sum(len(x) for x in q)
 
 
@@ -157,6 +184,25 @@ class B200Engine(B200SlotProbs):
         s = self.tok(state_text, add_special_tokens=True, truncation=True,
                      max_length=max(1, max_len - reserve))["input_ids"]
         return s, q
+
+    def _option_idx(self, rendered: list, base: int) -> torch.Tensor:
+        """infer.py:221-237 / 414-441: the last token of each option's line, from the offsets
+        `_fit` kept (front truncation included), offset by `base`; -1 pads."""
+        rows = []
+        for rq, offs in zip(rendered, self._last_offsets, strict=True):
+            out = []
+            for s0, e0 in rq.option_spans:
+                last = -1
+                for j, (lo, hi) in enumerate(offs):
+                    if hi > lo and lo >= s0 and hi <= e0:
+                        last = j
+                if last < 0:
+                    raise ValueError(f"option span ({s0},{e0}) has no tokens left; the prompt was truncated "
+                                     "through its option list")
+                out.append(last)
+            rows.append(out)
+        width = max(len(r) for r in rows)
+        return torch.tensor([[base + i for i in r] + [-1] * (width - len(r)) for r in rows], dtype=torch.long)
 
     def evaluate(self, request: Any) -> Any:
         """infer.py:341-408 (needs strands_decider's prompting and schema modules)."""

@@ -85,6 +85,7 @@ class DecisionModel:
         _lib.check(_lib.load().b200_model_workspace_bytes(h, max_tokens, C.byref(nbytes)))
         self.workspace = torch.empty(int(nbytes.value), dtype=torch.uint8, device=self.device)
         self._alloc_pool(pool_slots, pool_kv_tokens or pool_slots * 512)
+        self.readout = None
 
     # ------------------------------------------------------------------ pool
     def _alloc_pool(self, slots: int, kv_tokens: int) -> None:
@@ -134,7 +135,8 @@ class DecisionModel:
             dec = _lib.DecideArgs(R, kmax, _lib.ptr(decide["last_tok"]), _lib.ptr(decide["opt_ids"]),
                                   _lib.ptr(decide["n_opts"]), _lib.ptr(decide["kinds"]), _lib.ptr(decide["temps"]),
                                   float(decide.get("ordinal_smoothing", 0.0)), _lib.ptr(out.probs),
-                                  _lib.ptr(out.argmax), _lib.ptr(out.confidence), _lib.ptr(out.score))
+                                  _lib.ptr(out.argmax), _lib.ptr(out.confidence), _lib.ptr(out.score),
+                                  _lib.ptr(decide["opt_tok"]) if decide.get("opt_tok") is not None else None)
         _lib.check(_lib.load().b200_model_forward(
             self._h, _lib.ptr(ids), C.byref(seqs), C.byref(self._pool), C.byref(dec) if dec is not None else None,
             _lib.ptr(self.workspace), self.workspace.numel(), _lib.stream_ptr(stream)))
@@ -159,21 +161,58 @@ class DecisionModel:
             cu.append(len(flat))
         return flat, cu
 
-    def _decide_dict(self, last_tok, opt_ids, n_opts, kinds, temps, ordinal_smoothing=0.0) -> dict:
-        kmax = max(max(len(o) for o in opt_ids), 1)
-        if kmax > 16:
-            raise ValueError("the option-token head reads at most 16 options")
-        padded = [list(o) + [0] * (kmax - len(o)) for o in opt_ids]
-        return {"last_tok": self._dev(last_tok), "opt_ids": self._dev(padded), "n_opts": self._dev(n_opts),
-                "kinds": self._dev([KIND.get(k, k) if isinstance(k, str) else int(k) for k in kinds]),
-                "temps": self._dev(temps, torch.float32), "ordinal_smoothing": ordinal_smoothing}
+    def _decide_dict(self, last_tok, opt_ids, n_opts, kinds, temps, ordinal_smoothing=0.0, opt_pos=None,
+                     cu=None) -> dict:
+        """Device decide arguments. With the option-token readout, opt_ids are each row's option
+        token ids (<= 16). With a trained readout (set_readout) opt_ids are unused; a pointer
+        head needs opt_pos: per row, the positions of its options' last tokens within the row's
+        own sequence (row i is tokens cu[i] .. cu[i+1] - 1 of the batch)."""
+        d = {"last_tok": self._dev(last_tok), "n_opts": self._dev(n_opts),
+             "kinds": self._dev([KIND.get(k, k) if isinstance(k, str) else int(k) for k in kinds]),
+             "temps": self._dev(temps, torch.float32), "ordinal_smoothing": ordinal_smoothing}
+        if self.readout is None:
+            kmax = max(max(len(o) for o in opt_ids), 1)
+            if kmax > 16:
+                raise ValueError("the option-token head reads at most 16 options")
+            d["opt_ids"] = self._dev([list(o) + [0] * (kmax - len(o)) for o in opt_ids])
+            return d
+        kmax = max(max(n_opts), 1)
+        if kmax > 32 or (self.readout.kind == "slot" and kmax > self.readout.out):
+            raise ValueError(f"question has {kmax} options; this readout scores at most "
+                             f"{32 if self.readout.kind == 'pointer' else min(32, self.readout.out)}")
+        d["opt_ids"] = torch.zeros(len(n_opts), kmax, dtype=torch.int32, device=self.device)
+        if self.readout.kind == "pointer":
+            if opt_pos is None:
+                raise ValueError("a pointer readout needs the option token positions (opt_pos)")
+            rows = []
+            for i, ps in enumerate(opt_pos):
+                if len(ps) < n_opts[i]:
+                    raise ValueError(f"row {i}: {n_opts[i]} options but {len(ps)} option positions")
+                n_i = cu[i + 1] - cu[i]
+                if any(not 0 <= int(p) < n_i for p in ps[: n_opts[i]]):
+                    raise ValueError(f"row {i}: an option position lies outside the forwarded sequence "
+                                     f"of {n_i} tokens (with a cached state, positions count from the suffix)")
+                rows.append([cu[i] + int(p) if int(p) >= 0 else -1 for p in ps[:kmax]]
+                            + [-1] * (kmax - min(len(ps), kmax)))
+            d["opt_tok"] = self._dev(rows)
+        return d
+
+    def set_readout(self, readout) -> None:
+        """Use a trained readout (readout.DeviceReadout) for the decision head; None returns to
+        the option-token logits. The readout's weights must stay alive while it is set."""
+        if readout is not None and readout.hidden != self.spec.hidden:
+            raise ValueError("readout hidden size does not match the model")
+        r = readout.struct() if readout is not None else None
+        _lib.check(_lib.load().b200_model_set_readout(self._h, C.byref(r) if r is not None else None))
+        self.readout = readout
 
     # ------------------------------------------------------------------ the two reference paths
     def score_prompts(self, rows: list[list[int]], opt_ids, n_opts, kinds, temps, ordinal_smoothing=0.0,
-                      stream=None) -> Decisions:
+                      stream=None, opt_pos=None) -> Decisions:
         """Full-prompt path: every row is a whole (state + question) prompt."""
         flat, cu = self._pack(rows)
-        d = self._decide_dict([c - 1 for c in cu[1:]], opt_ids, n_opts, kinds, temps, ordinal_smoothing)
+        d = self._decide_dict([c - 1 for c in cu[1:]], opt_ids, n_opts, kinds, temps, ordinal_smoothing, opt_pos,
+                              cu)
         return self.forward(self._dev(flat), self._dev(cu), decide=d, max_len=max(map(len, rows)), stream=stream)
 
     def prefill_states(self, states: list[list[int]], slots: list[int], stream=None) -> None:
@@ -191,10 +230,12 @@ class DecisionModel:
                      stream=stream)
 
     def score_suffixes(self, suffixes: list[list[int]], slots: list[int], opt_ids, n_opts, kinds, temps,
-                       ordinal_smoothing=0.0, stream=None) -> Decisions:
-        """Forward question suffixes against their states' pool slots and decide."""
+                       ordinal_smoothing=0.0, stream=None, opt_pos=None) -> Decisions:
+        """Forward question suffixes against their states' pool slots and decide (opt_pos, for a
+        pointer readout, are positions within each suffix)."""
         flat, cu = self._pack(suffixes)
-        d = self._decide_dict([c - 1 for c in cu[1:]], opt_ids, n_opts, kinds, temps, ordinal_smoothing)
+        d = self._decide_dict([c - 1 for c in cu[1:]], opt_ids, n_opts, kinds, temps, ordinal_smoothing, opt_pos,
+                              cu)
         return self.forward(self._dev(flat), self._dev(cu), prefix_slot=self._dev(slots), decide=d,
                             max_len=max(map(len, suffixes)), stream=stream)
 

@@ -107,3 +107,30 @@ def request_batch(w: Workload, vocab: int, first: int = 0, count: int | None = N
         out.append({"state": state, "questions": qs, "kinds": kinds, "n_opts": nopts,
                     "opt_ids": [[11 + j for j in range(k)] for k in nopts]})
     return out
+
+
+# ----------------------------------------------------------------------------- readouts
+
+
+def readout_params(kind: str, hidden: int, out: int, mlp_hidden: int = 0, seed: int = 0) -> dict[str, torch.Tensor]:
+    """Seeded weights of a trained readout under the reference's parameter names
+    (SlotHead / PointerHead, src/strands_decider/modeling.py:99-158): LayerNorm weight 1 +
+    N(0, 0.1) and bias N(0, 0.1); linear weights N(0, in^-1/2), biases N(0, 0.02).
+    kind "slot" (out = num_slots, optional GELU layer of mlp_hidden) or "pointer" (out = dim)."""
+    def n(name, shape, std):
+        return randn(seed, f"readout.{name}", shape, "cpu", std)
+
+    W = {"norm.weight": 1.0 + n("norm.weight", (hidden,), 0.1), "norm.bias": n("norm.bias", (hidden,), 0.1)}
+    if kind == "pointer":
+        for p in ("q", "k"):
+            W[f"{p}.weight"] = n(f"{p}.weight", (out, hidden), hidden ** -0.5)
+            W[f"{p}.bias"] = n(f"{p}.bias", (out,), 0.02)
+    elif mlp_hidden > 0:
+        W["proj.0.weight"] = n("proj.0.weight", (mlp_hidden, hidden), hidden ** -0.5)
+        W["proj.0.bias"] = n("proj.0.bias", (mlp_hidden,), 0.02)
+        W["proj.2.weight"] = n("proj.2.weight", (out, mlp_hidden), mlp_hidden ** -0.5)
+        W["proj.2.bias"] = n("proj.2.bias", (out,), 0.02)
+    else:
+        W["proj.weight"] = n("proj.weight", (out, hidden), hidden ** -0.5)
+        W["proj.bias"] = n("proj.bias", (out,), 0.02)
+    return W

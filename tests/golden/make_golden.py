@@ -13,7 +13,10 @@ What runs is the reference's own code, unmodified:
     option tokens (`frozen_slot_log_probs`, `modeling.py:412-438`), on the full-prompt
     path (`infer.py:253-279`), right-padded as `SystemOneEngine._pad` does;
   * the answer formulas `derive_confidence` / `derive_score_confidence` (`schema.py`);
-  * transformers' `torch_chunk_gated_delta_rule` with an initial state (`TF:234-311`).
+  * transformers' `torch_chunk_gated_delta_rule` with an initial state (`TF:234-311`);
+  * the trained readouts `SlotHead` / `PointerHead` with `gather_options`
+    (`modeling.py:99-190`) on the tiny torso's hidden states (`--readouts-only` regenerates
+    just that fixture).
 
 The fixtures are small .npz files committed beside this script; the tests read only
 them (the reference is not present where the GPU tests run).
@@ -110,8 +113,61 @@ def reference_probs(torso, rows, opt_ids, n_opts, temps, pad_id=0):
     return lp.exp().numpy(), pooled.numpy(), hidden.numpy(), mask.numpy()
 
 
+READOUT_CASES = (("slot", 24, 0), ("slot_mlp", 24, 64), ("pointer", 64, 0))
+
+
+def readout_case_inputs(spec):
+    """The tiny readout case: 3 prompts, option-line end positions (-1 pads), option counts,
+    temperatures; regenerated from seeds by the generator and by the tests alike."""
+    g = torch.Generator().manual_seed(7)
+    lens = (61, 38, 90)
+    rows = [torch.randint(0, spec.vocab, (n,), generator=g).tolist() for n in lens]
+    nopt = [3, 5, 4]
+    opt_idx = np.full((3, 5), -1, np.int32)
+    for i, (n, k) in enumerate(zip(lens, nopt, strict=True)):
+        # option lines end at increasing positions in the last 30 tokens, before <answer>
+        opt_idx[i, :k] = sorted(torch.randperm(28, generator=g)[:k].add(n - 30).tolist())
+    return rows, opt_idx, nopt, [1.0, 0.8, 1.3]
+
+
+def make_readouts() -> None:
+    """5. trained readouts (SlotHead with and without its GELU layer, PointerHead) of the
+    reference on the tiny int4 torso's final hidden states."""
+    from strands_decider.modeling import (PointerHead, SlotHead, apply_temperature, gather_options,
+                                          masked_log_softmax, pool_last_token)
+
+    from oracle import synth as osynth
+    from strands_decider_b200 import config, synth
+
+    spec = config.TINY
+    W = osynth.logical_weights(spec, seed=1, fmt="int4")
+    torso = build_reference_torso(spec, W)
+    rows, opt_idx, nopt, temps = readout_case_inputs(spec)
+    width = max(len(r) for r in rows)
+    ids = torch.tensor([r + [0] * (width - len(r)) for r in rows])
+    mask = torch.tensor([[1] * len(r) + [0] * (width - len(r)) for r in rows])
+    out = {}
+    with torch.inference_mode():
+        hidden = torso(input_ids=ids, attention_mask=mask, return_dict=True).last_hidden_state
+        pooled = pool_last_token(hidden, mask).to(torch.float32)
+        options = gather_options(hidden, torch.from_numpy(opt_idx).long()).to(torch.float32)
+        for name, out_dim, mlp in READOUT_CASES:
+            kind = "pointer" if name == "pointer" else "slot"
+            head = (PointerHead(spec.hidden, dim=out_dim) if kind == "pointer"
+                    else SlotHead(spec.hidden, out_dim, hidden=mlp)).eval()
+            head.load_state_dict(synth.readout_params(kind, spec.hidden, out_dim, mlp, seed=11))
+            logits = head(pooled, options) if kind == "pointer" else head(pooled)
+            lp = masked_log_softmax(apply_temperature(logits, torch.tensor(temps)), torch.tensor(nopt))
+            out[f"probs_{name}"] = lp.exp().numpy().astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "tiny_int4_readouts.npz"), **out)
+    print("readouts", {k: v.shape for k, v in out.items()})
+
+
 def main(reference_root: str) -> None:
     sys.path.insert(0, os.path.join(reference_root, "src"))
+    if "--readouts-only" in sys.argv:
+        make_readouts()
+        return
     import transformers.models.qwen3_5.modeling_qwen3_5 as q35
     from strands_decider.schema import derive_confidence, derive_score_confidence
 
@@ -190,8 +246,9 @@ def main(reference_root: str) -> None:
     np.savez_compressed(os.path.join(HERE, "answer_formulas.npz"), probs=flat,
                         n=np.array([len(d) for d in dists]), confidence=np.array(conf),
                         score_confidence=np.array(sconf), score_confidence_s01=np.array(sconf_s))
+    make_readouts()
     print("done")
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 and not sys.argv[1].startswith("--") else "/root/reference")

@@ -149,3 +149,52 @@ def test_state_dict_loader_rejects_missing_and_misshapen_tensors():
     sd["layers.0.mlp.down_proj.weight"] = sd["layers.0.mlp.down_proj.weight"][:, :-128]
     with pytest.raises(ValueError, match="shape"):
         DeviceWeights.from_state_dict(spec, sd)
+
+
+class _Rendered:
+    """The two fields of the reference's RenderedQuestion a pointer readout reads."""
+
+    def __init__(self, text, option_spans, n_slots, kind):
+        self.text, self.option_spans, self.n_slots, self.kind = text, option_spans, n_slots, kind
+
+
+def test_engine_pointer_head_paths_match_each_other_and_the_oracle():
+    """head_type "pointer": option positions come from the fitted questions' token offsets
+    (infer.py:221-237) on both paths, and the device head matches the oracle's PointerHead."""
+    from oracle import head as OH
+    from oracle import synth as osynth
+    from oracle import torso as OT
+    from strands_decider_b200 import synth
+    from strands_decider_b200.readout import DeviceReadout
+
+    spec, eng, tok = _engine()
+    eng.model.config.head_type = "pointer"
+    params = synth.readout_params("pointer", spec.hidden, 64, seed=4)
+    eng._rt.set_readout(DeviceReadout("pointer", params, spec.hidden))
+    g = torch.Generator().manual_seed(5)
+    state = _text(g, 40)
+    rendered, texts = [], []
+    for n in (3, 4):
+        lines = [_text(g, 3) for _ in range(n)]
+        head = _text(g, 6)
+        text, spans = head, []
+        for ln in lines:
+            text += " " + ln
+            spans.append((len(text) - len(ln), len(text)))
+        text += " answer"
+        texts.append(text)
+        rendered.append(_Rendered(text, spans, n, "choice"))
+    pb, _ = eng._slot_probs_batched(state, texts, [3, 4], ["choice"] * 2, rendered=rendered)
+    pp, _ = eng._slot_probs_shared_prefix(state, texts, [3, 4], ["choice"] * 2, rendered=rendered)
+    assert (pb - pp).abs().max().item() < 2e-4
+    s, q = eng._fit(state, texts)
+    pos = eng._option_idx(rendered, 0).tolist()
+    W = osynth.logical_weights(spec, seed=3)
+    cfg = osynth.torso_config(spec)
+    hid = [OT.forward_sequence(cfg, W, torch.tensor(s + x))[0] for x in q]
+    pooled = torch.stack([h[-1] for h in hid])
+    opts = torch.stack([h[torch.tensor([len(s) + p if p >= 0 else 0 for p in ps])] for h, ps in zip(hid, pos)])
+    logits = OH.pointer_head(pooled, opts, params)
+    want = OH.decide_from_logits(logits, torch.tensor([3, 4]), torch.tensor([1.0, 1.0]))
+    assert (pb - want).abs().max().item() < 2e-3
+    eng._rt.set_readout(None)

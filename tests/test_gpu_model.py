@@ -174,3 +174,54 @@ def test_oracle_prefix_path_matches_device_prefix_path():
     got = m.score_requests([{"state": st.tolist(), "questions": [q.tolist() for q in qs], "kinds": [1, 1],
                              "n_opts": [4, 4], "opt_ids": [[11, 12, 13, 14]] * 2}]).cpu()
     assert torch.abs(got.probs - want).max().item() < PROB_TOL
+
+
+@pytest.mark.parametrize("case", ["slot", "slot_mlp", "pointer"])
+def test_trained_readouts_match_reference_golden(case):
+    """SlotHead / PointerHead on the device (b200_model_set_readout, head_decide_kernel) against
+    the reference's heads on the tiny int4 torso (tests/golden/tiny_int4_readouts.npz), on the
+    full-prompt path and on the shared-prefix path."""
+    from strands_decider_b200 import synth
+    from strands_decider_b200.readout import DeviceReadout
+    from tests.golden.make_golden import READOUT_CASES, readout_case_inputs
+
+    g = np.load(os.path.join(GOLDEN, "tiny_int4_readouts.npz"))
+    spec = config.TINY
+    m = _model(spec, seed=1, fmt="int4")
+    rows, opt_idx, nopt, temps = readout_case_inputs(spec)
+    name, out, mlp = next(c for c in READOUT_CASES if c[0] == case)
+    kind = "pointer" if case == "pointer" else "slot"
+    m.set_readout(DeviceReadout(kind, synth.readout_params(kind, spec.hidden, out, mlp, seed=11), spec.hidden))
+    opt_pos = opt_idx.tolist() if kind == "pointer" else None
+    full = m.score_prompts(rows, None, nopt, [1] * 3, temps, opt_pos=opt_pos).cpu()
+    want = g[f"probs_{case}"][:, : full.probs.shape[1]]
+    assert np.abs(full.probs.numpy() - want).max() < PROB_TOL
+    assert np.array_equal(full.argmax.numpy(), want.argmax(1))
+    # the same questions as suffixes of a cached state (positions then count from the suffix;
+    # every option line lies in the suffix)
+    cut = 5
+    states = [r[:cut] for r in rows]
+    sufs = [r[cut:] for r in rows]
+    m.prefill_states(states, [0, 1, 2])
+    spos = [[p - cut if p >= 0 else -1 for p in ps] for ps in opt_idx.tolist()] if kind == "pointer" else None
+    cached = m.score_suffixes(sufs, [0, 1, 2], None, nopt, [1] * 3, temps, opt_pos=spos).cpu()
+    assert np.abs(cached.probs.numpy() - full.probs.numpy()).max() < 1e-3
+    m.set_readout(None)
+
+
+def test_readout_argument_checks():
+    from strands_decider_b200 import synth
+    from strands_decider_b200.readout import DeviceReadout
+
+    spec = config.TINY
+    m = _model(spec, seed=1, fmt="int4")
+    m.set_readout(DeviceReadout("pointer", synth.readout_params("pointer", spec.hidden, 32, seed=2), spec.hidden))
+    with pytest.raises(ValueError, match="opt_pos"):
+        m.score_prompts([[1, 2, 3, 4]], None, [2], [1], [1.0])
+    with pytest.raises(ValueError, match="outside"):
+        m.score_prompts([[1, 2, 3, 4]], None, [2], [1], [1.0], opt_pos=[[1, 4]])
+    m.set_readout(DeviceReadout("slot", synth.readout_params("slot", spec.hidden, 4, seed=2), spec.hidden))
+    with pytest.raises(ValueError, match="at most"):
+        m.score_prompts([[1, 2, 3, 4]], None, [5], [1], [1.0])
+    with pytest.raises(ValueError, match="lacks"):
+        DeviceReadout("slot", {"norm.weight": torch.ones(spec.hidden)}, spec.hidden)

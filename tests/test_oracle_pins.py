@@ -189,3 +189,30 @@ def test_int4_nibble_order():
                                    << (np.arange(8, dtype=np.uint32) * 4), axis=2)).view(np.int32)
     assert np.array_equal(Q.unpack_int4(packed), q)
     assert packed.view(np.uint32)[0, 0] == 0xD32087F1
+
+
+@pytest.mark.parametrize("case", ["slot", "slot_mlp", "pointer"])
+def test_trained_readouts_match_reference(case):
+    """SlotHead (one linear, and Linear-GELU-Linear) and PointerHead with gather_options
+    (modeling.py:99-190) over the tiny int4 torso's final hidden states."""
+    from strands_decider_b200 import synth
+    from tests.golden.make_golden import READOUT_CASES, readout_case_inputs
+
+    g = _load("tiny_int4_readouts.npz")
+    spec = config.TINY
+    W = osynth.logical_weights(spec, seed=1, fmt="int4")
+    cfg = osynth.torso_config(spec)
+    rows, opt_idx, nopt, temps = readout_case_inputs(spec)
+    name, out, mlp = next(c for c in READOUT_CASES if c[0] == case)
+    kind = "pointer" if case == "pointer" else "slot"
+    Hd = synth.readout_params(kind, spec.hidden, out, mlp, seed=11)
+    with torch.inference_mode():
+        hid = [T.forward_sequence(cfg, W, torch.tensor(r))[0] for r in rows]
+        pooled = torch.stack([h[-1] for h in hid])
+        if kind == "pointer":
+            opts = torch.stack([h[torch.from_numpy(opt_idx[i]).long().clamp_min(0)] for i, h in enumerate(hid)])
+            logits = H.pointer_head(pooled, opts, Hd)
+        else:
+            logits = H.slot_head(pooled, Hd)
+        probs = H.decide_from_logits(logits, torch.tensor(nopt), torch.tensor(temps))
+    np.testing.assert_allclose(probs.numpy(), g[f"probs_{case}"], atol=2e-5)
