@@ -53,6 +53,9 @@ class DeciderConfig:
     temperature: float = 1.0
     temperature_by_kind: dict[str, float] = field(default_factory=dict)
     ordinal_smoothing: float = 0.0
+    pointer_dim: int = 256
+    head_hidden: int = 0
+    extra: dict[str, Any] = field(default_factory=dict)   # the checkpoint config's other fields
 
 
 class _Readout:
