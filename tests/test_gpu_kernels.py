@@ -230,7 +230,7 @@ def test_linear_rejects_bad_shapes():
 # ----------------------------------------------------------------------------- GDN mixer
 
 
-@pytest.mark.parametrize("batch", ["few", "many"])
+@pytest.mark.parametrize("batch", ["few", "many", "large"])
 def test_gdn_mixer_matches_oracle_chunk_rule(batch):
     """conv + gating + chunked delta rule + gated norm, ragged sequences, against the
     oracle's restatement of TF:462-530 on the same bf16 inputs. A few sequences run on
@@ -240,13 +240,15 @@ def test_gdn_mixer_matches_oracle_chunk_rule(batch):
     from oracle import torso as T
     from strands_decider_b200 import _lib
 
-    H, dk = 2, 128
+    H, dk = (16 if batch == "large" else 2), 128
     conv_dim, vdim = 3 * H * dk, H * dk
     g = torch.Generator().manual_seed(0)
     if batch == "few":
         lens = [1, 31, 32, 33, 100]
-    else:   # 40 sequences x 2 heads: more CTAs than half the SMs
+    elif batch == "many":   # 40 sequences x 2 heads: more CTAs than half the SMs
         lens = [int(x) for x in torch.randint(1, 80, (40,), generator=g)]
+    else:   # 4200 tokens x 16 heads: the prep kernel's large-batch form
+        lens = [1, 2, 3, 700, 1500, 1994]   # (4200 x 16 >= 64K token-heads: 8 tokens per warp)
     Ttot = sum(lens)
     mix = torch.randn(Ttot, conv_dim + vdim + 2 * H, generator=g)
     ab = mix[:, conv_dim + vdim:]

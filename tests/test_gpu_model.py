@@ -158,6 +158,25 @@ def test_prefix_cache_equals_full_prompt_with_many_sequences():
     assert torch.equal(cached.argmax, full.argmax)
 
 
+def test_prefix_cache_equals_full_prompt_at_large_batch():
+    """Prefix ≡ full prompt with 400 requests (about 40 000 tokens per forward), where the GDN
+    prep kernel runs its large-batch form (8 tokens per warp), reading conv history from the
+    pool."""
+    m = _model(config.TINY, seed=2, fmt="int4", max_tokens=81920, slots=400)
+    g = torch.Generator().manual_seed(8)
+    V = config.TINY.vocab
+    reqs = []
+    for _ in range(400):
+        st = torch.randint(0, V, (int(torch.randint(1, 160, (1,), generator=g)),), generator=g).tolist()
+        q = torch.randint(0, V, (int(torch.randint(70, 110, (1,), generator=g)),), generator=g).tolist()
+        reqs.append({"state": st, "questions": [q], "kinds": [1], "n_opts": [3], "opt_ids": [[11, 12, 13]]})
+    cached = m.score_requests(reqs).cpu()
+    rows = [r["state"] + r["questions"][0] for r in reqs]
+    full = m.score_prompts(rows, [[11, 12, 13]] * 400, [3] * 400, [1] * 400, [1.0] * 400).cpu()
+    assert torch.abs(cached.probs - full.probs).max().item() < 1e-3
+    assert (cached.argmax == full.argmax).float().mean().item() > 0.99
+
+
 def test_oracle_prefix_path_matches_device_prefix_path():
     """Same requests through the oracle's explicit cache and the device pool."""
     m = _model(config.TINY, seed=1, fmt="nvfp4")
