@@ -131,12 +131,18 @@ typedef struct b200_seqs {
 /* The prefix-state pool that replaces the reference's cache fork (infer.py:79-124,
  * _expand_cache): question suffixes read a state's cache in place by slot index, so the
  * `expand(n).contiguous()` copies of infer.py:103,107 never happen. One pool per model;
- * arrays are indexed [layer of that kind][slot]. A sequence that continues a prefix
- * (prefix_slot >= 0) must not also save (save_slot >= 0). */
+ * arrays are indexed [layer of that kind][slot]. A saving sequence (save_slot >= 0) either
+ * has no prefix and fills the slot from position 0, or continues its own slot
+ * (prefix_slot == save_slot) and appends: the GDN state and conv history are replaced by the
+ * continued ones and its keys / values go after the slot's existing ones, so the slot's
+ * region in k_cache / v_cache (from slot_kv[slot]) must have room for the grown length.
+ * Saving into a slot other than the prefix slot is refused (fault word, nothing saved).
+ * b200_model_forward sets slot_len[save_slot] after the whole forward; the kernel-level
+ * entry points leave slot_len to the caller. */
 typedef struct b200_prefix_pool {
   int32_t n_slots;
   int32_t kv_capacity;     /* tokens per attention layer in k_cache / v_cache */
-  int32_t* slot_len;       /* [n_slots]: cached length (positions); written by saving prefills */
+  int32_t* slot_len;       /* [n_slots]: cached length (positions); set by b200_model_forward for saved slots */
   const int32_t* slot_kv;  /* [n_slots]: token offset of the slot's keys in k_cache / v_cache (host-assigned) */
   float* gdn_state;        /* [n_gdn_layers][n_slots][heads][dk][dv] fp32 (TF:285-305 state) */
   float* conv_hist;        /* [n_gdn_layers][n_slots][conv_width-1][conv_dim] fp32 (TF:462-464) */

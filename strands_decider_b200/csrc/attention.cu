@@ -66,8 +66,13 @@ __global__ void attn_prep_kernel(const AttnArgs a) {
   const float* nw = nullptr;
   uint16_t* dst;
   uint16_t* pool_dst = nullptr;
+  // a saving sequence stores its keys / values after the slot's existing ones when it saves
+  // into its own prefix slot (append), at the slot's start when it has no prefix; saving into
+  // a different slot than its prefix would need the prefix copied and is refused
   bool save = ss >= 0 && ss < a.n_slots && a.k_pool;
-  if (save && (a.slot_kv[ss] < 0 || a.slot_kv[ss] + j >= a.kv_capacity)) {
+  const bool pvalid = ps >= 0 && ps < a.n_slots;
+  const int kv0 = save ? a.slot_kv[ss] + (pvalid ? P : 0) : 0;
+  if (save && ((pvalid && ps != ss) || a.slot_kv[ss] < 0 || kv0 + j >= a.kv_capacity)) {
     if (lane == 0) raise_fault(FAULT_BAD_INDEX);
     save = false;
   }
@@ -80,12 +85,12 @@ __global__ void attn_prep_kernel(const AttnArgs a) {
     src = row + nq * 2 * HD + kh * HD;
     nw = a.p.k_norm;
     dst = a.k_buf + (size_t(t) * nkv + kh) * HD;
-    if (save) pool_dst = a.k_pool + (size_t(a.slot_kv[ss] + j) * nkv + kh) * HD;
+    if (save) pool_dst = a.k_pool + (size_t(kv0 + j) * nkv + kh) * HD;
   } else {
     const int vh = warp - nq - nkv;
     src = row + nq * 2 * HD + nkv * HD + vh * HD;
     dst = a.v_buf + (size_t(t) * nkv + vh) * HD;
-    if (save) pool_dst = a.v_pool + (size_t(a.slot_kv[ss] + j) * nkv + vh) * HD;
+    if (save) pool_dst = a.v_pool + (size_t(kv0 + j) * nkv + vh) * HD;
   }
   float x[PER];
 #pragma unroll

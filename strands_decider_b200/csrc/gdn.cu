@@ -4,8 +4,7 @@
 // gdn_prep_kernel, one warp per (head, TPW consecutive tokens), fully parallel:
 //   causal depthwise conv (width 4) + SiLU over the head's q, k, v channels (the 3 previous
 //   raw inputs come from the sequence itself or the prefix slot's history), l2norm(q) *
-//   dk^-1/2, l2norm(k), beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias); a sequence
-//   that saves its cache also writes its last 3 raw inputs (the conv history) to the pool.
+//   dk^-1/2, l2norm(k), beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias).
 // gdn_mixer_kernel, one CTA (8 warps) per (sequence, head), chunks of GC = 32 tokens in order:
 //   1. G = cumsum(g) within the chunk
 //   2. q, k and [beta v | beta k e^G] as hi/lo planes in shared memory
@@ -211,7 +210,7 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const GdnArgs a) {
   const float a_coef = -__expf(a.p.a_log[h]), dt_bias = a.p.dt_bias[h];
   int seq = gdn_find_seq(a.cu, a.n_seqs, t_begin);
   int tok0 = a.cu[seq], tend = a.cu[seq + 1];
-  int pslot = -1, sv = -1;
+  int pslot = -1;
   bool pvalid = false, fresh = true;
   float4 win[3][3];  // [row: p-3, p-2, p-1][part]
   for (int t = t_begin; t < t_end; ++t) {
@@ -225,8 +224,6 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const GdnArgs a) {
     if (fresh) {
       pslot = a.prefix_slot ? a.prefix_slot[seq] : -1;
       pvalid = pslot >= 0 && pslot < a.n_slots;
-      const int ss = a.save_slot ? a.save_slot[seq] : -1;
-      sv = (ss >= 0 && ss < a.n_slots) ? ss : -1;
 #pragma unroll
       for (int r = 0; r < 3; ++r) prep_row(a, key_dim, h, lane, tok0, p - 3 + r, pvalid, pslot, conv_dim, win[r]);
       fresh = false;
@@ -274,16 +271,6 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const GdnArgs a) {
       const float* ab = a.mix + size_t(t) * a.ld_mix + conv_dim + value_dim;
       dst[GQKV] = sigmoid(ab[h]);
       dst[GQKV + 1] = a_coef * softplus(ab[H + h] + dt_bias);
-    }
-    // conv history of a saving sequence: its last 3 raw inputs (the window now ends at p)
-    if (sv >= 0 && t == tend - 1) {
-#pragma unroll
-      for (int r = 0; r < 3; ++r) {
-#pragma unroll
-        for (int part = 0; part < 3; ++part)
-          *reinterpret_cast<float4*>(a.conv_pool + (size_t(sv) * 3 + r) * conv_dim + part * key_dim + h * GD + lane * 4) =
-              win[r][part];
-      }
     }
   }
 }
@@ -747,7 +734,33 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
         dst[r * GD + col0 + c] = S[nt][e];
       }
     }
-    if (h == 0 && slice == 0 && tid == 0) a.slot_len[sslot] = (pvalid ? a.slot_len[pslot] : 0) + len;
+    // the saved conv history: the sequence's last 3 raw inputs (head h's q / k / v channels);
+    // positions before the sequence come from the prefix slot's history. Everything is read
+    // before anything is written, so a sequence may save into its own prefix slot (append).
+    if (slice == 0) {
+      constexpr int PER_T = (3 * 3 * GD + GDN_THREADS - 1) / GDN_THREADS;
+      float hv[PER_T];
+#pragma unroll
+      for (int i = 0; i < PER_T; ++i) {
+        const int idx = tid + i * GDN_THREADS;
+        hv[i] = 0.0f;
+        if (idx < 3 * 3 * GD) {
+          const int r = idx / (3 * GD), part = (idx / GD) % 3, c = idx % GD;
+          const int q = len - 3 + r, ch = part * key_dim + h * GD + c;
+          if (q >= 0) hv[i] = a.mix[size_t(tok0 + q) * a.ld_mix + ch];
+          else if (pvalid) hv[i] = a.conv_pool[(size_t(pslot) * 3 + (3 + q)) * conv_dim + ch];
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < PER_T; ++i) {
+        const int idx = tid + i * GDN_THREADS;
+        if (idx < 3 * 3 * GD) {
+          const int r = idx / (3 * GD), part = (idx / GD) % 3, c = idx % GD;
+          a.conv_pool[(size_t(sslot) * 3 + r) * conv_dim + part * key_dim + h * GD + c] = hv[i];
+        }
+      }
+    }
   }
   if constexpr (NS > 1) {
     // no CTA leaves while another may still read its part[] (the last chunk's exchange)

@@ -242,6 +242,20 @@ extern "C" int b200_model_set_globals(b200_model* m, const uint16_t* embed, cons
   return B200_OK;
 }
 
+// After a forward that saved states: each saving sequence's slot holds its prefix's tokens
+// (when it appended to its own slot) plus its own. Updated once, after every layer has read
+// the old lengths.
+__global__ void slot_len_kernel(const int32_t* cu, int n_seqs, const int32_t* prefix_slot, const int32_t* save_slot,
+                                int32_t* slot_len, int n_slots) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= n_seqs) return;
+  const int ss = save_slot[s];
+  if (ss < 0 || ss >= n_slots) return;
+  const int ps = prefix_slot ? prefix_slot[s] : -1;
+  const int base = (ps >= 0 && ps < n_slots) ? slot_len[ps] : 0;
+  slot_len[ss] = base + cu[s + 1] - cu[s];
+}
+
 extern "C" int b200_model_set_readout(b200_model* m, const b200_readout* head) {
   if (!m) return sdb_fail(B200_ERR_ARG, "b200_model_set_readout: null model");
   if (!head) {
@@ -314,6 +328,12 @@ extern "C" int b200_model_forward(b200_model* m, const int32_t* ids, const b200_
     if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.gate_up, g, wdq, stream))) return rc;
     b200_linear_out d{B200_EP_RESID_ADD, c.hidden, x, c.hidden, 0};
     if ((rc = run_linear(*m, act, act + L.act_lo, T, c.inter, w.down, d, wdq, stream))) return rc;
+  }
+  if (seqs->save_slot) {
+    if (!pool || !pool->slot_len) return sdb_fail(B200_ERR_ARG, "b200_model_forward: save slots need a pool");
+    slot_len_kernel<<<(seqs->n_seqs + 127) / 128, 128, 0, st>>>(seqs->cu_seqlens, seqs->n_seqs, seqs->prefix_slot,
+                                                               seqs->save_slot, pool->slot_len, pool->n_slots);
+    SDB_LAUNCH_CHECK();
   }
   if (decide && decide->n_rows > 0) {
     if (m->readout.kind != B200_HEAD_OPTION_TOKEN) {

@@ -215,19 +215,49 @@ class DecisionModel:
                               cu)
         return self.forward(self._dev(flat), self._dev(cu), decide=d, max_len=max(map(len, rows)), stream=stream)
 
-    def prefill_states(self, states: list[list[int]], slots: list[int], stream=None) -> None:
-        """Forward each state once and keep its cache in the given pool slots."""
-        if max(slots) >= self.pool_slots:
-            raise ValueError("pool slot out of range")
+    def prefill_states(self, states: list[list[int]], slots: list[int], stream=None, reserve: int = 0) -> None:
+        """Forward each state once and keep its cache in the given pool slots. The pool is laid
+        out afresh for these slots (other slots are dropped); `reserve` tokens of key/value room
+        are left after each state for append_states."""
+        if max(slots) >= self.pool_slots or min(slots) < 0 or len(set(slots)) != len(slots):
+            raise ValueError("pool slots must be distinct and in range")
         flat, cu = self._pack(states)
-        if cu[-1] > self.kv_capacity:
-            raise ValueError("states exceed the pool's KV capacity")
         kv = torch.zeros(self.pool_slots, dtype=torch.int32)
-        for s, c in zip(slots, cu[:-1]):
-            kv[s] = c
+        self._slot_room = [0] * self.pool_slots
+        self._slot_len = [-1] * self.pool_slots
+        off = 0
+        for s, st in zip(slots, states):
+            kv[s] = off
+            self._slot_room[s] = len(st) + reserve
+            self._slot_len[s] = len(st)
+            off += len(st) + reserve
+        if off > self.kv_capacity:
+            raise ValueError("states (with their reserve) exceed the pool's KV capacity")
         self.slot_kv.copy_(kv.to(self.device, non_blocking=True))
         self.forward(self._dev(flat), self._dev(cu), save_slot=self._dev(slots), max_len=max(map(len, states)),
                      stream=stream)
+
+    def append_states(self, tokens: list[list[int]], slots: list[int], stream=None) -> None:
+        """Grow cached states in place: forward tokens[i] as the continuation of slot slots[i]
+        and save the continued GDN state, conv history and keys / values back into that slot
+        (one token at a time is the decode-time update). The slot must have been prefilled
+        with enough `reserve` for the grown length."""
+        room = getattr(self, "_slot_room", None)
+        if room is None:
+            raise ValueError("append_states needs slots laid out by prefill_states")
+        if len(set(slots)) != len(slots):
+            raise ValueError("pool slots must be distinct")
+        for s, t in zip(slots, tokens, strict=True):
+            if not 0 <= s < self.pool_slots or self._slot_len[s] < 0:
+                raise ValueError(f"slot {s} holds no state")
+            if self._slot_len[s] + len(t) > room[s]:
+                raise ValueError(f"slot {s}: {self._slot_len[s]} + {len(t)} tokens exceed its room of {room[s]}")
+        flat, cu = self._pack(tokens)
+        sl = self._dev(slots)
+        self.forward(self._dev(flat), self._dev(cu), prefix_slot=sl, save_slot=sl, max_len=max(map(len, tokens)),
+                     stream=stream)
+        for s, t in zip(slots, tokens):
+            self._slot_len[s] += len(t)
 
     def score_suffixes(self, suffixes: list[list[int]], slots: list[int], opt_ids, n_opts, kinds, temps,
                        ordinal_smoothing=0.0, stream=None, opt_pos=None) -> Decisions:

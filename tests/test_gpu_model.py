@@ -244,3 +244,30 @@ def test_readout_argument_checks():
         m.score_prompts([[1, 2, 3, 4]], None, [5], [1], [1.0])
     with pytest.raises(ValueError, match="lacks"):
         DeviceReadout("slot", {"norm.weight": torch.ones(spec.hidden)}, spec.hidden)
+
+
+@pytest.mark.parametrize("fmt", ["int4", "ternary"])
+def test_appended_states_equal_full_prompts(fmt):
+    """Growing cached states in place (append_states: GDN state, conv history and keys /
+    values continued and saved back into the same slot), by a multi-token chunk and then one
+    token at a time, then scoring questions against them, equals the full prompts."""
+    m = _model(config.TINY, seed=1, fmt=fmt, slots=4)
+    g = torch.Generator().manual_seed(6)
+    V = config.TINY.vocab
+    r = lambda n: torch.randint(0, V, (n,), generator=g).tolist()  # noqa: E731
+    states = [r(50), r(3), r(1)]
+    chunks = [r(37), r(70), r(2)]
+    singles = [[r(1) for _ in range(3)] for _ in range(3)]
+    qs = [r(9), r(33), r(5)]
+    m.prefill_states(states, [0, 1, 2], reserve=120)
+    m.append_states(chunks, [0, 1, 2])
+    for step in range(3):
+        m.append_states([singles[i][step] for i in range(3)], [0, 1, 2])
+    opt = [[11, 12, 13]] * 3
+    cached = m.score_suffixes(qs, [0, 1, 2], opt, [3] * 3, [1] * 3, [1.0] * 3).cpu()
+    rows = [states[i] + chunks[i] + sum(singles[i], []) + qs[i] for i in range(3)]
+    full = m.score_prompts(rows, opt, [3] * 3, [1] * 3, [1.0] * 3).cpu()
+    assert torch.abs(cached.probs - full.probs).max().item() < 1e-3
+    assert torch.equal(cached.argmax, full.argmax)
+    with pytest.raises(ValueError, match="room"):
+        m.append_states([r(130)], [2])
