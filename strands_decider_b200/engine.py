@@ -146,6 +146,118 @@ class B200SlotProbs:
         return dec.probs.float().cpu(), len(s) + sum(len(x) for x in q)
 
 
+    def _slot_probs_many(self, items: list[dict]) -> list[tuple[torch.Tensor, int]]:
+        """Several requests' `_slot_probs_shared_prefix` in two launches: every state into its
+        own pool slot in one prefill, then every request's questions against their slots in
+        one suffix forward. items: dicts with state_text, question_texts, n_slots, kinds and
+        optionally rendered. Returns each request's (probs [n, K], input-token count)."""
+        states, sufs, slots, n_all, kinds_all, temps_all, opt_ids, opt_pos = [], [], [], [], [], [], [], []
+        spans = []
+        ht = self._head_type()
+        for i, it in enumerate(items):
+            s, q = self._fit(it["state_text"], it["question_texts"])   # also keeps this request's offsets
+            ra = self._readout_args(it.get("rendered"), it["n_slots"], 0)
+            states.append(s)
+            spans.append((len(sufs), len(q), len(s) + sum(len(x) for x in q)))
+            sufs.extend(q)
+            slots.extend([i] * len(q))
+            n_all.extend(it["n_slots"])
+            kinds_all.extend(it["kinds"])
+            temps_all.extend(self._temps(it["kinds"]))
+            if ht == "option_token":
+                opt_ids.extend(ra["opt_ids"])
+            if ht == "pointer":
+                opt_pos.extend(ra["opt_pos"])
+        if len(items) > self._rt.pool_slots:
+            raise ValueError(f"{len(items)} requests exceed the pool's {self._rt.pool_slots} slots")
+        self._rt.prefill_states(states, list(range(len(items))))
+        dec = self._rt.score_suffixes(sufs, slots, opt_ids or None, n_all, kinds_all, temps_all,
+                                      getattr(self.model.config, "ordinal_smoothing", 0.0),
+                                      opt_pos=opt_pos or None)
+        probs = dec.probs.float().cpu()
+        out = []
+        for (start, n, ntok), it in zip(spans, items, strict=True):
+            k = max(it["n_slots"])
+            out.append((probs[start:start + n, :k].contiguous(), ntok))
+        return out
+
+
+class RequestBatcher:
+    """Continuous batching for a serving process: requests submitted from many threads (the
+    HTTP server's workers) are collected for up to `window_ms` (or until `max_requests` or
+    `max_tokens` are pending) and answered by one shared prefill through
+    `engine._slot_probs_many`, instead of one request at a time (the reference serves one
+    request per engine call, server.py:124-125). `submit` returns a Future of
+    (probs [n, K], input-token count); an engine error fails every request of its batch."""
+
+    def __init__(self, engine: Any, max_requests: int = 32, max_tokens: int = 65536, window_ms: float = 2.0):
+        import queue
+
+        self.engine, self.max_tokens = engine, max_tokens
+        rt = getattr(engine, "_rt", None)   # one pool slot per request of a batch
+        self.max_requests = min(max_requests, rt.pool_slots) if rt is not None else max_requests
+        self.window = window_ms / 1e3
+        self._q: queue.Queue = queue.Queue()
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, name="b200-batcher", daemon=True)
+        self._thread.start()
+
+    def submit(self, state_text: str, question_texts: list[str], n_slots: list[int], kinds: list[str],
+               rendered: Any = None):
+        from concurrent.futures import Future
+
+        if self._stop.is_set():
+            raise RuntimeError("the batcher is closed")
+        fut: Future = Future()
+        est = (len(state_text) + sum(len(q) for q in question_texts)) // 2 + 1   # rough token estimate
+        self._q.put(({"state_text": state_text, "question_texts": question_texts, "n_slots": n_slots,
+                      "kinds": kinds, "rendered": rendered}, est, fut))
+        return fut
+
+    def close(self) -> None:
+        self._stop.set()
+        self._q.put(None)
+        self._thread.join(timeout=10)
+
+    def _run(self) -> None:
+        import queue
+        import time
+
+        carry = None
+        while not self._stop.is_set():
+            first = carry or self._q.get()
+            carry = None
+            if first is None:
+                break
+            batch, tokens = [first], first[1]
+            deadline = time.monotonic() + self.window
+            while len(batch) < self.max_requests:
+                left = deadline - time.monotonic()
+                if left <= 0:
+                    break
+                try:
+                    nxt = self._q.get(timeout=left)
+                except queue.Empty:
+                    break
+                if nxt is None:
+                    self._stop.set()
+                    break
+                if tokens + nxt[1] > self.max_tokens:
+                    carry = nxt   # starts the next batch
+                    break
+                batch.append(nxt)
+                tokens += nxt[1]
+            try:
+                with self.engine._lock:
+                    results = self.engine._slot_probs_many([b[0] for b in batch])
+            except Exception as e:   # every request of the batch sees the engine's error
+                for b in batch:
+                    b[2].set_exception(e)
+                continue
+            for b, r in zip(batch, results, strict=True):
+                b[2].set_result(r)
+
+
 class B200Engine(B200SlotProbs):
     """Standalone engine: the host logic of SystemOneEngine restated (for machines where the
     reference is not installed), with the device overrides. One evaluation at a time."""

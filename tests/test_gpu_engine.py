@@ -38,7 +38,7 @@ def _text(g: torch.Generator, n: int) -> str:
     return " ".join(WORDS[int(i)] for i in torch.randint(0, len(WORDS), (n,), generator=g))
 
 
-def _engine(max_length=256):
+def _engine(max_length=256, slots=2):
     from strands_decider_b200 import config
     from strands_decider_b200.engine import B200Engine, DeciderConfig, EngineConfig
     from strands_decider_b200.runtime import DecisionModel
@@ -46,7 +46,7 @@ def _engine(max_length=256):
 
     spec = config.TINY
     w = DeviceWeights.synthetic(spec, seed=3, latent_device="cpu")
-    rt = DecisionModel(w, max_tokens=2048, pool_slots=2, pool_kv_tokens=512)
+    rt = DecisionModel(w, max_tokens=2048, pool_slots=slots, pool_kv_tokens=1024)
     tok = _tokenizer()
     eng = B200Engine(rt, tok, DeciderConfig(max_length=max_length, temperature_by_kind={"score": 1.5}),
                      EngineConfig(max_batch=8))
@@ -198,3 +198,42 @@ def test_engine_pointer_head_paths_match_each_other_and_the_oracle():
     want = OH.decide_from_logits(logits, torch.tensor([3, 4]), torch.tensor([1.0, 1.0]))
     assert (pb - want).abs().max().item() < 2e-3
     eng._rt.set_readout(None)
+
+
+def test_many_requests_in_two_launches_match_one_at_a_time():
+    """_slot_probs_many (every state in one prefill, every question in one suffix forward) and
+    the RequestBatcher fed from several threads give each request what its own
+    _slot_probs_shared_prefix gives."""
+    import threading
+
+    from strands_decider_b200.engine import RequestBatcher
+
+    spec, eng, tok = _engine(slots=8)
+    g = torch.Generator().manual_seed(11)
+    items = []
+    for i in range(5):
+        nq = 1 + i % 3
+        items.append({"state_text": _text(g, 20 + 9 * i), "question_texts": [_text(g, 4 + j) for j in range(nq)],
+                      "n_slots": [2 + (i + j) % 3 for j in range(nq)], "kinds": ["choice"] * nq})
+    want = [eng._slot_probs_shared_prefix(it["state_text"], it["question_texts"], it["n_slots"], it["kinds"])
+            for it in items]
+    got = eng._slot_probs_many(items)
+    for (pw, nw), (pg, ng) in zip(want, got, strict=True):
+        assert ng == nw and pg.shape == pw.shape
+        assert (pg - pw).abs().max().item() < 2e-4
+    b = RequestBatcher(eng, max_requests=4, window_ms=20)
+    futs = [None] * len(items)
+
+    def go(i):
+        it = items[i]
+        futs[i] = b.submit(it["state_text"], it["question_texts"], it["n_slots"], it["kinds"])
+
+    ts = [threading.Thread(target=go, args=(i,)) for i in range(len(items))]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    for (pw, nw), f in zip(want, futs, strict=True):
+        pg, ng = f.result(timeout=60)
+        assert ng == nw and (pg - pw).abs().max().item() < 2e-4
+    b.close()
