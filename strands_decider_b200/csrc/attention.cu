@@ -180,6 +180,7 @@ template <int HD>
 __global__ void __launch_bounds__(128 * fa_dg<HD>(), 2) attn_flash_kernel(const AttnArgs a) {
   constexpr int CH = HD / 8;  // 16-byte chunks per row
   constexpr int DG = fa_dg<HD>(), NT = 128 * DG, DW = HD / DG;  // DW: value columns per warp
+  pdl_trigger();  // the out-projection GEMM may set up once the last wave of this grid runs
   extern __shared__ uint8_t fa_smem[];
   uint8_t* sQ = fa_smem;                          // [FA_Q][HD]
   uint8_t* sK = sQ + FA_Q * HD * 2;               // [2][FA_K][HD]

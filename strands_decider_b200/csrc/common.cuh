@@ -146,6 +146,13 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start while the previous kernel in the stream finishes; it must call pdl_wait() before
+// touching any memory that kernel reads or writes. pdl_trigger() lets the next such kernel
+// be scheduled once every CTA of this one has issued it. Both are no-ops without PDL.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Prefetch [src, src + bytes) into L2 (16-byte aligned address, size a multiple of 16).
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");

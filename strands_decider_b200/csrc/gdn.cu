@@ -300,6 +300,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
   extern __shared__ __align__(128) uint8_t gdn_smem_raw[];
   SMT& sm = *reinterpret_cast<SMT*>(gdn_smem_raw);
   float (*const O)[SMT::UP] = sm.ru.uw.U;
+  pdl_trigger();  // the out-projection GEMM may set up once the last wave of this grid runs
   const int h = blockIdx.x / NS, slice = blockIdx.x % NS, col0 = slice * DV, seq = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;

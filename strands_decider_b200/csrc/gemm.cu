@@ -278,6 +278,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // everything above touched only this CTA's shared memory and tensor memory: with PDL it
+  // overlapped the previous kernel's tail; from here on inputs and outputs are shared
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ---------------- producer: activations (TMA) and packed weights (bulk copies)
@@ -584,7 +588,20 @@ static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_lo, const CU
   if (args.ksplit > 1 && EP == B200_EP_STORE)
     SDB_CUDA(cudaMemset2DAsync(a.o.out, size_t(a.o.ldo) * 4, 0, size_t(a.o.n_valid) * 4, a.m, st));
   const int units = tiles * args.ksplit;
-  gemm_tc_kernel<BN, FMT, EP, SPLIT><<<std::min(units, n_sm), GEMM_THREADS, smem, st>>>(map, map_lo, map_b, args);
+  // programmatic dependent launch: the CTA set-up (barriers, TMEM, descriptor prefetch)
+  // overlaps the tail of the kernel before it in the stream (the kernel waits before its
+  // first shared access)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(std::min(units, n_sm));
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SDB_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, FMT, EP, SPLIT>, map, map_lo, map_b, args));
   SDB_LAUNCH_CHECK();
   return B200_OK;
 }

@@ -36,6 +36,7 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t&
 // hidden % 128 == 0.
 __global__ void rmsnorm_kernel(const float* __restrict__ x, int rows, int hidden, const float* __restrict__ w,
                                float eps, uint16_t* __restrict__ out, long long lo_offset) {
+  pdl_trigger();  // the GEMM that reads this output may set up meanwhile
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -66,6 +67,7 @@ __global__ void __launch_bounds__(256) rmsnorm_block_kernel(const float* __restr
                                                             const float* __restrict__ w, float eps,
                                                             uint16_t* __restrict__ out, long long lo_offset) {
   __shared__ float part[8];
+  pdl_trigger();  // the GEMM that reads this output may set up meanwhile
   const int row = blockIdx.x, tid = threadIdx.x;
   const int n4 = hidden / 1024;  // float4 per thread
   const float4* xr = reinterpret_cast<const float4*>(x + size_t(row) * hidden);

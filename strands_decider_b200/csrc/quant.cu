@@ -113,6 +113,7 @@ __global__ void quant_ternary_kernel(const float* __restrict__ w, int n, int k, 
 template <int FMT>
 __global__ void dequant_kernel(b200_qweight w, uint16_t* __restrict__ out) {
   __shared__ uint32_t lut[16];
+  pdl_trigger();  // the GEMM that reads this output may set up meanwhile
   if (threadIdx.x < 16) lut[threadIdx.x] = ternary_pair_bits(threadIdx.x);
   __syncthreads();
   const int per_row = w.k / 32;
