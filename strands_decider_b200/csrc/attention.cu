@@ -47,6 +47,8 @@ __device__ __forceinline__ int find_seq(const int32_t* cu, int n, int t) {
 template <int HD>
 __global__ void attn_prep_kernel(const AttnArgs a) {
   constexpr int PER = HD / 32;
+  pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
+  pdl_trigger();
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = a.p.heads, nkv = a.p.kv_heads;
@@ -180,7 +182,8 @@ template <int HD>
 __global__ void __launch_bounds__(128 * fa_dg<HD>(), 2) attn_flash_kernel(const AttnArgs a) {
   constexpr int CH = HD / 8;  // 16-byte chunks per row
   constexpr int DG = fa_dg<HD>(), NT = 128 * DG, DW = HD / DG;  // DW: value columns per warp
-  pdl_trigger();  // the out-projection GEMM may set up once the last wave of this grid runs
+  pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
+  pdl_trigger();
   extern __shared__ uint8_t fa_smem[];
   uint8_t* sQ = fa_smem;                          // [FA_Q][HD]
   uint8_t* sK = sQ + FA_Q * HD * 2;               // [2][FA_K][HD]
@@ -361,8 +364,7 @@ __global__ void __launch_bounds__(128 * fa_dg<HD>(), 2) attn_flash_kernel(const 
 template <int HD>
 static int launch_attn(const AttnArgs& a, int n_tokens, int n_seqs, int max_len, cudaStream_t st) {
   const int warps = a.p.heads + 2 * a.p.kv_heads;
-  attn_prep_kernel<HD><<<n_tokens, 32 * warps, 0, st>>>(a);
-  SDB_LAUNCH_CHECK();
+  SDB_CUDA(launch_pdl(attn_prep_kernel<HD>, dim3(n_tokens), dim3(32 * warps), 0, st, a));
   constexpr int smem = FA_Q * HD * 2 + 4 * FA_K * HD * 2;
   static bool attr = false;
   if (!attr) {
@@ -370,8 +372,7 @@ static int launch_attn(const AttnArgs& a, int n_tokens, int n_seqs, int max_len,
     attr = true;
   }
   dim3 grid((max_len + FA_Q - 1) / FA_Q, n_seqs, a.p.heads);
-  attn_flash_kernel<HD><<<grid, 128 * fa_dg<HD>(), smem, st>>>(a);
-  SDB_LAUNCH_CHECK();
+  SDB_CUDA(launch_pdl(attn_flash_kernel<HD>, grid, dim3(128 * fa_dg<HD>()), smem, st, a));
   return B200_OK;
 }
 

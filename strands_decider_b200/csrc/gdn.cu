@@ -204,6 +204,9 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const GdnArgs a) {
     wsm[part][ch & 3][ch >> 2] = *reinterpret_cast<const float4*>(a.p.conv_w + (part * key_dim + h * GD + ch) * 4);
   }
   __syncthreads();
+  // the conv taps above are weights; everything below comes from the kernels before this one
+  pdl_wait();
+  pdl_trigger();
   const int t_begin = (blockIdx.x * 8 + warp) * TPW;
   if (t_begin >= T) return;
   const int t_end = min(T, t_begin + TPW);
@@ -300,7 +303,8 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
   extern __shared__ __align__(128) uint8_t gdn_smem_raw[];
   SMT& sm = *reinterpret_cast<SMT*>(gdn_smem_raw);
   float (*const O)[SMT::UP] = sm.ru.uw.U;
-  pdl_trigger();  // the out-projection GEMM may set up once the last wave of this grid runs
+  pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
+  pdl_trigger();
   const int h = blockIdx.x / NS, slice = blockIdx.x % NS, col0 = slice * DV, seq = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;
@@ -818,14 +822,14 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
   a.n_tokens = s->n_tokens;
   if (long(s->n_tokens) * p->heads >= 64L * 1024) {  // enough warps at 8 tokens each to fill the GPU
     constexpr int TPW = PREP_TPW_LARGE;
-    gdn_prep_kernel<TPW><<<dim3((s->n_tokens + 8 * TPW - 1) / (8 * TPW), p->heads), 256, 0, st>>>(a);
+    SDB_CUDA(launch_pdl(gdn_prep_kernel<TPW>, dim3((s->n_tokens + 8 * TPW - 1) / (8 * TPW), p->heads), dim3(256), 0,
+                        st, a));
   } else {
-    gdn_prep_kernel<1><<<dim3((s->n_tokens + 7) / 8, p->heads), 256, 0, st>>>(a);
+    SDB_CUDA(launch_pdl(gdn_prep_kernel<1>, dim3((s->n_tokens + 7) / 8, p->heads), dim3(256), 0, st, a));
   }
-  SDB_LAUNCH_CHECK();
   if (long(s->n_seqs) * p->heads * 2 > 148) {  // enough (sequence, head) CTAs: one per head
-    gdn_mixer_kernel<GD><<<dim3(p->heads, s->n_seqs), GDN_THREADS, sizeof(GdnSmem<GD>), st>>>(a);
-    SDB_LAUNCH_CHECK();
+    SDB_CUDA(launch_pdl(gdn_mixer_kernel<GD>, dim3(p->heads, s->n_seqs), dim3(GDN_THREADS), sizeof(GdnSmem<GD>), st,
+                        a));
     return B200_OK;
   }
   // few sequences (latency): a cluster of 128 / GDN_DV_SPLIT CTAs per head, each owning a
@@ -836,13 +840,15 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
   cfg.blockDim = dim3(GDN_THREADS);
   cfg.dynamicSmemBytes = sizeof(GdnSmem<GDN_DV_SPLIT>);
   cfg.stream = st;
-  cudaLaunchAttribute attr_cl[1];
+  cudaLaunchAttribute attr_cl[2];
   attr_cl[0].id = cudaLaunchAttributeClusterDimension;
   attr_cl[0].val.clusterDim.x = NS;
   attr_cl[0].val.clusterDim.y = 1;
   attr_cl[0].val.clusterDim.z = 1;
+  attr_cl[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr_cl[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr_cl;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   SDB_CUDA(cudaLaunchKernelEx(&cfg, gdn_mixer_kernel<GDN_DV_SPLIT>, a));
   SDB_LAUNCH_CHECK();
   return B200_OK;

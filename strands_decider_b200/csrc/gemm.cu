@@ -281,7 +281,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   // everything above touched only this CTA's shared memory and tensor memory: with PDL it
   // overlapped the previous kernel's tail; from here on inputs and outputs are shared
   pdl_wait();
-  pdl_trigger();
+  // With one unit per CTA (small M) the next kernel may be scheduled now, so its launch
+  // overlaps this one. A persistent multi-unit grid lets it start only at exit: its CTAs
+  // would otherwise sit on the SMs for the whole GEMM and slow it.
+  if (n_units <= int(gridDim.x)) pdl_trigger();
 
   if (warp == 0) {
     // ---------------- producer: activations (TMA) and packed weights (bulk copies)
@@ -469,6 +472,8 @@ __device__ float simt_dot(const GemmArgs& a, const uint16_t* x, const uint16_t* 
 template <int FMT, int EP>
 __global__ void gemm_simt_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ xl, int ldx,
                                  const GemmArgs a) {
+  pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
+  pdl_trigger();
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   const int m = blockIdx.y;
   const b200_linear_out& o = a.o;
@@ -591,18 +596,8 @@ static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_lo, const CU
   // programmatic dependent launch: the CTA set-up (barriers, TMEM, descriptor prefetch)
   // overlaps the tail of the kernel before it in the stream (the kernel waits before its
   // first shared access)
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(std::min(units, n_sm));
-  cfg.blockDim = dim3(GEMM_THREADS);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  SDB_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, FMT, EP, SPLIT>, map, map_lo, map_b, args));
-  SDB_LAUNCH_CHECK();
+  SDB_CUDA(launch_pdl(gemm_tc_kernel<BN, FMT, EP, SPLIT>, dim3(std::min(units, n_sm)), dim3(GEMM_THREADS), smem, st,
+                      map, map_lo, map_b, args));
   return B200_OK;
 }
 
@@ -646,11 +641,14 @@ static int dispatch_simt(const uint16_t* x, const uint16_t* xl, int ldx, const G
   const int ncols = a.o.epilogue == B200_EP_SWIGLU ? a.o.n_valid / 2 : a.o.n_valid;
   dim3 grid((ncols + 127) / 128, a.m);
   switch (a.o.epilogue) {
-    case B200_EP_STORE: gemm_simt_kernel<FMT, B200_EP_STORE><<<grid, 128, 0, st>>>(x, xl, ldx, a); break;
-    case B200_EP_RESID_ADD: gemm_simt_kernel<FMT, B200_EP_RESID_ADD><<<grid, 128, 0, st>>>(x, xl, ldx, a); break;
-    default: gemm_simt_kernel<FMT, B200_EP_SWIGLU><<<grid, 128, 0, st>>>(x, xl, ldx, a); break;
+    case B200_EP_STORE:
+      SDB_CUDA(launch_pdl(gemm_simt_kernel<FMT, B200_EP_STORE>, grid, dim3(128), 0, st, x, xl, ldx, a));
+      break;
+    case B200_EP_RESID_ADD:
+      SDB_CUDA(launch_pdl(gemm_simt_kernel<FMT, B200_EP_RESID_ADD>, grid, dim3(128), 0, st, x, xl, ldx, a));
+      break;
+    default: SDB_CUDA(launch_pdl(gemm_simt_kernel<FMT, B200_EP_SWIGLU>, grid, dim3(128), 0, st, x, xl, ldx, a)); break;
   }
-  SDB_LAUNCH_CHECK();
   return B200_OK;
 }
 

@@ -36,7 +36,8 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t&
 // hidden % 128 == 0.
 __global__ void rmsnorm_kernel(const float* __restrict__ x, int rows, int hidden, const float* __restrict__ w,
                                float eps, uint16_t* __restrict__ out, long long lo_offset) {
-  pdl_trigger();  // the GEMM that reads this output may set up meanwhile
+  pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -67,7 +68,8 @@ __global__ void __launch_bounds__(256) rmsnorm_block_kernel(const float* __restr
                                                             const float* __restrict__ w, float eps,
                                                             uint16_t* __restrict__ out, long long lo_offset) {
   __shared__ float part[8];
-  pdl_trigger();  // the GEMM that reads this output may set up meanwhile
+  pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
+  pdl_trigger();
   const int row = blockIdx.x, tid = threadIdx.x;
   const int n4 = hidden / 1024;  // float4 per thread
   const float4* xr = reinterpret_cast<const float4*>(x + size_t(row) * hidden);
@@ -110,6 +112,8 @@ __global__ void __launch_bounds__(256) rmsnorm_block_kernel(const float* __restr
 // masked softmax and derives the answer numbers. hidden <= 4096, kmax <= 16.
 __global__ void decide_kernel(const float* __restrict__ x, int hidden, const float* __restrict__ fnorm, float eps,
                               const uint16_t* __restrict__ table, b200_decide_args d, int vocab, int n_tokens) {
+  pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= d.n_rows) return;
@@ -335,6 +339,8 @@ __global__ void __launch_bounds__(HEAD_THREADS) head_decide_kernel(const float* 
                                                                     b200_readout hd, b200_decide_args d, int n_tokens,
                                                                     int ybuf) {
   extern __shared__ float hsm[];
+  pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
+  pdl_trigger();
   float* v = hsm;
   float* y = v + hidden;
   float* q = y + ybuf;
@@ -404,8 +410,8 @@ int sdb_decide_readout(const float* x, int32_t hidden, const float* final_norm, 
     return sdb_fail(B200_ERR_ARG, "b200_decide_readout: a pointer head needs opt_tok (option token positions)");
   const int ybuf = std::max(hd->out, hd->mlp_hidden);
   const size_t smem = size_t(hidden + ybuf + hd->out + HEAD_KMAX + 8) * 4;  // <= 37 KB by the checks above
-  head_decide_kernel<<<d->n_rows, HEAD_THREADS, smem, st>>>(x, hidden, final_norm, eps, *hd, *d, n_tokens, ybuf);
-  SDB_LAUNCH_CHECK();
+  SDB_CUDA(launch_pdl(head_decide_kernel, dim3(d->n_rows), dim3(HEAD_THREADS), smem, st, x, hidden, final_norm, eps,
+                      *hd, *d, n_tokens, ybuf));
   return B200_OK;
 }
 
@@ -442,11 +448,11 @@ extern "C" int b200_rmsnorm(const float* x, int32_t rows, int32_t hidden, const 
   if (rows <= 0 || hidden % 128 != 0 || lo_offset % 8 != 0)
     return sdb_fail(B200_ERR_SHAPE, "b200_rmsnorm: hidden % 128 and lo_offset % 8 must be 0");
   if (rows <= 1024 && hidden % 1024 == 0 && hidden <= 4096)
-    rmsnorm_block_kernel<<<rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, hidden, w, eps, out, lo_offset);
+    SDB_CUDA(launch_pdl(rmsnorm_block_kernel, dim3(rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), x,
+                        hidden, w, eps, out, lo_offset));
   else
-    rmsnorm_kernel<<<(rows + 7) / 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, rows, hidden, w, eps, out,
-                                                                                     lo_offset);
-  SDB_LAUNCH_CHECK();
+    SDB_CUDA(launch_pdl(rmsnorm_kernel, dim3((rows + 7) / 8), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), x,
+                        rows, hidden, w, eps, out, lo_offset));
   return B200_OK;
 }
 
@@ -459,8 +465,8 @@ int sdb_decide_vocab(const float* x, int32_t hidden, const float* final_norm, fl
   if (!d->last_tok || !d->opt_ids || !d->n_opts || !d->kinds || !d->temperature || !d->probs || !d->argmax ||
       !d->confidence || !d->score)
     return sdb_fail(B200_ERR_ARG, "b200_decide: null array");
-  decide_kernel<<<(d->n_rows + 3) / 4, 128, 0, st>>>(x, hidden, final_norm, eps, table, *d, vocab, n_tokens);
-  SDB_LAUNCH_CHECK();
+  SDB_CUDA(launch_pdl(decide_kernel, dim3((d->n_rows + 3) / 4), dim3(128), 0, st, x, hidden, final_norm, eps, table,
+                      *d, vocab, n_tokens));
   return B200_OK;
 }
 

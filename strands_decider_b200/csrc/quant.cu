@@ -113,7 +113,9 @@ __global__ void quant_ternary_kernel(const float* __restrict__ w, int n, int k, 
 template <int FMT>
 __global__ void dequant_kernel(b200_qweight w, uint16_t* __restrict__ out) {
   __shared__ uint32_t lut[16];
-  pdl_trigger();  // the GEMM that reads this output may set up meanwhile
+  // the packed weights are constant, but `out` may still be read by the GEMM before this kernel
+  pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
+  pdl_trigger();
   if (threadIdx.x < 16) lut[threadIdx.x] = ternary_pair_bits(threadIdx.x);
   __syncthreads();
   const int per_row = w.k / 32;
@@ -232,13 +234,13 @@ extern "C" int b200_dequantize(const b200_qweight* w, uint16_t* out, b200_stream
   const int total = w->n * (w->k / 32);
   const dim3 grid((total + 255) / 256), block(256);
   switch (w->format) {
-    case B200_W_BF16: dequant_kernel<B200_W_BF16><<<grid, block, 0, st>>>(*w, out); break;
-    case B200_W_INT4G128: dequant_kernel<B200_W_INT4G128><<<grid, block, 0, st>>>(*w, out); break;
+    case B200_W_BF16: SDB_CUDA(launch_pdl(dequant_kernel<B200_W_BF16>, grid, block, 0, st, *w, out)); break;
+    case B200_W_INT4G128: SDB_CUDA(launch_pdl(dequant_kernel<B200_W_INT4G128>, grid, block, 0, st, *w, out)); break;
     case B200_W_NVFP4:
       if (!w->row_scale) return sdb_fail(B200_ERR_ARG, "b200_dequantize: nvfp4 needs row_scale");
-      dequant_kernel<B200_W_NVFP4><<<grid, block, 0, st>>>(*w, out);
+      SDB_CUDA(launch_pdl(dequant_kernel<B200_W_NVFP4>, grid, block, 0, st, *w, out));
       break;
-    case B200_W_TERNARY: dequant_kernel<B200_W_TERNARY><<<grid, block, 0, st>>>(*w, out); break;
+    case B200_W_TERNARY: SDB_CUDA(launch_pdl(dequant_kernel<B200_W_TERNARY>, grid, block, 0, st, *w, out)); break;
     default: return sdb_fail(B200_ERR_FORMAT, "b200_dequantize: unknown format");
   }
   SDB_LAUNCH_CHECK();

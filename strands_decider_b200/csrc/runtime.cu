@@ -247,6 +247,7 @@ extern "C" int b200_model_set_globals(b200_model* m, const uint16_t* embed, cons
 // the old lengths.
 __global__ void slot_len_kernel(const int32_t* cu, int n_seqs, const int32_t* prefix_slot, const int32_t* save_slot,
                                 int32_t* slot_len, int n_slots) {
+  sdb::pdl_wait();  // slot lengths are read by every layer's kernels before this one
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= n_seqs) return;
   const int ss = save_slot[s];
@@ -331,9 +332,8 @@ extern "C" int b200_model_forward(b200_model* m, const int32_t* ids, const b200_
   }
   if (seqs->save_slot) {
     if (!pool || !pool->slot_len) return sdb_fail(B200_ERR_ARG, "b200_model_forward: save slots need a pool");
-    slot_len_kernel<<<(seqs->n_seqs + 127) / 128, 128, 0, st>>>(seqs->cu_seqlens, seqs->n_seqs, seqs->prefix_slot,
-                                                               seqs->save_slot, pool->slot_len, pool->n_slots);
-    SDB_LAUNCH_CHECK();
+    SDB_CUDA(sdb::launch_pdl(slot_len_kernel, dim3((seqs->n_seqs + 127) / 128), dim3(128), 0, st, seqs->cu_seqlens,
+                        seqs->n_seqs, seqs->prefix_slot, seqs->save_slot, pool->slot_len, pool->n_slots));
   }
   if (decide && decide->n_rows > 0) {
     if (m->readout.kind != B200_HEAD_OPTION_TOKEN) {
