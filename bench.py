@@ -288,7 +288,9 @@ def gemm_roofline(model, tokens: int, pk: dict, reps: int = 20) -> dict:
 
     achieved = algorithmic FLOPs (2 M N K) / GEMM time. The activations enter as two bf16
     planes (hi + lo, fp32-level precision), so the tensor pipe executes 2x the algorithmic
-    FLOPs; frac is against the measured bf16 peak and is therefore bounded by 0.5."""
+    FLOPs; frac is against the measured bf16 peak and is therefore bounded by 0.5. With e4m3 low
+    planes (lo_plane "e4m3") the low plane runs as e4m3 MMAs at twice the rate: 1.5x the
+    algorithmic FLOPs in bf16-MMA terms, so frac is bounded by 2/3."""
     import ctypes as C
 
     from strands_decider_b200 import _lib
@@ -300,19 +302,31 @@ def gemm_roofline(model, tokens: int, pk: dict, reps: int = 20) -> dict:
     o = _lib.LinearOut(_lib.EP_SWIGLU, 2 * s.inter, _lib.ptr(out), s.inter, tokens * s.inter)
     qw = pw.qweight()
     st = torch.cuda.current_stream()
-    dequant = tokens >= 4096 and s.weight_format != "bf16"
+    lo8 = tokens >= 4096 and getattr(model, "lo_plane", "bf16") == "e4m3"
+    dequant = lo8 or (tokens >= 4096 and s.weight_format != "bf16")
     if dequant:
         wdq = torch.empty(pw.n, pw.k, dtype=torch.bfloat16, device="cuda")
+        wdq8 = torch.empty(pw.n, pw.k, dtype=torch.uint8, device="cuda")
         qb = _lib.QWeight()
         qb.format, qb.n, qb.k, qb.data = _lib.FMT["bf16"], pw.n, pw.k, _lib.ptr(wdq)
 
         def unpack():
-            _lib.call("b200_dequantize", C.byref(qw), _lib.ptr(wdq), st.cuda_stream)
+            if lo8:
+                _lib.call("b200_dequantize_lo8", C.byref(qw), _lib.ptr(wdq), _lib.ptr(wdq8), st.cuda_stream)
+            else:
+                _lib.call("b200_dequantize", C.byref(qw), _lib.ptr(wdq), st.cuda_stream)
     gw = qb if dequant else qw
+    if lo8:
+        o.lo_format = _lib.LO_E4M3
+        xl8 = torch.zeros(tokens, s.hidden, dtype=torch.uint8, device="cuda")
 
     def launch():
-        _lib.call("b200_linear", _lib.ptr(xp[0]), _lib.ptr(xp[1]), tokens, s.hidden, s.hidden, C.byref(gw),
-                  C.byref(o), st.cuda_stream)
+        if lo8:
+            _lib.call("b200_linear_lo8", _lib.ptr(xp[0]), _lib.ptr(xl8), tokens, s.hidden, s.hidden, _lib.ptr(wdq),
+                      _lib.ptr(wdq8), pw.n, C.byref(o), st.cuda_stream)
+        else:
+            _lib.call("b200_linear", _lib.ptr(xp[0]), _lib.ptr(xp[1]), tokens, s.hidden, s.hidden, C.byref(gw),
+                      C.byref(o), st.cuda_stream)
 
     def timed(fn) -> float:
         for _ in range(3):
@@ -337,11 +351,13 @@ def gemm_roofline(model, tokens: int, pk: dict, reps: int = 20) -> dict:
         if per_tok:
             traffic = round(per_tok * tokens)
     wname = "bf16 (dequantised once per call)" if dequant else s.weight_format
+    planes = "lo8" if lo8 else "split"
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
             "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": traffic,
-            "kernel": f"gemm_tc_kernel<256,{wname},swiglu,split> M={tokens} N={2 * s.inter} K={s.hidden}",
+            "kernel": f"gemm_tc_kernel<256,{wname},swiglu,{planes}> M={tokens} N={2 * s.inter} K={s.hidden}",
             "ms_per_launch": round(ms, 4), "dequant_ms_per_launch": round(dq_ms, 4) if dq_ms else None,
-            "mma_flops_per_algorithmic_flop": 2, "peak_src": pk["src"] + " bf16 burst (tcgen05 kind::f16)"}
+            "mma_flops_per_algorithmic_flop": 1.5 if lo8 else 2,
+            "peak_src": pk["src"] + " bf16 burst (tcgen05 kind::f16)"}
 
 
 WORKLOADS = {
@@ -437,6 +453,8 @@ def main() -> None:
     ap.add_argument("--requests-per-step", type=int, default=0, help="0 = the workload's default")
     ap.add_argument("--cpu-sample", type=int, default=3, help="requests in the CPU baseline sample (0 = skip)")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
+    ap.add_argument("--lo-plane", default="bf16", choices=["bf16", "e4m3"],
+                    help="low activation plane of the large-batch GEMMs (DecisionModel lo_plane)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -504,7 +522,8 @@ def main() -> None:
     slots = R if prefix else 1
     kv = max(b.n_state_tokens for b in batches) if prefix else 1
     weights = DeviceWeights.synthetic(spec, seed=0, device="cuda", latent_device="cuda")
-    model = DecisionModel(weights, max_tokens=max_tok, pool_slots=slots, pool_kv_tokens=max(kv, 1))
+    model = DecisionModel(weights, max_tokens=max_tok, pool_slots=slots, pool_kv_tokens=max(kv, 1),
+                          lo_plane=args.lo_plane)
     stream = torch.cuda.current_stream()
     use_graph = not args.no_graph
     graphs = [StepGraph(model, b) for b in batches] if use_graph else None
@@ -600,7 +619,7 @@ def main() -> None:
                    "requests_per_step": R, "decisions_per_step": b0.n_decisions,
                    "tokens_per_step": b0.tokens, "question_tokens": wl.question_len,
                    "path": "prefix cache (state once, questions against its pool slot)" if prefix else "full prompts",
-                   "cuda_graphs": use_graph,
+                   "cuda_graphs": use_graph, "lo_plane": args.lo_plane,
                    "l2": "inputs larger than L2 (0.8 GB weights + GBs of activations per step)",
                    "parallelism": f"dp{world} (requests LPT-sharded, answers all-gathered over NCCL)"},
         "linear_tflops": round(fl / (ms * 1e-3) / 1e12 / world, 1),

@@ -82,6 +82,10 @@ int b200_quantize(int32_t format, const float* w, int32_t n, int32_t k, void* da
                   float* row_scale, b200_stream stream);
 /* Unpack a packed weight to bf16 out[n, k], exactly as the GEMM's shared-memory unpacker. */
 int b200_dequantize(const b200_qweight* w, uint16_t* out, b200_stream stream);
+/* The two weight copies b200_linear_lo8 reads, from a packed (or bf16) weight: w_hi bf16
+ * [n, k] = dequant(W) * 2^B200_LO8_SHIFT (exact: a power-of-two rescale of b200_dequantize's
+ * output) and w_lo8 e4m3 [n, k] = e4m3_rn_satfinite(dequant(W) * 2^B200_LO8_W_SHIFT). */
+int b200_dequantize_lo8(const b200_qweight* w, uint16_t* w_hi, uint8_t* w_lo8, b200_stream stream);
 /* Bytes of the streaming copy of a packed [n, k] weight (n % 256 == 0, k % 128 == 0). */
 int b200_tile_bytes(int32_t format, int32_t n, int32_t k, size_t* tile_bytes, size_t* tile_scale_bytes);
 /* Write the streaming copy: tiles[n/256][k/64][256 rows][row bytes of 64 columns] and, for
@@ -104,16 +108,35 @@ int b200_tile_weights(const b200_qweight* w, void* tiles, void* tile_scales, b20
  * Only columns < n_valid are written (n_valid a multiple of 32; of 128 for SwiGLU). */
 enum b200_epilogue { B200_EP_STORE = 0, B200_EP_RESID_ADD = 1, B200_EP_SWIGLU = 2 };
 
+/* Format of a low activation plane (lo = x - bf16_rn(x), same element index as the hi plane):
+ *   B200_LO_BF16  bf16_rn(lo), 2 bytes per element
+ *   B200_LO_E4M3  e4m3_rn_satfinite(lo * 2^B200_LO8_X_SHIFT), 1 byte per element (a row of
+ *                 ldx elements is ldx bytes); read by b200_linear_lo8 */
+enum b200_lo_format { B200_LO_BF16 = 0, B200_LO_E4M3 = 1 };
+#define B200_LO8_X_SHIFT 6
+#define B200_LO8_W_SHIFT 6
+#define B200_LO8_SHIFT (B200_LO8_X_SHIFT + B200_LO8_W_SHIFT)
+
 typedef struct b200_linear_out {
   int32_t epilogue;
   int32_t n_valid;
   void* out;
   int32_t ldo;
   int64_t lo_offset;
+  int32_t lo_format; /* SwiGLU: format of the lo plane written at out + lo_offset (b200_lo_format) */
 } b200_linear_out;
 
 int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m, int32_t k, int32_t ldx,
                 const b200_qweight* w, const b200_linear_out* out, b200_stream stream);
+/* The e4m3-low-plane GEMM: y = (x_hi . w_hi + x_lo8 . w_lo8) * 2^-B200_LO8_SHIFT, i.e. x @ W^T
+ * with the low plane at e4m3 precision, for the weight copies of b200_dequantize_lo8 ([n, k],
+ * n % 256 == 0, k % 128 == 0). x_hi bf16 [m, ldx]; x_lo8 the B200_LO_E4M3 plane [m, ldx] bytes
+ * (ldx a multiple of 16). Per 64 k the tensor cores run four bf16 MMAs (K = 16) for the hi plane
+ * and two e4m3 MMAs (K = 32, twice the rate) for the low plane into one fp32 accumulator: 3/4 of
+ * the tensor work of two bf16 planes. Same epilogues and n_valid rules as b200_linear. */
+int b200_linear_lo8(const uint16_t* x_hi, const uint8_t* x_lo8, int32_t m, int32_t k, int32_t ldx,
+                    const uint16_t* w_hi, const uint8_t* w_lo8, int32_t n, const b200_linear_out* out,
+                    b200_stream stream);
 /* Same contract on plain CUDA cores (fp32 FMA), used by the tests to cross-check b200_linear. */
 int b200_linear_simt(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m, int32_t k, int32_t ldx,
                      const b200_qweight* w, const b200_linear_out* out, b200_stream stream);
@@ -160,6 +183,9 @@ int b200_embed(const int32_t* ids, int32_t n_tokens, const uint16_t* table, int3
  * as the two bf16 planes of a GEMM input: hi at out [rows, hidden], lo at out + lo_offset. */
 int b200_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
                  int64_t lo_offset, b200_stream stream);
+/* Same, with the lo plane in B200_LO_E4M3 form at (uint8_t*)(out + lo_offset) [rows, hidden]. */
+int b200_rmsnorm_lo8(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
+                     int64_t lo_offset, b200_stream stream);
 
 /* One Gated-DeltaNet token mixer after its in-projection (TF:462-530): depthwise causal
  * conv (width conv_width) + SiLU, q/k l2norm, beta = sigmoid(b), g = -exp(A_log) *
@@ -298,6 +324,10 @@ typedef struct b200_model_config {
    * every 128-token tile); smaller batches stream the packed tiles. 0 = the library default
    * (4096), < 0 = never. */
   int32_t dequant_min_tokens;
+  /* Low activation plane of the GEMMs on the dequantised path (b200_lo_format): B200_LO_BF16
+   * keeps two bf16 planes everywhere; B200_LO_E4M3 stores it as e4m3 and runs those GEMMs
+   * as b200_linear_lo8 (3/4 of the tensor work). Streamed-tile GEMMs always use bf16 planes. */
+  int32_t lo_format;
 } b200_model_config;
 
 typedef struct b200_layer_weights {

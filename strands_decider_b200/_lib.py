@@ -22,6 +22,9 @@ STATUS = {1: "ARG", 2: "SHAPE", 3: "FORMAT", 4: "CUDA", 5: "WORKSPACE", 6: "TIME
 
 FMT = {"bf16": 0, "int4": 1, "nvfp4": 2, "ternary": 3}
 EP_STORE, EP_RESID_ADD, EP_SWIGLU = 0, 1, 2
+LO_BF16, LO_E4M3 = 0, 1
+LO8_X_SHIFT, LO8_W_SHIFT = 6, 6
+LO8_SHIFT = LO8_X_SHIFT + LO8_W_SHIFT
 LAYER_GDN, LAYER_ATTN = 0, 1
 
 
@@ -39,7 +42,7 @@ class QWeight(C.Structure):
 
 class LinearOut(C.Structure):
     _fields_ = [("epilogue", C.c_int32), ("n_valid", C.c_int32), ("out", C.c_void_p), ("ldo", C.c_int32),
-                ("lo_offset", C.c_int64)]
+                ("lo_offset", C.c_int64), ("lo_format", C.c_int32)]
 
 
 class Seqs(C.Structure):
@@ -87,7 +90,7 @@ class ModelConfig(C.Structure):
                 ("gdn_dv", C.c_int32), ("conv_width", C.c_int32), ("attn_heads", C.c_int32),
                 ("attn_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("rope_dim", C.c_int32),
                 ("max_pos", C.c_int32), ("eps", C.c_float), ("weight_format", C.c_int32),
-                ("dequant_min_tokens", C.c_int32)]
+                ("dequant_min_tokens", C.c_int32), ("lo_format", C.c_int32)]
 
 
 class LayerWeights(C.Structure):
@@ -104,12 +107,15 @@ _SIGS = {
     "b200_read_fault": ([C.POINTER(C.c_uint)], C.c_int),
     "b200_quantize": ([_I, _P, _I, _I, _P, _P, _P, _P], C.c_int),
     "b200_dequantize": ([C.POINTER(QWeight), _P, _P], C.c_int),
+    "b200_dequantize_lo8": ([C.POINTER(QWeight), _P, _P, _P], C.c_int),
     "b200_tile_bytes": ([_I, _I, _I, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)], C.c_int),
     "b200_tile_weights": ([C.POINTER(QWeight), _P, _P, _P], C.c_int),
     "b200_linear": ([_P, _P, _I, _I, _I, C.POINTER(QWeight), C.POINTER(LinearOut), _P], C.c_int),
     "b200_linear_simt": ([_P, _P, _I, _I, _I, C.POINTER(QWeight), C.POINTER(LinearOut), _P], C.c_int),
+    "b200_linear_lo8": ([_P, _P, _I, _I, _I, _P, _P, _I, C.POINTER(LinearOut), _P], C.c_int),
     "b200_embed": ([_P, _I, _P, _I, _P, _P], C.c_int),
     "b200_rmsnorm": ([_P, _I, _I, _P, C.c_float, _P, C.c_int64, _P], C.c_int),
+    "b200_rmsnorm_lo8": ([_P, _I, _I, _P, C.c_float, _P, C.c_int64, _P], C.c_int),
     "b200_gdn_mixer": ([C.POINTER(GdnParams), C.POINTER(Seqs), _P, _I, _P, C.c_int64, C.POINTER(PrefixPool), _I,
                         _P, _P], C.c_int),
     "b200_gdn_scratch_floats": ([_I, _I], C.c_int),

@@ -26,6 +26,7 @@ struct AttnArgs {
   uint16_t* v_buf;
   uint16_t* out;
   long long lo_offset;
+  int lo8;  // lo plane as e4m3 bytes (B200_LO_E4M3) instead of bf16
   const int32_t* slot_len;
   const int32_t* slot_kv;
   uint16_t* k_pool;   // this layer's [kv_capacity][kv_heads][head_dim]
@@ -354,7 +355,10 @@ __global__ void __launch_bounds__(128 * fa_dg<HD>(), 2) attn_flash_kernel(const 
       const float y1 = o[j][2 * r + 1] * inv[r] * sigmoid(gate[d + 1]);
       const uint16_t h0 = f32_to_bf16_rn(y0), h1 = f32_to_bf16_rn(y1);
       *reinterpret_cast<uint32_t*>(dst + d) = uint32_t(h0) | (uint32_t(h1) << 16);
-      if (a.lo_offset)
+      if (a.lo_offset && a.lo8)
+        *reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(a.out + a.lo_offset) + (t * nq + h) * HD + d) =
+            f32x2_to_e4m3x2(lo8_value(y0, h0), lo8_value(y1, h1));
+      else if (a.lo_offset)
         *reinterpret_cast<uint32_t*>(dst + a.lo_offset + d) =
             pack_bf16x2(y0 - bf16_to_f32(h0), y1 - bf16_to_f32(h1));
     }
@@ -382,7 +386,7 @@ using namespace sdb;
 
 int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qkv, int32_t ld_qkv, uint16_t* q_buf,
                   uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool,
-                  int32_t layer, cudaStream_t st) {
+                  int32_t layer, int lo8, cudaStream_t st) {
   if (!p || !s || !qkv || !q_buf || !k_buf || !v_buf || !out) return sdb_fail(B200_ERR_ARG, "b200_attention: null pointer");
   if (!p->q_norm || !p->k_norm || !p->rope_cos || !p->rope_sin) return sdb_fail(B200_ERR_ARG, "b200_attention: null param");
   if (p->heads <= 0 || p->kv_heads <= 0 || p->heads % p->kv_heads != 0 || p->heads + 2 * p->kv_heads > 32)
@@ -408,6 +412,7 @@ int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qk
   a.v_buf = v_buf;
   a.out = out;
   a.lo_offset = lo_offset;
+  a.lo8 = lo8;
   a.n_slots = uses_pool ? pool->n_slots : 0;
   a.kv_capacity = uses_pool ? pool->kv_capacity : 0;
   a.slot_len = uses_pool ? pool->slot_len : nullptr;
@@ -427,7 +432,7 @@ int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qk
 extern "C" int b200_attention(const b200_attn_params* p, const b200_seqs* seqs, const float* qkv, int32_t ld_qkv,
                               uint16_t* q_buf, uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset,
                               const b200_prefix_pool* pool, int32_t attn_layer, b200_stream stream) {
-  return sdb_attention(p, seqs, qkv, ld_qkv, q_buf, k_buf, v_buf, out, lo_offset, pool, attn_layer,
+  return sdb_attention(p, seqs, qkv, ld_qkv, q_buf, k_buf, v_buf, out, lo_offset, pool, attn_layer, 0,
                        reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -474,6 +479,6 @@ extern "C" int b200_attention_noalloc(const b200_attn_params* p, const b200_seqs
   uint16_t* q_buf = base;
   uint16_t* k_buf = q_buf + T * p->heads * p->head_dim;
   uint16_t* v_buf = k_buf + T * p->kv_heads * p->head_dim;
-  return sdb_attention(p, seqs, qkv, ld_qkv, q_buf, k_buf, v_buf, out, lo_offset, pool, attn_layer,
+  return sdb_attention(p, seqs, qkv, ld_qkv, q_buf, k_buf, v_buf, out, lo_offset, pool, attn_layer, 0,
                        reinterpret_cast<cudaStream_t>(stream));
 }

@@ -55,6 +55,43 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return uint32_t(f32_to_bf16_rn(lo)) | (uint32_t(f32_to_bf16_rn(hi)) << 16);
 }
 
+// ----------------------------------------------------------------------------- e4m3 low plane
+// With B200_LO_E4M3 the low activation plane lo = x - bf16(x) is stored as
+// e4m3(lo * 2^B200_LO8_X_SHIFT): one byte per element, at the same element index as the hi
+// plane (so a row of ldx elements is ldx bytes). Conversions round to nearest even and
+// saturate at +-448.
+__device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float a, float b) {  // a -> low byte
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+  return r;
+}
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
+  return uint32_t(f32x2_to_e4m3x2(a, b)) | (uint32_t(f32x2_to_e4m3x2(c, d)) << 16);
+}
+// The stored low-plane byte of x given its hi plane value h (bf16 bits).
+__device__ __forceinline__ float lo8_value(float x, uint16_t h) {
+  return (x - bf16_to_f32(h)) * float(1 << B200_LO8_X_SHIFT);
+}
+
+// Four consecutive activations at element e (e % 4 == 0) of a hi/lo plane pair: the hi
+// plane bf16_rn(v) at out[e]; the lo plane at out + lo_offset as bf16_rn(v - hi), or as its
+// e4m3 byte with lo8; no lo plane when lo_offset is 0.
+__device__ __forceinline__ void store_planes4(uint16_t* out, long long lo_offset, bool lo8, size_t e, float a,
+                                              float b, float c, float d) {
+  const uint16_t h0 = f32_to_bf16_rn(a), h1 = f32_to_bf16_rn(b), h2 = f32_to_bf16_rn(c), h3 = f32_to_bf16_rn(d);
+  *reinterpret_cast<uint2*>(out + e) =
+      make_uint2(uint32_t(h0) | (uint32_t(h1) << 16), uint32_t(h2) | (uint32_t(h3) << 16));
+  if (!lo_offset) return;
+  if (lo8) {
+    *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(out + lo_offset) + e) =
+        e4m3x4(lo8_value(a, h0), lo8_value(b, h1), lo8_value(c, h2), lo8_value(d, h3));
+  } else {
+    *reinterpret_cast<uint2*>(out + lo_offset + e) =
+        make_uint2(pack_bf16x2(a - bf16_to_f32(h0), b - bf16_to_f32(h1)),
+                   pack_bf16x2(c - bf16_to_f32(h2), d - bf16_to_f32(h3)));
+  }
+}
+
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 __device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + __expf(-x)); }
 __device__ __forceinline__ float softplus(float x) { return x > 20.0f ? x : log1pf(__expf(x)); }
@@ -175,6 +212,18 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
          (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 
+// Same for a K-major tile of 64-byte rows written by TMA with 64-byte swizzle (an e4m3
+// tile 64 k wide): 8-row core groups 512 bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t saddr) {
+  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(512 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(4) << 61);
+}
+
+// Instruction descriptor, kind::f8f6f4: D fp32, A and B e4m3 (format code 0), both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_e4m3(int M, int N) {
+  return (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
 // Instruction descriptor, kind::f16: D fp32, A and B bf16, both K-major, M x N.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
@@ -197,6 +246,16 @@ __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint6
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D (+)= A * B for e4m3 A and B, K = 32 per instruction, fp32 accumulate in TMEM.
+__device__ __forceinline__ void umma_e4m3(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

@@ -47,6 +47,7 @@ struct GdnArgs {
                          // one head is one contiguous run of GC records (GPREP * 4 = 1552 bytes each)
   uint16_t* out;         // hi plane [T, value_dim]; lo plane at out + lo_offset
   long long lo_offset;
+  int lo8;               // lo plane as e4m3 bytes (B200_LO_E4M3) instead of bf16
   int32_t* slot_len;
   float* state_pool;     // this layer's [n_slots][heads][dk][dv]
   float* conv_pool;      // this layer's [n_slots][conv_width-1][conv_dim]
@@ -708,19 +709,19 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
             y[e] = nw[e] * (ov[i][e] * r) * silu(zv[i][e]);
             hb[e] = f32_to_bf16_rn(y[e]);
           }
-          uint16_t* dst = a.out + size_t(tok0 + c0 + j) * value_dim + h * GD + col0 + lane * CPL;
+          const size_t e0 = size_t(tok0 + c0 + j) * value_dim + h * GD + col0 + lane * CPL;
           if constexpr (CPL == 4) {
-            *reinterpret_cast<uint2*>(dst) =
-                make_uint2(uint32_t(hb[0]) | (uint32_t(hb[1]) << 16), uint32_t(hb[2]) | (uint32_t(hb[3]) << 16));
-            if (a.lo_offset)
-              *reinterpret_cast<uint2*>(dst + a.lo_offset) =
-                  make_uint2(pack_bf16x2(y[0] - bf16_to_f32(hb[0]), y[1] - bf16_to_f32(hb[1])),
-                             pack_bf16x2(y[2] - bf16_to_f32(hb[2]), y[3] - bf16_to_f32(hb[3])));
+            store_planes4(a.out, a.lo_offset, a.lo8, e0, y[0], y[1], y[2], y[3]);
           } else {
 #pragma unroll
             for (int e = 0; e < CPL; ++e) {
-              dst[e] = hb[e];
-              if (a.lo_offset) dst[e + a.lo_offset] = f32_to_bf16_rn(y[e] - bf16_to_f32(hb[e]));
+              a.out[e0 + e] = hb[e];
+              if (!a.lo_offset) continue;
+              if (a.lo8)
+                reinterpret_cast<uint8_t*>(a.out + a.lo_offset)[e0 + e] =
+                    uint8_t(f32x2_to_e4m3x2(lo8_value(y[e], hb[e]), 0.0f));
+              else
+                a.out[e0 + e + a.lo_offset] = f32_to_bf16_rn(y[e] - bf16_to_f32(hb[e]));
             }
           }
         }
@@ -780,7 +781,8 @@ using namespace sdb;
 int sdb_gdn_prep_floats(int heads, int n_tokens) { return n_tokens * heads * GPREP; }
 
 int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix, int32_t ld_mix, uint16_t* out,
-                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, float* prep, cudaStream_t st) {
+                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, float* prep, int lo8,
+                  cudaStream_t st) {
   if (!p || !s || !mix || !out) return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: null pointer");
   if (p->dk != GD || p->dv != GD || p->conv_width != 4)
     return sdb_fail(B200_ERR_UNSUPPORTED, "b200_gdn_mixer: only dk = dv = 128 and conv width 4 are built");
@@ -802,6 +804,7 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
   a.ld_mix = ld_mix;
   a.out = out;
   a.lo_offset = lo_offset;
+  a.lo8 = lo8;
   const int conv_dim = 3 * p->heads * GD;
   if (ld_mix % 4 != 0 || (reinterpret_cast<uintptr_t>(mix) & 15) || (reinterpret_cast<uintptr_t>(out) & 7))
     return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: mix must be 16-byte aligned with ld_mix % 4 == 0, out 8-byte aligned");
@@ -857,7 +860,7 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
 extern "C" int b200_gdn_mixer(const b200_gdn_params* p, const b200_seqs* seqs, const float* mix, int32_t ld_mix,
                               uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool, int32_t gdn_layer,
                               float* scratch, b200_stream stream) {
-  return sdb_gdn_mixer(p, seqs, mix, ld_mix, out, lo_offset, pool, gdn_layer, scratch,
+  return sdb_gdn_mixer(p, seqs, mix, ld_mix, out, lo_offset, pool, gdn_layer, scratch, 0,
                        reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -18,6 +18,12 @@
 // bytes), full_w (packed weight bytes), full_b (256 unpacking threads), empty
 // (tcgen05.commit); the two accumulators by acc_full (tcgen05.commit) and acc_empty (the 4
 // epilogue warps). Every wait is bounded.
+//
+// The e4m3-low-plane form (PL_LO8, bf16 weight copies only): the low activation plane is
+// e4m3(lo * 2^6) and meets an e4m3 copy of W * 2^6, while the hi plane meets W * 2^12 in bf16,
+// so both products share one accumulator at scale 2^12 (undone in the epilogue). Per 64 k:
+// four bf16 MMAs (K = 16) and two e4m3 MMAs (K = 32, 64-byte swizzled tiles) instead of
+// eight bf16 MMAs.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -42,6 +48,9 @@ constexpr int gemm_stages(int bn) { return bn == 128 ? 4 : 3; }
 // Packed weight tiles are prefetched into L2 this many k-blocks ahead of the copy into a stage.
 constexpr int GEMM_L2_AHEAD = 6;
 
+// activation planes: hi only, hi + bf16 lo, hi + e4m3 lo (the last with bf16 weights only)
+constexpr int PL_ONE = 0, PL_SPLIT = 1, PL_LO8 = 2;
+
 constexpr int GEMM_TILE_ROWS = 256;  // rows of one b200_tile_weights tile (a 128-column tile reads half of one)
 
 struct GemmArgs {
@@ -64,15 +73,18 @@ __device__ __forceinline__ GemmUnit gemm_unit(const GemmArgs& a, int u, int nk) 
   return {mt * GEMM_BM, nt * BN, ks * nk / a.ksplit, (ks + 1) * nk / a.ksplit};
 }
 
-template <int BN, int FMT, bool SPLIT>
+template <int BN, int FMT, int PL>
 struct GemmSmem {
+  static_assert(PL != PL_LO8 || FMT == B200_W_BF16, "the e4m3 low plane pairs with bf16 weight copies");
   static constexpr bool PACKED = FMT != B200_W_BF16;
-  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;          // one activation plane
-  static constexpr int A_STAGE = A_BYTES * (SPLIT ? 2 : 1);
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;          // the hi activation plane
+  static constexpr int A_LO_BYTES = PL == PL_SPLIT ? A_BYTES : PL == PL_LO8 ? GEMM_BM * GEMM_BK : 0;
+  static constexpr int A_STAGE = A_BYTES + A_LO_BYTES;
   static constexpr int B_BYTES = BN * GEMM_BK * 2;               // unpacked bf16 weight tile
+  static constexpr int B8_BYTES = PL == PL_LO8 ? BN * GEMM_BK : 0;  // e4m3 weight tile
   static constexpr int W_BYTES = PACKED ? BN * tile_row_bytes(FMT) : 0;
   static constexpr int S_BYTES = BN * tile_scale_row_bytes(FMT);
-  static constexpr int STAGE = A_STAGE + B_BYTES + W_BYTES + S_BYTES;
+  static constexpr int STAGE = A_STAGE + B_BYTES + B8_BYTES + W_BYTES + S_BYTES;
   static constexpr int STAGES = gemm_stages(BN);
   static constexpr int BARS = 4 * STAGES + 4;
   static constexpr int TOTAL = STAGES * STAGE + 1024 + BARS * 8 + 16 + 64;
@@ -136,6 +148,13 @@ __device__ __forceinline__ void epilogue_chunk_atomic(const GemmArgs& a, int row
   }
 }
 
+// PL_LO8 accumulates y * 2^B200_LO8_SHIFT: scale 32 accumulators back (exact).
+__device__ __forceinline__ void lo8_unscale(uint32_t (&v)[32]) {
+  constexpr float s = 1.0f / float(1 << B200_LO8_SHIFT);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * s);
+}
+
 // hi = bf16_rn(x), lo = bf16_rn(x - hi): the two planes of an fp32 activation.
 __device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
   const uint16_t ha = f32_to_bf16_rn(a), hb = f32_to_bf16_rn(b);
@@ -161,7 +180,19 @@ __device__ __forceinline__ void epilogue_swiglu(const GemmArgs& a, int row, int 
     split_bf16x2(h[4], h[5], hi.z, lo.z);
     split_bf16x2(h[6], h[7], hi.w, lo.w);
     reinterpret_cast<uint4*>(dst)[j] = hi;
-    if (o.lo_offset) reinterpret_cast<uint4*>(dst + o.lo_offset)[j] = lo;
+    if (!o.lo_offset) continue;
+    if (o.lo_format == B200_LO_E4M3) {
+      const uint16_t* hb = reinterpret_cast<const uint16_t*>(&hi);
+      float l[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) l[e] = lo8_value(h[e], hb[e]);
+      // the e4m3 plane: one byte per element at the hi plane's element index
+      uint8_t* lo8 = reinterpret_cast<uint8_t*>(reinterpret_cast<uint16_t*>(o.out) + o.lo_offset) +
+                     size_t(row) * o.ldo + ocol;
+      reinterpret_cast<uint2*>(lo8)[j] = make_uint2(e4m3x4(l[0], l[1], l[2], l[3]), e4m3x4(l[4], l[5], l[6], l[7]));
+    } else {
+      reinterpret_cast<uint4*>(dst + o.lo_offset)[j] = lo;
+    }
   }
 }
 
@@ -231,16 +262,18 @@ __device__ __forceinline__ void unpack_unit_smem(uint8_t* sB, const uint8_t* sW,
 }
 
 // --------------------------------------------------------------------------- kernel
-template <int BN, int FMT, int EP, bool SPLIT>
+template <int BN, int FMT, int EP, int PL>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA_lo,
-                   const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
-  using SM = GemmSmem<BN, FMT, SPLIT>;
+                   const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmB8,
+                   const GemmArgs args) {
+  using SM = GemmSmem<BN, FMT, PL>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;                                   // STAGES x A_STAGE
   uint8_t* sB = sA + SM::STAGES * SM::A_STAGE;         // STAGES x B_BYTES
-  uint8_t* sW = sB + SM::STAGES * SM::B_BYTES;         // STAGES x W_BYTES
+  uint8_t* sB8 = sB + SM::STAGES * SM::B_BYTES;        // STAGES x B8_BYTES (PL_LO8)
+  uint8_t* sW = sB8 + SM::STAGES * SM::B8_BYTES;       // STAGES x W_BYTES
   uint8_t* sS = sW + SM::STAGES * SM::W_BYTES;         // STAGES x S_BYTES
   uint64_t* bars = reinterpret_cast<uint64_t*>(sS + SM::STAGES * SM::S_BYTES);
   uint64_t* full_a = bars;
@@ -290,8 +323,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ---------------- producer: activations (TMA) and packed weights (bulk copies)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
-      if constexpr (SPLIT) tma_prefetch_desc(&tmA_lo);
+      if constexpr (PL != PL_ONE) tma_prefetch_desc(&tmA_lo);
       if constexpr (!SM::PACKED) tma_prefetch_desc(&tmB);
+      if constexpr (PL == PL_LO8) tma_prefetch_desc(&tmB8);
       constexpr int RB = SM::PACKED ? tile_row_bytes(FMT) : 0, SB = tile_scale_row_bytes(FMT);
       uint32_t it = 0;
       for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
@@ -319,11 +353,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if constexpr (SM::S_BYTES > 0)
               bulk_load(sS + s * SM::S_BYTES, stiles + (lt + kt) * GEMM_TILE_ROWS * SB, SM::S_BYTES, &full_w[s]);
           }
-          mbar_arrive_expect_tx(&full_a[s], SM::A_STAGE + (SM::PACKED ? 0 : SM::B_BYTES));
+          mbar_arrive_expect_tx(&full_a[s], SM::A_STAGE + (SM::PACKED ? 0 : SM::B_BYTES) + SM::B8_BYTES);
           tma_load_2d(sA + s * SM::A_STAGE, &tmA, &full_a[s], kt * GEMM_BK, m0);
-          if constexpr (SPLIT)
+          // (an e4m3 tile's x coordinate is in bytes = elements: kt * 64, a multiple of 16)
+          if constexpr (PL != PL_ONE)
             tma_load_2d(sA + s * SM::A_STAGE + SM::A_BYTES, &tmA_lo, &full_a[s], kt * GEMM_BK, m0);
           if constexpr (!SM::PACKED) tma_load_2d(sB + s * SM::B_BYTES, &tmB, &full_a[s], kt * GEMM_BK, n0);
+          if constexpr (PL == PL_LO8) tma_load_2d(sB8 + s * SM::B8_BYTES, &tmB8, &full_a[s], kt * GEMM_BK, n0);
         }
       }
     }
@@ -331,6 +367,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ---------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(GEMM_BM, BN);
+      constexpr uint32_t idesc8 = umma_idesc_e4m3(GEMM_BM, BN);
       uint32_t it = 0, local = 0;
       for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++local) {
         const GemmUnit w = gemm_unit<BN>(args, u, nk);
@@ -349,7 +386,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < GEMM_BK / 16; ++j) {  // +32 bytes of K per MMA = +2 in 16-byte units
             umma_bf16(acc, ad + 2 * j, bd + 2 * j, idesc, (kt != w.kb0 || j != 0) ? 1u : 0u);
-            if constexpr (SPLIT) umma_bf16(acc, ad + (SM::A_BYTES >> 4) + 2 * j, bd + 2 * j, idesc, 1u);
+            if constexpr (PL == PL_SPLIT) umma_bf16(acc, ad + (SM::A_BYTES >> 4) + 2 * j, bd + 2 * j, idesc, 1u);
+          }
+          if constexpr (PL == PL_LO8) {  // 64-byte e4m3 rows: K = 32 per MMA, +32 bytes = +2
+            const uint64_t ald = umma_desc_sw64(smem_addr(sA + s * SM::A_STAGE + SM::A_BYTES));
+            const uint64_t bld = umma_desc_sw64(smem_addr(sB8 + s * SM::B8_BYTES));
+#pragma unroll
+            for (int j = 0; j < GEMM_BK / 32; ++j) umma_e4m3(acc, ald + 2 * j, bld + 2 * j, idesc8, 1u);
           }
           umma_commit(&empty[s]);
         }
@@ -378,6 +421,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             tmem_ld_32x32b_x32(tl + b * 128 + c * 32, g);
             tmem_ld_32x32b_x32(tl + b * 128 + 64 + c * 32, u);
             tmem_ld_wait();
+            if constexpr (PL == PL_LO8) {
+              lo8_unscale(g);
+              lo8_unscale(u);
+            }
             epilogue_swiglu(args, row, (n0 + b * 128) / 2 + c * 32, g, u);
           }
         }
@@ -387,6 +434,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint32_t v[32];
           tmem_ld_32x32b_x32(tl + c * 32, v);
           tmem_ld_wait();
+          if constexpr (PL == PL_LO8) lo8_unscale(v);
           if (args.ksplit > 1) epilogue_chunk_atomic(args, row, n0 + c * 32, v);
           else epilogue_chunk<EP>(args, row, n0 + c * 32, v);
         }
@@ -514,17 +562,24 @@ static int get_encode_fn() {
   return g_encode ? B200_OK : sdb_fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
 }
 
-static int make_act_map(CUtensorMap* map, const uint16_t* x, int m, int k, int ldx, int box_rows = GEMM_BM) {
+// [m, k] row-major tiles of GEMM_BK columns x box_rows rows: bf16 with 128-byte swizzle (128-byte
+// rows), or e4m3 bytes with 64-byte swizzle (64-byte rows). ld is in elements.
+static int make_tile_map(CUtensorMap* map, const void* x, bool e4m3, int m, int k, int ld, int box_rows) {
   if (int rc = get_encode_fn()) return rc;
+  const int eb = e4m3 ? 1 : 2;
   cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(m)};
-  cuuint64_t strides[1] = {cuuint64_t(ldx) * 2};
+  cuuint64_t strides[1] = {cuuint64_t(ld) * eb};
   cuuint32_t box[2] = {GEMM_BK, cuuint32_t(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  CUresult r = g_encode(map, e4m3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                        const_cast<void*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        e4m3 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return sdb_fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activation tile");
+  if (r != CUDA_SUCCESS) return sdb_fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled failed for a GEMM tile");
   return B200_OK;
+}
+static int make_act_map(CUtensorMap* map, const uint16_t* x, int m, int k, int ldx, int box_rows = GEMM_BM) {
+  return make_tile_map(map, x, false, m, k, ldx, box_rows);
 }
 
 static int check_linear(const uint16_t* x, const uint16_t* xl, int m, int k, int ldx, const b200_qweight* w,
@@ -544,6 +599,8 @@ static int check_linear(const uint16_t* x, const uint16_t* xl, int m, int k, int
   if (o->epilogue != B200_EP_SWIGLU && o->ldo < o->n_valid)
     return sdb_fail(B200_ERR_SHAPE, "b200_linear: ldo < n_valid");
   if (o->epilogue < 0 || o->epilogue > 2) return sdb_fail(B200_ERR_ARG, "b200_linear: unknown epilogue");
+  if (o->lo_format != B200_LO_BF16 && o->lo_format != B200_LO_E4M3)
+    return sdb_fail(B200_ERR_ARG, "b200_linear: unknown lo_format");
   if (w->format < 0 || w->format > 3) return sdb_fail(B200_ERR_FORMAT, "b200_linear: unknown weight format");
   if (w->format != B200_W_BF16 && !w->scales) return sdb_fail(B200_ERR_ARG, "b200_linear: missing scales");
   if (w->format == B200_W_NVFP4 && !w->row_scale) return sdb_fail(B200_ERR_ARG, "b200_linear: missing row_scale");
@@ -571,14 +628,14 @@ static int sm_count() {  // one process drives one device
   return n_sm;
 }
 
-template <int BN, int FMT, int EP, bool SPLIT>
-static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b, const GemmArgs& a,
-                     cudaStream_t st) {
-  constexpr int smem = GemmSmem<BN, FMT, SPLIT>::TOTAL;
+template <int BN, int FMT, int EP, int PL>
+static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b,
+                     const CUtensorMap& map_b8, const GemmArgs& a, cudaStream_t st) {
+  constexpr int smem = GemmSmem<BN, FMT, PL>::TOTAL;
   static_assert(smem <= 227 * 1024, "GEMM shared memory exceeds the 227 KB per-CTA limit");
   static bool attr_set = false;  // per instantiation; one process drives one device
   if (!attr_set) {
-    SDB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, FMT, EP, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    SDB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, FMT, EP, PL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   smem));
     attr_set = true;
   }
@@ -596,8 +653,8 @@ static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_lo, const CU
   // programmatic dependent launch: the CTA set-up (barriers, TMEM, descriptor prefetch)
   // overlaps the tail of the kernel before it in the stream (the kernel waits before its
   // first shared access)
-  SDB_CUDA(launch_pdl(gemm_tc_kernel<BN, FMT, EP, SPLIT>, dim3(std::min(units, n_sm)), dim3(GEMM_THREADS), smem, st,
-                      map, map_lo, map_b, args));
+  SDB_CUDA(launch_pdl(gemm_tc_kernel<BN, FMT, EP, PL>, dim3(std::min(units, n_sm)), dim3(GEMM_THREADS), smem, st,
+                      map, map_lo, map_b, map_b8, args));
   return B200_OK;
 }
 
@@ -608,31 +665,31 @@ static int tile_bn(const GemmArgs& a) {
   return 2 * tiles256 <= sm_count() ? 128 : 256;
 }
 
-template <int FMT, bool SPLIT>
-static int dispatch_ep(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b, const GemmArgs& a,
-                       cudaStream_t st) {
+template <int FMT, int PL>
+static int dispatch_ep(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b,
+                       const CUtensorMap& map_b8, const GemmArgs& a, cudaStream_t st) {
   const bool narrow = tile_bn(a) == 128;
   switch (a.o.epilogue) {
     case B200_EP_STORE:
-      return narrow ? launch_tc<128, FMT, B200_EP_STORE, SPLIT>(map, map_lo, map_b, a, st)
-                    : launch_tc<256, FMT, B200_EP_STORE, SPLIT>(map, map_lo, map_b, a, st);
+      return narrow ? launch_tc<128, FMT, B200_EP_STORE, PL>(map, map_lo, map_b, map_b8, a, st)
+                    : launch_tc<256, FMT, B200_EP_STORE, PL>(map, map_lo, map_b, map_b8, a, st);
     case B200_EP_RESID_ADD:
-      return narrow ? launch_tc<128, FMT, B200_EP_RESID_ADD, SPLIT>(map, map_lo, map_b, a, st)
-                    : launch_tc<256, FMT, B200_EP_RESID_ADD, SPLIT>(map, map_lo, map_b, a, st);
+      return narrow ? launch_tc<128, FMT, B200_EP_RESID_ADD, PL>(map, map_lo, map_b, map_b8, a, st)
+                    : launch_tc<256, FMT, B200_EP_RESID_ADD, PL>(map, map_lo, map_b, map_b8, a, st);
     default:
-      return narrow ? launch_tc<128, FMT, B200_EP_SWIGLU, SPLIT>(map, map_lo, map_b, a, st)
-                    : launch_tc<256, FMT, B200_EP_SWIGLU, SPLIT>(map, map_lo, map_b, a, st);
+      return narrow ? launch_tc<128, FMT, B200_EP_SWIGLU, PL>(map, map_lo, map_b, map_b8, a, st)
+                    : launch_tc<256, FMT, B200_EP_SWIGLU, PL>(map, map_lo, map_b, map_b8, a, st);
   }
 }
 
-template <bool SPLIT>
+template <int PL>
 static int dispatch_fmt(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b, const GemmArgs& a,
                         cudaStream_t st) {
   switch (a.w.format) {
-    case B200_W_BF16: return dispatch_ep<B200_W_BF16, SPLIT>(map, map_lo, map_b, a, st);
-    case B200_W_INT4G128: return dispatch_ep<B200_W_INT4G128, SPLIT>(map, map_lo, map_b, a, st);
-    case B200_W_NVFP4: return dispatch_ep<B200_W_NVFP4, SPLIT>(map, map_lo, map_b, a, st);
-    default: return dispatch_ep<B200_W_TERNARY, SPLIT>(map, map_lo, map_b, a, st);
+    case B200_W_BF16: return dispatch_ep<B200_W_BF16, PL>(map, map_lo, map_b, map, a, st);
+    case B200_W_INT4G128: return dispatch_ep<B200_W_INT4G128, PL>(map, map_lo, map_b, map, a, st);
+    case B200_W_NVFP4: return dispatch_ep<B200_W_NVFP4, PL>(map, map_lo, map_b, map, a, st);
+    default: return dispatch_ep<B200_W_TERNARY, PL>(map, map_lo, map_b, map, a, st);
   }
 }
 
@@ -676,7 +733,25 @@ extern "C" int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m
     map_b = map;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  return x_lo ? dispatch_fmt<true>(map, map_lo, map_b, a, st) : dispatch_fmt<false>(map, map_lo, map_b, a, st);
+  return x_lo ? dispatch_fmt<PL_SPLIT>(map, map_lo, map_b, a, st) : dispatch_fmt<PL_ONE>(map, map_lo, map_b, a, st);
+}
+
+extern "C" int b200_linear_lo8(const uint16_t* x_hi, const uint8_t* x_lo8, int32_t m, int32_t k, int32_t ldx,
+                               const uint16_t* w_hi, const uint8_t* w_lo8, int32_t n, const b200_linear_out* out,
+                               b200_stream stream) {
+  if (!x_lo8 || !w_lo8) return sdb_fail(B200_ERR_ARG, "b200_linear_lo8: null low plane or e4m3 weight");
+  const b200_qweight w{B200_W_BF16, n, k, w_hi, nullptr, nullptr, nullptr, nullptr};
+  if (int rc = check_linear(x_hi, reinterpret_cast<const uint16_t*>(x_lo8), m, k, ldx, &w, out)) return rc;
+  if (ldx % 16 != 0 || (reinterpret_cast<uintptr_t>(w_hi) & 15) || (reinterpret_cast<uintptr_t>(w_lo8) & 15))
+    return sdb_fail(B200_ERR_SHAPE, "b200_linear_lo8: ldx % 16 and 16-byte aligned weight copies required");
+  GemmArgs a{w, *out, m, k, 1};
+  const int bn = tile_bn(a);
+  CUtensorMap map, map_lo, map_b, map_b8;
+  if (int rc = make_tile_map(&map, x_hi, false, m, k, ldx, GEMM_BM)) return rc;
+  if (int rc = make_tile_map(&map_lo, x_lo8, true, m, k, ldx, GEMM_BM)) return rc;
+  if (int rc = make_tile_map(&map_b, w_hi, false, n, k, k, bn)) return rc;
+  if (int rc = make_tile_map(&map_b8, w_lo8, true, n, k, k, bn)) return rc;
+  return dispatch_ep<B200_W_BF16, PL_LO8>(map, map_lo, map_b, map_b8, a, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int b200_linear_simt(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m, int32_t k, int32_t ldx,

@@ -25,17 +25,11 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const uint16_t* __
   }
 }
 
-// hi = bf16_rn(x), lo = bf16_rn(x - hi) for two values, packed.
-__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
-  const uint16_t ha = f32_to_bf16_rn(a), hb = f32_to_bf16_rn(b);
-  hi = uint32_t(ha) | (uint32_t(hb) << 16);
-  lo = pack_bf16x2(a - bf16_to_f32(ha), b - bf16_to_f32(hb));
-}
 
-// One warp per row: y = x * rsqrt(mean(x^2) + eps) * (1 + w) as hi/lo bf16 planes.
-// hidden % 128 == 0.
+// One warp per row: y = x * rsqrt(mean(x^2) + eps) * (1 + w) as hi/lo planes (lo in bf16, or
+// e4m3 with lo8). hidden % 128 == 0.
 __global__ void rmsnorm_kernel(const float* __restrict__ x, int rows, int hidden, const float* __restrict__ w,
-                               float eps, uint16_t* __restrict__ out, long long lo_offset) {
+                               float eps, uint16_t* __restrict__ out, long long lo_offset, int lo8) {
   pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
   pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -49,16 +43,11 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, int rows, int hidden
   }
   ss = warp_sum(ss);
   const float r = rsqrtf(ss / float(hidden) + eps);
-  uint2* o = reinterpret_cast<uint2*>(out + size_t(row) * hidden);
-  uint2* ol = reinterpret_cast<uint2*>(out + lo_offset + size_t(row) * hidden);
   const float4* wr = reinterpret_cast<const float4*>(w);
   for (int i = lane; i < hidden / 4; i += 32) {
     float4 v = xr[i], g = __ldg(wr + i);
-    uint2 hi, lo;
-    split2(v.x * r * (1.0f + g.x), v.y * r * (1.0f + g.y), hi.x, lo.x);
-    split2(v.z * r * (1.0f + g.z), v.w * r * (1.0f + g.w), hi.y, lo.y);
-    o[i] = hi;
-    if (lo_offset) ol[i] = lo;
+    store_planes4(out, lo_offset, lo8, size_t(row) * hidden + 4 * i, v.x * r * (1.0f + g.x), v.y * r * (1.0f + g.y),
+                  v.z * r * (1.0f + g.z), v.w * r * (1.0f + g.w));
   }
 }
 
@@ -66,7 +55,8 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, int rows, int hidden
 // (hidden <= 4096, hidden % 1024 == 0), so each row costs one load round trip.
 __global__ void __launch_bounds__(256) rmsnorm_block_kernel(const float* __restrict__ x, int hidden,
                                                             const float* __restrict__ w, float eps,
-                                                            uint16_t* __restrict__ out, long long lo_offset) {
+                                                            uint16_t* __restrict__ out, long long lo_offset,
+                                                            int lo8) {
   __shared__ float part[8];
   pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
   pdl_trigger();
@@ -89,19 +79,14 @@ __global__ void __launch_bounds__(256) rmsnorm_block_kernel(const float* __restr
 #pragma unroll
   for (int i = 0; i < 8; ++i) tot += part[i];
   const float r = rsqrtf(tot / float(hidden) + eps);
-  uint2* o = reinterpret_cast<uint2*>(out + size_t(row) * hidden);
-  uint2* ol = reinterpret_cast<uint2*>(out + lo_offset + size_t(row) * hidden);
   const float4* wr = reinterpret_cast<const float4*>(w);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     if (i < n4) {
       const int j = tid + 256 * i;
       const float4 g = __ldg(wr + j);
-      uint2 hi, lo;
-      split2(v[i].x * r * (1.0f + g.x), v[i].y * r * (1.0f + g.y), hi.x, lo.x);
-      split2(v[i].z * r * (1.0f + g.z), v[i].w * r * (1.0f + g.w), hi.y, lo.y);
-      o[j] = hi;
-      if (lo_offset) ol[j] = lo;
+      store_planes4(out, lo_offset, lo8, size_t(row) * hidden + 4 * j, v[i].x * r * (1.0f + g.x),
+                    v[i].y * r * (1.0f + g.y), v[i].z * r * (1.0f + g.z), v[i].w * r * (1.0f + g.w));
     }
   }
 }
@@ -442,18 +427,28 @@ int sdb_embed_vocab(const int32_t* ids, int32_t n_tokens, const uint16_t* table,
   return B200_OK;
 }
 
+int sdb_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
+                int64_t lo_offset, int lo8, cudaStream_t st) {
+  if (!x || !w || !out) return sdb_fail(B200_ERR_ARG, "b200_rmsnorm: null pointer");
+  if (rows <= 0 || hidden % 128 != 0 || lo_offset % 8 != 0 || (reinterpret_cast<uintptr_t>(out) & 15))
+    return sdb_fail(B200_ERR_SHAPE, "b200_rmsnorm: hidden % 128 and lo_offset % 8 must be 0, out 16-byte aligned");
+  if (rows <= 1024 && hidden % 1024 == 0 && hidden <= 4096)
+    SDB_CUDA(launch_pdl(rmsnorm_block_kernel, dim3(rows), dim3(256), 0, st, x, hidden, w, eps, out, lo_offset, lo8));
+  else
+    SDB_CUDA(launch_pdl(rmsnorm_kernel, dim3((rows + 7) / 8), dim3(256), 0, st, x, rows, hidden, w, eps, out,
+                        lo_offset, lo8));
+  return B200_OK;
+}
+
 extern "C" int b200_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
                             int64_t lo_offset, b200_stream stream) {
-  if (!x || !w || !out) return sdb_fail(B200_ERR_ARG, "b200_rmsnorm: null pointer");
-  if (rows <= 0 || hidden % 128 != 0 || lo_offset % 8 != 0)
-    return sdb_fail(B200_ERR_SHAPE, "b200_rmsnorm: hidden % 128 and lo_offset % 8 must be 0");
-  if (rows <= 1024 && hidden % 1024 == 0 && hidden <= 4096)
-    SDB_CUDA(launch_pdl(rmsnorm_block_kernel, dim3(rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), x,
-                        hidden, w, eps, out, lo_offset));
-  else
-    SDB_CUDA(launch_pdl(rmsnorm_kernel, dim3((rows + 7) / 8), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), x,
-                        rows, hidden, w, eps, out, lo_offset));
-  return B200_OK;
+  return sdb_rmsnorm(x, rows, hidden, w, eps, out, lo_offset, 0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b200_rmsnorm_lo8(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
+                                int64_t lo_offset, b200_stream stream) {
+  if (!lo_offset) return sdb_fail(B200_ERR_ARG, "b200_rmsnorm_lo8: lo_offset must locate the e4m3 plane");
+  return sdb_rmsnorm(x, rows, hidden, w, eps, out, lo_offset, 1, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int sdb_decide_vocab(const float* x, int32_t hidden, const float* final_norm, float eps, const uint16_t* table,

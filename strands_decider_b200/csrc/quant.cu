@@ -109,9 +109,11 @@ __global__ void quant_ternary_kernel(const float* __restrict__ w, int n, int k, 
   }
 }
 
-// Standalone dequantiser: one thread per 32 weights, through the GEMM's own unpackers.
+// Standalone dequantiser: one thread per 32 weights, through the GEMM's own unpackers. With
+// out8, the two copies of b200_linear_lo8 instead: out = W * 2^B200_LO8_SHIFT (bf16, exact)
+// and out8 = e4m3(W * 2^B200_LO8_W_SHIFT).
 template <int FMT>
-__global__ void dequant_kernel(b200_qweight w, uint16_t* __restrict__ out) {
+__global__ void dequant_kernel(b200_qweight w, uint16_t* __restrict__ out, uint8_t* __restrict__ out8) {
   __shared__ uint32_t lut[16];
   // the packed weights are constant, but `out` may still be read by the GEMM before this kernel
   pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
@@ -132,6 +134,23 @@ __global__ void dequant_kernel(b200_qweight w, uint16_t* __restrict__ out) {
     float gs;
     load32<FMT>(w, row, k0, raw, sc, gs);
     unpack32<FMT>(raw, sc, gs, dst, lut);
+  }
+  if (out8) {
+    uint16_t* h = reinterpret_cast<uint16_t*>(dst);
+    uint32_t q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float f[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) f[e] = bf16_to_f32(h[4 * i + e]);
+      constexpr float ws = float(1 << B200_LO8_W_SHIFT), hs = float(1 << B200_LO8_SHIFT);
+      q[i] = e4m3x4(f[0] * ws, f[1] * ws, f[2] * ws, f[3] * ws);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) h[4 * i + e] = f32_to_bf16_rn(f[e] * hs);  // a power of two: exact
+    }
+    uint4* o8 = reinterpret_cast<uint4*>(out8 + size_t(row) * w.k + k0);
+    o8[0] = make_uint4(q[0], q[1], q[2], q[3]);
+    o8[1] = make_uint4(q[4], q[5], q[6], q[7]);
   }
   uint4* o = reinterpret_cast<uint4*>(out + size_t(row) * w.k + k0);
   for (int c = 0; c < 4; ++c) o[c] = dst[c];
@@ -227,22 +246,35 @@ extern "C" int b200_quantize(int32_t format, const float* w, int32_t n, int32_t 
   return B200_OK;
 }
 
-extern "C" int b200_dequantize(const b200_qweight* w, uint16_t* out, b200_stream stream) {
+static int dequantize(const b200_qweight* w, uint16_t* out, uint8_t* out8, cudaStream_t st) {
   if (!w || !out || !w->data) return sdb_fail(B200_ERR_ARG, "b200_dequantize: null pointer");
   if (w->n <= 0 || w->k <= 0 || w->k % 128 != 0) return sdb_fail(B200_ERR_SHAPE, "b200_dequantize: bad shape");
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(out8)) & 15)
+    return sdb_fail(B200_ERR_SHAPE, "b200_dequantize: outputs must be 16-byte aligned");
   const int total = w->n * (w->k / 32);
   const dim3 grid((total + 255) / 256), block(256);
   switch (w->format) {
-    case B200_W_BF16: SDB_CUDA(launch_pdl(dequant_kernel<B200_W_BF16>, grid, block, 0, st, *w, out)); break;
-    case B200_W_INT4G128: SDB_CUDA(launch_pdl(dequant_kernel<B200_W_INT4G128>, grid, block, 0, st, *w, out)); break;
+    case B200_W_BF16: SDB_CUDA(launch_pdl(dequant_kernel<B200_W_BF16>, grid, block, 0, st, *w, out, out8)); break;
+    case B200_W_INT4G128:
+      SDB_CUDA(launch_pdl(dequant_kernel<B200_W_INT4G128>, grid, block, 0, st, *w, out, out8));
+      break;
     case B200_W_NVFP4:
       if (!w->row_scale) return sdb_fail(B200_ERR_ARG, "b200_dequantize: nvfp4 needs row_scale");
-      SDB_CUDA(launch_pdl(dequant_kernel<B200_W_NVFP4>, grid, block, 0, st, *w, out));
+      SDB_CUDA(launch_pdl(dequant_kernel<B200_W_NVFP4>, grid, block, 0, st, *w, out, out8));
       break;
-    case B200_W_TERNARY: SDB_CUDA(launch_pdl(dequant_kernel<B200_W_TERNARY>, grid, block, 0, st, *w, out)); break;
+    case B200_W_TERNARY:
+      SDB_CUDA(launch_pdl(dequant_kernel<B200_W_TERNARY>, grid, block, 0, st, *w, out, out8));
+      break;
     default: return sdb_fail(B200_ERR_FORMAT, "b200_dequantize: unknown format");
   }
-  SDB_LAUNCH_CHECK();
   return B200_OK;
+}
+
+extern "C" int b200_dequantize(const b200_qweight* w, uint16_t* out, b200_stream stream) {
+  return dequantize(w, out, nullptr, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b200_dequantize_lo8(const b200_qweight* w, uint16_t* w_hi, uint8_t* w_lo8, b200_stream stream) {
+  if (!w_lo8) return sdb_fail(B200_ERR_ARG, "b200_dequantize_lo8: null e4m3 output");
+  return dequantize(w, w_hi, w_lo8, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -24,7 +24,8 @@ int sdb_embed_vocab(const int32_t* ids, int32_t n_tokens, const uint16_t* table,
 int sdb_decide_vocab(const float* x, int32_t hidden, const float* final_norm, float eps, const uint16_t* table,
                      const b200_decide_args* d, int vocab, int n_tokens, cudaStream_t st);
 int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix, int32_t ld_mix, uint16_t* out,
-                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, float* prep, cudaStream_t st);
+                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, float* prep, int lo8,
+                  cudaStream_t st);
 int sdb_gdn_prep_floats(int heads, int n_tokens);
 namespace sdb {
 int sdb_check_readout(const b200_readout* hd, int hidden);
@@ -33,7 +34,9 @@ int sdb_decide_readout(const float* x, int32_t hidden, const float* final_norm, 
 }  // namespace sdb
 int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qkv, int32_t ld_qkv, uint16_t* q_buf,
                   uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool,
-                  int32_t layer, cudaStream_t st);
+                  int32_t layer, int lo8, cudaStream_t st);
+int sdb_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
+                int64_t lo_offset, int lo8, cudaStream_t st);
 
 extern "C" const char* b200_last_error(void) { return g_last_error.c_str(); }
 extern "C" int b200_version(void) { return 100; }
@@ -77,6 +80,8 @@ struct b200_model {
     const int from = cfg.dequant_min_tokens == 0 ? 4096 : cfg.dequant_min_tokens;
     return from > 0 && T >= from;
   }
+  // GEMMs of this batch run on e4m3 low planes (b200_linear_lo8)
+  bool lo8_at(int T) const { return cfg.lo_format == B200_LO_E4M3 && dequant_at(T); }
   bool has_attn() const {
     for (int i = 0; i < cfg.n_layers; ++i)
       if (cfg.layer_kind[i] == B200_LAYER_ATTN) return true;
@@ -94,8 +99,10 @@ namespace {
 //   q, k, v  bf16                    attention scratch (post norm + RoPE)
 //   prep fp32                        GDN scratch (conv / l2norm / gating outputs)
 //   wdq  bf16 [N, K]                 one dequantised weight (batches of >= dequant_min_tokens)
+//   wdq8 e4m3 [N, K]                 its e4m3 copy (lo_format B200_LO_E4M3)
+// With e4m3 low planes the xn / act lo planes hold one byte per element in the same space.
 struct WsLayout {
-  size_t x, xn, mix, act, q, k, v, prep, wdq, total;
+  size_t x, xn, mix, act, q, k, v, prep, wdq, wdq8, total;
   int mix_cols, act_cols;
   long long xn_lo, act_lo;  // element offsets of the lo planes
 };
@@ -137,15 +144,21 @@ WsLayout layout(const b200_model& m, int T) {
         most = std::max(most, size_t(q->n) * size_t(q->k));
     }
     L.wdq = take(most * 2);
+    if (m.lo8_at(T)) L.wdq8 = take(most);
   }
   L.total = off;
   return L;
 }
 
 // One linear layer: for large batches the packed weight is first dequantised into the bf16
-// buffer (bit-exact with the GEMM's own unpack), then the GEMM streams it by TMA.
+// buffer (bit-exact with the GEMM's own unpack), then the GEMM streams it by TMA. With e4m3
+// low planes (wdq8) the dequantiser writes the two copies b200_linear_lo8 reads.
 int run_linear(const b200_model& m, const uint16_t* x, const uint16_t* x_lo, int T, int k, const b200_qweight& w,
-               const b200_linear_out& o, uint16_t* wdq, b200_stream stream) {
+               const b200_linear_out& o, uint16_t* wdq, uint8_t* wdq8, b200_stream stream) {
+  if (wdq8) {
+    if (int rc = b200_dequantize_lo8(&w, wdq, wdq8, stream)) return rc;
+    return b200_linear_lo8(x, reinterpret_cast<const uint8_t*>(x_lo), T, k, k, wdq, wdq8, w.n, &o, stream);
+  }
   if (wdq && m.dequant_at(T) && w.format != B200_W_BF16) {
     if (int rc = b200_dequantize(&w, wdq, stream)) return rc;
     b200_qweight wb{};
@@ -173,6 +186,8 @@ extern "C" int b200_model_create(const b200_model_config* cfg, b200_model** out)
   if (cfg->n_layers <= 0 || cfg->n_layers > 64 || cfg->hidden % 128 != 0 || cfg->inter % 128 != 0)
     return sdb_fail(B200_ERR_SHAPE, "b200_model_create: bad layer count or hidden/inter not a multiple of 128");
   if (cfg->weight_format < 0 || cfg->weight_format > 3) return sdb_fail(B200_ERR_FORMAT, "b200_model_create: format");
+  if (cfg->lo_format != B200_LO_BF16 && cfg->lo_format != B200_LO_E4M3)
+    return sdb_fail(B200_ERR_ARG, "b200_model_create: unknown lo_format");
   auto* m = new b200_model();
   m->cfg = *cfg;
   m->layers.resize(cfg->n_layers);
@@ -299,36 +314,40 @@ extern "C" int b200_model_forward(b200_model* m, const int32_t* ids, const b200_
   uint16_t* vb = reinterpret_cast<uint16_t*>(ws + L.v);
   float* prep = reinterpret_cast<float*>(ws + L.prep);
   uint16_t* wdq = L.wdq ? reinterpret_cast<uint16_t*>(ws + L.wdq) : nullptr;
+  uint8_t* wdq8 = L.wdq8 ? ws + L.wdq8 : nullptr;
+  const int lo8 = wdq8 ? 1 : 0;
   const uint16_t* xn_lo = xn + L.xn_lo;
 
   int rc;
   if ((rc = sdb_embed_vocab(ids, T, m->embed, c.hidden, x, c.vocab, st))) return rc;
   for (int li = 0; li < c.n_layers; ++li) {
     const b200_layer_weights& w = m->layers[li];
-    if ((rc = b200_rmsnorm(x, T, c.hidden, w.input_norm, c.eps, xn, L.xn_lo, stream))) return rc;
+    if ((rc = sdb_rmsnorm(x, T, c.hidden, w.input_norm, c.eps, xn, L.xn_lo, lo8, st))) return rc;
     int mix_in_dim;
     if (c.layer_kind[li] == B200_LAYER_GDN) {
       const int n = m->gdn_in_cols();
       b200_linear_out o{B200_EP_STORE, n, mix, n, 0};
-      if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.mix_in, o, wdq, stream))) return rc;
-      if ((rc = sdb_gdn_mixer(&w.gdn, seqs, mix, n, act, L.act_lo, pool, m->kind_index[li], prep, st))) return rc;
+      if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.mix_in, o, wdq, wdq8, stream))) return rc;
+      if ((rc = sdb_gdn_mixer(&w.gdn, seqs, mix, n, act, L.act_lo, pool, m->kind_index[li], prep, lo8, st)))
+        return rc;
       mix_in_dim = m->value_dim();
     } else {
       const int n = m->attn_qkv();
       b200_linear_out o{B200_EP_STORE, n, mix, n, 0};
-      if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.mix_in, o, wdq, stream))) return rc;
+      if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.mix_in, o, wdq, wdq8, stream))) return rc;
       b200_attn_params ap{c.attn_heads, c.attn_kv_heads, c.head_dim, c.rope_dim, c.max_pos, c.eps,
                           w.q_norm, w.k_norm, m->rope_cos, m->rope_sin};
-      if ((rc = sdb_attention(&ap, seqs, mix, n, qb, kb, vb, act, L.act_lo, pool, m->kind_index[li], st))) return rc;
+      if ((rc = sdb_attention(&ap, seqs, mix, n, qb, kb, vb, act, L.act_lo, pool, m->kind_index[li], lo8, st)))
+        return rc;
       mix_in_dim = m->attn_o_in();
     }
     b200_linear_out r{B200_EP_RESID_ADD, c.hidden, x, c.hidden, 0};
-    if ((rc = run_linear(*m, act, act + L.act_lo, T, mix_in_dim, w.mix_out, r, wdq, stream))) return rc;
-    if ((rc = b200_rmsnorm(x, T, c.hidden, w.post_norm, c.eps, xn, L.xn_lo, stream))) return rc;
-    b200_linear_out g{B200_EP_SWIGLU, 2 * c.inter, act, c.inter, L.act_lo};
-    if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.gate_up, g, wdq, stream))) return rc;
+    if ((rc = run_linear(*m, act, act + L.act_lo, T, mix_in_dim, w.mix_out, r, wdq, wdq8, stream))) return rc;
+    if ((rc = sdb_rmsnorm(x, T, c.hidden, w.post_norm, c.eps, xn, L.xn_lo, lo8, st))) return rc;
+    b200_linear_out g{B200_EP_SWIGLU, 2 * c.inter, act, c.inter, L.act_lo, lo8 ? B200_LO_E4M3 : B200_LO_BF16};
+    if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.gate_up, g, wdq, wdq8, stream))) return rc;
     b200_linear_out d{B200_EP_RESID_ADD, c.hidden, x, c.hidden, 0};
-    if ((rc = run_linear(*m, act, act + L.act_lo, T, c.inter, w.down, d, wdq, stream))) return rc;
+    if ((rc = run_linear(*m, act, act + L.act_lo, T, c.inter, w.down, d, wdq, wdq8, stream))) return rc;
   }
   if (seqs->save_slot) {
     if (!pool || !pool->slot_len) return sdb_fail(B200_ERR_ARG, "b200_model_forward: save slots need a pool");

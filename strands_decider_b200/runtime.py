@@ -52,9 +52,14 @@ class Decisions:
 class DecisionModel:
     def __init__(self, weights: DeviceWeights, max_tokens: int = 8192, pool_slots: int = 64,
                  pool_kv_tokens: int | None = None, device: str | torch.device = "cuda",
-                 dequant_min_tokens: int = 0):
+                 dequant_min_tokens: int = 0, lo_plane: str = "bf16"):
         """dequant_min_tokens: batches of at least this many tokens run each GEMM on a bf16 copy
-        of its weight dequantised once per call (0 = the library default, 4096; < 0 = never)."""
+        of its weight dequantised once per call (0 = the library default, 4096; < 0 = never).
+        lo_plane: the low activation plane of those GEMMs, "bf16" (two bf16 planes, about 16
+        significant bits) or "e4m3" (e4m3 low plane against an e4m3 weight copy: 3/4 of the
+        tensor work, about 12 significant bits in the low term)."""
+        if lo_plane not in ("bf16", "e4m3"):
+            raise ValueError(f"lo_plane must be 'bf16' or 'e4m3', not {lo_plane!r}")
         _lib.load()
         self.w = weights
         self.spec = s = weights.spec
@@ -69,6 +74,8 @@ class DecisionModel:
         cfg.rope_dim, cfg.max_pos, cfg.eps = s.rope_dim, s.max_positions, s.eps
         cfg.weight_format = _lib.FMT[s.weight_format]
         cfg.dequant_min_tokens = dequant_min_tokens
+        cfg.lo_format = _lib.LO_E4M3 if lo_plane == "e4m3" else _lib.LO_BF16
+        self.lo_plane = lo_plane
         self._cfg = cfg
         h = C.c_void_p()
         _lib.check(_lib.load().b200_model_create(C.byref(cfg), C.byref(h)))
