@@ -453,7 +453,7 @@ def main() -> None:
     ap.add_argument("--requests-per-step", type=int, default=0, help="0 = the workload's default")
     ap.add_argument("--cpu-sample", type=int, default=3, help="requests in the CPU baseline sample (0 = skip)")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
-    ap.add_argument("--lo-plane", default="bf16", choices=["bf16", "e4m3"],
+    ap.add_argument("--lo-plane", default="e4m3", choices=["bf16", "e4m3"],
                     help="low activation plane of the large-batch GEMMs (DecisionModel lo_plane)")
     args = ap.parse_args()
 

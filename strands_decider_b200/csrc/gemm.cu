@@ -27,6 +27,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 
 #include "dequant.cuh"
@@ -58,6 +59,7 @@ struct GemmArgs {
   b200_linear_out o;
   int m, k;
   int ksplit;  // > 1: each output tile is summed from ksplit K-ranges by fp32 atomic adds
+  int ngroup;  // CTA pairs: N tiles per group (units walk all row tiles of one group, then the next)
 };
 
 // Work unit u -> output tile (m0, n0) and its K range [kb0, kb1) in GEMM_BK blocks. N is
@@ -327,6 +329,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if constexpr (!SM::PACKED) tma_prefetch_desc(&tmB);
       if constexpr (PL == PL_LO8) tma_prefetch_desc(&tmB8);
       constexpr int RB = SM::PACKED ? tile_row_bytes(FMT) : 0, SB = tile_scale_row_bytes(FMT);
+      const uint64_t keep = l2_evict_last_policy();  // weight tiles: re-read for every row tile
       uint32_t it = 0;
       for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
         const GemmUnit w = gemm_unit<BN>(args, u, nk);
@@ -358,8 +361,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           // (an e4m3 tile's x coordinate is in bytes = elements: kt * 64, a multiple of 16)
           if constexpr (PL != PL_ONE)
             tma_load_2d(sA + s * SM::A_STAGE + SM::A_BYTES, &tmA_lo, &full_a[s], kt * GEMM_BK, m0);
-          if constexpr (!SM::PACKED) tma_load_2d(sB + s * SM::B_BYTES, &tmB, &full_a[s], kt * GEMM_BK, n0);
-          if constexpr (PL == PL_LO8) tma_load_2d(sB8 + s * SM::B8_BYTES, &tmB8, &full_a[s], kt * GEMM_BK, n0);
+          if constexpr (!SM::PACKED) tma_load_2d_hint(sB + s * SM::B_BYTES, &tmB, &full_a[s], kt * GEMM_BK, n0, keep);
+          if constexpr (PL == PL_LO8)
+            tma_load_2d_hint(sB8 + s * SM::B8_BYTES, &tmB8, &full_a[s], kt * GEMM_BK, n0, keep);
         }
       }
     }
@@ -483,6 +487,210 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// --------------------------------------------------------------------------- CTA pairs
+// Large M with bf16 weight copies (the dequantised path, hi + bf16 or e4m3 lo planes): a
+// cluster of two CTAs computes 256 x 256 tiles with tcgen05.mma.cta_group::2 (M = 256). Each
+// CTA stages its own 128 activation rows and its half (128 rows) of the weight tile; the
+// leader CTA's MMAs read both CTAs' shared memory at the same offsets, and each CTA's tensor
+// memory holds its 128 accumulator rows x 256 columns (x 2 buffers). Per FLOP every SM then
+// streams and reads half the weight bytes of a one-CTA 128 x 256 tile, which is what bounds
+// the one-CTA kernel here (shared-memory operand traffic, not the tensor pipe's rate).
+//   warp 0 (both CTAs)   one lane streams the stage: TMA loads signalled on the leader's
+//                        full barrier (the leader also posts the pair's expected bytes)
+//   warp 1 (leader)      one lane issues the pair MMAs; commits release both CTAs' stage
+//                        (empty) and accumulator (acc_full) barriers
+//   warps 2..5 (both)    epilogue of the CTA's 128 rows; one arrival per warp on the
+//                        leader's acc_empty (8 per tile)
+constexpr int GEMM2_THREADS = 192;
+constexpr int GEMM2_STAGES = 4;
+
+template <int PL>
+struct Gemm2Smem {
+  static constexpr int A_BYTES = 128 * GEMM_BK * 2;
+  static constexpr int A_LO_BYTES = PL == PL_SPLIT ? A_BYTES : PL == PL_LO8 ? 128 * GEMM_BK : 0;
+  static constexpr int A_STAGE = A_BYTES + A_LO_BYTES;
+  static constexpr int B_BYTES = 128 * GEMM_BK * 2;                 // this CTA's half of the bf16 weight tile
+  static constexpr int B8_BYTES = PL == PL_LO8 ? 128 * GEMM_BK : 0;  // and of the e4m3 copy
+  static constexpr int STAGE = A_STAGE + B_BYTES + B8_BYTES;
+  static constexpr int STAGES = GEMM2_STAGES;
+  static constexpr int BARS = 2 * STAGES + 4;
+  static constexpr int TOTAL = STAGES * STAGE + 1024 + BARS * 8 + 16;
+};
+
+template <int EP, int PL>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA_lo,
+                     const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmB8,
+                     const GemmArgs args) {
+  using SM = Gemm2Smem<PL>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;                              // STAGES x A_STAGE
+  uint8_t* sB = sA + SM::STAGES * SM::A_STAGE;    // STAGES x B_BYTES
+  uint8_t* sB8 = sB + SM::STAGES * SM::B_BYTES;   // STAGES x B8_BYTES
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB8 + SM::STAGES * SM::B8_BYTES);
+  uint64_t* full = bars;                           // [STAGES], the leader's are used
+  uint64_t* empty = bars + SM::STAGES;             // [STAGES], both CTAs'
+  uint64_t* acc_full = bars + 2 * SM::STAGES;      // [2], both CTAs'
+  uint64_t* acc_empty = bars + 2 * SM::STAGES + 2; // [2], the leader's are used
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + SM::BARS);
+
+  const uint32_t rank = cluster_ctarank();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = args.k / GEMM_BK;
+  const int n_tiles_n = args.w.n / 256, m_tiles = (args.m + 255) / 256;
+  const int n_units = n_tiles_n * m_tiles;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  // unit -> (row tile, column tile): groups of ngroup column tiles, row tiles within a group,
+  // so the weight rows a group re-reads stay in L2 while the activations stream past
+  const int G = args.ngroup;
+  auto tile_of = [&](int u, int& mt, int& nt) {
+    const int g = u / (G * m_tiles), r = u - g * G * m_tiles;
+    const int gs = min(G, n_tiles_n - g * G);
+    mt = r / gs;
+    nt = g * G + r % gs;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SM::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);
+    }
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised and tensor memory allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  if (n_units <= n_pairs) pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      if constexpr (PL != PL_ONE) tma_prefetch_desc(&tmA_lo);
+      tma_prefetch_desc(&tmB);
+      if constexpr (PL == PL_LO8) tma_prefetch_desc(&tmB8);
+      const uint32_t full0 = mapa_shared(smem_addr(full), 0);
+      const uint64_t keep = l2_evict_last_policy();  // weight tiles: re-read for every row tile
+      uint32_t it = 0;
+      for (int u = pair; u < n_units; u += n_pairs) {
+        int mt, nt;
+        tile_of(u, mt, nt);
+        const int m0 = mt * 256 + int(rank) * 128, n0 = nt * 256 + int(rank) * 128;
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % SM::STAGES;
+          const uint32_t ph = (it / SM::STAGES) & 1;
+          mbar_wait(&empty[s], ph ^ 1, FAULT_GEMM_WAIT_EMPTY);
+          const uint32_t fb = full0 + 8u * s;
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * SM::STAGE);
+          tma_load_2d_pair(sA + s * SM::A_STAGE, &tmA, fb, kt * GEMM_BK, m0);
+          if constexpr (PL != PL_ONE) tma_load_2d_pair(sA + s * SM::A_STAGE + SM::A_BYTES, &tmA_lo, fb, kt * GEMM_BK, m0);
+          tma_load_2d_pair_hint(sB + s * SM::B_BYTES, &tmB, fb, kt * GEMM_BK, n0, keep);
+          if constexpr (PL == PL_LO8)
+            tma_load_2d_pair_hint(sB8 + s * SM::B8_BYTES, &tmB8, fb, kt * GEMM_BK, n0, keep);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(256, 256);
+      constexpr uint32_t idesc8 = umma_idesc_e4m3(256, 256);
+      const uint32_t empty1 = mapa_shared(smem_addr(empty), 1), acc_full1 = mapa_shared(smem_addr(acc_full), 1);
+      uint32_t it = 0, local = 0;
+      for (int u = pair; u < n_units; u += n_pairs, ++local) {
+        const uint32_t ab = local & 1, aph = (local >> 1) & 1;
+        mbar_wait(&acc_empty[ab], aph ^ 1, FAULT_GEMM_WAIT_ACCUM);
+        tc_fence_after();
+        const uint32_t acc = tmem_base + ab * 256;
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % SM::STAGES;
+          const uint32_t ph = (it / SM::STAGES) & 1;
+          mbar_wait(&full[s], ph, FAULT_GEMM_WAIT_FULL_A);
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128(smem_addr(sA + s * SM::A_STAGE));
+          const uint64_t bd = umma_desc_sw128(smem_addr(sB + s * SM::B_BYTES));
+#pragma unroll
+          for (int j = 0; j < GEMM_BK / 16; ++j) {
+            umma_pair_bf16(acc, ad + 2 * j, bd + 2 * j, idesc, (kt != 0 || j != 0) ? 1u : 0u);
+            if constexpr (PL == PL_SPLIT) umma_pair_bf16(acc, ad + (SM::A_BYTES >> 4) + 2 * j, bd + 2 * j, idesc, 1u);
+          }
+          if constexpr (PL == PL_LO8) {
+            const uint64_t ald = umma_desc_sw64(smem_addr(sA + s * SM::A_STAGE + SM::A_BYTES));
+            const uint64_t bld = umma_desc_sw64(smem_addr(sB8 + s * SM::B8_BYTES));
+#pragma unroll
+            for (int j = 0; j < GEMM_BK / 32; ++j) umma_pair_e4m3(acc, ald + 2 * j, bld + 2 * j, idesc8, 1u);
+          }
+          umma_pair_commit(smem_addr(&empty[s]));  // both CTAs may refill stage s
+          umma_pair_commit(empty1 + 8u * s);
+        }
+        umma_pair_commit(smem_addr(&acc_full[ab]));
+        umma_pair_commit(acc_full1 + 8u * ab);
+      }
+    }
+    __syncwarp();
+  } else {
+    // epilogue: warp (2..5) owns TMEM lanes 32*(warp%4)..+31 of this CTA's 128 rows
+    const int q = warp & 3;
+    const uint32_t acc_empty0 = mapa_shared(smem_addr(acc_empty), 0);
+    uint32_t local = 0;
+    for (int u = pair; u < n_units; u += n_pairs, ++local) {
+      int mt, nt;
+      tile_of(u, mt, nt);
+      const int m0 = mt * 256 + int(rank) * 128, n0 = nt * 256;
+      const uint32_t ab = local & 1, aph = (local >> 1) & 1;
+      mbar_wait(&acc_full[ab], aph, FAULT_GEMM_WAIT_ACCUM);
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const uint32_t tl = tmem_base + ab * 256 + (uint32_t(q * 32) << 16);
+      if constexpr (EP == B200_EP_SWIGLU) {
+#pragma unroll 1
+        for (int b = 0; b < 2; ++b) {
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            uint32_t g[32], v[32];
+            tmem_ld_32x32b_x32(tl + b * 128 + c * 32, g);
+            tmem_ld_32x32b_x32(tl + b * 128 + 64 + c * 32, v);
+            tmem_ld_wait();
+            if constexpr (PL == PL_LO8) {
+              lo8_unscale(g);
+              lo8_unscale(v);
+            }
+            epilogue_swiglu(args, row, (n0 + b * 128) / 2 + c * 32, g, v);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tl + c * 32, v);
+          tmem_ld_wait();
+          if constexpr (PL == PL_LO8) lo8_unscale(v);
+          epilogue_chunk<EP>(args, row, n0 + c * 32, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8u * ab);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // neither CTA leaves while the other may still read or signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
   }
 }
 
@@ -682,6 +890,56 @@ static int dispatch_ep(const CUtensorMap& map, const CUtensorMap& map_lo, const 
   }
 }
 
+// The CTA-pair kernel: bf16 weight copies, 256 x 256 tiles, at least one tile per pair.
+template <int EP, int PL>
+static int launch_pair(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b,
+                       const CUtensorMap& map_b8, const GemmArgs& a, cudaStream_t st) {
+  constexpr int smem = Gemm2Smem<PL>::TOTAL;
+  static_assert(smem <= 227 * 1024, "GEMM shared memory exceeds the 227 KB per-CTA limit");
+  static int max_pairs = 0;  // per instantiation; one process drives one device
+  if (!max_pairs) {
+    SDB_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<EP, PL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sm_count() & ~1);
+    cfg.blockDim = dim3(GEMM2_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<EP, PL>, &cfg) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = sm_count() / 2;
+    }
+    max_pairs = n;
+  }
+  GemmArgs args = a;
+  args.ksplit = 1;
+  // Weight bytes of all column tiles beyond what L2 keeps alongside the activation stream
+  // (about 48 MB here: the 126 MB L2 holds a line in each die's half when both dies read it)
+  // -> groups of column tiles of at most about 40 MB each.
+  const int n_tiles_n = a.w.n / 256;
+  const double tile_bytes = 256.0 * a.k * (PL == PL_LO8 ? 3 : 2);
+  const int groups = n_tiles_n * tile_bytes <= 48e6 ? 1 : int(std::ceil(n_tiles_n * tile_bytes / 40e6));
+  args.ngroup = (n_tiles_n + groups - 1) / groups;
+  const int units = n_tiles_n * ((a.m + 255) / 256);
+  SDB_CUDA(launch_pdl(gemm_pair_kernel<EP, PL>, dim3(2 * std::min(units, max_pairs)), dim3(GEMM2_THREADS), smem, st,
+                      map, map_lo, map_b, map_b8, args));
+  return B200_OK;
+}
+
+template <int PL>
+static int dispatch_pair(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b,
+                         const CUtensorMap& map_b8, const GemmArgs& a, cudaStream_t st) {
+  switch (a.o.epilogue) {
+    case B200_EP_STORE: return launch_pair<B200_EP_STORE, PL>(map, map_lo, map_b, map_b8, a, st);
+    case B200_EP_RESID_ADD: return launch_pair<B200_EP_RESID_ADD, PL>(map, map_lo, map_b, map_b8, a, st);
+    default: return launch_pair<B200_EP_SWIGLU, PL>(map, map_lo, map_b, map_b8, a, st);
+  }
+}
+
+// Pairs pay off once every pair has a whole 256 x 256 tile.
+static bool pair_path(const GemmArgs& a) {
+  return (a.w.n / 256) * ((a.m + 255) / 256) >= sm_count() / 2;
+}
+
 template <int PL>
 static int dispatch_fmt(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b, const GemmArgs& a,
                         cudaStream_t st) {
@@ -725,14 +983,19 @@ extern "C" int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m
     map_lo = map;
   }
   GemmArgs a{*w, *out, m, k, 1};
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (w->format == B200_W_BF16) {  // the weight tile streams through TMA as [n, k] bf16, one box per N tile
     if (reinterpret_cast<uintptr_t>(w->data) & 15) return sdb_fail(B200_ERR_SHAPE, "b200_linear: bf16 W unaligned");
+    if (pair_path(a)) {  // each CTA of a pair loads 128 of the tile's 256 weight rows
+      if (int rc = make_act_map(&map_b, reinterpret_cast<const uint16_t*>(w->data), w->n, k, k, 128)) return rc;
+      return x_lo ? dispatch_pair<PL_SPLIT>(map, map_lo, map_b, map_b, a, st)
+                  : dispatch_pair<PL_ONE>(map, map_lo, map_b, map_b, a, st);
+    }
     const int bn = tile_bn(a);
     if (int rc = make_act_map(&map_b, reinterpret_cast<const uint16_t*>(w->data), w->n, k, k, bn)) return rc;
   } else {
     map_b = map;
   }
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return x_lo ? dispatch_fmt<PL_SPLIT>(map, map_lo, map_b, a, st) : dispatch_fmt<PL_ONE>(map, map_lo, map_b, a, st);
 }
 
@@ -745,13 +1008,16 @@ extern "C" int b200_linear_lo8(const uint16_t* x_hi, const uint8_t* x_lo8, int32
   if (ldx % 16 != 0 || (reinterpret_cast<uintptr_t>(w_hi) & 15) || (reinterpret_cast<uintptr_t>(w_lo8) & 15))
     return sdb_fail(B200_ERR_SHAPE, "b200_linear_lo8: ldx % 16 and 16-byte aligned weight copies required");
   GemmArgs a{w, *out, m, k, 1};
-  const int bn = tile_bn(a);
+  const bool pair = pair_path(a);
+  const int bn = pair ? 128 : tile_bn(a);  // weight rows per TMA box (a pair CTA loads half a tile)
   CUtensorMap map, map_lo, map_b, map_b8;
   if (int rc = make_tile_map(&map, x_hi, false, m, k, ldx, GEMM_BM)) return rc;
   if (int rc = make_tile_map(&map_lo, x_lo8, true, m, k, ldx, GEMM_BM)) return rc;
   if (int rc = make_tile_map(&map_b, w_hi, false, n, k, k, bn)) return rc;
   if (int rc = make_tile_map(&map_b8, w_lo8, true, n, k, k, bn)) return rc;
-  return dispatch_ep<B200_W_BF16, PL_LO8>(map, map_lo, map_b, map_b8, a, reinterpret_cast<cudaStream_t>(stream));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (pair) return dispatch_pair<PL_LO8>(map, map_lo, map_b, map_b8, a, st);
+  return dispatch_ep<B200_W_BF16, PL_LO8>(map, map_lo, map_b, map_b8, a, st);
 }
 
 extern "C" int b200_linear_simt(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m, int32_t k, int32_t ldx,

@@ -1,6 +1,6 @@
 """Standalone launches of the hot kernels at the 2B shape, for timing and profiling.
 
-    python -m strands_decider_b200.kernel_cases gemm [--m 8192] [--fmt nvfp4] [--ep swiglu]
+    python -m strands_decider_b200.kernel_cases gemm [--m 8192] [--fmt nvfp4] [--ep swiglu] [--planes split]
     python -m strands_decider_b200.kernel_cases gdn [--seqs 32] [--len 512]
     python -m strands_decider_b200.kernel_cases attention [--seqs 1] [--len 96]
 
@@ -47,8 +47,10 @@ def _profiled(fn) -> None:
         raise RuntimeError("a kernel recorded a fault")
 
 
-def gemm_case(m: int, fmt: str, ep: str, n: int = 2 * 6144, k: int = 2048):
-    """b200_linear with x as two bf16 planes [2, m, k] and a packed [n, k] weight."""
+def gemm_case(m: int, fmt: str, ep: str, n: int = 2 * 6144, k: int = 2048, planes: str = "split"):
+    """b200_linear with x as two bf16 planes [2, m, k] and a packed [n, k] weight; with planes
+    "lo8", b200_linear_lo8 on the weight's two copies (b200_dequantize_lo8) and an e4m3 low
+    plane, as large batches run it with lo_plane "e4m3"."""
     g = torch.Generator(device="cuda").manual_seed(0)
     if ep == "swiglu":
         gate = W.quantize(fmt, torch.randn(n // 2, k, device="cuda", generator=g) * 0.02)
@@ -66,6 +68,19 @@ def gemm_case(m: int, fmt: str, ep: str, n: int = 2 * 6144, k: int = 2048):
         o = _lib.LinearOut(_lib.EP_STORE if ep == "store" else _lib.EP_RESID_ADD, n, _lib.ptr(out), n, 0)
     qw = pw.qweight()
     keep = (pw, xp, out)
+    if planes == "lo8":
+        whi = torch.empty(pw.n, k, dtype=torch.bfloat16, device="cuda")
+        wlo8 = torch.empty(pw.n, k, dtype=torch.uint8, device="cuda")
+        _lib.call("b200_dequantize_lo8", C.byref(qw), _lib.ptr(whi), _lib.ptr(wlo8), _lib.stream_ptr())
+        xl8 = torch.randint(0, 0x38, (m, k), dtype=torch.uint8, device="cuda", generator=g)  # e4m3 below 1.0
+        o.lo_format = _lib.LO_E4M3
+        keep = (pw, xp, out, whi, wlo8, xl8)
+
+        def launch_lo8():
+            _lib.call("b200_linear_lo8", _lib.ptr(keep[1][0]), _lib.ptr(keep[5]), m, k, k, _lib.ptr(keep[3]),
+                      _lib.ptr(keep[4]), pw.n, C.byref(o), _lib.stream_ptr())
+
+        return launch_lo8, 2.0 * m * n * k
 
     def launch():
         _lib.call("b200_linear", _lib.ptr(keep[1][0]), _lib.ptr(keep[1][1]), m, k, k, C.byref(qw), C.byref(o),
@@ -136,6 +151,7 @@ def main() -> None:
     ap.add_argument("--ep", default="swiglu", choices=["swiglu", "store", "resid"])
     ap.add_argument("--n", type=int, default=2 * 6144)
     ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--planes", default="split", choices=["split", "lo8"])
     ap.add_argument("--seqs", type=int, default=32)
     ap.add_argument("--len", type=int, default=512)
     ap.add_argument("--reps", type=int, default=10)
@@ -144,8 +160,8 @@ def main() -> None:
         raise SystemExit("kernel_cases needs a CUDA device")
     _lib.load()
     if args.case == "gemm":
-        launch, flops = gemm_case(args.m, args.fmt, args.ep, args.n, args.k)
-        label = f"gemm {args.fmt} {args.ep} M={args.m} N={args.n} K={args.k}"
+        launch, flops = gemm_case(args.m, args.fmt, args.ep, args.n, args.k, args.planes)
+        label = f"gemm {args.fmt} {args.ep} {args.planes} M={args.m} N={args.n} K={args.k}"
     elif args.case == "gdn":
         launch, flops = gdn_case(args.seqs, args.len)
         label = f"gdn {args.seqs} x {args.len} tokens, 16 heads (prep + chunk kernels)"

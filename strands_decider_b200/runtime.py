@@ -52,7 +52,7 @@ class Decisions:
 class DecisionModel:
     def __init__(self, weights: DeviceWeights, max_tokens: int = 8192, pool_slots: int = 64,
                  pool_kv_tokens: int | None = None, device: str | torch.device = "cuda",
-                 dequant_min_tokens: int = 0, lo_plane: str = "bf16"):
+                 dequant_min_tokens: int = 0, lo_plane: str = "e4m3"):
         """dequant_min_tokens: batches of at least this many tokens run each GEMM on a bf16 copy
         of its weight dequantised once per call (0 = the library default, 4096; < 0 = never).
         lo_plane: the low activation plane of those GEMMs, "bf16" (two bf16 planes, about 16

@@ -241,3 +241,82 @@ def test_forward_on_e4m3_low_planes_matches_reference_golden(fmt):
     if fmt == "int4":
         assert np.abs(outs["e4m3"].probs.numpy() - g["probs"]).max() < 2e-3
         assert np.array_equal(outs["e4m3"].argmax.numpy(), g["probs"].argmax(1))
+
+
+# ----------------------------------------------------------------------------- CTA pairs
+# Batches with at least one 256 x 256 tile per SM pair run the bf16-weight GEMMs (two bf16
+# planes, one plane, or the e4m3 low plane above) on CTA pairs (tcgen05 .cta_group::2).
+
+
+@pytest.mark.parametrize("planes", ["split", "one"])
+@pytest.mark.parametrize("ep", ["store", "resid", "swiglu"])
+def test_pair_gemm_bf16_weights_large_m_with_tail(planes, ep):
+    """M = 2125: 9 row tiles of 256, the last one's second CTA entirely past M."""
+    from strands_decider_b200 import _lib
+
+    m, k, n = 2125, 1024, 2560
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(31))
+    xp = _lib.split_planes(x).cuda()
+    w = _weights(n, k, 32).to(torch.bfloat16).cuda()
+    qw = _lib.QWeight()
+    qw.format, qw.n, qw.k, qw.data = _lib.FMT["bf16"], n, k, _lib.ptr(w)
+    lo_off = 0
+    if ep == "store":
+        out, ldo, e = torch.full((m, n), 7.0, device="cuda"), n, _lib.EP_STORE
+    elif ep == "resid":
+        out, ldo, e = torch.randn(m, n, device="cuda"), n, _lib.EP_RESID_ADD
+    else:
+        ldo, e = n // 2, _lib.EP_SWIGLU
+        out = torch.zeros(2, m, ldo, dtype=torch.bfloat16, device="cuda")
+        lo_off = m * ldo
+    before = out.clone()
+    o = _lib.LinearOut(e, n, _lib.ptr(out), ldo, lo_off, 0)
+    _lib.call("b200_linear", _lib.ptr(xp[0]), _lib.ptr(xp[1]) if planes == "split" else None, m, k, k, C.byref(qw),
+              C.byref(o), _lib.stream_ptr())
+    torch.cuda.synchronize()
+    xv = xp[0].double().cpu() + (xp[1].double().cpu() if planes == "split" else 0)
+    y = xv @ w.double().cpu().T
+    if ep == "swiglu":
+        yb = y.view(m, -1, 2, 64)
+        ref = (torch.nn.functional.silu(yb[:, :, 0]) * yb[:, :, 1]).reshape(m, n // 2)
+        got = out[0].double().cpu() + out[1].double().cpu()
+        assert (got - ref).abs().max().item() / ref.abs().max().item() < 1e-4
+        return
+    got = out.double().cpu() - (before.double().cpu() if ep == "resid" else 0)
+    assert (got - y).abs().max().item() < 2e-5 * y.abs().max().item() + 1e-6
+
+
+def test_pair_gemm_lo8_tail():
+    from strands_decider_b200 import _lib
+
+    m, k, n = 2125, 2048, 2560
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(33))
+    xh, xl8 = _x_planes(x)
+    _, whi, wlo8, _ = _lo8_copies("nvfp4", n, k, 34)
+    out, before = _run_lo8(xh, xl8, whi, wlo8, _lib.EP_RESID_ADD, n)
+    ref = _operand_product(xh, xl8, whi, wlo8)
+    got = out.double().cpu() - before.double().cpu()
+    assert (got - ref).abs().max().item() < 2e-5 * ref.abs().max().item()
+
+
+def test_e4m3_low_planes_on_the_2b_decider_stay_inside_the_bar():
+    """The 2B-shape NVFP4 decider, 3 prompts x 512 tokens with every GEMM on the dequantised
+    path (CTA pairs): e4m3 low planes against two bf16 planes (the latter within 1e-5 of the
+    fp32 oracle). The CPU emulation of this case measures 6.9e-4 against fp32."""
+    from strands_decider_b200.runtime import DecisionModel
+    from strands_decider_b200.weights import DeviceWeights
+
+    spec = config.HYBRID_2B
+    w = DeviceWeights.synthetic(spec, seed=0, device="cuda", latent_device="cuda")
+    g = torch.Generator().manual_seed(0)
+    rows = [torch.randint(0, spec.vocab, (512,), generator=g).tolist() for _ in range(3)]
+    outs = {}
+    for lo in ("bf16", "e4m3"):
+        m = DecisionModel(w, max_tokens=2048, pool_slots=1, pool_kv_tokens=16, dequant_min_tokens=1, lo_plane=lo)
+        outs[lo] = m.score_prompts(rows, [[11, 12, 13]] * 3, [3] * 3, ["choice"] * 3, [1.0] * 3).cpu().probs
+        del m
+    d = (outs["e4m3"] - outs["bf16"]).abs().max().item()
+    assert d < 1.5e-3, d
+    top2 = outs["bf16"].topk(2, dim=1).values
+    clear = (top2[:, 0] - top2[:, 1]) > 2 * d
+    assert torch.equal(outs["e4m3"].argmax(1)[clear], outs["bf16"].argmax(1)[clear])

@@ -35,14 +35,14 @@ def _cuda():
     assert _lib.read_fault() == 0
 
 
-def _model(spec, seed, fmt=None, max_tokens=4096, slots=16, dequant_min_tokens=0):
+def _model(spec, seed, fmt=None, max_tokens=4096, slots=16, dequant_min_tokens=0, lo_plane="e4m3"):
     from strands_decider_b200.runtime import DecisionModel
     from strands_decider_b200.weights import DeviceWeights
 
     spec = spec.with_format(fmt) if fmt else spec
     w = DeviceWeights.synthetic(spec, seed=seed, latent_device="cpu", keep_logical=True)
     return DecisionModel(w, max_tokens=max_tokens, pool_slots=slots, pool_kv_tokens=max_tokens,
-                         dequant_min_tokens=dequant_min_tokens)
+                         dequant_min_tokens=dequant_min_tokens, lo_plane=lo_plane)
 
 
 def _logical_digest(model):
@@ -73,7 +73,7 @@ def test_dequantised_weight_path_matches_the_streamed_path(fmt):
     rows = g["ids"].tolist()
     outs = []
     for dq in (-1, 1):
-        m = _model(spec, seed=0, dequant_min_tokens=dq)
+        m = _model(spec, seed=0, dequant_min_tokens=dq, lo_plane="bf16")
         outs.append(m.score_prompts(rows, [[11, 12, 13]] * 4, [3] * 4, ["choice"] * 4, [1.0] * 4).cpu())
         del m
     # the dequantised bf16 weights equal the GEMM's own unpack bit for bit; what differs is
