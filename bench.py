@@ -352,9 +352,13 @@ def gemm_roofline(model, tokens: int, pk: dict, reps: int = 20) -> dict:
             traffic = round(per_tok * tokens)
     wname = "bf16 (dequantised once per call)" if dequant else s.weight_format
     planes = "lo8" if lo8 else "split"
+    n_sm = torch.cuda.get_device_properties(0).multi_processor_count
+    pair = dequant and (2 * s.inter // 256) * ((tokens + 255) // 256) >= n_sm // 2
+    kname = (f"gemm_pair_kernel<swiglu,{planes}> (CTA pairs, 256x256 tiles, weights {wname})" if pair
+             else f"gemm_tc_kernel<256,{wname},swiglu,{planes}>")
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
             "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": traffic,
-            "kernel": f"gemm_tc_kernel<256,{wname},swiglu,{planes}> M={tokens} N={2 * s.inter} K={s.hidden}",
+            "kernel": f"{kname} M={tokens} N={2 * s.inter} K={s.hidden}",
             "ms_per_launch": round(ms, 4), "dequant_ms_per_launch": round(dq_ms, 4) if dq_ms else None,
             "mma_flops_per_algorithmic_flop": 1.5 if lo8 else 2,
             "peak_src": pk["src"] + " bf16 burst (tcgen05 kind::f16)"}
