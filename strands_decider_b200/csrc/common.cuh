@@ -94,6 +94,9 @@ __device__ __forceinline__ void store_planes4(uint16_t* out, long long lo_offset
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 __device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// silu with the approximate division (__fdividef, 2 ulp; x / inf = 0 for very negative x):
+// for instruction-bound elementwise loops
+__device__ __forceinline__ float silu_approx(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float softplus(float x) { return x > 20.0f ? x : log1pf(__expf(x)); }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -177,47 +177,42 @@ __device__ __forceinline__ int gdn_find_seq(const int32_t* cu, int n, int t) {
 // slides in registers), 1 for small ones (latency: every warp loads its 4 rows at once)
 constexpr int PREP_TPW_LARGE = 8;
 
-// x rows p (sequence position) of the lane's 4 channels in each of q, k, v: the sequence's
-// own in-projection output for p >= 0, the prefix slot's conv history for p in [-3, 0),
-// zeros without a prefix
-__device__ __forceinline__ void prep_row(const GdnArgs& a, int key_dim, int h, int lane, int tok0, int p,
-                                         bool pvalid, int pslot, int conv_dim, float4 (&x)[3]) {
-#pragma unroll
-  for (int part = 0; part < 3; ++part) {
-    const int ch = part * key_dim + h * GD + lane * 4;
-    if (p >= 0) x[part] = *reinterpret_cast<const float4*>(a.mix + size_t(tok0 + p) * a.ld_mix + ch);
-    else if (pvalid) x[part] = *reinterpret_cast<const float4*>(a.conv_pool + (size_t(pslot) * 3 + (3 + p)) * conv_dim + ch);
-    else x[part] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-}
-
-// grid (ceil(T / 64), heads), 8 warps: warp w of block b handles head blockIdx.y, tokens
-// 64 b + 8 w .. +7; lane l owns channels 4l..4l+3 of the head's q, k and v. The warp keeps
-// the conv weights and the last 3 input rows in registers and loads each input row once.
+// grid (3 heads, ceil(T / (8 TPW))), 8 warps: warp w of block (3 h + part, b) handles head h,
+// part (0 q, 1 k, 2 v) and tokens 8 TPW b + TPW w .. +TPW-1; lane l owns channels 4l..4l+3 of
+// that part. Blocks run (head, part) fastest, so the blocks resident at one time read whole
+// rows of the in-projection output (DRAM pages opened once) rather than one head's 512-byte
+// strip down all T rows. The warp keeps the last 3 input rows in registers and loads each
+// input row once, two tokens ahead (token t's row is mix row t whatever its sequence, so
+// the prefetch needs no sequence lookup). One part per warp keeps the registers low enough
+// for 4 blocks per SM, whose loads in flight cover HBM latency.
 template <int TPW>
-__global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const GdnArgs a) {
-  __shared__ float4 wsm[3][4][32];  // conv taps (oldest first) of channel base[part] + 4 lane + c
+__global__ void __launch_bounds__(256, 4) gdn_prep_kernel(const GdnArgs a) {
+  __shared__ float4 wsm[4][32];  // conv taps (oldest first) of channel 4 lane + c of this part
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int h = blockIdx.y, H = a.p.heads, T = a.n_tokens;
+  const int h = blockIdx.x / 3, part = blockIdx.x % 3, H = a.p.heads, T = a.n_tokens;
   const int key_dim = H * GD, conv_dim = 3 * key_dim, value_dim = key_dim;
-  for (int i = threadIdx.x; i < 3 * GD; i += blockDim.x) {
-    const int part = i / GD, ch = i % GD;
-    wsm[part][ch & 3][ch >> 2] = *reinterpret_cast<const float4*>(a.p.conv_w + (part * key_dim + h * GD + ch) * 4);
+  const int ch0 = part * key_dim + h * GD;  // this part's first channel of the head
+  if (threadIdx.x < GD) {
+    const int ch = threadIdx.x;
+    wsm[ch & 3][ch >> 2] = *reinterpret_cast<const float4*>(a.p.conv_w + size_t(ch0 + ch) * 4);
   }
   __syncthreads();
   // the conv taps above are weights; everything below comes from the kernels before this one
   pdl_wait();
   pdl_trigger();
-  const int t_begin = (blockIdx.x * 8 + warp) * TPW;
+  const int t_begin = (blockIdx.y * 8 + warp) * TPW;
   if (t_begin >= T) return;
   const int t_end = min(T, t_begin + TPW);
-  const float a_coef = -__expf(a.p.a_log[h]), dt_bias = a.p.dt_bias[h];
   int seq = gdn_find_seq(a.cu, a.n_seqs, t_begin);
   int tok0 = a.cu[seq], tend = a.cu[seq + 1];
-  int pslot = -1;
-  bool pvalid = false, fresh = true;
-  float4 win[3][3];  // [row: p-3, p-2, p-1][part]
+  bool fresh = true;
+  const float* xrow = a.mix + ch0 + lane * 4;  // + t * ld: token t's 4 channels of this lane
+  float4 win[3];  // rows p-3, p-2, p-1
+  float4 x = *reinterpret_cast<const float4*>(xrow + size_t(t_begin) * a.ld_mix), x1 = x;
+  if (t_begin + 1 < t_end) x1 = *reinterpret_cast<const float4*>(xrow + size_t(t_begin + 1) * a.ld_mix);
   for (int t = t_begin; t < t_end; ++t) {
+    float4 xn = x1;
+    if (t + 2 < t_end) xn = *reinterpret_cast<const float4*>(xrow + size_t(t + 2) * a.ld_mix);  // in flight meanwhile
     while (t >= tend) {  // next (possibly empty) sequence; ends because t < T = cu[n_seqs]
       ++seq;
       tok0 = tend;
@@ -226,56 +221,53 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const GdnArgs a) {
     }
     const int p = t - tok0;
     if (fresh) {
-      pslot = a.prefix_slot ? a.prefix_slot[seq] : -1;
-      pvalid = pslot >= 0 && pslot < a.n_slots;
+      // rows p-3..p-1: the sequence's own for positions >= 0, else the prefix slot's conv
+      // history, else zeros
+      const int pslot = a.prefix_slot ? a.prefix_slot[seq] : -1;
+      const bool pvalid = pslot >= 0 && pslot < a.n_slots;
 #pragma unroll
-      for (int r = 0; r < 3; ++r) prep_row(a, key_dim, h, lane, tok0, p - 3 + r, pvalid, pslot, conv_dim, win[r]);
+      for (int r = 0; r < 3; ++r) {
+        const int q = p - 3 + r;
+        if (q >= 0) win[r] = *reinterpret_cast<const float4*>(xrow + size_t(tok0 + q) * a.ld_mix);
+        else if (pvalid)
+          win[r] = *reinterpret_cast<const float4*>(a.conv_pool + (size_t(pslot) * 3 + (3 + q)) * conv_dim + ch0 +
+                                                    lane * 4);
+        else win[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
       fresh = false;
     }
-    float4 x[3];
-    prep_row(a, key_dim, h, lane, tok0, p, pvalid, pslot, conv_dim, x);
-    float o[3][4];
-#pragma unroll
-    for (int part = 0; part < 3; ++part) {
-      const float xi[4][4] = {{win[0][part].x, win[1][part].x, win[2][part].x, x[part].x},
-                              {win[0][part].y, win[1][part].y, win[2][part].y, x[part].y},
-                              {win[0][part].z, win[1][part].z, win[2][part].z, x[part].z},
-                              {win[0][part].w, win[1][part].w, win[2][part].w, x[part].w}};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float4 w = wsm[part][c][lane];
-        float acc = 0.0f;
-        acc = fmaf(w.x, xi[c][0], acc);
-        acc = fmaf(w.y, xi[c][1], acc);
-        acc = fmaf(w.z, xi[c][2], acc);
-        acc = fmaf(w.w, xi[c][3], acc);
-        o[part][c] = silu(acc);
-      }
-    }
-#pragma unroll
-    for (int part = 0; part < 3; ++part) {
-      win[0][part] = win[1][part];
-      win[1][part] = win[2][part];
-      win[2][part] = x[part];
-    }
-    float sq = 0.f, sk = 0.f;
+    const float xi[4][4] = {{win[0].x, win[1].x, win[2].x, x.x},
+                            {win[0].y, win[1].y, win[2].y, x.y},
+                            {win[0].z, win[1].z, win[2].z, x.z},
+                            {win[0].w, win[1].w, win[2].w, x.w}};
+    float o[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      sq += o[0][c] * o[0][c];
-      sk += o[1][c] * o[1][c];
+      const float4 w = wsm[c][lane];
+      float acc = 0.0f;
+      acc = fmaf(w.x, xi[c][0], acc);
+      acc = fmaf(w.y, xi[c][1], acc);
+      acc = fmaf(w.z, xi[c][2], acc);
+      acc = fmaf(w.w, xi[c][3], acc);
+      o[c] = silu_approx(acc);
     }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    const float rq = rsqrtf(sq + 1e-6f) * rsqrtf(float(GD)), rk = rsqrtf(sk + 1e-6f);
+    win[0] = win[1];
+    win[1] = win[2];
+    win[2] = x;
+    float r = 1.0f;
+    if (part < 2) {  // q, k: l2norm over the head's 128 channels; q also takes 1 / sqrt(dk)
+      const float ss = warp_sum(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
+      r = rsqrtf(ss + 1e-6f) * (part == 0 ? rsqrtf(float(GD)) : 1.0f);
+    }
     float* dst = a.prep + (size_t(h) * T + t) * GPREP;
-    reinterpret_cast<float4*>(dst)[lane] = make_float4(o[0][0] * rq, o[0][1] * rq, o[0][2] * rq, o[0][3] * rq);
-    reinterpret_cast<float4*>(dst + GD)[lane] = make_float4(o[1][0] * rk, o[1][1] * rk, o[1][2] * rk, o[1][3] * rk);
-    reinterpret_cast<float4*>(dst + 2 * GD)[lane] = make_float4(o[2][0], o[2][1], o[2][2], o[2][3]);
-    if (lane == 0) {
+    reinterpret_cast<float4*>(dst + part * GD)[lane] = make_float4(o[0] * r, o[1] * r, o[2] * r, o[3] * r);
+    if (part == 2 && lane == 0) {
       const float* ab = a.mix + size_t(t) * a.ld_mix + conv_dim + value_dim;
       dst[GQKV] = sigmoid(ab[h]);
-      dst[GQKV + 1] = a_coef * softplus(ab[H + h] + dt_bias);
+      dst[GQKV + 1] = -__expf(a.p.a_log[h]) * softplus(ab[H + h] + a.p.dt_bias[h]);
     }
+    x = x1;
+    x1 = xn;
   }
 }
 
@@ -823,12 +815,13 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
     attr = true;
   }
   a.n_tokens = s->n_tokens;
+  if (s->n_tokens > 65535 * 8 * PREP_TPW_LARGE) return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: too many tokens");
   if (long(s->n_tokens) * p->heads >= 64L * 1024) {  // enough warps at 8 tokens each to fill the GPU
     constexpr int TPW = PREP_TPW_LARGE;
-    SDB_CUDA(launch_pdl(gdn_prep_kernel<TPW>, dim3((s->n_tokens + 8 * TPW - 1) / (8 * TPW), p->heads), dim3(256), 0,
+    SDB_CUDA(launch_pdl(gdn_prep_kernel<TPW>, dim3(3 * p->heads, (s->n_tokens + 8 * TPW - 1) / (8 * TPW)), dim3(256), 0,
                         st, a));
   } else {
-    SDB_CUDA(launch_pdl(gdn_prep_kernel<1>, dim3((s->n_tokens + 7) / 8, p->heads), dim3(256), 0, st, a));
+    SDB_CUDA(launch_pdl(gdn_prep_kernel<1>, dim3(3 * p->heads, (s->n_tokens + 7) / 8), dim3(256), 0, st, a));
   }
   if (long(s->n_seqs) * p->heads * 2 > 148) {  // enough (sequence, head) CTAs: one per head
     SDB_CUDA(launch_pdl(gdn_mixer_kernel<GD>, dim3(p->heads, s->n_seqs), dim3(GDN_THREADS), sizeof(GdnSmem<GD>), st,
