@@ -698,7 +698,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
           uint16_t hb[CPL];
 #pragma unroll
           for (int e = 0; e < CPL; ++e) {
-            y[e] = nw[e] * (ov[i][e] * r) * silu(zv[i][e]);
+            y[e] = nw[e] * (ov[i][e] * r) * silu_approx(zv[i][e]);
             hb[e] = f32_to_bf16_rn(y[e]);
           }
           const size_t e0 = size_t(tok0 + c0 + j) * value_dim + h * GD + col0 + lane * CPL;
