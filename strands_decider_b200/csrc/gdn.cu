@@ -526,7 +526,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
 #pragma unroll
         for (int e = 0; e < 4; ++e) ws[i][0][e] = ws[i][1][e] = qs[i][0][e] = qs[i][1][e] = 0.0f;
       if (warp < 2 * NB6) {
-#pragma unroll 1
+#pragma unroll 2
         for (int k0 = 0; k0 < GD; k0 += 16) {
           uint32_t wh[4], wl[4], qh[4], ql[4];
           frag_a<GD>(wh, sm.ru.uw.Wh, m0, k0, lane);
