@@ -175,7 +175,7 @@ __device__ __forceinline__ void epilogue_swiglu(const GemmArgs& a, int row, int 
   for (int j = 0; j < 4; ++j) {
     float h[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) h[e] = silu(__uint_as_float(g[8 * j + e])) * __uint_as_float(u[8 * j + e]);
+    for (int e = 0; e < 8; ++e) h[e] = silu_approx(__uint_as_float(g[8 * j + e])) * __uint_as_float(u[8 * j + e]);
     uint4 hi, lo;
     split_bf16x2(h[0], h[1], hi.x, lo.x);
     split_bf16x2(h[2], h[3], hi.y, lo.y);
