@@ -175,14 +175,27 @@ def cpu_baseline(spec: config.ModelSpec, wl: config.Workload, n_requests: int = 
 # ----------------------------------------------------------------------------- GPU arm
 
 
-def launches_per_forward(spec: config.ModelSpec, decide: bool, tokens: int = 0) -> int:
-    """Kernels one b200_model_forward launches (embed, per layer: 2 norms, 4 GEMMs and the
-    mixer's kernels, then the head); forwards of >= 4096 tokens also dequantise each of the
-    4 weights per layer once."""
-    dq = 4 if tokens >= 4096 and spec.weight_format != "bf16" else 0
-    n = 1 + (1 if decide else 0)
+def _store_split(rows: int, tokens: int, n_sm: int = 148) -> bool:
+    """Whether the in-projection's store GEMM splits K (and so first zeroes its output), as
+    gemm.cu decides: 128-column tiles when two 256-column tiles per SM or fewer, then a K split
+    when two tiles per SM or fewer."""
+    mt = (tokens + 127) // 128
+    bn = 128 if 2 * (rows // 256) * mt <= n_sm else 256
+    return 2 * (rows // bn) * mt <= n_sm
+
+
+def launches_per_forward(spec: config.ModelSpec, decide: bool, tokens: int = 0, saves: bool = False,
+                         lo_plane: str = "e4m3") -> int:
+    """Kernels one b200_model_forward launches: embed; per layer 2 norms, 4 GEMMs and the
+    mixer's 2 kernels, plus a zeroing kernel before a split-K in-projection (small batches);
+    forwards of >= 4096 tokens also dequantise each of the 4 weights per layer once (bf16
+    weights too with the e4m3 low plane); the slot-length update when states are saved; the head."""
+    big = tokens >= 4096
+    dq = 4 if big and (spec.weight_format != "bf16" or lo_plane == "e4m3") else 0
+    n = 1 + (1 if decide else 0) + (1 if saves else 0)
     for lt in spec.layer_types:
-        n += 2 + 4 + 2 + dq  # GDN: prep + chunk kernel; attention: prep + flash kernel
+        rows = spec.gdn_in_rows_padded if lt == config.GDN else -(-spec.attn_qkv_rows // 256) * 256
+        n += 2 + 4 + 2 + dq + (0 if big or not _store_split(rows, tokens) else 1)
     return n
 
 
@@ -441,7 +454,7 @@ def latency(args) -> None:
                            "min": round(ms[0], 4), "runs": runs},
             "e2e": {"value": round(pct(ms2, 0.5), 4), "unit": "ms", "p99": round(pct(ms2, 0.99), 4),
                     "h2d_bytes_per_step": b.h2d_bytes, "d2h_bytes_per_step": out_host.numel() * 4},
-            "gpu_launches": runs * launches_per_forward(spec, True), "clocks": clk, "cpu_baseline": cb}
+            "gpu_launches": runs * launches_per_forward(spec, True, b.tokens), "clocks": clk, "cpu_baseline": cb}
     if cb:
         cb["ms_per_request"] = round(1e3 / cb["value"], 1)
     print(json.dumps(line), flush=True)
@@ -629,8 +642,8 @@ def main() -> None:
         "linear_tflops": round(fl / (ms * 1e-3) / 1e12 / world, 1),
         "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
                 "d2h_bytes_per_step": d2h // args.steps},
-        "gpu_launches": sum(((launches_per_forward(spec, False, b.n_state_tokens) if prefix else 0)
-                             + launches_per_forward(spec, True, b.n_suffix_tokens))
+        "gpu_launches": sum(((launches_per_forward(spec, False, b.n_state_tokens, True, args.lo_plane) if prefix else 0)
+                             + launches_per_forward(spec, True, b.n_suffix_tokens, lo_plane=args.lo_plane))
                             for b in (batches[(args.warmup + i) % len(batches)] for i in range(args.steps))) * world,
         "roofline": roof, "clocks": clk, "cpu_baseline": cb,
     }

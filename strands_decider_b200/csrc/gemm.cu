@@ -755,6 +755,16 @@ __global__ void gemm_simt_kernel(const uint16_t* __restrict__ x, const uint16_t*
   }
 }
 
+// Zero rows [m][0, n) of an fp32 [m, ld] output before a split-K store accumulates into it
+// (a kernel rather than a memset so that it joins the programmatic-dependent-launch chain).
+// n % 4 == 0 and ld % 4 == 0 (b200_linear's n_valid % 32 and ldo % 8 rules).
+__global__ void zero_rows_kernel(float* __restrict__ out, int ld, int n) {
+  pdl_wait();
+  pdl_trigger();
+  float4* row = reinterpret_cast<float4*>(out + size_t(blockIdx.x) * ld);
+  for (int i = threadIdx.x; i < n / 4; i += blockDim.x) row[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
 // --------------------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
@@ -856,7 +866,8 @@ static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_lo, const CU
   args.ksplit = 1;
   if (EP != B200_EP_SWIGLU && 2 * tiles <= n_sm) args.ksplit = std::max(1, std::min({n_sm / tiles, nk / 2, 16}));
   if (args.ksplit > 1 && EP == B200_EP_STORE)
-    SDB_CUDA(cudaMemset2DAsync(a.o.out, size_t(a.o.ldo) * 4, 0, size_t(a.o.n_valid) * 4, a.m, st));
+    SDB_CUDA(launch_pdl(zero_rows_kernel, dim3(a.m), dim3(256), 0, st, reinterpret_cast<float*>(a.o.out), a.o.ldo,
+                        a.o.n_valid));
   const int units = tiles * args.ksplit;
   // programmatic dependent launch: the CTA set-up (barriers, TMEM, descriptor prefetch)
   // overlaps the tail of the kernel before it in the stream (the kernel waits before its
