@@ -403,7 +403,7 @@ def latency(args) -> None:
     spec, wl = config.HYBRID_2B.with_format("ternary"), config.LATENCY_WORKLOAD
     torch.cuda.set_device(0)
     weights = DeviceWeights.synthetic(spec, seed=0, device="cuda", latent_device="cuda")
-    model = DecisionModel(weights, max_tokens=128, pool_slots=1, pool_kv_tokens=128)
+    model = DecisionModel(weights, max_tokens=128, pool_slots=1, pool_kv_tokens=128, lo_plane=args.lo_plane)
     reqs = request_batch(wl, spec.vocab, 0, 1)
     reqs[0]["id"] = 0
     b = Batch(reqs, "cuda", pinned=True, kmax=3, prefix=False)
@@ -447,7 +447,7 @@ def latency(args) -> None:
             "warmup": max(args.warmup, 20), "ms_per_step": round(statistics.mean(ms), 4),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": wl.name, "model": spec.name, "weights": "ternary", "tokens": b.tokens,
+            "config": {"workload": wl.name, "model": spec.name, "weights": "ternary", "tokens": b.tokens, "lo_plane": args.lo_plane,
                        "path": "full prompt, one CUDA graph per request",
                        "l2": "weights (0.34 GB ternary + 1 GB embedding) exceed L2; no flush between replays"},
             "latency_ms": {"p50": round(pct(ms, 0.5), 4), "p99": round(pct(ms, 0.99), 4),
