@@ -210,9 +210,22 @@ __global__ void __launch_bounds__(256, 4) gdn_prep_kernel(const GdnArgs a) {
   float4 win[3];  // rows p-3, p-2, p-1
   float4 x = *reinterpret_cast<const float4*>(xrow + size_t(t_begin) * a.ld_mix), x1 = x;
   if (t_begin + 1 < t_end) x1 = *reinterpret_cast<const float4*>(xrow + size_t(t_begin + 1) * a.ld_mix);
+  // v warps, lanes 0 / 1: the gating inputs b / a of the head, loaded two tokens ahead like the rows
+  const bool gate_lane = part == 2 && lane < 2;
+  const float* grow = a.mix + conv_dim + value_dim + (lane == 0 ? h : H + h);
+  const float a_coef = gate_lane ? -__expf(a.p.a_log[h]) : 0.0f, dt_bias = gate_lane ? a.p.dt_bias[h] : 0.0f;
+  float g = 0.0f, g1 = 0.0f;
+  if (gate_lane) {
+    g = grow[size_t(t_begin) * a.ld_mix];
+    if (t_begin + 1 < t_end) g1 = grow[size_t(t_begin + 1) * a.ld_mix];
+  }
   for (int t = t_begin; t < t_end; ++t) {
     float4 xn = x1;
-    if (t + 2 < t_end) xn = *reinterpret_cast<const float4*>(xrow + size_t(t + 2) * a.ld_mix);  // in flight meanwhile
+    float gn = 0.0f;
+    if (t + 2 < t_end) {  // in flight meanwhile
+      xn = *reinterpret_cast<const float4*>(xrow + size_t(t + 2) * a.ld_mix);
+      if (gate_lane) gn = grow[size_t(t + 2) * a.ld_mix];
+    }
     while (t >= tend) {  // next (possibly empty) sequence; ends because t < T = cu[n_seqs]
       ++seq;
       tok0 = tend;
@@ -261,13 +274,12 @@ __global__ void __launch_bounds__(256, 4) gdn_prep_kernel(const GdnArgs a) {
     }
     float* dst = a.prep + (size_t(h) * T + t) * GPREP;
     reinterpret_cast<float4*>(dst + part * GD)[lane] = make_float4(o[0] * r, o[1] * r, o[2] * r, o[3] * r);
-    if (part == 2 && lane == 0) {
-      const float* ab = a.mix + size_t(t) * a.ld_mix + conv_dim + value_dim;
-      dst[GQKV] = sigmoid(ab[h]);
-      dst[GQKV + 1] = -__expf(a.p.a_log[h]) * softplus(ab[H + h] + a.p.dt_bias[h]);
-    }
+    if (gate_lane)  // beta = sigmoid(b) (lane 0), g = -exp(A_log) softplus(a + dt_bias) (lane 1)
+      dst[GQKV + lane] = lane == 0 ? __fdividef(1.0f, 1.0f + __expf(-g)) : a_coef * softplus(g + dt_bias);
     x = x1;
     x1 = xn;
+    g = g1;
+    g1 = gn;
   }
 }
 
