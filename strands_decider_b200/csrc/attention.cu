@@ -95,9 +95,25 @@ __global__ void attn_prep_kernel(const AttnArgs a) {
     dst = a.v_buf + (size_t(t) * nkv + vh) * HD;
     if (save) pool_dst = a.v_pool + (size_t(kv0 + j) * nkv + vh) * HD;
   }
+  // the lane's PER consecutive elements as 16-byte loads (row and head offsets are multiples of
+  // 4 floats) and, below, one 16-byte bf16 store per 8 elements
+  static_assert(PER % 4 == 0 || PER == 2, "head_dim / 32 elements per lane");
+  constexpr int VW = PER % 4 == 0 ? 4 : 2;  // floats per vector load
   float x[PER];
 #pragma unroll
-  for (int e = 0; e < PER; ++e) x[e] = src[lane * PER + e];
+  for (int e = 0; e < PER; e += VW) {
+    if constexpr (VW == 4) {
+      const float4 v = *reinterpret_cast<const float4*>(src + lane * PER + e);
+      x[e] = v.x;
+      x[e + 1] = v.y;
+      x[e + 2] = v.z;
+      x[e + 3] = v.w;
+    } else {
+      const float2 v = *reinterpret_cast<const float2*>(src + lane * PER + e);
+      x[e] = v.x;
+      x[e + 1] = v.y;
+    }
+  }
   if (nw) {
     float ss2 = 0.0f;
 #pragma unroll
@@ -105,7 +121,7 @@ __global__ void attn_prep_kernel(const AttnArgs a) {
     ss2 = warp_sum(ss2);
     const float r = rsqrtf(ss2 / float(HD) + a.p.eps);
 #pragma unroll
-    for (int e = 0; e < PER; ++e) x[e] = x[e] * r * (1.0f + nw[lane * PER + e]);
+    for (int e = 0; e < PER; ++e) x[e] *= r * (1.0f + __ldg(nw + lane * PER + e));
     // partial RoPE: dims [0, rope_dim) rotate as pairs (i, i + rope_dim/2)
     const int half = a.p.rope_dim / 2;
     const int xd = half / PER;  // lane distance between paired elements
@@ -122,11 +138,21 @@ __global__ void attn_prep_kernel(const AttnArgs a) {
       }
     }
   }
+  if constexpr (PER % 8 == 0) {
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const uint16_t b = f32_to_bf16_rn(x[e]);
-    dst[lane * PER + e] = b;
-    if (pool_dst) pool_dst[lane * PER + e] = b;
+    for (int e = 0; e < PER; e += 8) {
+      const uint4 b = make_uint4(pack_bf16x2(x[e], x[e + 1]), pack_bf16x2(x[e + 2], x[e + 3]),
+                                 pack_bf16x2(x[e + 4], x[e + 5]), pack_bf16x2(x[e + 6], x[e + 7]));
+      *reinterpret_cast<uint4*>(dst + lane * PER + e) = b;
+      if (pool_dst) *reinterpret_cast<uint4*>(pool_dst + lane * PER + e) = b;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < PER; e += 2) {
+      const uint32_t b = pack_bf16x2(x[e], x[e + 1]);
+      *reinterpret_cast<uint32_t*>(dst + lane * PER + e) = b;
+      if (pool_dst) *reinterpret_cast<uint32_t*>(pool_dst + lane * PER + e) = b;
+    }
   }
 }
 
@@ -407,6 +433,10 @@ int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qk
   a.n_seqs = s->n_seqs;
   a.qkv = qkv;
   a.ld_qkv = ld_qkv;
+  // the prep kernel reads each lane's elements and writes q / k / v as whole vectors
+  if (ld_qkv % 4 != 0 || ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(q_buf) |
+                           reinterpret_cast<uintptr_t>(k_buf) | reinterpret_cast<uintptr_t>(v_buf)) & 15))
+    return sdb_fail(B200_ERR_SHAPE, "b200_attention: qkv and the q/k/v buffers must be 16-byte aligned, ld_qkv % 4 == 0");
   a.q_buf = q_buf;
   a.k_buf = k_buf;
   a.v_buf = v_buf;
