@@ -279,6 +279,9 @@ __global__ void __launch_bounds__(128 * fa_dg<HD>(), 2) attn_flash_kernel(const 
     cp_async_wait<1>();
     __syncthreads();
     const uint32_t sKa = smem_addr(sK + buf * FA_K * HD * 2), sVa = smem_addr(sV + buf * FA_K * HD * 2);
+    // A warp whose 16 rows are all past the sequence (short sequences), or whose queries all
+    // precede this key tile (causal), would only add zeros: it keeps to the loads and barriers.
+    if (q0 + qrow0 < len && tile * FA_K <= P + q0 + qrow0 + 15) {
     // ---- S = Q K^T : 16 x 32 per warp
     float sc[4][4];
 #pragma unroll
@@ -361,6 +364,7 @@ __global__ void __launch_bounds__(128 * fa_dg<HD>(), 2) attn_flash_kernel(const 
         mma_bf16_16816(o[2 * nd], a4, vb[0], vb[1]);
         mma_bf16_16816(o[2 * nd + 1], a4, vb[2], vb[3]);
       }
+    }
     }
     __syncthreads();
   }
