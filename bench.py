@@ -443,6 +443,18 @@ def latency(args) -> None:
         return v[min(len(v) - 1, int(q * len(v)))]
 
     cb = cpu_baseline(spec, wl, 1, full_prompt=True) if args.cpu_sample > 0 else None
+    # Latency roofline: the forward must stream every linear's ternary weights (2 bits each) from
+    # HBM once; its algorithmic FLOPs (2 x params x tokens) at the bf16 peak are the other bound.
+    pk = peaks()
+    p50 = pct(ms, 0.5)
+    wbytes = spec.linear_params() * 0.25
+    flops = 2.0 * spec.linear_params() * b.tokens
+    roof = {"bound": "hbm", "achieved": round(wbytes / (p50 * 1e-3) / 1e9, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(wbytes / (p50 * 1e-3) / 1e9 / pk["hbm_gbs"], 4), "traffic": None,
+            "kernel": "whole forward: every linear's packed weights streamed once",
+            "hbm_bound_ms": round(wbytes / (pk["hbm_gbs"] * 1e9) * 1e3, 4),
+            "mma_bound_ms": round(flops / (pk["bf16_tflops"] * 1e12) * 1e3, 4),
+            "peak_src": pk["src"] + " copy bandwidth"}
     line = {"metric": METRIC, "value": round(pct(ms, 0.5), 4), "unit": "ms", "n_gpus": 1, "steps": runs,
             "warmup": max(args.warmup, 20), "ms_per_step": round(statistics.mean(ms), 4),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -454,7 +466,8 @@ def latency(args) -> None:
                            "min": round(ms[0], 4), "runs": runs},
             "e2e": {"value": round(pct(ms2, 0.5), 4), "unit": "ms", "p99": round(pct(ms2, 0.99), 4),
                     "h2d_bytes_per_step": b.h2d_bytes, "d2h_bytes_per_step": out_host.numel() * 4},
-            "gpu_launches": runs * launches_per_forward(spec, True, b.tokens), "clocks": clk, "cpu_baseline": cb}
+            "gpu_launches": runs * launches_per_forward(spec, True, b.tokens), "roofline": roof, "clocks": clk,
+            "cpu_baseline": cb}
     if cb:
         cb["ms_per_request"] = round(1e3 / cb["value"], 1)
     print(json.dumps(line), flush=True)
