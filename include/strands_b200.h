@@ -207,6 +207,17 @@ typedef struct b200_gdn_params {
 int b200_gdn_mixer(const b200_gdn_params* p, const b200_seqs* seqs, const float* mix, int32_t ld_mix,
                    uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool, int32_t gdn_layer,
                    float* scratch, b200_stream stream);
+/* b200_gdn_mixer picks its scan by the batch: the token-by-token recurrent form
+ * (torch_recurrent_gated_delta_rule, TF:314-353) when n_tokens <= n_seqs (single-token
+ * appends to cached states), the chunked rule otherwise. These two force one of them, with
+ * the same arguments and results (the state after the last token, outputs per token); the
+ * recurrent one needs norm_w, scratch and the pool's gdn_state 16-byte aligned. */
+int b200_gdn_mixer_recurrent(const b200_gdn_params* p, const b200_seqs* seqs, const float* mix, int32_t ld_mix,
+                             uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool, int32_t gdn_layer,
+                             float* scratch, b200_stream stream);
+int b200_gdn_mixer_chunked(const b200_gdn_params* p, const b200_seqs* seqs, const float* mix, int32_t ld_mix,
+                           uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool, int32_t gdn_layer,
+                           float* scratch, b200_stream stream);
 /* fp32 scratch floats b200_gdn_mixer needs for a batch of n_tokens. */
 int b200_gdn_scratch_floats(int32_t heads, int32_t n_tokens);
 

@@ -118,6 +118,10 @@ _SIGS = {
     "b200_rmsnorm_lo8": ([_P, _I, _I, _P, C.c_float, _P, C.c_int64, _P], C.c_int),
     "b200_gdn_mixer": ([C.POINTER(GdnParams), C.POINTER(Seqs), _P, _I, _P, C.c_int64, C.POINTER(PrefixPool), _I,
                         _P, _P], C.c_int),
+    "b200_gdn_mixer_recurrent": ([C.POINTER(GdnParams), C.POINTER(Seqs), _P, _I, _P, C.c_int64,
+                                  C.POINTER(PrefixPool), _I, _P, _P], C.c_int),
+    "b200_gdn_mixer_chunked": ([C.POINTER(GdnParams), C.POINTER(Seqs), _P, _I, _P, C.c_int64,
+                                C.POINTER(PrefixPool), _I, _P, _P], C.c_int),
     "b200_gdn_scratch_floats": ([_I, _I], C.c_int),
     "b200_attention": ([C.POINTER(AttnParams), C.POINTER(Seqs), _P, _I, _P, _P, _P, _P, C.c_int64,
                         C.POINTER(PrefixPool), _I, _P], C.c_int),

@@ -294,6 +294,37 @@ __device__ __forceinline__ void gdn_stage_chunk(float* stage, uint64_t* bar, con
   bulk_load(stage, a.prep + (size_t(h) * a.n_tokens + tok0 + c) * GPREP, bytes, bar);
 }
 
+// The saved conv history of head h (called by all GDN_THREADS threads of one CTA): the
+// sequence's last 3 raw inputs of the head's q / k / v channels; positions before the
+// sequence come from the prefix slot's history. Everything is read before anything is
+// written, so a sequence may save into its own prefix slot (append).
+__device__ __forceinline__ void gdn_save_conv(const GdnArgs& a, int h, int tok0, int len, int pslot, bool pvalid,
+                                              int sslot) {
+  const int key_dim = a.p.heads * GD, conv_dim = 3 * key_dim;
+  constexpr int PER_T = (3 * 3 * GD + GDN_THREADS - 1) / GDN_THREADS;
+  float hv[PER_T];
+#pragma unroll
+  for (int i = 0; i < PER_T; ++i) {
+    const int idx = threadIdx.x + i * GDN_THREADS;
+    hv[i] = 0.0f;
+    if (idx < 3 * 3 * GD) {
+      const int r = idx / (3 * GD), part = (idx / GD) % 3, c = idx % GD;
+      const int q = len - 3 + r, ch = part * key_dim + h * GD + c;
+      if (q >= 0) hv[i] = a.mix[size_t(tok0 + q) * a.ld_mix + ch];
+      else if (pvalid) hv[i] = a.conv_pool[(size_t(pslot) * 3 + (3 + q)) * conv_dim + ch];
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < PER_T; ++i) {
+    const int idx = threadIdx.x + i * GDN_THREADS;
+    if (idx < 3 * 3 * GD) {
+      const int r = idx / (3 * GD), part = (idx / GD) % 3, c = idx % GD;
+      a.conv_pool[(size_t(sslot) * 3 + r) * conv_dim + part * key_dim + h * GD + c] = hv[i];
+    }
+  }
+}
+
 // grid (heads * NS, n_seqs), NS = 128 / DV CTAs per (sequence, head) forming one cluster; the
 // CTA with cluster rank `slice` owns value columns col0 = slice * DV .. col0 + DV - 1 of the
 // state, U, Vn and O. The dv columns of the delta rule are independent except for the gated
@@ -744,37 +775,113 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
         dst[r * GD + col0 + c] = S[nt][e];
       }
     }
-    // the saved conv history: the sequence's last 3 raw inputs (head h's q / k / v channels);
-    // positions before the sequence come from the prefix slot's history. Everything is read
-    // before anything is written, so a sequence may save into its own prefix slot (append).
-    if (slice == 0) {
-      constexpr int PER_T = (3 * 3 * GD + GDN_THREADS - 1) / GDN_THREADS;
-      float hv[PER_T];
-#pragma unroll
-      for (int i = 0; i < PER_T; ++i) {
-        const int idx = tid + i * GDN_THREADS;
-        hv[i] = 0.0f;
-        if (idx < 3 * 3 * GD) {
-          const int r = idx / (3 * GD), part = (idx / GD) % 3, c = idx % GD;
-          const int q = len - 3 + r, ch = part * key_dim + h * GD + c;
-          if (q >= 0) hv[i] = a.mix[size_t(tok0 + q) * a.ld_mix + ch];
-          else if (pvalid) hv[i] = a.conv_pool[(size_t(pslot) * 3 + (3 + q)) * conv_dim + ch];
-        }
-      }
-      __syncthreads();
-#pragma unroll
-      for (int i = 0; i < PER_T; ++i) {
-        const int idx = tid + i * GDN_THREADS;
-        if (idx < 3 * 3 * GD) {
-          const int r = idx / (3 * GD), part = (idx / GD) % 3, c = idx % GD;
-          a.conv_pool[(size_t(sslot) * 3 + r) * conv_dim + part * key_dim + h * GD + c] = hv[i];
-        }
-      }
-    }
+    if (slice == 0) gdn_save_conv(a, h, tok0, len, pslot, pvalid, sslot);
   }
   if constexpr (NS > 1) {
     // no CTA leaves while another may still read its part[] (the last chunk's exchange)
     cg::this_cluster().sync();
+  }
+}
+
+// ----------------------------------------------------------------------------- recurrent kernel
+
+// Token-by-token form of the same rule (TF:314-353), for batches whose sequences are one
+// token long (appends of a single token to a cached state) or a few: per token
+//   S <- e^g S;  delta = beta (v - S^T k);  S <- S + k delta^T;  o = S^T q,
+// computed as a = S^T k and b = S^T q over the state before the update, so that
+//   delta = beta (v - e^g a)  and  o = e^g b + delta (k . q)
+// come out of one pass over S. grid (heads, n_seqs), 8 warps: warp w owns the state rows (key
+// dims) 16w..16w+15 and lane l the value columns 4l..4l+3, so one row of a warp is one
+// coalesced 512-byte float4 access and the fp32 state stays in registers for the whole
+// sequence. The column sums are reduced across the 8 warps through shared memory (one barrier
+// per token; the partials are double-buffered by token parity, so the next token's writes never
+// meet this token's reads). Every warp then holds o for all 128 columns; warp (t mod 8) applies
+// the gated RMSNorm to token t and stores its planes.
+__global__ void __launch_bounds__(GDN_THREADS, 2) gdn_step_kernel(const GdnArgs a) {
+  __shared__ float4 part[2][GDN_THREADS / 32][2][32];  // [parity][warp][S^T k | S^T q][lane]
+  __shared__ float part_kq[2][GDN_THREADS / 32];
+  pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
+  pdl_trigger();
+  const int h = blockIdx.x, seq = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = a.p.heads;
+  const int key_dim = H * GD, value_dim = H * GD, conv_dim = 2 * key_dim + value_dim;
+  const int tok0 = a.cu[seq], len = a.cu[seq + 1] - tok0;
+  const int pslot = a.prefix_slot ? a.prefix_slot[seq] : -1;
+  const int sslot = a.save_slot ? a.save_slot[seq] : -1;
+  const bool pvalid = pslot >= 0 && pslot < a.n_slots;
+  const bool svalid = sslot >= 0 && sslot < a.n_slots;
+  if ((pslot >= a.n_slots || sslot >= a.n_slots) && threadIdx.x == 0) raise_fault(FAULT_BAD_INDEX);
+
+  float4 S[16];  // S[i] = state row 16 * warp + i, columns 4 * lane .. 4 * lane + 3
+  {
+    const float* src = pvalid ? a.state_pool + (size_t(pslot) * H + h) * GD * GD : nullptr;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      S[i] = src ? reinterpret_cast<const float4*>(src + (16 * warp + i) * GD)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const float4 nw = reinterpret_cast<const float4*>(a.p.norm_w)[lane];
+
+  for (int t = 0; t < len; ++t) {
+    const float* rec = a.prep + (size_t(h) * a.n_tokens + tok0 + t) * GPREP;  // q | k | v | beta, g
+    float qr[16], kr[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // the warp's 16 rows of q and k: the same address in every lane
+      const float4 q4 = reinterpret_cast<const float4*>(rec + 16 * warp)[i];
+      const float4 k4 = reinterpret_cast<const float4*>(rec + GD + 16 * warp)[i];
+      qr[4 * i] = q4.x, qr[4 * i + 1] = q4.y, qr[4 * i + 2] = q4.z, qr[4 * i + 3] = q4.w;
+      kr[4 * i] = k4.x, kr[4 * i + 1] = k4.y, kr[4 * i + 2] = k4.z, kr[4 * i + 3] = k4.w;
+    }
+    const float4 v = reinterpret_cast<const float4*>(rec + 2 * GD)[lane];
+    const float beta = rec[GQKV], eg = expf(rec[GQKV + 1]);
+    float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pq = pk;
+    float kq = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      pk.x = fmaf(S[i].x, kr[i], pk.x), pk.y = fmaf(S[i].y, kr[i], pk.y);
+      pk.z = fmaf(S[i].z, kr[i], pk.z), pk.w = fmaf(S[i].w, kr[i], pk.w);
+      pq.x = fmaf(S[i].x, qr[i], pq.x), pq.y = fmaf(S[i].y, qr[i], pq.y);
+      pq.z = fmaf(S[i].z, qr[i], pq.z), pq.w = fmaf(S[i].w, qr[i], pq.w);
+      kq = fmaf(kr[i], qr[i], kq);
+    }
+    const int par = t & 1;
+    part[par][warp][0][lane] = pk;
+    part[par][warp][1][lane] = pq;
+    if (lane == 0) part_kq[par][warp] = kq;
+    __syncthreads();
+    float4 sk = make_float4(0.f, 0.f, 0.f, 0.f), sq = sk;
+    float kqs = 0.0f;
+#pragma unroll
+    for (int w = 0; w < GDN_THREADS / 32; ++w) {  // the same order in every warp: identical sums
+      const float4 x = part[par][w][0][lane], y = part[par][w][1][lane];
+      sk.x += x.x, sk.y += x.y, sk.z += x.z, sk.w += x.w;
+      sq.x += y.x, sq.y += y.y, sq.z += y.z, sq.w += y.w;
+      kqs += part_kq[par][w];
+    }
+    const float4 d = make_float4(beta * (v.x - eg * sk.x), beta * (v.y - eg * sk.y), beta * (v.z - eg * sk.z),
+                                 beta * (v.w - eg * sk.w));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      S[i].x = fmaf(kr[i], d.x, eg * S[i].x), S[i].y = fmaf(kr[i], d.y, eg * S[i].y);
+      S[i].z = fmaf(kr[i], d.z, eg * S[i].z), S[i].w = fmaf(kr[i], d.w, eg * S[i].w);
+    }
+    if (warp == (t & (GDN_THREADS / 32 - 1))) {  // gated RMSNorm (TF:175-190) of token t
+      const float o[4] = {fmaf(eg, sq.x, d.x * kqs), fmaf(eg, sq.y, d.y * kqs), fmaf(eg, sq.z, d.z * kqs),
+                          fmaf(eg, sq.w, d.w * kqs)};
+      const float r = rsqrtf(warp_sum(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]) / float(GD) + a.p.eps);
+      const float4 z =
+          *reinterpret_cast<const float4*>(a.mix + size_t(tok0 + t) * a.ld_mix + conv_dim + h * GD + 4 * lane);
+      store_planes4(a.out, a.lo_offset, a.lo8, size_t(tok0 + t) * value_dim + h * GD + 4 * lane,
+                    nw.x * (o[0] * r) * silu_approx(z.x), nw.y * (o[1] * r) * silu_approx(z.y),
+                    nw.z * (o[2] * r) * silu_approx(z.z), nw.w * (o[3] * r) * silu_approx(z.w));
+    }
+  }
+
+  if (svalid) {
+    float* dst = a.state_pool + (size_t(sslot) * H + h) * GD * GD;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) reinterpret_cast<float4*>(dst + (16 * warp + i) * GD)[lane] = S[i];
+    gdn_save_conv(a, h, tok0, len, pslot, pvalid, sslot);
   }
 }
 
@@ -784,9 +891,14 @@ using namespace sdb;
 
 int sdb_gdn_prep_floats(int heads, int n_tokens) { return n_tokens * heads * GPREP; }
 
-int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix, int32_t ld_mix, uint16_t* out,
-                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, float* prep, int lo8,
-                  cudaStream_t st) {
+// mode: GDN_AUTO picks the recurrent kernel when no sequence of the batch can be longer than
+// one token on average (n_tokens <= n_seqs: single-token appends), the chunk kernel otherwise;
+// GDN_CHUNK / GDN_RECURRENT force one.
+enum { GDN_AUTO = 0, GDN_CHUNK = 1, GDN_RECURRENT = 2 };
+
+static int sdb_gdn_mixer_mode(const b200_gdn_params* p, const b200_seqs* s, const float* mix, int32_t ld_mix,
+                              uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer,
+                              float* prep, int lo8, int mode, cudaStream_t st) {
   if (!p || !s || !mix || !out) return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: null pointer");
   if (p->dk != GD || p->dv != GD || p->conv_width != 4)
     return sdb_fail(B200_ERR_UNSUPPORTED, "b200_gdn_mixer: only dk = dv = 128 and conv width 4 are built");
@@ -827,6 +939,10 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
     attr = true;
   }
   a.n_tokens = s->n_tokens;
+  const bool recurrent = mode == GDN_RECURRENT || (mode == GDN_AUTO && s->n_tokens <= s->n_seqs);
+  if (recurrent && ((reinterpret_cast<uintptr_t>(p->norm_w) & 15) || (reinterpret_cast<uintptr_t>(prep) & 15) ||
+                    (a.state_pool && (reinterpret_cast<uintptr_t>(a.state_pool) & 15))))
+    return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: norm_w, scratch and the pool's gdn_state must be 16-byte aligned");
   if (s->n_tokens > 65535 * 8 * PREP_TPW_LARGE) return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: too many tokens");
   if (long(s->n_tokens) * p->heads >= 64L * 1024) {  // enough warps at 8 tokens each to fill the GPU
     constexpr int TPW = PREP_TPW_LARGE;
@@ -834,6 +950,10 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
                         st, a));
   } else {
     SDB_CUDA(launch_pdl(gdn_prep_kernel<1>, dim3(3 * p->heads, (s->n_tokens + 7) / 8), dim3(256), 0, st, a));
+  }
+  if (recurrent) {
+    SDB_CUDA(launch_pdl(gdn_step_kernel, dim3(p->heads, s->n_seqs), dim3(GDN_THREADS), 0, st, a));
+    return B200_OK;
   }
   if (long(s->n_seqs) * p->heads * 2 > 148) {  // enough (sequence, head) CTAs: one per head
     SDB_CUDA(launch_pdl(gdn_mixer_kernel<GD>, dim3(p->heads, s->n_seqs), dim3(GDN_THREADS), sizeof(GdnSmem<GD>), st,
@@ -862,11 +982,33 @@ int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix
   return B200_OK;
 }
 
+int sdb_gdn_mixer(const b200_gdn_params* p, const b200_seqs* s, const float* mix, int32_t ld_mix, uint16_t* out,
+                  int64_t lo_offset, const b200_prefix_pool* pool, int32_t layer, float* prep, int lo8,
+                  cudaStream_t st) {
+  return sdb_gdn_mixer_mode(p, s, mix, ld_mix, out, lo_offset, pool, layer, prep, lo8, GDN_AUTO, st);
+}
+
 extern "C" int b200_gdn_mixer(const b200_gdn_params* p, const b200_seqs* seqs, const float* mix, int32_t ld_mix,
                               uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool, int32_t gdn_layer,
                               float* scratch, b200_stream stream) {
-  return sdb_gdn_mixer(p, seqs, mix, ld_mix, out, lo_offset, pool, gdn_layer, scratch, 0,
-                       reinterpret_cast<cudaStream_t>(stream));
+  return sdb_gdn_mixer_mode(p, seqs, mix, ld_mix, out, lo_offset, pool, gdn_layer, scratch, 0, GDN_AUTO,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b200_gdn_mixer_recurrent(const b200_gdn_params* p, const b200_seqs* seqs, const float* mix,
+                                        int32_t ld_mix, uint16_t* out, int64_t lo_offset,
+                                        const b200_prefix_pool* pool, int32_t gdn_layer, float* scratch,
+                                        b200_stream stream) {
+  return sdb_gdn_mixer_mode(p, seqs, mix, ld_mix, out, lo_offset, pool, gdn_layer, scratch, 0, GDN_RECURRENT,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b200_gdn_mixer_chunked(const b200_gdn_params* p, const b200_seqs* seqs, const float* mix,
+                                      int32_t ld_mix, uint16_t* out, int64_t lo_offset,
+                                      const b200_prefix_pool* pool, int32_t gdn_layer, float* scratch,
+                                      b200_stream stream) {
+  return sdb_gdn_mixer_mode(p, seqs, mix, ld_mix, out, lo_offset, pool, gdn_layer, scratch, 0, GDN_CHUNK,
+                            reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int b200_gdn_scratch_floats(int32_t heads, int32_t n_tokens) { return sdb_gdn_prep_floats(heads, n_tokens); }

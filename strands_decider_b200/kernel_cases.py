@@ -1,7 +1,7 @@
 """Standalone launches of the hot kernels at the 2B shape, for timing and profiling.
 
     python -m strands_decider_b200.kernel_cases gemm [--m 8192] [--fmt nvfp4] [--ep swiglu] [--planes split]
-    python -m strands_decider_b200.kernel_cases gdn [--seqs 32] [--len 512]
+    python -m strands_decider_b200.kernel_cases gdn [--seqs 32] [--len 512] [--scan auto|chunked|recurrent] [--prefix]
     python -m strands_decider_b200.kernel_cases attention [--seqs 1] [--len 96]
 
 Each case builds seeded synthetic operands on cuda:0, runs a few warm-up launches, prints
@@ -89,8 +89,13 @@ def gemm_case(m: int, fmt: str, ep: str, n: int = 2 * 6144, k: int = 2048, plane
     return launch, 2.0 * m * n * k
 
 
-def gdn_case(seqs: int, length: int, heads: int = 16):
-    """b200_gdn_mixer (prep + chunk kernels) over `seqs` sequences of `length` tokens."""
+GDN_ENTRY = {"auto": "b200_gdn_mixer", "chunked": "b200_gdn_mixer_chunked", "recurrent": "b200_gdn_mixer_recurrent"}
+
+
+def gdn_case(seqs: int, length: int, heads: int = 16, scan: str = "auto", prefix: bool = False):
+    """b200_gdn_mixer (prep + scan kernels) over `seqs` sequences of `length` tokens; `scan`
+    forces the chunked or the recurrent kernel; with `prefix` every sequence continues its own
+    pool slot's state and conv history and saves the continued ones back (an append)."""
     g = torch.Generator(device="cuda").manual_seed(0)
     ld = 3 * heads * 128 + heads * 128 + 2 * heads
     T = seqs * length
@@ -102,13 +107,24 @@ def gdn_case(seqs: int, length: int, heads: int = 16):
     nw = torch.ones(128, device="cuda")
     p = _lib.GdnParams(heads, 128, 128, 4, 1e-6, _lib.ptr(conv_w), _lib.ptr(a_log), _lib.ptr(dt), _lib.ptr(nw))
     cu = torch.arange(0, T + 1, length, dtype=torch.int32, device="cuda")
-    s = _lib.Seqs(seqs, T, length, _lib.ptr(cu), None, None)
     scratch = torch.empty(_lib.load().b200_gdn_scratch_floats(heads, T), device="cuda")
-    keep = (mix, out, conv_w, a_log, dt, nw, cu, scratch)
+    keep = [mix, out, conv_w, a_log, dt, nw, cu, scratch]
+    pool = None
+    if prefix:
+        slots = torch.arange(seqs, dtype=torch.int32, device="cuda")
+        state = 0.05 * torch.randn(seqs, heads, 128, 128, device="cuda", generator=g)
+        hist = torch.randn(seqs, 3, 3 * heads * 128, device="cuda", generator=g)
+        slot_len = torch.zeros(seqs, dtype=torch.int32, device="cuda")
+        keep += [slots, state, hist, slot_len]
+        pool = C.byref(_lib.PrefixPool(seqs, 0, _lib.ptr(slot_len), _lib.ptr(slot_len), _lib.ptr(state),
+                                       _lib.ptr(hist), None, None))
+        s = _lib.Seqs(seqs, T, length, _lib.ptr(cu), _lib.ptr(slots), _lib.ptr(slots))
+    else:
+        s = _lib.Seqs(seqs, T, length, _lib.ptr(cu), None, None)
 
     def launch():
-        _lib.call("b200_gdn_mixer", C.byref(p), C.byref(s), _lib.ptr(keep[0]), ld, _lib.ptr(keep[1]),
-                  T * heads * 128, None, 0, _lib.ptr(keep[7]), _lib.stream_ptr())
+        _lib.call(GDN_ENTRY[scan], C.byref(p), C.byref(s), _lib.ptr(keep[0]), ld, _lib.ptr(keep[1]),
+                  T * heads * 128, pool, 0, _lib.ptr(keep[7]), _lib.stream_ptr())
 
     return launch, None
 
@@ -155,6 +171,8 @@ def main() -> None:
     ap.add_argument("--seqs", type=int, default=32)
     ap.add_argument("--len", type=int, default=512)
     ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--scan", default="auto", choices=sorted(GDN_ENTRY))
+    ap.add_argument("--prefix", action="store_true", help="gdn: sequences continue (and save) pool slots")
     args = ap.parse_args()
     if not torch.cuda.is_available():
         raise SystemExit("kernel_cases needs a CUDA device")
@@ -163,8 +181,9 @@ def main() -> None:
         launch, flops = gemm_case(args.m, args.fmt, args.ep, args.n, args.k, args.planes)
         label = f"gemm {args.fmt} {args.ep} {args.planes} M={args.m} N={args.n} K={args.k}"
     elif args.case == "gdn":
-        launch, flops = gdn_case(args.seqs, args.len)
-        label = f"gdn {args.seqs} x {args.len} tokens, 16 heads (prep + chunk kernels)"
+        launch, flops = gdn_case(args.seqs, args.len, scan=args.scan, prefix=args.prefix)
+        label = (f"gdn {args.seqs} x {args.len} tokens, 16 heads (prep + {args.scan} scan"
+                 f"{', appended to pool slots' if args.prefix else ''})")
     else:
         launch, flops = attention_case(args.seqs, args.len)
         label = f"attention {args.seqs} x {args.len} tokens (prep + flash kernels)"

@@ -288,6 +288,86 @@ def test_gdn_mixer_matches_oracle_chunk_rule(batch):
         assert err < 2e-4, (n, err)
 
 
+@pytest.mark.parametrize("lens", [[1] * 37, [0, 1, 1, 2, 5, 40]], ids=["single-token", "ragged"])
+def test_gdn_recurrent_appends_match_oracle(lens):
+    """The token-by-token kernel (what b200_gdn_mixer runs for single-token appends) continues
+    every sequence from its pool slot's state and conv history and saves the continued ones
+    back into the same slot. Outputs, saved states and saved conv histories against the
+    oracle's recurrent rule (TF:314-353) with the gated norm; the chunked kernel on the same
+    batch agrees with it, and the automatic choice for one token per sequence is the
+    recurrent kernel itself (bit-identical)."""
+    import torch.nn.functional as F
+
+    from oracle import torso as T
+    from strands_decider_b200 import _lib
+
+    H, dk = 2, 128
+    conv_dim, vdim = 3 * H * dk, H * dk
+    n = len(lens)
+    g = torch.Generator().manual_seed(3)
+    Ttot = sum(lens)
+    mix = torch.randn(Ttot, conv_dim + vdim + 2 * H, generator=g)
+    ab = mix[:, conv_dim + vdim:]
+    conv_w = torch.rand(conv_dim, 4, generator=g) - 0.5
+    a_log = torch.log(torch.rand(H, generator=g) * 0.99 + 0.01)
+    dt_bias = torch.ones(H)
+    norm_w = 1 + 0.1 * torch.randn(dk, generator=g)
+    state0 = 0.05 * torch.randn(1, n, H, dk, dk, generator=g)
+    hist0 = torch.randn(1, n, 3, conv_dim, generator=g)
+    cu = [0]
+    for m in lens:
+        cu.append(cu[-1] + m)
+    keep = [conv_w.cuda(), a_log.cuda(), dt_bias.cuda(), norm_w.cuda()]
+    p = _lib.GdnParams(H, 128, 128, 4, 1e-6, *[_lib.ptr(t) for t in keep])
+    cu_d = torch.tensor(cu, dtype=torch.int32, device="cuda")
+    slots = torch.arange(n, dtype=torch.int32, device="cuda")
+    seqs = _lib.Seqs(n, Ttot, max(lens), _lib.ptr(cu_d), _lib.ptr(slots), _lib.ptr(slots))
+    mix_d = mix.cuda()
+    slot_len = torch.zeros(n, dtype=torch.int32, device="cuda")
+    slot_kv = torch.zeros(n, dtype=torch.int32, device="cuda")
+
+    def run(entry):
+        st, hist = state0.cuda(), hist0.cuda()
+        pool = _lib.PrefixPool(n, 0, _lib.ptr(slot_len), _lib.ptr(slot_kv), _lib.ptr(st), _lib.ptr(hist), None, None)
+        out = torch.zeros(2, Ttot, vdim, dtype=torch.bfloat16, device="cuda")
+        scratch = torch.empty(_lib.load().b200_gdn_scratch_floats(H, Ttot), device="cuda")
+        _lib.call(entry, _ref(p), _ref(seqs), _lib.ptr(mix_d), mix.shape[1], _lib.ptr(out), Ttot * vdim,
+                  _ref(pool), 0, _lib.ptr(scratch), _lib.stream_ptr())
+        torch.cuda.synchronize()
+        return out.float().cpu(), st.cpu(), hist.cpu()
+
+    out_r, st_r, hist_r = run("b200_gdn_mixer_recurrent")
+    got = out_r[0] + out_r[1]
+    for i, m in enumerate(lens):
+        rows = slice(cu[i], cu[i + 1])
+        x = mix[rows].float()
+        xin = torch.cat([hist0[0, i], x[:, :conv_dim]], 0)
+        conv = torch.zeros(m, conv_dim)
+        for j in range(4):
+            conv = conv + xin[j:j + m] * conv_w[:, j]
+        conv = F.silu(conv)
+        q, k, v = conv[:, :H * dk].view(m, H, dk), conv[:, H * dk:2 * H * dk].view(m, H, dk), conv[:, 2 * H * dk:].view(m, H, dk)
+        beta = ab[rows, :H].sigmoid()
+        gg = -a_log.exp() * F.softplus(ab[rows, H:] + dt_bias)
+        o, s_want = T.recurrent_gated_delta_rule(q, k, v, gg, beta, initial_state=state0[0, i])
+        err_s = (st_r[0, i] - s_want).abs().max().item() / s_want.abs().max().item()
+        assert err_s < 1e-4, (i, m, err_s)
+        assert torch.equal(hist_r[0, i], xin[-3:]), (i, m)   # the last 3 raw inputs, bit-exact
+        if m:
+            z = x[:, conv_dim:conv_dim + vdim].reshape(-1, dk)
+            want = T.gated_rms_norm(o.reshape(-1, dk), z, norm_w, 1e-6).reshape(m, vdim)
+            err = (got[rows] - want).abs().max().item() / (want.abs().max().item() + 1e-6)
+            assert err < 2e-4, (i, m, err)
+
+    out_c, st_c, hist_c = run("b200_gdn_mixer_chunked")
+    assert ((out_c[0] + out_c[1]) - got).abs().max().item() < 4e-4 * got.abs().max().item()
+    assert (st_c - st_r).abs().max().item() < 5e-4 * st_r.abs().max().item()
+    assert torch.equal(hist_c, hist_r)
+    if Ttot <= n:
+        out_a, st_a, _ = run("b200_gdn_mixer")
+        assert torch.equal(out_a, out_r) and torch.equal(st_a, st_r)
+
+
 @pytest.mark.parametrize("fmt", ["int4", "nvfp4", "ternary"])
 def test_tile_weights_layout(fmt):
     """The GEMM's streaming copy holds exactly the canonical bytes, chunked per
