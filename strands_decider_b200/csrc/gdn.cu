@@ -793,13 +793,19 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
 // come out of one pass over S. grid (heads, n_seqs), 8 warps: warp w owns the state rows (key
 // dims) 16w..16w+15 and lane l the value columns 4l..4l+3, so one row of a warp is one
 // coalesced 512-byte float4 access and the fp32 state stays in registers for the whole
-// sequence. The column sums are reduced across the 8 warps through shared memory (one barrier
-// per token; the partials are double-buffered by token parity, so the next token's writes never
-// meet this token's reads). Every warp then holds o for all 128 columns; warp (t mod 8) applies
-// the gated RMSNorm to token t and stores its planes.
+// sequence. The prep records arrive in shared memory by bulk copies of GSTEP_TB tokens, one
+// block ahead (double-buffered, bounded waits), so no token waits on DRAM. The column sums are
+// reduced across the 8 warps through shared memory (one barrier per token; the partials are
+// double-buffered by token parity, so the next token's writes never meet this token's reads).
+// Every warp then holds o for all 128 columns; warp (t mod 8) applies the gated RMSNorm to
+// token t, with its z gate row loaded when the token's block starts.
+constexpr int GSTEP_TB = GDN_THREADS / 32;  // tokens per staged block: one per warp
+
 __global__ void __launch_bounds__(GDN_THREADS, 2) gdn_step_kernel(const GdnArgs a) {
+  __shared__ __align__(128) float stage[2][GSTEP_TB * GPREP];
   __shared__ float4 part[2][GDN_THREADS / 32][2][32];  // [parity][warp][S^T k | S^T q][lane]
   __shared__ float part_kq[2][GDN_THREADS / 32];
+  __shared__ __align__(8) uint64_t bar[2];
   pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
   pdl_trigger();
   const int h = blockIdx.x, seq = blockIdx.y;
@@ -812,6 +818,18 @@ __global__ void __launch_bounds__(GDN_THREADS, 2) gdn_step_kernel(const GdnArgs 
   const bool pvalid = pslot >= 0 && pslot < a.n_slots;
   const bool svalid = sslot >= 0 && sslot < a.n_slots;
   if ((pslot >= a.n_slots || sslot >= a.n_slots) && threadIdx.x == 0) raise_fault(FAULT_BAD_INDEX);
+  const float* recs = a.prep + (size_t(h) * a.n_tokens + tok0) * GPREP;  // this head's records, token-major
+  auto stage_block = [&](int b) {  // records of tokens b * TB .. (one thread)
+    const uint32_t bytes = uint32_t(min(GSTEP_TB, len - b * GSTEP_TB)) * GPREP * 4;
+    mbar_arrive_expect_tx(&bar[b & 1], bytes);
+    bulk_load(stage[b & 1], recs + size_t(b) * GSTEP_TB * GPREP, bytes, &bar[b & 1]);
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    mbar_fence_init();
+    if (len > 0) stage_block(0);
+  }
 
   float4 S[16];  // S[i] = state row 16 * warp + i, columns 4 * lane .. 4 * lane + 3
   {
@@ -821,59 +839,74 @@ __global__ void __launch_bounds__(GDN_THREADS, 2) gdn_step_kernel(const GdnArgs 
       S[i] = src ? reinterpret_cast<const float4*>(src + (16 * warp + i) * GD)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   const float4 nw = reinterpret_cast<const float4*>(a.p.norm_w)[lane];
+  __syncthreads();  // barriers initialised
 
-  for (int t = 0; t < len; ++t) {
-    const float* rec = a.prep + (size_t(h) * a.n_tokens + tok0 + t) * GPREP;  // q | k | v | beta, g
-    float qr[16], kr[16];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {  // the warp's 16 rows of q and k: the same address in every lane
-      const float4 q4 = reinterpret_cast<const float4*>(rec + 16 * warp)[i];
-      const float4 k4 = reinterpret_cast<const float4*>(rec + GD + 16 * warp)[i];
-      qr[4 * i] = q4.x, qr[4 * i + 1] = q4.y, qr[4 * i + 2] = q4.z, qr[4 * i + 3] = q4.w;
-      kr[4 * i] = k4.x, kr[4 * i + 1] = k4.y, kr[4 * i + 2] = k4.z, kr[4 * i + 3] = k4.w;
+  for (int b = 0; b * GSTEP_TB < len; ++b) {
+    const int nb = min(GSTEP_TB, len - b * GSTEP_TB);
+    float4 z = make_float4(0.f, 0.f, 0.f, 0.f);  // the z gate of token b * TB + warp (normed by this warp)
+    if (warp < nb)
+      z = *reinterpret_cast<const float4*>(a.mix + size_t(tok0 + b * GSTEP_TB + warp) * a.ld_mix + conv_dim + h * GD +
+                                           4 * lane);
+    if (threadIdx.x == 0 && (b + 1) * GSTEP_TB < len) {
+      // the other buffer was last read by block b - 1, before the barriers all threads passed since
+      fence_proxy_async_smem();
+      stage_block(b + 1);
     }
-    const float4 v = reinterpret_cast<const float4*>(rec + 2 * GD)[lane];
-    const float beta = rec[GQKV], eg = expf(rec[GQKV + 1]);
-    float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pq = pk;
-    float kq = 0.0f;
+    const bool landed = mbar_wait(&bar[b & 1], (b >> 1) & 1, FAULT_GDN_WAIT_STAGE);
+    if (__syncthreads_or(!landed)) break;  // a copy that never landed: give up (fault recorded)
+    for (int tt = 0; tt < nb; ++tt) {
+      const int t = b * GSTEP_TB + tt;
+      const float* rec = stage[b & 1] + tt * GPREP;  // q | k | v | beta, g
+      float qr[16], kr[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      pk.x = fmaf(S[i].x, kr[i], pk.x), pk.y = fmaf(S[i].y, kr[i], pk.y);
-      pk.z = fmaf(S[i].z, kr[i], pk.z), pk.w = fmaf(S[i].w, kr[i], pk.w);
-      pq.x = fmaf(S[i].x, qr[i], pq.x), pq.y = fmaf(S[i].y, qr[i], pq.y);
-      pq.z = fmaf(S[i].z, qr[i], pq.z), pq.w = fmaf(S[i].w, qr[i], pq.w);
-      kq = fmaf(kr[i], qr[i], kq);
-    }
-    const int par = t & 1;
-    part[par][warp][0][lane] = pk;
-    part[par][warp][1][lane] = pq;
-    if (lane == 0) part_kq[par][warp] = kq;
-    __syncthreads();
-    float4 sk = make_float4(0.f, 0.f, 0.f, 0.f), sq = sk;
-    float kqs = 0.0f;
+      for (int i = 0; i < 4; ++i) {  // the warp's 16 rows of q and k (a broadcast read)
+        const float4 q4 = reinterpret_cast<const float4*>(rec + 16 * warp)[i];
+        const float4 k4 = reinterpret_cast<const float4*>(rec + GD + 16 * warp)[i];
+        qr[4 * i] = q4.x, qr[4 * i + 1] = q4.y, qr[4 * i + 2] = q4.z, qr[4 * i + 3] = q4.w;
+        kr[4 * i] = k4.x, kr[4 * i + 1] = k4.y, kr[4 * i + 2] = k4.z, kr[4 * i + 3] = k4.w;
+      }
+      const float4 v = reinterpret_cast<const float4*>(rec + 2 * GD)[lane];
+      const float beta = rec[GQKV], eg = expf(rec[GQKV + 1]);
+      float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pq = pk;
+      float kq = 0.0f;
 #pragma unroll
-    for (int w = 0; w < GDN_THREADS / 32; ++w) {  // the same order in every warp: identical sums
-      const float4 x = part[par][w][0][lane], y = part[par][w][1][lane];
-      sk.x += x.x, sk.y += x.y, sk.z += x.z, sk.w += x.w;
-      sq.x += y.x, sq.y += y.y, sq.z += y.z, sq.w += y.w;
-      kqs += part_kq[par][w];
-    }
-    const float4 d = make_float4(beta * (v.x - eg * sk.x), beta * (v.y - eg * sk.y), beta * (v.z - eg * sk.z),
-                                 beta * (v.w - eg * sk.w));
+      for (int i = 0; i < 16; ++i) {
+        pk.x = fmaf(S[i].x, kr[i], pk.x), pk.y = fmaf(S[i].y, kr[i], pk.y);
+        pk.z = fmaf(S[i].z, kr[i], pk.z), pk.w = fmaf(S[i].w, kr[i], pk.w);
+        pq.x = fmaf(S[i].x, qr[i], pq.x), pq.y = fmaf(S[i].y, qr[i], pq.y);
+        pq.z = fmaf(S[i].z, qr[i], pq.z), pq.w = fmaf(S[i].w, qr[i], pq.w);
+        kq = fmaf(kr[i], qr[i], kq);
+      }
+      const int par = t & 1;
+      part[par][warp][0][lane] = pk;
+      part[par][warp][1][lane] = pq;
+      if (lane == 0) part_kq[par][warp] = kq;
+      __syncthreads();
+      float4 sk = make_float4(0.f, 0.f, 0.f, 0.f), sq = sk;
+      float kqs = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      S[i].x = fmaf(kr[i], d.x, eg * S[i].x), S[i].y = fmaf(kr[i], d.y, eg * S[i].y);
-      S[i].z = fmaf(kr[i], d.z, eg * S[i].z), S[i].w = fmaf(kr[i], d.w, eg * S[i].w);
-    }
-    if (warp == (t & (GDN_THREADS / 32 - 1))) {  // gated RMSNorm (TF:175-190) of token t
-      const float o[4] = {fmaf(eg, sq.x, d.x * kqs), fmaf(eg, sq.y, d.y * kqs), fmaf(eg, sq.z, d.z * kqs),
-                          fmaf(eg, sq.w, d.w * kqs)};
-      const float r = rsqrtf(warp_sum(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]) / float(GD) + a.p.eps);
-      const float4 z =
-          *reinterpret_cast<const float4*>(a.mix + size_t(tok0 + t) * a.ld_mix + conv_dim + h * GD + 4 * lane);
-      store_planes4(a.out, a.lo_offset, a.lo8, size_t(tok0 + t) * value_dim + h * GD + 4 * lane,
-                    nw.x * (o[0] * r) * silu_approx(z.x), nw.y * (o[1] * r) * silu_approx(z.y),
-                    nw.z * (o[2] * r) * silu_approx(z.z), nw.w * (o[3] * r) * silu_approx(z.w));
+      for (int w = 0; w < GDN_THREADS / 32; ++w) {  // the same order in every warp: identical sums
+        const float4 x = part[par][w][0][lane], y = part[par][w][1][lane];
+        sk.x += x.x, sk.y += x.y, sk.z += x.z, sk.w += x.w;
+        sq.x += y.x, sq.y += y.y, sq.z += y.z, sq.w += y.w;
+        kqs += part_kq[par][w];
+      }
+      const float4 d = make_float4(beta * (v.x - eg * sk.x), beta * (v.y - eg * sk.y), beta * (v.z - eg * sk.z),
+                                   beta * (v.w - eg * sk.w));
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        S[i].x = fmaf(kr[i], d.x, eg * S[i].x), S[i].y = fmaf(kr[i], d.y, eg * S[i].y);
+        S[i].z = fmaf(kr[i], d.z, eg * S[i].z), S[i].w = fmaf(kr[i], d.w, eg * S[i].w);
+      }
+      if (warp == tt) {  // gated RMSNorm (TF:175-190) of token t
+        const float o[4] = {fmaf(eg, sq.x, d.x * kqs), fmaf(eg, sq.y, d.y * kqs), fmaf(eg, sq.z, d.z * kqs),
+                            fmaf(eg, sq.w, d.w * kqs)};
+        const float r =
+            rsqrtf(warp_sum(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]) / float(GD) + a.p.eps);
+        store_planes4(a.out, a.lo_offset, a.lo8, size_t(tok0 + t) * value_dim + h * GD + 4 * lane,
+                      nw.x * (o[0] * r) * silu_approx(z.x), nw.y * (o[1] * r) * silu_approx(z.y),
+                      nw.z * (o[2] * r) * silu_approx(z.z), nw.w * (o[3] * r) * silu_approx(z.w));
+      }
     }
   }
 
