@@ -360,9 +360,11 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = 16 * warp + g8 + 8 * (e >> 1), c = 8 * nt + 2 * t4 + (e & 1);
-        S[nt][e] = src ? src[r * GD + col0 + c] : 0.0f;
+      for (int hr = 0; hr < 2; ++hr) {  // columns c, c + 1 as one 8-byte load
+        const int r = 16 * warp + g8 + 8 * hr, c = 8 * nt + 2 * t4;
+        const float2 v = src ? *reinterpret_cast<const float2*>(src + r * GD + col0 + c) : make_float2(0.f, 0.f);
+        S[nt][2 * hr] = v.x;
+        S[nt][2 * hr + 1] = v.y;
       }
     }
   }
@@ -382,6 +384,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
   uint32_t phase = 0;
   for (int c0 = 0; c0 < len; c0 += GC) {
     const int L = min(GC, len - c0);
+    const bool need_state = svalid || c0 + GC < len;  // the state after this chunk is used
     const bool landed = mbar_wait(&sm.bar, phase, FAULT_GDN_WAIT_STAGE);
     phase ^= 1u;
     if constexpr (NS == 1) {
@@ -602,7 +605,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
               const float v0 = ok ? sm.ru.uw.U[r][c] - ws[i][half][2 * hr] : 0.0f;
               const float v1 = ok ? sm.ru.uw.U[r][c + 1] - ws[i][half][2 * hr + 1] : 0.0f;
               split_store(sm.Vh, sm.Vl, soff<DV>(r, c), v0, v1);
-              split_store(sm.Th, sm.Tl, soff<DV>(r, c), v0 * sm.eL[r], v1 * sm.eL[r]);
+              if (need_state) split_store(sm.Th, sm.Tl, soff<DV>(r, c), v0 * sm.eL[r], v1 * sm.eL[r]);
               O[r][c] = qs[i][half][2 * hr] * sm.eG[r];  // overwrites U[r][c], read just above by this thread
               O[r][c + 1] = qs[i][half][2 * hr + 1] * sm.eG[r];
             }
@@ -651,8 +654,9 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
         }
       }
     }
-    // ---- 7b. S = e^{G_last} S + k^T (Vn e^{G_last - G}): warp w owns S rows 16w..16w+15
-    {
+    // ---- 7b. S = e^{G_last} S + k^T (Vn e^{G_last - G}): warp w owns S rows 16w..16w+15;
+    //          skipped after the last chunk of a sequence that saves no state (a question)
+    if (need_state) {
       const float el = __expf(sm.G[L - 1]);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
@@ -674,12 +678,14 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       }
     }
     __syncthreads();  // all reads of the old S planes (step 6) and of O's partials are done
+    if (need_state) {
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+      for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-      for (int hr = 0; hr < 2; ++hr)
-        split_store(sm.Sh, sm.Sl, soff<DV>(16 * warp + g8 + 8 * hr, 8 * nt + 2 * t4), S[nt][2 * hr],
-                    S[nt][2 * hr + 1]);
+        for (int hr = 0; hr < 2; ++hr)
+          split_store(sm.Sh, sm.Sl, soff<DV>(16 * warp + g8 + 8 * hr, 8 * nt + 2 * t4), S[nt][2 * hr],
+                      S[nt][2 * hr + 1]);
+      }
     }
     // ---- 8. gated RMSNorm of the O rows -> hi/lo planes; warp w owns rows w, w + 8, ...;
     //         lane l owns this CTA's columns CPL*l .. CPL*l + CPL - 1

@@ -1,7 +1,7 @@
 """Standalone launches of the hot kernels at the 2B shape, for timing and profiling.
 
     python -m strands_decider_b200.kernel_cases gemm [--m 8192] [--fmt nvfp4] [--ep swiglu] [--planes split]
-    python -m strands_decider_b200.kernel_cases gdn [--seqs 32] [--len 512] [--scan auto|chunked|recurrent] [--prefix]
+    python -m strands_decider_b200.kernel_cases gdn [--seqs 32] [--len 512] [--scan auto|chunked|recurrent] [--prefix read|append]
     python -m strands_decider_b200.kernel_cases attention [--seqs 1] [--len 96]
 
 Each case builds seeded synthetic operands on cuda:0, runs a few warm-up launches, prints
@@ -92,10 +92,11 @@ def gemm_case(m: int, fmt: str, ep: str, n: int = 2 * 6144, k: int = 2048, plane
 GDN_ENTRY = {"auto": "b200_gdn_mixer", "chunked": "b200_gdn_mixer_chunked", "recurrent": "b200_gdn_mixer_recurrent"}
 
 
-def gdn_case(seqs: int, length: int, heads: int = 16, scan: str = "auto", prefix: bool = False):
+def gdn_case(seqs: int, length: int, heads: int = 16, scan: str = "auto", prefix: str = ""):
     """b200_gdn_mixer (prep + scan kernels) over `seqs` sequences of `length` tokens; `scan`
-    forces the chunked or the recurrent kernel; with `prefix` every sequence continues its own
-    pool slot's state and conv history and saves the continued ones back (an append)."""
+    forces the chunked or the recurrent kernel. prefix "read": every sequence starts from its own
+    pool slot's state and conv history (a question against a cached state); "append": it also
+    saves the continued ones back into the slot."""
     g = torch.Generator(device="cuda").manual_seed(0)
     ld = 3 * heads * 128 + heads * 128 + 2 * heads
     T = seqs * length
@@ -118,7 +119,7 @@ def gdn_case(seqs: int, length: int, heads: int = 16, scan: str = "auto", prefix
         keep += [slots, state, hist, slot_len]
         pool = C.byref(_lib.PrefixPool(seqs, 0, _lib.ptr(slot_len), _lib.ptr(slot_len), _lib.ptr(state),
                                        _lib.ptr(hist), None, None))
-        s = _lib.Seqs(seqs, T, length, _lib.ptr(cu), _lib.ptr(slots), _lib.ptr(slots))
+        s = _lib.Seqs(seqs, T, length, _lib.ptr(cu), _lib.ptr(slots), _lib.ptr(slots) if prefix == "append" else None)
     else:
         s = _lib.Seqs(seqs, T, length, _lib.ptr(cu), None, None)
 
@@ -172,7 +173,8 @@ def main() -> None:
     ap.add_argument("--len", type=int, default=512)
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--scan", default="auto", choices=sorted(GDN_ENTRY))
-    ap.add_argument("--prefix", action="store_true", help="gdn: sequences continue (and save) pool slots")
+    ap.add_argument("--prefix", default="", choices=["", "read", "append"],
+                    help="gdn: sequences start from (read) or continue and save (append) pool slots")
     args = ap.parse_args()
     if not torch.cuda.is_available():
         raise SystemExit("kernel_cases needs a CUDA device")
@@ -183,7 +185,7 @@ def main() -> None:
     elif args.case == "gdn":
         launch, flops = gdn_case(args.seqs, args.len, scan=args.scan, prefix=args.prefix)
         label = (f"gdn {args.seqs} x {args.len} tokens, 16 heads (prep + {args.scan} scan"
-                 f"{', appended to pool slots' if args.prefix else ''})")
+                 f"{', prefix ' + args.prefix if args.prefix else ''})")
     else:
         launch, flops = attention_case(args.seqs, args.len)
         label = f"attention {args.seqs} x {args.len} tokens (prep + flash kernels)"
