@@ -416,6 +416,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
     __syncthreads();
     if (tid < GC) sm.eL[tid] = tid < L ? __expf(sm.G[L - 1] - sm.G[tid]) : 0.0f;
     // ---- 2. q, k, [beta v | beta k e^G] as hi/lo planes (rows past L are zero)
+#pragma unroll
     for (int j = warp; j < GC; j += GDN_THREADS / 32) {
       float4 q = make_float4(0.f, 0.f, 0.f, 0.f), k = q, v = q;
       if (j < L) {
@@ -438,27 +439,34 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       fence_proxy_async_smem();
       gdn_stage_chunk(sm.stage, &sm.bar, a, h, tok0, len, c0 + GC);
     }
-    // ---- 3. A = beta k k^T, P = q k^T (x decay, masked): warp -> rows 16*(w>>2), cols 8*(w&3)
+    // ---- 3. A = beta k k^T, P = q k^T (x decay, masked): warp -> rows 16*(w>>2), cols 8*(w&3);
+    //         each of the three split passes accumulates apart (three short dependency chains)
     {
       const int m0 = 16 * (warp >> 2), n0 = 8 * (warp & 3);
       float kk[4] = {0, 0, 0, 0}, qk[4] = {0, 0, 0, 0};
+      float kk1[4] = {0, 0, 0, 0}, qk1[4] = {0, 0, 0, 0}, kk2[4] = {0, 0, 0, 0}, qk2[4] = {0, 0, 0, 0};
+      // B fragment of the n-tile n0 (8 keys) x k16 from both planes in one ldmatrix.x4: lanes 0-15
+      // address the hi plane, 16-31 the lo plane -> {hi b0, hi b1, lo b0, lo b1}
+      const uint16_t* bplane = lane < 16 ? sm.Kh : sm.Kl;
 #pragma unroll 2
       for (int k0 = 0; k0 < GD; k0 += 16) {
-        uint32_t kh[4], kl[4], qh[4], ql[4], bh[4], bl[4];
+        uint32_t kh[4], kl[4], qh[4], ql[4], b[4];
         frag_a<GD>(kh, sm.Kh, m0, k0, lane);
         frag_a<GD>(kl, sm.Kl, m0, k0, lane);
         frag_a<GD>(qh, sm.Qh, m0, k0, lane);
         frag_a<GD>(ql, sm.Ql, m0, k0, lane);
-        frag_b<GD>(bh, sm.Kh, n0 & ~15, k0, lane);   // n-tiles (n0&~15) and +8
-        frag_b<GD>(bl, sm.Kl, n0 & ~15, k0, lane);
-        const int sel = (n0 & 8) ? 2 : 0;
-        const uint32_t b0h = bh[sel], b1h = bh[sel + 1], b0l = bl[sel], b1l = bl[sel + 1];
-        mma16816(kk, kh, b0h, b1h);
-        mma16816(kk, kh, b0l, b1l);
-        mma16816(kk, kl, b0h, b1h);
-        mma16816(qk, qh, b0h, b1h);
-        mma16816(qk, qh, b0l, b1l);
-        mma16816(qk, ql, b0h, b1h);
+        ldsm4(b, smem_addr(bplane) + soff<GD>(n0 + (lane & 7), k0 + (((lane >> 3) & 1) << 3)));
+        mma16816(kk, kh, b[0], b[1]);
+        mma16816(qk, qh, b[0], b[1]);
+        mma16816(kk1, kh, b[2], b[3]);
+        mma16816(qk1, qh, b[2], b[3]);
+        mma16816(kk2, kl, b[0], b[1]);
+        mma16816(qk2, ql, b[0], b[1]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        kk[e] += kk1[e] + kk2[e];
+        qk[e] += qk1[e] + qk2[e];
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -677,6 +685,27 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
         }
       }
     }
+    // the z gates of all the warp's step-8 rows (and the norm weights), loaded here so that their
+    // latency passes under the barrier and the state-plane stores
+    constexpr int CPL = DV / 32;
+    float nw[CPL], zv[GC / 8][CPL];
+#pragma unroll
+    for (int e = 0; e < CPL; ++e) nw[e] = a.p.norm_w[col0 + lane * CPL + e];
+#pragma unroll
+    for (int i = 0; i < GC / 8; ++i) {
+      const int j = warp + 8 * i;
+      const float* z = a.mix + size_t(tok0 + c0 + (j < L ? j : 0)) * a.ld_mix + conv_dim + h * GD + col0 + lane * CPL;
+      if constexpr (CPL == 4) {
+        const float4 z4 = j < L ? *reinterpret_cast<const float4*>(z) : make_float4(0.f, 0.f, 0.f, 0.f);
+        zv[i][0] = z4.x;
+        zv[i][1] = z4.y;
+        zv[i][2] = z4.z;
+        zv[i][3] = z4.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < CPL; ++e) zv[i][e] = j < L ? z[e] : 0.0f;
+      }
+    }
     __syncthreads();  // all reads of the old S planes (step 6) and of O's partials are done
     if (need_state) {
 #pragma unroll
@@ -690,26 +719,8 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
     // ---- 8. gated RMSNorm of the O rows -> hi/lo planes; warp w owns rows w, w + 8, ...;
     //         lane l owns this CTA's columns CPL*l .. CPL*l + CPL - 1
     {
-      constexpr int CPL = DV / 32;
       const int cpar = (c0 / GC) & 1;
-      float nw[CPL], zv[GC / 8][CPL], ov[GC / 8][CPL], ss[GC / 8];
-#pragma unroll
-      for (int e = 0; e < CPL; ++e) nw[e] = a.p.norm_w[col0 + lane * CPL + e];
-#pragma unroll
-      for (int i = 0; i < GC / 8; ++i) {  // the z gates of all the warp's rows, loaded before any is used
-        const int j = warp + 8 * i;
-        const float* z = a.mix + size_t(tok0 + c0 + (j < L ? j : 0)) * a.ld_mix + conv_dim + h * GD + col0 + lane * CPL;
-        if constexpr (CPL == 4) {
-          const float4 z4 = j < L ? *reinterpret_cast<const float4*>(z) : make_float4(0.f, 0.f, 0.f, 0.f);
-          zv[i][0] = z4.x;
-          zv[i][1] = z4.y;
-          zv[i][2] = z4.z;
-          zv[i][3] = z4.w;
-        } else {
-#pragma unroll
-          for (int e = 0; e < CPL; ++e) zv[i][e] = j < L ? z[e] : 0.0f;
-        }
-      }
+      float ov[GC / 8][CPL], ss[GC / 8];
 #pragma unroll
       for (int i = 0; i < GC / 8; ++i) {
         const int j = warp + 8 * i;
