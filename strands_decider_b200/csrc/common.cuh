@@ -51,8 +51,11 @@ __device__ __forceinline__ uint16_t f32_to_bf16_rn(float x) {
   return *reinterpret_cast<uint16_t*>(&h);
 }
 
+// {bf16_rn(lo), bf16_rn(hi)} in one conversion (lo in the low half)
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return uint32_t(f32_to_bf16_rn(lo)) | (uint32_t(f32_to_bf16_rn(hi)) << 16);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // ----------------------------------------------------------------------------- e4m3 low plane

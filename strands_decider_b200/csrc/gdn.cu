@@ -113,21 +113,22 @@ __device__ __forceinline__ uint32_t soff(int r, int col) {
   return uint32_t(r * RL * 2 + ((c ^ sw) << 4) + (col & 7) * 2);
 }
 
+// the low plane of a pair packed as h = {bf16(a), bf16(b)}: {bf16(a - hi(a)), bf16(b - hi(b))}
+__device__ __forceinline__ uint32_t lo_pair(float a, float b, uint32_t h) {
+  return pack_bf16x2(a - __uint_as_float(h << 16), b - __uint_as_float(h & 0xffff0000u));
+}
+
 // four consecutive values (8-byte aligned offset): one 8-byte store per plane
 __device__ __forceinline__ void split_store4(uint16_t* hi, uint16_t* lo, uint32_t off, float4 v) {
-  const uint16_t h0 = f32_to_bf16_rn(v.x), h1 = f32_to_bf16_rn(v.y), h2 = f32_to_bf16_rn(v.z), h3 = f32_to_bf16_rn(v.w);
-  *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(hi) + off) =
-      make_uint2(uint32_t(h0) | (uint32_t(h1) << 16), uint32_t(h2) | (uint32_t(h3) << 16));
-  *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(lo) + off) =
-      make_uint2(pack_bf16x2(v.x - bf16_to_f32(h0), v.y - bf16_to_f32(h1)),
-                 pack_bf16x2(v.z - bf16_to_f32(h2), v.w - bf16_to_f32(h3)));
+  const uint32_t h01 = pack_bf16x2(v.x, v.y), h23 = pack_bf16x2(v.z, v.w);
+  *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(hi) + off) = make_uint2(h01, h23);
+  *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(lo) + off) = make_uint2(lo_pair(v.x, v.y, h01), lo_pair(v.z, v.w, h23));
 }
 
 __device__ __forceinline__ void split_store(uint16_t* hi, uint16_t* lo, uint32_t off, float a, float b) {
-  const uint16_t ha = f32_to_bf16_rn(a), hb = f32_to_bf16_rn(b);
-  *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(hi) + off) = uint32_t(ha) | (uint32_t(hb) << 16);
-  *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(lo) + off) =
-      pack_bf16x2(a - bf16_to_f32(ha), b - bf16_to_f32(hb));
+  const uint32_t h = pack_bf16x2(a, b);
+  *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(hi) + off) = h;
+  *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(lo) + off) = lo_pair(a, b, h);
 }
 
 // A fragment (16 x 16) of a plane stored [m][k] with RL elements per row, rows m0.., cols k0..
