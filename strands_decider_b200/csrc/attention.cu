@@ -383,14 +383,14 @@ __global__ void __launch_bounds__(128 * fa_dg<HD>(), 2) attn_flash_kernel(const 
       const int d = col0 + j * 8 + tq * 2;
       const float y0 = o[j][2 * r] * inv[r] * sigmoid(gate[d]);
       const float y1 = o[j][2 * r + 1] * inv[r] * sigmoid(gate[d + 1]);
-      const uint16_t h0 = f32_to_bf16_rn(y0), h1 = f32_to_bf16_rn(y1);
-      *reinterpret_cast<uint32_t*>(dst + d) = uint32_t(h0) | (uint32_t(h1) << 16);
+      const uint32_t hp = pack_bf16x2(y0, y1);
+      *reinterpret_cast<uint32_t*>(dst + d) = hp;
       if (a.lo_offset && a.lo8)
         *reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(a.out + a.lo_offset) + (t * nq + h) * HD + d) =
-            f32x2_to_e4m3x2(lo8_value(y0, h0), lo8_value(y1, h1));
+            f32x2_to_e4m3x2((y0 - bf16x2_lo(hp)) * float(1 << B200_LO8_X_SHIFT),
+                            (y1 - bf16x2_hi(hp)) * float(1 << B200_LO8_X_SHIFT));
       else if (a.lo_offset)
-        *reinterpret_cast<uint32_t*>(dst + a.lo_offset + d) =
-            pack_bf16x2(y0 - bf16_to_f32(h0), y1 - bf16_to_f32(h1));
+        *reinterpret_cast<uint32_t*>(dst + a.lo_offset + d) = lo_pair(y0, y1, hp);
     }
   }
 }

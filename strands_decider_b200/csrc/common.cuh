@@ -57,6 +57,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
+// the two halves of a packed pair h = pack_bf16x2(a, b) as floats: bf16_rn(a), bf16_rn(b)
+__device__ __forceinline__ float bf16x2_lo(uint32_t h) { return __uint_as_float(h << 16); }
+__device__ __forceinline__ float bf16x2_hi(uint32_t h) { return __uint_as_float(h & 0xffff0000u); }
+// the low plane of a pair packed as h = pack_bf16x2(a, b): {bf16_rn(a - hi(a)), bf16_rn(b - hi(b))}
+__device__ __forceinline__ uint32_t lo_pair(float a, float b, uint32_t h) {
+  return pack_bf16x2(a - bf16x2_lo(h), b - bf16x2_hi(h));
+}
 
 // ----------------------------------------------------------------------------- e4m3 low plane
 // With B200_LO_E4M3 the low activation plane lo = x - bf16(x) is stored as
@@ -81,17 +88,16 @@ __device__ __forceinline__ float lo8_value(float x, uint16_t h) {
 // e4m3 byte with lo8; no lo plane when lo_offset is 0.
 __device__ __forceinline__ void store_planes4(uint16_t* out, long long lo_offset, bool lo8, size_t e, float a,
                                               float b, float c, float d) {
-  const uint16_t h0 = f32_to_bf16_rn(a), h1 = f32_to_bf16_rn(b), h2 = f32_to_bf16_rn(c), h3 = f32_to_bf16_rn(d);
-  *reinterpret_cast<uint2*>(out + e) =
-      make_uint2(uint32_t(h0) | (uint32_t(h1) << 16), uint32_t(h2) | (uint32_t(h3) << 16));
+  const uint32_t h01 = pack_bf16x2(a, b), h23 = pack_bf16x2(c, d);
+  *reinterpret_cast<uint2*>(out + e) = make_uint2(h01, h23);
   if (!lo_offset) return;
   if (lo8) {
+    constexpr float S = float(1 << B200_LO8_X_SHIFT);
     *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(out + lo_offset) + e) =
-        e4m3x4(lo8_value(a, h0), lo8_value(b, h1), lo8_value(c, h2), lo8_value(d, h3));
+        e4m3x4((a - bf16x2_lo(h01)) * S, (b - bf16x2_hi(h01)) * S, (c - bf16x2_lo(h23)) * S,
+               (d - bf16x2_hi(h23)) * S);
   } else {
-    *reinterpret_cast<uint2*>(out + lo_offset + e) =
-        make_uint2(pack_bf16x2(a - bf16_to_f32(h0), b - bf16_to_f32(h1)),
-                   pack_bf16x2(c - bf16_to_f32(h2), d - bf16_to_f32(h3)));
+    *reinterpret_cast<uint2*>(out + lo_offset + e) = make_uint2(lo_pair(a, b, h01), lo_pair(c, d, h23));
   }
 }
 

@@ -113,11 +113,6 @@ __device__ __forceinline__ uint32_t soff(int r, int col) {
   return uint32_t(r * RL * 2 + ((c ^ sw) << 4) + (col & 7) * 2);
 }
 
-// the low plane of a pair packed as h = {bf16(a), bf16(b)}: {bf16(a - hi(a)), bf16(b - hi(b))}
-__device__ __forceinline__ uint32_t lo_pair(float a, float b, uint32_t h) {
-  return pack_bf16x2(a - __uint_as_float(h << 16), b - __uint_as_float(h & 0xffff0000u));
-}
-
 // four consecutive values (8-byte aligned offset): one 8-byte store per plane
 __device__ __forceinline__ void split_store4(uint16_t* hi, uint16_t* lo, uint32_t off, float4 v) {
   const uint32_t h01 = pack_bf16x2(v.x, v.y), h23 = pack_bf16x2(v.z, v.w);

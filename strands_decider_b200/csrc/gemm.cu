@@ -159,9 +159,8 @@ __device__ __forceinline__ void lo8_unscale(uint32_t (&v)[32]) {
 
 // hi = bf16_rn(x), lo = bf16_rn(x - hi): the two planes of an fp32 activation.
 __device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
-  const uint16_t ha = f32_to_bf16_rn(a), hb = f32_to_bf16_rn(b);
-  hi = uint32_t(ha) | (uint32_t(hb) << 16);
-  lo = pack_bf16x2(a - bf16_to_f32(ha), b - bf16_to_f32(hb));
+  hi = pack_bf16x2(a, b);
+  lo = lo_pair(a, b, hi);
 }
 
 // SwiGLU: gate chunk g and up chunk u (same 32 intermediate features) -> 32 outputs as
