@@ -28,6 +28,7 @@ namespace cg = cooperative_groups;
 namespace sdb {
 
 constexpr int GC = 32;          // chunk length
+static_assert(GC == 32, "the decay scan of a chunk is one warp scan");
 constexpr int GD = 128;         // key / value head dim
 constexpr int GQKV = 3 * GD;
 constexpr int GPREP = GQKV + 4;   // per (token, head): q | k | v | beta, g, pad
@@ -392,25 +393,28 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
     }
     if (lane < GC / 8 && warp + 8 * lane < L)  // the z gate rows this warp reads in step 8
       bulk_prefetch_l2(a.mix + size_t(tok0 + c0 + warp + 8 * lane) * a.ld_mix + conv_dim + h * GD + col0, DV * 4);
-    // ---- 1. cumulative decay within the chunk
-    if (tid < GC) {
-      float gj = 0.0f, bj = 0.0f;
-      if (tid < L) {
-        bj = sm.stage[tid * GPREP + GQKV];
-        gj = sm.stage[tid * GPREP + GQKV + 1];
+    // ---- 1. cumulative decay within the chunk: every warp scans the chunk's g itself (lane l
+    //         holds G_l), so the planes of step 2 need no barrier after it; warp 0 publishes
+    //         G, beta, e^G and e^{G_{L-1} - G} for the later steps
+    float bl = 0.0f, Gl = 0.0f;
+    {
+      if (lane < L) {
+        bl = sm.stage[lane * GPREP + GQKV];
+        Gl = sm.stage[lane * GPREP + GQKV + 1];
       }
-      float v = gj;  // inclusive warp scan
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float n = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += n;
+      for (int o = 1; o < 32; o <<= 1) {  // inclusive warp scan
+        const float n = __shfl_up_sync(0xffffffffu, Gl, o);
+        if (lane >= o) Gl += n;
       }
-      sm.G[tid] = v;
-      sm.beta[tid] = bj;
-      sm.eG[tid] = __expf(v);
+      if (warp == 0) {
+        const float GL = __shfl_sync(0xffffffffu, Gl, L - 1);
+        sm.G[lane] = Gl;
+        sm.beta[lane] = bl;
+        sm.eG[lane] = __expf(Gl);
+        sm.eL[lane] = lane < L ? __expf(GL - Gl) : 0.0f;
+      }
     }
-    __syncthreads();
-    if (tid < GC) sm.eL[tid] = tid < L ? __expf(sm.G[L - 1] - sm.G[tid]) : 0.0f;
     // ---- 2. q, k, [beta v | beta k e^G] as hi/lo planes (rows past L are zero)
 #pragma unroll
     for (int j = warp; j < GC; j += GDN_THREADS / 32) {
@@ -421,7 +425,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
         k = reinterpret_cast<const float4*>(pr + GD)[lane];
         if (lane < DV / 4) v = reinterpret_cast<const float4*>(pr + 2 * GD + col0)[lane];
       }
-      const float bj = sm.beta[j], bke = bj * sm.eG[j];
+      const float bj = __shfl_sync(0xffffffffu, bl, j), bke = bj * __expf(__shfl_sync(0xffffffffu, Gl, j));
       const int c = lane * 4;
       split_store4(sm.Qh, sm.Ql, soff<GD>(j, c), q);
       split_store4(sm.Kh, sm.Kl, soff<GD>(j, c), k);
@@ -775,7 +779,8 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
         }
       }
     }
-    __syncthreads();
+    // no barrier here: the next chunk's first shared-memory writes (step 1) come after the
+    // barrier at the top of its iteration
   }
 
   if (svalid) {
