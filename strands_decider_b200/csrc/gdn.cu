@@ -955,6 +955,7 @@ static int sdb_gdn_mixer_mode(const b200_gdn_params* p, const b200_seqs* s, cons
     return sdb_fail(B200_ERR_UNSUPPORTED, "b200_gdn_mixer: only dk = dv = 128 and conv width 4 are built");
   if (!p->conv_w || !p->a_log || !p->dt_bias || !p->norm_w) return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: null param");
   if (s->n_seqs <= 0 || !s->cu_seqlens) return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: empty batch");
+  if (s->n_seqs > 65535) return sdb_fail(B200_ERR_SHAPE, "b200_gdn_mixer: at most 65535 sequences per call");
   const bool uses_pool = s->prefix_slot || s->save_slot;
   if (uses_pool && (!pool || !pool->gdn_state || !pool->conv_hist || !pool->slot_len))
     return sdb_fail(B200_ERR_ARG, "b200_gdn_mixer: prefix/save slots need a pool");
