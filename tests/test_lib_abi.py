@@ -78,6 +78,28 @@ def test_linear_shape_checks_on_host(lib):
     assert lib.b200_linear(p16, p16 + 8, 4, 1024, 1024, C.byref(w), C.byref(o), None) == 2  # lo plane unaligned
 
 
+@pytest.mark.parametrize("entry", ["b200_gdn_mixer", "b200_gdn_mixer_chunked", "b200_gdn_mixer_recurrent"])
+def test_gdn_mixer_argument_checks_on_host(lib, entry):
+    """Every GDN entry point refuses bad arguments with a status before touching the device."""
+    from strands_decider_b200 import _lib
+
+    buf = (C.c_uint8 * 256)()
+    p16 = (C.cast(buf, C.c_void_p).value + 15) // 16 * 16
+    f = getattr(lib, entry)
+    params = _lib.GdnParams(2, 128, 128, 4, 1e-6, p16, p16, p16, p16)
+    seqs = _lib.Seqs(1, 4, 4, p16, None, None)
+    ld = 3 * 256 + 256 + 4
+    assert f(None, C.byref(seqs), p16, ld, p16, 0, None, 0, p16, None) == 1            # null params
+    bad = _lib.GdnParams(2, 64, 128, 4, 1e-6, p16, p16, p16, p16)
+    assert f(C.byref(bad), C.byref(seqs), p16, ld, p16, 0, None, 0, p16, None) == 7     # dk 64 is not built
+    many = _lib.Seqs(70000, 70000, 1, p16, None, None)
+    assert f(C.byref(params), C.byref(many), p16, ld, p16, 0, None, 0, p16, None) == 2  # grid limit
+    slotted = _lib.Seqs(1, 4, 4, p16, p16, None)
+    assert f(C.byref(params), C.byref(slotted), p16, ld, p16, 0, None, 0, p16, None) == 1  # slots need a pool
+    assert f(C.byref(params), C.byref(seqs), p16, ld, p16, 0, None, 0, None, None) == 1    # no scratch
+    assert f(C.byref(params), C.byref(seqs), p16, ld - 4, p16, 0, None, 0, p16, None) == 2  # ld_mix too narrow
+
+
 def test_model_context_host_side(lib):
     from strands_decider_b200 import _lib, config
 
