@@ -614,8 +614,9 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
               const float v1 = ok ? sm.ru.uw.U[r][c + 1] - ws[i][half][2 * hr + 1] : 0.0f;
               split_store(sm.Vh, sm.Vl, soff<DV>(r, c), v0, v1);
               if (need_state) split_store(sm.Th, sm.Tl, soff<DV>(r, c), v0 * sm.eL[r], v1 * sm.eL[r]);
-              O[r][c] = qs[i][half][2 * hr] * sm.eG[r];  // overwrites U[r][c], read just above by this thread
-              O[r][c + 1] = qs[i][half][2 * hr + 1] * sm.eG[r];
+              // overwrites U[r][c], U[r][c + 1], read just above by this thread (c even: 8-byte store)
+              *reinterpret_cast<float2*>(&O[r][c]) =
+                  make_float2(qs[i][half][2 * hr] * sm.eG[r], qs[i][half][2 * hr + 1] * sm.eG[r]);
             }
           }
         }
@@ -655,8 +656,9 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
 #pragma unroll
             for (int hr = 0; hr < 2; ++hr) {
               const int r = m0 + g8 + 8 * hr, c = 16 * nb + 8 * half + 2 * t4;
-              O[r][c] += pv[i][half][2 * hr];
-              O[r][c + 1] += pv[i][half][2 * hr + 1];
+              float2* o2 = reinterpret_cast<float2*>(&O[r][c]);
+              const float2 prev = *o2;
+              *o2 = make_float2(prev.x + pv[i][half][2 * hr], prev.y + pv[i][half][2 * hr + 1]);
             }
           }
         }
@@ -725,11 +727,18 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       for (int i = 0; i < GC / 8; ++i) {
         const int j = warp + 8 * i;
         float q = 0.0f;
+        if constexpr (CPL == 4) {  // one 16-byte load (rows of O are 16-byte aligned: UP % 4 == 0)
+          const float4 o4 = *reinterpret_cast<const float4*>(&O[j][lane * 4]);
+          ov[i][0] = o4.x;
+          ov[i][1] = o4.y;
+          ov[i][2] = o4.z;
+          ov[i][3] = o4.w;
+        } else {
 #pragma unroll
-        for (int e = 0; e < CPL; ++e) {
-          ov[i][e] = O[j][lane * CPL + e];
-          q += ov[i][e] * ov[i][e];
+          for (int e = 0; e < CPL; ++e) ov[i][e] = O[j][lane * CPL + e];
         }
+#pragma unroll
+        for (int e = 0; e < CPL; ++e) q += ov[i][e] * ov[i][e];
         ss[i] = warp_sum(q);
         if constexpr (NS > 1) {
           if (lane == 0) sm.part[cpar][j] = ss[i];
