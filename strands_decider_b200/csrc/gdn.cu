@@ -557,8 +557,8 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
             for (int hr = 0; hr < 2; ++hr) {
               const int r = m0 + g8 + 8 * hr, c = 16 * nb + 8 * half + 2 * t4;
               if (c < DV) {
-                sm.ru.uw.U[r][c] = acc[i][half][2 * hr];
-                sm.ru.uw.U[r][c + 1] = acc[i][half][2 * hr + 1];
+                *reinterpret_cast<float2*>(&sm.ru.uw.U[r][c]) =
+                    make_float2(acc[i][half][2 * hr], acc[i][half][2 * hr + 1]);
               } else {
                 split_store(sm.ru.uw.Wh, sm.ru.uw.Wl, soff<GD>(r, c - DV), acc[i][half][2 * hr],
                             acc[i][half][2 * hr + 1]);
@@ -610,8 +610,9 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
             for (int hr = 0; hr < 2; ++hr) {
               const int r = m0 + g8 + 8 * hr, c = 16 * nb + 8 * half + 2 * t4;
               const bool ok = r < L;
-              const float v0 = ok ? sm.ru.uw.U[r][c] - ws[i][half][2 * hr] : 0.0f;
-              const float v1 = ok ? sm.ru.uw.U[r][c + 1] - ws[i][half][2 * hr + 1] : 0.0f;
+              const float2 u2 = *reinterpret_cast<const float2*>(&sm.ru.uw.U[r][c]);  // c even
+              const float v0 = ok ? u2.x - ws[i][half][2 * hr] : 0.0f;
+              const float v1 = ok ? u2.y - ws[i][half][2 * hr + 1] : 0.0f;
               split_store(sm.Vh, sm.Vl, soff<DV>(r, c), v0, v1);
               if (need_state) split_store(sm.Th, sm.Tl, soff<DV>(r, c), v0 * sm.eL[r], v1 * sm.eL[r]);
               // overwrites U[r][c], U[r][c + 1], read just above by this thread (c even: 8-byte store)
