@@ -247,8 +247,9 @@ class DecisionModel:
     def append_states(self, tokens: list[list[int]], slots: list[int], stream=None) -> None:
         """Grow cached states in place: forward tokens[i] as the continuation of slot slots[i]
         and save the continued GDN state, conv history and keys / values back into that slot
-        (one token at a time is the decode-time update). The slot must have been prefilled
-        with enough `reserve` for the grown length."""
+        (one token at a time is the decode-time update: a batch of single tokens runs the GDN
+        layers through the token-by-token recurrent kernel, longer ones through the chunk
+        kernel). The slot must have been prefilled with enough `reserve` for the grown length."""
         room = getattr(self, "_slot_room", None)
         if room is None:
             raise ValueError("append_states needs slots laid out by prefill_states")
