@@ -503,15 +503,15 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_mixer_kernel(const GdnArgs
       float mval = 0.0f;
 #pragma unroll
       for (int j = 0; j < 16; ++j) mval = fmaf(sm.A[16 + i][j], sm.A[j][c], mval);
-      float* scratch = reinterpret_cast<float*>(sm.Vh);  // Vh (>= 2 KB) is first written in step 6
-      __syncthreads();
+      // Vh (>= 2 KB) is first written in step 6; its last reads (the previous chunk's step 7a)
+      // are several barriers back
+      float* scratch = reinterpret_cast<float*>(sm.Vh);
       scratch[i * 16 + c] = mval;
       __syncthreads();
       float t = 0.0f;
 #pragma unroll
       for (int j = 0; j < 16; ++j) t = fmaf(sm.A[16 + i][16 + j], scratch[j * 16 + c], t);
-      __syncthreads();
-      sm.A[16 + i][c] = -t;
+      sm.A[16 + i][c] = -t;  // A10 was last read above, before the barrier
     }
     __syncthreads();
     for (int i = tid; i < GC * GC / 2; i += GDN_THREADS) {
