@@ -16,7 +16,10 @@ What runs is the reference's own code, unmodified:
   * transformers' `torch_chunk_gated_delta_rule` with an initial state (`TF:234-311`);
   * the trained readouts `SlotHead` / `PointerHead` with `gather_options`
     (`modeling.py:99-190`) on the tiny torso's hidden states (`--readouts-only` regenerates
-    just that fixture).
+    just that fixture);
+  * transformers' token-by-token `torch_recurrent_gated_delta_rule` (`TF:314-353`) on the
+    chunk-rule inputs, the form single-token appends take (`--recurrent-only` regenerates just
+    that fixture).
 
 The fixtures are small .npz files committed beside this script; the tests read only
 them (the reference is not present where the GPU tests run).
@@ -163,10 +166,29 @@ def make_readouts() -> None:
     print("readouts", {k: v.shape for k, v in out.items()})
 
 
+def make_recurrent_rule() -> None:
+    """transformers' recurrent rule (TF:314-353) on the chunk-rule inputs, with an initial state."""
+    import transformers.models.qwen3_5.modeling_qwen3_5 as q35
+
+    out = {}
+    for seq in CHUNK_SEQS:
+        x, state = chunk_rule_inputs(seq)
+        o, s = q35.torch_recurrent_gated_delta_rule(**{k: v[None] for k, v in x.items()},
+                                                    initial_state=state[None], output_final_state=True,
+                                                    use_qk_l2norm_in_kernel=True)
+        out[f"s{seq}_out"] = o[0].numpy()
+        out[f"s{seq}_state"] = s[0].numpy()
+    np.savez_compressed(os.path.join(HERE, "recurrent_rule.npz"), **out)
+    print("recurrent rule", sorted(out))
+
+
 def main(reference_root: str) -> None:
     sys.path.insert(0, os.path.join(reference_root, "src"))
     if "--readouts-only" in sys.argv:
         make_readouts()
+        return
+    if "--recurrent-only" in sys.argv:
+        make_recurrent_rule()
         return
     import transformers.models.qwen3_5.modeling_qwen3_5 as q35
     from strands_decider.schema import derive_confidence, derive_score_confidence
@@ -232,6 +254,7 @@ def main(reference_root: str) -> None:
         out[f"s{seq}_out"] = o[0].numpy()
         out[f"s{seq}_state"] = s[0].numpy()
     np.savez_compressed(os.path.join(HERE, "chunk_rule.npz"), **out)
+    make_recurrent_rule()
 
     # 4. answer formulas
     dists = [[1 / 3, 1 / 3, 1 / 3], [1.0, 0.0, 0.0], [0.88, 0.12, 0.0], [0.7, 0.2, 0.1],

@@ -38,6 +38,17 @@ def test_chunk_rule_matches_reference_with_initial_state(seq):
     torch.testing.assert_close(s, torch.from_numpy(g[f"s{seq}_state"]), rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("seq", CHUNK_SEQS)
+def test_recurrent_rule_matches_reference_with_initial_state(seq):
+    """The restated token-by-token rule against transformers' own (TF:314-353), the form of
+    single-token appends: correlated keys, non-zero initial state."""
+    g = _load("recurrent_rule.npz")
+    x, state = chunk_rule_inputs(seq)
+    o, s = T.recurrent_gated_delta_rule(x["query"], x["key"], x["value"], x["g"], x["beta"], state)
+    torch.testing.assert_close(o, torch.from_numpy(g[f"s{seq}_out"]), rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(s, torch.from_numpy(g[f"s{seq}_state"]), rtol=1e-4, atol=1e-4)
+
+
 @pytest.mark.parametrize("seq", [1, 64, 130])
 def test_chunk_rule_equals_token_recurrence(seq):
     x, state = chunk_rule_inputs(seq)
