@@ -400,11 +400,12 @@ static int launch_attn(const AttnArgs& a, int n_tokens, int n_seqs, int max_len,
   const int warps = a.p.heads + 2 * a.p.kv_heads;
   SDB_CUDA(launch_pdl(attn_prep_kernel<HD>, dim3(n_tokens), dim3(32 * warps), 0, st, a));
   constexpr int smem = FA_Q * HD * 2 + 4 * FA_K * HD * 2;
-  static bool attr = false;
-  if (!attr) {
+  static DeviceOnce attr;  // per head_dim and device
+  const int r = once_per_device(attr, [](int) -> int {
     SDB_CUDA(cudaFuncSetAttribute(attn_flash_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+    return B200_OK;
+  });
+  if (r != B200_OK) return r;
   dim3 grid((max_len + FA_Q - 1) / FA_Q, n_seqs, a.p.heads);
   SDB_CUDA(launch_pdl(attn_flash_kernel<HD>, grid, dim3(128 * fa_dg<HD>()), smem, st, a));
   return B200_OK;
@@ -479,9 +480,8 @@ constexpr size_t kAttnNoAllocBytes = size_t(8) << 20;  // 8 MiB per device
 static __device__ __align__(256) uint16_t g_attn_noalloc_scratch[kAttnNoAllocBytes / 2];
 
 namespace {
-constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
-uint16_t* g_noalloc_ptr[kMaxDevices] = {};
+uint16_t* g_noalloc_ptr[sdb::kMaxDevices] = {};
 }  // namespace
 
 extern "C" int b200_attention_noalloc(const b200_attn_params* p, const b200_seqs* seqs, const float* qkv,
@@ -513,6 +513,8 @@ extern "C" int b200_attention_noalloc(const b200_attn_params* p, const b200_seqs
   uint16_t* q_buf = base;
   uint16_t* k_buf = q_buf + T * p->heads * p->head_dim;
   uint16_t* v_buf = k_buf + T * p->kv_heads * p->head_dim;
-  return sdb_attention(p, seqs, qkv, ld_qkv, q_buf, k_buf, v_buf, out, lo_offset, pool, attn_layer, 0,
-                       reinterpret_cast<cudaStream_t>(stream));
+  const int r = sdb_attention(p, seqs, qkv, ld_qkv, q_buf, k_buf, v_buf, out, lo_offset, pool, attn_layer, 0,
+                              reinterpret_cast<cudaStream_t>(stream));
+  if (r != B200_OK) sdb_rename_error("b200_attention:", "b200_attention_noalloc:");  // the caller's entry point
+  return r;
 }

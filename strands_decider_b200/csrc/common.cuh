@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <utility>
 
 #include "strands_b200.h"
@@ -429,3 +430,36 @@ inline cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t
 
 void sdb_set_last_error(const char* msg);
 int sdb_fail(int status, const char* msg);
+// Rewrites the calling thread's last error message when it starts with `from` so that it
+// starts with `to` instead (an entry point that wraps another reports under its own name).
+void sdb_rename_error(const char* from, const char* to);
+
+namespace sdb {
+// Device ids this library keeps per-device state for.
+constexpr int kMaxDevices = 64;
+
+// Kernel attributes (such as the dynamic shared-memory limit) are per device, and one process
+// may drive several GPUs from several host threads. A DeviceOnce runs a set-up step once per
+// device, under its lock, with that device current; the step returns a B200 status and is
+// retried on the next call if it failed.
+struct DeviceOnce {
+  std::mutex mu;
+  uint64_t done = 0;
+};
+
+template <typename F>
+inline int once_per_device(DeviceOnce& once, F&& setup) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return sdb_fail(B200_ERR_CUDA, "cannot determine the current CUDA device (or its id is >= 64)");
+  std::lock_guard<std::mutex> lk(once.mu);
+  if ((once.done >> dev) & 1) return B200_OK;
+  const int r = setup(dev);
+  if (r == B200_OK) once.done |= uint64_t(1) << dev;
+  return r;
+}
+
+// Streaming multiprocessors of the current device (looked up once per device; 148 when the
+// runtime cannot say).
+int sm_count();
+}  // namespace sdb

@@ -992,14 +992,15 @@ static int sdb_gdn_mixer_mode(const b200_gdn_params* p, const b200_seqs* s, cons
   a.slot_len = uses_pool ? pool->slot_len : nullptr;
   a.state_pool = uses_pool ? pool->gdn_state + size_t(layer) * pool->n_slots * p->heads * GD * GD : nullptr;
   a.conv_pool = uses_pool ? pool->conv_hist + size_t(layer) * pool->n_slots * 3 * conv_dim : nullptr;
-  static bool attr = false;
-  if (!attr) {
+  static DeviceOnce attr;
+  const int attr_status = once_per_device(attr, [](int) -> int {
     SDB_CUDA(cudaFuncSetAttribute(gdn_mixer_kernel<GD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   int(sizeof(GdnSmem<GD>))));
     SDB_CUDA(cudaFuncSetAttribute(gdn_mixer_kernel<GDN_DV_SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   int(sizeof(GdnSmem<GDN_DV_SPLIT>))));
-    attr = true;
-  }
+    return B200_OK;
+  });
+  if (attr_status != B200_OK) return attr_status;
   a.n_tokens = s->n_tokens;
   const bool recurrent = mode == GDN_RECURRENT || (mode == GDN_AUTO && s->n_tokens <= s->n_seqs);
   if (recurrent && ((reinterpret_cast<uintptr_t>(p->norm_w) & 15) || (reinterpret_cast<uintptr_t>(prep) & 15) ||

@@ -833,29 +833,18 @@ static int check_tiles(const b200_qweight* w) {
   return B200_OK;
 }
 
-static int sm_count() {  // one process drives one device
-  static int n_sm = 0;
-  if (!n_sm) {
-    int dev = 0, v = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
-      n_sm = v;
-    else
-      n_sm = 148;
-  }
-  return n_sm;
-}
-
 template <int BN, int FMT, int EP, int PL>
 static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_lo, const CUtensorMap& map_b,
                      const CUtensorMap& map_b8, const GemmArgs& a, cudaStream_t st) {
   constexpr int smem = GemmSmem<BN, FMT, PL>::TOTAL;
   static_assert(smem <= 227 * 1024, "GEMM shared memory exceeds the 227 KB per-CTA limit");
-  static bool attr_set = false;  // per instantiation; one process drives one device
-  if (!attr_set) {
+  static DeviceOnce attr;  // per instantiation and device
+  const int r = once_per_device(attr, [](int) -> int {
     SDB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, FMT, EP, PL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   smem));
-    attr_set = true;
-  }
+    return B200_OK;
+  });
+  if (r != B200_OK) return r;
   const int n_sm = sm_count();
   GemmArgs args = a;
   const int tiles = (a.w.n / BN) * ((a.m + GEMM_BM - 1) / GEMM_BM);
@@ -906,8 +895,9 @@ static int launch_pair(const CUtensorMap& map, const CUtensorMap& map_lo, const 
                        const CUtensorMap& map_b8, const GemmArgs& a, cudaStream_t st) {
   constexpr int smem = Gemm2Smem<PL>::TOTAL;
   static_assert(smem <= 227 * 1024, "GEMM shared memory exceeds the 227 KB per-CTA limit");
-  static int max_pairs = 0;  // per instantiation; one process drives one device
-  if (!max_pairs) {
+  static DeviceOnce attr;                       // per instantiation and device
+  static int max_pairs_dev[kMaxDevices] = {};   // written under attr's lock, once per device
+  const int r = once_per_device(attr, [](int dev) -> int {
     SDB_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<EP, PL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sm_count() & ~1);
@@ -918,8 +908,13 @@ static int launch_pair(const CUtensorMap& map, const CUtensorMap& map_lo, const 
       (void)cudaGetLastError();
       n = sm_count() / 2;
     }
-    max_pairs = n;
-  }
+    max_pairs_dev[dev] = n;
+    return B200_OK;
+  });
+  if (r != B200_OK) return r;
+  int dev = 0;
+  SDB_CUDA(cudaGetDevice(&dev));
+  const int max_pairs = max_pairs_dev[dev];
   GemmArgs args = a;
   args.ksplit = 1;
   // Weight bytes of all column tiles beyond what L2 keeps alongside the activation stream

@@ -13,10 +13,27 @@ int sdb_fail(int status, const char* msg) {
   sdb_set_last_error(msg);
   return status;
 }
+void sdb_rename_error(const char* from, const char* to) {
+  const size_t n = std::char_traits<char>::length(from);
+  if (g_last_error.compare(0, n, from) == 0) g_last_error = std::string(to) + g_last_error.substr(n);
+}
 
 namespace sdb {
 __device__ unsigned int g_fault = 0;
+
+int sm_count() {
+  static std::mutex mu;
+  static int n_sm[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!n_sm[dev]) {
+    int v = 0;
+    n_sm[dev] = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0 ? v : 148;
+  }
+  return n_sm[dev];
 }
+}  // namespace sdb
 
 // kernels' internal entry points (other translation units)
 int sdb_embed_vocab(const int32_t* ids, int32_t n_tokens, const uint16_t* table, int32_t hidden, float* x, int vocab,
