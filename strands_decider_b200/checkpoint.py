@@ -21,7 +21,8 @@ import glob
 import json
 import os
 import re
-from dataclasses import fields
+from dataclasses import dataclass, field, fields
+from typing import Any
 
 import torch
 
@@ -69,14 +70,24 @@ def torso_state(sd: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
 def merge_lora(sd: dict[str, torch.Tensor], adapter_dir: str) -> dict[str, torch.Tensor]:
     """W + scaling * (B @ A) for every adapted linear (peft's merge_and_unload for LoRA):
     scaling = lora_alpha / r, or lora_alpha / sqrt(r) with use_rslora. Returns a new dict with
-    fp32 merged weights; raises if an adapted weight is missing from the base."""
+    fp32 merged weights. Only plain linear LoRA is merged: options that change the arithmetic
+    without adding tensors (fan_in_fan_out, per-module rank or alpha patterns, DoRA) and any
+    adapter tensor other than lora_A / lora_B weight pairs (DoRA magnitudes, LoRA biases,
+    embedding LoRA, saved modules) are refused, as the reference's MLX merge refuses them
+    (mlx_engine.py:74-118); so is an adapted weight missing from the base."""
     cfg = json.load(open(os.path.join(adapter_dir, "adapter_config.json"), encoding="utf-8"))
     r, alpha = int(cfg["r"]), float(cfg["lora_alpha"])
-    if cfg.get("fan_in_fan_out"):
-        raise ValueError("fan_in_fan_out adapters are not supported")
+    unsupported = [k for k in ("fan_in_fan_out", "rank_pattern", "alpha_pattern", "use_dora") if cfg.get(k)]
+    if unsupported:
+        raise ValueError(f"{adapter_dir}: cannot merge an adapter with {unsupported}")
     scaling = alpha / (r ** 0.5 if cfg.get("use_rslora") else r)
-    ad = torso_state({re.sub(r"\.lora_([AB])(\.default)?\.weight$", r".lora_\1.weight", k): v
-                      for k, v in read_tensors(adapter_dir).items()})
+    raw = {re.sub(r"\.lora_([AB])(\.default)?\.weight$", r".lora_\1.weight", k): v
+           for k, v in read_tensors(adapter_dir).items()}
+    other = sorted(k for k in raw if not k.endswith((".lora_A.weight", ".lora_B.weight")))
+    if other:
+        raise ValueError(f"{adapter_dir}: only lora_A / lora_B weight pairs merge; cannot merge "
+                         f"{other[:3]}{' ...' if len(other) > 3 else ''}")
+    ad = torso_state(raw)
     out = dict(sd)
     for ka in [k for k in ad if k.endswith(".lora_A.weight")]:
         base = ka[: -len(".lora_A.weight")]
@@ -91,18 +102,32 @@ def merge_lora(sd: dict[str, torch.Tensor], adapter_dir: str) -> dict[str, torch
     return out
 
 
-def decider_config(checkpoint_dir: str):
-    """The checkpoint's config as engine.DeciderConfig (fields it does not know are kept in
-    `.extra`)."""
-    from .engine import DeciderConfig
+@dataclass
+class CheckpointConfig:
+    """The fields of a checkpoint's decider config file (strands_decider_config.json, the
+    format of modeling.py:43-97) that the loader reads; every other field is kept in `extra`."""
 
+    base_model: str = ""
+    head_type: str = "slot"
+    num_slots: int = 24
+    pointer_dim: int = 256
+    head_hidden: int = 0
+    max_length: int = 3072
+    temperature: float = 1.0
+    temperature_by_kind: dict[str, float] = field(default_factory=dict)
+    ordinal_smoothing: float = 0.0
+    extra: dict[str, Any] = field(default_factory=dict)
+
+
+def decider_config(checkpoint_dir: str) -> CheckpointConfig:
+    """The checkpoint's config file, read into a CheckpointConfig."""
     path = next((os.path.join(checkpoint_dir, n) for n in CONFIG_NAMES
                  if os.path.exists(os.path.join(checkpoint_dir, n))), None)
     if path is None:
         raise FileNotFoundError(f"{checkpoint_dir}: no {' or '.join(CONFIG_NAMES)}")
     raw = json.load(open(path, encoding="utf-8"))
-    known = {f.name for f in fields(DeciderConfig)} - {"extra"}
-    return DeciderConfig(**{k: v for k, v in raw.items() if k in known},
+    known = {f.name for f in fields(CheckpointConfig)} - {"extra"}
+    return CheckpointConfig(**{k: v for k, v in raw.items() if k in known},
                          extra={k: v for k, v in raw.items() if k not in known})
 
 
@@ -120,7 +145,7 @@ def head_state(checkpoint_dir: str) -> dict[str, torch.Tensor]:
 
 def load_decider(checkpoint_dir: str, base, weight_format: str = "nvfp4", device: str = "cuda",
                  hf_config=None):
-    """(DeviceWeights, DeviceReadout or None, DeciderConfig, ModelSpec) for a checkpoint.
+    """(DeviceWeights, DeviceReadout or None, CheckpointConfig, ModelSpec) for a checkpoint.
 
     base: the base model's weights, a directory of safetensors shards (with its config.json)
     or a state dict; hf_config: its transformers text config when `base` is a state dict.

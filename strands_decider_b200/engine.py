@@ -4,26 +4,27 @@ strands-decider's device plugins override exactly two methods of `SystemOneEngin
 (src/strands_decider/infer.py:127-411): `_slot_probs_batched` (infer.py:253-279) and
 `_slot_probs_shared_prefix` (infer.py:281-337); `MLXEngine` is the precedent
 (src/strands_decider/mlx_engine.py:121-205). `B200SlotProbs` is that pair, running the
-torso prefill, the prefix-state cache and the option-token readout on the GPU through the
-native runtime (runtime.DecisionModel -> libstrands_b200.so). It works on top of:
+torso prefill, the prefix-state cache and the decision head on the GPU through the native
+runtime (runtime.DecisionModel -> libstrands_b200.so).
 
-  * the reference's own engine, when strands_decider is installed:
-    `reference_engine_class()` returns `class B200Engine(B200SlotProbs, SystemOneEngine)`,
-    so rendering, tokenisation, `_fit`, batching, temperatures and the answer read-back
-    are the reference's own code (the MLX pattern);
-  * `B200Engine`, a standalone mirror of the engine's host logic (`_fit`,
-    `_temperatures`, `_option_token_ids`, `evaluate`) for machines without the reference.
+Everything else is the reference's own code, inherited: `reference_engine_class()` returns
+`class B200Engine(B200SlotProbs, SystemOneEngine)`, so `evaluate` (rendering, the
+`num_slots` refusal, chunking by `max_batch`, the `UnforkableCache` fallback, the answer
+read-back), `_fit`, `_temperatures`, `_option_idx` and `_pad` are strands-decider's. The
+engine therefore needs the `strands_decider` package importable; `load_engine` builds one
+from a checkpoint directory, as `strands_decider.infer.load_engine` does for the torch
+devices (infer.py:476-496).
 
 Contract of both methods (infer.py:253-337): return (probs [n, K] float32 on the CPU with
 entries past each row's n_slots equal to 0, input-token count). The readout is the
-frozen torso's option-number distribution (`frozen_slot_log_probs`, modeling.py:412-438):
-slot k is the tied-embedding row of the token "k+1".
+checkpoint's trained head ("slot" / "pointer", modeling.py:99-180) or, with head_type
+"option_token", the frozen torso's option-number distribution (`frozen_slot_log_probs`,
+modeling.py:412-438): slot k is the tied-embedding row of the token "k+1".
 """
 
 from __future__ import annotations
 
 import threading
-from dataclasses import dataclass, field
 from typing import Any
 
 import torch
@@ -31,39 +32,15 @@ import torch
 from .runtime import KIND, DecisionModel
 
 
-@dataclass
-class EngineConfig:
-    """Mirror of infer.EngineConfig (infer.py:55-66) with device "b200"."""
+class Readout:
+    """What the engine reads from StrandsDeciderModel besides the torso (as mlx_engine's
+    _Readout): the decider config (strands_decider.modeling.StrandsDeciderConfig), the
+    tokenizer, and the trained head module if any (the device head is built from it)."""
 
-    device: str = "b200"
-    use_prefix_cache: bool = True
-    max_batch: int = 32
-    model_name: str = "strands-decider-0.1.0"
-    max_question_fraction: float = 0.75
-    strict_window: bool = False
-
-
-@dataclass
-class DeciderConfig:
-    """The fields of StrandsDeciderConfig (modeling.py:43-97) the engine reads."""
-
-    max_length: int = 3072
-    num_slots: int = 24
-    head_type: str = "option_token"
-    temperature: float = 1.0
-    temperature_by_kind: dict[str, float] = field(default_factory=dict)
-    ordinal_smoothing: float = 0.0
-    pointer_dim: int = 256
-    head_hidden: int = 0
-    extra: dict[str, Any] = field(default_factory=dict)   # the checkpoint config's other fields
-
-
-class _Readout:
-    """What the engine reads from StrandsDeciderModel besides the torso (as mlx_engine._Readout)."""
-
-    def __init__(self, config: Any, tokenizer: Any):
+    def __init__(self, config: Any, tokenizer: Any, head: Any = None):
         self.config = config
         self.tokenizer = tokenizer
+        self.head = head
 
 
 def option_token_ids(tokenizer: Any, num_slots: int) -> list[int]:
@@ -258,122 +235,73 @@ class RequestBatcher:
                 b[2].set_result(r)
 
 
-class B200Engine(B200SlotProbs):
-    """Standalone engine: the host logic of SystemOneEngine restated (for machines where the
-    reference is not installed), with the device overrides. One evaluation at a time."""
-
-    def __init__(self, runtime: DecisionModel, tokenizer: Any, decider_config: Any = None,
-                 config: EngineConfig | None = None):
-        self.cfg = config or EngineConfig()
-        self.model = _Readout(decider_config or DeciderConfig(), tokenizer)
-        self.tok = tokenizer
-        self.device = "cpu"  # where the small index/temperature tensors live, as in MLXEngine
-        self._rt = runtime
-        self._lock = threading.Lock()
-        self._last_offsets: list = []
-
-    def _temperatures(self, kinds: list[str]) -> torch.Tensor:
-        """infer.py:163-171."""
-        cfg = self.model.config
-        by_kind = getattr(cfg, "temperature_by_kind", None) or {}
-        return torch.tensor([float(by_kind.get(k, cfg.temperature)) for k in kinds], dtype=torch.float32)
-
-    def _fit(self, state_text: str, question_texts: list[str]) -> tuple[list[int], list[list[int]]]:
-        """infer.py:174-219: the question gets first claim on the window and is cut from the front."""
-        max_len = self.model.config.max_length
-        enc = self.tok(question_texts, add_special_tokens=False, return_offsets_mapping=True)
-        q = enc["input_ids"]
-        offs = enc["offset_mapping"]
-        longest = max(len(x) for x in q)
-        if self.cfg.strict_window:
-            s = self.tok(state_text, add_special_tokens=True)["input_ids"]
-            if len(s) + longest > max_len:
-                raise ValueError(f"prompt of {len(s) + longest} tokens exceeds the context window of "
-                                 f"{max_len} tokens")
-            self._last_offsets = list(offs)
-            return s, q
-        reserve = min(longest, max(1, int(max_len * self.cfg.max_question_fraction)))
-        cut = [max(0, len(x) - reserve) for x in q]
-        self._last_offsets = [o[c:] for o, c in zip(offs, cut, strict=True)]
-        q = [x[c:] for x, c in zip(q, cut, strict=True)]
-        s = self.tok(state_text, add_special_tokens=True, truncation=True,
-                     max_length=max(1, max_len - reserve))["input_ids"]
-        return s, q
-
-    def _option_idx(self, rendered: list, base: int) -> torch.Tensor:
-        """infer.py:221-237 / 414-441: the last token of each option's line, from the offsets
-        `_fit` kept (front truncation included), offset by `base`; -1 pads."""
-        rows = []
-        for rq, offs in zip(rendered, self._last_offsets, strict=True):
-            out = []
-            for s0, e0 in rq.option_spans:
-                last = -1
-                for j, (lo, hi) in enumerate(offs):
-                    if hi > lo and lo >= s0 and hi <= e0:
-                        last = j
-                if last < 0:
-                    raise ValueError(f"option span ({s0},{e0}) has no tokens left; the prompt was truncated "
-                                     "through its option list")
-                out.append(last)
-            rows.append(out)
-        width = max(len(r) for r in rows)
-        return torch.tensor([[base + i for i in r] + [-1] * (width - len(r)) for r in rows], dtype=torch.long)
-
-    def evaluate(self, request: Any) -> Any:
-        """infer.py:341-408 (needs strands_decider's prompting and schema modules)."""
-        with self._lock:
-            try:
-                from strands_decider.infer import _to_answer
-                from strands_decider.prompting import render_question, render_state
-                from strands_decider.schema import SystemOneResponse, Usage
-            except ImportError as e:  # pragma: no cover - depends on the host install
-                raise RuntimeError("evaluate() needs the strands-decider package for prompt rendering and "
-                                   "answer types; the token-level API (_slot_probs_*) does not") from e
-            if getattr(request, "images", None):
-                raise ValueError("this engine has no vision tower; serve with --vision for images")
-            names = list(request.questions.keys())
-            rendered = [render_question(request.questions[n]) for n in names]
-            state_text = render_state(request.state)
-            answers, total = {}, 0
-            for start in range(0, len(names), self.cfg.max_batch):
-                chunk = slice(start, start + self.cfg.max_batch)
-                rq = rendered[chunk]
-                slots = [r.n_slots for r in rq]
-                kinds = [r.kind for r in rq]
-                texts = [r.text for r in rq]
-                if self.cfg.use_prefix_cache and len(rq) > 1:
-                    probs, ntok = self._slot_probs_shared_prefix(state_text, texts, slots, kinds, rendered=rq)
-                else:
-                    probs, ntok = self._slot_probs_batched(state_text, texts, slots, kinds, rendered=rq)
-                total += ntok
-                for i, name in enumerate(names[chunk]):
-                    answers[name] = _to_answer(rq[i], probs[i, : rq[i].n_slots].tolist(),
-                                               ordinal_smoothing=self.model.config.ordinal_smoothing)
-            return SystemOneResponse(model=self.cfg.model_name, answers=answers,
-                                     usage=Usage(input_tokens=total, output_tokens=len(names)))
+_ENGINE_CLASS = None
 
 
 def reference_engine_class():
-    """`class B200Engine(B200SlotProbs, strands_decider.infer.SystemOneEngine)`, built on
-    the installed reference (raises ImportError when it is not installed)."""
+    """`class B200Engine(B200SlotProbs, strands_decider.infer.SystemOneEngine)`, built once
+    on the installed reference (raises ImportError when `strands_decider` is not importable).
+
+    `B200Engine(runtime, readout, config)`: runtime a DecisionModel, readout a `Readout`
+    (config, tokenizer), config the reference's `EngineConfig` (its `device` is "b200")."""
+    global _ENGINE_CLASS
+    if _ENGINE_CLASS is not None:
+        return _ENGINE_CLASS
     from strands_decider.infer import SystemOneEngine
 
-    class ReferenceB200Engine(B200SlotProbs, SystemOneEngine):
+    class B200Engine(B200SlotProbs, SystemOneEngine):
         def __init__(self, runtime: DecisionModel, readout: Any, config: Any):
             # Not SystemOneEngine.__init__: that moves a torch torso to a torch device
-            # (mlx_engine.py:124-137 does the same).
+            # (mlx_engine.py:124-137 does the same). These are the attributes the inherited
+            # helpers read; `device` is where their small index and temperature tensors live.
             self.cfg = config
             self.model = readout
             self.tok = readout.tokenizer
             self.device = "cpu"
             self._rt = runtime
+            # one evaluation at a time: `_fit` leaves the request's option offsets on the
+            # engine for `_option_idx` (mlx_engine.py:134-141)
             self._lock = threading.Lock()
 
         def evaluate(self, request):
             with self._lock:
                 return super().evaluate(request)
 
-    return ReferenceB200Engine
+    _ENGINE_CLASS = B200Engine
+    return B200Engine
+
+
+def load_engine(checkpoint: str, *, device: str = "b200", use_prefix_cache: bool = True, base: Any = None,
+                weight_format: str = "nvfp4", max_tokens: int = 16384, pool_slots: int = 64,
+                pool_kv_tokens: int | None = None, lo_plane: str = "e4m3"):
+    """The `--device b200` branch of strands_decider.infer.load_engine (infer.py:476-496):
+    an engine for a checkpoint directory, with the torso quantised into `weight_format` on the
+    GPU. `base` is the base model (a directory of safetensors shards with its config.json, or
+    a state dict); None reads the checkpoint config's `base_model`, which must then be a local
+    directory (nothing is downloaded). Refuses before loading anything when no B200 is usable.
+    The decider config and the tokenizer are read by the reference's own code
+    (StrandsDeciderConfig.from_json, AutoTokenizer with its pad fallback, modeling.py:556-567)."""
+    if device != "b200":
+        raise ValueError(f"this loader serves device 'b200', not {device!r}")
+    require_b200()
+    from strands_decider.infer import EngineConfig
+    from strands_decider.modeling import StrandsDeciderConfig, config_path
+    from transformers import AutoTokenizer
+
+    from . import checkpoint as ck
+
+    cfg = StrandsDeciderConfig.from_json(config_path(checkpoint))
+    tok = AutoTokenizer.from_pretrained(checkpoint)
+    if tok.pad_token is None:
+        tok.pad_token = tok.eos_token
+    weights, readout, _, _ = ck.load_decider(checkpoint, base if base is not None else cfg.base_model,
+                                             weight_format=weight_format)
+    rt = DecisionModel(weights, max_tokens=max_tokens, pool_slots=pool_slots, pool_kv_tokens=pool_kv_tokens,
+                       lo_plane=lo_plane)
+    if readout is not None:
+        rt.set_readout(readout)          # the runtime keeps the readout (and its weights) alive
+    return reference_engine_class()(rt, Readout(cfg, tok), EngineConfig(device="b200",
+                                                                        use_prefix_cache=use_prefix_cache))
 
 
 def b200_available() -> bool:
@@ -397,5 +325,3 @@ def require_b200() -> None:
         raise RuntimeError("device 'b200' needs an NVIDIA B200 (sm_100a) and the built library: "
                            "python -m strands_decider_b200.build")
 
-
-KINDS = KIND

@@ -124,3 +124,25 @@ def test_load_decider_quantises_the_merged_checkpoint(tmp_path):
             for (na, ta), (nb, tb) in zip(la[key].parts(), lb[key].parts(), strict=True):
                 assert na == nb and torch.equal(ta, tb), key
     assert readout is not None and readout.kind == "slot" and readout.out == 24 and cfg.head_type == "slot"
+
+
+@pytest.mark.parametrize("bad", ["rank_pattern", "alpha_pattern", "use_dora", "fan_in_fan_out", "magnitude"])
+def test_lora_merge_refuses_what_it_cannot_merge(tmp_path, bad):
+    """Adapter options that change the arithmetic without adding tensors, and adapter tensors
+    other than lora_A / lora_B pairs (here a DoRA magnitude vector), are refused."""
+    from safetensors.torch import load_file, save_file
+
+    spec = config.TINY
+    sd = ck.torso_state(_base_state(spec))
+    path = tmp_path / "lora"
+    _write_adapter(str(path), spec)
+    cfg = json.load(open(path / "adapter_config.json"))
+    if bad == "magnitude":
+        ad = load_file(str(path / "adapter_model.safetensors"))
+        ad["base_model.model.layers.0.mlp.gate_proj.lora_magnitude_vector"] = torch.ones(spec.inter)
+        save_file(ad, str(path / "adapter_model.safetensors"))
+    else:
+        cfg[bad] = {"gate_proj": 8} if bad.endswith("pattern") else True
+        json.dump(cfg, open(path / "adapter_config.json", "w"))
+    with pytest.raises(ValueError, match="cannot merge"):
+        ck.merge_lora(sd, str(path))

@@ -1,10 +1,13 @@
 """The `--device b200` engine's two overrides and the checkpoint-style weight loader, on the GPU.
 
 * `_slot_probs_batched` (infer.py:253-279) and `_slot_probs_shared_prefix` (infer.py:281-337)
-  through `B200Engine` with a word-level tokenizer (the fixture pattern of the reference's
+  through the engine built on the reference's own `SystemOneEngine` (reference_engine_class),
+  with a word-level tokenizer (the fixture pattern of the reference's
   tests/test_mlx_engine.py:56-67): both paths agree with each other, return the reference's
   contract (probs [n, K] float32 with zeros past n_slots, the input-token count) and match
-  the oracle's full-prompt probabilities within 2e-3.
+  the oracle's full-prompt probabilities within 2e-3. `_fit`, `_temperatures` and
+  `_option_idx` are the reference's, inherited. These tests need the reference package
+  importable (tests/conftest.py says where it is looked for) and skip without it.
 * `DeviceWeights.from_state_dict` on a transformers-named state dict packs the same bytes
   as the synthetic loader from the same latents.
 """
@@ -39,8 +42,13 @@ def _text(g: torch.Generator, n: int) -> str:
 
 
 def _engine(max_length=256, slots=2):
+    from tests.conftest import require_reference
+
+    infer = require_reference()
+    from strands_decider.modeling import StrandsDeciderConfig
+
     from strands_decider_b200 import config
-    from strands_decider_b200.engine import B200Engine, DeciderConfig, EngineConfig
+    from strands_decider_b200.engine import Readout, reference_engine_class
     from strands_decider_b200.runtime import DecisionModel
     from strands_decider_b200.weights import DeviceWeights
 
@@ -48,8 +56,9 @@ def _engine(max_length=256, slots=2):
     w = DeviceWeights.synthetic(spec, seed=3, latent_device="cpu")
     rt = DecisionModel(w, max_tokens=2048, pool_slots=slots, pool_kv_tokens=1024)
     tok = _tokenizer()
-    eng = B200Engine(rt, tok, DeciderConfig(max_length=max_length, temperature_by_kind={"score": 1.5}),
-                     EngineConfig(max_batch=8))
+    dc = StrandsDeciderConfig(max_length=max_length, head_type="option_token", use_lora=False,
+                              temperature_by_kind={"score": 1.5})
+    eng = reference_engine_class()(rt, Readout(dc, tok), infer.EngineConfig(device="b200", max_batch=8))
     return spec, eng, tok
 
 
