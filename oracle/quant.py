@@ -222,13 +222,30 @@ def nvfp4_block_scale(sb: np.ndarray, gs) -> np.ndarray:
     return bf16_round((e4m3_decode(sb) * np.float32(gs)).astype(np.float32))
 
 
-def dequantize_nvfp4(packed: np.ndarray, sb: np.ndarray, gs: float) -> np.ndarray:
+def dequantize_nvfp4_elementwise(packed: np.ndarray, sb: np.ndarray, gs: float) -> np.ndarray:
+    """bf16_rn(e2m1_value(code) * scale[n, b]) element by element (the definition)."""
     codes = unpack_nvfp4(packed)
     n, k = codes.shape
     vals = e2m1_decode(codes).reshape(n, k // NVFP4_BLOCK, NVFP4_BLOCK)
     scale = nvfp4_block_scale(sb, gs)
     prod = (vals * scale[:, :, None]).astype(np.float32)
     return bf16_round(prod.reshape(n, k))
+
+
+def dequantize_nvfp4(packed: np.ndarray, sb: np.ndarray, gs: float) -> np.ndarray:
+    """The same values as dequantize_nvfp4_elementwise, table-driven: for one tensor (one gs)
+    a value depends only on the (scale byte, code nibble) pair, so the definition is applied
+    once to all 256 x 16 pairs and every element is a table lookup. Bit-identical by
+    construction; fast enough for billions of weights."""
+    codes16 = np.arange(16, dtype=np.uint8)
+    pairs = np.repeat(codes16[None, :], 256, axis=0)                       # [256 scale bytes, 16 codes]
+    packed_tab = (pairs[:, 0::2] | (pairs[:, 1::2] << 4)).astype(np.uint8)  # [256, 8]: 16 codes per row
+    sb_tab = np.arange(256, dtype=np.uint8)[:, None]                        # one block of 16 per row
+    lut = dequantize_nvfp4_elementwise(packed_tab, sb_tab, gs).reshape(256 * 16)
+    codes = unpack_nvfp4(packed)
+    n, k = codes.shape
+    sbe = np.repeat(np.ascontiguousarray(sb, dtype=np.uint8).astype(np.uint16), NVFP4_BLOCK, axis=1)
+    return lut[sbe * 16 + codes]
 
 
 # ----------------------------------------------------------------------------- ternary

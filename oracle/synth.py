@@ -36,17 +36,20 @@ def quantized_linears(spec: ModelSpec, seed: int, fmt: str | None = None):
 
 
 def logical_weights(spec: ModelSpec, seed: int, fmt: str | None = None,
-                    packed: dict | None = None) -> dict:
+                    packed: dict | None = None, embed: torch.Tensor | None = None) -> dict:
     """fp32 weights in the nested form oracle.torso expects.
 
     `packed` (name -> parts) may supply already-quantised tensors (for instance read back
-    from the device); otherwise they are quantised here from the seeded latents."""
+    from the device); otherwise they are quantised here from the seeded latents. `embed`
+    may supply the tied embedding table (for instance the device's), else it is regenerated
+    from the seed."""
     fmt = fmt or spec.weight_format
     deq = {}
     src = packed.items() if packed is not None else quantized_linears(spec, seed, fmt)
     for name, parts in src:
         deq[name] = torch.from_numpy(Q.dequantize(fmt, parts).copy())
-    W = {"embed": synth.embedding(spec, seed).float(), "final_norm": synth.final_norm(spec, seed),
+    W = {"embed": (embed if embed is not None else synth.embedding(spec, seed)).float(),
+         "final_norm": synth.final_norm(spec, seed),
          "layers": []}
     for li in range(spec.n_layers):
         p = f"layers.{li}."
@@ -82,3 +85,16 @@ def packed_digest(parts_by_name) -> str:
             h.update(key.encode())
             h.update(np.ascontiguousarray(parts_by_name[name][key]).tobytes())
     return h.hexdigest()
+
+
+def device_logical_weights(dw, seed: int) -> dict:
+    """The oracle's fp32 weights for a device model built with keep_logical=True: every
+    logical linear's packed bytes read back from the GPU and dequantised here by oracle.quant
+    (the device's own dequantiser is not used), the tied embedding table copied from the GPU
+    (it may have been generated there), and the small parameters regenerated from the seed."""
+    from strands_decider_b200.weights import packed_to_numpy
+
+    if not dw.logical:
+        raise ValueError("the device weights were built without keep_logical=True")
+    packed = {name: packed_to_numpy(pw) for name, pw in dw.logical.items()}
+    return logical_weights(dw.spec, seed, fmt=dw.spec.weight_format, packed=packed, embed=dw.embed.cpu())

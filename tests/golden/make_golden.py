@@ -1,8 +1,10 @@
 """Generate the golden fixtures by running the reference itself.
 
-Run in a container that has the reference checkout (read-only) and transformers:
+Run where the reference and transformers are importable, naming the reference by its
+checkout root (the directory holding `src/strands_decider`) or by a directory that holds the
+installed `strands_decider` package, as the first argument or in STRANDS_DECIDER_SRC:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference checkout> [--readouts-only | ...]
 
 What runs is the reference's own code, unmodified:
   * the torso: transformers' `Qwen3_5ForCausalLM(cfg).model` (the module strands-decider
@@ -19,7 +21,9 @@ What runs is the reference's own code, unmodified:
     just that fixture);
   * transformers' token-by-token `torch_recurrent_gated_delta_rule` (`TF:314-353`) on the
     chunk-rule inputs, the form single-token appends take (`--recurrent-only` regenerates just
-    that fixture).
+    that fixture);
+  * the torso at the 2B shapes (head_dim 256, vocab 248320; 4 layers) on one prompt
+    (`--hybrid2b-only` regenerates just that fixture).
 
 The fixtures are small .npz files committed beside this script; the tests read only
 them (the reference is not present where the GPU tests run).
@@ -116,6 +120,64 @@ def reference_probs(torso, rows, opt_ids, n_opts, temps, pad_id=0):
     return lp.exp().numpy(), pooled.numpy(), hidden.numpy(), mask.numpy()
 
 
+# The 2B shapes (hidden 2048, GDN 16 heads x 128, attention 8q/2kv x 256 with partial RoPE,
+# FFN 6144, vocab 248320 tied) in a 4-layer torso [GDN x3, attention], bf16 weights: pins the
+# oracle at head_dim 256 and the full vocabulary. The layers are the 2B model's own; 24 of them
+# only repeat these four.
+PIN_BLOCK_ROWS = 4096
+PIN_OPTS = ([11, 12, 13], [248300, 248310, 248319, 5])
+
+
+def hybrid2b_pin_spec():
+    import dataclasses
+
+    from strands_decider_b200 import config
+
+    return dataclasses.replace(config.HYBRID_2B, name="hybrid-2b-shapes-4-layers",
+                               layer_types=config.hybrid_pattern(4), weight_format="bf16")
+
+
+def hybrid2b_pin_inputs(spec):
+    g = torch.Generator().manual_seed(22)
+    return torch.randint(0, spec.vocab, (160,), generator=g).tolist()
+
+
+def hybrid2b_pin_weights(spec, rows=None):
+    """The pin's weights in oracle.torso's nested form: linears and small parameters from the
+    seeded synthetic generators (seed 2) rounded to bf16; the tied embedding N(0, 0.02) in
+    blocks of PIN_BLOCK_ROWS rows, each block from its own generator, rounded to bf16. With
+    `rows`, only the blocks holding those rows are generated (the others stay zero), which is
+    all a forward over those ids and option rows reads."""
+    from oracle import synth as osynth
+
+    W = osynth.logical_weights(spec, seed=2, fmt="bf16")
+    emb = torch.zeros(spec.vocab, spec.hidden)
+    blocks = range((spec.vocab + PIN_BLOCK_ROWS - 1) // PIN_BLOCK_ROWS)
+    if rows is not None:
+        blocks = sorted({int(r) // PIN_BLOCK_ROWS for r in rows})
+    for b in blocks:
+        g = torch.Generator().manual_seed(1000 + b)
+        lo, hi = b * PIN_BLOCK_ROWS, min(spec.vocab, (b + 1) * PIN_BLOCK_ROWS)
+        emb[lo:hi] = (torch.randn(hi - lo, spec.hidden, generator=g) * 0.02).to(torch.bfloat16).float()
+    W["embed"] = emb
+    return W
+
+
+def make_hybrid2b_pin():
+    """The reference torso at the 2B shapes (4 layers) on one 160-token prompt, read out over two
+    option sets (one reaching the last vocabulary rows)."""
+    spec = hybrid2b_pin_spec()
+    W = hybrid2b_pin_weights(spec)
+    torso = build_reference_torso(spec, W)
+    ids = hybrid2b_pin_inputs(spec)
+    probs, pooled, hidden, _ = reference_probs(torso, [ids, ids], [list(o) for o in PIN_OPTS],
+                                               [len(o) for o in PIN_OPTS], [1.0, 0.8])
+    np.savez_compressed(os.path.join(HERE, "hybrid2b_shapes_bf16.npz"), ids=np.array(ids, np.int32),
+                        probs=probs.astype(np.float32), pooled=pooled[0].astype(np.float32),
+                        hidden_tail=hidden[0, -3:].astype(np.float32))
+    print("hybrid-2b shapes pin", probs)
+
+
 READOUT_CASES = (("slot", 24, 0), ("slot_mlp", 24, 64), ("pointer", 64, 0))
 
 
@@ -182,13 +244,26 @@ def make_recurrent_rule() -> None:
     print("recurrent rule", sorted(out))
 
 
+def reference_import_path(root: str) -> str:
+    """The directory to put on sys.path for `import strands_decider`: root/src for a
+    checkout, root itself for an installed copy."""
+    src = os.path.join(root, "src")
+    path = src if os.path.isdir(os.path.join(src, "strands_decider")) else root
+    if not os.path.isdir(os.path.join(path, "strands_decider")):
+        raise SystemExit(f"no strands_decider package under {root!r}")
+    return path
+
+
 def main(reference_root: str) -> None:
-    sys.path.insert(0, os.path.join(reference_root, "src"))
+    sys.path.insert(0, reference_import_path(reference_root))
     if "--readouts-only" in sys.argv:
         make_readouts()
         return
     if "--recurrent-only" in sys.argv:
         make_recurrent_rule()
+        return
+    if "--hybrid2b-only" in sys.argv:
+        make_hybrid2b_pin()
         return
     import transformers.models.qwen3_5.modeling_qwen3_5 as q35
     from strands_decider.schema import derive_confidence, derive_score_confidence
@@ -270,8 +345,14 @@ def main(reference_root: str) -> None:
                         n=np.array([len(d) for d in dists]), confidence=np.array(conf),
                         score_confidence=np.array(sconf), score_confidence_s01=np.array(sconf_s))
     make_readouts()
+    make_hybrid2b_pin()
     print("done")
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 and not sys.argv[1].startswith("--") else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 and not sys.argv[1].startswith("--") else os.environ.get(
+        "STRANDS_DECIDER_SRC")
+    if not root:
+        raise SystemExit("usage: make_golden.py <reference checkout or install dir> [--...-only] "
+                         "(or set STRANDS_DECIDER_SRC)")
+    main(root)

@@ -114,6 +114,26 @@ def test_tiny_ragged_matches_reference(fmt):
             np.testing.assert_allclose(hid.numpy(), g["hidden"][i, : len(r)], rtol=1e-4, atol=1e-4)
 
 
+def test_oracle_at_the_2b_shapes_matches_reference():
+    """hidden 2048, GDN 16 heads, attention 8q/2kv x head_dim 256 with partial RoPE, FFN 6144 and
+    the 248320-row tied embedding (4 layers, bf16 weights): final hidden states and option
+    probabilities, including option rows at the end of the vocabulary."""
+    from tests.golden.make_golden import PIN_OPTS, hybrid2b_pin_spec, hybrid2b_pin_weights
+
+    g = _load("hybrid2b_shapes_bf16.npz")
+    spec = hybrid2b_pin_spec()
+    ids = g["ids"].astype(np.int64).tolist()
+    W = hybrid2b_pin_weights(spec, rows=ids + [o for opts in PIN_OPTS for o in opts])
+    cfg = osynth.torso_config(spec)
+    hid, _ = T.forward_sequence(cfg, W, torch.tensor(ids))
+    np.testing.assert_allclose(hid[-3:].numpy(), g["hidden_tail"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(hid[-1].numpy(), g["pooled"], rtol=1e-4, atol=1e-4)
+    for i, opts in enumerate(PIN_OPTS):
+        p = H.decide(hid[-1:], W["embed"], torch.tensor([opts]), torch.tensor([len(opts)]),
+                     torch.tensor([[1.0, 0.8][i]]))
+        np.testing.assert_allclose(p[0].numpy(), g["probs"][i, : len(opts)], atol=1e-5)
+
+
 def test_prefix_cache_continuation_equals_full_prompt():
     """The property tests/test_prefix_cache.py:43-64 asserts for the reference: a suffix
     forwarded against a cached state equals the full prompt, at every suffix position.
@@ -192,6 +212,21 @@ def test_quantise_roundtrip_properties(fmt):
         assert rel < 0.02
     err = np.abs(d - w).mean() / np.abs(w).mean()
     assert err < {"int4": 0.15, "nvfp4": 0.12, "ternary": 0.6}[fmt]
+
+
+def test_nvfp4_table_dequantiser_equals_the_elementwise_definition():
+    """The table-driven NVFP4 dequantiser (used for whole 2B-shape models) returns the same
+    bits as the definition applied element by element, including zero blocks and every
+    (scale byte, code) pair that occurs."""
+    rng = np.random.default_rng(7)
+    for amp in (0.02, 3.0):
+        w = (rng.standard_normal((96, 1024)) * amp).astype(np.float32)
+        w[5, :16] = 0.0
+        w[7, 16:32] *= 1e-4                      # tiny blocks: small scale bytes
+        p = Q.quantize("nvfp4", w)
+        a = Q.dequantize("nvfp4", p)
+        b = Q.dequantize_nvfp4_elementwise(p["data"], p["scales"], float(np.asarray(p["global_scale"]).reshape(-1)[0]))
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
 def test_int4_nibble_order():
