@@ -50,7 +50,8 @@ int b200_read_fault(unsigned int* fault_out);
 
 /* ---------------------------------------------------------------- packed weights
  * Replaces the bf16 `nn.Linear` weights of TF:417-420, TF:403, TF:632-643, TF:701-703.
- * Formats (bit-exact definitions in oracle/quant.py and DESIGN.md):
+ * Formats (each element dequantises to bf16_rn(code value x its scale); the quantisation
+ * rules are b200_quantize's):
  *   B200_W_BF16     data uint16 [n, k]
  *   B200_W_INT4G128 data int32 [n, k/8] (8 nibbles per word, element k at bits 4*(k%8)),
  *                   scales bf16 [n, k/128]

@@ -20,6 +20,7 @@ import torch
 
 PROB_SLOTS = 8            # probabilities carried per answer record (kmax <= 8)
 REC = 4 + PROB_SLOTS      # question id, argmax, confidence, score, probs...
+PAD_ID = 2 ** 31 - 1      # question id of a padding record (sorts after every real one)
 
 
 def request_cost(r: dict) -> int:
@@ -49,45 +50,71 @@ def shard_loads(costs: list[int], shards: list[list[int]]) -> list[int]:
 
 @dataclass
 class AnswerRecords:
-    """Answers of one rank as fixed-size fp32 records (one row per question)."""
+    """Answers of one rank as fixed-size int32 records, one row per question: column 0 the
+    question id and column 1 the argmax as integers, columns 2.. the fp32 bit patterns of
+    the confidence, the score and the probabilities (`as_floats` reads them back). Integer
+    ids stay exact up to 2^31 - 2 (fp32 would collide past 2^24)."""
 
-    rows: torch.Tensor   # [n, REC]
+    rows: torch.Tensor   # [n, REC] int32
 
     @classmethod
     def pack(cls, qids, argmax, confidence, score, probs) -> AnswerRecords:
-        n = len(qids)
-        rows = torch.zeros(n, REC, dtype=torch.float32, device=probs.device)
-        rows[:, 0] = torch.as_tensor(qids, dtype=torch.float32, device=probs.device)
-        rows[:, 1] = argmax.float()
-        rows[:, 2] = confidence.float()
-        rows[:, 3] = score.float()
+        dev = probs.device
+        if isinstance(qids, torch.Tensor):
+            if qids.dtype not in (torch.int32, torch.int64):
+                raise TypeError("question ids must be an integer tensor")
+            q = qids.to(device=dev, dtype=torch.int32)
+        else:
+            qids = list(qids)
+            if qids and not 0 <= min(qids) <= max(qids) < PAD_ID:
+                raise ValueError(f"question ids must lie in [0, {PAD_ID})")
+            q = torch.as_tensor(qids, dtype=torch.int32, device=dev)
+        n = int(q.numel())
+        f = torch.zeros(n, REC, dtype=torch.float32, device=dev)
+        f[:, 2] = confidence.float()
+        f[:, 3] = score.float()
         k = min(probs.shape[1], PROB_SLOTS)
-        rows[:, 4:4 + k] = probs[:, :k].float()
+        f[:, 4:4 + k] = probs[:, :k].float()
+        rows = f.view(torch.int32)
+        rows[:, 0] = q
+        rows[:, 1] = argmax.to(torch.int32)
         return cls(rows)
 
+    @staticmethod
+    def as_floats(rows: torch.Tensor) -> torch.Tensor:
+        """[n, REC] float32: ids and argmax as values, the rest as stored."""
+        f = rows.view(torch.float32).clone()
+        f[:, 0] = rows[:, 0].float()
+        f[:, 1] = rows[:, 1].float()
+        return f
 
-def gather_answers(local: AnswerRecords, group=None) -> torch.Tensor:
-    """All-gather every rank's records; returns [total, REC] sorted by question id.
 
-    Counts differ per rank, so the counts go first (one small collective) and the records
-    are padded to the largest count (id -1 marks padding). Every rank issues the same two
-    collectives in the same order."""
+def gather_answers(local: AnswerRecords, capacity: int, total: int | None = None, group=None) -> torch.Tensor:
+    """All-gather every rank's records with ONE collective; returns int32 [n, REC] sorted by
+    question id.
+
+    Every rank pads its records to `capacity` rows (the most any rank holds, which the shard
+    plan gives every rank without a collective; padding rows carry id PAD_ID) and issues the
+    same single all-gather. The result is sorted on the device, padding last, and cut to
+    `total` rows when the caller knows the real count (no host synchronisation); with
+    total=None the padding rows are dropped, which reads the count back to the host."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
-    dev = local.rows.device
-    n = torch.tensor([local.rows.shape[0]], dtype=torch.int64, device=dev)
-    counts = [torch.zeros_like(n) for _ in range(world)]
-    dist.all_gather(counts, n, group=group)
-    mx = int(max(int(c) for c in counts))
-    padded = torch.full((mx, REC), -1.0, dtype=torch.float32, device=dev)
-    padded[: local.rows.shape[0]] = local.rows
-    out = torch.empty(world * mx, REC, dtype=torch.float32, device=dev)
+    n, dev = local.rows.shape[0], local.rows.device
+    if n > capacity:
+        raise ValueError(f"{n} answer records exceed the gather capacity of {capacity}")
+    padded = torch.full((capacity, REC), 0, dtype=torch.int32, device=dev)
+    padded[:, 0] = PAD_ID
+    padded[:n] = local.rows
     if dev.type == "cuda":
+        out = torch.empty(world * capacity, REC, dtype=torch.int32, device=dev)
         dist.all_gather_into_tensor(out, padded, group=group)
     else:
         parts = [torch.empty_like(padded) for _ in range(world)]
         dist.all_gather(parts, padded, group=group)
         out = torch.cat(parts)
-    out = out[out[:, 0] >= 0]
-    return out[torch.argsort(out[:, 0])]
+    out = out[torch.argsort(out[:, 0], stable=True)]
+    if total is not None:
+        return out[:total]
+    return out[out[:, 0] != PAD_ID]

@@ -69,7 +69,11 @@ def _worker(rank: int, world: int, port: int, q: mp.Queue, fail_rank: int) -> No
         if rank == fail_rank:
             raise RuntimeError("rank failed before the gather")
         rec = _fake_answers(shards[rank], 3)
-        out = dispatch.gather_answers(rec)
+        # every rank knows every shard, so the gather capacity needs no collective
+        capacity = 3 * max(len(s) for s in shards)
+        out = dispatch.gather_answers(rec, capacity, total=3 * len(reqs))
+        dropped = dispatch.gather_answers(rec, capacity)      # padding dropped via the host
+        assert torch.equal(out, dropped)
         q.put((rank, "ok", out.tolist()))
         dist.destroy_process_group()
     except Exception as e:  # report, never hang the parent
@@ -101,9 +105,22 @@ def test_gather_answers_over_gloo(world):
     for rank in range(world):
         status, payload = res[rank]
         assert status == "ok", payload
-        got = torch.tensor(payload)
+        got = torch.tensor(payload, dtype=torch.int32)
         assert got.shape == want.shape
         assert torch.equal(got, want)
+        f = dispatch.AnswerRecords.as_floats(got)
+        assert torch.equal(f[:, 0], torch.arange(30, dtype=torch.float32))
+
+
+def test_answer_records_keep_large_question_ids_exact():
+    """Ids past 2^24 (where fp32 collides) survive packing, and padding ids are refused."""
+    ids = [2 ** 24 + 1, 2 ** 24, 2 ** 31 - 2]
+    probs = torch.tensor([[0.2, 0.8], [0.6, 0.4], [0.5, 0.5]])
+    rec = dispatch.AnswerRecords.pack(ids, probs.argmax(1), probs.max(1).values, torch.zeros(3), probs)
+    assert rec.rows.dtype == torch.int32 and rec.rows[:, 0].tolist() == ids
+    assert torch.equal(dispatch.AnswerRecords.as_floats(rec.rows)[:, 4:6], probs)
+    with pytest.raises(ValueError):
+        dispatch.AnswerRecords.pack([dispatch.PAD_ID], probs[:1].argmax(1), probs[:1, 0], torch.zeros(1), probs[:1])
 
 
 def test_dead_rank_is_detected_by_the_survivors():
