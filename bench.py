@@ -543,6 +543,97 @@ def run_case(args) -> None:
     _case_profiled(launch)
 
 
+# ----------------------------------------------------------------------------- int4 GEMM microbench
+C2_SHAPES = [(m, n) for n in (6144, 2048) for m in (1, 16, 256, 4096)]
+C2_K = 2048
+
+
+def c2_gemm(pk: dict, reps: int = 50, check: bool = True) -> list[dict]:
+    """The int4 weight-only GEMM microbench: y = x @ dequant(W)^T, W N(0, 0.02) [N, 2048]
+    quantised to int4 g128 (bf16 scales, 8 nibbles per int32), x bf16 N(0, 1) [M, 2048] (one
+    bf16 plane: the activations are bf16), y fp32, for M in {1, 16, 256, 4096} and N in
+    {6144, 2048}. Each shape launches `reps` times back to back through b200_linear, each launch
+    on a different copy of the weight (the copies together exceed twice the 126 MB L2, so every
+    launch streams its weight from HBM); time per launch = CUDA-event time / reps.
+
+    roofline: bytes = N K / 2 (codes) + N K / 64 (bf16 scale per 128) + 2 M K (x) + 4 M N (y);
+    flops = 2 M N K; bound time = max(bytes / measured HBM copy bandwidth, flops / measured bf16
+    GEMM peak); frac = bound time / measured time. Parity: y against an fp64 product of x and the
+    oracle's dequantisation of the packed bytes (read back), as the largest error relative to
+    max |y| (up to 256 rows checked)."""
+    import numpy as np
+
+    from oracle import quant as OQ
+    from strands_decider_b200.weights import packed_to_numpy
+
+    torch.cuda.set_device(0)
+    st = torch.cuda.current_stream()
+    out = []
+    for n in sorted({n for _, n in C2_SHAPES}, reverse=True):
+        g = torch.Generator(device="cuda").manual_seed(n)
+        base = WT.quantize("int4", torch.randn(n, C2_K, device="cuda", generator=g) * 0.02)
+        base.ensure_tiles()
+        per_copy = base.tiles.numel() + base.tile_scales.numel()
+        copies = [base] + [WT.PackedWeight("int4", n, C2_K, base.data, base.scales, None, base.tiles.clone(),
+                                           base.tile_scales.clone())
+                           for _ in range(max(1, int(2 * 126e6 * 1.2 // per_copy)))]
+        qws = [c.qweight() for c in copies]
+        w64 = torch.from_numpy(OQ.dequantize("int4", packed_to_numpy(base)).astype(np.float64)) if check else None
+        for m, nn in C2_SHAPES:
+            if nn != n:
+                continue
+            x = torch.randn(m, C2_K, device="cuda", generator=g).to(torch.bfloat16)
+            y = torch.empty(m, n, device="cuda")
+            o = _lib.LinearOut(_lib.EP_STORE, n, _lib.ptr(y), n, 0)
+
+            def launch(i):
+                _lib.call("b200_linear", _lib.ptr(x), None, m, C2_K, C2_K, C.byref(qws[i % len(qws)]), C.byref(o),
+                          st.cuda_stream)
+
+            for i in range(3):
+                launch(i)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for i in range(reps):
+                launch(3 + i)
+            e1.record(st)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / reps * 1e3
+            nbytes = n * C2_K // 2 + n * C2_K // 64 + 2 * m * C2_K + 4 * m * n
+            flops = 2.0 * m * n * C2_K
+            t_hbm = nbytes / (pk["hbm_gbs"] * 1e9) * 1e6
+            t_mma = flops / (pk["bf16_tflops"] * 1e12) * 1e6
+            rec = {"m": m, "n": n, "k": C2_K, "us": round(us, 3), "gbs": round(nbytes / us / 1e3, 1),
+                   "tflops": round(flops / us / 1e6, 1), "bound": "hbm" if t_hbm >= t_mma else "tensor",
+                   "roofline_us": round(max(t_hbm, t_mma), 3), "frac": round(max(t_hbm, t_mma) / us, 3)}
+            if check:
+                launch(0)
+                rows = min(m, 256)
+                ref = x[:rows].double().cpu() @ w64.T
+                got = y[:rows].double().cpu()
+                rec["max_rel_err"] = float((got - ref).abs().max() / ref.abs().max())
+            out.append(rec)
+        del copies, qws
+        torch.cuda.empty_cache()
+    assert _lib.read_fault() == 0
+    return out
+
+
+def c2_main(args) -> None:
+    pk = peaks()
+    shapes = c2_gemm(pk, reps=max(args.steps, 20))
+    worst = min(r["frac"] for r in shapes)
+    line = {"metric": "int4 g128 weight-only GEMM time per launch (K=2048)", "value": round(worst, 3),
+            "unit": "min roofline fraction over shapes", "n_gpus": 1, "higher_is_better": True,
+            "dtype": "bf16 x int4", "data": "synthetic",
+            "config": {"workload": "int4-gemm-microbench", "k": C2_K, "m": [1, 16, 256, 4096], "n": [6144, 2048],
+                       "l2": "weight copies rotated per launch (together > 2 x L2)",
+                       "peaks": f"{pk['src']}: HBM {pk['hbm_gbs']} GB/s, bf16 {pk['bf16_tflops']} TFLOP/s"},
+            "shapes": shapes}
+    print(json.dumps(line), flush=True)
+
+
 WORKLOADS = {
     "nvfp4": (config.HYBRID_2B, config.HYBRID_2B_WORKLOAD, 128, True),
     "prefix": (config.HYBRID_2B, config.PREFIX_CACHE_WORKLOAD, 32, True),
@@ -645,7 +736,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="nvfp4", choices=sorted(WORKLOADS) + ["latency"])
+    ap.add_argument("--workload", default="nvfp4", choices=sorted(WORKLOADS) + ["latency", "gemm"])
     ap.add_argument("--requests-per-step", type=int, default=0, help="0 = the workload's default")
     ap.add_argument("--cpu-sample", type=int, default=3, help="requests in the CPU baseline sample (0 = skip)")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
@@ -667,6 +758,9 @@ def main() -> None:
     args = ap.parse_args()
     if args.case:
         run_case(args)
+        return
+    if args.workload == "gemm":
+        c2_main(args)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

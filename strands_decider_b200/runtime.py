@@ -230,6 +230,7 @@ class DecisionModel:
         self._alloc_pool(pool_slots, pool_kv_tokens or pool_slots * 512)
         self.readout = None
         self.use_graphs = graphs
+        self.max_graphs = 64          # captured buckets kept (oldest dropped first)
         self._graphs: dict = {}
 
     # ------------------------------------------------------------------ pool
@@ -378,6 +379,9 @@ class DecisionModel:
         key = (b, dec["ordinal_smoothing"] if dec is not None else 0.0)
         g = self._graphs.get(key)
         if g is None:
+            if len(self._graphs) >= self.max_graphs:       # drop the oldest capture
+                torch.cuda.synchronize(self.device)        # none of its replays still running
+                self._graphs.pop(next(iter(self._graphs)))
             g = self._graphs[key] = _Graph(self, b)
             g.ordinal_smoothing = key[1]
         g.fill(flat, cu, prefix, save, dec)
@@ -406,8 +410,8 @@ class DecisionModel:
             g.launch(self, stream=side, slots=False)
         st.wait_stream(side)
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=st):
-            g.out = g.launch(self, stream=st)
+        with torch.cuda.graph(graph):   # captures on a side stream, after a device synchronisation
+            g.out = g.launch(self, stream=torch.cuda.current_stream(self.device))
         g.graph = graph
 
     def _dev(self, x, dtype=torch.int32) -> torch.Tensor:
