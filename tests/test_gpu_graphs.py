@@ -5,7 +5,10 @@ shape bucket, with the batch padded up to the bucket by dummy sequences.
   from eager launches of the same kernels (the batch is sized so that no GEMM splits K, whose
   atomic partial sums are the one source of run-to-run differences).
 * Padded batches (the prefix path, ragged states and questions) answer as the eager path
-  within 1e-5 with the same argmax, and the padding reads and writes no cached state.
+  within 1e-4 with the same argmax, and the padding reads and writes no cached state. (A padded
+  batch has more rows, which can change how a small GEMM splits K and so the order of its fp32
+  partial sums: differences of a few 1e-5 in a probability, as between two eager runs of
+  batches of different sizes.)
 * Batches that fall in the same bucket share one graph.
 """
 
@@ -71,9 +74,9 @@ def test_padded_buckets_answer_as_eager_and_leave_the_pool_alone(tiny):
                      "kinds": [1] * len(qlens), "n_opts": [3] * len(qlens), "opt_ids": [[11, 12, 13]] * len(qlens)})
     got = mg.score_requests(reqs, ordinal_smoothing=0.1).cpu()
     want = me.score_requests(reqs, ordinal_smoothing=0.1).cpu()
-    assert (got.probs - want.probs).abs().max().item() < 1e-5
+    assert (got.probs - want.probs).abs().max().item() < 1e-4
     assert torch.equal(got.argmax, want.argmax)
-    assert (got.confidence - want.confidence).abs().max().item() < 1e-5
+    assert (got.confidence - want.confidence).abs().max().item() < 1e-4
     # the dummies saved nothing: the pools of both models hold the same states
     for a, b in ((mg.gdn_state, me.gdn_state), (mg.conv_hist, me.conv_hist)):
         assert (a[:, :4] - b[:, :4]).abs().max().item() < 1e-4
@@ -87,7 +90,7 @@ def test_padded_buckets_answer_as_eager_and_leave_the_pool_alone(tiny):
     qs = [r["questions"][0] for r in reqs]
     a = mg.score_suffixes(qs, [0, 1, 2, 3], [[11, 12]] * 4, [2] * 4, [0] * 4, [1.0] * 4).cpu()
     b = me.score_suffixes(qs, [0, 1, 2, 3], [[11, 12]] * 4, [2] * 4, [0] * 4, [1.0] * 4).cpu()
-    assert (a.probs - b.probs).abs().max().item() < 1e-5
+    assert (a.probs - b.probs).abs().max().item() < 1e-4
 
 
 def test_batches_in_one_bucket_share_a_graph(tiny):
@@ -98,5 +101,5 @@ def test_batches_in_one_bucket_share_a_graph(tiny):
         rows = [torch.randint(0, V, (n,), generator=g).tolist() for n in lens]
         got = mg.score_prompts(rows, [[11, 12, 13]] * 2, [3, 3], [1, 1], [1.0, 1.0]).cpu()
         want = me.score_prompts(rows, [[11, 12, 13]] * 2, [3, 3], [1, 1], [1.0, 1.0]).cpu()
-        assert (got.probs - want.probs).abs().max().item() < 1e-5
+        assert (got.probs - want.probs).abs().max().item() < 1e-4
     assert len(mg._graphs) == 1

@@ -41,7 +41,8 @@ def _requests():
         "overdue": NoulQuestion(instructions="Is an item already overdue?"),
         "tone": ScoreQuestion(instructions="How upset does the member sound?", criteria=["calm", "tense", "upset"]),
         "topic": ChoiceQuestion(instructions="What is the message mainly about?",
-                                criteria=["a loan", "a fee", "a room", "a card", "something else"]),
+                                criteria={"loan": "borrowing or renewing", "fee": "money owed", "room": "a booking",
+                                          "card": "a member card", "other": "something else"}),
     }
     policy = ("Members may borrow ten items at a time for three weeks. A loan renews twice unless "
               "someone else holds the item. Cards with more than five dollars of fees are blocked. ")
@@ -142,6 +143,7 @@ def test_b200_engine_refuses_like_the_reference(checkpoint):
     b200 = load_engine(checkpoint, weight_format="bf16", max_tokens=2048, pool_slots=2)
     if b200.model.config.head_type != "slot":
         pytest.skip("the option-count limit applies to slot heads")
-    many = ChoiceQuestion(instructions="pick", criteria=[f"option {i}" for i in range(b200.model.config.num_slots + 1)])
+    many = ChoiceQuestion(instructions="pick",
+                          criteria={f"o{i}": f"option {i}" for i in range(b200.model.config.num_slots + 1)})
     with pytest.raises(ValueError, match="slots"):
         b200.evaluate(SystemOneRequest(state="a loan", questions={"q": many}))
