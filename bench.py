@@ -445,8 +445,8 @@ def gemm_case(m: int, fmt: str, ep: str, n: int = 2 * 6144, k: int = 2048, plane
         return launch_lo8, 2.0 * m * n * k
 
     def launch():
-        _lib.call("b200_linear", _lib.ptr(keep[1][0]), _lib.ptr(keep[1][1]), m, k, k, C.byref(qw), C.byref(o),
-                  _lib.stream_ptr())
+        _lib.call("b200_linear", _lib.ptr(keep[1][0]), _lib.ptr(keep[1][1]) if planes == "split" else None, m, k, k,
+                  C.byref(qw), C.byref(o), _lib.stream_ptr())
 
     return launch, 2.0 * m * n * k
 
@@ -757,7 +757,8 @@ def main() -> None:
     ap.add_argument("--ep", default="swiglu", choices=["swiglu", "store", "resid"])
     ap.add_argument("--n", type=int, default=2 * 6144)
     ap.add_argument("--k", type=int, default=2048)
-    ap.add_argument("--planes", default="split", choices=["split", "lo8"])
+    ap.add_argument("--planes", default="split", choices=["split", "lo8", "one"],
+                    help="gemm case: activation planes (two bf16, bf16 + e4m3, or one bf16 plane)")
     ap.add_argument("--seqs", type=int, default=32)
     ap.add_argument("--len", type=int, default=512)
     ap.add_argument("--reps", type=int, default=10)
