@@ -764,6 +764,264 @@ __global__ void zero_rows_kernel(float* __restrict__ out, int ld, int n) {
   for (int i = threadIdx.x; i < n / 4; i += blockDim.x) row[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
+// --------------------------------------------------------------------------- small M (swap-AB)
+// Batches of at most 64 rows (single-token state appends, small request batches, the int4
+// microbench at M = 1 and 16): the weight tile is the MMA's A operand (M = 128 weight rows)
+// and the activations its B operand (N = NT = 16 or 64 token rows), so neither tensor work nor
+// shared memory goes to padding rows. One CTA = one 128-row weight tile over one K range (split
+// K across CTAs for the store / residual epilogues). Streaming the packed weights is the bound,
+// so the producer issues the bulk copies of the range's first SK_WSLOTS k-blocks (all of a
+// K range up to 1024) before it waits on the kernel before it in the stream (the weights do not
+// depend on that kernel), keeping up to ~70 KB per CTA in flight; the unpack warps decode each
+// k-block into a bf16 ring as it lands.
+//   warp 0      producer: packed weight k-blocks (1-D bulk copies into a ring of SK_WSLOTS
+//               slots, refilled as the unpack warps release them) and, per stage, the
+//               activation planes (TMA, NT rows x 64 k; rows past m read as zeros)
+//   warp 1      TMEM (max(NT, 32) columns) and the MMAs: per 16 k one tcgen05.mma per plane,
+//               M = 128, N = NT, A = the bf16 weight stage, B = the activation stage
+//   warps 2..5  epilogue: TMEM lane = weight row (output column), column = token; a warp
+//               writes 32 consecutive outputs of a token at a time (fp32 store or residual
+//               add, split-K partials by red.add into a zeroed output or the residual, or
+//               SwiGLU: the up rows' two quarters hand their values to the gate rows' two
+//               quarters through shared memory)
+//   warps 6..13 unpack: weight slot -> swizzled K-major bf16 stage (unpack_unit_smem, the
+//               same decode as gemm_tc_kernel, bit-exact with b200_dequantize)
+constexpr int SK_STAGES = 4;
+constexpr int SK_WSLOTS = 16;
+constexpr int SK_ROWS = 128;
+constexpr int SK_MAX_M = 64;
+
+template <int FMT, int PL, int NT>
+struct SkinnySmem {
+  static_assert(PL != PL_LO8, "the small-M kernel takes one or two bf16 activation planes");
+  static constexpr bool PACKED = FMT != B200_W_BF16;
+  static constexpr int X_BYTES = NT * GEMM_BK * 2;  // one activation plane of a stage
+  static constexpr int X_STAGE = X_BYTES * (PL == PL_SPLIT ? 2 : 1);
+  static constexpr int B_BYTES = SK_ROWS * GEMM_BK * 2;  // the unpacked bf16 weight stage
+  static constexpr int W_BYTES = PACKED ? SK_ROWS * tile_row_bytes(FMT) : 0;
+  static constexpr int S_BYTES = PACKED ? SK_ROWS * tile_scale_row_bytes(FMT) : 0;
+  static constexpr int WSLOTS = PACKED ? SK_WSLOTS : 1;
+  static constexpr int SWAP_BYTES = 2 * NT * 32 * 4;  // SwiGLU hand-over: 2 quarters x NT tokens x 32 rows
+  static constexpr int BARS = 2 * WSLOTS + 3 * SK_STAGES + 1;
+  static constexpr int TOTAL = SK_STAGES * (B_BYTES + X_STAGE) + WSLOTS * (W_BYTES + S_BYTES) + SWAP_BYTES +
+                               BARS * 8 + 16 + 64 + 1024;
+  static_assert(X_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "128-byte-swizzled tiles need 1024-byte alignment");
+};
+
+template <int FMT, int EP, int PL, int NT>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmX_lo,
+                       const __grid_constant__ CUtensorMap tmW, const GemmArgs args) {
+  using SM = SkinnySmem<FMT, PL, NT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = smem;                                // SK_STAGES x B_BYTES
+  uint8_t* sX = sB + SK_STAGES * SM::B_BYTES;        // SK_STAGES x X_STAGE
+  uint8_t* sW = sX + SK_STAGES * SM::X_STAGE;        // WSLOTS x W_BYTES
+  uint8_t* sS = sW + SM::WSLOTS * SM::W_BYTES;       // WSLOTS x S_BYTES
+  float* sSwap = reinterpret_cast<float*>(sS + SM::WSLOTS * SM::S_BYTES);  // [2][NT][32]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sSwap) + SM::SWAP_BYTES);
+  uint64_t* full_w = bars;                           // [WSLOTS] weight slot landed
+  uint64_t* empty_w = bars + SM::WSLOTS;             // [WSLOTS] weight slot unpacked
+  uint64_t* full_x = bars + 2 * SM::WSLOTS;          // [STAGES] activation planes (and bf16 weights) landed
+  uint64_t* full_b = full_x + SK_STAGES;             // [STAGES] bf16 weight stage written
+  uint64_t* empty = full_b + SK_STAGES;              // [STAGES] the stage's MMAs are done
+  uint64_t* acc_full = empty + SK_STAGES;            // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint32_t* lut = tmem_slot + 4;                     // 16 words: ternary pair table
+  constexpr uint32_t TM_COLS = NT < 32 ? 32 : NT;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = args.k / GEMM_BK;
+  const int n_tiles = args.w.n / SK_ROWS;
+  const int n0 = (int(blockIdx.x) % n_tiles) * SK_ROWS, ks = int(blockIdx.x) / n_tiles;
+  const int kb0 = ks * nk / args.ksplit, kb1 = (ks + 1) * nk / args.ksplit;
+  const int nkb = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < SM::WSLOTS; ++i) {
+      mbar_init(&full_w[i], 1);
+      mbar_init(&empty_w[i], GEMM_UNPACK_THREADS);
+    }
+    for (int s = 0; s < SK_STAGES; ++s) {
+      mbar_init(&full_x[s], 1);
+      mbar_init(&full_b[s], GEMM_UNPACK_THREADS);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&acc_full[0], 1);
+    mbar_fence_init();
+  }
+  if (threadIdx.x < 16) lut[threadIdx.x] = ternary_pair_bits(threadIdx.x);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // one unit per CTA: the next kernel may be scheduled now (it waits for this one's results)
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ---------------- producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmX);
+      if constexpr (PL == PL_SPLIT) tma_prefetch_desc(&tmX_lo);
+      if constexpr (!SM::PACKED) tma_prefetch_desc(&tmW);
+      constexpr int RB = SM::PACKED ? tile_row_bytes(FMT) : 0, SB = tile_scale_row_bytes(FMT);
+      // this tile's rows inside the 256-row streaming tiles: tile n0 / 256, row offset n0 % 256
+      const size_t lt = size_t(n0 / GEMM_TILE_ROWS) * nk, sub = n0 % GEMM_TILE_ROWS;
+      const uint8_t* wtiles = reinterpret_cast<const uint8_t*>(args.w.tiles) + sub * RB;
+      const uint8_t* stiles = reinterpret_cast<const uint8_t*>(args.w.tile_scales) + sub * SB;
+      auto issue_w = [&](int i) {  // k-block kb0 + i into slot i % WSLOTS
+        const int slot = i % SM::WSLOTS;
+        const size_t kt = lt + kb0 + i;
+        mbar_arrive_expect_tx(&full_w[slot], SM::W_BYTES + SM::S_BYTES);
+        bulk_load(sW + slot * SM::W_BYTES, wtiles + kt * GEMM_TILE_ROWS * RB, SM::W_BYTES, &full_w[slot]);
+        if constexpr (SM::S_BYTES > 0)
+          bulk_load(sS + slot * SM::S_BYTES, stiles + kt * GEMM_TILE_ROWS * SB, SM::S_BYTES, &full_w[slot]);
+      };
+      if constexpr (SM::PACKED) {
+        for (int i = 0; i < min(nkb, SM::WSLOTS); ++i) issue_w(i);
+      }
+      pdl_wait();  // the activations come from the kernel before this one
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % SK_STAGES;
+        const uint32_t ph = (i / SK_STAGES) & 1;
+        mbar_wait(&empty[s], ph ^ 1, FAULT_GEMM_WAIT_EMPTY);
+        mbar_arrive_expect_tx(&full_x[s], SM::X_STAGE + (SM::PACKED ? 0 : SM::B_BYTES));
+        tma_load_2d(sX + s * SM::X_STAGE, &tmX, &full_x[s], (kb0 + i) * GEMM_BK, 0);
+        if constexpr (PL == PL_SPLIT)
+          tma_load_2d(sX + s * SM::X_STAGE + SM::X_BYTES, &tmX_lo, &full_x[s], (kb0 + i) * GEMM_BK, 0);
+        if constexpr (!SM::PACKED) tma_load_2d(sB + s * SM::B_BYTES, &tmW, &full_x[s], (kb0 + i) * GEMM_BK, n0);
+        if constexpr (SM::PACKED) {
+          if (i + SM::WSLOTS < nkb) {  // refill slot i once its k-block is unpacked
+            mbar_wait(&empty_w[i % SM::WSLOTS], (i / SM::WSLOTS) & 1, FAULT_GEMM_WAIT_EMPTY);
+            issue_w(i + SM::WSLOTS);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: D[weight row][token] += W_stage . X_stage^T
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(SK_ROWS, NT);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % SK_STAGES;
+        const uint32_t ph = (i / SK_STAGES) & 1;
+        mbar_wait(&full_x[s], ph, FAULT_GEMM_WAIT_FULL_A);
+        if constexpr (SM::PACKED) mbar_wait(&full_b[s], ph, FAULT_GEMM_WAIT_FULL_B);
+        tc_fence_after();
+        const uint64_t ad = umma_desc_sw128(smem_addr(sB + s * SM::B_BYTES));
+        const uint64_t bd = umma_desc_sw128(smem_addr(sX + s * SM::X_STAGE));
+#pragma unroll
+        for (int j = 0; j < GEMM_BK / 16; ++j) {  // +32 bytes of K per MMA = +2 in 16-byte units
+          umma_bf16(tmem_base, ad + 2 * j, bd + 2 * j, idesc, (i != 0 || j != 0) ? 1u : 0u);
+          if constexpr (PL == PL_SPLIT) umma_bf16(tmem_base, ad + 2 * j, bd + (SM::X_BYTES >> 4) + 2 * j, idesc, 1u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(&acc_full[0]);
+    }
+    __syncwarp();
+  } else if (warp < GEMM_UNPACK_WARP0) {
+    // ---------------- epilogue: quarter q holds weight rows n0 + 32q .. n0 + 32q + 31
+    const int q = warp & 3;
+    pdl_wait();  // the output (or residual) may be read or written by the kernel before this one
+    mbar_wait(&acc_full[0], 0, FAULT_GEMM_WAIT_ACCUM);
+    tc_fence_after();
+    const uint32_t tl = tmem_base + (uint32_t(q * 32) << 16);
+    uint32_t v[TM_COLS];
+    {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tl, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = r[j];
+    }
+    if constexpr (TM_COLS > 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tl + 32, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[32 + j] = r[j];
+    }
+    const b200_linear_out& o = args.o;
+    if constexpr (EP == B200_EP_SWIGLU) {
+      // rows 0..63 of the tile are gate features n0/2 .. n0/2 + 63, rows 64..127 the matching up
+      if (q >= 2) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) sSwap[((q - 2) * NT + t) * 32 + lane] = __uint_as_float(v[t]);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+      if (q < 2) {
+        const int ocol = n0 / 2 + q * 32 + lane;
+        if (2 * ocol < o.n_valid) {
+          uint16_t* dst = reinterpret_cast<uint16_t*>(o.out);
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            if (t < args.m) {
+              const float h = silu_approx(__uint_as_float(v[t])) * sSwap[(q * NT + t) * 32 + lane];
+              const uint16_t hb = f32_to_bf16_rn(h);
+              const size_t e = size_t(t) * o.ldo + ocol;
+              dst[e] = hb;
+              if (o.lo_offset) {
+                if (o.lo_format == B200_LO_E4M3)
+                  reinterpret_cast<uint8_t*>(dst + o.lo_offset)[e] = uint8_t(f32x2_to_e4m3x2(lo8_value(h, hb), 0.0f));
+                else
+                  dst[o.lo_offset + e] = f32_to_bf16_rn(h - bf16_to_f32(hb));
+              }
+            }
+          }
+        }
+      }
+    } else {
+      const int col = n0 + q * 32 + lane;
+      if (col < o.n_valid) {
+        float* dst = reinterpret_cast<float*>(o.out) + col;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          if (t < args.m) {
+            const float y = __uint_as_float(v[t]);
+            float* p = dst + size_t(t) * o.ldo;
+            if (args.ksplit > 1) asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(y) : "memory");
+            else if constexpr (EP == B200_EP_RESID_ADD) *p += y;
+            else *p = y;
+          }
+        }
+      }
+    }
+  } else {
+    // ---------------- weight unpack (256 threads): slot -> swizzled bf16 stage
+    if constexpr (SM::PACKED) {
+      const int t = threadIdx.x - GEMM_UNPACK_WARP0 * 32;
+      const int r = t >> 1, h = t & 1;  // one (row, 32-column half) unit per thread per k-block
+      const uint32_t row_sc =
+          FMT == B200_W_TERNARY ? uint32_t(__ldg(reinterpret_cast<const uint16_t*>(args.w.scales) + n0 + r)) : 0u;
+      const float row_gs = FMT == B200_W_NVFP4 ? __ldg(args.w.row_scale + n0 + r) : 1.0f;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % SK_STAGES, ws = i % SM::WSLOTS;
+        const uint32_t ph = (i / SK_STAGES) & 1, wph = (i / SM::WSLOTS) & 1;
+        mbar_wait(&full_w[ws], wph, FAULT_GEMM_WAIT_FULL_W);
+        mbar_wait(&empty[s], ph ^ 1, FAULT_GEMM_WAIT_EMPTY);
+        unpack_unit_smem<FMT>(sB + s * SM::B_BYTES, sW + ws * SM::W_BYTES, sS + ws * SM::S_BYTES, r, h, row_sc,
+                              row_gs, lut);
+        fence_proxy_async_smem();
+        mbar_arrive(&full_b[s]);
+        mbar_arrive(&empty_w[ws]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TM_COLS);
+  }
+}
+
 // --------------------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
@@ -972,6 +1230,59 @@ static int dispatch_simt(const uint16_t* x, const uint16_t* xl, int ldx, const G
   return B200_OK;
 }
 
+// The small-M kernel: K split so that about one unit per SM exists (the SwiGLU needs whole
+// sums and is never split); a split store first zeroes its output.
+template <int FMT, int EP, int PL, int NT>
+static int launch_skinny(const CUtensorMap& mx, const CUtensorMap& mx_lo, const CUtensorMap& mw, const GemmArgs& a,
+                         cudaStream_t st) {
+  using SM = SkinnySmem<FMT, PL, NT>;
+  static_assert(SM::TOTAL <= 227 * 1024, "small-M GEMM shared memory exceeds the 227 KB per-CTA limit");
+  static DeviceOnce attr;
+  const int r = once_per_device(attr, [](int) -> int {
+    SDB_CUDA(cudaFuncSetAttribute(gemm_skinny_kernel<FMT, EP, PL, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SM::TOTAL));
+    return B200_OK;
+  });
+  if (r != B200_OK) return r;
+  GemmArgs args = a;
+  const int tiles = a.w.n / SK_ROWS, nk = a.k / GEMM_BK;
+  args.ksplit = EP == B200_EP_SWIGLU ? 1 : std::max(1, std::min(sm_count() / tiles, nk / 2));
+  if (args.ksplit > 1 && EP == B200_EP_STORE)
+    SDB_CUDA(launch_pdl(zero_rows_kernel, dim3(a.m), dim3(256), 0, st, reinterpret_cast<float*>(a.o.out), a.o.ldo,
+                        a.o.n_valid));
+  SDB_CUDA(launch_pdl(gemm_skinny_kernel<FMT, EP, PL, NT>, dim3(tiles * args.ksplit), dim3(GEMM_THREADS), SM::TOTAL,
+                      st, mx, mx_lo, mw, args));
+  return B200_OK;
+}
+
+template <int FMT, int PL>
+static int dispatch_skinny_ep(const CUtensorMap& mx, const CUtensorMap& mx_lo, const CUtensorMap& mw,
+                              const GemmArgs& a, cudaStream_t st) {
+  const bool wide = a.m > 16;
+  switch (a.o.epilogue) {
+    case B200_EP_STORE:
+      return wide ? launch_skinny<FMT, B200_EP_STORE, PL, 64>(mx, mx_lo, mw, a, st)
+                  : launch_skinny<FMT, B200_EP_STORE, PL, 16>(mx, mx_lo, mw, a, st);
+    case B200_EP_RESID_ADD:
+      return wide ? launch_skinny<FMT, B200_EP_RESID_ADD, PL, 64>(mx, mx_lo, mw, a, st)
+                  : launch_skinny<FMT, B200_EP_RESID_ADD, PL, 16>(mx, mx_lo, mw, a, st);
+    default:
+      return wide ? launch_skinny<FMT, B200_EP_SWIGLU, PL, 64>(mx, mx_lo, mw, a, st)
+                  : launch_skinny<FMT, B200_EP_SWIGLU, PL, 16>(mx, mx_lo, mw, a, st);
+  }
+}
+
+template <int PL>
+static int dispatch_skinny(const CUtensorMap& mx, const CUtensorMap& mx_lo, const CUtensorMap& mw, const GemmArgs& a,
+                           cudaStream_t st) {
+  switch (a.w.format) {
+    case B200_W_BF16: return dispatch_skinny_ep<B200_W_BF16, PL>(mx, mx_lo, mw, a, st);
+    case B200_W_INT4G128: return dispatch_skinny_ep<B200_W_INT4G128, PL>(mx, mx_lo, mw, a, st);
+    case B200_W_NVFP4: return dispatch_skinny_ep<B200_W_NVFP4, PL>(mx, mx_lo, mw, a, st);
+    default: return dispatch_skinny_ep<B200_W_TERNARY, PL>(mx, mx_lo, mw, a, st);
+  }
+}
+
 }  // namespace sdb
 
 using namespace sdb;
@@ -989,6 +1300,23 @@ extern "C" int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m
   }
   GemmArgs a{*w, *out, m, k, 1};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (m <= SK_MAX_M) {  // small M: weights as the MMA's A operand, tokens as N (swap-AB)
+    const int nt = m > 16 ? 64 : 16;
+    CUtensorMap mx, mx_lo, mw;
+    if (int rc = make_act_map(&mx, x_hi, m, k, ldx, nt)) return rc;
+    if (x_lo) {
+      if (int rc = make_act_map(&mx_lo, x_lo, m, k, ldx, nt)) return rc;
+    } else {
+      mx_lo = mx;
+    }
+    if (w->format == B200_W_BF16) {
+      if (reinterpret_cast<uintptr_t>(w->data) & 15) return sdb_fail(B200_ERR_SHAPE, "b200_linear: bf16 W unaligned");
+      if (int rc = make_act_map(&mw, reinterpret_cast<const uint16_t*>(w->data), w->n, k, k, SK_ROWS)) return rc;
+    } else {
+      mw = mx;
+    }
+    return x_lo ? dispatch_skinny<PL_SPLIT>(mx, mx_lo, mw, a, st) : dispatch_skinny<PL_ONE>(mx, mx_lo, mw, a, st);
+  }
   if (w->format == B200_W_BF16) {  // the weight tile streams through TMA as [n, k] bf16, one box per N tile
     if (reinterpret_cast<uintptr_t>(w->data) & 15) return sdb_fail(B200_ERR_SHAPE, "b200_linear: bf16 W unaligned");
     if (pair_path(a)) {  // each CTA of a pair loads 128 of the tile's 256 weight rows

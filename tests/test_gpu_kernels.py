@@ -213,6 +213,54 @@ def test_linear_large_k_and_m_tail():
     assert (out.double().cpu() - ref).abs().max().item() / ref.abs().max().item() < 2e-5
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("m", [1, 16, 17, 64])
+@pytest.mark.parametrize("ep", ["store", "resid", "swiglu"])
+def test_linear_small_m_matches_reference(fmt, m, ep):
+    """Batches of at most 64 rows run the swap-AB kernel (weights as the MMA's 128-row A
+    operand, tokens as N = 16 or 64; split K for the store and residual epilogues, whole K with
+    the weight ring refilled for the SwiGLU): fp64 product of the same operands, and the CUDA-
+    core cross-check."""
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    k = 2048
+    _, xp = _planes(m, k, 40 + m)
+    if ep == "swiglu":
+        inter = 384
+        gate = W.quantize(fmt, _weights(inter, k, seed=41).cuda())
+        up = W.quantize(fmt, _weights(inter, k, seed=42).cuda())
+        pw = W.interleave_gate_up(gate, up)
+        ref = torch.nn.functional.silu(_reference(xp, gate)) * _reference(xp, up)
+        for fn in ("b200_linear", "b200_linear_simt"):
+            out, _ = _linear(fn, xp, pw, _lib.EP_SWIGLU, n_valid=2 * inter)
+            got = out[0].double().cpu() + out[1].double().cpu()
+            assert (got - ref).abs().max().item() / ref.abs().max().item() < 1e-4, fn
+        return
+    pw = W.concat_rows([W.quantize(fmt, _weights(736, k, seed=43).cuda())])   # 768 rows, 736 valid
+    ref = _reference(xp, pw)[:, :736]
+    e = _lib.EP_STORE if ep == "store" else _lib.EP_RESID_ADD
+    for fn in ("b200_linear", "b200_linear_simt"):
+        out, before = _linear(fn, xp, pw, e, n_valid=736)
+        got = out.double().cpu() - (before.double().cpu() if ep == "resid" else 0)
+        assert (got - ref).abs().max().item() < 2e-5 * ref.abs().max().item() + 1e-6, fn
+
+
+@pytest.mark.parametrize("split", [True, False])
+def test_linear_small_m_whole_k_with_weight_ring(split):
+    """96 weight tiles of 128 rows leave no room to split K: each CTA streams all 32 k-blocks
+    through its 16-slot weight ring (the refill path), one or two activation planes."""
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    m, k, n = 9, 2048, 12288
+    _, xp = _planes(m, k, 50)
+    pw = W.concat_rows([W.quantize("nvfp4", _weights(n, k, seed=51).cuda())])
+    ref = _reference(xp, pw, split=split)
+    out, _ = _linear("b200_linear", xp, pw, _lib.EP_STORE, split=split)
+    assert (out.double().cpu() - ref).abs().max().item() / ref.abs().max().item() < 2e-5
+
+
 def test_linear_rejects_bad_shapes():
     from strands_decider_b200 import _lib
     from strands_decider_b200 import weights as W

@@ -13,13 +13,18 @@ within 2e-3 (they are rounded to 4 places), the choices must match, and so must 
 
 The reference's CPU engine runs whole prompts (use_prefix_cache=False): under the installed
 transformers its shared-prefix path drops the cached GDN state, so it is not an oracle. The
-B200 engine is checked on both of its paths against it. Needs the reference package
-(tests/conftest.py says where it is looked for); skipped without it.
+B200 engine is checked on both of its paths against it. The reference runs in a child process
+that sees no GPU, as on a CPU host: with a GPU visible, transformers hands the Gated-DeltaNet
+scan of a CPU torso to flash-linear-attention's GPU kernels, which refuse CPU tensors. Needs
+the reference package (tests/conftest.py says where it is looked for); skipped without it.
 """
 
 from __future__ import annotations
 
+import json
 import os
+import subprocess
+import sys
 
 import pytest
 import torch
@@ -109,22 +114,49 @@ def _numbers(response) -> dict:
     return out
 
 
-@pytest.mark.parametrize("prefix", [False, True])
-def test_b200_engine_answers_as_the_reference_cpu_engine(checkpoint, prefix):
+def _reference_cpu_answers(checkpoint: str) -> dict:
+    """The reference CPU engine's answers and usage for every request, whole-prompt path, plus
+    the usage its shared-prefix path reports, from a child process with no GPU visible."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-m", "tests.test_gpu_reference_engine", checkpoint], cwd=root, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
+def _cpu_main(checkpoint: str) -> None:
+    from tests.conftest import require_reference as _ensure_path  # noqa: F401  (puts the reference on sys.path)
     from strands_decider.infer import load_engine as load_reference
 
+    whole = load_reference(checkpoint, device="cpu", use_prefix_cache=False)
+    shared = load_reference(checkpoint, device="cpu", use_prefix_cache=True)
+    out = {"answers": [], "usage_whole": [], "usage_shared": []}
+    for request in _requests():
+        resp = whole.evaluate(request)
+        out["answers"].append(_numbers(resp))
+        out["usage_whole"].append(resp.usage.model_dump())
+        out["usage_shared"].append(shared.evaluate(request).usage.model_dump())
+    print(json.dumps(out))
+
+
+@pytest.fixture(scope="module")
+def reference_answers(checkpoint):
+    return _reference_cpu_answers(checkpoint)
+
+
+@pytest.mark.parametrize("prefix", [False, True])
+def test_b200_engine_answers_as_the_reference_cpu_engine(checkpoint, reference_answers, prefix):
     from strands_decider_b200 import _lib
     from strands_decider_b200.engine import load_engine
 
-    cpu_whole = load_reference(checkpoint, device="cpu", use_prefix_cache=False)
-    cpu_same_path = load_reference(checkpoint, device="cpu", use_prefix_cache=prefix)
     b200 = load_engine(checkpoint, weight_format="bf16", use_prefix_cache=prefix, max_tokens=4096, pool_slots=4)
-    assert type(b200).evaluate is not None and "SystemOneEngine" in [c.__name__ for c in type(b200).__mro__]
-    for request in _requests():
-        want, got = cpu_whole.evaluate(request), b200.evaluate(request)
+    assert "SystemOneEngine" in [c.__name__ for c in type(b200).__mro__]
+    for i, request in enumerate(_requests()):
+        got = b200.evaluate(request)
         # the token count depends only on the path taken, not on its numerics
-        assert got.usage == cpu_same_path.evaluate(request).usage
-        w, g = _numbers(want), _numbers(got)
+        assert got.usage.model_dump() == reference_answers["usage_shared" if prefix else "usage_whole"][i]
+        w, g = reference_answers["answers"][i], _numbers(got)
         assert w.keys() == g.keys()
         for name in w:
             assert g[name][0] == pytest.approx(w[name][0], abs=TOL), (name, g[name], w[name])
@@ -147,3 +179,7 @@ def test_b200_engine_refuses_like_the_reference(checkpoint):
                           criteria={f"o{i}": f"option {i}" for i in range(b200.model.config.num_slots + 1)})
     with pytest.raises(ValueError, match="slots"):
         b200.evaluate(SystemOneRequest(state="a loan", questions={"q": many}))
+
+
+if __name__ == "__main__":   # the reference CPU engine's side, run by _reference_cpu_answers
+    _cpu_main(sys.argv[1])
