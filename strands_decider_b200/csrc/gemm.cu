@@ -769,62 +769,70 @@ __global__ void zero_rows_kernel(float* __restrict__ out, int ld, int n) {
 // microbench at M = 1 and 16): the weight tile is the MMA's A operand (M = 128 weight rows)
 // and the activations its B operand (N = NT = 16 or 64 token rows), so neither tensor work nor
 // shared memory goes to padding rows. One CTA = one 128-row weight tile over one K range (split
-// K across CTAs for the store / residual epilogues). Streaming the packed weights is the bound,
-// so the producer issues the bulk copies of the range's first SK_WSLOTS k-blocks (all of a
-// K range up to 1024) before it waits on the kernel before it in the stream (the weights do not
-// depend on that kernel), keeping up to ~70 KB per CTA in flight; the unpack warps decode each
-// k-block into a bf16 ring as it lands.
-//   warp 0      producer: packed weight k-blocks (1-D bulk copies into a ring of SK_WSLOTS
-//               slots, refilled as the unpack warps release them) and, per stage, the
-//               activation planes (TMA, NT rows x 64 k; rows past m read as zeros)
+// K across CTAs for the store / residual epilogues). Nothing in the main loop waits on a
+// round trip to memory once the data is in flight:
+//   * the producer issues the bulk copies of the range's first SK_WSLOTS packed weight k-blocks
+//     (all of a K range up to 1024) before it waits on the kernel before it in the stream (the
+//     weights do not depend on that kernel), then the activation tiles of up to SK_XSLOTS
+//     k-blocks at once (all of them for NT = 16);
+//   * two groups of 8 unpack warps decode alternate k-blocks into a 4-stage bf16 ring, so the
+//     fixed cost of one k-block's decode overlaps the next one's.
+//   warp 0      producer: packed weight k-blocks (1-D bulk copies into SK_WSLOTS slots,
+//               refilled as the unpack warps release them) and activation planes (TMA, NT rows
+//               x 64 k per k-block; rows past m read as zeros)
 //   warp 1      TMEM (max(NT, 32) columns) and the MMAs: per 16 k one tcgen05.mma per plane,
-//               M = 128, N = NT, A = the bf16 weight stage, B = the activation stage
+//               M = 128, N = NT, A = the bf16 weight stage, B = the activation slot
 //   warps 2..5  epilogue: TMEM lane = weight row (output column), column = token; a warp
 //               writes 32 consecutive outputs of a token at a time (fp32 store or residual
 //               add, split-K partials by red.add into a zeroed output or the residual, or
 //               SwiGLU: the up rows' two quarters hand their values to the gate rows' two
 //               quarters through shared memory)
-//   warps 6..13 unpack: weight slot -> swizzled K-major bf16 stage (unpack_unit_smem, the
-//               same decode as gemm_tc_kernel, bit-exact with b200_dequantize)
+//   warps 6..21 unpack, group (warp - 6) / 8 taking k-blocks of its parity: weight slot ->
+//               swizzled K-major bf16 stage (unpack_unit_smem, the same decode as
+//               gemm_tc_kernel, bit-exact with b200_dequantize)
 constexpr int SK_STAGES = 4;
 constexpr int SK_WSLOTS = 16;
 constexpr int SK_ROWS = 128;
 constexpr int SK_MAX_M = 64;
+constexpr int SK_UNPACK_GROUPS = 2;
+constexpr int SK_THREADS = GEMM_THREADS + (SK_UNPACK_GROUPS - 1) * GEMM_UNPACK_THREADS;  // 704
 
 template <int FMT, int PL, int NT>
 struct SkinnySmem {
   static_assert(PL != PL_LO8, "the small-M kernel takes one or two bf16 activation planes");
   static constexpr bool PACKED = FMT != B200_W_BF16;
-  static constexpr int X_BYTES = NT * GEMM_BK * 2;  // one activation plane of a stage
+  static constexpr int X_BYTES = NT * GEMM_BK * 2;  // one activation plane of one k-block
   static constexpr int X_STAGE = X_BYTES * (PL == PL_SPLIT ? 2 : 1);
+  static constexpr int XSLOTS = NT <= 16 ? 16 : 4;     // activation k-blocks held at once
   static constexpr int B_BYTES = SK_ROWS * GEMM_BK * 2;  // the unpacked bf16 weight stage
   static constexpr int W_BYTES = PACKED ? SK_ROWS * tile_row_bytes(FMT) : 0;
   static constexpr int S_BYTES = PACKED ? SK_ROWS * tile_scale_row_bytes(FMT) : 0;
   static constexpr int WSLOTS = PACKED ? SK_WSLOTS : 1;
   static constexpr int SWAP_BYTES = 2 * NT * 32 * 4;  // SwiGLU hand-over: 2 quarters x NT tokens x 32 rows
-  static constexpr int BARS = 2 * WSLOTS + 3 * SK_STAGES + 1;
-  static constexpr int TOTAL = SK_STAGES * (B_BYTES + X_STAGE) + WSLOTS * (W_BYTES + S_BYTES) + SWAP_BYTES +
+  static constexpr int BARS = 2 * WSLOTS + 2 * XSLOTS + 2 * SK_STAGES + 1;
+  static constexpr int TOTAL = SK_STAGES * B_BYTES + XSLOTS * X_STAGE + WSLOTS * (W_BYTES + S_BYTES) + SWAP_BYTES +
                                BARS * 8 + 16 + 64 + 1024;
   static_assert(X_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "128-byte-swizzled tiles need 1024-byte alignment");
 };
 
 template <int FMT, int EP, int PL, int NT>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(SK_THREADS, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmX_lo,
                        const __grid_constant__ CUtensorMap tmW, const GemmArgs args) {
   using SM = SkinnySmem<FMT, PL, NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sB = smem;                                // SK_STAGES x B_BYTES
-  uint8_t* sX = sB + SK_STAGES * SM::B_BYTES;        // SK_STAGES x X_STAGE
-  uint8_t* sW = sX + SK_STAGES * SM::X_STAGE;        // WSLOTS x W_BYTES
+  uint8_t* sX = sB + SK_STAGES * SM::B_BYTES;        // XSLOTS x X_STAGE
+  uint8_t* sW = sX + SM::XSLOTS * SM::X_STAGE;       // WSLOTS x W_BYTES
   uint8_t* sS = sW + SM::WSLOTS * SM::W_BYTES;       // WSLOTS x S_BYTES
   float* sSwap = reinterpret_cast<float*>(sS + SM::WSLOTS * SM::S_BYTES);  // [2][NT][32]
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sSwap) + SM::SWAP_BYTES);
   uint64_t* full_w = bars;                           // [WSLOTS] weight slot landed
   uint64_t* empty_w = bars + SM::WSLOTS;             // [WSLOTS] weight slot unpacked
-  uint64_t* full_x = bars + 2 * SM::WSLOTS;          // [STAGES] activation planes (and bf16 weights) landed
-  uint64_t* full_b = full_x + SK_STAGES;             // [STAGES] bf16 weight stage written
+  uint64_t* full_x = bars + 2 * SM::WSLOTS;          // [XSLOTS] activation slot (and bf16 weight stage) landed
+  uint64_t* empty_x = full_x + SM::XSLOTS;           // [XSLOTS] the slot's MMAs are done
+  uint64_t* full_b = empty_x + SM::XSLOTS;           // [STAGES] bf16 weight stage written
   uint64_t* empty = full_b + SK_STAGES;              // [STAGES] the stage's MMAs are done
   uint64_t* acc_full = empty + SK_STAGES;            // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
@@ -843,8 +851,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&full_w[i], 1);
       mbar_init(&empty_w[i], GEMM_UNPACK_THREADS);
     }
+    for (int i = 0; i < SM::XSLOTS; ++i) {
+      mbar_init(&full_x[i], 1);
+      mbar_init(&empty_x[i], 1);
+    }
     for (int s = 0; s < SK_STAGES; ++s) {
-      mbar_init(&full_x[s], 1);
       mbar_init(&full_b[s], GEMM_UNPACK_THREADS);
       mbar_init(&empty[s], 1);
     }
@@ -887,14 +898,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       pdl_wait();  // the activations come from the kernel before this one
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % SK_STAGES;
-        const uint32_t ph = (i / SK_STAGES) & 1;
-        mbar_wait(&empty[s], ph ^ 1, FAULT_GEMM_WAIT_EMPTY);
-        mbar_arrive_expect_tx(&full_x[s], SM::X_STAGE + (SM::PACKED ? 0 : SM::B_BYTES));
-        tma_load_2d(sX + s * SM::X_STAGE, &tmX, &full_x[s], (kb0 + i) * GEMM_BK, 0);
+        const int xs = i % SM::XSLOTS;
+        mbar_wait(&empty_x[xs], ((i / SM::XSLOTS) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
+        if constexpr (!SM::PACKED)  // bf16 weights stream straight into the stage
+          mbar_wait(&empty[i % SK_STAGES], ((i / SK_STAGES) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
+        mbar_arrive_expect_tx(&full_x[xs], SM::X_STAGE + (SM::PACKED ? 0 : SM::B_BYTES));
+        tma_load_2d(sX + xs * SM::X_STAGE, &tmX, &full_x[xs], (kb0 + i) * GEMM_BK, 0);
         if constexpr (PL == PL_SPLIT)
-          tma_load_2d(sX + s * SM::X_STAGE + SM::X_BYTES, &tmX_lo, &full_x[s], (kb0 + i) * GEMM_BK, 0);
-        if constexpr (!SM::PACKED) tma_load_2d(sB + s * SM::B_BYTES, &tmW, &full_x[s], (kb0 + i) * GEMM_BK, n0);
+          tma_load_2d(sX + xs * SM::X_STAGE + SM::X_BYTES, &tmX_lo, &full_x[xs], (kb0 + i) * GEMM_BK, 0);
+        if constexpr (!SM::PACKED)
+          tma_load_2d(sB + (i % SK_STAGES) * SM::B_BYTES, &tmW, &full_x[xs], (kb0 + i) * GEMM_BK, n0);
         if constexpr (SM::PACKED) {
           if (i + SM::WSLOTS < nkb) {  // refill slot i once its k-block is unpacked
             mbar_wait(&empty_w[i % SM::WSLOTS], (i / SM::WSLOTS) & 1, FAULT_GEMM_WAIT_EMPTY);
@@ -904,23 +917,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer: D[weight row][token] += W_stage . X_stage^T
+    // ---------------- MMA issuer: D[weight row][token] += W_stage . X_slot^T
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(SK_ROWS, NT);
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % SK_STAGES;
-        const uint32_t ph = (i / SK_STAGES) & 1;
-        mbar_wait(&full_x[s], ph, FAULT_GEMM_WAIT_FULL_A);
-        if constexpr (SM::PACKED) mbar_wait(&full_b[s], ph, FAULT_GEMM_WAIT_FULL_B);
+        const int s = i % SK_STAGES, xs = i % SM::XSLOTS;
+        mbar_wait(&full_x[xs], (i / SM::XSLOTS) & 1, FAULT_GEMM_WAIT_FULL_A);
+        if constexpr (SM::PACKED) mbar_wait(&full_b[s], (i / SK_STAGES) & 1, FAULT_GEMM_WAIT_FULL_B);
         tc_fence_after();
         const uint64_t ad = umma_desc_sw128(smem_addr(sB + s * SM::B_BYTES));
-        const uint64_t bd = umma_desc_sw128(smem_addr(sX + s * SM::X_STAGE));
+        const uint64_t bd = umma_desc_sw128(smem_addr(sX + xs * SM::X_STAGE));
 #pragma unroll
         for (int j = 0; j < GEMM_BK / 16; ++j) {  // +32 bytes of K per MMA = +2 in 16-byte units
           umma_bf16(tmem_base, ad + 2 * j, bd + 2 * j, idesc, (i != 0 || j != 0) ? 1u : 0u);
           if constexpr (PL == PL_SPLIT) umma_bf16(tmem_base, ad + 2 * j, bd + (SM::X_BYTES >> 4) + 2 * j, idesc, 1u);
         }
         umma_commit(&empty[s]);
+        umma_commit(&empty_x[xs]);
       }
       umma_commit(&acc_full[0]);
     }
@@ -993,18 +1006,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
   } else {
-    // ---------------- weight unpack (256 threads): slot -> swizzled bf16 stage
+    // ---------------- weight unpack: group g takes k-blocks g, g + 2, ... (slot -> bf16 stage)
     if constexpr (SM::PACKED) {
-      const int t = threadIdx.x - GEMM_UNPACK_WARP0 * 32;
+      const int ut = threadIdx.x - GEMM_UNPACK_WARP0 * 32;
+      const int grp = ut / GEMM_UNPACK_THREADS, t = ut % GEMM_UNPACK_THREADS;
       const int r = t >> 1, h = t & 1;  // one (row, 32-column half) unit per thread per k-block
       const uint32_t row_sc =
           FMT == B200_W_TERNARY ? uint32_t(__ldg(reinterpret_cast<const uint16_t*>(args.w.scales) + n0 + r)) : 0u;
       const float row_gs = FMT == B200_W_NVFP4 ? __ldg(args.w.row_scale + n0 + r) : 1.0f;
-      for (int i = 0; i < nkb; ++i) {
+      for (int i = grp; i < nkb; i += SK_UNPACK_GROUPS) {
         const int s = i % SK_STAGES, ws = i % SM::WSLOTS;
-        const uint32_t ph = (i / SK_STAGES) & 1, wph = (i / SM::WSLOTS) & 1;
-        mbar_wait(&full_w[ws], wph, FAULT_GEMM_WAIT_FULL_W);
-        mbar_wait(&empty[s], ph ^ 1, FAULT_GEMM_WAIT_EMPTY);
+        mbar_wait(&full_w[ws], (i / SM::WSLOTS) & 1, FAULT_GEMM_WAIT_FULL_W);
+        mbar_wait(&empty[s], ((i / SK_STAGES) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
         unpack_unit_smem<FMT>(sB + s * SM::B_BYTES, sW + ws * SM::W_BYTES, sS + ws * SM::S_BYTES, r, h, row_sc,
                               row_gs, lut);
         fence_proxy_async_smem();
@@ -1250,7 +1263,7 @@ static int launch_skinny(const CUtensorMap& mx, const CUtensorMap& mx_lo, const 
   if (args.ksplit > 1 && EP == B200_EP_STORE)
     SDB_CUDA(launch_pdl(zero_rows_kernel, dim3(a.m), dim3(256), 0, st, reinterpret_cast<float*>(a.o.out), a.o.ldo,
                         a.o.n_valid));
-  SDB_CUDA(launch_pdl(gemm_skinny_kernel<FMT, EP, PL, NT>, dim3(tiles * args.ksplit), dim3(GEMM_THREADS), SM::TOTAL,
+  SDB_CUDA(launch_pdl(gemm_skinny_kernel<FMT, EP, PL, NT>, dim3(tiles * args.ksplit), dim3(SK_THREADS), SM::TOTAL,
                       st, mx, mx_lo, mw, args));
   return B200_OK;
 }
