@@ -294,12 +294,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     for (int s = 0; s < SM::STAGES; ++s) {
       mbar_init(&full_a[s], 1);
       mbar_init(&full_w[s], 1);
-      mbar_init(&full_b[s], GEMM_UNPACK_THREADS);
+      mbar_init(&full_b[s], GEMM_UNPACK_THREADS / 32);  // one arrival per unpack warp
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4 * 32);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
     }
     mbar_fence_init();
   }
@@ -443,7 +443,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[ab]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
     }
   } else {
     // ---------------- weight unpack (256 threads): shared chunk -> swizzled bf16 tile
@@ -474,8 +475,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             unpack_unit_smem<FMT>(stage, sW + s * SM::W_BYTES, sS + s * SM::S_BYTES, u >> 1, u & 1, row_sc[i],
                                   row_gs[i], lut);
           }
+          // each thread makes its own stores visible to the tensor cores; then one arrival
+          // per warp (256 arrivals on one barrier would serialise for hundreds of cycles)
           fence_proxy_async_smem();
-          mbar_arrive(&full_b[s]);
+          __syncwarp();
+          if ((threadIdx.x & 31) == 0) mbar_arrive(&full_b[s]);
         }
       }
     }
@@ -849,14 +853,14 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < SM::WSLOTS; ++i) {
       mbar_init(&full_w[i], 1);
-      mbar_init(&empty_w[i], GEMM_UNPACK_THREADS);
+      mbar_init(&empty_w[i], GEMM_UNPACK_THREADS / 32);  // one arrival per unpack warp
     }
     for (int i = 0; i < SM::XSLOTS; ++i) {
       mbar_init(&full_x[i], 1);
       mbar_init(&empty_x[i], 1);
     }
     for (int s = 0; s < SK_STAGES; ++s) {
-      mbar_init(&full_b[s], GEMM_UNPACK_THREADS);
+      mbar_init(&full_b[s], GEMM_UNPACK_THREADS / 32);
       mbar_init(&empty[s], 1);
     }
     mbar_init(&acc_full[0], 1);
@@ -1020,9 +1024,12 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
         mbar_wait(&empty[s], ((i / SK_STAGES) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
         unpack_unit_smem<FMT>(sB + s * SM::B_BYTES, sW + ws * SM::W_BYTES, sS + ws * SM::S_BYTES, r, h, row_sc,
                               row_gs, lut);
-        fence_proxy_async_smem();
-        mbar_arrive(&full_b[s]);
-        mbar_arrive(&empty_w[ws]);
+        fence_proxy_async_smem();  // this thread's stores, visible to the tensor cores
+        __syncwarp();
+        if (lane == 0) {            // one arrival per warp
+          mbar_arrive(&full_b[s]);
+          mbar_arrive(&empty_w[ws]);
+        }
       }
     }
   }
