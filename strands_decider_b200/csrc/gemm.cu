@@ -813,6 +813,12 @@ struct SkinnySmem {
   static constexpr int S_BYTES = PACKED ? SK_ROWS * tile_scale_row_bytes(FMT) : 0;
   static constexpr int WSLOTS = PACKED ? SK_WSLOTS : 1;
   static constexpr int SWAP_BYTES = 2 * NT * 32 * 4;  // SwiGLU hand-over: 2 quarters x NT tokens x 32 rows
+  // Independent accumulators in TMEM, summed by the epilogue: an N = 16 MMA is a few cycles of
+  // tensor work, so one chain of dependent MMAs into a single accumulator would run at the
+  // MMA's latency; ACC chains run side by side. MMA j of a k-block (j = 0..3 per 16 k, plus 4
+  // for the low plane with 8 accumulators) feeds accumulator j % ACC.
+  static constexpr int ACC = NT <= 16 ? 8 : 4;
+  static constexpr int TM_COLS = ACC * NT < 32 ? 32 : ACC * NT;
   static constexpr int BARS = 2 * WSLOTS + 2 * XSLOTS + 2 * SK_STAGES + 1;
   static constexpr int TOTAL = SK_STAGES * B_BYTES + XSLOTS * X_STAGE + WSLOTS * (W_BYTES + S_BYTES) + SWAP_BYTES +
                                BARS * 8 + 16 + 64 + 1024;
@@ -841,7 +847,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   uint64_t* acc_full = empty + SK_STAGES;            // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   uint32_t* lut = tmem_slot + 4;                     // 16 words: ternary pair table
-  constexpr uint32_t TM_COLS = NT < 32 ? 32 : NT;
+  constexpr uint32_t TM_COLS = SM::TM_COLS;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = args.k / GEMM_BK;
@@ -933,8 +939,12 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
         const uint64_t bd = umma_desc_sw128(smem_addr(sX + xs * SM::X_STAGE));
 #pragma unroll
         for (int j = 0; j < GEMM_BK / 16; ++j) {  // +32 bytes of K per MMA = +2 in 16-byte units
-          umma_bf16(tmem_base, ad + 2 * j, bd + 2 * j, idesc, (i != 0 || j != 0) ? 1u : 0u);
-          if constexpr (PL == PL_SPLIT) umma_bf16(tmem_base, ad + 2 * j, bd + (SM::X_BYTES >> 4) + 2 * j, idesc, 1u);
+          const uint32_t acc_hi = tmem_base + uint32_t((j % SM::ACC) * NT);
+          const uint32_t acc_lo = tmem_base + uint32_t(((j + 4) % SM::ACC) * NT);
+          umma_bf16(acc_hi, ad + 2 * j, bd + 2 * j, idesc, i != 0 ? 1u : 0u);
+          if constexpr (PL == PL_SPLIT)
+            umma_bf16(acc_lo, ad + 2 * j, bd + (SM::X_BYTES >> 4) + 2 * j, idesc,
+                      (i != 0 || SM::ACC <= 4) ? 1u : 0u);
         }
         umma_commit(&empty[s]);
         umma_commit(&empty_x[xs]);
@@ -949,62 +959,67 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     mbar_wait(&acc_full[0], 0, FAULT_GEMM_WAIT_ACCUM);
     tc_fence_after();
     const uint32_t tl = tmem_base + (uint32_t(q * 32) << 16);
-    uint32_t v[TM_COLS];
-    {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tl, r);
-      tmem_ld_wait();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = r[j];
-    }
-    if constexpr (TM_COLS > 32) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tl + 32, r);
-      tmem_ld_wait();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[32 + j] = r[j];
-    }
     const b200_linear_out& o = args.o;
-    if constexpr (EP == B200_EP_SWIGLU) {
-      // rows 0..63 of the tile are gate features n0/2 .. n0/2 + 63, rows 64..127 the matching up
-      if (q >= 2) {
+    // accumulators used: all ACC with two planes or ACC == 4, else the first 4 (the hi plane's)
+    constexpr int USED = (PL == PL_SPLIT || SM::ACC <= 4) ? SM::ACC : 4;
+    constexpr int TC = NT < 32 ? NT : 32;  // tokens per chunk
+#pragma unroll 1
+    for (int t0 = 0; t0 < NT; t0 += TC) {
+      // the sum of the accumulators (their MMAs covered disjoint k) for tokens t0 .. t0 + TC - 1
+      float v[TC];
 #pragma unroll
-        for (int t = 0; t < NT; ++t) sSwap[((q - 2) * NT + t) * 32 + lane] = __uint_as_float(v[t]);
+      for (int t = 0; t < TC; ++t) v[t] = 0.0f;
+#pragma unroll
+      for (int a = 0; a < USED; a += 32 / TC) {  // one 32-column load covers 32 / TC accumulators
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tl + uint32_t(a * NT + t0), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          if (a + c / TC < USED) v[c % TC] += __uint_as_float(r[c]);
+        }
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
-      if (q < 2) {
-        const int ocol = n0 / 2 + q * 32 + lane;
-        if (2 * ocol < o.n_valid) {
-          uint16_t* dst = reinterpret_cast<uint16_t*>(o.out);
+      if constexpr (EP == B200_EP_SWIGLU) {
+        // rows 0..63 of the tile are gate features n0/2 .. n0/2 + 63, rows 64..127 the matching up
+        if (q >= 2) {
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            if (t < args.m) {
-              const float h = silu_approx(__uint_as_float(v[t])) * sSwap[(q * NT + t) * 32 + lane];
-              const uint16_t hb = f32_to_bf16_rn(h);
-              const size_t e = size_t(t) * o.ldo + ocol;
-              dst[e] = hb;
-              if (o.lo_offset) {
-                if (o.lo_format == B200_LO_E4M3)
-                  reinterpret_cast<uint8_t*>(dst + o.lo_offset)[e] = uint8_t(f32x2_to_e4m3x2(lo8_value(h, hb), 0.0f));
-                else
-                  dst[o.lo_offset + e] = f32_to_bf16_rn(h - bf16_to_f32(hb));
+          for (int t = 0; t < TC; ++t) sSwap[((q - 2) * NT + t0 + t) * 32 + lane] = v[t];
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+        if (q < 2) {
+          const int ocol = n0 / 2 + q * 32 + lane;
+          if (2 * ocol < o.n_valid) {
+            uint16_t* dst = reinterpret_cast<uint16_t*>(o.out);
+#pragma unroll
+            for (int t = 0; t < TC; ++t) {
+              if (t0 + t < args.m) {
+                const float h = silu_approx(v[t]) * sSwap[(q * NT + t0 + t) * 32 + lane];
+                const uint16_t hb = f32_to_bf16_rn(h);
+                const size_t e = size_t(t0 + t) * o.ldo + ocol;
+                dst[e] = hb;
+                if (o.lo_offset) {
+                  if (o.lo_format == B200_LO_E4M3)
+                    reinterpret_cast<uint8_t*>(dst + o.lo_offset)[e] =
+                        uint8_t(f32x2_to_e4m3x2(lo8_value(h, hb), 0.0f));
+                  else
+                    dst[o.lo_offset + e] = f32_to_bf16_rn(h - bf16_to_f32(hb));
+                }
               }
             }
           }
         }
-      }
-    } else {
-      const int col = n0 + q * 32 + lane;
-      if (col < o.n_valid) {
-        float* dst = reinterpret_cast<float*>(o.out) + col;
+      } else {
+        const int col = n0 + q * 32 + lane;
+        if (col < o.n_valid) {
+          float* dst = reinterpret_cast<float*>(o.out) + col;
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          if (t < args.m) {
-            const float y = __uint_as_float(v[t]);
-            float* p = dst + size_t(t) * o.ldo;
-            if (args.ksplit > 1) asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(y) : "memory");
-            else if constexpr (EP == B200_EP_RESID_ADD) *p += y;
-            else *p = y;
+          for (int t = 0; t < TC; ++t) {
+            if (t0 + t < args.m) {
+              float* p = dst + size_t(t0 + t) * o.ldo;
+              if (args.ksplit > 1) asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v[t]) : "memory");
+              else if constexpr (EP == B200_EP_RESID_ADD) *p += v[t];
+              else *p = v[t];
+            }
           }
         }
       }
