@@ -132,13 +132,15 @@ def _oracle_weights(spec: config.ModelSpec) -> dict:
 
 
 def cpu_baseline(spec: config.ModelSpec, wl: config.Workload, n_requests: int = 1, n_questions: int | None = None,
-                 full_prompt: bool = False) -> dict:
+                 full_prompt: bool = False, W: dict | None = None) -> dict:
     """The CPU oracle (a restatement of the reference's torso and readout) on a bounded
     sample of the same workload: the first n_requests requests (their first n_questions
     questions) through the prefix-cache path (state once, then each question against the
     state's cache) or, with full_prompt, each question as one full prompt; fp32 on all
-    host threads. Weights are fp32 tensors of the same shapes (the per-token arithmetic
-    does not depend on their values)."""
+    host threads. W: the oracle's weights (for a parity check, the device's own weights
+    dequantised by the oracle); by default fp32 tensors of the same shapes (the per-token
+    arithmetic does not depend on their values). The returned dict carries the sample's
+    probabilities under "_probs" (rows in request, question order)."""
     from oracle import head as OH
     from oracle import synth as osynth
     from oracle import torso as OT
@@ -147,7 +149,8 @@ def cpu_baseline(spec: config.ModelSpec, wl: config.Workload, n_requests: int = 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     cfg = osynth.torso_config(spec)
-    W = _oracle_weights(spec)
+    W = W if W is not None else _oracle_weights(spec)
+    probs = []
     reqs = synth.request_batch(wl, spec.vocab, 0, n_requests)
     decisions = 0
     tokens = 0
@@ -164,14 +167,26 @@ def cpu_baseline(spec: config.ModelSpec, wl: config.Workload, n_requests: int = 
                 hid, _ = OT.forward_sequence(cfg, W, torch.tensor(ids), cache=cache)
                 tokens += len(ids)
                 n = r["n_opts"][qi]
-                OH.decide(hid[-1:], W["embed"], torch.tensor([r["opt_ids"][qi]]), torch.tensor([n]),
-                          torch.tensor([1.0]))
+                probs.append(OH.decide(hid[-1:], W["embed"], torch.tensor([r["opt_ids"][qi]]), torch.tensor([n]),
+                                       torch.tensor([1.0]))[0])
                 decisions += 1
     dt = time.perf_counter() - t0
     path = "full prompts" if full_prompt else "prefix-cache path"
     return {"value": decisions / dt, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{n_requests} request(s) of {wl.name}, {decisions} decisions, {tokens} tokens, {path}, "
-                      f"fp32 torch on {cores} threads, {dt:.1f} s"}
+                      f"fp32 torch on {cores} threads, {dt:.1f} s", "_probs": probs}
+
+
+def parity_check(gpu_probs: torch.Tensor, cpu_probs: list[torch.Tensor], n_opts: list[int]) -> dict:
+    """The timed graphs' answers for the CPU sample's questions against the oracle's:
+    the largest probability difference and whether every choice (argmax) agrees."""
+    d, agree = 0.0, True
+    for i, (want, n) in enumerate(zip(cpu_probs, n_opts, strict=True)):
+        got = gpu_probs[i, :n].double()
+        d = max(d, float((got - want[:n].double()).abs().max()))
+        agree = agree and int(got.argmax()) == int(want[:n].argmax())
+    return {"max_dp": d, "argmax_equal": agree, "questions": len(cpu_probs), "tolerance": 2e-3,
+            "oracle": "fp32 CPU oracle on the device's weights (packed bytes read back, dequantised by oracle.quant)"}
 
 
 # ----------------------------------------------------------------------------- GPU arm
@@ -523,11 +538,70 @@ def attention_case(seqs: int, length: int):
 
 
 
+def small_kernels_case(tokens: int = 8192, rows: int = 384):
+    """One launch each of the kernels outside the GEMM / mixer / attention, at the 2B shapes:
+    the embedding gather (tokens ids of the 248320 x 2048 bf16 table), RMSNorm into two bf16
+    planes and into the e4m3 low-plane form (tokens x 2048 fp32), the option-token decision head
+    and the pointer-head readout (rows questions over a tokens x 2048 residual), and the weight
+    dequantiser and NVFP4 quantiser on the 12288 x 2048 gate/up weight."""
+    from strands_decider_b200 import synth
+    from strands_decider_b200.readout import DeviceReadout
+
+    spec = config.HYBRID_2B
+    H = spec.hidden
+    g = torch.Generator(device="cuda").manual_seed(0)
+    table = (torch.randn(spec.vocab, H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    ids = torch.randint(0, spec.vocab, (tokens,), device="cuda", dtype=torch.int32, generator=g)
+    x = torch.empty(tokens, H, device="cuda")
+    w_norm = 0.1 * torch.randn(H, device="cuda", generator=g)
+    planes = torch.empty(2, tokens, H, dtype=torch.bfloat16, device="cuda")
+    last = torch.randint(0, tokens, (rows,), device="cuda", dtype=torch.int32, generator=g)
+    opt = torch.arange(11, 14, device="cuda", dtype=torch.int32).repeat(rows, 1).contiguous()
+    nopt = torch.full((rows,), 3, device="cuda", dtype=torch.int32)
+    kinds = torch.arange(rows, device="cuda", dtype=torch.int32) % 3
+    temps = torch.ones(rows, device="cuda")
+    outs = [torch.empty(rows, 3, device="cuda"), torch.empty(rows, dtype=torch.int32, device="cuda"),
+            torch.empty(rows, device="cuda"), torch.empty(rows, device="cuda")]
+    opt_tok = torch.randint(0, tokens, (rows, 3), device="cuda", dtype=torch.int32, generator=g)
+    dec = _lib.DecideArgs(rows, 3, _lib.ptr(last), _lib.ptr(opt), _lib.ptr(nopt), _lib.ptr(kinds), _lib.ptr(temps),
+                          0.0, *[_lib.ptr(t) for t in outs], None)
+    dec_ptr = _lib.DecideArgs(rows, 3, _lib.ptr(last), _lib.ptr(opt), _lib.ptr(nopt), _lib.ptr(kinds), _lib.ptr(temps),
+                              0.0, *[_lib.ptr(t) for t in outs], _lib.ptr(opt_tok))
+    head = DeviceReadout("pointer", synth.readout_params("pointer", H, 256, seed=1), H)
+    hs = head.struct()
+    wlat = torch.randn(2 * spec.inter, H, device="cuda", generator=g) * 0.02
+    pw = WT.quantize("nvfp4", wlat)
+    qw = pw.qweight()
+    wbf = torch.empty(2 * spec.inter, H, dtype=torch.bfloat16, device="cuda")
+    qd = torch.empty_like(pw.data)
+    qs = torch.empty_like(pw.scales)
+    qr = torch.empty_like(pw.row_scale)
+    keep = (table, ids, x, w_norm, planes, last, opt, nopt, kinds, temps, outs, opt_tok, head, pw, wbf, qd, qs, qr)
+    st = _lib.stream_ptr()
+
+    def launch():
+        k = keep
+        _lib.call("b200_embed", _lib.ptr(k[1]), tokens, _lib.ptr(k[0]), H, _lib.ptr(k[2]), st)
+        _lib.call("b200_rmsnorm", _lib.ptr(k[2]), tokens, H, _lib.ptr(k[3]), 1e-6, _lib.ptr(k[4]), tokens * H, st)
+        _lib.call("b200_rmsnorm_lo8", _lib.ptr(k[2]), tokens, H, _lib.ptr(k[3]), 1e-6, _lib.ptr(k[4]), tokens * H, st)
+        _lib.call("b200_decide", _lib.ptr(k[2]), H, _lib.ptr(k[3]), 1e-6, _lib.ptr(k[0]), C.byref(dec), st)
+        _lib.call("b200_decide_readout", _lib.ptr(k[2]), H, _lib.ptr(k[3]), 1e-6, C.byref(hs), C.byref(dec_ptr), tokens,
+                  st)
+        _lib.call("b200_dequantize", C.byref(qw), _lib.ptr(k[14]), st)
+        _lib.call("b200_quantize", _lib.FMT["nvfp4"], _lib.ptr(wlat), 2 * spec.inter, H, _lib.ptr(k[15]),
+                  _lib.ptr(k[16]), _lib.ptr(k[17]), st)
+
+    return launch, None
+
+
 def run_case(args) -> None:
     if not torch.cuda.is_available():
         raise SystemExit("--case needs a CUDA device")
     _lib.load()
-    if args.case == "gemm":
+    if args.case == "small":
+        launch, flops = small_kernels_case()
+        label = "embed, rmsnorm (bf16 / e4m3 low plane), decide, pointer readout, dequantise, quantise (2B shapes)"
+    elif args.case == "gemm":
         launch, flops = gemm_case(args.m, args.fmt, args.ep, args.n, args.k, args.planes)
         label = f"gemm {args.fmt} {args.ep} {args.planes} M={args.m} N={args.n} K={args.k}"
     elif args.case == "gdn":
@@ -750,6 +824,8 @@ def latency(args) -> None:
         return v[min(len(v) - 1, int(q * len(v)))]
 
     cb = cpu_baseline(spec, wl, 1, full_prompt=True) if args.cpu_sample > 0 else None
+    if cb:
+        cb.pop("_probs")
     # Latency roofline: the forward must stream every linear's ternary weights (2 bits each) from
     # HBM once; its algorithmic FLOPs (2 x params x tokens) at the bf16 peak are the other bound.
     pk = peaks()
@@ -792,7 +868,8 @@ def main() -> None:
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
     ap.add_argument("--lo-plane", default="e4m3", choices=["bf16", "e4m3"],
                     help="low activation plane of the large-batch GEMMs (DecisionModel lo_plane)")
-    ap.add_argument("--case", choices=["gemm", "gdn", "attention"], help="time (and profile) one kernel alone")
+    ap.add_argument("--case", choices=["gemm", "gdn", "attention", "small"],
+                    help="time (and profile) one kernel alone (small: the head, norm, embedding and (de)quantisers)")
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--fmt", default="nvfp4", choices=list(config.WEIGHT_FORMATS))
     ap.add_argument("--ep", default="swiglu", choices=["swiglu", "store", "resid"])
@@ -822,6 +899,7 @@ def main() -> None:
             if rank == 0:
                 spec, wl = config.HYBRID_2B.with_format("ternary"), config.LATENCY_WORKLOAD
                 cb = cpu_baseline(spec, wl, 1, full_prompt=True)
+                cb.pop("_probs")
                 ms = 1e3 / cb["value"]
                 print(json.dumps({"metric": METRIC, "value": round(ms, 2), "unit": "ms", "impl": "reference",
                                   "higher_is_better": False, "config": {"workload": wl.name, "model": spec.name},
@@ -840,6 +918,7 @@ def main() -> None:
             return
         n_q = None if wl.n_questions <= 3 else 4
         cb = cpu_baseline(spec, wl, max(args.cpu_sample, 1), n_questions=n_q, full_prompt=not prefix)
+        cb.pop("_probs")
         line = {"metric": METRIC, "value": round(cb["value"], 4), "unit": UNIT, "impl": "reference",
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -878,9 +957,10 @@ def main() -> None:
     max_tok = max(max(b.n_state_tokens, b.n_suffix_tokens) for b in batches)
     slots = R if prefix else 1
     kv = max(b.n_state_tokens for b in batches) if prefix else 1
-    weights = DeviceWeights.synthetic(spec, seed=0, device="cuda", latent_device="cuda")
+    parity = world == 1 and args.cpu_sample > 0
+    weights = DeviceWeights.synthetic(spec, seed=0, device="cuda", latent_device="cuda", keep_logical=parity)
     model = DecisionModel(weights, max_tokens=max_tok, pool_slots=slots, pool_kv_tokens=max(kv, 1),
-                          lo_plane=args.lo_plane)
+                          lo_plane=args.lo_plane, graphs=False)
     stream = torch.cuda.current_stream()
     use_graph = not args.no_graph
     graphs = [StepGraph(model, b) for b in batches] if use_graph else None
@@ -942,6 +1022,8 @@ def main() -> None:
     ms_e2e = f0.elapsed_time(f1)
     clk = clocks.stop()
 
+    # the timed graphs' last answers for the first batch (its first requests are the CPU sample's)
+    b0_probs = (graphs[0].out.probs if use_graph else run_step(model, batches[0], stream).probs).cpu()
     t = torch.tensor([ms, ms_e2e, float(decisions), float(tokens)], device="cuda")
     if world > 1:
         g = [torch.zeros_like(t) for _ in range(world)]
@@ -963,12 +1045,22 @@ def main() -> None:
         dist.destroy_process_group()
     if rank != 0:
         return
-    cb = None
-    if world == 1 and args.cpu_sample > 0:
+    cb, par = None, None
+    if parity:
+        from oracle import synth as osynth
+
+        W = osynth.device_logical_weights(weights, seed=0)
         del model, weights
         torch.cuda.empty_cache()
         n_q = None if wl.n_questions <= 3 else 4
-        cb = cpu_baseline(spec, wl, args.cpu_sample, n_questions=n_q, full_prompt=not prefix)
+        cb = cpu_baseline(spec, wl, args.cpu_sample, n_questions=n_q, full_prompt=not prefix, W=W)
+        del W
+        sample = [r for r in reqs_all[: args.cpu_sample]]
+        assert all(r["id"] == i for i, r in enumerate(sample)) and batches[0].prefix == prefix
+        rows = [i * wl.n_questions + q for i in range(len(sample)) for q in range(n_q or wl.n_questions)]
+        assert shards[0][: len(sample)] == list(range(len(sample)))   # batch 0 starts with the sample
+        par = parity_check(b0_probs[rows], cb.pop("_probs"),
+                           [r["n_opts"][q] for r in sample for q in range(n_q or wl.n_questions)])
     b0 = batches[0]
     fl = 2.0 * spec.linear_params() * total_tok
     line = {
@@ -988,7 +1080,7 @@ def main() -> None:
         "gpu_launches": sum(((launches_per_forward(spec, False, b.n_state_tokens, True, args.lo_plane) if prefix else 0)
                              + launches_per_forward(spec, True, b.n_suffix_tokens, lo_plane=args.lo_plane))
                             for b in (batches[(args.warmup + i) % len(batches)] for i in range(args.steps))) * world,
-        "roofline": roof, "clocks": clk, "cpu_baseline": cb,
+        "roofline": roof, "clocks": clk, "cpu_baseline": cb, "parity": par,
     }
     print(json.dumps(line), flush=True)
 
