@@ -771,11 +771,12 @@ def _kmax(wl: config.Workload) -> int:
     return wl.option_range[1] if wl.option_range else max(wl.options)
 
 
-def latency(args) -> None:
+def latency(args, emit: bool = True, cpu: bool = True) -> dict:
     """p50 / p99 single-request latency: one 96-token request (93-token state + 3-token
     question, one 3-way choice) as one full-prompt forward of the ternary 2B-shape decider,
     CUDA-graphed, each replay timed alone with CUDA events (inputs resident; e2e adds the
-    96 ids' upload and the answer's download to every replay)."""
+    96 ids' upload and the answer's download to every replay). Returns the JSON line (printed
+    when emit); cpu=False leaves out the CPU baseline."""
     from strands_decider_b200 import _lib
     from strands_decider_b200.runtime import DecisionModel
     from strands_decider_b200.synth import request_batch
@@ -823,7 +824,7 @@ def latency(args) -> None:
     def pct(v, q):
         return v[min(len(v) - 1, int(q * len(v)))]
 
-    cb = cpu_baseline(spec, wl, 1, full_prompt=True) if args.cpu_sample > 0 else None
+    cb = cpu_baseline(spec, wl, 1, full_prompt=True) if (cpu and args.cpu_sample > 0) else None
     if cb:
         cb.pop("_probs")
     # Latency roofline: the forward must stream every linear's ternary weights (2 bits each) from
@@ -853,7 +854,11 @@ def latency(args) -> None:
             "cpu_baseline": cb}
     if cb:
         cb["ms_per_request"] = round(1e3 / cb["value"], 1)
-    print(json.dumps(line), flush=True)
+    if emit:
+        print(json.dumps(line), flush=True)
+    del g, model, weights
+    torch.cuda.empty_cache()
+    return line
 
 
 def main() -> None:
@@ -866,6 +871,9 @@ def main() -> None:
     ap.add_argument("--requests-per-step", type=int, default=0, help="0 = the workload's default")
     ap.add_argument("--cpu-sample", type=int, default=3, help="requests in the CPU baseline sample (0 = skip)")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
+    ap.add_argument("--extras", action=argparse.BooleanOptionalAction, default=True,
+                    help="one GPU, default workload: add the int4 GEMM microbench summary and the "
+                         "single-request latency to the line")
     ap.add_argument("--lo-plane", default="e4m3", choices=["bf16", "e4m3"],
                     help="low activation plane of the large-batch GEMMs (DecisionModel lo_plane)")
     ap.add_argument("--case", choices=["gemm", "gdn", "attention", "small"],
@@ -1040,6 +1048,17 @@ def main() -> None:
     del graphs
     roof = gemm_roofline(model, batches[0].n_state_tokens or batches[0].n_suffix_tokens, pk) if rank == 0 else None
     assert _lib.read_fault() == 0
+    extras = {}
+    if world == 1 and args.extras and args.workload == "nvfp4":
+        # the int4 GEMM microbench and the single-request latency, measured in the same run
+        extras["c2_gemm"] = [{k: r[k] for k in ("m", "n", "us", "bound", "roofline_us", "frac", "path")}
+                             for r in c2_gemm(pk, reps=30, check=False)]
+        lat = latency(args, emit=False, cpu=False)
+        extras["latency"] = {"workload": lat["config"]["workload"], "p50_ms": lat["latency_ms"]["p50"],
+                             "p99_ms": lat["latency_ms"]["p99"], "e2e_p50_ms": lat["e2e"]["value"],
+                             "roofline": {k: lat["roofline"][k] for k in ("bound", "frac", "hbm_bound_ms",
+                                                                           "mma_bound_ms")},
+                             "clocks": lat["clocks"]}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1080,7 +1099,7 @@ def main() -> None:
         "gpu_launches": sum(((launches_per_forward(spec, False, b.n_state_tokens, True, args.lo_plane) if prefix else 0)
                              + launches_per_forward(spec, True, b.n_suffix_tokens, lo_plane=args.lo_plane))
                             for b in (batches[(args.warmup + i) % len(batches)] for i in range(args.steps))) * world,
-        "roofline": roof, "clocks": clk, "cpu_baseline": cb, "parity": par,
+        "roofline": roof, "clocks": clk, "cpu_baseline": cb, "parity": par, **extras,
     }
     print(json.dumps(line), flush=True)
 
