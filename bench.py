@@ -744,6 +744,81 @@ def c2_gemm(pk: dict, reps: int = 50, check: bool = True) -> list[dict]:
     return out
 
 
+def c2_native_fp4(pk: dict, reps: int = 50) -> list[dict]:
+    """The native NVFP4 (W4A4) GEMM at the microbench's shapes: W the same N(0, 0.02) latent
+    quantised to NVFP4, x bf16 N(0, 1) quantised to NVFP4 activations (b200_quantize_act_nvfp4,
+    timed apart), y fp32, b200_linear_nvfp4_native, 50 launches on rotating weight copies in one
+    CUDA graph. The tensor bound is taken at 4 x the measured bf16 GEMM peak (the dense e2m1 :
+    bf16 tensor-rate ratio, 9 : 2.25 PFLOP/s nominal)."""
+    torch.cuda.set_device(0)
+    st = torch.cuda.current_stream()
+    fp4_peak = 4 * pk["bf16_tflops"]
+    out = []
+
+    def gtime(fn):
+        for i in range(3):
+            fn(i, st)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            cs = torch.cuda.current_stream()
+            for i in range(reps):
+                fn(3 + i, cs)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        graph.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps * 1e3
+
+    for n in sorted({n for _, n in C2_SHAPES}, reverse=True):
+        g = torch.Generator(device="cuda").manual_seed(n)
+        base = WT.quantize("nvfp4", torch.randn(n, C2_K, device="cuda", generator=g) * 0.02)
+        nb = C.c_size_t()
+        _lib.check(_lib.load().b200_nvfp4_sf_atom_bytes(n, C2_K, C.byref(nb)))
+        atoms = torch.empty(nb.value, dtype=torch.uint8, device="cuda")
+        _lib.call("b200_nvfp4_sf_atoms", _lib.ptr(base.scales), n, C2_K, _lib.ptr(atoms), st.cuda_stream)
+        per_copy = base.data.numel() + atoms.numel()
+        ncop = max(1, int(2 * 126e6 * 1.2 // per_copy))
+        copies = [(WT.PackedWeight("nvfp4", n, C2_K, base.data.clone(), base.scales, base.row_scale), atoms.clone())
+                  for _ in range(ncop)]
+        qws = [(c.qweight(), a) for c, a in copies]
+        for m, nn in C2_SHAPES:
+            if nn != n:
+                continue
+            x = torch.randn(m, C2_K, device="cuda", generator=g).to(torch.bfloat16).float()
+            codes = torch.empty(m, C2_K // 2, dtype=torch.uint8, device="cuda")
+            _lib.check(_lib.load().b200_nvfp4_sf_atom_bytes(m, C2_K, C.byref(nb)))
+            xsf = torch.empty(nb.value, dtype=torch.uint8, device="cuda")
+            y = torch.empty(m, n, device="cuda")
+            o = _lib.LinearOut(_lib.EP_STORE, n, _lib.ptr(y), n, 0, 0)
+
+            def quant(i, stream):
+                _lib.call("b200_quantize_act_nvfp4", _lib.ptr(x), m, C2_K, C2_K, _lib.ptr(codes), _lib.ptr(xsf),
+                          stream.cuda_stream)
+
+            def gemm(i, stream):
+                qw, wa = qws[i % len(qws)]
+                _lib.call("b200_linear_nvfp4_native", _lib.ptr(codes), _lib.ptr(xsf), m, C2_K, C.byref(qw),
+                          _lib.ptr(wa), C.byref(o), stream.cuda_stream)
+
+            quant(0, st)
+            us_q, us = gtime(quant), gtime(gemm)
+            nbytes = n * C2_K // 2 + n * C2_K // 16 + m * C2_K // 2 + m * C2_K // 16 + 4 * m * n
+            flops = 2.0 * m * n * C2_K
+            t_hbm = nbytes / (pk["hbm_gbs"] * 1e9) * 1e6
+            t_mma = flops / (fp4_peak * 1e12) * 1e6
+            out.append({"m": m, "n": n, "us": round(us, 3), "us_act_quant": round(us_q, 3),
+                        "tflops": round(flops / us / 1e6, 1), "bound": "hbm" if t_hbm >= t_mma else "tensor",
+                        "roofline_us": round(max(t_hbm, t_mma), 3), "frac": round(max(t_hbm, t_mma) / us, 3)})
+        del copies, qws
+        torch.cuda.empty_cache()
+    assert _lib.read_fault() == 0
+    return out
+
+
 def c2_main(args) -> None:
     pk = peaks()
     shapes = c2_gemm(pk, reps=max(args.steps, 20))
@@ -754,7 +829,11 @@ def c2_main(args) -> None:
             "config": {"workload": "int4-gemm-microbench", "k": C2_K, "m": [1, 16, 256, 4096], "n": [6144, 2048],
                        "l2": "weight copies rotated per launch (together > 2 x L2)",
                        "peaks": f"{pk['src']}: HBM {pk['hbm_gbs']} GB/s, bf16 {pk['bf16_tflops']} TFLOP/s"},
-            "shapes": shapes}
+            "shapes": shapes,
+            "nvfp4_native": {"what": "W4A4 on the block-scaled tensor cores (kind::mxf4nvf4); activations "
+                                     "quantised to NVFP4 first (us_act_quant); not the runtime's path (4-bit "
+                                     "activations move the decider's probabilities by up to 0.5)",
+                             "peak_tflops": 4 * pk["bf16_tflops"], "shapes": c2_native_fp4(pk, reps=max(args.steps, 20))}}
     print(json.dumps(line), flush=True)
 
 

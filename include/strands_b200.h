@@ -142,6 +142,31 @@ int b200_linear_lo8(const uint16_t* x_hi, const uint8_t* x_lo8, int32_t m, int32
 int b200_linear_simt(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m, int32_t k, int32_t ldx,
                      const b200_qweight* w, const b200_linear_out* out, b200_stream stream);
 
+/* ---------------------------------------------------------------- native NVFP4 (W4A4)
+ * The block-scaled tensor-core path (tcgen05.mma kind::mxf4nvf4): activations AND weights in
+ * NVFP4, y[t, n] = row_scale[n] * sum over 16-blocks b of sa[t, b] * sw[n, b] * sum e2m1 a * e2m1 w.
+ * Replaces the same `nn.Linear` calls as b200_linear (TF:417-420, TF:632-643, TF:701-703), at
+ * four times the bf16 tensor rate, but with 4-bit activations: on the 2B-shape decider that
+ * moves option probabilities by up to 0.5 against the fp32 reference, far outside the 2e-3
+ * bar, so the model runtime does not use it; it is offered for callers that accept W4A4.
+ * Scale factors travel in 512-byte atoms per 128 rows and 64 k: byte 16*(r%32) + 4*((r%128)/32)
+ * + (b%4) of atom [r/128][b/4] holds the unsigned-e4m3 scale of row r, 16-block b. */
+/* Bytes of scale atoms for a [rows, k] NVFP4 matrix (rows rounded up to 128; k % 64 == 0). */
+int b200_nvfp4_sf_atom_bytes(int32_t rows, int32_t k, size_t* bytes);
+/* Activation quantiser: x fp32 [m, ldx] -> codes uint8 [m, k/2] (element k in the low nibble of
+ * byte k/2 when k is even) and scale atoms (rows m .. round_up(m, 128) written as zeros).
+ * Per 16-block: scale byte = e4m3_rn_sat(amax / 6), code = e2m1_rn_sat(x / scale), 0 for a zero
+ * scale. No tensor scale (block maxima from about 3e-3 to 2688 are representable). */
+int b200_quantize_act_nvfp4(const float* x, int32_t m, int32_t k, int32_t ldx, uint8_t* codes, uint8_t* sf_atoms,
+                            b200_stream stream);
+/* A packed NVFP4 weight's scales [rows][k/16] (rows % 128 == 0) -> scale atoms. */
+int b200_nvfp4_sf_atoms(const uint8_t* scales, int32_t rows, int32_t k, uint8_t* sf_atoms, b200_stream stream);
+/* y = x @ W^T on the block-scaled MMA: x as b200_quantize_act_nvfp4 left it, W a B200_W_NVFP4
+ * weight (data, row_scale) with its scale atoms w_sf; k % 256 == 0, n % 128 == 0. Epilogues and
+ * n_valid rules as b200_linear (SwiGLU writes bf16 planes). */
+int b200_linear_nvfp4_native(const uint8_t* x_codes, const uint8_t* x_sf, int32_t m, int32_t k, const b200_qweight* w,
+                             const uint8_t* w_sf, const b200_linear_out* out, b200_stream stream);
+
 /* ---------------------------------------------------------------- ragged batches, prefix cache */
 typedef struct b200_seqs {
   int32_t n_seqs;

@@ -248,6 +248,59 @@ def dequantize_nvfp4(packed: np.ndarray, sb: np.ndarray, gs: float) -> np.ndarra
     return lut[sbe * 16 + codes]
 
 
+# ----------------------------------------------------------------------------- NVFP4 activations (W4A4)
+# The block-scaled tensor-core path quantises the activations too. Per row and 16-block of
+# an activation x [M, K]: scale byte sb = e4m3_rn_sat(amax / 6) (fp32 divide; no tensor scale),
+# code = e2m1_rn_sat(x / e4m3_value(sb)) (fp32 divide), 0 where the scale is 0; packed as the
+# weights are. The MMA then forms, in fp32, sum_b sa[t, b] * sw[n, b] * sum e2m1(a) * e2m1(w)
+# over each 16-block b, and the epilogue multiplies by the weight's tensor scale: every product
+# is exact, so an fp64 sum is the reference (the device differs by fp32 accumulation only).
+
+
+def quantize_act_nvfp4(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """x fp32 [M, K] -> (packed uint8 [M, K/2], scale bytes uint8 [M, K/16])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m, k = x.shape
+    assert k % NVFP4_BLOCK == 0
+    b = x.reshape(m, k // NVFP4_BLOCK, NVFP4_BLOCK)
+    sb = e4m3_encode((np.abs(b).max(axis=2) / np.float32(6.0)).astype(np.float32))
+    s = e4m3_decode(sb)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        v = (b / s[:, :, None]).astype(np.float32)
+    v = np.where(s[:, :, None] == 0, np.float32(0), v)
+    codes = e2m1_encode(v).reshape(m, k)
+    return (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8), sb
+
+
+def nvfp4_sf_atoms(scales: np.ndarray) -> np.ndarray:
+    """Scale bytes [rows, K/16] -> the 512-byte atoms the block-scaled MMA reads, rows padded
+    with zero scales to a multiple of 128: byte 16 (r % 32) + 4 ((r % 128) / 32) + (b % 4) of
+    atom [r / 128][b / 4] is the scale of row r, 16-block b."""
+    scales = np.asarray(scales, dtype=np.uint8)
+    rows, nb = scales.shape
+    rp = (rows + 127) // 128 * 128
+    pad = np.zeros((rp, nb), np.uint8)
+    pad[:rows] = scales
+    # [tile, m1, m0, atom, j] -> [tile, atom, m0, m1, j]
+    a = pad.reshape(rp // 128, 4, 32, nb // 4, 4).transpose(0, 3, 2, 1, 4)
+    return np.ascontiguousarray(a).reshape(-1)
+
+
+def nvfp4_values(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """e2m1 code x its block's e4m3 scale, exactly, as float64 [rows, K]."""
+    codes = unpack_nvfp4(packed)
+    rows, k = codes.shape
+    v = e2m1_decode(codes).astype(np.float64).reshape(rows, k // NVFP4_BLOCK, NVFP4_BLOCK)
+    return (v * e4m3_decode(scales).astype(np.float64)[:, :, None]).reshape(rows, k)
+
+
+def nvfp4_native_product(act_packed, act_scales, w_packed, w_scales, w_gs) -> np.ndarray:
+    """What the block-scaled GEMM computes, in float64: x_q @ w_q^T times the weight's tensor
+    scale (w_gs: a scalar or one value per weight row)."""
+    y = nvfp4_values(act_packed, act_scales) @ nvfp4_values(w_packed, w_scales).T
+    return y * np.asarray(w_gs, dtype=np.float64).reshape(1, -1)
+
+
 # ----------------------------------------------------------------------------- ternary
 
 

@@ -128,6 +128,10 @@ _SIGS = {
     "b200_attention_noalloc": ([C.POINTER(AttnParams), C.POINTER(Seqs), _P, _I, _P, C.c_int64,
                                 C.POINTER(PrefixPool), _I, _P], C.c_int),
     "b200_decide": ([_P, _I, _P, C.c_float, _P, C.POINTER(DecideArgs), _P], C.c_int),
+    "b200_nvfp4_sf_atom_bytes": ([_I, _I, C.POINTER(C.c_size_t)], C.c_int),
+    "b200_quantize_act_nvfp4": ([_P, _I, _I, _I, _P, _P, _P], C.c_int),
+    "b200_nvfp4_sf_atoms": ([_P, _I, _I, _P, _P], C.c_int),
+    "b200_linear_nvfp4_native": ([_P, _P, _I, _I, C.POINTER(QWeight), _P, C.POINTER(LinearOut), _P], C.c_int),
     "b200_decide_readout": ([_P, _I, _P, C.c_float, C.POINTER(Readout), C.POINTER(DecideArgs), _I, _P], C.c_int),
     "b200_model_create": ([C.POINTER(ModelConfig), C.POINTER(C.c_void_p)], C.c_int),
     "b200_model_destroy": ([_P], C.c_int),

@@ -49,6 +49,8 @@ class _Linear:
         how = self.mode.get(self.cls)
         if how == "lo8":
             return _lo8_product(x, self.w)
+        if how == "nvfp4":
+            return _nvfp4_act(x) @ self.w.T
         x = _bf16(x) if how == "bf16" else _planes(x) if how == "planes" else x
         return x @ self.w.T
 
@@ -63,6 +65,15 @@ def _lo8_product(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     e4m3(2^6 (x - hi)) against the e4m3 weight copy e4m3(2^6 W), both scaled back."""
     hi = _bf16(x)
     return hi @ w.T + _e4m3(x - hi, 6) @ _e4m3(w, 6).T
+
+
+def _nvfp4_act(x: torch.Tensor) -> torch.Tensor:
+    """The activation as the block-scaled NVFP4 MMA sees it (e2m1 x e4m3 scale per 16)."""
+    from oracle import quant as Q
+
+    flat = x.reshape(-1, x.shape[-1]).float().numpy()
+    c, s = Q.quantize_act_nvfp4(flat)
+    return torch.from_numpy(Q.nvfp4_values(c, s).astype(np.float32)).reshape(x.shape)
 
 
 def _wrap(W, mode):
@@ -115,3 +126,11 @@ def test_e4m3_low_plane_everywhere_meets_the_bar(case):
     """The large-batch default: hi plane in bf16, low plane and its weight copy in e4m3
     (about 2.9e-4 here, 7x inside the bar; 6.9e-4 on the 2B-shape decider)."""
     assert _err(case, {c: "lo8" for c in ("in_proj", "out_proj", "gate_up", "down")}) < TOL / 4
+
+
+def test_nvfp4_activations_miss_the_bar_by_far(case):
+    """The native NVFP4 (W4A4) tensor-core path quantises every GEMM input to e2m1 with an
+    e4m3 scale per 16: on the reduced decider that alone moves a probability by far more than
+    the bar (on the 2B-shape decider, 3 x 512 tokens, by 0.51, with every argmax changed), so
+    the runtime keeps 4-bit weights with hi + lo activation planes."""
+    assert _err(case, {c: "nvfp4" for c in ("in_proj", "out_proj", "gate_up", "down")}) > 10 * TOL
