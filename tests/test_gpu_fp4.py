@@ -154,6 +154,8 @@ def test_native_gemm_rejects_other_formats_and_shapes():
     out = torch.zeros(4, 256, device="cuda")
     o = _lib.LinearOut(_lib.EP_STORE, 256, _lib.ptr(out), 256, 0, 0)
     qw = pw.qweight()
+    rs = torch.ones(256, device="cuda")
+    qw.row_scale = _lib.ptr(rs)        # everything present: the format is what is refused
     with pytest.raises(_lib.B200Error) as e:
         _lib.call("b200_linear_nvfp4_native", _lib.ptr(b), _lib.ptr(b), 4, 512, C.byref(qw), _lib.ptr(b), C.byref(o),
                   _lib.stream_ptr())
