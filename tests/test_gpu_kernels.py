@@ -443,7 +443,15 @@ def test_tile_weights_layout(fmt):
 @pytest.mark.parametrize("hd", [128, 256])
 def test_attention_matches_reference(with_prefix, hd):
     """q/k RMSNorm(1+w), partial RoPE, causal GQA softmax over (prefix-pool keys +) own
-    keys, times sigmoid(gate) (TF:647-690), ragged lengths around the 64/32 tile sizes."""
+    keys, times sigmoid(gate) (TF:647-690), ragged lengths around the 64/32 tile sizes.
+
+    Three bounds, from tight to loose: (1) the prep kernel's q / k / v (bf16 after norm and
+    RoPE, the kernel's storage format) within one bf16 rounding of the fp64 values; (2) the
+    attention output within 5e-3 (relative to its max) of fp64 attention over those same bf16
+    q / k / v, the remaining error being the bf16 probabilities of the P V product and fp32
+    accumulation; (3) end to end against fp64 from the fp32 inputs within 2e-2, which also
+    carries the bf16 rounding of q and k into the scores (whole-model parity is checked in
+    probabilities elsewhere)."""
     from oracle import torso as OT
     from strands_decider_b200 import _lib, config
     from strands_decider_b200.runtime import rope_tables
@@ -506,6 +514,18 @@ def test_attention_matches_reference(with_prefix, hd):
         o = torch.einsum("hts,shd->thd", s.softmax(-1), vr).reshape(n, -1) * torch.sigmoid(gate)
         err = (got[cu[i]:cu[i + 1]] - o).abs().max().item() / o.abs().max().item()
         assert err < 2e-2, (n, P[i], err)
+        # (1) the stored q / k / v are the fp64 values rounded to bf16 (one rounding, 2^-8 relative)
+        qd, kd, vd = (t[cu[i]:cu[i + 1]].double().cpu() for t in (qb, kb, vb))
+        for stored, exact in ((qd, q), (kd, k), (vd, v)):
+            assert ((stored - exact).abs() <= exact.abs() * 2.0 ** -8 + 1e-6).all()
+        # (2) attention over exactly the stored bf16 q / k / v and pool keys
+        ka, va = torch.cat([kp, kd]), torch.cat([vp, vd])
+        kr, vr = ka.repeat_interleave(nq // nkv, 1), va.repeat_interleave(nq // nkv, 1)
+        s = torch.einsum("thd,shd->hts", qd, kr) * hd ** -0.5
+        s = s.masked_fill((torch.arange(P[i] + n)[None, :] > pos[:, None])[None], float("-inf"))
+        o = torch.einsum("hts,shd->thd", s.softmax(-1), vr).reshape(n, -1) * torch.sigmoid(gate)
+        err = (got[cu[i]:cu[i + 1]] - o).abs().max().item() / o.abs().max().item()
+        assert err < 5e-3, (n, P[i], err)
 
 
 @pytest.mark.parametrize("rows,hidden", [(5, 2048), (96, 1024), (3000, 2048), (40, 256)])
