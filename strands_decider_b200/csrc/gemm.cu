@@ -126,8 +126,8 @@ __device__ __forceinline__ void unit_values(const Raw32<FMT>& raw, uint4 (&out)[
 // Unpack unit (row r, half h) of a stage from its shared-memory chunk into the swizzled
 // B tile. `rowc` is the per-row constant (ternary scale bits / NVFP4 row scale).
 template <int FMT>
-__device__ __forceinline__ void unpack_unit_smem(uint8_t* sB, const uint8_t* sW, const uint8_t* sS, int r, int h,
-                                                 uint32_t row_sc, float row_gs, const uint32_t* lut) {
+__device__ __forceinline__ void unpack_unit_regs(const uint8_t* sW, const uint8_t* sS, int r, int h, uint32_t row_sc,
+                                                 float row_gs, const uint32_t* lut, uint4 (&out)[4]) {
   constexpr int RB = tile_row_bytes(FMT);
   uint4 raw;
   if constexpr (FMT == B200_W_TERNARY) {
@@ -140,8 +140,14 @@ __device__ __forceinline__ void unpack_unit_smem(uint8_t* sB, const uint8_t* sW,
   if constexpr (FMT == B200_W_INT4G128) sc = *reinterpret_cast<const uint16_t*>(sS + r * 2);
   else if constexpr (FMT == B200_W_NVFP4) sc = *reinterpret_cast<const uint16_t*>(sS + r * 4 + h * 2);
   else sc = row_sc;
-  uint4 out[4];
   unpack32<FMT>(raw, sc, row_gs, out, lut);
+}
+
+template <int FMT>
+__device__ __forceinline__ void unpack_unit_smem(uint8_t* sB, const uint8_t* sW, const uint8_t* sS, int r, int h,
+                                                 uint32_t row_sc, float row_gs, const uint32_t* lut) {
+  uint4 out[4];
+  unpack_unit_regs<FMT>(sW, sS, r, h, row_sc, row_gs, lut, out);
   uint8_t* rowp = sB + r * 128;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
@@ -656,83 +662,149 @@ __global__ void zero_rows_kernel(float* __restrict__ out, int ld, int n) {
   for (int i = threadIdx.x; i < n / 4; i += blockDim.x) row[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-// --------------------------------------------------------------------------- small M (swap-AB)
-// Batches of at most 64 rows (single-token state appends, small request batches, the int4
-// microbench at M = 1 and 16): the weight tile is the MMA's A operand (M = 128 weight rows)
-// and the activations its B operand (N = NT = 16 or 64 token rows), so neither tensor work nor
-// shared memory goes to padding rows. One CTA = one 128-row weight tile over one K range (split
-// K across CTAs for the store / residual epilogues). Nothing in the main loop waits on a
-// round trip to memory once the data is in flight:
-//   * the producer issues the bulk copies of the range's first SK_WSLOTS packed weight k-blocks
-//     (all of a K range up to 1024) before it waits on the kernel before it in the stream (the
-//     weights do not depend on that kernel), then the activation tiles of up to SK_XSLOTS
-//     k-blocks at once (all of them for NT = 16);
-//   * two groups of 8 unpack warps decode alternate k-blocks into a 4-stage bf16 ring, so the
-//     fixed cost of one k-block's decode overlaps the next one's.
-//   warp 0      producer: packed weight k-blocks (1-D bulk copies into SK_WSLOTS slots,
-//               refilled as the unpack warps release them) and activation planes (TMA, NT rows
-//               x 64 k per k-block; rows past m read as zeros)
-//   warp 1      TMEM (max(NT, 32) columns) and the MMAs: per 16 k one tcgen05.mma per plane,
-//               M = 128, N = NT, A = the bf16 weight stage, B = the activation slot
-//   warps 2..5  epilogue: TMEM lane = weight row (output column), column = token; a warp
-//               writes 32 consecutive outputs of a token at a time (fp32 store or residual
-//               add, split-K partials by red.add into a zeroed output or the residual, or
-//               SwiGLU: the up rows' two quarters hand their values to the gate rows' two
-//               quarters through shared memory)
-//   warps 6..21 unpack, group (warp - 6) / 8 taking k-blocks of its parity: weight slot ->
-//               swizzled K-major bf16 stage (unpack_unit_smem, the same decode as
-//               gemm_tc_kernel, bit-exact with b200_dequantize)
-constexpr int SK_STAGES = 4;
-constexpr int SK_WSLOTS = 16;
-constexpr int SK_ROWS = 128;
-constexpr int SK_MAX_M = 64;
-constexpr int SK_UNPACK_GROUPS = 2;
-constexpr int SK_THREADS = GEMM_THREADS + (SK_UNPACK_GROUPS - 1) * GEMM_UNPACK_THREADS;  // 704
+// Vector fp32 atomic add (sm_90+): one split-K partial of four consecutive outputs.
+__device__ __forceinline__ void red_add_v4(float* p, const float4& v) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+// Rows of the swap-AB epilogue's staging tile sT[token][weight row] (floats; 128 + 4 so that
+// the column-wise writes and the row-wise 16-byte reads are both conflict-free).
+constexpr int SWAP_LD = 132;
+
+// The swap-AB epilogue for tokens t0 .. t0 + TC - 1 of a 128-row weight tile at n0. Epilogue
+// warp q (TMEM lane quarter q) holds in v[t] the sum of weight row 32 q + lane for token
+// t0 + t. The chunk is turned around in shared memory so that each warp then writes whole
+// token rows (tokens t0 + q, t0 + q + 4, ...): the tile's 128 output columns as one float4 per
+// lane (fp32 store, residual add, or red.global.add.v4 of a split-K partial), or, for the
+// SwiGLU (tile rows 0..63 = gate features n0/2 .. n0/2 + 63, rows 64..127 the matching up
+// features), its 64 features as one bf16 pair per lane and plane. The 4 epilogue warps meet
+// at named barrier 1 before the reads and after them (the next chunk reuses sT).
+template <int EP, int TC>
+__device__ __forceinline__ void swap_ab_epilogue(const GemmArgs& args, int n0, int q, int lane, int t0,
+                                                 const float (&v)[TC], float* sT) {
+  const b200_linear_out& o = args.o;
+#pragma unroll
+  for (int t = 0; t < TC; ++t) sT[t * SWAP_LD + 32 * q + lane] = v[t];
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll 1
+  for (int t = q; t < TC && t0 + t < args.m; t += 4) {
+    const size_t row = size_t(t0 + t) * o.ldo;
+    const float* st = sT + t * SWAP_LD;
+    if constexpr (EP == B200_EP_SWIGLU) {
+      const int ocol = n0 / 2 + 2 * lane;  // features ocol, ocol + 1
+      if (2 * ocol + 2 <= o.n_valid) {
+        const float2 g = *reinterpret_cast<const float2*>(st + 2 * lane);
+        const float2 u = *reinterpret_cast<const float2*>(st + 64 + 2 * lane);
+        const float h0 = silu_approx(g.x) * u.x, h1 = silu_approx(g.y) * u.y;
+        const uint32_t hb = pack_bf16x2(h0, h1);
+        uint16_t* dst = reinterpret_cast<uint16_t*>(o.out);
+        *reinterpret_cast<uint32_t*>(dst + row + ocol) = hb;
+        if (o.lo_offset) {
+          if (o.lo_format == B200_LO_E4M3)
+            *reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(dst + o.lo_offset) + row + ocol) =
+                f32x2_to_e4m3x2(lo8_value(h0, uint16_t(hb & 0xFFFFu)), lo8_value(h1, uint16_t(hb >> 16)));
+          else
+            *reinterpret_cast<uint32_t*>(dst + o.lo_offset + row + ocol) = lo_pair(h0, h1, hb);
+        }
+      }
+    } else {
+      const int col = n0 + 4 * lane;
+      if (col < o.n_valid) {
+        const float4 val = *reinterpret_cast<const float4*>(st + 4 * lane);
+        float* p = reinterpret_cast<float*>(o.out) + row + col;
+        if (args.ksplit > 1) {
+          red_add_v4(p, val);
+        } else if constexpr (EP == B200_EP_RESID_ADD) {
+          float4 r = *reinterpret_cast<const float4*>(p);
+          r.x += val.x;
+          r.y += val.y;
+          r.z += val.z;
+          r.w += val.w;
+          *reinterpret_cast<float4*>(p) = r;
+        } else {
+          *reinterpret_cast<float4*>(p) = val;
+        }
+      }
+    }
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+constexpr int SK_ROWS = 128;  // weight rows per swap-AB tile (the MMA's M)
+
+// --------------------------------------------------------------------------- small M, weights in TMEM
+// Batches of at most 128 rows on packed weights (the forward of a single request of about
+// 100 tokens, small request batches, state appends, the int4 microbench at M = 1 and 16).
+// Swap-AB: the 128-row weight tile is the MMA's A operand (M = 128) and the tokens its B
+// operand (N = NT or 2 NT), so no MMA work goes to padding token rows. The decoded weight
+// tile never goes through shared memory: the unpack warps write it into tensor memory with
+// tcgen05.st and each tcgen05.mma reads A (128 weight rows x 16 k) from there, so the
+// shared-memory port carries only the activations. One CTA = one weight tile over one K
+// range (K split across CTAs for the store and residual epilogues).
+// The two activation planes form one B operand (hi tokens in rows 0..NT-1, lo tokens in rows
+// NT..2NT-1 of the slot), so one MMA per 16 k covers both and the epilogue adds the column
+// halves of the accumulator.
+//   warp 0      producer: packed weight k-blocks (1-D bulk copies into TS_WSLOTS slots, the
+//               first ones before the programmatic-dependent wait: weights do not depend on
+//               the kernel before) and activation planes (TMA, NT rows x 64 k per plane; rows
+//               past m read as zeros)
+//   warp 1      TMEM and the MMAs: per 16 k one tcgen05.mma, M = 128, N = NT or 2 NT,
+//               A = the weight stage in TMEM, B = the activation slot
+//   warps 2..5  epilogue: TMEM lane quarter -> registers -> swap_ab_epilogue, 32 tokens a chunk
+//   warps 6..13 unpack: warp w decodes the 32-k half (w - 6) / 4 of rows 32 (w % 4) ..
+//               32 (w % 4) + 31 (its TMEM lane quarter) of each k-block into 16 columns of a
+//               32-column TMEM stage (two bf16 per column, lower k in the low half); same
+//               decode as every other GEMM here, bit-exact with b200_dequantize
+constexpr int TS_STAGES = 4;
+constexpr int TS_WSLOTS = 8;
+constexpr int TS_MAX_M = 128;
+constexpr int TS_UNPACK_WARPS = 8;
+constexpr int TS_THREADS = 32 * (GEMM_UNPACK_WARP0 + TS_UNPACK_WARPS);  // 448
+
+constexpr int pow2_cols(int c) { return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512; }
 
 template <int FMT, int PL, int NT>
-struct SkinnySmem {
-  static_assert(PL != PL_LO8, "the small-M kernel takes one or two bf16 activation planes");
-  static constexpr bool PACKED = FMT != B200_W_BF16;
-  static constexpr int X_BYTES = NT * GEMM_BK * 2;  // one activation plane of one k-block
-  static constexpr int X_STAGE = X_BYTES * (PL == PL_SPLIT ? 2 : 1);
-  static constexpr int XSLOTS = NT <= 16 ? 16 : 4;     // activation k-blocks held at once
-  static constexpr int B_BYTES = SK_ROWS * GEMM_BK * 2;  // the unpacked bf16 weight stage
-  static constexpr int W_BYTES = PACKED ? SK_ROWS * tile_row_bytes(FMT) : 0;
-  static constexpr int S_BYTES = PACKED ? SK_ROWS * tile_scale_row_bytes(FMT) : 0;
-  static constexpr int WSLOTS = PACKED ? SK_WSLOTS : 1;
-  static constexpr int SWAP_BYTES = 2 * NT * 32 * 4;  // SwiGLU hand-over: 2 quarters x NT tokens x 32 rows
-  // Independent accumulators in TMEM, summed by the epilogue: an N = 16 MMA is a few cycles of
-  // tensor work, so one chain of dependent MMAs into a single accumulator would run at the
-  // MMA's latency; ACC chains run side by side. MMA j of a k-block (j = 0..3 per 16 k, plus 4
-  // for the low plane with 8 accumulators) feeds accumulator j % ACC.
-  static constexpr int ACC = NT <= 16 ? 8 : 4;
-  static constexpr int TM_COLS = ACC * NT < 32 ? 32 : ACC * NT;
-  static constexpr int BARS = 2 * WSLOTS + 2 * XSLOTS + 2 * SK_STAGES + 1;
-  static constexpr int TOTAL = SK_STAGES * B_BYTES + XSLOTS * X_STAGE + WSLOTS * (W_BYTES + S_BYTES) + SWAP_BYTES +
-                               BARS * 8 + 16 + 64 + 1024;
-  static_assert(X_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "128-byte-swizzled tiles need 1024-byte alignment");
+struct TsSmem {
+  static_assert(FMT != B200_W_BF16 && PL != PL_LO8, "packed weights and one or two bf16 activation planes");
+  static_assert(NT == 16 || NT == 64 || NT == 128, "token tiles of 16, 64 or 128");
+  static constexpr int N = PL == PL_SPLIT ? 2 * NT : NT;   // the MMA's N: hi tokens, then lo tokens
+  static constexpr int X_PLANE = NT * GEMM_BK * 2;          // one plane of one k-block (NT rows of 128 B)
+  static constexpr int X_STAGE = N * GEMM_BK * 2;
+  static constexpr int XSLOTS = X_STAGE <= 4096 ? 16 : X_STAGE <= 8192 ? 8 : 4;
+  static constexpr int W_BYTES = SK_ROWS * tile_row_bytes(FMT);
+  static constexpr int S_BYTES = SK_ROWS * tile_scale_row_bytes(FMT);
+  static constexpr int TC = NT < 32 ? NT : 32;                // epilogue tokens per chunk
+  static constexpr int SWAP_BYTES = TC * SWAP_LD * 4;         // the epilogue's staging tile
+  static constexpr int ACC_COLS = N < 32 ? 32 : N;          // accumulator columns 0 .. N-1
+  static constexpr int A_COL0 = ACC_COLS;                   // weight stage s: columns A_COL0 + 32 s ..
+  static constexpr int TM_COLS = pow2_cols(A_COL0 + 32 * TS_STAGES);
+  static constexpr int BARS = 2 * TS_WSLOTS + 2 * XSLOTS + 2 * TS_STAGES + 1;
+  static constexpr int TOTAL =
+      XSLOTS * X_STAGE + TS_WSLOTS * (W_BYTES + S_BYTES) + SWAP_BYTES + BARS * 8 + 16 + 64 + 1024;
+  static_assert(X_PLANE % 1024 == 0, "128-byte-swizzled activation tiles need 1024-byte alignment");
+  static_assert(A_COL0 + 32 * TS_STAGES <= TM_COLS && TM_COLS <= 512, "TMEM columns");
 };
 
 template <int FMT, int EP, int PL, int NT>
-__global__ void __launch_bounds__(SK_THREADS, 1)
-    gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmX_lo,
-                       const __grid_constant__ CUtensorMap tmW, const GemmArgs args) {
-  using SM = SkinnySmem<FMT, PL, NT>;
+__global__ void __launch_bounds__(TS_THREADS, 1)
+    gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmX_lo,
+                   const GemmArgs args) {
+  using SM = TsSmem<FMT, PL, NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sB = smem;                                // SK_STAGES x B_BYTES
-  uint8_t* sX = sB + SK_STAGES * SM::B_BYTES;        // XSLOTS x X_STAGE
-  uint8_t* sW = sX + SM::XSLOTS * SM::X_STAGE;       // WSLOTS x W_BYTES
-  uint8_t* sS = sW + SM::WSLOTS * SM::W_BYTES;       // WSLOTS x S_BYTES
-  float* sSwap = reinterpret_cast<float*>(sS + SM::WSLOTS * SM::S_BYTES);  // [2][NT][32]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sSwap) + SM::SWAP_BYTES);
+  uint8_t* sX = smem;                                // XSLOTS x X_STAGE
+  uint8_t* sW = sX + SM::XSLOTS * SM::X_STAGE;       // TS_WSLOTS x W_BYTES
+  uint8_t* sS = sW + TS_WSLOTS * SM::W_BYTES;        // TS_WSLOTS x S_BYTES
+  float* sT = reinterpret_cast<float*>(sS + TS_WSLOTS * SM::S_BYTES);  // [TC][SWAP_LD]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sT) + SM::SWAP_BYTES);
   uint64_t* full_w = bars;                           // [WSLOTS] weight slot landed
-  uint64_t* empty_w = bars + SM::WSLOTS;             // [WSLOTS] weight slot unpacked
-  uint64_t* full_x = bars + 2 * SM::WSLOTS;          // [XSLOTS] activation slot (and bf16 weight stage) landed
+  uint64_t* empty_w = bars + TS_WSLOTS;              // [WSLOTS] weight slot decoded
+  uint64_t* full_x = bars + 2 * TS_WSLOTS;           // [XSLOTS] activation slot landed
   uint64_t* empty_x = full_x + SM::XSLOTS;           // [XSLOTS] the slot's MMAs are done
-  uint64_t* full_b = empty_x + SM::XSLOTS;           // [STAGES] bf16 weight stage written
-  uint64_t* empty = full_b + SK_STAGES;              // [STAGES] the stage's MMAs are done
-  uint64_t* acc_full = empty + SK_STAGES;            // [1]
+  uint64_t* full_a = empty_x + SM::XSLOTS;           // [STAGES] TMEM weight stage written
+  uint64_t* empty_a = full_a + TS_STAGES;            // [STAGES] the stage's MMAs are done
+  uint64_t* acc_full = empty_a + TS_STAGES;          // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   uint32_t* lut = tmem_slot + 4;                     // 16 words: ternary pair table
   constexpr uint32_t TM_COLS = SM::TM_COLS;
@@ -745,17 +817,17 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   const int nkb = kb1 - kb0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < SM::WSLOTS; ++i) {
+    for (int i = 0; i < TS_WSLOTS; ++i) {
       mbar_init(&full_w[i], 1);
-      mbar_init(&empty_w[i], GEMM_UNPACK_THREADS / 32);  // one arrival per unpack warp
+      mbar_init(&empty_w[i], TS_UNPACK_WARPS);  // one arrival per unpack warp
     }
     for (int i = 0; i < SM::XSLOTS; ++i) {
       mbar_init(&full_x[i], 1);
       mbar_init(&empty_x[i], 1);
     }
-    for (int s = 0; s < SK_STAGES; ++s) {
-      mbar_init(&full_b[s], GEMM_UNPACK_THREADS / 32);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < TS_STAGES; ++s) {
+      mbar_init(&full_a[s], TS_UNPACK_WARPS);
+      mbar_init(&empty_a[s], 1);
     }
     mbar_init(&acc_full[0], 1);
     mbar_fence_init();
@@ -769,72 +841,56 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // one unit per CTA: the next kernel may be scheduled now (it waits for this one's results)
-  pdl_trigger();
+  pdl_trigger();  // one unit per CTA: the next kernel may be scheduled now (it waits for this one's results)
 
   if (warp == 0) {
     // ---------------- producer
     if (lane == 0) {
       tma_prefetch_desc(&tmX);
       if constexpr (PL == PL_SPLIT) tma_prefetch_desc(&tmX_lo);
-      if constexpr (!SM::PACKED) tma_prefetch_desc(&tmW);
-      constexpr int RB = SM::PACKED ? tile_row_bytes(FMT) : 0, SB = tile_scale_row_bytes(FMT);
+      constexpr int RB = tile_row_bytes(FMT), SB = tile_scale_row_bytes(FMT);
       // this tile's rows inside the 256-row streaming tiles: tile n0 / 256, row offset n0 % 256
       const size_t lt = size_t(n0 / GEMM_TILE_ROWS) * nk, sub = n0 % GEMM_TILE_ROWS;
       const uint8_t* wtiles = reinterpret_cast<const uint8_t*>(args.w.tiles) + sub * RB;
       const uint8_t* stiles = reinterpret_cast<const uint8_t*>(args.w.tile_scales) + sub * SB;
       auto issue_w = [&](int i) {  // k-block kb0 + i into slot i % WSLOTS
-        const int slot = i % SM::WSLOTS;
+        const int slot = i % TS_WSLOTS;
         const size_t kt = lt + kb0 + i;
         mbar_arrive_expect_tx(&full_w[slot], SM::W_BYTES + SM::S_BYTES);
         bulk_load(sW + slot * SM::W_BYTES, wtiles + kt * GEMM_TILE_ROWS * RB, SM::W_BYTES, &full_w[slot]);
         if constexpr (SM::S_BYTES > 0)
           bulk_load(sS + slot * SM::S_BYTES, stiles + kt * GEMM_TILE_ROWS * SB, SM::S_BYTES, &full_w[slot]);
       };
-      if constexpr (SM::PACKED) {
-        for (int i = 0; i < min(nkb, SM::WSLOTS); ++i) issue_w(i);
-      }
+      for (int i = 0; i < min(nkb, TS_WSLOTS); ++i) issue_w(i);
       pdl_wait();  // the activations come from the kernel before this one
       for (int i = 0; i < nkb; ++i) {
         const int xs = i % SM::XSLOTS;
         mbar_wait(&empty_x[xs], ((i / SM::XSLOTS) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
-        if constexpr (!SM::PACKED)  // bf16 weights stream straight into the stage
-          mbar_wait(&empty[i % SK_STAGES], ((i / SK_STAGES) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
-        mbar_arrive_expect_tx(&full_x[xs], SM::X_STAGE + (SM::PACKED ? 0 : SM::B_BYTES));
+        mbar_arrive_expect_tx(&full_x[xs], SM::X_STAGE);
         tma_load_2d(sX + xs * SM::X_STAGE, &tmX, &full_x[xs], (kb0 + i) * GEMM_BK, 0);
         if constexpr (PL == PL_SPLIT)
-          tma_load_2d(sX + xs * SM::X_STAGE + SM::X_BYTES, &tmX_lo, &full_x[xs], (kb0 + i) * GEMM_BK, 0);
-        if constexpr (!SM::PACKED)
-          tma_load_2d(sB + (i % SK_STAGES) * SM::B_BYTES, &tmW, &full_x[xs], (kb0 + i) * GEMM_BK, n0);
-        if constexpr (SM::PACKED) {
-          if (i + SM::WSLOTS < nkb) {  // refill slot i once its k-block is unpacked
-            mbar_wait(&empty_w[i % SM::WSLOTS], (i / SM::WSLOTS) & 1, FAULT_GEMM_WAIT_EMPTY);
-            issue_w(i + SM::WSLOTS);
-          }
+          tma_load_2d(sX + xs * SM::X_STAGE + SM::X_PLANE, &tmX_lo, &full_x[xs], (kb0 + i) * GEMM_BK, 0);
+        if (i + TS_WSLOTS < nkb) {  // refill weight slot i once its k-block is decoded
+          mbar_wait(&empty_w[i % TS_WSLOTS], (i / TS_WSLOTS) & 1, FAULT_GEMM_WAIT_EMPTY);
+          issue_w(i + TS_WSLOTS);
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer: D[weight row][token] += W_stage . X_slot^T
+    // ---------------- MMA issuer: D[weight row][token] += W_stage (TMEM) . X_slot^T
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(SK_ROWS, NT);
+      constexpr uint32_t idesc = umma_idesc_bf16(SK_ROWS, SM::N);
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % SK_STAGES, xs = i % SM::XSLOTS;
+        const int s = i % TS_STAGES, xs = i % SM::XSLOTS;
         mbar_wait(&full_x[xs], (i / SM::XSLOTS) & 1, FAULT_GEMM_WAIT_FULL_A);
-        if constexpr (SM::PACKED) mbar_wait(&full_b[s], (i / SK_STAGES) & 1, FAULT_GEMM_WAIT_FULL_B);
+        mbar_wait(&full_a[s], (i / TS_STAGES) & 1, FAULT_GEMM_WAIT_FULL_B);
         tc_fence_after();
-        const uint64_t ad = umma_desc_sw128(smem_addr(sB + s * SM::B_BYTES));
         const uint64_t bd = umma_desc_sw128(smem_addr(sX + xs * SM::X_STAGE));
+        const uint32_t ta = tmem_base + uint32_t(SM::A_COL0 + 32 * s);
 #pragma unroll
-        for (int j = 0; j < GEMM_BK / 16; ++j) {  // +32 bytes of K per MMA = +2 in 16-byte units
-          const uint32_t acc_hi = tmem_base + uint32_t((j % SM::ACC) * NT);
-          const uint32_t acc_lo = tmem_base + uint32_t(((j + 4) % SM::ACC) * NT);
-          umma_bf16(acc_hi, ad + 2 * j, bd + 2 * j, idesc, i != 0 ? 1u : 0u);
-          if constexpr (PL == PL_SPLIT)
-            umma_bf16(acc_lo, ad + 2 * j, bd + (SM::X_BYTES >> 4) + 2 * j, idesc,
-                      (i != 0 || SM::ACC <= 4) ? 1u : 0u);
-        }
-        umma_commit(&empty[s]);
+        for (int j = 0; j < GEMM_BK / 16; ++j)  // 16 k = 8 TMEM columns of A, 32 bytes of B
+          umma_bf16_ts(tmem_base, ta + uint32_t(8 * j), bd + 2 * j, idesc, (i | j) != 0 ? 1u : 0u);
+        umma_commit(&empty_a[s]);
         umma_commit(&empty_x[xs]);
       }
       umma_commit(&acc_full[0]);
@@ -847,92 +903,50 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     mbar_wait(&acc_full[0], 0, FAULT_GEMM_WAIT_ACCUM);
     tc_fence_after();
     const uint32_t tl = tmem_base + (uint32_t(q * 32) << 16);
-    const b200_linear_out& o = args.o;
-    // accumulators used: all ACC with two planes or ACC == 4, else the first 4 (the hi plane's)
-    constexpr int USED = (PL == PL_SPLIT || SM::ACC <= 4) ? SM::ACC : 4;
-    constexpr int TC = NT < 32 ? NT : 32;  // tokens per chunk
+    constexpr int TC = SM::TC;
 #pragma unroll 1
-    for (int t0 = 0; t0 < NT; t0 += TC) {
-      // the sum of the accumulators (their MMAs covered disjoint k) for tokens t0 .. t0 + TC - 1
+    for (int t0 = 0; t0 < NT && t0 < args.m; t0 += TC) {
       float v[TC];
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tl + uint32_t(t0), r);  // NT = 16: hi in columns 0..15, lo in 16..31
+      tmem_ld_wait();
 #pragma unroll
-      for (int t = 0; t < TC; ++t) v[t] = 0.0f;
+      for (int t = 0; t < TC; ++t) v[t] = __uint_as_float(r[t]);
+      if constexpr (PL == PL_SPLIT) {
+        if constexpr (NT < 32) {
 #pragma unroll
-      for (int a = 0; a < USED; a += 32 / TC) {  // one 32-column load covers 32 / TC accumulators
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tl + uint32_t(a * NT + t0), r);
-        tmem_ld_wait();
+          for (int t = 0; t < TC; ++t) v[t] += __uint_as_float(r[NT + t]);
+        } else {
+          tmem_ld_32x32b_x32(tl + uint32_t(NT + t0), r);
+          tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          if (a + c / TC < USED) v[c % TC] += __uint_as_float(r[c]);
+          for (int t = 0; t < TC; ++t) v[t] += __uint_as_float(r[t]);
         }
       }
-      if constexpr (EP == B200_EP_SWIGLU) {
-        // rows 0..63 of the tile are gate features n0/2 .. n0/2 + 63, rows 64..127 the matching up
-        if (q >= 2) {
-#pragma unroll
-          for (int t = 0; t < TC; ++t) sSwap[((q - 2) * NT + t0 + t) * 32 + lane] = v[t];
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
-        if (q < 2) {
-          const int ocol = n0 / 2 + q * 32 + lane;
-          if (2 * ocol < o.n_valid) {
-            uint16_t* dst = reinterpret_cast<uint16_t*>(o.out);
-#pragma unroll
-            for (int t = 0; t < TC; ++t) {
-              if (t0 + t < args.m) {
-                const float h = silu_approx(v[t]) * sSwap[(q * NT + t0 + t) * 32 + lane];
-                const uint16_t hb = f32_to_bf16_rn(h);
-                const size_t e = size_t(t0 + t) * o.ldo + ocol;
-                dst[e] = hb;
-                if (o.lo_offset) {
-                  if (o.lo_format == B200_LO_E4M3)
-                    reinterpret_cast<uint8_t*>(dst + o.lo_offset)[e] =
-                        uint8_t(f32x2_to_e4m3x2(lo8_value(h, hb), 0.0f));
-                  else
-                    dst[o.lo_offset + e] = f32_to_bf16_rn(h - bf16_to_f32(hb));
-                }
-              }
-            }
-          }
-        }
-      } else {
-        const int col = n0 + q * 32 + lane;
-        if (col < o.n_valid) {
-          float* dst = reinterpret_cast<float*>(o.out) + col;
-#pragma unroll
-          for (int t = 0; t < TC; ++t) {
-            if (t0 + t < args.m) {
-              float* p = dst + size_t(t0 + t) * o.ldo;
-              if (args.ksplit > 1) asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v[t]) : "memory");
-              else if constexpr (EP == B200_EP_RESID_ADD) *p += v[t];
-              else *p = v[t];
-            }
-          }
-        }
-      }
+      swap_ab_epilogue<EP, TC>(args, n0, q, lane, t0, v, sT);
     }
   } else {
-    // ---------------- weight unpack: group g takes k-blocks g, g + 2, ... (slot -> bf16 stage)
-    if constexpr (SM::PACKED) {
-      const int ut = threadIdx.x - GEMM_UNPACK_WARP0 * 32;
-      const int grp = ut / GEMM_UNPACK_THREADS, t = ut % GEMM_UNPACK_THREADS;
-      const int r = t >> 1, h = t & 1;  // one (row, 32-column half) unit per thread per k-block
-      const uint32_t row_sc =
-          FMT == B200_W_TERNARY ? uint32_t(__ldg(reinterpret_cast<const uint16_t*>(args.w.scales) + n0 + r)) : 0u;
-      const float row_gs = FMT == B200_W_NVFP4 ? __ldg(args.w.row_scale + n0 + r) : 1.0f;
-      for (int i = grp; i < nkb; i += SK_UNPACK_GROUPS) {
-        const int s = i % SK_STAGES, ws = i % SM::WSLOTS;
-        mbar_wait(&full_w[ws], (i / SM::WSLOTS) & 1, FAULT_GEMM_WAIT_FULL_W);
-        mbar_wait(&empty[s], ((i / SK_STAGES) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
-        unpack_unit_smem<FMT>(sB + s * SM::B_BYTES, sW + ws * SM::W_BYTES, sS + ws * SM::S_BYTES, r, h, row_sc,
-                              row_gs, lut);
-        fence_proxy_async_smem();  // this thread's stores, visible to the tensor cores
-        __syncwarp();
-        if (lane == 0) {            // one arrival per warp
-          mbar_arrive(&full_b[s]);
-          mbar_arrive(&empty_w[ws]);
-        }
+    // ---------------- weight unpack into the TMEM stage
+    const int u = warp - GEMM_UNPACK_WARP0, q = warp & 3, h = u >> 2;
+    const int r = 32 * q + lane;  // weight row = TMEM lane
+    const uint32_t row_sc =
+        FMT == B200_W_TERNARY ? uint32_t(__ldg(reinterpret_cast<const uint16_t*>(args.w.scales) + n0 + r)) : 0u;
+    const float row_gs = FMT == B200_W_NVFP4 ? __ldg(args.w.row_scale + n0 + r) : 1.0f;
+    const uint32_t ta = tmem_base + (uint32_t(32 * q) << 16) + uint32_t(SM::A_COL0 + 16 * h);
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % TS_STAGES, ws = i % TS_WSLOTS;
+      mbar_wait(&full_w[ws], (i / TS_WSLOTS) & 1, FAULT_GEMM_WAIT_FULL_W);
+      mbar_wait(&empty_a[s], ((i / TS_STAGES) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
+      tc_fence_after();
+      uint4 vals[4];
+      unpack_unit_regs<FMT>(sW + ws * SM::W_BYTES, sS + ws * SM::S_BYTES, r, h, row_sc, row_gs, lut, vals);
+      tmem_st_32x32b_x16(ta + uint32_t(32 * s), vals);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {  // one arrival per warp
+        mbar_arrive(&full_a[s]);
+        mbar_arrive(&empty_w[ws]);
       }
     }
   }
@@ -1153,16 +1167,15 @@ static int dispatch_simt(const uint16_t* x, const uint16_t* xl, int ldx, const G
   return B200_OK;
 }
 
-// The small-M kernel: K split so that about one unit per SM exists (the SwiGLU needs whole
-// sums and is never split); a split store first zeroes its output.
+// The TMEM-weight kernel: K split so that about one unit per SM exists (the SwiGLU needs
+// whole sums and is never split); a split store first zeroes its output.
 template <int FMT, int EP, int PL, int NT>
-static int launch_skinny(const CUtensorMap& mx, const CUtensorMap& mx_lo, const CUtensorMap& mw, const GemmArgs& a,
-                         cudaStream_t st) {
-  using SM = SkinnySmem<FMT, PL, NT>;
+static int launch_ts(const CUtensorMap& mx, const CUtensorMap& mx_lo, const GemmArgs& a, cudaStream_t st) {
+  using SM = TsSmem<FMT, PL, NT>;
   static_assert(SM::TOTAL <= 227 * 1024, "small-M GEMM shared memory exceeds the 227 KB per-CTA limit");
   static DeviceOnce attr;
   const int r = once_per_device(attr, [](int) -> int {
-    SDB_CUDA(cudaFuncSetAttribute(gemm_skinny_kernel<FMT, EP, PL, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    SDB_CUDA(cudaFuncSetAttribute(gemm_ts_kernel<FMT, EP, PL, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SM::TOTAL));
     return B200_OK;
   });
@@ -1173,36 +1186,38 @@ static int launch_skinny(const CUtensorMap& mx, const CUtensorMap& mx_lo, const 
   if (args.ksplit > 1 && EP == B200_EP_STORE)
     SDB_CUDA(launch_pdl(zero_rows_kernel, dim3(a.m), dim3(256), 0, st, reinterpret_cast<float*>(a.o.out), a.o.ldo,
                         a.o.n_valid));
-  SDB_CUDA(launch_pdl(gemm_skinny_kernel<FMT, EP, PL, NT>, dim3(tiles * args.ksplit), dim3(SK_THREADS), SM::TOTAL,
-                      st, mx, mx_lo, mw, args));
+  SDB_CUDA(launch_pdl(gemm_ts_kernel<FMT, EP, PL, NT>, dim3(tiles * args.ksplit), dim3(TS_THREADS), SM::TOTAL, st,
+                      mx, mx_lo, args));
   return B200_OK;
 }
 
-template <int FMT, int PL>
-static int dispatch_skinny_ep(const CUtensorMap& mx, const CUtensorMap& mx_lo, const CUtensorMap& mw,
-                              const GemmArgs& a, cudaStream_t st) {
-  const bool wide = a.m > 16;
+template <int FMT, int PL, int NT>
+static int dispatch_ts_ep(const CUtensorMap& mx, const CUtensorMap& mx_lo, const GemmArgs& a, cudaStream_t st) {
   switch (a.o.epilogue) {
-    case B200_EP_STORE:
-      return wide ? launch_skinny<FMT, B200_EP_STORE, PL, 64>(mx, mx_lo, mw, a, st)
-                  : launch_skinny<FMT, B200_EP_STORE, PL, 16>(mx, mx_lo, mw, a, st);
-    case B200_EP_RESID_ADD:
-      return wide ? launch_skinny<FMT, B200_EP_RESID_ADD, PL, 64>(mx, mx_lo, mw, a, st)
-                  : launch_skinny<FMT, B200_EP_RESID_ADD, PL, 16>(mx, mx_lo, mw, a, st);
-    default:
-      return wide ? launch_skinny<FMT, B200_EP_SWIGLU, PL, 64>(mx, mx_lo, mw, a, st)
-                  : launch_skinny<FMT, B200_EP_SWIGLU, PL, 16>(mx, mx_lo, mw, a, st);
+    case B200_EP_STORE: return launch_ts<FMT, B200_EP_STORE, PL, NT>(mx, mx_lo, a, st);
+    case B200_EP_RESID_ADD: return launch_ts<FMT, B200_EP_RESID_ADD, PL, NT>(mx, mx_lo, a, st);
+    default: return launch_ts<FMT, B200_EP_SWIGLU, PL, NT>(mx, mx_lo, a, st);
   }
 }
 
-template <int PL>
-static int dispatch_skinny(const CUtensorMap& mx, const CUtensorMap& mx_lo, const CUtensorMap& mw, const GemmArgs& a,
-                           cudaStream_t st) {
+template <int PL, int NT>
+static int dispatch_ts(const CUtensorMap& mx, const CUtensorMap& mx_lo, const GemmArgs& a, cudaStream_t st) {
   switch (a.w.format) {
-    case B200_W_BF16: return dispatch_skinny_ep<B200_W_BF16, PL>(mx, mx_lo, mw, a, st);
-    case B200_W_INT4G128: return dispatch_skinny_ep<B200_W_INT4G128, PL>(mx, mx_lo, mw, a, st);
-    case B200_W_NVFP4: return dispatch_skinny_ep<B200_W_NVFP4, PL>(mx, mx_lo, mw, a, st);
-    default: return dispatch_skinny_ep<B200_W_TERNARY, PL>(mx, mx_lo, mw, a, st);
+    case B200_W_INT4G128: return dispatch_ts_ep<B200_W_INT4G128, PL, NT>(mx, mx_lo, a, st);
+    case B200_W_NVFP4: return dispatch_ts_ep<B200_W_NVFP4, PL, NT>(mx, mx_lo, a, st);
+    default: return dispatch_ts_ep<B200_W_TERNARY, PL, NT>(mx, mx_lo, a, st);
+  }
+}
+
+// Token tile of the TMEM-weight kernel: 16, 64 or 128 rows.
+static int ts_tile(int m) { return m <= 16 ? 16 : m <= 64 ? 64 : 128; }
+
+template <int PL>
+static int dispatch_ts_nt(const CUtensorMap& mx, const CUtensorMap& mx_lo, const GemmArgs& a, cudaStream_t st) {
+  switch (ts_tile(a.m)) {
+    case 16: return dispatch_ts<PL, 16>(mx, mx_lo, a, st);
+    case 64: return dispatch_ts<PL, 64>(mx, mx_lo, a, st);
+    default: return dispatch_ts<PL, 128>(mx, mx_lo, a, st);
   }
 }
 
@@ -1223,22 +1238,16 @@ extern "C" int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m
   }
   GemmArgs a{*w, *out, m, k, 1};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (m <= SK_MAX_M) {  // small M: weights as the MMA's A operand, tokens as N (swap-AB)
-    const int nt = m > 16 ? 64 : 16;
-    CUtensorMap mx, mx_lo, mw;
+  if (m <= TS_MAX_M && w->format != B200_W_BF16) {  // small M, packed weights: decoded into TMEM (swap-AB)
+    const int nt = ts_tile(m);
+    CUtensorMap mx, mx_lo;
     if (int rc = make_act_map(&mx, x_hi, m, k, ldx, nt)) return rc;
     if (x_lo) {
       if (int rc = make_act_map(&mx_lo, x_lo, m, k, ldx, nt)) return rc;
     } else {
       mx_lo = mx;
     }
-    if (w->format == B200_W_BF16) {
-      if (reinterpret_cast<uintptr_t>(w->data) & 15) return sdb_fail(B200_ERR_SHAPE, "b200_linear: bf16 W unaligned");
-      if (int rc = make_act_map(&mw, reinterpret_cast<const uint16_t*>(w->data), w->n, k, k, SK_ROWS)) return rc;
-    } else {
-      mw = mx;
-    }
-    return x_lo ? dispatch_skinny<PL_SPLIT>(mx, mx_lo, mw, a, st) : dispatch_skinny<PL_ONE>(mx, mx_lo, mw, a, st);
+    return x_lo ? dispatch_ts_nt<PL_SPLIT>(mx, mx_lo, a, st) : dispatch_ts_nt<PL_ONE>(mx, mx_lo, a, st);
   }
   if (w->format == B200_W_BF16) {  // the weight tile streams through TMA as [n, k] bf16, one box per N tile
     if (reinterpret_cast<uintptr_t>(w->data) & 15) return sdb_fail(B200_ERR_SHAPE, "b200_linear: bf16 W unaligned");

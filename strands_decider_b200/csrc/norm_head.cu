@@ -91,59 +91,115 @@ __global__ void __launch_bounds__(256) rmsnorm_block_kernel(const float* __restr
   }
 }
 
-// Decision head: one warp per decision row. Gathers the row's last token from the fp32
-// residual stream, applies the final RMSNorm (1 + w), dots it with the option tokens'
-// tied-embedding rows, divides by the row's temperature (clamped at 1e-6), takes the
-// masked softmax and derives the answer numbers. hidden <= 4096, kmax <= 16.
-__global__ void decide_kernel(const float* __restrict__ x, int hidden, const float* __restrict__ fnorm, float eps,
-                              const uint16_t* __restrict__ table, b200_decide_args d, int vocab, int n_tokens) {
+// Decision head: one CTA of DECIDE_THREADS per decision row. Gathers the row's last token from
+// the fp32 residual stream, applies the final RMSNorm (1 + w), dots it with the option tokens'
+// tied-embedding rows, divides by the row's temperature (clamped at 1e-6), takes the masked
+// softmax and derives the answer numbers. Each thread holds 8-element chunks c = tid, tid + 256
+// of the row (hidden <= 4096, a multiple of 32), so every load of the row, the norm weight and
+// the option rows is in flight at once (a single-request forward waits on this kernel's
+// latency, not its bytes). kmax <= 16.
+constexpr int DECIDE_THREADS = 256;
+constexpr int DECIDE_CHUNKS = 4096 / 8 / DECIDE_THREADS;  // 8-element chunks per thread
+
+__global__ void __launch_bounds__(DECIDE_THREADS)
+    decide_kernel(const float* __restrict__ x, int hidden, const float* __restrict__ fnorm, float eps,
+                  const uint16_t* __restrict__ table, b200_decide_args d, int vocab, int n_tokens) {
+  __shared__ float red[17][DECIDE_THREADS / 32];  // [0]: sum of squares, [1 + k]: option k's dot
   pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
   pdl_trigger();
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= d.n_rows) return;
+  const int row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int tok = d.last_tok[row];
   if (tok < 0 || tok >= n_tokens) {
-    if (lane == 0) raise_fault(FAULT_BAD_INDEX);
+    if (threadIdx.x == 0) raise_fault(FAULT_BAD_INDEX);
     tok = 0;
   }
-  const float* xr = x + size_t(tok) * hidden;
-  constexpr int MAXP = 4096 / 32;
-  float h[MAXP];
+  const int n = d.n_opts[row];
+  const int nk = min(min(n, d.kmax), 16);
+  const int n8 = hidden / 8;
+  int ids[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    ids[k] = 0;
+    if (k < nk) {
+      const int id = d.opt_ids[row * d.kmax + k];
+      if (id < 0 || id >= vocab) {
+        if (threadIdx.x == 0) raise_fault(FAULT_BAD_INDEX);
+      } else {
+        ids[k] = id;
+      }
+    }
+  }
+  const float4* xr = reinterpret_cast<const float4*>(x + size_t(tok) * hidden);
+  const float4* wr = reinterpret_cast<const float4*>(fnorm);
+  float h[DECIDE_CHUNKS][8];
   float ss = 0.0f;
 #pragma unroll
-  for (int j = 0; j < MAXP; ++j) {
-    const int i = lane + 32 * j;
-    h[j] = i < hidden ? xr[i] : 0.0f;
-    ss += h[j] * h[j];
+  for (int c = 0; c < DECIDE_CHUNKS; ++c) {
+    const int j = threadIdx.x + c * DECIDE_THREADS;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (j < n8) {
+      a = xr[2 * j];
+      b = xr[2 * j + 1];
+    }
+    h[c][0] = a.x, h[c][1] = a.y, h[c][2] = a.z, h[c][3] = a.w;
+    h[c][4] = b.x, h[c][5] = b.y, h[c][6] = b.z, h[c][7] = b.w;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += h[c][e] * h[c][e];
   }
   ss = warp_sum(ss);
-  const float r = rsqrtf(ss / float(hidden) + eps);
+  if (lane == 0) red[0][warp] = ss;
+  __syncthreads();
+  float tot = 0.0f;
 #pragma unroll
-  for (int j = 0; j < MAXP; ++j) {
-    const int i = lane + 32 * j;
-    h[j] = i < hidden ? h[j] * r * (1.0f + fnorm[i]) : 0.0f;
+  for (int w = 0; w < DECIDE_THREADS / 32; ++w) tot += red[0][w];
+  const float r = rsqrtf(tot / float(hidden) + eps);
+#pragma unroll
+  for (int c = 0; c < DECIDE_CHUNKS; ++c) {
+    const int j = threadIdx.x + c * DECIDE_THREADS;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (j < n8) {
+      a = __ldg(wr + 2 * j);
+      b = __ldg(wr + 2 * j + 1);
+    }
+    const float g[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[c][e] = h[c][e] * r * (1.0f + g[e]);
   }
-  const int n = d.n_opts[row];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    if (k < nk) {
+      const uint4* er = reinterpret_cast<const uint4*>(table + size_t(ids[k]) * hidden);
+      float acc = 0.0f;
+#pragma unroll
+      for (int c = 0; c < DECIDE_CHUNKS; ++c) {
+        const int j = threadIdx.x + c * DECIDE_THREADS;
+        if (j < n8) {
+          const uint4 e = __ldg(er + j);
+          const uint32_t w4[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc = fmaf(h[c][2 * i], bf16x2_lo(w4[i]), acc);
+            acc = fmaf(h[c][2 * i + 1], bf16x2_hi(w4[i]), acc);
+          }
+        }
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) red[1 + k][warp] = acc;
+    }
+  }
+  __syncthreads();
+  if (warp != 0) return;
   const float temp = fmaxf(d.temperature[row], 1e-6f);
   float logit[16];
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
     logit[k] = -1e4f;  // MASK_VALUE for slots past n (modeling.py:39, 210-221)
-    if (k < d.kmax && k < n) {
-      int id = d.opt_ids[row * d.kmax + k];
-      if (id < 0 || id >= vocab) {
-        raise_fault(FAULT_BAD_INDEX);
-        id = 0;
-      }
-      const uint16_t* e = table + size_t(id) * hidden;
-      float acc = 0.0f;
+    if (k < nk) {
+      float dot = 0.0f;
 #pragma unroll
-      for (int j = 0; j < MAXP; ++j) {
-        const int i = lane + 32 * j;
-        if (i < hidden) acc = fmaf(h[j], bf16_to_f32(e[i]), acc);
-      }
-      logit[k] = warp_sum(acc) / temp;
+      for (int w = 0; w < DECIDE_THREADS / 32; ++w) dot += red[1 + k][w];
+      logit[k] = dot / temp;
     }
   }
   // masked softmax over the first n slots
@@ -457,10 +513,12 @@ int sdb_decide_vocab(const float* x, int32_t hidden, const float* final_norm, fl
   if (d->n_rows <= 0) return B200_OK;
   if (d->kmax < 1 || d->kmax > 16 || hidden > 4096 || hidden % 32 != 0)
     return sdb_fail(B200_ERR_SHAPE, "b200_decide: kmax must be 1..16 and hidden <= 4096");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(final_norm) | reinterpret_cast<uintptr_t>(table)) & 15)
+    return sdb_fail(B200_ERR_SHAPE, "b200_decide: x, final_norm and table must be 16-byte aligned");
   if (!d->last_tok || !d->opt_ids || !d->n_opts || !d->kinds || !d->temperature || !d->probs || !d->argmax ||
       !d->confidence || !d->score)
     return sdb_fail(B200_ERR_ARG, "b200_decide: null array");
-  SDB_CUDA(launch_pdl(decide_kernel, dim3((d->n_rows + 3) / 4), dim3(128), 0, st, x, hidden, final_norm, eps, table,
+  SDB_CUDA(launch_pdl(decide_kernel, dim3(d->n_rows), dim3(DECIDE_THREADS), 0, st, x, hidden, final_norm, eps, table,
                       *d, vocab, n_tokens));
   return B200_OK;
 }

@@ -214,13 +214,14 @@ def test_linear_large_k_and_m_tail():
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-@pytest.mark.parametrize("m", [1, 16, 17, 64])
+@pytest.mark.parametrize("m", [1, 16, 17, 64, 96, 128])
 @pytest.mark.parametrize("ep", ["store", "resid", "swiglu"])
 def test_linear_small_m_matches_reference(fmt, m, ep):
-    """Batches of at most 64 rows run the swap-AB kernel (weights as the MMA's 128-row A
-    operand, tokens as N = 16 or 64; split K for the store and residual epilogues, whole K with
-    the weight ring refilled for the SwiGLU): fp64 product of the same operands, and the CUDA-
-    core cross-check."""
+    """Batches of at most 128 rows on packed weights run the swap-AB kernel (weights decoded
+    into tensor memory as the MMA's 128-row A operand, both activation planes in one B operand
+    of N = 2 x 16, 64 or 128 tokens; split K for the store and residual epilogues, whole K with
+    the weight ring refilled for the SwiGLU; bf16 weights take the general kernel): fp64 product
+    of the same operands, and the CUDA-core cross-check."""
     from strands_decider_b200 import _lib
     from strands_decider_b200 import weights as W
 
@@ -249,7 +250,7 @@ def test_linear_small_m_matches_reference(fmt, m, ep):
 @pytest.mark.parametrize("split", [True, False])
 def test_linear_small_m_whole_k_with_weight_ring(split):
     """96 weight tiles of 128 rows leave no room to split K: each CTA streams all 32 k-blocks
-    through its 16-slot weight ring (the refill path), one or two activation planes."""
+    through its weight ring (the refill path), one or two activation planes."""
     from strands_decider_b200 import _lib
     from strands_decider_b200 import weights as W
 
