@@ -687,8 +687,10 @@ __device__ __forceinline__ void swap_ab_epilogue(const GemmArgs& args, int n0, i
 #pragma unroll
   for (int t = 0; t < TC; ++t) sT[t * SWAP_LD + 32 * q + lane] = v[t];
   asm volatile("bar.sync 1, 128;" ::: "memory");
-#pragma unroll 1
-  for (int t = q; t < TC && t0 + t < args.m; t += 4) {
+#pragma unroll
+  for (int tt = 0; tt < TC / 4; ++tt) {
+    const int t = q + 4 * tt;
+    if (t0 + t >= args.m) break;
     const size_t row = size_t(t0 + t) * o.ldo;
     const float* st = sT + t * SWAP_LD;
     if constexpr (EP == B200_EP_SWIGLU) {
@@ -745,45 +747,50 @@ constexpr int SK_ROWS = 128;  // weight rows per swap-AB tile (the MMA's M)
 // The two activation planes form one B operand (hi tokens in rows 0..NT-1, lo tokens in rows
 // NT..2NT-1 of the slot), so one MMA per 16 k covers both and the epilogue adds the column
 // halves of the accumulator.
-//   warp 0      producer: packed weight k-blocks (1-D bulk copies into TS_WSLOTS slots, the
-//               first ones before the programmatic-dependent wait: weights do not depend on
-//               the kernel before) and activation planes (TMA, NT rows x 64 k per plane; rows
-//               past m read as zeros)
+//   warp 0      activation producer: both planes of each k-block (TMA, tile_m rows x 64 k per
+//               plane; rows past m read as zeros) into as many slots as shared memory holds
 //   warp 1      TMEM and the MMAs: per 16 k one tcgen05.mma, M = 128, N = NT or 2 NT,
 //               A = the weight stage in TMEM, B = the activation slot
-//   warps 2..5  epilogue: TMEM lane quarter -> registers -> swap_ab_epilogue, 32 tokens a chunk
+//   warps 2..5  first the weights: one lane runs the packed weight ring (1-D bulk copies into
+//               TS_WSLOTS slots, each refilled once decoded), the others pull later k-blocks
+//               into L2; then the epilogue: TMEM lane quarter -> registers -> swap_ab_epilogue
 //   warps 6..13 unpack: warp w decodes the 32-k half (w - 6) / 4 of rows 32 (w % 4) ..
 //               32 (w % 4) + 31 (its TMEM lane quarter) of each k-block into 16 columns of a
 //               32-column TMEM stage (two bf16 per column, lower k in the low half); same
 //               decode as every other GEMM here, bit-exact with b200_dequantize
 constexpr int TS_STAGES = 4;
 constexpr int TS_WSLOTS = 8;
+constexpr int TS_MAX_XSLOTS = 16;
 constexpr int TS_MAX_M = 128;
 constexpr int TS_UNPACK_WARPS = 8;
 constexpr int TS_THREADS = 32 * (GEMM_UNPACK_WARP0 + TS_UNPACK_WARPS);  // 448
+constexpr int TS_SMEM_LIMIT = 227 * 1024;
 
 constexpr int pow2_cols(int c) { return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512; }
 
+// Shared memory: activation slots (args.xslots x X_STAGE, 1024-aligned), then the packed weight
+// slots, their scales, the epilogue's staging tile, the barriers, the TMEM address and the
+// ternary table. NT is the token capacity (16 or 128); the tile actually loaded and multiplied
+// is args.tile_m rows (m rounded up to 16), so the MMA's N, the slot size and the slot count
+// follow the batch at run time.
 template <int FMT, int PL, int NT>
 struct TsSmem {
   static_assert(FMT != B200_W_BF16 && PL != PL_LO8, "packed weights and one or two bf16 activation planes");
-  static_assert(NT == 16 || NT == 64 || NT == 128, "token tiles of 16, 64 or 128");
-  static constexpr int N = PL == PL_SPLIT ? 2 * NT : NT;   // the MMA's N: hi tokens, then lo tokens
-  static constexpr int X_PLANE = NT * GEMM_BK * 2;          // one plane of one k-block (NT rows of 128 B)
-  static constexpr int X_STAGE = N * GEMM_BK * 2;
-  static constexpr int XSLOTS = X_STAGE <= 4096 ? 16 : X_STAGE <= 8192 ? 8 : 4;
+  static_assert(NT == 16 || NT == 128, "token capacities of 16 or 128");
+  static constexpr int PLANES = PL == PL_SPLIT ? 2 : 1;
   static constexpr int W_BYTES = SK_ROWS * tile_row_bytes(FMT);
   static constexpr int S_BYTES = SK_ROWS * tile_scale_row_bytes(FMT);
   static constexpr int TC = NT < 32 ? NT : 32;                // epilogue tokens per chunk
   static constexpr int SWAP_BYTES = TC * SWAP_LD * 4;         // the epilogue's staging tile
-  static constexpr int ACC_COLS = N < 32 ? 32 : N;          // accumulator columns 0 .. N-1
-  static constexpr int A_COL0 = ACC_COLS;                   // weight stage s: columns A_COL0 + 32 s ..
-  static constexpr int TM_COLS = pow2_cols(A_COL0 + 32 * TS_STAGES);
-  static constexpr int BARS = 2 * TS_WSLOTS + 2 * XSLOTS + 2 * TS_STAGES + 1;
-  static constexpr int TOTAL =
-      XSLOTS * X_STAGE + TS_WSLOTS * (W_BYTES + S_BYTES) + SWAP_BYTES + BARS * 8 + 16 + 64 + 1024;
-  static_assert(X_PLANE % 1024 == 0, "128-byte-swizzled activation tiles need 1024-byte alignment");
-  static_assert(A_COL0 + 32 * TS_STAGES <= TM_COLS && TM_COLS <= 512, "TMEM columns");
+  // TMEM: args.accs accumulators of acc_stride(tile_m) columns from column 0, then the weight
+  // stages (stage s at columns a_col0 + 32 s); capacity 16 allocates 256 columns, 128 all 512
+  static constexpr int TM_COLS = NT < 32 ? 256 : 512;
+  static constexpr int acc_stride(int tile_m) { return (PLANES * tile_m + 31) / 32 * 32; }
+  static constexpr int max_accs(int tile_m) { return 2 * acc_stride(tile_m) + 32 * TS_STAGES <= TM_COLS ? 2 : 1; }
+  static constexpr int BARS = 2 * TS_WSLOTS + 2 * TS_MAX_XSLOTS + 2 * TS_STAGES + 1;
+  static constexpr int FIXED = TS_WSLOTS * (W_BYTES + S_BYTES) + SWAP_BYTES + BARS * 8 + 16 + 64;
+  static constexpr int x_stage(int tile_m) { return PLANES * tile_m * GEMM_BK * 2; }
+  static_assert(acc_stride(NT) + 32 * TS_STAGES <= TM_COLS, "TMEM columns");
 };
 
 template <int FMT, int EP, int PL, int NT>
@@ -792,17 +799,20 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                    const GemmArgs args) {
   using SM = TsSmem<FMT, PL, NT>;
   extern __shared__ uint8_t smem_raw[];
+  const int tile_m = args.tile_m, xslots = args.xslots, accs = args.accs;
+  const int acc_stride = SM::acc_stride(tile_m), a_col0 = accs * acc_stride;
+  const int x_plane = tile_m * GEMM_BK * 2, x_stage = SM::x_stage(tile_m);
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sX = smem;                                // XSLOTS x X_STAGE
-  uint8_t* sW = sX + SM::XSLOTS * SM::X_STAGE;       // TS_WSLOTS x W_BYTES
+  uint8_t* sX = smem;                                // xslots x x_stage
+  uint8_t* sW = sX + xslots * x_stage;               // TS_WSLOTS x W_BYTES
   uint8_t* sS = sW + TS_WSLOTS * SM::W_BYTES;        // TS_WSLOTS x S_BYTES
   float* sT = reinterpret_cast<float*>(sS + TS_WSLOTS * SM::S_BYTES);  // [TC][SWAP_LD]
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sT) + SM::SWAP_BYTES);
   uint64_t* full_w = bars;                           // [WSLOTS] weight slot landed
   uint64_t* empty_w = bars + TS_WSLOTS;              // [WSLOTS] weight slot decoded
-  uint64_t* full_x = bars + 2 * TS_WSLOTS;           // [XSLOTS] activation slot landed
-  uint64_t* empty_x = full_x + SM::XSLOTS;           // [XSLOTS] the slot's MMAs are done
-  uint64_t* full_a = empty_x + SM::XSLOTS;           // [STAGES] TMEM weight stage written
+  uint64_t* full_x = bars + 2 * TS_WSLOTS;           // [xslots] activation slot landed
+  uint64_t* empty_x = full_x + TS_MAX_XSLOTS;        // [xslots] the slot's MMAs are done
+  uint64_t* full_a = empty_x + TS_MAX_XSLOTS;        // [STAGES] TMEM weight stage written
   uint64_t* empty_a = full_a + TS_STAGES;            // [STAGES] the stage's MMAs are done
   uint64_t* acc_full = empty_a + TS_STAGES;          // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
@@ -816,21 +826,34 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
   const int kb0 = ks * nk / args.ksplit, kb1 = (ks + 1) * nk / args.ksplit;
   const int nkb = kb1 - kb0;
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < TS_WSLOTS; ++i) {
-      mbar_init(&full_w[i], 1);
-      mbar_init(&empty_w[i], TS_UNPACK_WARPS);  // one arrival per unpack warp
+  // this tile's packed rows inside the 256-row streaming tiles: tile n0 / 256, row offset n0 % 256
+  constexpr int RB = tile_row_bytes(FMT), SB = tile_scale_row_bytes(FMT);
+  const size_t lt = size_t(n0 / GEMM_TILE_ROWS) * nk, sub = n0 % GEMM_TILE_ROWS;
+  const uint8_t* wtiles = reinterpret_cast<const uint8_t*>(args.w.tiles) + sub * RB;
+  const uint8_t* stiles = reinterpret_cast<const uint8_t*>(args.w.tile_scales) + sub * SB;
+  auto issue_w = [&](int i) {  // k-block kb0 + i into slot i % WSLOTS
+    const int slot = i % TS_WSLOTS;
+    const size_t kt = lt + kb0 + i;
+    mbar_arrive_expect_tx(&full_w[slot], SM::W_BYTES + SM::S_BYTES);
+    bulk_load(sW + slot * SM::W_BYTES, wtiles + kt * GEMM_TILE_ROWS * RB, SM::W_BYTES, &full_w[slot]);
+    if constexpr (SM::S_BYTES > 0)
+      bulk_load(sS + slot * SM::S_BYTES, stiles + kt * GEMM_TILE_ROWS * SB, SM::S_BYTES, &full_w[slot]);
+  };
+
+  if (warp == 0) {  // barriers: one lane each
+    for (int b = lane; b < SM::BARS; b += 32) {
+      uint32_t count = 1;
+      if (b < 2 * TS_WSLOTS) count = b < TS_WSLOTS ? 1 : TS_UNPACK_WARPS;       // full_w, empty_w
+      else if (b >= 2 * TS_WSLOTS + 2 * TS_MAX_XSLOTS && b < 2 * TS_WSLOTS + 2 * TS_MAX_XSLOTS + TS_STAGES)
+        count = TS_UNPACK_WARPS;                                                  // full_a
+      else if (b == SM::BARS - 1) count = accs;                                   // acc_full
+      mbar_init(&bars[b], count);
     }
-    for (int i = 0; i < SM::XSLOTS; ++i) {
-      mbar_init(&full_x[i], 1);
-      mbar_init(&empty_x[i], 1);
-    }
-    for (int s = 0; s < TS_STAGES; ++s) {
-      mbar_init(&full_a[s], TS_UNPACK_WARPS);
-      mbar_init(&empty_a[s], 1);
-    }
-    mbar_init(&acc_full[0], 1);
     mbar_fence_init();
+    if (lane == 0) {
+      tma_prefetch_desc(&tmX);
+      if constexpr (PL == PL_SPLIT) tma_prefetch_desc(&tmX_lo);
+    }
   }
   if (threadIdx.x < 16) lut[threadIdx.x] = ternary_pair_bits(threadIdx.x);
   if (warp == 1) {
@@ -843,84 +866,102 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   pdl_trigger();  // one unit per CTA: the next kernel may be scheduled now (it waits for this one's results)
 
+  // One MMA-issuing thread: k-blocks first, first + accs, ... into accumulator `first`. Issuing a
+  // tcgen05.mma costs its thread a fixed time whatever N is, so at small N two threads
+  // (accumulators) issue twice as fast; the epilogue adds them. With two, the activation slots
+  // are even in number, so each slot (and each of the 4 weight stages) serves one issuer.
+  auto mma_loop = [&](int first) {
+    const uint32_t idesc = umma_idesc_bf16(SK_ROWS, SM::PLANES * tile_m);
+    const uint32_t acc = tmem_base + uint32_t(first * acc_stride);
+    for (int i = first; i < nkb; i += accs) {
+      const int s = i % TS_STAGES, xs = i % xslots;
+      mbar_wait(&full_x[xs], (i / xslots) & 1, FAULT_GEMM_WAIT_FULL_A);
+      mbar_wait(&full_a[s], (i / TS_STAGES) & 1, FAULT_GEMM_WAIT_FULL_B);
+      tc_fence_after();
+      const uint64_t bd = umma_desc_sw128(smem_addr(sX + xs * x_stage));
+      const uint32_t ta = tmem_base + uint32_t(a_col0 + 32 * s);
+#pragma unroll
+      for (int j = 0; j < GEMM_BK / 16; ++j)  // 16 k = 8 TMEM columns of A, 32 bytes of B
+        umma_bf16_ts(acc, ta + uint32_t(8 * j), bd + 2 * j, idesc, (i >= accs || j != 0) ? 1u : 0u);
+      umma_commit(&empty_a[s]);
+      umma_commit(&empty_x[xs]);
+    }
+    umma_commit(&acc_full[0]);
+  };
+
   if (warp == 0) {
-    // ---------------- producer
+    // ---------------- activation producer (the weight ring has its own thread, warp 2)
     if (lane == 0) {
-      tma_prefetch_desc(&tmX);
-      if constexpr (PL == PL_SPLIT) tma_prefetch_desc(&tmX_lo);
-      constexpr int RB = tile_row_bytes(FMT), SB = tile_scale_row_bytes(FMT);
-      // this tile's rows inside the 256-row streaming tiles: tile n0 / 256, row offset n0 % 256
-      const size_t lt = size_t(n0 / GEMM_TILE_ROWS) * nk, sub = n0 % GEMM_TILE_ROWS;
-      const uint8_t* wtiles = reinterpret_cast<const uint8_t*>(args.w.tiles) + sub * RB;
-      const uint8_t* stiles = reinterpret_cast<const uint8_t*>(args.w.tile_scales) + sub * SB;
-      auto issue_w = [&](int i) {  // k-block kb0 + i into slot i % WSLOTS
-        const int slot = i % TS_WSLOTS;
-        const size_t kt = lt + kb0 + i;
-        mbar_arrive_expect_tx(&full_w[slot], SM::W_BYTES + SM::S_BYTES);
-        bulk_load(sW + slot * SM::W_BYTES, wtiles + kt * GEMM_TILE_ROWS * RB, SM::W_BYTES, &full_w[slot]);
-        if constexpr (SM::S_BYTES > 0)
-          bulk_load(sS + slot * SM::S_BYTES, stiles + kt * GEMM_TILE_ROWS * SB, SM::S_BYTES, &full_w[slot]);
-      };
-      for (int i = 0; i < min(nkb, TS_WSLOTS); ++i) issue_w(i);
       pdl_wait();  // the activations come from the kernel before this one
       for (int i = 0; i < nkb; ++i) {
-        const int xs = i % SM::XSLOTS;
-        mbar_wait(&empty_x[xs], ((i / SM::XSLOTS) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
-        mbar_arrive_expect_tx(&full_x[xs], SM::X_STAGE);
-        tma_load_2d(sX + xs * SM::X_STAGE, &tmX, &full_x[xs], (kb0 + i) * GEMM_BK, 0);
+        const int xs = i % xslots;
+        mbar_wait(&empty_x[xs], ((i / xslots) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
+        mbar_arrive_expect_tx(&full_x[xs], uint32_t(x_stage));
+        tma_load_2d(sX + xs * x_stage, &tmX, &full_x[xs], (kb0 + i) * GEMM_BK, 0);
         if constexpr (PL == PL_SPLIT)
-          tma_load_2d(sX + xs * SM::X_STAGE + SM::X_PLANE, &tmX_lo, &full_x[xs], (kb0 + i) * GEMM_BK, 0);
-        if (i + TS_WSLOTS < nkb) {  // refill weight slot i once its k-block is decoded
-          mbar_wait(&empty_w[i % TS_WSLOTS], (i / TS_WSLOTS) & 1, FAULT_GEMM_WAIT_EMPTY);
-          issue_w(i + TS_WSLOTS);
-        }
+          tma_load_2d(sX + xs * x_stage + x_plane, &tmX_lo, &full_x[xs], (kb0 + i) * GEMM_BK, 0);
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer: D[weight row][token] += W_stage (TMEM) . X_slot^T
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(SK_ROWS, SM::N);
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % TS_STAGES, xs = i % SM::XSLOTS;
-        mbar_wait(&full_x[xs], (i / SM::XSLOTS) & 1, FAULT_GEMM_WAIT_FULL_A);
-        mbar_wait(&full_a[s], (i / TS_STAGES) & 1, FAULT_GEMM_WAIT_FULL_B);
-        tc_fence_after();
-        const uint64_t bd = umma_desc_sw128(smem_addr(sX + xs * SM::X_STAGE));
-        const uint32_t ta = tmem_base + uint32_t(SM::A_COL0 + 32 * s);
-#pragma unroll
-        for (int j = 0; j < GEMM_BK / 16; ++j)  // 16 k = 8 TMEM columns of A, 32 bytes of B
-          umma_bf16_ts(tmem_base, ta + uint32_t(8 * j), bd + 2 * j, idesc, (i | j) != 0 ? 1u : 0u);
-        umma_commit(&empty_a[s]);
-        umma_commit(&empty_x[xs]);
-      }
-      umma_commit(&acc_full[0]);
-    }
+    // ---------------- MMA issuer: D[weight row][token] += W_stage (TMEM) . X_slot^T (k-blocks
+    // of parity 0 when a second issuer in warp 3 takes parity 1)
+    if (lane == 0) mma_loop(0);
     __syncwarp();
   } else if (warp < GEMM_UNPACK_WARP0) {
     // ---------------- epilogue: quarter q holds weight rows n0 + 32q .. n0 + 32q + 31
     const int q = warp & 3;
+    // Until the accumulator is ready, the epilogue warps feed the weights (which do not depend
+    // on the kernel before this one): lane 0 of warp 2 runs the weight ring (its first
+    // TS_WSLOTS k-blocks, then a refill as each slot is decoded); warps 3..5 pull the K range's
+    // later k-blocks into L2, one per thread, so that the refills come from L2.
+    if (warp == GEMM_EPI_WARP0 + 1 && accs == 2) {  // ---------------- the second MMA issuer
+      if (lane == 0) mma_loop(1);
+      __syncwarp();
+    }
+    if (warp == GEMM_EPI_WARP0) {
+      if (lane == 0) {
+        for (int i = 0; i < min(nkb, TS_WSLOTS); ++i) issue_w(i);
+        for (int i = TS_WSLOTS; i < nkb; ++i) {
+          mbar_wait(&empty_w[i % TS_WSLOTS], ((i / TS_WSLOTS) - 1) & 1, FAULT_GEMM_WAIT_EMPTY);
+          issue_w(i);
+        }
+      }
+      __syncwarp();
+    } else {
+      const int i = TS_WSLOTS + (warp - GEMM_EPI_WARP0 - 1) * 32 + lane;
+      if (i < nkb) {
+        const size_t kt = lt + kb0 + i;
+        bulk_prefetch_l2(wtiles + kt * GEMM_TILE_ROWS * RB, SM::W_BYTES);
+        if constexpr (SM::S_BYTES > 0) bulk_prefetch_l2(stiles + kt * GEMM_TILE_ROWS * SB, SM::S_BYTES);
+      }
+    }
     pdl_wait();  // the output (or residual) may be read or written by the kernel before this one
     mbar_wait(&acc_full[0], 0, FAULT_GEMM_WAIT_ACCUM);
     tc_fence_after();
     const uint32_t tl = tmem_base + (uint32_t(q * 32) << 16);
     constexpr int TC = SM::TC;
 #pragma unroll 1
-    for (int t0 = 0; t0 < NT && t0 < args.m; t0 += TC) {
+    for (int t0 = 0; t0 < tile_m && t0 < args.m; t0 += TC) {
       float v[TC];
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tl + uint32_t(t0), r);  // NT = 16: hi in columns 0..15, lo in 16..31
-      tmem_ld_wait();
 #pragma unroll
-      for (int t = 0; t < TC; ++t) v[t] = __uint_as_float(r[t]);
-      if constexpr (PL == PL_SPLIT) {
-        if constexpr (NT < 32) {
+      for (int t = 0; t < TC; ++t) v[t] = 0.0f;
+      for (int a = 0; a < accs; ++a) {
+        const uint32_t ta = tl + uint32_t(a * acc_stride);
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(ta + uint32_t(t0), r);  // capacity 16: hi in columns 0..15, lo in 16..31
+        tmem_ld_wait();
 #pragma unroll
-          for (int t = 0; t < TC; ++t) v[t] += __uint_as_float(r[NT + t]);
-        } else {
-          tmem_ld_32x32b_x32(tl + uint32_t(NT + t0), r);
-          tmem_ld_wait();
+        for (int t = 0; t < TC; ++t) v[t] += __uint_as_float(r[t]);
+        if constexpr (PL == PL_SPLIT) {
+          if constexpr (NT < 32) {
 #pragma unroll
-          for (int t = 0; t < TC; ++t) v[t] += __uint_as_float(r[t]);
+            for (int t = 0; t < TC; ++t) v[t] += __uint_as_float(r[NT + t]);
+          } else {
+            tmem_ld_32x32b_x32(ta + uint32_t(tile_m + t0), r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int t = 0; t < TC; ++t) v[t] += __uint_as_float(r[t]);
+          }
         }
       }
       swap_ab_epilogue<EP, TC>(args, n0, q, lane, t0, v, sT);
@@ -932,7 +973,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     const uint32_t row_sc =
         FMT == B200_W_TERNARY ? uint32_t(__ldg(reinterpret_cast<const uint16_t*>(args.w.scales) + n0 + r)) : 0u;
     const float row_gs = FMT == B200_W_NVFP4 ? __ldg(args.w.row_scale + n0 + r) : 1.0f;
-    const uint32_t ta = tmem_base + (uint32_t(32 * q) << 16) + uint32_t(SM::A_COL0 + 16 * h);
+    const uint32_t ta = tmem_base + (uint32_t(32 * q) << 16) + uint32_t(a_col0 + 16 * h);
     for (int i = 0; i < nkb; ++i) {
       const int s = i % TS_STAGES, ws = i % TS_WSLOTS;
       mbar_wait(&full_w[ws], (i / TS_WSLOTS) & 1, FAULT_GEMM_WAIT_FULL_W);
@@ -1168,26 +1209,33 @@ static int dispatch_simt(const uint16_t* x, const uint16_t* xl, int ldx, const G
 }
 
 // The TMEM-weight kernel: K split so that about one unit per SM exists (the SwiGLU needs
-// whole sums and is never split); a split store first zeroes its output.
+// whole sums and is never split); a split store first zeroes its output. The activation tile is
+// m rounded up to 16 rows; as many activation slots as the shared memory holds (at most 16).
 template <int FMT, int EP, int PL, int NT>
 static int launch_ts(const CUtensorMap& mx, const CUtensorMap& mx_lo, const GemmArgs& a, cudaStream_t st) {
   using SM = TsSmem<FMT, PL, NT>;
-  static_assert(SM::TOTAL <= 227 * 1024, "small-M GEMM shared memory exceeds the 227 KB per-CTA limit");
   static DeviceOnce attr;
   const int r = once_per_device(attr, [](int) -> int {
     SDB_CUDA(cudaFuncSetAttribute(gemm_ts_kernel<FMT, EP, PL, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  SM::TOTAL));
+                                  TS_SMEM_LIMIT));
     return B200_OK;
   });
   if (r != B200_OK) return r;
   GemmArgs args = a;
   const int tiles = a.w.n / SK_ROWS, nk = a.k / GEMM_BK;
   args.ksplit = EP == B200_EP_SWIGLU ? 1 : std::max(1, std::min(sm_count() / tiles, nk / 2));
+  args.tile_m = (a.m + 15) / 16 * 16;
+  const int x_stage = SM::x_stage(args.tile_m);
+  args.xslots = std::min(TS_MAX_XSLOTS, (TS_SMEM_LIMIT - 1024 - SM::FIXED) / x_stage);
+  args.accs = SM::max_accs(args.tile_m);
+  if (args.accs == 2) args.xslots &= ~1;  // each slot serves one of the two MMA issuers
+  if (args.tile_m > NT || args.xslots < 2) return sdb_fail(B200_ERR_SHAPE, "b200_linear: small-M tile does not fit");
+  const int smem = 1024 + args.xslots * x_stage + SM::FIXED;
   if (args.ksplit > 1 && EP == B200_EP_STORE)
     SDB_CUDA(launch_pdl(zero_rows_kernel, dim3(a.m), dim3(256), 0, st, reinterpret_cast<float*>(a.o.out), a.o.ldo,
                         a.o.n_valid));
-  SDB_CUDA(launch_pdl(gemm_ts_kernel<FMT, EP, PL, NT>, dim3(tiles * args.ksplit), dim3(TS_THREADS), SM::TOTAL, st,
-                      mx, mx_lo, args));
+  SDB_CUDA(launch_pdl(gemm_ts_kernel<FMT, EP, PL, NT>, dim3(tiles * args.ksplit), dim3(TS_THREADS), smem, st, mx,
+                      mx_lo, args));
   return B200_OK;
 }
 
@@ -1209,16 +1257,9 @@ static int dispatch_ts(const CUtensorMap& mx, const CUtensorMap& mx_lo, const Ge
   }
 }
 
-// Token tile of the TMEM-weight kernel: 16, 64 or 128 rows.
-static int ts_tile(int m) { return m <= 16 ? 16 : m <= 64 ? 64 : 128; }
-
 template <int PL>
 static int dispatch_ts_nt(const CUtensorMap& mx, const CUtensorMap& mx_lo, const GemmArgs& a, cudaStream_t st) {
-  switch (ts_tile(a.m)) {
-    case 16: return dispatch_ts<PL, 16>(mx, mx_lo, a, st);
-    case 64: return dispatch_ts<PL, 64>(mx, mx_lo, a, st);
-    default: return dispatch_ts<PL, 128>(mx, mx_lo, a, st);
-  }
+  return a.m <= 16 ? dispatch_ts<PL, 16>(mx, mx_lo, a, st) : dispatch_ts<PL, 128>(mx, mx_lo, a, st);
 }
 
 }  // namespace sdb
@@ -1239,7 +1280,7 @@ extern "C" int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m
   GemmArgs a{*w, *out, m, k, 1};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (m <= TS_MAX_M && w->format != B200_W_BF16) {  // small M, packed weights: decoded into TMEM (swap-AB)
-    const int nt = ts_tile(m);
+    const int nt = (m + 15) / 16 * 16;
     CUtensorMap mx, mx_lo;
     if (int rc = make_act_map(&mx, x_hi, m, k, ldx, nt)) return rc;
     if (x_lo) {

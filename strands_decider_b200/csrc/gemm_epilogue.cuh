@@ -13,6 +13,9 @@ struct GemmArgs {
   int m, k;
   int ksplit;  // > 1: each output tile is summed from ksplit K-ranges by fp32 atomic adds
   int ngroup;  // CTA pairs: N tiles per group (units walk all row tiles of one group, then the next)
+  int tile_m;  // small-M kernel: token rows per activation plane (m rounded up to 16)
+  int xslots;  // small-M kernel: activation k-blocks held in shared memory at once
+  int accs;    // small-M kernel: TMEM accumulators (= MMA-issuing threads), 1 or 2
 };
 
 // --------------------------------------------------------------------------- epilogue
