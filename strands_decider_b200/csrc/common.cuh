@@ -176,6 +176,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// mbar_wait for waiters off the critical path (a warp that idles until a late phase): after
+// each failed test the thread sleeps, so that it takes no issue slots from the warps that
+// produce the phase.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, unsigned int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (true) {
+    __nanosleep(256);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++it & 63u) == 0) {
+      if (*reinterpret_cast<volatile unsigned int*>(&g_fault) != 0) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_fault(site);
+        return false;
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -936,7 +936,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
       }
     }
     pdl_wait();  // the output (or residual) may be read or written by the kernel before this one
-    mbar_wait(&acc_full[0], 0, FAULT_GEMM_WAIT_ACCUM);
+    mbar_wait_idle(&acc_full[0], 0, FAULT_GEMM_WAIT_ACCUM);
     tc_fence_after();
     const uint32_t tl = tmem_base + (uint32_t(q * 32) << 16);
     constexpr int TC = SM::TC;
