@@ -1112,6 +1112,7 @@ def main() -> None:
     # the timed graphs' last answers for the first batch (its first requests are the CPU sample's)
     b0_probs = (graphs[0].out.probs if use_graph else run_step(model, batches[0], stream).probs).cpu()
     t = torch.tensor([ms, ms_e2e, float(decisions), float(tokens)], device="cuda")
+    per_rank = None
     if world > 1:
         g = [torch.zeros_like(t) for _ in range(world)]
         dist.all_gather(g, t)
@@ -1119,6 +1120,10 @@ def main() -> None:
         ms_e2e = max(float(x[1]) for x in g)
         total = sum(float(x[2]) for x in g)
         total_tok = sum(float(x[3]) for x in g)
+        # each rank's own device time and work per step: the LPT shards' balance
+        per_rank = [{"rank": r, "ms_per_step": round(float(x[0]) / args.steps, 3),
+                     "tokens_per_step": int(float(x[3]) / args.steps),
+                     "decisions_per_step": int(float(x[2]) / args.steps)} for r, x in enumerate(g)]
     else:
         total, total_tok = float(decisions), float(tokens)
     value = total / (ms * 1e-3)
@@ -1180,6 +1185,8 @@ def main() -> None:
                             for b in (batches[(args.warmup + i) % len(batches)] for i in range(args.steps))) * world,
         "roofline": roof, "clocks": clk, "cpu_baseline": cb, "parity": par, **extras,
     }
+    if per_rank:
+        line["per_rank"] = per_rank
     print(json.dumps(line), flush=True)
 
 

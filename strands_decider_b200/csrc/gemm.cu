@@ -1262,6 +1262,10 @@ static int dispatch_ts_nt(const CUtensorMap& mx, const CUtensorMap& mx_lo, const
   return a.m <= 16 ? dispatch_ts<PL, 16>(mx, mx_lo, a, st) : dispatch_ts<PL, 128>(mx, mx_lo, a, st);
 }
 
+// b200_linear takes the small-M kernel (whose store epilogue splits K and clears its output
+// with a separate launch) for these batches.
+bool linear_small_m(int32_t m, int32_t format) { return m <= TS_MAX_M && format != B200_W_BF16; }
+
 }  // namespace sdb
 
 using namespace sdb;
@@ -1279,7 +1283,7 @@ extern "C" int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m
   }
   GemmArgs a{*w, *out, m, k, 1};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (m <= TS_MAX_M && w->format != B200_W_BF16) {  // small M, packed weights: decoded into TMEM (swap-AB)
+  if (linear_small_m(m, w->format)) {  // small M, packed weights: decoded into TMEM (swap-AB)
     const int nt = (m + 15) / 16 * 16;
     CUtensorMap mx, mx_lo;
     if (int rc = make_act_map(&mx, x_hi, m, k, ldx, nt)) return rc;

@@ -52,15 +52,22 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, int rows, int hidden
 }
 
 // Few rows (a latency-bound batch): one 256-thread block per row, the row held in registers
-// (hidden <= 4096, hidden % 1024 == 0), so each row costs one load round trip.
+// (hidden <= 4096, hidden % 1024 == 0), so each row costs one load round trip. With `zero`,
+// each block also clears row `row` of that fp32 [rows, zero_ld] buffer (zero_n floats, a
+// multiple of 4): the next GEMM's split-K accumulator, so that it needs no clearing launch.
 __global__ void __launch_bounds__(256) rmsnorm_block_kernel(const float* __restrict__ x, int hidden,
                                                             const float* __restrict__ w, float eps,
                                                             uint16_t* __restrict__ out, long long lo_offset,
-                                                            int lo8) {
+                                                            int lo8, float* __restrict__ zero, int zero_ld,
+                                                            int zero_n) {
   __shared__ float part[8];
   pdl_wait();  // inputs come from the kernel before this one (programmatic dependent launch)
   pdl_trigger();
   const int row = blockIdx.x, tid = threadIdx.x;
+  if (zero) {
+    float4* z = reinterpret_cast<float4*>(zero + size_t(row) * zero_ld);
+    for (int i = tid; i < zero_n / 4; i += 256) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   const int n4 = hidden / 1024;  // float4 per thread
   const float4* xr = reinterpret_cast<const float4*>(x + size_t(row) * hidden);
   float4 v[4];
@@ -483,13 +490,21 @@ int sdb_embed_vocab(const int32_t* ids, int32_t n_tokens, const uint16_t* table,
   return B200_OK;
 }
 
+// `zero` (optional, fp32 [rows, zero_ld], zero_n floats per row cleared): only with the
+// one-block-per-row form, which rmsnorm_folds_zero() tells the caller in advance.
+bool rmsnorm_folds_zero(int32_t rows, int32_t hidden) { return rows <= 1024 && hidden % 1024 == 0 && hidden <= 4096; }
+
 int sdb_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
-                int64_t lo_offset, int lo8, cudaStream_t st) {
+                int64_t lo_offset, int lo8, cudaStream_t st, float* zero, int32_t zero_ld, int32_t zero_n) {
   if (!x || !w || !out) return sdb_fail(B200_ERR_ARG, "b200_rmsnorm: null pointer");
   if (rows <= 0 || hidden % 128 != 0 || lo_offset % 8 != 0 || (reinterpret_cast<uintptr_t>(out) & 15))
     return sdb_fail(B200_ERR_SHAPE, "b200_rmsnorm: hidden % 128 and lo_offset % 8 must be 0, out 16-byte aligned");
-  if (rows <= 1024 && hidden % 1024 == 0 && hidden <= 4096)
-    SDB_CUDA(launch_pdl(rmsnorm_block_kernel, dim3(rows), dim3(256), 0, st, x, hidden, w, eps, out, lo_offset, lo8));
+  if (zero && (!rmsnorm_folds_zero(rows, hidden) || zero_n % 4 != 0 || zero_ld % 4 != 0 || zero_n > zero_ld ||
+               (reinterpret_cast<uintptr_t>(zero) & 15)))
+    return sdb_fail(B200_ERR_SHAPE, "b200_rmsnorm: bad region to clear");
+  if (rmsnorm_folds_zero(rows, hidden))
+    SDB_CUDA(launch_pdl(rmsnorm_block_kernel, dim3(rows), dim3(256), 0, st, x, hidden, w, eps, out, lo_offset, lo8,
+                        zero, zero_ld, zero_n));
   else
     SDB_CUDA(launch_pdl(rmsnorm_kernel, dim3((rows + 7) / 8), dim3(256), 0, st, x, rows, hidden, w, eps, out,
                         lo_offset, lo8));
@@ -498,13 +513,13 @@ int sdb_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, fl
 
 extern "C" int b200_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
                             int64_t lo_offset, b200_stream stream) {
-  return sdb_rmsnorm(x, rows, hidden, w, eps, out, lo_offset, 0, reinterpret_cast<cudaStream_t>(stream));
+  return sdb_rmsnorm(x, rows, hidden, w, eps, out, lo_offset, 0, reinterpret_cast<cudaStream_t>(stream), nullptr, 0, 0);
 }
 
 extern "C" int b200_rmsnorm_lo8(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
                                 int64_t lo_offset, b200_stream stream) {
   if (!lo_offset) return sdb_fail(B200_ERR_ARG, "b200_rmsnorm_lo8: lo_offset must locate the e4m3 plane");
-  return sdb_rmsnorm(x, rows, hidden, w, eps, out, lo_offset, 1, reinterpret_cast<cudaStream_t>(stream));
+  return sdb_rmsnorm(x, rows, hidden, w, eps, out, lo_offset, 1, reinterpret_cast<cudaStream_t>(stream), nullptr, 0, 0);
 }
 
 int sdb_decide_vocab(const float* x, int32_t hidden, const float* final_norm, float eps, const uint16_t* table,

@@ -53,7 +53,12 @@ int sdb_attention(const b200_attn_params* p, const b200_seqs* s, const float* qk
                   uint16_t* k_buf, uint16_t* v_buf, uint16_t* out, int64_t lo_offset, const b200_prefix_pool* pool,
                   int32_t layer, int lo8, cudaStream_t st);
 int sdb_rmsnorm(const float* x, int32_t rows, int32_t hidden, const float* w, float eps, uint16_t* out,
-                int64_t lo_offset, int lo8, cudaStream_t st);
+                int64_t lo_offset, int lo8, cudaStream_t st, float* zero = nullptr, int32_t zero_ld = 0,
+                int32_t zero_n = 0);
+bool rmsnorm_folds_zero(int32_t rows, int32_t hidden);
+namespace sdb {
+bool linear_small_m(int32_t m, int32_t format);
+}  // namespace sdb
 
 extern "C" const char* b200_last_error(void) { return g_last_error.c_str(); }
 extern "C" int b200_version(void) { return 100; }
@@ -339,18 +344,26 @@ extern "C" int b200_model_forward(b200_model* m, const int32_t* ids, const b200_
   if ((rc = sdb_embed_vocab(ids, T, m->embed, c.hidden, x, c.vocab, st))) return rc;
   for (int li = 0; li < c.n_layers; ++li) {
     const b200_layer_weights& w = m->layers[li];
-    if ((rc = sdb_rmsnorm(x, T, c.hidden, w.input_norm, c.eps, xn, L.xn_lo, lo8, st))) return rc;
+    // A small batch's in-projection splits K and accumulates its partials into `mix`: the
+    // norm before it clears `mix` and the GEMM adds into it (no clearing launch of its own).
+    const int n_in = c.layer_kind[li] == B200_LAYER_GDN ? m->gdn_in_cols() : m->attn_qkv();
+    const bool fold = !wdq8 && !m->dequant_at(T) && sdb::linear_small_m(T, w.mix_in.format) &&
+                      rmsnorm_folds_zero(T, c.hidden);
+    if ((rc = sdb_rmsnorm(x, T, c.hidden, w.input_norm, c.eps, xn, L.xn_lo, lo8, st, fold ? mix : nullptr, n_in,
+                          n_in)))
+      return rc;
+    const int in_ep = fold ? B200_EP_RESID_ADD : B200_EP_STORE;
     int mix_in_dim;
     if (c.layer_kind[li] == B200_LAYER_GDN) {
       const int n = m->gdn_in_cols();
-      b200_linear_out o{B200_EP_STORE, n, mix, n, 0};
+      b200_linear_out o{in_ep, n, mix, n, 0};
       if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.mix_in, o, wdq, wdq8, stream))) return rc;
       if ((rc = sdb_gdn_mixer(&w.gdn, seqs, mix, n, act, L.act_lo, pool, m->kind_index[li], prep, lo8, st)))
         return rc;
       mix_in_dim = m->value_dim();
     } else {
       const int n = m->attn_qkv();
-      b200_linear_out o{B200_EP_STORE, n, mix, n, 0};
+      b200_linear_out o{in_ep, n, mix, n, 0};
       if ((rc = run_linear(*m, xn, xn_lo, T, c.hidden, w.mix_in, o, wdq, wdq8, stream))) return rc;
       b200_attn_params ap{c.attn_heads, c.attn_kv_heads, c.head_dim, c.rope_dim, c.max_pos, c.eps,
                           w.q_norm, w.k_norm, m->rope_cos, m->rope_sin};
