@@ -5,8 +5,11 @@
 //   one query head each; the next kv_heads warps do the same for the keys, and the last
 //   kv_heads warps copy the values. Keys and values go to the batch scratch, and, for a
 //   sequence that saves its cache, to the prefix pool as well.
-// attn_flash_kernel: tensor-core flash attention over the prefix slot's keys (positions
-//   0..P-1) then the sequence's own keys (P..P+j), causal, times sigmoid(gate).
+// attn_tc_kernel: flash attention on tcgen05 (S and O in tensor memory, P written back to
+//   tensor memory as the A operand of P V) over the prefix slot's keys (positions 0..P-1) then
+//   the sequence's own keys (P..P+j), causal, times sigmoid(gate); 128-row tiles of the query
+//   heads that share a kv head. attn_flash_kernel (mma.sync) serves query groups of other
+//   sizes.
 #include <mutex>
 
 #include "common.cuh"
@@ -395,10 +398,437 @@ __global__ void __launch_bounds__(128 * fa_dg<HD>(), 2) attn_flash_kernel(const 
   }
 }
 
+// ----------------------------------------------------------------------------- tcgen05 flash kernel
+// Flash attention on the 5th-generation tensor cores. One CTA = 128 query rows of one sequence
+// and one kv head: the gqa query heads that share the kv head, 128 / gqa positions each (row
+// r = position (r / gqa), head (r % gqa)), so a short question fills the MMA and every K / V
+// tile serves all gqa heads at once.
+//   warp 0      TMA: the Q tile once (a 4-D box over [token][kv head][head in group][dim]),
+//               then each key tile's K into a 2-stage ring
+//   warp 1      TMEM and the MMAs: S_j = Q K_j^T (M = 128, N = 64 keys, K = head_dim; both
+//               operands K-major in shared memory) into one of two S buffers, then
+//               O += P_j V_j (A = P_j from TMEM, B = V_j MN-major in shared memory, N = head_dim)
+//   warps 2..9  softmax: two warps per TMEM lane quarter, each thread one query row (its lane)
+//               and half of the tile's 64 keys; the pair exchanges its row maxima through
+//               shared memory, so both take the same decisions. P_j goes to TMEM as bf16.
+//               Epilogue: O / l staged in the (then idle) Q / K / V shared memory, then written
+//               row by row by whole warps (coalesced gate loads and plane stores)
+//   warp 10     TMA: each key tile's V into its own 2-stage ring (freed only after P V)
+// Key tiles: the prefix slot's keys [0, P) in tiles of 64 (the last partial), then the
+// sequence's own [P, n_keys). Columns of a partial tile and keys after a query's position are
+// masked to -inf before the max; rows of a box past the keys hold finite values (the prefix
+// pool's other rows, other sequences' keys, or zeros past the tensor).
+// Online softmax with a lazy rescale: P = exp(s - m_ref) with m_ref raised (and O, l scaled
+// by exp(m_ref_old - m_ref_new), O read from and written back to TMEM by the same threads)
+// only when a tile's max exceeds m_ref by more than AT_RESCALE; otherwise P <= e^AT_RESCALE,
+// and since O and l share m_ref the quotient is the same.
+constexpr int AT_BK = 64;
+constexpr int AT_ROWS = 128;
+constexpr int AT_SOFTMAX_WARPS = 8;
+constexpr int AT_THREADS = 32 * (3 + AT_SOFTMAX_WARPS);  // 352
+constexpr int AT_V_WARP = 2 + AT_SOFTMAX_WARPS;          // 10
+constexpr float AT_RESCALE = 8.0f;
+
+template <int HD>
+struct AtSmem {
+  static constexpr int ATOMS = HD / 64;                // 64-wide head_dim atoms
+  static constexpr int Q_ATOM = AT_ROWS * 128;         // 128 rows x 128 bytes
+  static constexpr int Q_BYTES = ATOMS * Q_ATOM;
+  static constexpr int KV_ATOM = AT_BK * 128;          // 64 keys x 128 bytes
+  static constexpr int KV_BYTES = ATOMS * KV_ATOM;     // one K or V tile
+  static constexpr int BARS = 1 + 2 * 8;               // q_full; k/v full/empty, s full/empty, p_full, pv_done x2
+  static constexpr int O_LD = HD + 4;                   // fp32 row stride of the epilogue's staged O
+  static constexpr int XCH = 2 * 2 * AT_ROWS * 4;       // row maxima of the two halves, by tile parity
+  static constexpr int TOTAL = 1024 + Q_BYTES + 4 * KV_BYTES + XCH + 2 * AT_ROWS * 4 + BARS * 8 + 16;
+  static_assert(AT_ROWS * O_LD * 4 <= Q_BYTES + 4 * KV_BYTES, "the staged O fits in the Q / K / V buffers");
+  // TMEM columns: O [0, HD), S_b at HD + 64 b, P_b (bf16 pairs) at HD + 128 + 32 b
+  static constexpr int S_COL = HD, P_COL = HD + 2 * AT_BK;
+  static constexpr int TM_COLS = P_COL + AT_BK <= 256 ? 256 : 512;
+  static_assert(P_COL + AT_BK <= 512, "TMEM columns");
+};
+
+template <int HD>
+__global__ void __launch_bounds__(AT_THREADS, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKp,
+                   const __grid_constant__ CUtensorMap tmVp, const AttnArgs a) {
+  using SM = AtSmem<HD>;
+  extern __shared__ uint8_t at_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(at_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                         // [ATOMS][128 rows][128 B]
+  uint8_t* sK = sQ + SM::Q_BYTES;             // [2][ATOMS][64 keys][128 B]
+  uint8_t* sV = sK + 2 * SM::KV_BYTES;        // [2][ATOMS][64 keys][128 B]
+  float* xmax = reinterpret_cast<float*>(sV + 2 * SM::KV_BYTES);  // [2 parity][2 half][128 rows]
+  float* lsum = xmax + 4 * AT_ROWS;                                  // [2 half][128 rows]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(lsum + 2 * AT_ROWS);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2] the S MMA read the tile
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2] the P V MMA read the tile
+  uint64_t* s_full = bars + 9;   // [2] S_j in TMEM
+  uint64_t* s_empty = bars + 11; // [2] the softmax warps read S_j
+  uint64_t* p_full = bars + 13;  // [2] P_j in TMEM
+  uint64_t* pv_done = bars + 15; // [2] O += P_j V_j complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + SM::BARS);
+
+  pdl_wait();  // q / k / v come from the prep kernel before this one
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int seq = blockIdx.y, kh = blockIdx.z;
+  const int nq = a.p.heads, nkv = a.p.kv_heads, gqa = nq / nkv, QT = AT_ROWS / gqa;
+  const int tok0 = a.cu[seq], len = a.cu[seq + 1] - tok0;
+  const int q0 = blockIdx.x * QT;
+  if (q0 >= len) {  // the whole CTA leaves before any barrier or TMEM use
+    pdl_trigger();
+    return;
+  }
+  const int ps = a.prefix_slot ? a.prefix_slot[seq] : -1;
+  bool pv = ps >= 0 && ps < a.n_slots;
+  int P = pv ? a.slot_len[ps] : 0;
+  if (pv && (a.slot_kv[ps] < 0 || a.slot_kv[ps] + P > a.kv_capacity)) {
+    if (threadIdx.x == 0) raise_fault(FAULT_BAD_INDEX);
+    pv = false;
+    P = 0;
+  }
+  const int pbase = pv ? a.slot_kv[ps] : 0;
+  const int n_keys = P + min(len, q0 + QT);  // causal: the tile's last position sees these
+  const int npt = (P + AT_BK - 1) / AT_BK;   // prefix tiles
+  const int nt = npt + (n_keys - P + AT_BK - 1) / AT_BK;
+  // tile j covers keys [kk0, kk0 + valid)
+  auto tile_start = [&](int j) { return j < npt ? j * AT_BK : P + (j - npt) * AT_BK; };
+  auto tile_valid = [&](int j) { return j < npt ? min(AT_BK, P - j * AT_BK) : min(AT_BK, n_keys - tile_start(j)); };
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&k_full[b], 1);
+      mbar_init(&k_empty[b], 1);
+      mbar_init(&v_full[b], 1);
+      mbar_init(&v_empty[b], 1);
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], AT_SOFTMAX_WARPS);  // one arrival per softmax warp
+      mbar_init(&p_full[b], AT_SOFTMAX_WARPS);
+      mbar_init(&pv_done[b], 1);
+    }
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, SM::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ---------------- Q, then the K ring
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      mbar_arrive_expect_tx(q_full, SM::Q_BYTES);
+      for (int at = 0; at < SM::ATOMS; ++at) tma_load_4d(sQ + at * SM::Q_ATOM, &tmQ, q_full, 64 * at, 0, kh, tok0 + q0);
+      for (int j = 0; j < nt; ++j) {
+        const int b = j & 1;
+        mbar_wait_idle(&k_empty[b], ((j >> 1) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
+        mbar_arrive_expect_tx(&k_full[b], SM::KV_BYTES);
+        const bool pool = j < npt;
+        const int row = pool ? pbase + j * AT_BK : tok0 + tile_start(j) - P;
+        for (int at = 0; at < SM::ATOMS; ++at)
+          tma_load_3d(sK + (b * SM::ATOMS + at) * SM::KV_ATOM, pool ? &tmKp : &tmK, &k_full[b], 64 * at, kh, row);
+      }
+    }
+  } else if (warp == AT_V_WARP) {
+    // ---------------- the V ring
+    if (lane == 0) {
+      for (int j = 0; j < nt; ++j) {
+        const int b = j & 1;
+        mbar_wait_idle(&v_empty[b], ((j >> 1) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
+        mbar_arrive_expect_tx(&v_full[b], SM::KV_BYTES);
+        const bool pool = j < npt;
+        const int row = pool ? pbase + j * AT_BK : tok0 + tile_start(j) - P;
+        for (int at = 0; at < SM::ATOMS; ++at)
+          tma_load_3d(sV + (b * SM::ATOMS + at) * SM::KV_ATOM, pool ? &tmVp : &tmV, &v_full[b], 64 * at, kh, row);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMAs: S_j, then O += P_{j-1} V_{j-1} (the softmax of tile j-1 overlaps S_j)
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(AT_ROWS, AT_BK);
+      constexpr uint32_t idesc_pv = umma_idesc_bf16(AT_ROWS, HD) | (1u << 16);  // B (V) MN-major
+      mbar_wait(q_full, 0, FAULT_GEMM_WAIT_FULL_A);
+      for (int j = 0; j <= nt; ++j) {
+        if (j < nt) {
+          const int b = j & 1;
+          mbar_wait(&k_full[b], (j >> 1) & 1, FAULT_GEMM_WAIT_FULL_A);
+          if (j >= 2) mbar_wait(&s_empty[b], ((j - 2) >> 1) & 1, FAULT_GEMM_WAIT_EMPTY);
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < HD / 16; ++k) {  // 16 of head_dim per MMA: atom k / 4, +32 bytes each
+            const uint64_t ad = umma_desc_sw128(smem_addr(sQ + (k >> 2) * SM::Q_ATOM)) + 2 * (k & 3);
+            const uint64_t bd = umma_desc_sw128(smem_addr(sK + (b * SM::ATOMS + (k >> 2)) * SM::KV_ATOM)) + 2 * (k & 3);
+            umma_bf16(tmem + uint32_t(SM::S_COL + AT_BK * b), ad, bd, idesc_s, k > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[b]);
+          umma_commit(&k_empty[b]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, b = jj & 1;
+          mbar_wait(&v_full[b], (jj >> 1) & 1, FAULT_GEMM_WAIT_FULL_B);
+          mbar_wait(&p_full[b], (jj >> 1) & 1, FAULT_GEMM_WAIT_FULL_B);
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < AT_BK / 16; ++k) {  // 16 keys per MMA: 8 TMEM columns of P, 2048 bytes of V
+            const uint64_t bd =
+                umma_desc_sw128_mn(smem_addr(sV + b * SM::ATOMS * SM::KV_ATOM + k * 2048), SM::KV_ATOM, 1024);
+            umma_bf16_ts(tmem, tmem + uint32_t(SM::P_COL + (AT_BK / 2) * b + 8 * k), bd, idesc_pv,
+                         (jj > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&v_empty[b]);
+          umma_commit(&pv_done[b]);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax (warps 2..9: TMEM lane quarter warp % 4, key half hf), then the epilogue
+    const int qd = warp & 3, hf = (warp - 2) >> 2, r = 32 * qd + lane;
+    const int qloc = r / gqa;
+    const int qpos = P + q0 + qloc;  // keys at or before this position are visible
+    const uint32_t tl = tmem + (uint32_t(32 * qd) << 16);
+    const float scale = rsqrtf(float(HD));
+    constexpr int HK = AT_BK / 2;   // keys per thread per tile
+    constexpr int HO = HD / 2;      // O columns this warp rescales
+    float m_ref = -INFINITY, l = 0.0f;
+    for (int j = 0; j < nt; ++j) {
+      const int b = j & 1;
+      mbar_wait(&s_full[b], (j >> 1) & 1, FAULT_GEMM_WAIT_ACCUM);
+      tc_fence_after();
+      float x[HK];
+      {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tl + uint32_t(SM::S_COL + AT_BK * b + HK * hf), v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < HK; ++c) x[c] = __uint_as_float(v[c]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[b]);
+      const int kk0 = tile_start(j) + HK * hf, valid = tile_valid(j) - HK * hf;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < HK; ++c) {
+        const bool vis = c < valid && kk0 + c <= qpos;
+        x[c] = vis ? x[c] * scale : -INFINITY;
+        mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
+      }
+      // the row's max over both halves: through shared memory, by tile parity
+      float* xm = xmax + b * 2 * AT_ROWS;
+      xm[hf * AT_ROWS + r] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + qd) : "memory");
+      const float mt = fmaxf(xm[r], xm[AT_ROWS + r]);
+      // lazy rescale (the pair decides alike); warp-wide, since TMEM loads and stores are
+      // warp-collective
+      const bool raise = mt > m_ref + AT_RESCALE;
+      if (__any_sync(0xffffffffu, raise)) {
+        // a raised row's old terms shrink by exp(m_old - m_new) (none to keep at m_old = -inf)
+        const float m_new = raise ? mt : m_ref;
+        float alpha = 1.0f;
+        if (raise) alpha = m_ref == -INFINITY ? 0.0f : __expf(m_ref - m_new);
+        l *= alpha;
+        if (j >= 1) {  // O holds tiles < j: scale this warp's half once their P V products are done
+          mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, FAULT_GEMM_WAIT_ACCUM);
+          tc_fence_after();
+#pragma unroll 1
+          for (int c0 = HO * hf; c0 < HO * hf + HO; c0 += 32) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tl + uint32_t(c0), v);
+            tmem_ld_wait();
+            uint4 w[4], w2[4];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              reinterpret_cast<uint32_t*>(w)[c] = __float_as_uint(__uint_as_float(v[c]) * alpha);
+              reinterpret_cast<uint32_t*>(w2)[c] = __float_as_uint(__uint_as_float(v[16 + c]) * alpha);
+            }
+            tmem_st_32x32b_x16(tl + uint32_t(c0), w);
+            tmem_st_32x32b_x16(tl + uint32_t(c0 + 16), w2);
+          }
+          tmem_st_wait();
+        }
+        m_ref = m_new;
+      }
+      // P_j into TMEM buffer b (this thread's 32 keys: 16 columns), once P_{j-2} V_{j-2} read it
+      if (j >= 2) mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, FAULT_GEMM_WAIT_ACCUM);
+      tc_fence_after();
+      float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      uint4 pw[4];
+      // masked keys hold -inf, so exp gives 0; a row still at m_ref = -inf has only masked keys
+      const float mb = m_ref == -INFINITY ? 0.0f : m_ref;
+#pragma unroll
+      for (int c = 0; c < HK; c += 2) {
+        const float p0 = __expf(x[c] - mb);
+        const float p1 = __expf(x[c + 1] - mb);
+        rs4[(c >> 1) & 3] += p0 + p1;
+        reinterpret_cast<uint32_t*>(pw)[c / 2] = pack_bf16x2(p0, p1);
+      }
+      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+      tmem_st_32x32b_x16(tl + uint32_t(SM::P_COL + (AT_BK / 2) * b + (HK / 2) * hf), pw);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+    }
+    // ---- epilogue 1: O / l (this warp's half of the columns) staged in shared memory
+    lsum[hf * AT_ROWS + r] = l;
+    mbar_wait(&pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, FAULT_GEMM_WAIT_ACCUM);
+    tc_fence_after();
+    float* sO = reinterpret_cast<float*>(sQ);  // Q, K and V are all consumed by now
+#pragma unroll 1
+    for (int c0 = HO * hf; c0 < HO * hf + HO; c0 += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tl + uint32_t(c0), v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 32; c += 4)
+        *reinterpret_cast<float4*>(sO + r * SM::O_LD + c0 + c) = make_float4(
+            __uint_as_float(v[c]), __uint_as_float(v[c + 1]), __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3]));
+    }
+    asm volatile("bar.sync 5, %0;" ::"n"(32 * AT_SOFTMAX_WARPS) : "memory");
+    // ---- epilogue 2: rows by whole warps: O / l * sigmoid(gate) -> hi / lo planes. A batch of
+    // ER rows is loaded (gates read-only, O from shared memory) before any of it is stored, so
+    // the loads of a batch overlap rather than wait behind the previous row's stores.
+    constexpr int CPL = HD / 32;  // columns per lane
+    constexpr int ER = 4;         // rows per batch and warp
+    const int sw = warp - 2;
+#pragma unroll 1
+    for (int rb = sw; rb < AT_ROWS; rb += ER * AT_SOFTMAX_WARPS) {
+      float g[ER][CPL], o[ER][CPL], inv[ER];
+      bool ok[ER];
+#pragma unroll
+      for (int e = 0; e < ER; ++e) {
+        const int rr = rb + e * AT_SOFTMAX_WARPS, ql = rr / gqa;
+        ok[e] = rr < AT_ROWS && q0 + ql < len;
+        const float lt = ok[e] ? lsum[rr] + lsum[AT_ROWS + rr] : 0.0f;
+        inv[e] = lt > 0.0f ? 1.0f / lt : 0.0f;
+        const size_t t = size_t(tok0 + q0 + (ok[e] ? ql : 0));
+        const int h = kh * gqa + rr % gqa;
+        const float* gate = a.qkv + t * a.ld_qkv + size_t(h) * 2 * HD + HD + CPL * lane;
+        const float* orow = sO + (ok[e] ? rr : 0) * SM::O_LD + CPL * lane;
+#pragma unroll
+        for (int c = 0; c < CPL; c += 2) {
+          const float2 gv = ok[e] ? __ldg(reinterpret_cast<const float2*>(gate + c)) : make_float2(0.f, 0.f);
+          const float2 ov = *reinterpret_cast<const float2*>(orow + c);
+          g[e][c] = gv.x;
+          g[e][c + 1] = gv.y;
+          o[e][c] = ov.x;
+          o[e][c + 1] = ov.y;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < ER; ++e) {
+        if (!ok[e]) continue;
+        const int rr = rb + e * AT_SOFTMAX_WARPS, ql = rr / gqa;
+        const size_t t = size_t(tok0 + q0 + ql);
+        const int h = kh * gqa + rr % gqa;
+        float y[CPL];
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) y[c] = o[e][c] * inv[e] * sigmoid_approx(g[e][c]);
+        uint32_t hw[CPL / 2], lw[CPL / 2];
+#pragma unroll
+        for (int c = 0; c < CPL; c += 2) hw[c / 2] = pack_bf16x2(y[c], y[c + 1]);
+        uint16_t* dst = a.out + (t * nq + h) * HD + CPL * lane;
+        if constexpr (CPL == 8) {
+          *reinterpret_cast<uint4*>(dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        } else if constexpr (CPL == 4) {
+          *reinterpret_cast<uint2*>(dst) = make_uint2(hw[0], hw[1]);
+        } else {
+          *reinterpret_cast<uint32_t*>(dst) = hw[0];
+        }
+        if (a.lo_offset) {
+          if (a.lo8) {
+            constexpr float S8 = float(1 << B200_LO8_X_SHIFT);
+            uint8_t* d8 = reinterpret_cast<uint8_t*>(a.out + a.lo_offset) + (t * nq + h) * HD + CPL * lane;
+#pragma unroll
+            for (int c = 0; c < CPL; c += 2)
+              reinterpret_cast<uint16_t*>(d8)[c / 2] = f32x2_to_e4m3x2((y[c] - bf16x2_lo(hw[c / 2])) * S8,
+                                                                       (y[c + 1] - bf16x2_hi(hw[c / 2])) * S8);
+          } else {
+#pragma unroll
+            for (int c = 0; c < CPL; c += 2) lw[c / 2] = lo_pair(y[c], y[c + 1], hw[c / 2]);
+            uint16_t* dl = dst + a.lo_offset;
+            if constexpr (CPL == 8) {
+              *reinterpret_cast<uint4*>(dl) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            } else if constexpr (CPL == 4) {
+              *reinterpret_cast<uint2*>(dl) = make_uint2(lw[0], lw[1]);
+            } else {
+              *reinterpret_cast<uint32_t*>(dl) = lw[0];
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, SM::TM_COLS);
+  }
+}
+
+// Q [tokens][q heads][head_dim] as 4-D (dim, head in group, kv head, token); K / V scratch and
+// the layer's pool as 3-D (dim, kv head, row). Boxes: 64 dims x gqa x 1 x 128/gqa rows for Q,
+// 64 dims x 1 x 64 rows for K and V.
+template <int HD>
+static int launch_attn_tc(const AttnArgs& a, int n_tokens, int n_seqs, int max_len, cudaStream_t st) {
+  using SM = AtSmem<HD>;
+  const int nq = a.p.heads, nkv = a.p.kv_heads, gqa = nq / nkv, QT = AT_ROWS / gqa;
+  CUtensorMap mq, mk, mv, mkp, mvp;
+  {
+    const uint64_t dims[4] = {uint64_t(HD), uint64_t(gqa), uint64_t(nkv), uint64_t(n_tokens)};
+    const uint64_t str[3] = {uint64_t(HD) * 2, uint64_t(gqa) * HD * 2, uint64_t(nq) * HD * 2};
+    const uint32_t box[4] = {64, uint32_t(gqa), 1, uint32_t(QT)};
+    if (int rc = encode_bf16_sw128(&mq, a.q_buf, 4, dims, str, box)) return rc;
+  }
+  {
+    const uint64_t dims[3] = {uint64_t(HD), uint64_t(nkv), uint64_t(n_tokens)};
+    const uint64_t str[2] = {uint64_t(HD) * 2, uint64_t(nkv) * HD * 2};
+    const uint32_t box[3] = {64, 1, AT_BK};
+    if (int rc = encode_bf16_sw128(&mk, a.k_buf, 3, dims, str, box)) return rc;
+    if (int rc = encode_bf16_sw128(&mv, a.v_buf, 3, dims, str, box)) return rc;
+    if (a.k_pool) {
+      const uint64_t pdims[3] = {uint64_t(HD), uint64_t(nkv), uint64_t(a.kv_capacity)};
+      if (int rc = encode_bf16_sw128(&mkp, a.k_pool, 3, pdims, str, box)) return rc;
+      if (int rc = encode_bf16_sw128(&mvp, a.v_pool, 3, pdims, str, box)) return rc;
+    } else {  // no prefix keys: never read
+      mkp = mk;
+      mvp = mv;
+    }
+  }
+  static DeviceOnce attr;
+  const int r = once_per_device(attr, [](int) -> int {
+    SDB_CUDA(cudaFuncSetAttribute(attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL));
+    return B200_OK;
+  });
+  if (r != B200_OK) return r;
+  dim3 grid((max_len + QT - 1) / QT, n_seqs, nkv);
+  SDB_CUDA(launch_pdl(attn_tc_kernel<HD>, grid, dim3(AT_THREADS), SM::TOTAL, st, mq, mk, mv, mkp, mvp, a));
+  return B200_OK;
+}
+
+// The tcgen05 kernel takes query groups of 1, 2, 4 or 8 heads per kv head.
+static bool attn_tc_ok(const AttnArgs& a) {
+  const int gqa = a.p.heads / a.p.kv_heads;
+  return gqa == 1 || gqa == 2 || gqa == 4 || gqa == 8;
+}
+
 template <int HD>
 static int launch_attn(const AttnArgs& a, int n_tokens, int n_seqs, int max_len, cudaStream_t st) {
   const int warps = a.p.heads + 2 * a.p.kv_heads;
   SDB_CUDA(launch_pdl(attn_prep_kernel<HD>, dim3(n_tokens), dim3(32 * warps), 0, st, a));
+  if (attn_tc_ok(a)) return launch_attn_tc<HD>(a, n_tokens, n_seqs, max_len, st);
   constexpr int smem = FA_Q * HD * 2 + 4 * FA_K * HD * 2;
   static DeviceOnce attr;  // per head_dim and device
   const int r = once_per_device(attr, [](int) -> int {

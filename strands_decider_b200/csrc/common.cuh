@@ -104,6 +104,8 @@ __device__ __forceinline__ void store_planes4(uint16_t* out, long long lo_offset
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 __device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// sigmoid with the approximate division (2 ulp; 0 for very negative x)
+__device__ __forceinline__ float sigmoid_approx(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 // silu with the approximate division (__fdividef, 2 ulp; x / inf = 0 for very negative x):
 // for instruction-bound elementwise loops
 __device__ __forceinline__ float silu_approx(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
@@ -210,6 +212,24 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 3-D / 4-D tiled loads (coordinates innermost first); the innermost coordinate x times the
+// element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
 // 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -243,6 +263,14 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
          (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// Shared-memory descriptor for an MN-major operand stored as 128-byte-swizzled tiles of 64
+// MN-elements (bf16) x K rows, 128 bytes per K row (what a TMA box of 64 elements x rows writes):
+// the 8-row K groups are `sbo` bytes apart and the 64-element MN atoms `lbo` bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
+         (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 
 // Same for a K-major tile of 64-byte rows written by TMA with 64-byte swizzle (an e4m3
@@ -479,6 +507,12 @@ void sdb_rename_error(const char* from, const char* to);
 namespace sdb {
 // Device ids this library keeps per-device state for.
 constexpr int kMaxDevices = 64;
+
+// A bf16 TMA tensor map with 128-byte swizzle: `rank` dims (innermost first, the innermost
+// box 64 elements), byte strides of dims 1..rank-1, the box per dim; out-of-range elements
+// read as zero. Defined in gemm.cu.
+int encode_bf16_sw128(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                      const uint32_t* box);
 
 // Kernel attributes (such as the dynamic shared-memory limit) are per device, and one process
 // may drive several GPUs from several host threads. A DeviceOnce runs a set-up step once per

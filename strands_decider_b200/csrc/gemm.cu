@@ -684,23 +684,31 @@ template <int EP, int TC>
 __device__ __forceinline__ void swap_ab_epilogue(const GemmArgs& args, int n0, int q, int lane, int t0,
                                                  const float (&v)[TC], float* sT) {
   const b200_linear_out& o = args.o;
+  constexpr int NTOK = TC / 4;  // tokens per warp
 #pragma unroll
   for (int t = 0; t < TC; ++t) sT[t * SWAP_LD + 32 * q + lane] = v[t];
   asm volatile("bar.sync 1, 128;" ::: "memory");
+  // every shared-memory (and residual) read of the warp's tokens comes before its first store,
+  // so the reads overlap instead of each waiting behind the previous token's store
+  if constexpr (EP == B200_EP_SWIGLU) {
+    const int ocol = n0 / 2 + 2 * lane;  // features ocol, ocol + 1
+    float2 g[NTOK], u[NTOK];
 #pragma unroll
-  for (int tt = 0; tt < TC / 4; ++tt) {
-    const int t = q + 4 * tt;
-    if (t0 + t >= args.m) break;
-    const size_t row = size_t(t0 + t) * o.ldo;
-    const float* st = sT + t * SWAP_LD;
-    if constexpr (EP == B200_EP_SWIGLU) {
-      const int ocol = n0 / 2 + 2 * lane;  // features ocol, ocol + 1
-      if (2 * ocol + 2 <= o.n_valid) {
-        const float2 g = *reinterpret_cast<const float2*>(st + 2 * lane);
-        const float2 u = *reinterpret_cast<const float2*>(st + 64 + 2 * lane);
-        const float h0 = silu_approx(g.x) * u.x, h1 = silu_approx(g.y) * u.y;
+    for (int tt = 0; tt < NTOK; ++tt) {
+      const float* st = sT + (q + 4 * tt) * SWAP_LD;
+      g[tt] = *reinterpret_cast<const float2*>(st + 2 * lane);
+      u[tt] = *reinterpret_cast<const float2*>(st + 64 + 2 * lane);
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // sT may be rewritten by the next chunk now
+    if (2 * ocol + 2 <= o.n_valid) {
+      uint16_t* dst = reinterpret_cast<uint16_t*>(o.out);
+#pragma unroll
+      for (int tt = 0; tt < NTOK; ++tt) {
+        const int t = q + 4 * tt;
+        if (t0 + t >= args.m) break;
+        const size_t row = size_t(t0 + t) * o.ldo;
+        const float h0 = silu_approx(g[tt].x) * u[tt].x, h1 = silu_approx(g[tt].y) * u[tt].y;
         const uint32_t hb = pack_bf16x2(h0, h1);
-        uint16_t* dst = reinterpret_cast<uint16_t*>(o.out);
         *reinterpret_cast<uint32_t*>(dst + row + ocol) = hb;
         if (o.lo_offset) {
           if (o.lo_format == B200_LO_E4M3)
@@ -710,27 +718,39 @@ __device__ __forceinline__ void swap_ab_epilogue(const GemmArgs& args, int n0, i
             *reinterpret_cast<uint32_t*>(dst + o.lo_offset + row + ocol) = lo_pair(h0, h1, hb);
         }
       }
-    } else {
-      const int col = n0 + 4 * lane;
-      if (col < o.n_valid) {
-        const float4 val = *reinterpret_cast<const float4*>(st + 4 * lane);
-        float* p = reinterpret_cast<float*>(o.out) + row + col;
+    }
+  } else {
+    const int col = n0 + 4 * lane;
+    float4 val[NTOK], res[NTOK];
+#pragma unroll
+    for (int tt = 0; tt < NTOK; ++tt) {
+      const int t = q + 4 * tt;
+      val[tt] = *reinterpret_cast<const float4*>(sT + t * SWAP_LD + 4 * lane);
+      res[tt] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if constexpr (EP == B200_EP_RESID_ADD) {
+        if (args.ksplit == 1 && col < o.n_valid && t0 + t < args.m)
+          res[tt] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(o.out) +
+                                                      size_t(t0 + t) * o.ldo + col);
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // sT may be rewritten by the next chunk now
+    if (col < o.n_valid) {
+#pragma unroll
+      for (int tt = 0; tt < NTOK; ++tt) {
+        const int t = q + 4 * tt;
+        if (t0 + t >= args.m) break;
+        float* p = reinterpret_cast<float*>(o.out) + size_t(t0 + t) * o.ldo + col;
         if (args.ksplit > 1) {
-          red_add_v4(p, val);
+          red_add_v4(p, val[tt]);
         } else if constexpr (EP == B200_EP_RESID_ADD) {
-          float4 r = *reinterpret_cast<const float4*>(p);
-          r.x += val.x;
-          r.y += val.y;
-          r.z += val.z;
-          r.w += val.w;
-          *reinterpret_cast<float4*>(p) = r;
+          *reinterpret_cast<float4*>(p) =
+              make_float4(res[tt].x + val[tt].x, res[tt].y + val[tt].y, res[tt].z + val[tt].z, res[tt].w + val[tt].w);
         } else {
-          *reinterpret_cast<float4*>(p) = val;
+          *reinterpret_cast<float4*>(p) = val[tt];
         }
       }
     }
   }
-  asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
 constexpr int SK_ROWS = 128;  // weight rows per swap-AB tile (the MMA's M)
@@ -1031,6 +1051,25 @@ static int make_tile_map(CUtensorMap* map, const void* x, bool e4m3, int m, int 
   if (r != CUDA_SUCCESS) return sdb_fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled failed for a GEMM tile");
   return B200_OK;
 }
+int encode_bf16_sw128(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                      const uint32_t* box) {
+  if (int rc = get_encode_fn()) return rc;
+  if (rank < 1 || rank > 5) return sdb_fail(B200_ERR_ARG, "encode_bf16_sw128: rank");
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i > 0) st[i - 1] = strides[i - 1];
+  }
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cuuint32_t(rank), const_cast<void*>(base), d, st, b, e,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return sdb_fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  return B200_OK;
+}
+
 static int make_act_map(CUtensorMap* map, const uint16_t* x, int m, int k, int ldx, int box_rows = GEMM_BM) {
   return make_tile_map(map, x, false, m, k, ldx, box_rows);
 }
