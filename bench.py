@@ -204,15 +204,17 @@ def _store_split(rows: int, tokens: int, n_sm: int = 148) -> bool:
 def launches_per_forward(spec: config.ModelSpec, decide: bool, tokens: int = 0, saves: bool = False,
                          lo_plane: str = "e4m3") -> int:
     """Kernels one b200_model_forward launches: embed; per layer 2 norms, 4 GEMMs and the
-    mixer's 2 kernels, plus a zeroing kernel before a split-K in-projection (small batches);
+    mixer's 2 kernels, plus a zeroing kernel before a split-K in-projection (batches of 129 to
+    4095 tokens; up to 128 tokens on packed weights the norm before it clears the output);
     forwards of >= 4096 tokens also dequantise each of the 4 weights per layer once (bf16
     weights too with the e4m3 low plane); the slot-length update when states are saved; the head."""
     big = tokens >= 4096
+    folded = tokens <= 128 and spec.weight_format != "bf16"
     dq = 4 if big and (spec.weight_format != "bf16" or lo_plane == "e4m3") else 0
     n = 1 + (1 if decide else 0) + (1 if saves else 0)
     for lt in spec.layer_types:
         rows = spec.gdn_in_rows_padded if lt == config.GDN else -(-spec.attn_qkv_rows // 256) * 256
-        n += 2 + 4 + 2 + dq + (0 if big or not _store_split(rows, tokens) else 1)
+        n += 2 + 4 + 2 + dq + (0 if big or folded or not _store_split(rows, tokens) else 1)
     return n
 
 

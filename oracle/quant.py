@@ -48,11 +48,12 @@ import numpy as np
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
-    """fp32 -> bf16 bit patterns (uint16), round to nearest, ties to even."""
+    """fp32 -> bf16 bit patterns (uint16), round to nearest, ties to even. In uint32: no
+    finite or infinite input overflows (the largest is 0xFF807FFF), and NaNs are replaced."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    u = x.view(np.uint32).astype(np.uint64)
-    bias = ((u >> 16) & 1) + 0x7FFF
-    r = ((u + bias) >> 16).astype(np.uint16)
+    u = x.view(np.uint32)
+    bias = ((u >> np.uint32(16)) & np.uint32(1)) + np.uint32(0x7FFF)
+    r = ((u + bias) >> np.uint32(16)).astype(np.uint16)
     nan = np.isnan(x)
     if nan.any():
         r = r.copy()
@@ -320,13 +321,19 @@ def pack_ternary(t: np.ndarray) -> np.ndarray:
     return np.bitwise_or.reduce(code << shifts, axis=2).astype(np.uint8)
 
 
+def _ternary_byte_table() -> np.ndarray:
+    """[256, 4] int8: the four codes of a byte (low bits first), 01 -> +1, 11 -> -1, else 0."""
+    c = (np.arange(256, dtype=np.int64)[:, None] >> (2 * np.arange(4))[None, :]) & 3
+    return np.where(c == 3, -1, np.where(c == 1, 1, 0)).astype(np.int8)
+
+
+_TERNARY_BYTES = _ternary_byte_table()
+
+
 def unpack_ternary(packed: np.ndarray) -> np.ndarray:
     p = np.ascontiguousarray(packed, dtype=np.uint8)
     n, kb = p.shape
-    shifts = (np.arange(4, dtype=np.uint8) * 2)[None, None, :]
-    c = ((p[:, :, None] >> shifts) & 3).astype(np.int64)
-    t = np.where(c == 3, -1, np.where(c == 1, 1, 0))
-    return t.reshape(n, kb * 4)
+    return _TERNARY_BYTES[p].reshape(n, kb * 4)
 
 
 def quantize_ternary(w: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
@@ -342,9 +349,11 @@ def quantize_ternary(w: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
 
 
 def dequantize_ternary(packed: np.ndarray, sbits: np.ndarray) -> np.ndarray:
+    """t * s with t in {-1, 0, +1} and s a bf16 value: already a bf16 value (its bf16 rounding
+    is the identity)."""
     t = unpack_ternary(packed).astype(np.float32)
     s = bf16_bits_to_f32(sbits)
-    return bf16_round((t * s[:, None]).astype(np.float32))
+    return (t * s[:, None]).astype(np.float32)
 
 
 # ----------------------------------------------------------------------------- dispatch
