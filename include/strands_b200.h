@@ -187,7 +187,9 @@ typedef struct b200_seqs {
  * region in k_cache / v_cache (from slot_kv[slot]) must have room for the grown length.
  * Saving into a slot other than the prefix slot is refused (fault word, nothing saved).
  * b200_model_forward sets slot_len[save_slot] after the whole forward; the kernel-level
- * entry points leave slot_len to the caller. */
+ * entry points leave slot_len to the caller. k_cache / v_cache must hold finite values
+ * everywhere (allocate them zeroed): attention reads whole 64-key tiles, and the keys past a
+ * slot's length are masked out of the softmax but still meet zero probabilities in P V. */
 typedef struct b200_prefix_pool {
   int32_t n_slots;
   int32_t kv_capacity;     /* tokens per attention layer in k_cache / v_cache */
