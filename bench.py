@@ -379,9 +379,11 @@ def gemm_roofline(model, tokens: int, pk: dict, reps: int = 20) -> dict:
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
-        per_tok = json.load(open(tp)).get("gate_up_dram_bytes_per_token")
+        # the weight copies once, the token-proportional rest (activations, outputs) per token
+        tj = json.load(open(tp))
+        per_tok = tj.get("gate_up_dram_bytes_per_token")
         if per_tok:
-            traffic = round(per_tok * tokens)
+            traffic = round(tj.get("gate_up_weight_bytes", 0) + per_tok * tokens)
     wname = "bf16 (dequantised once per call)" if dequant else s.weight_format
     planes = "lo8" if lo8 else "split"
     n_sm = torch.cuda.get_device_properties(0).multi_processor_count
