@@ -441,10 +441,13 @@ def test_tile_weights_layout(fmt):
 
 
 @pytest.mark.parametrize("with_prefix", [False, True])
-@pytest.mark.parametrize("hd", [128, 256])
-def test_attention_matches_reference(with_prefix, hd):
+@pytest.mark.parametrize("hd", [64, 128, 256])
+@pytest.mark.parametrize("heads", [(8, 2), (4, 4), (8, 1), (6, 2)])
+def test_attention_matches_reference(with_prefix, hd, heads):
     """q/k RMSNorm(1+w), partial RoPE, causal GQA softmax over (prefix-pool keys +) own
     keys, times sigmoid(gate) (TF:647-690), ragged lengths around the 64/32 tile sizes.
+    Query groups of 4, 1 and 8 heads per kv head run the tcgen05 kernel (128-row tiles of
+    32, 128 and 16 positions); 3 runs the mma.sync kernel.
 
     Three bounds, from tight to loose: (1) the prep kernel's q / k / v (bf16 after norm and
     RoPE, the kernel's storage format) within one bf16 rounding of the fp64 values; (2) the
@@ -457,8 +460,8 @@ def test_attention_matches_reference(with_prefix, hd):
     from strands_decider_b200 import _lib, config
     from strands_decider_b200.runtime import rope_tables
 
-    nq, nkv = 8, 2
-    spec = config.HYBRID_2B if hd == 256 else config.REDUCED_1024
+    nq, nkv = heads
+    spec = {256: config.HYBRID_2B, 128: config.REDUCED_1024, 64: config.TINY}[hd]
     g = torch.Generator().manual_seed(hd)
     lens = [1, 37, 64, 65, 130]
     P = [0, 0, 0, 0, 0] if not with_prefix else [5, 0, 70, 33, 2]
