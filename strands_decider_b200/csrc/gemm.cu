@@ -889,13 +889,15 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
   // One MMA-issuing thread: k-blocks first, first + accs, ... into accumulator `first`. Issuing a
   // tcgen05.mma costs its thread a fixed time whatever N is, so at small N two threads
   // (accumulators) issue twice as fast; the epilogue adds them. With two, the activation slots
-  // are even in number, so each slot (and each of the 4 weight stages) serves one issuer.
+  // are even in number, so each slot (and each of the 4 weight stages) serves one issuer. The
+  // activation slot and its phase are counters: this thread's loop is the critical path, and a
+  // division by the run-time slot count costs it tens of dependent instructions.
   auto mma_loop = [&](int first) {
     const uint32_t idesc = umma_idesc_bf16(SK_ROWS, SM::PLANES * tile_m);
     const uint32_t acc = tmem_base + uint32_t(first * acc_stride);
-    for (int i = first; i < nkb; i += accs) {
-      const int s = i % TS_STAGES, xs = i % xslots;
-      mbar_wait(&full_x[xs], (i / xslots) & 1, FAULT_GEMM_WAIT_FULL_A);
+    for (int i = first, xs = first, xph = 0; i < nkb; i += accs) {  // k-block i: slot i % xslots, phase (i / xslots) & 1
+      const int s = i % TS_STAGES;
+      mbar_wait(&full_x[xs], uint32_t(xph), FAULT_GEMM_WAIT_FULL_A);
       mbar_wait(&full_a[s], (i / TS_STAGES) & 1, FAULT_GEMM_WAIT_FULL_B);
       tc_fence_after();
       const uint64_t bd = umma_desc_sw128(smem_addr(sX + xs * x_stage));
@@ -905,6 +907,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         umma_bf16_ts(acc, ta + uint32_t(8 * j), bd + 2 * j, idesc, (i >= accs || j != 0) ? 1u : 0u);
       umma_commit(&empty_a[s]);
       umma_commit(&empty_x[xs]);
+      xs += accs;
+      if (xs >= xslots) xs -= xslots, xph ^= 1;
     }
     umma_commit(&acc_full[0]);
   };
@@ -913,13 +917,13 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     // ---------------- activation producer (the weight ring has its own thread, warp 2)
     if (lane == 0) {
       pdl_wait();  // the activations come from the kernel before this one
-      for (int i = 0; i < nkb; ++i) {
-        const int xs = i % xslots;
-        mbar_wait(&empty_x[xs], ((i / xslots) & 1) ^ 1, FAULT_GEMM_WAIT_EMPTY);
+      for (int i = 0, xs = 0, xph = 0; i < nkb; ++i) {  // slot i % xslots, phase (i / xslots) & 1
+        mbar_wait(&empty_x[xs], uint32_t(xph ^ 1), FAULT_GEMM_WAIT_EMPTY);
         mbar_arrive_expect_tx(&full_x[xs], uint32_t(x_stage));
         tma_load_2d(sX + xs * x_stage, &tmX, &full_x[xs], (kb0 + i) * GEMM_BK, 0);
         if constexpr (PL == PL_SPLIT)
           tma_load_2d(sX + xs * x_stage + x_plane, &tmX_lo, &full_x[xs], (kb0 + i) * GEMM_BK, 0);
+        if (++xs == xslots) xs = 0, xph ^= 1;
       }
     }
   } else if (warp == 1) {

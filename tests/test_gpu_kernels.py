@@ -262,6 +262,23 @@ def test_linear_small_m_whole_k_with_weight_ring(split):
     assert (out.double().cpu() - ref).abs().max().item() / ref.abs().max().item() < 2e-5
 
 
+@pytest.mark.parametrize("m,split", [(8, False), (16, True), (32, True), (96, True)])
+def test_linear_small_m_ragged_k_ranges(m, split):
+    """A down-projection shape (K = 6144, 16 weight tiles): K splits 9 ways into ranges of 10 and
+    11 k-blocks, so the two MMA issuers (alternate k-blocks) get ranges of unequal length and
+    the activation slots wrap at different points, one or two planes."""
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    k, n = 6144, 2048
+    _, xp = _planes(m, k, 60 + m)
+    pw = W.concat_rows([W.quantize("ternary", _weights(n, k, seed=61).cuda())])
+    ref = _reference(xp, pw, split=split)
+    out, before = _linear("b200_linear", xp, pw, _lib.EP_RESID_ADD, split=split)
+    got = out.double().cpu() - before.double().cpu()
+    assert (got - ref).abs().max().item() < 2e-5 * ref.abs().max().item() + 1e-6
+
+
 def test_linear_rejects_bad_shapes():
     from strands_decider_b200 import _lib
     from strands_decider_b200 import weights as W
