@@ -724,7 +724,8 @@ def c2_gemm(pk: dict, reps: int = 50, check: bool = True) -> list[dict]:
             flops = 2.0 * m * n * C2_K
             t_hbm = nbytes / (pk["hbm_gbs"] * 1e9) * 1e6
             t_mma = flops / (pk["bf16_tflops"] * 1e12) * 1e6
-            path = "packed tiles unpacked in the GEMM" if us_dq is None else "dequantised once + bf16 GEMM"
+            path = ("dequantised once + bf16 GEMM" if us_dq is not None else
+                    "weights streamed through registers (<= 16 rows)" if m <= 16 else "packed tiles unpacked in the GEMM")
             us_best = us if us_dq is None else us_dq
             rec = {"m": m, "n": n, "k": C2_K, "us": round(us_best, 3), "path": path,
                    "gbs": round(nbytes / us_best / 1e3, 1), "tflops": round(flops / us_best / 1e6, 1),

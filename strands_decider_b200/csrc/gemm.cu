@@ -1309,6 +1309,10 @@ static int dispatch_ts_nt(const CUtensorMap& mx, const CUtensorMap& mx_lo, const
 // with a separate launch) for these batches.
 bool linear_small_m(int32_t m, int32_t format) { return m <= TS_MAX_M && format != B200_W_BF16; }
 
+// At most 16 rows on packed weights: the register-streamed kernel (gemm_rs.cu).
+bool linear_rs(int32_t m, int32_t format);
+int sdb_linear_rs(const uint16_t* x, const uint16_t* xl, int ldx, const GemmArgs& a, cudaStream_t st);
+
 }  // namespace sdb
 
 using namespace sdb;
@@ -1326,6 +1330,7 @@ extern "C" int b200_linear(const uint16_t* x_hi, const uint16_t* x_lo, int32_t m
   }
   GemmArgs a{*w, *out, m, k, 1};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (linear_rs(m, w->format)) return sdb_linear_rs(x_hi, x_lo, ldx, a, st);  // <= 16 rows, packed
   if (linear_small_m(m, w->format)) {  // small M, packed weights: decoded into TMEM (swap-AB)
     const int nt = (m + 15) / 16 * 16;
     CUtensorMap mx, mx_lo;

@@ -214,10 +214,12 @@ def test_linear_large_k_and_m_tail():
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-@pytest.mark.parametrize("m", [1, 16, 17, 64, 96, 128])
+@pytest.mark.parametrize("m", [1, 5, 9, 16, 17, 64, 96, 128])
 @pytest.mark.parametrize("ep", ["store", "resid", "swiglu"])
 def test_linear_small_m_matches_reference(fmt, m, ep):
-    """Batches of at most 128 rows on packed weights run the swap-AB kernel (weights decoded
+    """Batches of at most 16 rows on packed weights run the register-streamed kernel (weights
+    decoded in registers into mma.sync A fragments, one or two 8-token tiles, the 8 warps' K
+    partials summed in shared memory); 17 to 128 rows run the swap-AB kernel (weights decoded
     into tensor memory as the MMA's 128-row A operand, both activation planes in one B operand
     of N = 2 x 16, 64 or 128 tokens; split K for the store and residual epilogues, whole K with
     the weight ring refilled for the SwiGLU; bf16 weights take the general kernel): fp64 product
@@ -245,6 +247,35 @@ def test_linear_small_m_matches_reference(fmt, m, ep):
         out, before = _linear(fn, xp, pw, e, n_valid=736)
         got = out.double().cpu() - (before.double().cpu() if ep == "resid" else 0)
         assert (got - ref).abs().max().item() < 2e-5 * ref.abs().max().item() + 1e-6, fn
+
+
+@pytest.mark.parametrize("m", [3, 12])
+def test_linear_small_m_swiglu_e4m3_low_plane(m):
+    """The SwiGLU of a batch of at most 16 rows written with an e4m3 low plane: hi = bf16_rn(h),
+    lo byte = e4m3_rn_satfinite((h - hi) 2^6); the planes recombine to the fp64 SwiGLU within the
+    e4m3 plane's precision, and the hi plane equals the bf16-low-plane call's hi plane."""
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    k, inter = 2048, 768
+    _, xp = _planes(m, k, 70 + m)
+    gate = W.quantize("nvfp4", _weights(inter, k, seed=71).cuda())
+    up = W.quantize("nvfp4", _weights(inter, k, seed=72).cuda())
+    pw = W.interleave_gate_up(gate, up)
+    ref = torch.nn.functional.silu(_reference(xp, gate)) * _reference(xp, up)
+    buf = torch.zeros(3 * m * inter, dtype=torch.uint8, device="cuda")  # hi plane (bf16), then the e4m3 bytes
+    hi = buf[: 2 * m * inter].view(torch.bfloat16).view(m, inter)
+    lo8 = buf[2 * m * inter:].view(m, inter)
+    o = _lib.LinearOut(_lib.EP_SWIGLU, 2 * inter, _lib.ptr(hi), inter, m * inter, 1)
+    qw = pw.qweight()
+    _lib.call("b200_linear", _lib.ptr(xp[0]), _lib.ptr(xp[1]), m, k, k, _ref(qw), _ref(o), _lib.stream_ptr())
+    torch.cuda.synchronize()
+    lo = torch.from_numpy(Q.e4m3_decode(lo8.cpu().numpy())).double() / 64.0
+    got = hi.double().cpu() + lo
+    # bf16 hi plane + e4m3 residual: about 12 significant bits per element
+    assert (got - ref).abs().max().item() / ref.abs().max().item() < 3e-4
+    out, _ = _linear("b200_linear", xp, pw, _lib.EP_SWIGLU, n_valid=2 * inter)
+    assert torch.equal(out[0], hi)
 
 
 @pytest.mark.parametrize("split", [True, False])
