@@ -14,6 +14,9 @@ by the fused head. Data are synthetic (seeded), weights random-init.
 Other workloads: `prefix` (512 requests with states of U[64, 2048] tokens, 32 questions of
 48 tokens, 2-5 options), `ternary-batch` (4096 single-question 96-token requests as full
 prompts, ternary weights) and `latency` (p50 / p99 of one 96-token request, CUDA-graphed).
+On one GPU the default line also carries a summary of each of them (`prefix_cache` and
+`ternary_batch`: 3 timed steps in a child process, with their own CPU baseline and parity;
+`latency`) and of the int4 GEMM microbench (`c2_gemm`); `--no-extras` leaves them out.
 
 Steps replay one CUDA graph per batch. Under torchrun (N > 1) the requests are sharded
 longest-processing-time first (weak scaling, no collective in the forward) and every step's
@@ -855,6 +858,29 @@ def _kmax(wl: config.Workload) -> int:
     return wl.option_range[1] if wl.option_range else max(wl.options)
 
 
+def other_workload(name: str, steps: int = 3, warmup: int = 3, cpu_sample: int = 3) -> dict:
+    """One more workload's line, measured in a child process of this run (its own model, CUDA
+    graphs, timed region, clocks, CPU baseline and parity), summarised for the default line so
+    that every configuration's number comes out of the same command."""
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE")}
+    cmd = [sys.executable, os.path.abspath(__file__), "--workload", name, "--steps", str(steps), "--warmup",
+           str(warmup), "--cpu-sample", str(cpu_sample), "--no-extras"]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env, cwd=ROOT)
+    except subprocess.TimeoutExpired:
+        return {"workload": name, "error": "timed out after 900 s"}
+    lines = [x for x in r.stdout.splitlines() if x.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return {"workload": name, "error": f"exit {r.returncode}: {r.stderr.strip()[-300:]}"}
+    d = json.loads(lines[-1])
+    cb = d.get("cpu_baseline") or {}
+    return {"workload": d["config"]["workload"], "value": d["value"], "unit": d["unit"], "steps": d["steps"],
+            "warmup": d["warmup"], "ms_per_step": d["ms_per_step"], "e2e": d["e2e"]["value"],
+            "decisions_per_step": d["config"]["decisions_per_step"], "tokens_per_step": d["config"]["tokens_per_step"],
+            "path": d["config"]["path"], "gpu_launches": d["gpu_launches"], "clocks": d["clocks"],
+            "parity": d.get("parity"), "cpu_baseline": {k: cb.get(k) for k in ("value", "cores", "kind", "sample")}}
+
+
 def latency(args, emit: bool = True, cpu: bool = True) -> dict:
     """p50 / p99 single-request latency: one 96-token request (93-token state + 3-token
     question, one 3-way choice) as one full-prompt forward of the ternary 2B-shape decider,
@@ -1028,6 +1054,15 @@ def main() -> None:
     from strands_decider_b200.weights import DeviceWeights
 
     torch.cuda.set_device(local)
+    extras = {}
+    if world == 1 and args.extras and args.workload == "nvfp4":
+        # the int4 GEMM microbench first, on a GPU that has not just run the power-capped main
+        # workload (its small launches follow the SM clock), with the clocks it ran at
+        csamp = ClockSampler(local)
+        csamp.start()
+        extras["c2_gemm"] = [{k: r[k] for k in ("m", "n", "us", "bound", "roofline_us", "frac", "path")}
+                             for r in c2_gemm(peaks(), reps=30, check=False)]
+        extras["c2_gemm_clocks"] = csamp.stop()
     if world > 1:
         from datetime import timedelta
 
@@ -1137,11 +1172,8 @@ def main() -> None:
     del graphs
     roof = gemm_roofline(model, batches[0].n_state_tokens or batches[0].n_suffix_tokens, pk) if rank == 0 else None
     assert _lib.read_fault() == 0
-    extras = {}
     if world == 1 and args.extras and args.workload == "nvfp4":
-        # the int4 GEMM microbench and the single-request latency, measured in the same run
-        extras["c2_gemm"] = [{k: r[k] for k in ("m", "n", "us", "bound", "roofline_us", "frac", "path")}
-                             for r in c2_gemm(pk, reps=30, check=False)]
+        # the single-request latency, measured in the same run
         lat = latency(args, emit=False, cpu=False)
         extras["latency"] = {"workload": lat["config"]["workload"], "p50_ms": lat["latency_ms"]["p50"],
                              "p99_ms": lat["latency_ms"]["p99"], "e2e_p50_ms": lat["e2e"]["value"],
@@ -1169,6 +1201,11 @@ def main() -> None:
         assert shards[0][: len(sample)] == list(range(len(sample)))   # batch 0 starts with the sample
         par = parity_check(b0_probs[rows], cb.pop("_probs"),
                            [r["n_opts"][q] for r in sample for q in range(n_q or wl.n_questions)])
+    if world == 1 and args.extras and args.workload == "nvfp4":
+        # the prefix-cache workload (512 x U[64, 2048] + 32 x 48) and the 4096 x 96 ternary batch,
+        # each a few steps in a child process
+        extras["prefix_cache"] = other_workload("prefix")
+        extras["ternary_batch"] = other_workload("ternary-batch")
     b0 = batches[0]
     fl = 2.0 * spec.linear_params() * total_tok
     line = {
