@@ -179,9 +179,9 @@ constexpr int PREP_TPW_LARGE = 8;
 // that part. Blocks run (head, part) fastest, so the blocks resident at one time read whole
 // rows of the in-projection output (DRAM pages opened once) rather than one head's 512-byte
 // strip down all T rows. The warp keeps the last 3 input rows in registers and loads each
-// input row once, two tokens ahead (token t's row is mix row t whatever its sequence, so
-// the prefetch needs no sequence lookup). One part per warp keeps the registers low enough
-// for 4 blocks per SM, whose loads in flight cover HBM latency.
+// input row once, four tokens ahead for large batches (two for TPW = 1; token t's row is mix
+// row t whatever its sequence, so the prefetch needs no sequence lookup). One part per warp
+// keeps the registers low enough for 4 blocks per SM, whose loads in flight cover HBM latency.
 template <int TPW>
 __global__ void __launch_bounds__(256, 4) gdn_prep_kernel(const GdnArgs a) {
   __shared__ float4 wsm[4][32];  // conv taps (oldest first) of channel 4 lane + c of this part
@@ -205,23 +205,34 @@ __global__ void __launch_bounds__(256, 4) gdn_prep_kernel(const GdnArgs a) {
   bool fresh = true;
   const float* xrow = a.mix + ch0 + lane * 4;  // + t * ld: token t's 4 channels of this lane
   float4 win[3];  // rows p-3, p-2, p-1
-  float4 x = *reinterpret_cast<const float4*>(xrow + size_t(t_begin) * a.ld_mix), x1 = x;
-  if (t_begin + 1 < t_end) x1 = *reinterpret_cast<const float4*>(xrow + size_t(t_begin + 1) * a.ld_mix);
-  // v warps, lanes 0 / 1: the gating inputs b / a of the head, loaded two tokens ahead like the rows
+  // v warps, lanes 0 / 1: the gating inputs b / a of the head, loaded ahead like the rows
   const bool gate_lane = part == 2 && lane < 2;
   const float* grow = a.mix + conv_dim + value_dim + (lane == 0 ? h : H + h);
   const float a_coef = gate_lane ? -__expf(a.p.a_log[h]) : 0.0f, dt_bias = gate_lane ? a.p.dt_bias[h] : 0.0f;
-  float g = 0.0f, g1 = 0.0f;
-  if (gate_lane) {
-    g = grow[size_t(t_begin) * a.ld_mix];
-    if (t_begin + 1 < t_end) g1 = grow[size_t(t_begin + 1) * a.ld_mix];
+  // rows t .. t + PD - 1 (and their gating inputs) in flight: xq[i] is row t + i
+  constexpr int PD = TPW >= 8 ? 4 : 2;
+  float4 xq[PD];
+  float gq[PD];
+#pragma unroll
+  for (int i = 0; i < PD; ++i) {
+    xq[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    gq[i] = 0.0f;
+    if (t_begin + i < t_end) {
+      xq[i] = *reinterpret_cast<const float4*>(xrow + size_t(t_begin + i) * a.ld_mix);
+      if (gate_lane) gq[i] = grow[size_t(t_begin + i) * a.ld_mix];
+    }
   }
   for (int t = t_begin; t < t_end; ++t) {
-    float4 xn = x1;
-    float gn = 0.0f;
-    if (t + 2 < t_end) {  // in flight meanwhile
-      xn = *reinterpret_cast<const float4*>(xrow + size_t(t + 2) * a.ld_mix);
-      if (gate_lane) gn = grow[size_t(t + 2) * a.ld_mix];
+    const float4 x = xq[0];
+    const float g = gq[0];
+#pragma unroll
+    for (int i = 0; i + 1 < PD; ++i) {
+      xq[i] = xq[i + 1];
+      gq[i] = gq[i + 1];
+    }
+    if (t + PD < t_end) {  // in flight meanwhile
+      xq[PD - 1] = *reinterpret_cast<const float4*>(xrow + size_t(t + PD) * a.ld_mix);
+      if (gate_lane) gq[PD - 1] = grow[size_t(t + PD) * a.ld_mix];
     }
     while (t >= tend) {  // next (possibly empty) sequence; ends because t < T = cu[n_seqs]
       ++seq;
@@ -273,10 +284,6 @@ __global__ void __launch_bounds__(256, 4) gdn_prep_kernel(const GdnArgs a) {
     reinterpret_cast<float4*>(dst + part * GD)[lane] = make_float4(o[0] * r, o[1] * r, o[2] * r, o[3] * r);
     if (gate_lane)  // beta = sigmoid(b) (lane 0), g = -exp(A_log) softplus(a + dt_bias) (lane 1)
       dst[GQKV + lane] = lane == 0 ? __fdividef(1.0f, 1.0f + __expf(-g)) : a_coef * softplus(g + dt_bias);
-    x = x1;
-    x1 = xn;
-    g = g1;
-    g1 = gn;
   }
 }
 

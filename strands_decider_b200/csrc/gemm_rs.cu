@@ -122,8 +122,9 @@ __device__ __forceinline__ void rs_load_x(const uint16_t* x, int ldx, int m, int
   v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
 }
 
-// grid: one CTA per group of RT 16-row weight tiles (row0 below); 8 warps over the k-blocks. NT8 token tiles of 8 (m <= 8 NT8); SPLIT adds the x_lo plane (a second MMA per A
-// fragment into the same accumulator).
+// grid: one CTA per group of RT 16-row weight tiles (row0 below); 8 warps over the k-blocks.
+// NT8 token tiles of 8 (m <= 8 NT8); SPLIT adds the x_lo plane (a second MMA per A fragment
+// into the same accumulator).
 template <int FMT, int EP, bool SPLIT, int RT, int NT8>
 __global__ void __launch_bounds__(RS_THREADS, 2) gemm_rs_kernel(const uint16_t* __restrict__ x,
                                                              const uint16_t* __restrict__ xl, int ldx,
