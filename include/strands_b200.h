@@ -95,7 +95,9 @@ int b200_tile_weights(const b200_qweight* w, void* tiles, void* tile_scales, b20
 
 /* ---------------------------------------------------------------- linear (GEMM)
  * y = x @ dequant(W)^T with a fused epilogue, fp32 accumulation in tensor memory (tcgen05
- * on sm_100a). Activations carry fp32-level precision as two bf16 planes, x = x_hi + x_lo
+ * on sm_100a); batches of at most 16 rows on packed weights stream the weights through
+ * registers into mma.sync instead (fp32 accumulation in registers; the weight-read-bound
+ * case). Activations carry fp32-level precision as two bf16 planes, x = x_hi + x_lo
  * (x_hi = bf16_rn(x), x_lo = bf16_rn(x - x_hi)); the tensor cores run one bf16 MMA per
  * plane into the same accumulator. Each plane is bf16 [m, ldx] row-major (ldx a multiple of
  * 8, 16-byte aligned). x_lo may be NULL for a single bf16 pass.
