@@ -310,6 +310,37 @@ def test_linear_small_m_ragged_k_ranges(m, split):
     assert (got - ref).abs().max().item() < 2e-5 * ref.abs().max().item() + 1e-6
 
 
+@pytest.mark.parametrize("fmt", ["int4", "nvfp4", "ternary"])
+@pytest.mark.parametrize("ep", ["store", "resid", "swiglu"])
+@pytest.mark.parametrize("split", [True, False])
+def test_linear_register_path_down_projection(fmt, ep, split):
+    """The register-streamed kernel (at most 16 rows) at a down-projection depth: K = 6144 gives
+    each of a CTA's 8 warps 12 k-blocks, so the 4-deep weight ring and 2-deep activation ring
+    wrap; 13 rows (two token tiles, the second partly past the batch), n_valid below the weight's
+    rows, one or two activation planes; fp64 product of the same operands."""
+    from strands_decider_b200 import _lib
+    from strands_decider_b200 import weights as W
+
+    m, k = 13, 6144
+    _, xp = _planes(m, k, 80)
+    if ep == "swiglu":
+        inter = 256
+        gate = W.quantize(fmt, _weights(inter, k, seed=81).cuda())
+        up = W.quantize(fmt, _weights(inter, k, seed=82).cuda())
+        pw = W.interleave_gate_up(gate, up)
+        ref = torch.nn.functional.silu(_reference(xp, gate, split)) * _reference(xp, up, split)
+        out, _ = _linear("b200_linear", xp, pw, _lib.EP_SWIGLU, n_valid=2 * inter, split=split)
+        got = out[0].double().cpu() + out[1].double().cpu()
+        assert (got - ref).abs().max().item() / ref.abs().max().item() < 1e-4
+        return
+    pw = W.concat_rows([W.quantize(fmt, _weights(480, k, seed=83).cuda())])   # 512 rows, 480 valid
+    ref = _reference(xp, pw, split)[:, :480]
+    e = _lib.EP_STORE if ep == "store" else _lib.EP_RESID_ADD
+    out, before = _linear("b200_linear", xp, pw, e, n_valid=480, split=split)
+    got = out.double().cpu() - (before.double().cpu() if ep == "resid" else 0)
+    assert (got - ref).abs().max().item() < 2e-5 * ref.abs().max().item() + 1e-6
+
+
 def test_linear_rejects_bad_shapes():
     from strands_decider_b200 import _lib
     from strands_decider_b200 import weights as W
